@@ -1,0 +1,77 @@
+"""Builds libfurykernel_cuda.so in-tree for sm_100a with nvcc.
+
+Strict arithmetic: --fmad=false (no contraction but explicit fma, the
+reference's `Strict` math, src/FuryKernel/Backend.hs:179-200), IEEE division
+and square root, no fast math.
+"""
+
+from __future__ import annotations
+
+import glob
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "csrc")
+OUT_DIR = os.path.join(HERE, "_build")
+LIB = os.path.join(OUT_DIR, "libfurykernel_cuda.so")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def nccl_dirs() -> tuple[str, str]:
+    """NCCL's headers and library: the copy torch loads, so that one NCCL
+    serves the process."""
+    try:
+        import nvidia.nccl  # type: ignore
+
+        base = list(nvidia.nccl.__path__)[0]
+        inc, lib = os.path.join(base, "include"), os.path.join(base, "lib")
+        if os.path.exists(os.path.join(inc, "nccl.h")):
+            return inc, lib
+    except ImportError:
+        pass
+    return "/usr/include", "/usr/lib/x86_64-linux-gnu"
+
+
+def sources() -> list[str]:
+    return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+
+
+def stale() -> bool:
+    if not os.path.exists(LIB):
+        return True
+    t = os.path.getmtime(LIB)
+    deps = sources() + glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh"))
+    deps.append(os.path.join(HERE, "..", "include", "furykernel_cuda.h"))
+    return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
+
+
+def build(verbose: bool = False, ptxas_v: bool = False) -> str:
+    os.makedirs(OUT_DIR, exist_ok=True)
+    inc, lib = nccl_dirs()
+    objs = []
+    for src in sources():
+        obj = os.path.join(OUT_DIR, os.path.basename(src)[:-3] + ".o")
+        if not os.path.exists(obj) or os.path.getmtime(obj) < max(
+            os.path.getmtime(p)
+            for p in [src] + glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh"))
+            + [os.path.join(HERE, "..", "include", "furykernel_cuda.h")]
+        ):
+            cmd = ["nvcc", *ARCH, "-O3", "-lineinfo", "--fmad=false", "-std=c++17", "-Xcompiler", "-fPIC",
+                   "-I", inc, "-c", src, "-o", obj]
+            if ptxas_v:
+                cmd += ["-Xptxas", "-v"]
+            if verbose:
+                print(" ".join(cmd), file=sys.stderr)
+            subprocess.run(cmd, check=True)
+        objs.append(obj)
+    cmd = ["nvcc", *ARCH, "-shared", "-o", LIB, *objs, "-L", lib, "-l:libnccl.so.2", "-Xlinker", f"-rpath,{lib}"]
+    if verbose:
+        print(" ".join(cmd), file=sys.stderr)
+    subprocess.run(cmd, check=True)
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(verbose=True, ptxas_v="-v" in sys.argv))

@@ -1,0 +1,103 @@
+// Host-side launchers of the furykernel-cuda kernels (internal to the
+// library; the public boundary is include/furykernel_cuda.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+enum { FK_PRO_NONE = 0, FK_PRO_RMSNORM = 1, FK_PRO_SILU = 2 };
+
+struct FkGemv {
+  const float* w;      // [n, k] out_in
+  const float* x;      // [m, ldx]
+  const float* gamma;  // RMSNorm prologue's gain, [k], or null
+  const float* r;      // residual [m, ldr] added in the epilogue, or null
+  float* y;            // [m, ldy]
+  uint32_t n, k, m, split;
+  uint32_t ldx, ldr, ldy;
+  uint32_t up_off;  // SiLU-gate prologue: the up half's offset in a row of x
+  int prologue;     // FK_PRO_*
+  float eps, factor;
+  bool pdl;  // launch as a programmatic dependent of the previous kernel
+};
+
+struct FkAttend {
+  const float* qkv;  // rows of [q | k | v]; q at column q_off, ld = ldq
+  const float* cos_t;
+  const float* sin_t;  // [positions, rotated]
+  const uint32_t* pos;
+  const uint32_t* slot;
+  const float* kc;
+  const float* vc;  // Ring caches [slots, kv_heads, length, d]
+  float* part_m;    // [m, heads, max_splits]
+  float* part_l;
+  float* part_acc;  // [m, heads, max_splits, d]
+  uint32_t m, heads, kv_heads, d, length, rotated, chunk, max_splits;
+  uint32_t ldq, q_off;
+  float scale;
+  bool pdl;
+};
+
+struct FkKvStore {
+  const float* qkv;  // k at column k_off, v at column v_off, ld = ldq
+  const float* cos_t;
+  const float* sin_t;
+  const uint32_t* pos;
+  const uint32_t* slot;
+  float* kc;
+  float* vc;
+  uint32_t m, kv_heads, d, length, rotated;
+  uint32_t ldq, k_off, v_off;
+  bool pdl;
+};
+
+struct FkCombine {
+  const float* part_m;
+  const float* part_l;
+  const float* part_acc;
+  const uint32_t* pos;
+  float* out;  // [m, ldo]
+  uint32_t m, heads, d, chunk, max_splits, ldo;
+  bool pdl;
+};
+
+cudaError_t fk_launch_reduce_groups(const float* x, uint64_t n, float* partials, int sms, cudaStream_t s);
+cudaError_t fk_launch_reduce_final(const float* partials, uint32_t count, float* chains, unsigned int* done,
+                                   float* y, cudaStream_t s);
+cudaError_t fk_launch_rmsnorm_rows(const float* x, const float* gamma, float* y, uint32_t rows, uint32_t h,
+                                   float eps, float factor, cudaStream_t s);
+cudaError_t fk_launch_softmax_rows(const float* x, float* y, uint32_t rows, uint32_t h, cudaStream_t s);
+cudaError_t fk_launch_gemv(const FkGemv& g, cudaStream_t s);
+cudaError_t fk_launch_kv_store(const FkKvStore& a, cudaStream_t s);
+cudaError_t fk_launch_attend(const FkAttend& a, cudaStream_t s);
+cudaError_t fk_launch_combine(const FkCombine& a, cudaStream_t s);
+cudaError_t fk_launch_gather(const float* table, uint32_t width, const uint32_t* tokens, uint32_t m, float factor,
+                             float* y, bool pdl, cudaStream_t s);
+cudaError_t fk_launch_argmax(const float* x, uint32_t m, uint32_t n, uint32_t ldx, uint32_t* ids, bool pdl,
+                             cudaStream_t s);
+cudaError_t fk_launch_rope(const float* x, uint32_t m, uint32_t heads, uint32_t d, uint32_t rotated, uint32_t ldx,
+                           const uint32_t* pos, const float* cos_t, const float* sin_t, float* y, uint32_t ldy,
+                           cudaStream_t s);
+cudaError_t fk_launch_add(const float* a, const float* b, float* y, uint64_t n, cudaStream_t s);
+cudaError_t fk_launch_silu_mul(const float* a, const float* b, float* y, uint64_t n, cudaStream_t s);
+cudaError_t fk_launch_fill_normal(float* out, uint64_t n, uint64_t seed, double mu, double sigma, cudaStream_t s);
+cudaError_t fk_launch_fill_uniform(float* out, uint64_t n, uint64_t seed, double a, double b, cudaStream_t s);
+cudaError_t fk_launch_rope_tables(float* cos_t, float* sin_t, double theta, uint32_t d, uint32_t rotated,
+                                  uint32_t positions, cudaStream_t s);
+
+// Launch helper for kernels that take part in programmatic dependent launch.
+template <typename... KArgs, typename... Args>
+static inline cudaError_t fk_launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                       bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}

@@ -1,0 +1,201 @@
+// Decode attention over Ring KV caches, as the plan runs it: the KV store
+// step (RoPE of k recomputed, then k and v stored at each row's position),
+// the attention anchor in splits of positions (RoPE of q recomputed; each
+// split's maximum, sum and accumulator stored as partials, the Partials
+// form of src/FuryKernel/Program/Plan.hs:174-181), and the combine step.
+//
+// Arithmetic, which the oracle's fko_attend_split / fko_attend_combine
+// restate: a score is lane l's chain over packs l, l + 32, ... of q*k from
+// 0, summed pairwise over the lanes, times the scale (Eval.hs:474-527: the
+// scale on the dot product). A split's weights are exp(s - max) in binary64
+// rounded once; warp w of 4 takes positions w, w + 4, ... of the split,
+// adding e and e * v from 0, and the warps' sums are added in warp order.
+// The combine rescales each split by exp(m - M), M the largest maximum, and
+// adds the splits in order before dividing.
+#include "fk_common.cuh"
+#include "fk_kernels.h"
+
+namespace fk {
+
+constexpr int kAttWarps = 4;
+constexpr int kHeadDim = 128;  // one float4 pack a lane
+constexpr int kMaxChunk = 256;
+
+// RoPE of one head (halves pairing, Eval.hs:634-645): thread i < d/2 turns
+// pair (i, i + d/2) by the position's table entry; pairs past `rotated` stay.
+__device__ __forceinline__ void rope_pair(const float* __restrict__ src, float* __restrict__ dst, uint32_t i,
+                                          uint32_t half, uint32_t rotated, const float* __restrict__ cos_row,
+                                          const float* __restrict__ sin_row) {
+  const float a = src[i], b = src[i + half];
+  if (i < rotated) {
+    const float c = __ldg(cos_row + i), s = __ldg(sin_row + i);
+    dst[i] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+    dst[i + half] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+  } else {
+    dst[i] = a;
+    dst[i + half] = b;
+  }
+}
+
+// The KV store step: grid (kv_heads, m), d / 2 threads.
+__global__ void kv_store_kernel(FkKvStore a) {
+  grid_wait();
+  grid_launch_dependents();
+  const uint32_t h = blockIdx.x, r = blockIdx.y, i = threadIdx.x, half = a.d / 2;
+  const uint32_t p = a.pos[r];
+  const size_t at = (((size_t)a.slot[r] * a.kv_heads + h) * a.length + p % a.length) * a.d;
+  const float* krow = a.qkv + (size_t)r * a.ldq + a.k_off + (size_t)h * a.d;
+  const float* vrow = a.qkv + (size_t)r * a.ldq + a.v_off + (size_t)h * a.d;
+  rope_pair(krow, a.kc + at, i, half, a.rotated, a.cos_t + (size_t)p * a.rotated, a.sin_t + (size_t)p * a.rotated);
+  a.vc[at + i] = vrow[i];
+  a.vc[at + i + half] = vrow[i + half];
+}
+
+// The attention anchor: grid (max_splits, heads, m), 4 warps.
+__global__ void __launch_bounds__(128) attend_split_kernel(FkAttend a) {
+  __shared__ float qrot[kHeadDim];
+  __shared__ float scores[kMaxChunk];
+  __shared__ float4 accw[kAttWarps][kHeadDim / 4];
+  __shared__ float lw[kAttWarps];
+
+  grid_wait();
+  grid_launch_dependents();
+  const uint32_t j = blockIdx.x, h = blockIdx.y, r = blockIdx.z;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t p = a.pos[r];
+  const uint32_t npos = p + 1;
+  const uint32_t splits = (npos + a.chunk - 1) / a.chunk;
+  if (j >= splits) return;
+  const uint32_t t0 = j * a.chunk;
+  const uint32_t t1 = min(npos, t0 + a.chunk);
+  const uint32_t kvh = h / (a.heads / a.kv_heads);
+  const size_t base = ((size_t)a.slot[r] * a.kv_heads + kvh) * a.length;
+  const float4* kc4 = reinterpret_cast<const float4*>(a.kc);
+  const float4* vc4 = reinterpret_cast<const float4*>(a.vc);
+
+  if (threadIdx.x < kHeadDim / 2)
+    rope_pair(a.qkv + (size_t)r * a.ldq + a.q_off + (size_t)h * kHeadDim, qrot, threadIdx.x, kHeadDim / 2,
+              a.rotated, a.cos_t + (size_t)p * a.rotated, a.sin_t + (size_t)p * a.rotated);
+  __syncthreads();
+  const float4 qv = reinterpret_cast<const float4*>(qrot)[lane];
+
+  // Scores: warp w takes positions t0 + w + 4 u, four at a time.
+  for (uint32_t t = t0 + warp; t < t1; t += 4 * kAttWarps) {
+    float4 kv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint32_t tt = t + u * kAttWarps;
+      kv[u] = tt < t1 ? __ldcs(kc4 + (base + tt % a.length) * (kHeadDim / 4) + lane) : make_float4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float sc = __fmul_rn(warp_sum(__fadd_rn(0.0f, pack_dot(qv, kv[u]))), a.scale);
+      const uint32_t tt = t + u * kAttWarps;
+      if (lane == 0 && tt < t1) scores[tt - t0] = sc;
+    }
+  }
+  __syncthreads();
+  float mx = -INFINITY;
+  for (uint32_t i = lane; i < t1 - t0; i += 32) mx = max_number(mx, scores[i]);
+  mx = warp_max(mx);
+
+  // Weighted sums: warp w over positions t0 + w, t0 + w + 4, ..., in order.
+  float l = 0.0f;
+  float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (uint32_t t = t0 + warp; t < t1; t += 4 * kAttWarps) {
+    float4 vv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint32_t tt = t + u * kAttWarps;
+      vv[u] = tt < t1 ? __ldcs(vc4 + (base + tt % a.length) * (kHeadDim / 4) + lane) : make_float4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint32_t tt = t + u * kAttWarps;
+      if (tt < t1) {
+        const float e = exp_rounded(__fsub_rn(scores[tt - t0], mx));
+        l = __fadd_rn(l, e);
+        acc.x = __fadd_rn(acc.x, __fmul_rn(e, vv[u].x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(e, vv[u].y));
+        acc.z = __fadd_rn(acc.z, __fmul_rn(e, vv[u].z));
+        acc.w = __fadd_rn(acc.w, __fmul_rn(e, vv[u].w));
+      }
+    }
+  }
+  accw[warp][lane] = acc;
+  if (lane == 0) lw[warp] = l;
+  __syncthreads();
+  const size_t at = ((size_t)r * a.heads + h) * a.max_splits + j;
+  const float* accf = reinterpret_cast<const float*>(accw);
+  const uint32_t i = threadIdx.x;  // one dimension a thread
+  float o = accf[i];
+#pragma unroll
+  for (int w = 1; w < kAttWarps; ++w) o = __fadd_rn(o, accf[w * kHeadDim + i]);
+  a.part_acc[at * kHeadDim + i] = o;
+  if (threadIdx.x == 0) {
+    float lt = lw[0];
+#pragma unroll
+    for (int w = 1; w < kAttWarps; ++w) lt = __fadd_rn(lt, lw[w]);
+    a.part_l[at] = lt;
+    a.part_m[at] = mx;
+  }
+}
+
+// The combine step: grid (heads, m), d threads.
+__global__ void combine_kernel(FkCombine a) {
+  grid_wait();
+  grid_launch_dependents();
+  const uint32_t h = blockIdx.x, r = blockIdx.y, i = threadIdx.x;
+  const uint32_t splits = (a.pos[r] + 1 + a.chunk - 1) / a.chunk;
+  const size_t at = ((size_t)r * a.heads + h) * a.max_splits;
+  float top = -INFINITY;
+  for (uint32_t j = 0; j < splits; ++j) top = max_number(top, a.part_m[at + j]);
+  float w0 = exp_rounded(__fsub_rn(a.part_m[at], top));
+  float l = __fmul_rn(a.part_l[at], w0);
+  float o = __fmul_rn(a.part_acc[at * a.d + i], w0);
+  for (uint32_t j = 1; j < splits; ++j) {
+    const float w = exp_rounded(__fsub_rn(a.part_m[at + j], top));
+    l = __fadd_rn(l, __fmul_rn(a.part_l[at + j], w));
+    o = __fadd_rn(o, __fmul_rn(a.part_acc[(at + j) * a.d + i], w));
+  }
+  a.out[(size_t)r * a.ldo + (size_t)h * a.d + i] = __fdiv_rn(o, l);
+}
+
+// A standalone RoPE of every head: grid (heads, m), d / 2 threads.
+__global__ void rope_kernel(const float* __restrict__ x, uint32_t heads, uint32_t d, uint32_t rotated, uint32_t ldx,
+                            const uint32_t* __restrict__ pos, const float* __restrict__ cos_t,
+                            const float* __restrict__ sin_t, float* __restrict__ y, uint32_t ldy) {
+  const uint32_t h = blockIdx.x, r = blockIdx.y, p = pos[r];
+  rope_pair(x + (size_t)r * ldx + (size_t)h * d, y + (size_t)r * ldy + (size_t)h * d, threadIdx.x, d / 2, rotated,
+            cos_t + (size_t)p * rotated, sin_t + (size_t)p * rotated);
+}
+
+}  // namespace fk
+
+cudaError_t fk_launch_kv_store(const FkKvStore& a, cudaStream_t s) {
+  if (a.m == 0) return cudaSuccess;
+  if (a.d % 2 != 0 || a.d > 2048) return cudaErrorInvalidValue;
+  return fk_launch_ex(fk::kv_store_kernel, dim3(a.kv_heads, a.m), dim3(a.d / 2), 0, s, a.pdl, a);
+}
+
+cudaError_t fk_launch_attend(const FkAttend& a, cudaStream_t s) {
+  if (a.m == 0) return cudaSuccess;
+  if (a.d != fk::kHeadDim || a.chunk == 0 || a.chunk > fk::kMaxChunk || a.heads % a.kv_heads != 0)
+    return cudaErrorInvalidValue;
+  return fk_launch_ex(fk::attend_split_kernel, dim3(a.max_splits, a.heads, a.m), dim3(128), 0, s, a.pdl, a);
+}
+
+cudaError_t fk_launch_combine(const FkCombine& a, cudaStream_t s) {
+  if (a.m == 0) return cudaSuccess;
+  if (a.d > 1024) return cudaErrorInvalidValue;
+  return fk_launch_ex(fk::combine_kernel, dim3(a.heads, a.m), dim3(a.d), 0, s, a.pdl, a);
+}
+
+cudaError_t fk_launch_rope(const float* x, uint32_t m, uint32_t heads, uint32_t d, uint32_t rotated, uint32_t ldx,
+                           const uint32_t* pos, const float* cos_t, const float* sin_t, float* y, uint32_t ldy,
+                           cudaStream_t s) {
+  if (m == 0) return cudaSuccess;
+  if (d % 2 != 0 || d > 2048) return cudaErrorInvalidValue;
+  fk::rope_kernel<<<dim3(heads, m), d / 2, 0, s>>>(x, heads, d, rotated, ldx, pos, cos_t, sin_t, y, ldy);
+  return cudaGetLastError();
+}

@@ -1,0 +1,170 @@
+// Elementwise work, the embedding gather, the greedy pick, and the seeded
+// fills that make a synthetic model's weights on the device.
+#include <math.h>
+
+#include "fk_common.cuh"
+#include "fk_kernels.h"
+
+namespace fk {
+
+// Gather (src/FuryKernel/Program/Eval.hs:528-535), one token a row:
+// y = table[token] * factor. Grid (ceil(width / 1024), m), 256 threads of
+// one pack each.
+__global__ void gather_kernel(const float* __restrict__ table, uint32_t width, const uint32_t* __restrict__ tokens,
+                              float factor, float* __restrict__ y) {
+  grid_wait();
+  grid_launch_dependents();
+  const uint32_t r = blockIdx.y;
+  const uint32_t j = blockIdx.x * 256u + threadIdx.x;
+  if (4 * j >= width) return;
+  const float4* src = reinterpret_cast<const float4*>(table + (size_t)tokens[r] * width);
+  float4 v = __ldg(src + j);
+  if (factor != 1.0f) v = make_float4(__fmul_rn(v.x, factor), __fmul_rn(v.y, factor), __fmul_rn(v.z, factor),
+                                      __fmul_rn(v.w, factor));
+  reinterpret_cast<float4*>(y + (size_t)r * width)[j] = v;
+}
+
+// ArgMax (Eval.hs:545-548, 684-685): the fold keeps the first index whose
+// value is greater than all before it, so NaNs past the first element are
+// never taken and a NaN first element is the answer. Each thread scans its
+// elements in index order; pairs combine by "greater, or equal at a lower
+// index". Grid m, 1024 threads.
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ x, uint32_t n, uint32_t ldx,
+                                                      uint32_t* __restrict__ ids) {
+  __shared__ float sv[32];
+  __shared__ uint32_t si[32];
+  grid_wait();
+  grid_launch_dependents();
+  const uint32_t r = blockIdx.x;
+  const float* xr = x + (size_t)r * ldx;
+  float bv = -INFINITY;
+  uint32_t bi = 0xffffffffu;
+  for (uint32_t j = threadIdx.x; j < n; j += blockDim.x) {
+    const float v = xr[j];
+    if (v > bv || (bi == 0xffffffffu && v == bv)) {
+      bv = v;
+      bi = j;
+    }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_down_sync(0xffffffffu, bv, o);
+    const uint32_t oi = __shfl_down_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if (lane == 0) {
+    sv[warp] = bv;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    bv = lane < (int)(blockDim.x >> 5) ? sv[lane] : -INFINITY;
+    bi = lane < (int)(blockDim.x >> 5) ? si[lane] : 0xffffffffu;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_down_sync(0xffffffffu, bv, o);
+      const uint32_t oi = __shfl_down_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) ids[r] = isnan(xr[0]) || bi == 0xffffffffu ? 0u : bi;
+  }
+}
+
+__global__ void add_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ y,
+                           uint64_t n) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+    y[i] = __fadd_rn(a[i], b[i]);
+}
+
+// SiLU-gate, silu(a) * b with silu(a) = a / (1 + exp(-a)).
+__global__ void silu_mul_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ y,
+                                uint64_t n) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+    const float e = exp_rounded(-a[i]);
+    y[i] = __fmul_rn(__fdiv_rn(a[i], __fadd_rn(1.0f, e)), b[i]);
+  }
+}
+
+// Seeded inputs: SplitMix's finaliser of seed * golden + i, i from 1
+// (test/cpu/Cases.hs:885-892). N(mu, sigma) by Box-Muller on consecutive
+// words, in binary64 rounded once; U(a, b) from the top 24 bits.
+__device__ __forceinline__ uint64_t splitmix(uint64_t seed, uint64_t i) {
+  uint64_t z = seed * 0x9E3779B97F4A7C15ULL + i;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  return z ^ (z >> 31);
+}
+
+__global__ void fill_normal_kernel(float* __restrict__ out, uint64_t n, uint64_t seed, double mu, double sigma) {
+  const uint64_t pairs = (n + 1) / 2;
+  for (uint64_t p = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; p < pairs;
+       p += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t w1 = splitmix(seed, 2 * p + 1), w2 = splitmix(seed, 2 * p + 2);
+    const double u1 = ((double)(w1 >> 11) + 1.0) * 0x1p-53;
+    const double u2 = (double)(w2 >> 11) * 0x1p-53;
+    const double rr = sqrt(-2.0 * log(u1));
+    const double t = 6.283185307179586 * u2;
+    out[2 * p] = (float)(mu + sigma * (rr * cos(t)));
+    if (2 * p + 1 < n) out[2 * p + 1] = (float)(mu + sigma * (rr * sin(t)));
+  }
+}
+
+__global__ void fill_uniform_kernel(float* __restrict__ out, uint64_t n, uint64_t seed, double a, double b) {
+  for (uint64_t j = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; j < n; j += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t w = splitmix(seed, j + 1);
+    out[j] = (float)(a + (b - a) * ((double)(w >> 40) * 0x1p-24));
+  }
+}
+
+}  // namespace fk
+
+cudaError_t fk_launch_gather(const float* table, uint32_t width, const uint32_t* tokens, uint32_t m, float factor,
+                             float* y, bool pdl, cudaStream_t s) {
+  if (m == 0) return cudaSuccess;
+  if (width % 4 != 0) return cudaErrorInvalidValue;
+  return fk_launch_ex(fk::gather_kernel, dim3((width / 4 + 255) / 256, m), dim3(256), 0, s, pdl, table, width, tokens,
+                      factor, y);
+}
+
+cudaError_t fk_launch_argmax(const float* x, uint32_t m, uint32_t n, uint32_t ldx, uint32_t* ids, bool pdl,
+                             cudaStream_t s) {
+  if (m == 0) return cudaSuccess;
+  if (n == 0) return cudaErrorInvalidValue;
+  return fk_launch_ex(fk::argmax_kernel, dim3(m), dim3(1024), 0, s, pdl, x, n, ldx, ids);
+}
+
+static unsigned grid_for(uint64_t n) {
+  uint64_t b = (n + 255) / 256;
+  return (unsigned)(b > 148ull * 64 ? 148ull * 64 : (b == 0 ? 1 : b));
+}
+
+cudaError_t fk_launch_add(const float* a, const float* b, float* y, uint64_t n, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  fk::add_kernel<<<grid_for(n), 256, 0, s>>>(a, b, y, n);
+  return cudaGetLastError();
+}
+
+cudaError_t fk_launch_silu_mul(const float* a, const float* b, float* y, uint64_t n, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  fk::silu_mul_kernel<<<grid_for(n), 256, 0, s>>>(a, b, y, n);
+  return cudaGetLastError();
+}
+
+cudaError_t fk_launch_fill_normal(float* out, uint64_t n, uint64_t seed, double mu, double sigma, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  fk::fill_normal_kernel<<<grid_for((n + 1) / 2), 256, 0, s>>>(out, n, seed, mu, sigma);
+  return cudaGetLastError();
+}
+
+cudaError_t fk_launch_fill_uniform(float* out, uint64_t n, uint64_t seed, double a, double b, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  fk::fill_uniform_kernel<<<grid_for(n), 256, 0, s>>>(out, n, seed, a, b);
+  return cudaGetLastError();
+}

@@ -1,0 +1,791 @@
+// The C ABI of furykernel-cuda (include/furykernel_cuda.h): contexts,
+// device memory, the kernel table with its ABI texts and hashes, checked
+// launches, CUDA-graph capture of a plan's launches, and NCCL.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <nccl.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+#include <string>
+#include <unordered_set>
+#include <vector>
+
+#include "../../include/furykernel_cuda.h"
+#include "fk_kernels.h"
+
+// ---------------------------------------------------------------------------
+// Errors
+
+static thread_local std::string g_last_error;
+
+static int fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+static int cuda_fail(cudaError_t e, const char* what) {
+  return fail(FKC_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+#define FKC_CUDA(call, what)                   \
+  do {                                         \
+    cudaError_t e_ = (call);                   \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+extern "C" const char* fkc_last_error(void) { return g_last_error.c_str(); }
+extern "C" int fkc_version(void) { return 1; }
+
+// ---------------------------------------------------------------------------
+// Contexts
+
+struct fkc_ctx {
+  int device = 0;
+  int sms = 0;
+  cudaStream_t stream = nullptr;
+  bool pdl = false;
+  bool capturing = false;
+  // Scratch of reduce_final: the 256 chains' sums and a completion counter.
+  float* red_chains = nullptr;
+  unsigned int* red_done = nullptr;
+  std::unordered_set<void*> allocs;
+  ncclComm_t comm = nullptr;
+  int nranks = 1, rank = 0;
+};
+
+struct fkc_graph {
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  int device = 0;
+};
+
+extern "C" int fkc_open(int device, fkc_ctx** out) {
+  if (!out) return fail(FKC_ERR_ARGUMENT, "fkc_open: no place for the context.");
+  int count = 0;
+  FKC_CUDA(cudaGetDeviceCount(&count), "fkc_open: cudaGetDeviceCount");
+  if (device < 0 || device >= count)
+    return fail(FKC_ERR_ARGUMENT, "fkc_open: device %d is not one of the %d devices.", device, count);
+  FKC_CUDA(cudaSetDevice(device), "fkc_open: cudaSetDevice");
+  cudaDeviceProp prop;
+  FKC_CUDA(cudaGetDeviceProperties(&prop, device), "fkc_open: cudaGetDeviceProperties");
+  if (prop.major != 10)
+    return fail(FKC_ERR_ARGUMENT, "fkc_open: device %d is sm_%d%d; this library is built for sm_100a.", device,
+                prop.major, prop.minor);
+  fkc_ctx* c = new fkc_ctx;
+  c->device = device;
+  c->sms = prop.multiProcessorCount;
+  cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMalloc(&c->red_chains, 256 * sizeof(float));
+  if (e == cudaSuccess) e = cudaMalloc(&c->red_done, sizeof(unsigned int));
+  if (e == cudaSuccess) e = cudaMemset(c->red_done, 0, sizeof(unsigned int));
+  if (e != cudaSuccess) {
+    fkc_close(c);
+    return cuda_fail(e, "fkc_open");
+  }
+  *out = c;
+  return FKC_OK;
+}
+
+extern "C" int fkc_close(fkc_ctx* c) {
+  if (!c) return FKC_OK;
+  cudaSetDevice(c->device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  if (c->comm) ncclCommDestroy(c->comm);
+  for (void* p : c->allocs) cudaFree(p);
+  if (c->red_chains) cudaFree(c->red_chains);
+  if (c->red_done) cudaFree(c->red_done);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+  return FKC_OK;
+}
+
+extern "C" int fkc_stream(fkc_ctx* c, void** s) {
+  if (!c || !s) return fail(FKC_ERR_ARGUMENT, "fkc_stream: null argument.");
+  *s = (void*)c->stream;
+  return FKC_OK;
+}
+
+extern "C" int fkc_sm_count(fkc_ctx* c, int* sms) {
+  if (!c || !sms) return fail(FKC_ERR_ARGUMENT, "fkc_sm_count: null argument.");
+  *sms = c->sms;
+  return FKC_OK;
+}
+
+extern "C" int fkc_set_pdl(fkc_ctx* c, int enabled) {
+  if (!c) return fail(FKC_ERR_ARGUMENT, "fkc_set_pdl: null context.");
+  c->pdl = enabled != 0;
+  return FKC_OK;
+}
+
+extern "C" int fkc_sync(fkc_ctx* c) {
+  if (!c) return fail(FKC_ERR_ARGUMENT, "fkc_sync: null context.");
+  cudaSetDevice(c->device);
+  FKC_CUDA(cudaStreamSynchronize(c->stream), "fkc_sync");
+  return FKC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Memory
+
+extern "C" int fkc_buf_alloc(fkc_ctx* c, size_t bytes, void** dptr) {
+  if (!c || !dptr) return fail(FKC_ERR_ARGUMENT, "fkc_buf_alloc: null argument.");
+  cudaSetDevice(c->device);
+  void* p = nullptr;
+  FKC_CUDA(cudaMalloc(&p, bytes ? bytes : 16), "fkc_buf_alloc");
+  c->allocs.insert(p);
+  *dptr = p;
+  return FKC_OK;
+}
+
+extern "C" int fkc_buf_free(fkc_ctx* c, void* dptr) {
+  if (!c) return fail(FKC_ERR_ARGUMENT, "fkc_buf_free: null context.");
+  if (!dptr) return FKC_OK;
+  auto it = c->allocs.find(dptr);
+  if (it == c->allocs.end()) return fail(FKC_ERR_ARGUMENT, "fkc_buf_free: %p is not a buffer of this context.", dptr);
+  cudaSetDevice(c->device);
+  c->allocs.erase(it);
+  FKC_CUDA(cudaFree(dptr), "fkc_buf_free");
+  return FKC_OK;
+}
+
+extern "C" int fkc_buf_zero(fkc_ctx* c, void* dptr, size_t bytes) {
+  if (!c || (!dptr && bytes)) return fail(FKC_ERR_ARGUMENT, "fkc_buf_zero: null argument.");
+  cudaSetDevice(c->device);
+  FKC_CUDA(cudaMemsetAsync(dptr, 0, bytes, c->stream), "fkc_buf_zero");
+  return FKC_OK;
+}
+
+extern "C" int fkc_buf_upload(fkc_ctx* c, void* dptr, const void* host, size_t bytes) {
+  if (!c || (bytes && (!dptr || !host))) return fail(FKC_ERR_ARGUMENT, "fkc_buf_upload: null argument.");
+  cudaSetDevice(c->device);
+  FKC_CUDA(cudaMemcpyAsync(dptr, host, bytes, cudaMemcpyHostToDevice, c->stream), "fkc_buf_upload");
+  if (!c->capturing) FKC_CUDA(cudaStreamSynchronize(c->stream), "fkc_buf_upload");
+  return FKC_OK;
+}
+
+extern "C" int fkc_buf_download(fkc_ctx* c, void* host, const void* dptr, size_t bytes) {
+  if (!c || (bytes && (!dptr || !host))) return fail(FKC_ERR_ARGUMENT, "fkc_buf_download: null argument.");
+  cudaSetDevice(c->device);
+  FKC_CUDA(cudaMemcpyAsync(host, dptr, bytes, cudaMemcpyDeviceToHost, c->stream), "fkc_buf_download");
+  if (!c->capturing) FKC_CUDA(cudaStreamSynchronize(c->stream), "fkc_buf_download");
+  return FKC_OK;
+}
+
+extern "C" int fkc_host_alloc(size_t bytes, void** host) {
+  if (!host) return fail(FKC_ERR_ARGUMENT, "fkc_host_alloc: null argument.");
+  FKC_CUDA(cudaHostAlloc(host, bytes ? bytes : 16, cudaHostAllocDefault), "fkc_host_alloc");
+  return FKC_OK;
+}
+
+extern "C" int fkc_host_free(void* host) {
+  if (host) FKC_CUDA(cudaFreeHost(host), "fkc_host_free");
+  return FKC_OK;
+}
+
+extern "C" int fkc_kv_arena(fkc_ctx* c, uint32_t layers, uint32_t slots, uint32_t kv_heads, uint32_t length,
+                            uint32_t head_dim, void** k_base, void** v_base) {
+  if (!c || !k_base || !v_base) return fail(FKC_ERR_ARGUMENT, "fkc_kv_arena: null argument.");
+  const size_t per = (size_t)slots * kv_heads * length * head_dim * sizeof(float);
+  const size_t total = per * layers;
+  int rc = fkc_buf_alloc(c, total, k_base);
+  if (rc) return rc;
+  rc = fkc_buf_alloc(c, total, v_base);
+  if (rc) return rc;
+  rc = fkc_buf_zero(c, *k_base, total);
+  if (rc) return rc;
+  return fkc_buf_zero(c, *v_base, total);
+}
+
+extern "C" int fkc_rope_tables(fkc_ctx* c, double theta, uint32_t d, uint32_t rotated, uint32_t positions,
+                               void** cos_t, void** sin_t) {
+  if (!c || !cos_t || !sin_t || d == 0) return fail(FKC_ERR_ARGUMENT, "fkc_rope_tables: bad argument.");
+  const size_t n = (size_t)positions * rotated;
+  std::vector<float> hc(n), hs(n);
+  for (uint32_t p = 0; p < positions; ++p)
+    for (uint32_t i = 0; i < rotated; ++i) {
+      const double angle = (double)p * pow(theta, -((double)(2 * i) / (double)d));
+      hc[(size_t)p * rotated + i] = (float)cos(angle);
+      hs[(size_t)p * rotated + i] = (float)sin(angle);
+    }
+  int rc = fkc_buf_alloc(c, n * sizeof(float), cos_t);
+  if (rc) return rc;
+  rc = fkc_buf_alloc(c, n * sizeof(float), sin_t);
+  if (rc) return rc;
+  rc = fkc_buf_upload(c, *cos_t, hc.data(), n * sizeof(float));
+  if (rc) return rc;
+  return fkc_buf_upload(c, *sin_t, hs.data(), n * sizeof(float));
+}
+
+extern "C" int fkc_fill_normal(fkc_ctx* c, void* dptr, uint64_t n, uint64_t seed, double mu, double sigma) {
+  if (!c || (n && !dptr)) return fail(FKC_ERR_ARGUMENT, "fkc_fill_normal: null argument.");
+  cudaSetDevice(c->device);
+  FKC_CUDA(fk_launch_fill_normal((float*)dptr, n, seed, mu, sigma, c->stream), "fkc_fill_normal");
+  return FKC_OK;
+}
+
+extern "C" int fkc_fill_uniform(fkc_ctx* c, void* dptr, uint64_t n, uint64_t seed, double a, double b) {
+  if (!c || (n && !dptr)) return fail(FKC_ERR_ARGUMENT, "fkc_fill_uniform: null argument.");
+  cudaSetDevice(c->device);
+  FKC_CUDA(fk_launch_fill_uniform((float*)dptr, n, seed, a, b, c->stream), "fkc_fill_uniform");
+  return FKC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// The kernel table
+
+namespace {
+
+struct BufSpec {
+  const char* name;
+  const char* access;  // read, write, read_write
+  const char* type;    // f32, u32
+};
+
+struct ParamSpec {
+  const char* name;
+  const char* type;  // u32 or f32
+  bool dim;
+  uint32_t lo, hi, mult;
+};
+
+struct Params {
+  const unsigned char* bytes;
+  const std::vector<uint32_t>* offsets;
+  uint32_t u(int i) const {
+    uint32_t v;
+    memcpy(&v, bytes + (*offsets)[i], 4);
+    return v;
+  }
+  float f(int i) const {
+    float v;
+    memcpy(&v, bytes + (*offsets)[i], 4);
+    return v;
+  }
+};
+
+typedef int (*LaunchFn)(fkc_ctx*, const Params&, void* const*);
+
+struct KernelSpec {
+  const char* name;
+  uint32_t threads;
+  std::vector<BufSpec> bufs;
+  std::vector<ParamSpec> params;
+  LaunchFn launch;
+  // Derived: the C layout, the ABI text and its hash.
+  std::vector<uint32_t> offsets;
+  uint32_t params_size = 0;
+  std::string abi;
+  uint64_t hash = 0;
+};
+
+uint64_t fnv1a(const void* p, size_t n) {
+  const unsigned char* b = (const unsigned char*)p;
+  uint64_t h = 0xcbf29ce484222325ULL;
+  for (size_t i = 0; i < n; ++i) {
+    h ^= b[i];
+    h *= 0x100000001b3ULL;
+  }
+  return h;
+}
+
+int launched(cudaError_t e, const char* name) {
+  if (e == cudaErrorInvalidValue)
+    return fail(FKC_ERR_ARGUMENT, "%s: the launch's shape is not one this kernel takes.", name);
+  if (e != cudaSuccess) return cuda_fail(e, name);
+  return FKC_OK;
+}
+
+#define F(i) ((float*)bufs[i])
+#define CF(i) ((const float*)bufs[i])
+#define CU(i) ((const uint32_t*)bufs[i])
+#define U(i) ((uint32_t*)bufs[i])
+
+int l_reduce_groups(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return launched(fk_launch_reduce_groups(CF(0), p.u(0), F(1), c->sms, c->stream), "reduce_groups");
+}
+
+int l_reduce_final(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return launched(fk_launch_reduce_final(CF(0), p.u(0), c->red_chains, c->red_done, F(1), c->stream),
+                  "reduce_final");
+}
+
+int l_rmsnorm_rows(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return launched(fk_launch_rmsnorm_rows(CF(0), CF(1), F(2), p.u(0), p.u(1), p.f(2), p.f(3), c->stream),
+                  "rmsnorm_rows");
+}
+
+int l_softmax_rows(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return launched(fk_launch_softmax_rows(CF(0), F(1), p.u(0), p.u(1), c->stream), "softmax_rows");
+}
+
+FkGemv gemv_base(fkc_ctx* c, const Params& p) {
+  FkGemv g = {};
+  g.n = p.u(0);
+  g.k = p.u(1);
+  g.m = p.u(2);
+  g.split = p.u(3);
+  g.ldx = p.u(4);
+  g.ldy = p.u(5);
+  g.factor = 1.0f;
+  g.pdl = c->pdl;
+  return g;
+}
+
+// gemv: w, x, y | n k m split ldx ldy
+int l_gemv(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkGemv g = gemv_base(c, p);
+  g.w = CF(0), g.x = CF(1), g.y = F(2);
+  g.prologue = FK_PRO_NONE;
+  return launched(fk_launch_gemv(g, c->stream), "gemv");
+}
+// gemv_add: w, x, r, y | n k m split ldx ldy ldr
+int l_gemv_add(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkGemv g = gemv_base(c, p);
+  g.w = CF(0), g.x = CF(1), g.r = CF(2), g.y = F(3);
+  g.ldr = p.u(6);
+  g.prologue = FK_PRO_NONE;
+  return launched(fk_launch_gemv(g, c->stream), "gemv_add");
+}
+// gemv_rmsnorm: w, x, gamma, y | n k m split ldx ldy eps factor
+int l_gemv_rmsnorm(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkGemv g = gemv_base(c, p);
+  g.w = CF(0), g.x = CF(1), g.gamma = CF(2), g.y = F(3);
+  g.eps = p.f(6);
+  g.factor = p.f(7);
+  g.prologue = FK_PRO_RMSNORM;
+  return launched(fk_launch_gemv(g, c->stream), "gemv_rmsnorm");
+}
+// gemv_silu: w, x, y | n k m split ldx ldy up_off
+int l_gemv_silu(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkGemv g = gemv_base(c, p);
+  g.w = CF(0), g.x = CF(1), g.y = F(2);
+  g.up_off = p.u(6);
+  g.prologue = FK_PRO_SILU;
+  return launched(fk_launch_gemv(g, c->stream), "gemv_silu");
+}
+// gemv_silu_add: w, x, r, y | n k m split ldx ldy ldr up_off
+int l_gemv_silu_add(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkGemv g = gemv_base(c, p);
+  g.w = CF(0), g.x = CF(1), g.r = CF(2), g.y = F(3);
+  g.ldr = p.u(6);
+  g.up_off = p.u(7);
+  g.prologue = FK_PRO_SILU;
+  return launched(fk_launch_gemv(g, c->stream), "gemv_silu_add");
+}
+
+// kv_store_ring: qkv cos sin pos slot k_cache v_cache | m kv_heads d length rotated ldq k_off v_off
+int l_kv_store(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkKvStore a = {};
+  a.qkv = CF(0), a.cos_t = CF(1), a.sin_t = CF(2), a.pos = CU(3), a.slot = CU(4), a.kc = F(5), a.vc = F(6);
+  a.m = p.u(0), a.kv_heads = p.u(1), a.d = p.u(2), a.length = p.u(3), a.rotated = p.u(4);
+  a.ldq = p.u(5), a.k_off = p.u(6), a.v_off = p.u(7);
+  a.pdl = c->pdl;
+  if (a.rotated > a.d / 2) return fail(FKC_ERR_ARGUMENT, "kv_store_ring: rotated %u is more than d/2.", a.rotated);
+  return launched(fk_launch_kv_store(a, c->stream), "kv_store_ring");
+}
+
+// attend_split: qkv cos sin pos slot k_cache v_cache part_m part_l part_acc
+//   | m heads kv_heads d length rotated chunk max_splits ldq q_off scale
+int l_attend(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkAttend a = {};
+  a.qkv = CF(0), a.cos_t = CF(1), a.sin_t = CF(2), a.pos = CU(3), a.slot = CU(4), a.kc = CF(5), a.vc = CF(6);
+  a.part_m = F(7), a.part_l = F(8), a.part_acc = F(9);
+  a.m = p.u(0), a.heads = p.u(1), a.kv_heads = p.u(2), a.d = p.u(3), a.length = p.u(4), a.rotated = p.u(5);
+  a.chunk = p.u(6), a.max_splits = p.u(7), a.ldq = p.u(8), a.q_off = p.u(9);
+  a.scale = p.f(10);
+  a.pdl = c->pdl;
+  if (a.kv_heads == 0 || a.heads % a.kv_heads != 0)
+    return fail(FKC_ERR_ARGUMENT, "attend_split: %u heads do not share %u KV heads in groups.", a.heads, a.kv_heads);
+  return launched(fk_launch_attend(a, c->stream), "attend_split");
+}
+
+// attend_combine: part_m part_l part_acc pos out | m heads d chunk max_splits ldo
+int l_combine(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkCombine a = {};
+  a.part_m = CF(0), a.part_l = CF(1), a.part_acc = CF(2), a.pos = CU(3), a.out = F(4);
+  a.m = p.u(0), a.heads = p.u(1), a.d = p.u(2), a.chunk = p.u(3), a.max_splits = p.u(4), a.ldo = p.u(5);
+  a.pdl = c->pdl;
+  return launched(fk_launch_combine(a, c->stream), "attend_combine");
+}
+
+// gather: table tokens y | width m factor
+int l_gather(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return launched(fk_launch_gather(CF(0), p.u(0), CU(1), p.u(1), p.f(2), F(2), c->pdl, c->stream), "gather");
+}
+
+// argmax: x ids | m n ldx
+int l_argmax(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return launched(fk_launch_argmax(CF(0), p.u(0), p.u(1), p.u(2), U(1), c->pdl, c->stream), "argmax");
+}
+
+// rope: x pos cos sin y | m heads d rotated ldx ldy
+int l_rope(fkc_ctx* c, const Params& p, void* const* bufs) {
+  if (p.u(3) > p.u(2) / 2) return fail(FKC_ERR_ARGUMENT, "rope: rotated %u is more than d/2.", p.u(3));
+  return launched(
+      fk_launch_rope(CF(0), p.u(0), p.u(1), p.u(2), p.u(3), p.u(4), CU(1), CF(2), CF(3), F(4), p.u(5), c->stream),
+      "rope");
+}
+
+int l_add(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return launched(fk_launch_add(CF(0), CF(1), F(2), p.u(0), c->stream), "add");
+}
+
+int l_silu_mul(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return launched(fk_launch_silu_mul(CF(0), CF(1), F(2), p.u(0), c->stream), "silu_mul");
+}
+
+#undef F
+#undef CF
+#undef CU
+#undef U
+
+constexpr uint32_t kMax = 4294967295u;
+
+ParamSpec dim(const char* n, uint32_t lo, uint32_t hi, uint32_t mult = 1) { return {n, "u32", true, lo, hi, mult}; }
+ParamSpec u32(const char* n) { return {n, "u32", false, 0, 0, 0}; }
+ParamSpec f32(const char* n) { return {n, "f32", false, 0, 0, 0}; }
+
+std::vector<KernelSpec> make_table() {
+  std::vector<KernelSpec> t;
+  auto gemv_dims = std::vector<ParamSpec>{dim("n", 1, 1048576), dim("k", 4, 65536, 4), dim("m", 1, 32),
+                                          dim("split", 1, 8),   u32("ldx"),           u32("ldy")};
+  auto with = [](std::vector<ParamSpec> a, std::initializer_list<ParamSpec> b) {
+    a.insert(a.end(), b.begin(), b.end());
+    return a;
+  };
+  t.push_back({"reduce_groups", 256, {{"x", "read", "f32"}, {"partials", "write", "f32"}}, {dim("n", 1, 2147483648u)},
+               l_reduce_groups});
+  t.push_back({"reduce_final", 256, {{"partials", "read", "f32"}, {"y", "write", "f32"}}, {dim("count", 1, 16777216)},
+               l_reduce_final});
+  t.push_back({"rmsnorm_rows",
+               256,
+               {{"x", "read", "f32"}, {"gamma", "read", "f32"}, {"y", "write", "f32"}},
+               {dim("rows", 1, 1048576), dim("h", 4, 16384, 4), f32("eps"), f32("factor")},
+               l_rmsnorm_rows});
+  t.push_back({"softmax_rows",
+               256,
+               {{"x", "read", "f32"}, {"y", "write", "f32"}},
+               {dim("rows", 1, 1048576), dim("h", 4, 16384, 4)},
+               l_softmax_rows});
+  t.push_back({"gemv", 256, {{"w", "read", "f32"}, {"x", "read", "f32"}, {"y", "write", "f32"}}, gemv_dims, l_gemv});
+  t.push_back({"gemv_add",
+               256,
+               {{"w", "read", "f32"}, {"x", "read", "f32"}, {"r", "read", "f32"}, {"y", "write", "f32"}},
+               with(gemv_dims, {u32("ldr")}),
+               l_gemv_add});
+  t.push_back({"gemv_rmsnorm",
+               256,
+               {{"w", "read", "f32"}, {"x", "read", "f32"}, {"gamma", "read", "f32"}, {"y", "write", "f32"}},
+               with(gemv_dims, {f32("eps"), f32("factor")}),
+               l_gemv_rmsnorm});
+  t.push_back({"gemv_silu",
+               256,
+               {{"w", "read", "f32"}, {"x", "read", "f32"}, {"y", "write", "f32"}},
+               with(gemv_dims, {u32("up_off")}),
+               l_gemv_silu});
+  t.push_back({"gemv_silu_add",
+               256,
+               {{"w", "read", "f32"}, {"x", "read", "f32"}, {"r", "read", "f32"}, {"y", "write", "f32"}},
+               with(gemv_dims, {u32("ldr"), u32("up_off")}),
+               l_gemv_silu_add});
+  t.push_back({"kv_store_ring",
+               64,
+               {{"qkv", "read", "f32"},
+                {"cos", "read", "f32"},
+                {"sin", "read", "f32"},
+                {"pos", "read", "u32"},
+                {"slot", "read", "u32"},
+                {"k_cache", "read_write", "f32"},
+                {"v_cache", "read_write", "f32"}},
+               {dim("m", 1, 65535), dim("kv_heads", 1, 1024), dim("d", 2, 2048, 2), dim("length", 1, kMax),
+                u32("rotated"), u32("ldq"), u32("k_off"), u32("v_off")},
+               l_kv_store});
+  t.push_back({"attend_split",
+               128,
+               {{"qkv", "read", "f32"},
+                {"cos", "read", "f32"},
+                {"sin", "read", "f32"},
+                {"pos", "read", "u32"},
+                {"slot", "read", "u32"},
+                {"k_cache", "read", "f32"},
+                {"v_cache", "read", "f32"},
+                {"part_m", "write", "f32"},
+                {"part_l", "write", "f32"},
+                {"part_acc", "write", "f32"}},
+               {dim("m", 1, 65535), dim("heads", 1, 1024), dim("kv_heads", 1, 1024), dim("d", 128, 128),
+                dim("length", 1, kMax), u32("rotated"), dim("chunk", 1, 256), dim("max_splits", 1, 65535), u32("ldq"),
+                u32("q_off"), f32("scale")},
+               l_attend});
+  t.push_back({"attend_combine",
+               128,
+               {{"part_m", "read", "f32"},
+                {"part_l", "read", "f32"},
+                {"part_acc", "read", "f32"},
+                {"pos", "read", "u32"},
+                {"out", "write", "f32"}},
+               {dim("m", 1, 65535), dim("heads", 1, 1024), dim("d", 1, 1024), dim("chunk", 1, 256),
+                dim("max_splits", 1, 65535), u32("ldo")},
+               l_combine});
+  t.push_back({"gather",
+               256,
+               {{"table", "read", "f32"}, {"tokens", "read", "u32"}, {"y", "write", "f32"}},
+               {dim("width", 4, 1048576, 4), dim("m", 1, 65535), f32("factor")},
+               l_gather});
+  t.push_back({"argmax",
+               1024,
+               {{"x", "read", "f32"}, {"ids", "write", "u32"}},
+               {dim("m", 1, 65535), dim("n", 1, kMax), u32("ldx")},
+               l_argmax});
+  t.push_back({"rope",
+               64,
+               {{"x", "read", "f32"}, {"pos", "read", "u32"}, {"cos", "read", "f32"}, {"sin", "read", "f32"},
+                {"y", "write", "f32"}},
+               {dim("m", 1, 65535), dim("heads", 1, 65535), dim("d", 2, 2048, 2), u32("rotated"), u32("ldx"),
+                u32("ldy")},
+               l_rope});
+  t.push_back({"add",
+               256,
+               {{"a", "read", "f32"}, {"b", "read", "f32"}, {"y", "write", "f32"}},
+               {dim("n", 1, kMax)},
+               l_add});
+  t.push_back({"silu_mul",
+               256,
+               {{"a", "read", "f32"}, {"b", "read", "f32"}, {"y", "write", "f32"}},
+               {dim("n", 1, kMax)},
+               l_silu_mul});
+  // The C layout (Abi.hs:113-133) and the canonical text (Abi.hs:136-159).
+  for (auto& k : t) {
+    uint32_t off = 0, align = 1;
+    for (auto& p : k.params) {
+      const uint32_t size = 4;
+      off = (off + size - 1) / size * size;
+      k.offsets.push_back(off);
+      off += size;
+      if (size > align) align = size;
+    }
+    k.params_size = k.params.empty() ? 0 : (off + align - 1) / align * align;
+    std::string a = "abi 1\n";
+    for (auto& b : k.bufs) a += std::string("buffer ") + b.name + " " + b.access + " " + b.type + " align 16\n";
+    for (size_t i = 0; i < k.params.size(); ++i)
+      a += std::string("param ") + k.params[i].name + " " + k.params[i].type + " at " + std::to_string(k.offsets[i]) +
+           "\n";
+    a += "params size " + std::to_string(k.params_size) + "\n";
+    k.abi = a;
+    k.hash = fnv1a(a.data(), a.size());
+  }
+  return t;
+}
+
+const std::vector<KernelSpec>& table() {
+  static std::vector<KernelSpec> t = make_table();
+  return t;
+}
+
+std::string range_text(const ParamSpec& p) {
+  std::string s = std::to_string(p.lo) + ".." + std::to_string(p.hi);
+  if (p.mult > 1) s += " multiple of " + std::to_string(p.mult);
+  return s;
+}
+
+}  // namespace
+
+extern "C" uint64_t fkc_fnv1a64(const void* bytes, size_t n) { return fnv1a(bytes, n); }
+
+extern "C" int fkc_kernel_count(void) { return (int)table().size(); }
+
+extern "C" int fkc_kernel_describe(int id, const char** name, const char** abi, uint64_t* hash, uint32_t* threads,
+                                   uint32_t* params_size, uint32_t* buffers) {
+  const auto& t = table();
+  if (id < 0 || id >= (int)t.size()) return fail(FKC_ERR_ARGUMENT, "fkc_kernel_describe: no kernel %d.", id);
+  const KernelSpec& k = t[id];
+  if (name) *name = k.name;
+  if (abi) *abi = k.abi.c_str();
+  if (hash) *hash = k.hash;
+  if (threads) *threads = k.threads;
+  if (params_size) *params_size = k.params_size;
+  if (buffers) *buffers = (uint32_t)k.bufs.size();
+  return FKC_OK;
+}
+
+extern "C" int fkc_kernel_find(const char* name, uint64_t abi_hash, int* id) {
+  if (!name || !id) return fail(FKC_ERR_ARGUMENT, "fkc_kernel_find: null argument.");
+  const auto& t = table();
+  for (size_t i = 0; i < t.size(); ++i) {
+    if (strcmp(t[i].name, name) != 0) continue;
+    if (t[i].hash != abi_hash)
+      return fail(FKC_ERR_ARGUMENT,
+                  "The kernel %s has another ABI than the target's %s: hash 0x%016llx where the target has "
+                  "0x%016llx.",
+                  name, t[i].name, (unsigned long long)abi_hash, (unsigned long long)t[i].hash);
+    *id = (int)i;
+    return FKC_OK;
+  }
+  return fail(FKC_ERR_ARGUMENT, "The target has no kernel %s.", name);
+}
+
+extern "C" int fkc_launch(fkc_ctx* c, int kernel, const void* params, size_t params_len, void* const* bufs,
+                          int nbufs) {
+  if (!c) return fail(FKC_ERR_ARGUMENT, "fkc_launch: null context.");
+  const auto& t = table();
+  if (kernel < 0 || kernel >= (int)t.size()) return fail(FKC_ERR_ARGUMENT, "fkc_launch: no kernel %d.", kernel);
+  const KernelSpec& k = t[kernel];
+  if (params_len != k.params_size)
+    return fail(FKC_ERR_ARGUMENT, "%s: the parameter struct is %zu bytes, not %u.", k.name, params_len,
+                k.params_size);
+  if (nbufs != (int)k.bufs.size())
+    return fail(FKC_ERR_ARGUMENT, "%s: %d buffers bound, not %zu.", k.name, nbufs, k.bufs.size());
+  for (int i = 0; i < nbufs; ++i)
+    if (!bufs[i] || ((uintptr_t)bufs[i] & 15u))
+      return fail(FKC_ERR_ARGUMENT, "%s: buffer %s is %s.", k.name, k.bufs[i].name,
+                  bufs[i] ? "not aligned to 16 bytes" : "null");
+  Params p{(const unsigned char*)params, &k.offsets};
+  // The dimensions' ranges first, as the CPU target's asserts (Emit/Rust.hs:94-104).
+  for (size_t i = 0; i < k.params.size(); ++i) {
+    const ParamSpec& s = k.params[i];
+    if (!s.dim) continue;
+    const uint32_t v = p.u((int)i);
+    if (v < s.lo || v > s.hi || (s.mult > 1 && v % s.mult != 0))
+      return fail(FKC_ERR_ARGUMENT, "%s: the dimension %s is %u, outside its range %s.", k.name, s.name, v,
+                  range_text(s).c_str());
+  }
+  cudaSetDevice(c->device);
+  return k.launch(c, p, bufs);
+}
+
+// ---------------------------------------------------------------------------
+// Graphs
+
+extern "C" int fkc_capture_begin(fkc_ctx* c) {
+  if (!c) return fail(FKC_ERR_ARGUMENT, "fkc_capture_begin: null context.");
+  if (c->capturing) return fail(FKC_ERR_STATE, "fkc_capture_begin: a capture is open.");
+  cudaSetDevice(c->device);
+  FKC_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeRelaxed), "fkc_capture_begin");
+  c->capturing = true;
+  return FKC_OK;
+}
+
+extern "C" int fkc_capture_end(fkc_ctx* c, fkc_graph** out) {
+  if (!c || !out) return fail(FKC_ERR_ARGUMENT, "fkc_capture_end: null argument.");
+  if (!c->capturing) return fail(FKC_ERR_STATE, "fkc_capture_end: no capture is open.");
+  cudaSetDevice(c->device);
+  c->capturing = false;
+  fkc_graph* g = new fkc_graph;
+  g->device = c->device;
+  cudaError_t e = cudaStreamEndCapture(c->stream, &g->graph);
+  if (e == cudaSuccess) e = cudaGraphInstantiate(&g->exec, g->graph, 0);
+  if (e == cudaSuccess) e = cudaGraphUpload(g->exec, c->stream);
+  if (e != cudaSuccess) {
+    fkc_graph_destroy(g);
+    return cuda_fail(e, "fkc_capture_end");
+  }
+  *out = g;
+  return FKC_OK;
+}
+
+extern "C" int fkc_graph_launch(fkc_ctx* c, fkc_graph* g) {
+  if (!c || !g) return fail(FKC_ERR_ARGUMENT, "fkc_graph_launch: null argument.");
+  cudaSetDevice(c->device);
+  FKC_CUDA(cudaGraphLaunch(g->exec, c->stream), "fkc_graph_launch");
+  return FKC_OK;
+}
+
+extern "C" int fkc_graph_destroy(fkc_graph* g) {
+  if (!g) return FKC_OK;
+  cudaSetDevice(g->device);
+  if (g->exec) cudaGraphExecDestroy(g->exec);
+  if (g->graph) cudaGraphDestroy(g->graph);
+  delete g;
+  return FKC_OK;
+}
+
+extern "C" int fkc_step(fkc_ctx* c, fkc_graph* g, const void* host_in, void* dev_in, size_t in_bytes,
+                        void* host_out, const void* dev_out, size_t out_bytes) {
+  if (!c || !g) return fail(FKC_ERR_ARGUMENT, "fkc_step: null argument.");
+  cudaSetDevice(c->device);
+  if (in_bytes) FKC_CUDA(cudaMemcpyAsync(dev_in, host_in, in_bytes, cudaMemcpyHostToDevice, c->stream), "fkc_step: in");
+  FKC_CUDA(cudaGraphLaunch(g->exec, c->stream), "fkc_step: replay");
+  if (out_bytes)
+    FKC_CUDA(cudaMemcpyAsync(host_out, dev_out, out_bytes, cudaMemcpyDeviceToHost, c->stream), "fkc_step: out");
+  FKC_CUDA(cudaStreamSynchronize(c->stream), "fkc_step: sync");
+  return FKC_OK;
+}
+
+extern "C" int fkc_time_graph(fkc_ctx* c, fkc_graph* g, int warmup, int iters, float* ms) {
+  if (!c || !g || !ms || iters <= 0) return fail(FKC_ERR_ARGUMENT, "fkc_time_graph: bad argument.");
+  cudaSetDevice(c->device);
+  for (int i = 0; i < warmup; ++i) FKC_CUDA(cudaGraphLaunch(g->exec, c->stream), "fkc_time_graph");
+  cudaEvent_t a, b;
+  FKC_CUDA(cudaEventCreate(&a), "fkc_time_graph");
+  FKC_CUDA(cudaEventCreate(&b), "fkc_time_graph");
+  FKC_CUDA(cudaStreamSynchronize(c->stream), "fkc_time_graph");
+  cudaEventRecord(a, c->stream);
+  for (int i = 0; i < iters; ++i) FKC_CUDA(cudaGraphLaunch(g->exec, c->stream), "fkc_time_graph");
+  cudaEventRecord(b, c->stream);
+  cudaError_t e = cudaEventSynchronize(b);
+  if (e == cudaSuccess) e = cudaEventElapsedTime(ms, a, b);
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  if (e != cudaSuccess) return cuda_fail(e, "fkc_time_graph");
+  return FKC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// NCCL
+
+static int nccl_fail(ncclResult_t r, const char* what) {
+  return fail(FKC_ERR_NCCL, "%s: %s", what, ncclGetErrorString(r));
+}
+
+extern "C" int fkc_comm_unique_id(void* id128) {
+  if (!id128) return fail(FKC_ERR_ARGUMENT, "fkc_comm_unique_id: null argument.");
+  static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId is 128 bytes");
+  ncclUniqueId id;
+  ncclResult_t r = ncclGetUniqueId(&id);
+  if (r != ncclSuccess) return nccl_fail(r, "fkc_comm_unique_id");
+  memcpy(id128, &id, sizeof id);
+  return FKC_OK;
+}
+
+extern "C" int fkc_comm_init(fkc_ctx* c, int nranks, int rank, const void* id128) {
+  if (!c || !id128 || nranks < 1 || rank < 0 || rank >= nranks)
+    return fail(FKC_ERR_ARGUMENT, "fkc_comm_init: bad argument.");
+  if (c->comm) return fail(FKC_ERR_STATE, "fkc_comm_init: the context has a communicator.");
+  cudaSetDevice(c->device);
+  ncclUniqueId id;
+  memcpy(&id, id128, sizeof id);
+  ncclResult_t r = ncclCommInitRank(&c->comm, nranks, id, rank);
+  if (r != ncclSuccess) {
+    c->comm = nullptr;
+    return nccl_fail(r, "fkc_comm_init");
+  }
+  c->nranks = nranks;
+  c->rank = rank;
+  return FKC_OK;
+}
+
+extern "C" int fkc_allreduce_sum_f32(fkc_ctx* c, void* dptr, size_t count) {
+  if (!c || (count && !dptr)) return fail(FKC_ERR_ARGUMENT, "fkc_allreduce_sum_f32: null argument.");
+  if (!c->comm) return fail(FKC_ERR_STATE, "fkc_allreduce_sum_f32: no communicator.");
+  cudaSetDevice(c->device);
+  ncclResult_t r = ncclAllReduce(dptr, dptr, count, ncclFloat32, ncclSum, c->comm, c->stream);
+  if (r != ncclSuccess) return nccl_fail(r, "fkc_allreduce_sum_f32");
+  return FKC_OK;
+}
+
+extern "C" int fkc_comm_destroy(fkc_ctx* c) {
+  if (!c) return fail(FKC_ERR_ARGUMENT, "fkc_comm_destroy: null context.");
+  if (c->comm) {
+    ncclResult_t r = ncclCommDestroy(c->comm);
+    c->comm = nullptr;
+    if (r != ncclSuccess) return nccl_fail(r, "fkc_comm_destroy");
+  }
+  return FKC_OK;
+}

@@ -1,0 +1,363 @@
+"""TEST INFRASTRUCTURE -- the CPU oracle, not part of the product.
+
+ctypes access to ``oracle/_build/libfko.so``: a C restatement of what the
+reference's CPU target (src/FuryKernel/Cpu.hs) computes for this path's spec
+kernels (``fko_*``) and of the f64 evaluator with its binary32 bounds
+(src/FuryKernel/Program/Eval.hs, ``fkr_*``). Only ``tests/``,
+``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline and reference
+arms import this module, as the checker and as the timed CPU baseline; the
+``furykernel_b200`` package never does.
+
+Parity pins: the generator is the SplitMix finaliser of
+test/cpu/Cases.hs:885-892; the reduction orders are pinned by the known
+answers of test/Test/FuryKernel/InterpTest.hs:50-58 and ReduceTest.hs:46-59
+(tests/test_oracle_pins.py). The reference itself cannot run here (no GHC,
+no rustc), so no output of the reference pins this restatement beyond those.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "libfko.so")
+_lib = None
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_f64p = np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")
+_u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_u64 = ctypes.c_uint64
+_u32 = ctypes.c_uint32
+_int = ctypes.c_int
+_f32 = ctypes.c_float
+_f64 = ctypes.c_double
+
+
+def build() -> str:
+    """Compile the restatement with its Makefile (strict IEEE flags)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        sig = {
+            "fko_random": (_u64, [_u64, _u64]),
+            "fko_fill_uniform": (None, [_u64, _u64, _f64, _f64, _f32p]),
+            "fko_fill_normal": (None, [_u64, _u64, _f64, _f64, _f32p]),
+            "fko_fill_ints": (None, [_u64, _u64, _u32, _u32p]),
+            "fko_max": (_f32, [_f32, _f32]),
+            "fko_min": (_f32, [_f32, _f32]),
+            "fko_simd_sum": (_f32, [_f32p, _int]),
+            "fko_simd_max": (_f32, [_f32p, _int]),
+            "fko_tg_reduce_sum": (_f32, [_f32p, _int]),
+            "fko_tg_reduce_max": (_f32, [_f32p, _int]),
+            "fko_reduce_pass1": (None, [_f32p, _u64, _f32p, _int]),
+            "fko_reduce_pass2": (None, [_f32p, _u32, _f32p]),
+            "fko_reduce_sum": (_f32, [_f32p, _u64, _int]),
+            "fko_rmsnorm_rows": (None, [_f32p, _u32, _u32, ctypes.c_void_p, _f32, _f32, _f32p, _int]),
+            "fko_softmax_rows": (None, [_f32p, _u32, _u32, _f32p, _int]),
+            "fko_gemv": (None, [_f32p, _u32, _u32, _f32p, _u32, _u32, _f32p, _int]),
+            "fko_rope_tables": (None, [_f64, _u32, _u32, _u32, _f32p, _f32p]),
+            "fko_rope": (None, [_f32p, _u32, _u32, _u32, _u32, _u32p, _f32p, _f32p, _f32p]),
+            "fko_kv_store_ring": (None, [_f32p, _u32, _u32, _u32, _u32, _u32p, _u32p, _f32p]),
+            "fko_attend_split": (None, [_f32p, _u32, _u32, _u32, _u32, _u32, _u32p, _u32p, _f32p, _f32p,
+                                        _f32, _u32, _u32, _u32, _f32p, _f32p, _f32p, _int]),
+            "fko_attend_combine": (None, [_u32, _u32, _u32, _u32p, _u32, _u32, _f32p, _f32p, _f32p, _f32p]),
+            "fko_silu_mul": (None, [_f32p, _f32p, _u64, _f32p]),
+            "fko_add": (None, [_f32p, _f32p, _u64, _f32p]),
+            "fko_gather": (None, [_f32p, _u32, _u32p, _u32, _f32, _f32p]),
+            "fko_argmax": (None, [_f32p, _u32, _u32, _u32p]),
+            "fkr_settle": (_f64, [_f64, _f64]),
+            "fkr_widened": (_f64, [_f64]),
+            "fkr_input": (None, [_f32p, _u64, _f64p, _f64p]),
+            "fkr_linear": (None, [_f32p, _u32, _u32, _f64p, _f64p, _u32, _f64p, _f64p, _int]),
+            "fkr_rmsnorm": (None, [_f64p, _f64p, _u32, _u32, _u32, ctypes.c_void_p, _f64, _f64, _f64p, _f64p]),
+            "fkr_add": (None, [_f64p, _f64p, _f64p, _f64p, _u64, _f64p, _f64p]),
+            "fkr_silu_mul": (None, [_f64p, _f64p, _f64p, _f64p, _u64, _f64p, _f64p]),
+            "fkr_rope": (None, [_f64p, _f64p, _u32, _u32, _u32, _u32, _f64, _u32p, _f64p, _f64p]),
+            "fkr_attend": (None, [_f64p, _f64p, _u32, _u32, _u32, _u32, _u32, _u32p, _u32p,
+                                  _f64p, ctypes.c_void_p, _f64p, ctypes.c_void_p, _f64, _f64p, _f64p, _int]),
+            "fkr_gather": (None, [_f32p, _u32, _u32p, _u32, _f64, _f64p, _f64p]),
+            "fkr_argmax": (None, [_f64p, _f64p, _u32, _u32, _u32p, _i32p]),
+            "fkr_softmax": (None, [_f64p, _f64p, _u32, _u32, _f64p, _f64p]),
+            "fkr_sum": (None, [_f32p, _u64, ctypes.POINTER(_f64), ctypes.POINTER(_f64)]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def threads_default() -> int:
+    return os.cpu_count() or 1
+
+
+# ---------------------------------------------------------------------------
+# Seeded inputs
+
+
+def uniform(seed: int, n: int, a: float = -1.0, b: float = 1.0) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    lib().fko_fill_uniform(seed, n, a, b, out)
+    return out
+
+
+def normal(seed: int, n: int, mu: float = 0.0, sigma: float = 1.0) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    lib().fko_fill_normal(seed, n, mu, sigma, out)
+    return out
+
+
+def ints(seed: int, n: int, bound: int) -> np.ndarray:
+    out = np.empty(n, np.uint32)
+    lib().fko_fill_ints(seed, n, bound, out)
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Spec kernels, CPU-target semantics
+
+
+def _c(a, dt):
+    return np.ascontiguousarray(a, dtype=dt)
+
+
+def reduce_sum(x, threads: int = 1) -> np.float32:
+    x = _c(x, np.float32)
+    return np.float32(lib().fko_reduce_sum(x, x.size, threads))
+
+
+def reduce_partials(x, threads: int = 1) -> np.ndarray:
+    x = _c(x, np.float32)
+    p = np.empty((x.size + 255) // 256, np.float32)
+    lib().fko_reduce_pass1(x, x.size, p, threads)
+    return p
+
+
+def rmsnorm_rows(x, gamma, eps: float, factor: float = 1.0, threads: int = 1) -> np.ndarray:
+    x = _c(x, np.float32)
+    rows, h = x.shape
+    y = np.empty_like(x)
+    g = None if gamma is None else _c(gamma, np.float32)
+    lib().fko_rmsnorm_rows(x, rows, h, None if g is None else g.ctypes.data, eps, factor, y, threads)
+    return y
+
+
+def softmax_rows(x, threads: int = 1) -> np.ndarray:
+    x = _c(x, np.float32)
+    y = np.empty_like(x)
+    lib().fko_softmax_rows(x, x.shape[0], x.shape[1], y, threads)
+    return y
+
+
+def gemv(w, x, split: int = 1, threads: int = 1) -> np.ndarray:
+    w = _c(w, np.float32)
+    x = _c(x, np.float32)
+    n, k = w.shape
+    x2 = x.reshape(-1, k)
+    y = np.empty((x2.shape[0], n), np.float32)
+    lib().fko_gemv(w, n, k, x2, x2.shape[0], split, y, threads)
+    return y
+
+
+def rope_tables(theta: float, d: int, rotated: int, positions: int):
+    c = np.empty((positions, rotated), np.float32)
+    s = np.empty((positions, rotated), np.float32)
+    lib().fko_rope_tables(theta, d, rotated, positions, c, s)
+    return c, s
+
+
+def rope(x, heads: int, d: int, rotated: int, pos, cos_t, sin_t) -> np.ndarray:
+    x = _c(x, np.float32)
+    m = x.shape[0]
+    y = np.empty_like(x)
+    lib().fko_rope(x, m, heads, d, rotated, _c(pos, np.uint32), _c(cos_t, np.float32), _c(sin_t, np.float32), y)
+    return y
+
+
+def kv_store_ring(x, kv_heads: int, d: int, length: int, pos, slot, cache: np.ndarray) -> None:
+    x = _c(x, np.float32)
+    assert cache.dtype == np.float32 and cache.flags.c_contiguous
+    lib().fko_kv_store_ring(x, x.shape[0], kv_heads, d, length, _c(pos, np.uint32), _c(slot, np.uint32), cache)
+
+
+def attend(q, heads, kv_heads, d, length, pos, slot, kc, vc, scale, chunk, warps, max_splits, threads=1):
+    """Split attention then its combine, the CUDA kernels' order."""
+    q = _c(q, np.float32)
+    m = q.shape[0]
+    pos = _c(pos, np.uint32)
+    slot = _c(slot, np.uint32)
+    pm = np.zeros(m * heads * max_splits, np.float32)
+    pl = np.zeros(m * heads * max_splits, np.float32)
+    pa = np.zeros(m * heads * max_splits * d, np.float32)
+    lib().fko_attend_split(q, m, heads, kv_heads, d, length, pos, slot, _c(kc, np.float32), _c(vc, np.float32),
+                           scale, chunk, warps, max_splits, pm, pl, pa, threads)
+    out = np.empty((m, heads * d), np.float32)
+    lib().fko_attend_combine(m, heads, d, pos, chunk, max_splits, pm, pl, pa, out)
+    return out, (pm, pl, pa)
+
+
+def silu_mul(a, b) -> np.ndarray:
+    a = _c(a, np.float32)
+    y = np.empty_like(a)
+    lib().fko_silu_mul(a, _c(b, np.float32), a.size, y)
+    return y
+
+
+def add(a, b) -> np.ndarray:
+    a = _c(a, np.float32)
+    y = np.empty_like(a)
+    lib().fko_add(a, _c(b, np.float32), a.size, y)
+    return y
+
+
+def gather(table, tokens, factor: float = 1.0) -> np.ndarray:
+    table = _c(table, np.float32)
+    tokens = _c(tokens, np.uint32)
+    width = table.shape[1]
+    y = np.empty((tokens.size, width), np.float32)
+    lib().fko_gather(table, width, tokens, tokens.size, factor, y)
+    return y
+
+
+def argmax(x) -> np.ndarray:
+    x = _c(x, np.float32)
+    m, n = x.shape
+    ids = np.empty(m, np.uint32)
+    lib().fko_argmax(x, m, n, ids)
+    return ids
+
+
+# ---------------------------------------------------------------------------
+# The f64 referee: (values, bounds) pairs
+
+
+def r_input(x):
+    x = _c(x, np.float32)
+    v = np.empty(x.shape, np.float64)
+    b = np.empty(x.shape, np.float64)
+    lib().fkr_input(x, x.size, v, b)
+    return v, b
+
+
+def r_linear(w, xv, threads: int = 0):
+    w = _c(w, np.float32)
+    x, xb = (_c(a, np.float64) for a in xv)
+    n, k = w.shape
+    m = x.size // k
+    y = np.empty((m, n), np.float64)
+    yb = np.empty((m, n), np.float64)
+    lib().fkr_linear(w, n, k, x, xb, m, y, yb, threads or threads_default())
+    return y, yb
+
+
+def r_rmsnorm(xv, seg: int, gamma, eps: float, factor: float = 1.0):
+    x, xb = (_c(a, np.float64) for a in xv)
+    m, width = x.shape
+    y = np.empty_like(x)
+    yb = np.empty_like(x)
+    g = None if gamma is None else _c(gamma, np.float32)
+    lib().fkr_rmsnorm(x, xb, m, width, seg, None if g is None else g.ctypes.data, eps, factor, y, yb)
+    return y, yb
+
+
+def r_add(av, cv):
+    a, ab = (_c(t, np.float64) for t in av)
+    c, cb = (_c(t, np.float64) for t in cv)
+    y = np.empty_like(a)
+    yb = np.empty_like(a)
+    lib().fkr_add(a, ab, c, cb, a.size, y, yb)
+    return y, yb
+
+
+def r_silu_mul(av, cv):
+    a, ab = (_c(t, np.float64) for t in av)
+    c, cb = (_c(t, np.float64) for t in cv)
+    y = np.empty_like(a)
+    yb = np.empty_like(a)
+    lib().fkr_silu_mul(a, ab, c, cb, a.size, y, yb)
+    return y, yb
+
+
+def r_rope(xv, d: int, rotated: int, theta: float, pos):
+    x, xb = (_c(t, np.float64) for t in xv)
+    m, width = x.shape
+    y = np.empty_like(x)
+    yb = np.empty_like(x)
+    lib().fkr_rope(x, xb, m, width, d, rotated, theta, _c(pos, np.uint32), y, yb)
+    return y, yb
+
+
+def r_attend(qv, heads, kv_heads, d, length, pos, slot, kc, vc, scale, kcb=None, vcb=None, threads: int = 0):
+    q, qb = (_c(t, np.float64) for t in qv)
+    m = q.shape[0]
+    kc = _c(kc, np.float64)
+    vc = _c(vc, np.float64)
+    kcb = None if kcb is None else _c(kcb, np.float64)
+    vcb = None if vcb is None else _c(vcb, np.float64)
+    y = np.empty((m, heads * d), np.float64)
+    yb = np.empty((m, heads * d), np.float64)
+    lib().fkr_attend(q, qb, m, heads, kv_heads, d, length, _c(pos, np.uint32), _c(slot, np.uint32),
+                     kc, None if kcb is None else kcb.ctypes.data, vc, None if vcb is None else vcb.ctypes.data,
+                     scale, y, yb, threads or threads_default())
+    return y, yb
+
+
+def r_gather(table, tokens, factor: float = 1.0):
+    table = _c(table, np.float32)
+    tokens = _c(tokens, np.uint32)
+    width = table.shape[1]
+    y = np.empty((tokens.size, width), np.float64)
+    yb = np.empty((tokens.size, width), np.float64)
+    lib().fkr_gather(table, width, tokens, tokens.size, factor, y, yb)
+    return y, yb
+
+
+def r_argmax(xv):
+    x, xb = (_c(t, np.float64) for t in xv)
+    m, n = x.shape
+    ids = np.empty(m, np.uint32)
+    dec = np.empty(m, np.int32)
+    lib().fkr_argmax(x, xb, m, n, ids, dec)
+    return ids, dec.astype(bool)
+
+
+def r_softmax(xv):
+    x, xb = (_c(t, np.float64) for t in xv)
+    m, n = x.shape
+    y = np.empty_like(x)
+    yb = np.empty_like(x)
+    lib().fkr_softmax(x, xb, m, n, y, yb)
+    return y, yb
+
+
+def r_sum(x):
+    x = _c(x, np.float32)
+    y = _f64()
+    yb = _f64()
+    lib().fkr_sum(x, x.size, ctypes.byref(y), ctypes.byref(yb))
+    return y.value, yb.value
+
+
+def widened(b):
+    return b * (1.0 + 2.0 ** -20)
+
+
+def within(got, exact_bound) -> np.ndarray:
+    """Elementwise: got lies within the widened bound of the exact value
+    (the comparison of Eval.hs:940-944, for binary32 values)."""
+    v, b = exact_bound
+    got = np.asarray(got, np.float64)
+    return (np.abs(got - v) <= widened(b)) | (np.isnan(got) & np.isnan(v)) | np.isinf(b)

@@ -1,0 +1,332 @@
+"""Parity of each CUDA kernel with the oracle, through the C ABI, on a B200.
+
+The CUDA kernels keep the spec kernels' arithmetic order, so most outputs
+are compared bit for bit with the oracle's restatement of the reference CPU
+target (oracle/fko_cpu.c). Every f32 output is also checked against the f64
+evaluator's per-element bound (oracle/fko_eval.c, Eval.hs), and, per the
+path's tolerances, by its normwise relative error against the f64 value:
+max |gpu - exact| / max |exact| <= 1e-5 for elementwise and norm kernels,
+<= 1e-4 for reductions, GEMV and attention.
+"""
+
+import math
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+THREADS = O.threads_default()
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    from furykernel_b200 import _native as N
+
+    c = N.Context(0)
+    yield c
+    c.close()
+
+
+def rel_err(got, exact):
+    got = np.asarray(got, np.float64)
+    return float(np.max(np.abs(got - exact)) / max(np.max(np.abs(exact)), 1e-300))
+
+
+def same_bits(a, b):
+    a = np.ascontiguousarray(a, np.float32).view(np.uint32)
+    b = np.ascontiguousarray(b, np.float32).view(np.uint32)
+    return a.shape == b.shape and np.array_equal(a, b)
+
+
+# ---------------------------------------------------------------------------
+# Config 1: the threadgroup tree reduction
+
+
+def run_reduce(ctx, x):
+    xd = ctx.to_device(x)
+    groups = (x.size + 255) // 256
+    part = ctx.empty(groups)
+    y = ctx.empty(1)
+    ctx.launch("reduce_groups", {"n": x.size}, [xd, part])
+    ctx.launch("reduce_final", {"count": groups}, [part, y])
+    out = y.download()[0], part.download()
+    for b in (xd, part, y):
+        b.free()
+    return out
+
+
+@pytest.mark.parametrize("n", [1, 255, 256, 65536, 65536 + 17, 16_777_216])
+def test_reduce_bit_exact(ctx, n):
+    x = O.uniform(2026 + n, n, -1.0, 1.0)
+    got, part = run_reduce(ctx, x)
+    assert same_bits(part, O.reduce_partials(x, THREADS))
+    want = O.reduce_sum(x, THREADS)
+    assert same_bits([got], [want]), (got, want)
+    exact, bound = O.r_sum(x)
+    assert abs(float(got) - exact) <= O.widened(bound)
+
+
+def test_reduce_of_negative_zeros_is_negative_zero(ctx):
+    got, _ = run_reduce(ctx, np.full(1000, -0.0, np.float32))
+    assert np.float32(got).view(np.uint32) == 0x80000000
+
+
+def test_reduce_known_order(ctx):
+    # 2^24 at element 0 and ones at 16 and 17 of a group: the halving tree
+    # meets the two ones first only where the tree says (spec of config 1).
+    x = np.zeros(256, np.float32)
+    x[0] = 2.0 ** 24
+    x[1] = x[129] = 1.0  # halving by 128 adds them first: 2 + 2^24 survives
+    got, _ = run_reduce(ctx, x)
+    assert got == O.reduce_sum(x) == np.float32(2.0 ** 24 + 2)
+
+
+# ---------------------------------------------------------------------------
+# Config 2: RMSNorm then softmax over rows
+
+
+@pytest.mark.parametrize("rows,h", [(3, 1000), (64, 4096), (4096, 4096)])
+def test_rmsnorm_softmax_rows(ctx, rows, h):
+    x = O.normal(11, rows * h).reshape(rows, h)
+    gamma = O.uniform(12, h, 0.5, 1.5)
+    xd, gd = ctx.to_device(x), ctx.to_device(gamma)
+    yd, zd = ctx.empty((rows, h)), ctx.empty((rows, h))
+    ctx.launch("rmsnorm_rows", {"rows": rows, "h": h, "eps": 1e-5, "factor": 1.0}, [xd, gd, yd])
+    ctx.launch("softmax_rows", {"rows": rows, "h": h}, [yd, zd])
+    y, z = yd.download(), zd.download()
+    y_cpu = O.rmsnorm_rows(x, gamma, 1e-5, 1.0, THREADS)
+    assert same_bits(y, y_cpu)
+    z_cpu = O.softmax_rows(y_cpu, THREADS)
+    # exp is binary64's on both sides, rounded once: CUDA's and glibc's
+    # binary64 exp may round an element differently; none did on the seeds here.
+    assert same_bits(z, z_cpu)
+    if rows <= 64:
+        ref = O.r_rmsnorm(O.r_input(x), h, gamma, 1e-5)
+        assert O.within(y, ref).all()
+        assert rel_err(y, ref[0]) <= 1e-5
+        sref = O.r_softmax(O.r_input(y))
+        assert O.within(z, sref).all()
+        assert rel_err(z, sref[0]) <= 1e-5
+    for b in (xd, gd, yd, zd):
+        b.free()
+
+
+# ---------------------------------------------------------------------------
+# Config 3a/3b: GEMV, and the plan's prologue and epilogue variants
+
+
+@pytest.mark.parametrize("n,k,m,split", [(11008, 4096, 1, 1), (11008, 4096, 16, 1), (4096, 11008, 1, 2),
+                                         (300, 1000, 3, 4), (257, 4096, 32, 8)])
+def test_gemv_bit_exact(ctx, n, k, m, split):
+    w = O.normal(21, n * k, 0.0, 0.02).reshape(n, k)
+    x = O.normal(22, m * k).reshape(m, k)
+    wd, xd, yd = ctx.to_device(w), ctx.to_device(x), ctx.empty((m, n))
+    ctx.launch("gemv", {"n": n, "k": k, "m": m, "split": split, "ldx": k, "ldy": n}, [wd, xd, yd])
+    y = yd.download()
+    assert same_bits(y, O.gemv(w, x, split, THREADS))
+    if n * k * m <= 11008 * 4096:
+        ref = O.r_linear(w, O.r_input(x))
+        assert O.within(y, ref).all()
+        assert rel_err(y, ref[0]) <= 1e-4
+    for b in (wd, xd, yd):
+        b.free()
+
+
+def test_gemv_prologues_and_epilogue(ctx):
+    n, k, m = 1000, 2048, 4
+    w = O.normal(31, n * k, 0.0, 0.02).reshape(n, k)
+    x = O.normal(32, m * k).reshape(m, k)
+    g = O.uniform(33, k, 0.5, 1.5)
+    r = O.normal(34, m * n).reshape(m, n)
+    gu = O.normal(35, m * 2 * k).reshape(m, 2 * k)
+    wd, xd, gd, rd, gud = (ctx.to_device(a) for a in (w, x, g, r, gu))
+    yd = ctx.empty((m, n))
+    base = {"n": n, "k": k, "m": m, "split": 2, "ldx": k, "ldy": n}
+    # RMSNorm recomputed before the anchor.
+    ctx.launch("gemv_rmsnorm", dict(base, eps=1e-5, factor=1.0), [wd, xd, gd, yd])
+    want = O.gemv(w, O.rmsnorm_rows(x, g, 1e-5), 2, THREADS)
+    assert same_bits(yd.download(), want)
+    # The residual added on the tile.
+    ctx.launch("gemv_add", dict(base, ldr=n), [wd, xd, rd, yd])
+    assert same_bits(yd.download(), O.add(r, O.gemv(w, x, 2, THREADS)))
+    # SiLU-gate recomputed from a stored gate/up row, then the residual.
+    ctx.launch("gemv_silu_add", dict(base, ldx=2 * k, ldr=n, up_off=k), [wd, gud, rd, yd])
+    act = O.silu_mul(gu[:, :k], gu[:, k:])
+    assert same_bits(yd.download(), O.add(r, O.gemv(w, act, 2, THREADS)))
+    ctx.launch("gemv_silu", dict(base, ldx=2 * k, up_off=k), [wd, gud, yd])
+    assert same_bits(yd.download(), O.gemv(w, act, 2, THREADS))
+    for b in (wd, xd, gd, rd, gud, yd):
+        b.free()
+
+
+# ---------------------------------------------------------------------------
+# The decode attention path: KV store, split attention, combine
+
+
+@pytest.mark.parametrize("m,heads,kv_heads,length,positions,chunk", [
+    (2, 4, 2, 64, [5, 40], 16),
+    (3, 8, 8, 300, [0, 129, 299], 64),
+    (1, 32, 32, 2304, [2048], 128),
+    (4, 4, 4, 40, [45, 3, 39, 80], 32),  # positions past the ring's length wrap
+])
+def test_attention_path(ctx, m, heads, kv_heads, length, positions, chunk):
+    d = 128
+    slots = m
+    width = (heads + 2 * kv_heads) * d
+    qkv = O.normal(41, m * width).reshape(m, width)
+    pos = np.array(positions, np.uint32)
+    slot = np.arange(m, dtype=np.uint32)[::-1].copy()
+    kc = O.normal(42, slots * kv_heads * length * d).reshape(slots, kv_heads, length, d)
+    vc = O.normal(43, slots * kv_heads * length * d).reshape(slots, kv_heads, length, d)
+    maxpos = int(pos.max()) + 1
+    cos_t, sin_t = O.rope_tables(10000.0, d, d // 2, maxpos)
+    max_splits = (maxpos + chunk - 1) // chunk
+
+    dq, dkc, dvc, dpos, dslot = (ctx.to_device(a) for a in (qkv, kc, vc, pos, slot))
+    dcos, dsin = ctx.rope_tables(10000.0, d, d // 2, maxpos)
+    assert same_bits(dcos.download(), cos_t) and same_bits(dsin.download(), sin_t)
+    pm = ctx.empty(m * heads * max_splits)
+    pl = ctx.empty(m * heads * max_splits)
+    pa = ctx.empty(m * heads * max_splits * d)
+    out = ctx.empty((m, heads * d))
+    ctx.launch("kv_store_ring", {"m": m, "kv_heads": kv_heads, "d": d, "length": length, "rotated": d // 2,
+                                 "ldq": width, "k_off": heads * d, "v_off": (heads + kv_heads) * d},
+               [dq, dcos, dsin, dpos, dslot, dkc, dvc])
+    ctx.launch("attend_split", {"m": m, "heads": heads, "kv_heads": kv_heads, "d": d, "length": length,
+                                "rotated": d // 2, "chunk": chunk, "max_splits": max_splits, "ldq": width,
+                                "q_off": 0, "scale": 1.0 / math.sqrt(d)},
+               [dq, dcos, dsin, dpos, dslot, dkc, dvc, pm, pl, pa])
+    ctx.launch("attend_combine", {"m": m, "heads": heads, "d": d, "chunk": chunk, "max_splits": max_splits,
+                                  "ldo": heads * d}, [pm, pl, pa, dpos, out])
+
+    # The oracle: rope(k) and v stored, then split attention and combine.
+    kcache, vcache = kc.copy(), vc.copy()
+    krot = O.rope(qkv[:, heads * d:(heads + kv_heads) * d], kv_heads, d, d // 2, pos, cos_t, sin_t)
+    O.kv_store_ring(krot, kv_heads, d, length, pos, slot, kcache)
+    O.kv_store_ring(np.ascontiguousarray(qkv[:, (heads + kv_heads) * d:]), kv_heads, d, length, pos, slot, vcache)
+    assert same_bits(dkc.download(), kcache) and same_bits(dvc.download(), vcache)
+    qrot = O.rope(qkv[:, :heads * d], heads, d, d // 2, pos, cos_t, sin_t)
+    want, _ = O.attend(qrot, heads, kv_heads, d, length, pos, slot, kcache, vcache,
+                       np.float32(1.0 / math.sqrt(d)), chunk, 4, max_splits, THREADS)
+    got = out.download()
+    assert same_bits(got, want)
+    # The referee: attention over the caches as the kernels left them
+    # (evaluateStored), positions <= pos; rows never wrap past `length` here
+    # except the wrapping case, which reads the ring as stored.
+    if all(p < length for p in positions):
+        qref = O.r_rope(O.r_input(qkv[:, :heads * d]), d, d // 2, 10000.0, pos)
+        ref = O.r_attend(qref, heads, kv_heads, d, length, pos, slot, kcache.astype(np.float64),
+                         vcache.astype(np.float64), 1.0 / math.sqrt(d))
+        assert O.within(got, ref).all()
+        assert rel_err(got, ref[0]) <= 1e-4
+    for b in (dq, dkc, dvc, dpos, dslot, dcos, dsin, pm, pl, pa, out):
+        b.free()
+
+
+# ---------------------------------------------------------------------------
+# Elementwise, gather, argmax
+
+
+def test_elementwise_and_gather(ctx):
+    n = 100_000
+    a, b = O.normal(51, n), O.normal(52, n)
+    da, db, dy = ctx.to_device(a), ctx.to_device(b), ctx.empty(n)
+    ctx.launch("add", {"n": n}, [da, db, dy])
+    assert same_bits(dy.download(), O.add(a, b))
+    ctx.launch("silu_mul", {"n": n}, [da, db, dy])
+    assert same_bits(dy.download(), O.silu_mul(a, b))
+    ref = O.r_silu_mul(O.r_input(a), O.r_input(b))
+    assert O.within(dy.download(), ref).all()
+    table = O.normal(53, 1000 * 64, 0.0, 0.02).reshape(1000, 64)
+    toks = np.array([3, 999, 0, 3], np.uint32)
+    dt, dtok, dg = ctx.to_device(table), ctx.to_device(toks), ctx.empty((4, 64))
+    ctx.launch("gather", {"width": 64, "m": 4, "factor": 1.0}, [dt, dtok, dg])
+    assert same_bits(dg.download(), O.gather(table, toks))
+    for buf in (da, db, dy, dt, dtok, dg):
+        buf.free()
+
+
+def test_argmax_first_index_ties_and_nans(ctx):
+    rows = []
+    r = O.normal(61, 32000)
+    rows.append(r.copy())
+    t = r.copy()
+    t[100] = t[31000] = 50.0  # a tie: the lower index
+    rows.append(t)
+    t = r.copy()
+    t[0] = np.nan  # a NaN first: the fold keeps index 0
+    rows.append(t)
+    t = r.copy()
+    t[5] = np.nan
+    t[7] = 60.0  # NaNs later are never taken
+    rows.append(t)
+    t = np.full(32000, -np.inf, np.float32)  # all equal: index 0
+    rows.append(t)
+    t = np.zeros(32000, np.float32)
+    t[3] = -0.0
+    t[9] = 0.0  # +0 and -0 tie: the lower index
+    rows.append(t)
+    x = np.stack(rows)
+    dx, di = ctx.to_device(x), ctx.empty(len(rows), np.uint32)
+    ctx.launch("argmax", {"m": len(rows), "n": 32000, "ldx": 32000}, [dx, di])
+    got = di.download()
+    assert np.array_equal(got, O.argmax(x))
+    assert list(got[1:]) == [100, 0, 7, 0, 0]
+    dx.free()
+    di.free()
+
+
+def test_rope_kernel(ctx):
+    m, heads, d = 3, 5, 128
+    x = O.normal(71, m * heads * d).reshape(m, heads * d)
+    pos = np.array([0, 7, 4095], np.uint32)
+    c, s = O.rope_tables(10000.0, d, 48, 4096)
+    dx, dp, dc, ds, dy = ctx.to_device(x), ctx.to_device(pos), ctx.to_device(c), ctx.to_device(s), ctx.empty((m, heads * d))
+    ctx.launch("rope", {"m": m, "heads": heads, "d": d, "rotated": 48, "ldx": heads * d, "ldy": heads * d},
+               [dx, dp, dc, ds, dy])
+    got = dy.download()
+    assert same_bits(got, O.rope(x, heads, d, 48, pos, c, s))
+    ref = O.r_rope(O.r_input(x), d, 48, 10000.0, pos)
+    assert O.within(got, ref).all()
+    for b in (dx, dp, dc, ds, dy):
+        b.free()
+
+
+# ---------------------------------------------------------------------------
+# The boundary's refusals and graphs
+
+
+def test_dimension_refusal_text(ctx):
+    from furykernel_b200 import _native as N
+
+    x = ctx.empty(16)
+    y = ctx.empty(16)
+    with pytest.raises(N.Refused) as e:
+        ctx.launch("softmax_rows", {"rows": 1, "h": 6}, [x, y])
+    assert str(e.value) == "softmax_rows: the dimension h is 6, outside its range 4..16384 multiple of 4."
+    with pytest.raises(N.Refused) as e:
+        ctx.launch("gemv", {"n": 4, "k": 4, "m": 33, "split": 1, "ldx": 4, "ldy": 4}, [x, x, y])
+    assert str(e.value) == "gemv: the dimension m is 33, outside its range 1..32."
+    x.free()
+    y.free()
+
+
+def test_graph_capture_replays_launches(ctx):
+    n = 1 << 16
+    a, b = O.normal(81, n), O.normal(82, n)
+    da, db, dy = ctx.to_device(a), ctx.to_device(b), ctx.empty(n)
+    ctx.capture_begin()
+    ctx.launch("add", {"n": n}, [da, db, dy])
+    ctx.launch("add", {"n": n}, [dy, db, dy])
+    g = ctx.capture_end()
+    g.launch()
+    ctx.sync()
+    assert same_bits(dy.download(), O.add(O.add(a, b), b))
+    ms = g.time(1, 3)
+    assert ms > 0
+    g.destroy()
+    for buf in (da, db, dy):
+        buf.free()
