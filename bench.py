@@ -1,0 +1,340 @@
+"""Decode throughput of the 32-layer Llama-shaped f32 model
+on B200, through the planned launch sequence captured as one CUDA graph.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+
+One step is one greedy decode step of the whole model at batch B (default
+1): the embedding gather, 32 planned layers (7 launches each), the head's
+norm + tied LM head + argmax, and the feedback of the ids. Weights are
+seeded N(0, 0.02) on the device; the KV cache holds a 512-position
+prompt's keys and values (seeded N(0, 1)) and decode continues from
+position 512. Every step streams the 26.4 GB of weights, far more than L2.
+
+--impl reference times the reference's CPU path instead: the C
+restatement of the FuryKernel.Cpu target's arithmetic (oracle/), on all host
+threads, over a bounded sample (one full-size layer and the head per step,
+scaled to 32 layers).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tokens/s, 32-layer Llama-shaped f32 (BASELINE config 5)"
+PROMPT = 512
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples of the SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.path = tempfile.mktemp(suffix=".csv")
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.device)], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            self.proc.wait()
+            self.f.close()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in open(self.path):
+                w = [x.strip() for x in line.split(",")]
+                if len(w) >= 9 and w[1].replace(".", "").isdigit():
+                    rows.append(w)
+        except OSError:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"]}
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(float(r[1]) for r in rows), "sm_max_mhz": float(rows[0][2]),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()) if rows else None,
+                "samples": len(rows), "reasons": reasons}
+
+
+# ---------------------------------------------------------------------------
+# The CPU path: the reference's CPU target restated (oracle/), timed
+
+
+def cpu_model(batch: int):
+    """Host copies of one full-size layer's weights, the tied embedding, the
+    norms and a layer's KV cache, seeded as the device's are."""
+    import numpy as np
+
+    from oracle import oracle as O
+
+    d, h, hd, f, V, L = 4096, 32, 128, 11008, 32000, 1024
+    w = {
+        "qkv": O.normal(11, 3 * d * d, 0.0, 0.02).reshape(3 * d, d),
+        "o": O.normal(12, d * d, 0.0, 0.02).reshape(d, d),
+        "gu": O.normal(13, 2 * f * d, 0.0, 0.02).reshape(2 * f, d),
+        "down": O.normal(14, d * f, 0.0, 0.02).reshape(d, f),
+        "embed": O.normal(15, V * d, 0.0, 0.02).reshape(V, d),
+        "g1": O.normal(16, d, 0.0, 0.02), "g2": O.normal(17, d, 0.0, 0.02), "gf": O.normal(18, d, 0.0, 0.02),
+        "kc": O.normal(20, batch * h * L * hd).reshape(batch, h, L, hd),
+        "vc": O.normal(21, batch * h * L * hd).reshape(batch, h, L, hd),
+    }
+    w["cos"], w["sin"] = O.rope_tables(10000.0, hd, hd // 2, L)
+    w["tok"] = O.ints(22, batch, V)
+    return w
+
+
+def cpu_sample(threads: int, batch: int, w: dict, min_seconds: float = 10.0):
+    """Seconds for one decode step of the full model on the CPU, from a
+    bounded sample: one full-size layer (q/k/v, RoPE, KV store, attention at
+    context 512, o, SiLU FFN) and the head per repetition, the layer's time
+    scaled by 32. Returns (seconds per step, description)."""
+    import math
+
+    import numpy as np
+
+    from oracle import oracle as O
+
+    d, h, hd, f, L = 4096, 32, 128, 11008, 1024
+    pos = np.full(batch, PROMPT, np.uint32)
+    slot = np.arange(batch, dtype=np.uint32)
+    eps, scale = np.float32(1e-5), np.float32(1.0 / math.sqrt(hd))
+
+    def layer(x):
+        qkv = O.gemv(w["qkv"], O.rmsnorm_rows(x, w["g1"], eps, 1.0, threads), 1, threads)
+        kr = O.rope(qkv[:, d:2 * d], h, hd, hd // 2, pos, w["cos"], w["sin"])
+        O.kv_store_ring(kr, h, hd, L, pos, slot, w["kc"])
+        O.kv_store_ring(np.ascontiguousarray(qkv[:, 2 * d:]), h, hd, L, pos, slot, w["vc"])
+        qr = O.rope(qkv[:, :d], h, hd, hd // 2, pos, w["cos"], w["sin"])
+        att, _ = O.attend(qr, h, h, hd, L, pos, slot, w["kc"], w["vc"], scale, 128, 4, L // 128, threads)
+        x1 = O.add(x, O.gemv(w["o"], att, 2, threads))
+        gu = O.gemv(w["gu"], O.rmsnorm_rows(x1, w["g2"], eps, 1.0, threads), 1, threads)
+        return O.add(x1, O.gemv(w["down"], O.silu_mul(gu[:, :f], gu[:, f:]), 2, threads))
+
+    def head(x):
+        return O.argmax(O.gemv(w["embed"], O.rmsnorm_rows(x, w["gf"], eps, 1.0, threads), 1, threads))
+
+    t_layer, t_head, reps = 0.0, 0.0, 0
+    start = time.perf_counter()
+    while reps < 1 or (time.perf_counter() - start < min_seconds and reps < 20):
+        x = O.gather(w["embed"], w["tok"])
+        t0 = time.perf_counter()
+        x = layer(x)
+        t1 = time.perf_counter()
+        head(x)
+        t2 = time.perf_counter()
+        t_layer += t1 - t0
+        t_head += t2 - t1
+        reps += 1
+    per_step = 32 * t_layer / reps + t_head / reps
+    desc = (f"{reps} repetition(s) of one full-size layer (d 4096, ffn 11008, 32 heads, context {PROMPT}) and the "
+            f"head (vocab 32000) at batch {batch}, CPU-target arithmetic in C; step = 32 x layer + head")
+    return per_step, desc
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    from oracle import oracle as O
+
+    O.build()
+    w = cpu_model(args.batch)
+    times = []
+    desc = ""
+    for _ in range(max(args.warmup, 0)):
+        cpu_sample(threads, args.batch, w, min_seconds=0.0)
+    for _ in range(args.steps):
+        t, desc = cpu_sample(threads, args.batch, w, min_seconds=0.0)
+        times.append(t)
+    per_step = sum(times) / len(times)
+    value = args.batch / per_step
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": {"workload": f"config 5 decode, batch {args.batch}, context {PROMPT}", "global_batch": args.batch,
+                   "seq_len": PROMPT, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": desc + "; per step one sample, OpenMP over rows and heads"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# Ours
+
+
+def run_ours(args):
+    import ctypes
+
+    import numpy as np
+
+    from furykernel_b200 import _native as N
+    from furykernel_b200.engine import Llama
+    from furykernel_b200.program.llama import LlamaShape
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from furykernel_b200 import tp
+
+        return tp.bench_main(args, METRIC, PROMPT)
+
+    b = args.batch
+    length = 4096 if b <= 4 else 1024
+    shape = LlamaShape(layers=args.layers, slots=b, length=length, positions=length)
+    ctx = N.Context(local)
+    eng = Llama(ctx, shape, b, seed=2026, chunk=128, prefill_kv=1.0)
+    tokens = np.arange(b, dtype=np.uint32) * 7 + 1
+    slots = np.arange(b, dtype=np.uint32)
+    eng.set_rows(tokens, np.full(b, PROMPT, np.uint32), slots)
+    graph = eng.capture()
+    for _ in range(args.warmup):
+        graph.launch()
+    ctx.sync()
+    eng.set_rows(tokens, np.full(b, PROMPT, np.uint32), slots)
+    with Clocks(local) as clk:
+        ms = graph.time(0, args.steps)
+    clocks = clk.summary()
+    ms_step = ms / args.steps
+    value = b * args.steps / (ms / 1e3)
+    hbm_peak, peak_kind = peaks()
+    contexts = [PROMPT + args.steps / 2] * b
+    step_bytes = eng.algorithmic_bytes(contexts)
+    step_gbs = step_bytes / (ms_step / 1e3) / 1e9
+
+    # The dominant kernel: the GEMV over [gate; up] (the largest weight
+    # stream), timed alone by CUDA events on the context's stream.
+    L = next(L for L in eng.launches if L.kernel == "gemv_rmsnorm" and L.params["n"] == 2 * shape.ffn)
+    for _ in range(3):
+        L.run(ctx)
+    ctx.sync()
+    import torch
+
+    torch.cuda.set_device(local)
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 20
+    e0.record(stream)
+    for _ in range(reps):
+        L.run(ctx)
+    e1.record(stream)
+    e1.synchronize()
+    k_ms = e0.elapsed_time(e1) / reps
+    p = L.params
+    k_bytes = 4 * (p["n"] * p["k"] + p["m"] * p["k"] + p["k"] + p["m"] * p["n"])
+    k_gbs = k_bytes / (k_ms / 1e3) / 1e9
+
+    # End to end through the C ABI: host token ids and positions in (pinned),
+    # the graph replayed, the greedy ids back, every step.
+    rs = eng.row_stride
+    host_in = N.pinned((3 * rs,), np.uint32)
+    host_out = N.pinned((b,), np.uint32)
+    host_in[:] = 0
+    host_in[:b] = tokens
+    host_in[rs:rs + b] = PROMPT
+    host_in[2 * rs:2 * rs + b] = slots
+    rows_ptr = eng.rows.ptr
+    for _ in range(3):
+        N.check(N.lib().fkc_step(ctx.handle, graph.handle, host_in.ctypes.data, rows_ptr, host_in.nbytes,
+                                 host_out.ctypes.data, eng.out_ids.ptr, host_out.nbytes))
+    host_in[rs:rs + b] = PROMPT
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        N.check(N.lib().fkc_step(ctx.handle, graph.handle, host_in.ctypes.data, rows_ptr, host_in.nbytes,
+                                 host_out.ctypes.data, eng.out_ids.ptr, host_out.nbytes))
+        host_in[:b] = host_out
+        host_in[rs:rs + b] += 1
+    e2e_s = time.perf_counter() - t0
+    e2e = b * args.steps / e2e_s
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded N(0,0.02) weights made on the device, KV of a 512-position prompt seeded N(0,1)",
+        "config": {"workload": f"config 5 decode, batch {b}, context {PROMPT}..{PROMPT + args.steps}",
+                   "model": "llama-shaped 32 layers, d 4096, 32 heads x 128, ffn 11008, vocab 32000, tied head",
+                   "global_batch": b, "seq_len": PROMPT, "parallelism": "tp1", "kv_length": length,
+                   "l2": "no flush: each step streams 26.4 GB of weights, > 126 MB L2"},
+        "hbm": {"step_algorithmic_bytes": step_bytes, "achieved_gbs": step_gbs,
+                "frac_of_8tbs": step_gbs / 8000.0, "frac_of_peak": step_gbs / hbm_peak, "peak": hbm_peak,
+                "peak_kind": peak_kind},
+        "roofline": {"kernel": "gemv_rmsnorm [gate;up] 22016 x 4096 (one launch, batch %d)" % b, "bound": "hbm",
+                     "achieved": k_gbs, "peak": hbm_peak, "unit": "GB/s", "frac": k_gbs / hbm_peak,
+                     "traffic": None, "algorithmic_bytes": k_bytes, "launch_ms": k_ms, "peak_kind": peak_kind},
+        "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": int(host_in.nbytes),
+                "d2h_bytes_per_step": int(host_out.nbytes)},
+        "gpu_launches": eng.launch_count() * args.steps,
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline and rank == 0:
+        threads = 1
+        t, desc = cpu_sample(threads, b, cpu_model(b))
+        line["cpu_baseline"] = {"value": b / t, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                "sample": desc + "; single-threaded, as the CPU target runs"}
+    print(json.dumps(line), flush=True)
+    graph.destroy()
+    ctx.close()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

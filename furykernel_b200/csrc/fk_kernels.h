@@ -80,6 +80,12 @@ cudaError_t fk_launch_rope(const float* x, uint32_t m, uint32_t heads, uint32_t 
                            cudaStream_t s);
 cudaError_t fk_launch_add(const float* a, const float* b, float* y, uint64_t n, cudaStream_t s);
 cudaError_t fk_launch_silu_mul(const float* a, const float* b, float* y, uint64_t n, cudaStream_t s);
+cudaError_t fk_launch_argmax_pairs(const float* x, uint32_t m, uint32_t n, uint32_t ldx, uint32_t offset,
+                                   uint32_t* pairs, bool pdl, cudaStream_t s);
+cudaError_t fk_launch_argmax_pick(const uint32_t* pairs, uint32_t shards, uint32_t m, uint32_t* ids, bool pdl,
+                                  cudaStream_t s);
+cudaError_t fk_launch_advance(const uint32_t* ids, uint32_t* tokens, uint32_t* pos, uint32_t m, bool pdl,
+                              cudaStream_t s);
 cudaError_t fk_launch_fill_normal(float* out, uint64_t n, uint64_t seed, double mu, double sigma, cudaStream_t s);
 cudaError_t fk_launch_fill_uniform(float* out, uint64_t n, uint64_t seed, double a, double b, cudaStream_t s);
 cudaError_t fk_launch_rope_tables(float* cos_t, float* sin_t, double theta, uint32_t d, uint32_t rotated,

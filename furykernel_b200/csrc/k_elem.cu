@@ -77,6 +77,90 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
   }
 }
 
+// A vocabulary shard's greedy candidate per row: its largest value and
+// that value's index plus the shard's offset, as argmax_kernel finds it
+// (first index of the maximum; a NaN first element wins). Grid m, 1024 threads.
+__global__ void __launch_bounds__(1024) argmax_pairs_kernel(const float* __restrict__ x, uint32_t n, uint32_t ldx,
+                                                            uint32_t offset, uint32_t* __restrict__ pairs) {
+  __shared__ float sv[32];
+  __shared__ uint32_t si[32];
+  grid_wait();
+  grid_launch_dependents();
+  const uint32_t r = blockIdx.x;
+  const float* xr = x + (size_t)r * ldx;
+  float bv = -INFINITY;
+  uint32_t bi = 0xffffffffu;
+  for (uint32_t j = threadIdx.x; j < n; j += blockDim.x) {
+    const float v = xr[j];
+    if (v > bv || (bi == 0xffffffffu && v == bv)) {
+      bv = v;
+      bi = j;
+    }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_down_sync(0xffffffffu, bv, o);
+    const uint32_t oi = __shfl_down_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if (lane == 0) {
+    sv[warp] = bv;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    bv = lane < (int)(blockDim.x >> 5) ? sv[lane] : -INFINITY;
+    bi = lane < (int)(blockDim.x >> 5) ? si[lane] : 0xffffffffu;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_down_sync(0xffffffffu, bv, o);
+      const uint32_t oi = __shfl_down_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      // Only the row's first element, in the first shard, wins as a NaN;
+      // a shard of NaNs alone offers no candidate (index 0xffffffff).
+      if (offset == 0 && isnan(xr[0])) {
+        bv = xr[0];
+        bi = 0;
+      }
+      pairs[2 * r] = __float_as_uint(bv);
+      pairs[2 * r + 1] = bi == 0xffffffffu ? bi : bi + offset;
+    }
+  }
+}
+
+// The greedy id from the shards' candidates, [shards][m][2], in shard order:
+// the fold over the whole row keeps the first shard's NaN-first candidate,
+// else the largest value, ties to the lower index.
+__global__ void argmax_pick_kernel(const uint32_t* __restrict__ pairs, uint32_t shards, uint32_t m,
+                                   uint32_t* __restrict__ ids) {
+  grid_wait();
+  grid_launch_dependents();
+  for (uint32_t r = threadIdx.x; r < m; r += blockDim.x) {
+    float bv = __uint_as_float(pairs[2 * r]);
+    uint32_t bi = pairs[2 * r + 1];
+    if (!isnan(bv)) {
+      for (uint32_t s = 1; s < shards; ++s) {
+        const float v = __uint_as_float(pairs[((size_t)s * m + r) * 2]);
+        const uint32_t i = pairs[((size_t)s * m + r) * 2 + 1];
+        if (v > bv || (v == bv && i < bi)) {
+          bv = v;
+          bi = i;
+        }
+      }
+    }
+    ids[r] = bi;
+  }
+}
+
 __global__ void add_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ y,
                            uint64_t n) {
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
@@ -123,7 +207,38 @@ __global__ void fill_uniform_kernel(float* __restrict__ out, uint64_t n, uint64_
   }
 }
 
+// The engine's greedy feedback between decode steps: each row's next token
+// is its greedy id and its position advances by one.
+__global__ void advance_kernel(const uint32_t* __restrict__ ids, uint32_t* __restrict__ tokens,
+                               uint32_t* __restrict__ pos, uint32_t m) {
+  grid_wait();
+  grid_launch_dependents();
+  for (uint32_t r = threadIdx.x; r < m; r += blockDim.x) {
+    tokens[r] = ids[r];
+    pos[r] = pos[r] + 1u;
+  }
+}
+
 }  // namespace fk
+
+cudaError_t fk_launch_argmax_pairs(const float* x, uint32_t m, uint32_t n, uint32_t ldx, uint32_t offset,
+                                   uint32_t* pairs, bool pdl, cudaStream_t s) {
+  if (m == 0) return cudaSuccess;
+  if (n == 0) return cudaErrorInvalidValue;
+  return fk_launch_ex(fk::argmax_pairs_kernel, dim3(m), dim3(1024), 0, s, pdl, x, n, ldx, offset, pairs);
+}
+
+cudaError_t fk_launch_argmax_pick(const uint32_t* pairs, uint32_t shards, uint32_t m, uint32_t* ids, bool pdl,
+                                  cudaStream_t s) {
+  if (m == 0) return cudaSuccess;
+  return fk_launch_ex(fk::argmax_pick_kernel, dim3(1), dim3(256), 0, s, pdl, pairs, shards, m, ids);
+}
+
+cudaError_t fk_launch_advance(const uint32_t* ids, uint32_t* tokens, uint32_t* pos, uint32_t m, bool pdl,
+                              cudaStream_t s) {
+  if (m == 0) return cudaSuccess;
+  return fk_launch_ex(fk::advance_kernel, dim3(1), dim3(256), 0, s, pdl, ids, tokens, pos, m);
+}
 
 cudaError_t fk_launch_gather(const float* table, uint32_t width, const uint32_t* tokens, uint32_t m, float factor,
                              float* y, bool pdl, cudaStream_t s) {

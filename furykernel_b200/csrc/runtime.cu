@@ -434,6 +434,22 @@ int l_rope(fkc_ctx* c, const Params& p, void* const* bufs) {
       "rope");
 }
 
+// argmax_pairs: x pairs | m n ldx offset
+int l_argmax_pairs(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return launched(fk_launch_argmax_pairs(CF(0), p.u(0), p.u(1), p.u(2), p.u(3), U(1), c->pdl, c->stream),
+                  "argmax_pairs");
+}
+
+// argmax_pick: pairs ids | shards m
+int l_argmax_pick(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return launched(fk_launch_argmax_pick(CU(0), p.u(0), p.u(1), U(1), c->pdl, c->stream), "argmax_pick");
+}
+
+// advance: ids tokens pos | m
+int l_advance(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return launched(fk_launch_advance(CU(0), U(1), U(2), p.u(0), c->pdl, c->stream), "advance");
+}
+
 int l_add(fkc_ctx* c, const Params& p, void* const* bufs) {
   return launched(fk_launch_add(CF(0), CF(1), F(2), p.u(0), c->stream), "add");
 }
@@ -551,6 +567,21 @@ std::vector<KernelSpec> make_table() {
                {dim("m", 1, 65535), dim("heads", 1, 65535), dim("d", 2, 2048, 2), u32("rotated"), u32("ldx"),
                 u32("ldy")},
                l_rope});
+  t.push_back({"argmax_pairs",
+               1024,
+               {{"x", "read", "f32"}, {"pairs", "write", "u32"}},
+               {dim("m", 1, 65535), dim("n", 1, kMax), u32("ldx"), u32("offset")},
+               l_argmax_pairs});
+  t.push_back({"argmax_pick",
+               256,
+               {{"pairs", "read", "u32"}, {"ids", "write", "u32"}},
+               {dim("shards", 1, 64), dim("m", 1, 65535)},
+               l_argmax_pick});
+  t.push_back({"advance",
+               256,
+               {{"ids", "read", "u32"}, {"tokens", "write", "u32"}, {"pos", "read_write", "u32"}},
+               {dim("m", 1, 65535)},
+               l_advance});
   t.push_back({"add",
                256,
                {{"a", "read", "f32"}, {"b", "read", "f32"}, {"y", "write", "f32"}},
@@ -777,6 +808,22 @@ extern "C" int fkc_allreduce_sum_f32(fkc_ctx* c, void* dptr, size_t count) {
   cudaSetDevice(c->device);
   ncclResult_t r = ncclAllReduce(dptr, dptr, count, ncclFloat32, ncclSum, c->comm, c->stream);
   if (r != ncclSuccess) return nccl_fail(r, "fkc_allreduce_sum_f32");
+  return FKC_OK;
+}
+
+extern "C" int fkc_allgather_u32(fkc_ctx* c, const void* send, void* recv, size_t count) {
+  if (!c || (count && (!send || !recv))) return fail(FKC_ERR_ARGUMENT, "fkc_allgather_u32: null argument.");
+  if (!c->comm) return fail(FKC_ERR_STATE, "fkc_allgather_u32: no communicator.");
+  cudaSetDevice(c->device);
+  ncclResult_t r = ncclAllGather(send, recv, count, ncclUint32, c->comm, c->stream);
+  if (r != ncclSuccess) return nccl_fail(r, "fkc_allgather_u32");
+  return FKC_OK;
+}
+
+extern "C" int fkc_comm_rank(fkc_ctx* c, int* rank, int* nranks) {
+  if (!c || !rank || !nranks) return fail(FKC_ERR_ARGUMENT, "fkc_comm_rank: null argument.");
+  *rank = c->rank;
+  *nranks = c->nranks;
   return FKC_OK;
 }
 

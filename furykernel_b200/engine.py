@@ -1,0 +1,484 @@
+"""The launch sequence of planned programs on the device.
+
+A plan's steps (src/FuryKernel/Program/Plan.hs:109-121) become one launch
+each of a kernel in the target's table: the step's anchors set the kernel,
+its recomputed operations become the kernel's prologue and its epilogues
+the kernel's epilogue. The step shapes of the Llama-shaped programs
+(furykernel_b200.program.llama) are the ones lowered; any other step shape
+is refused with the step's text.
+
+Memory: a stored value lives in a device buffer of its rows; the anchors of
+one step (horizontal q/k/v, gate/up) write adjacent columns of one buffer,
+and their weights lie adjacent in the weight arena, so the step is one GEMV
+over the concatenated rows. KV caches are Ring arenas per layer.
+
+`Llama` builds a whole decode step -- the embedding gather, every layer's
+plan, the head's plan -- captures it as one CUDA graph, and replays it per
+step: host token ids in, greedy ids out.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import _native as N
+from .program import plan as PL
+from .program.graph import SCache, SRowInts, SWeight
+from .program.llama import LlamaShape, embed_program, head_program, layer_program
+
+
+class Unlowerable(N.Refused):
+    """A step whose shape no kernel of the target runs."""
+
+
+@dataclass
+class View:
+    """A stored value: its buffer, its first column and the buffer's row stride."""
+
+    buf: object  # DeviceBuffer or int address
+    col: int
+    ld: int
+    width: int
+
+    @property
+    def base(self) -> int:
+        return self.buf.ptr if isinstance(self.buf, N.DeviceBuffer) else int(self.buf)
+
+    @property
+    def ptr(self) -> int:
+        return self.base + 4 * self.col
+
+
+@dataclass
+class Launch:
+    kernel: str
+    params: dict
+    bufs: list
+
+    def run(self, ctx: N.Context) -> None:
+        ctx.launch(self.kernel, self.params, self.bufs)
+
+
+@dataclass
+class Binding:
+    """What a program's sources and stored values are on the device."""
+
+    weights: dict = field(default_factory=dict)  # source name -> address
+    ints: dict = field(default_factory=dict)  # source name -> address of [m] u32
+    caches: dict = field(default_factory=dict)  # source name -> address of the layer's Ring
+    values: dict = field(default_factory=dict)  # value name -> View
+    m: int = 1
+
+
+def _work_text(p, step) -> str:
+    return "; ".join(f"{w.kind.lower()} {p.node(w.node).name}" for w in step.work)
+
+
+def lower_step(p, step, b: Binding, tables: dict, attn: dict) -> Launch:
+    """One step of a plan as one launch (the step shapes of the Llama plans)."""
+    work = [(w.kind, p.node(w.node)) for w in step.work]
+    anchors = [n for k, n in work if k == "Anchor"]
+    recomputed = {n.outputs[0]: n for k, n in work if k == "Recompute"}
+    epilogues = [n for k, n in work if k == "Epilogue"]
+    vname = lambda v: p.value(v).name  # noqa: E731
+
+    def stored(v) -> View:
+        view = b.values.get(vname(v))
+        if view is None:
+            raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: {vname(v)} is not stored where the step reads it.")
+        return view
+
+    if anchors and all(n.op.kind == "Linear" for n in anchors):
+        x_id = anchors[0].op.values[0]
+        if any(n.op.values[0] != x_id for n in anchors):
+            raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: anchors of different inputs: {_work_text(p, step)}")
+        ws = [p.source(n.op.sources[0]) for n in anchors]
+        w0 = b.weights[ws[0].name]
+        n_total = sum(w.kind.dims[0] for w in ws)
+        k = ws[0].kind.dims[1]
+        addr = w0
+        for w in ws:  # the anchors' weights must lie adjacent
+            if b.weights[w.name] != addr:
+                raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: the weights of its anchors are not adjacent.")
+            addr += 4 * w.kind.dims[0] * k
+        if epilogues:
+            (ep,) = epilogues
+            if ep.op.kind != "Add" or len(anchors) != 1:
+                raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: epilogue {ep.name} is not one residual add.")
+            tile = anchors[0].outputs[0]
+            r_id = ep.op.values[0] if ep.op.values[1] == tile else ep.op.values[1]
+            y = stored(ep.outputs[0])
+        else:
+            y = b.values[vname(anchors[0].outputs[0])]
+            for n in anchors[1:]:  # adjacent columns
+                nxt = b.values[vname(n.outputs[0])]
+                if nxt.buf is not y.buf:
+                    raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: its anchors' outputs are not adjacent.")
+        split = attn.get("split", 1)
+        base = {"n": n_total, "k": k, "m": b.m, "split": split, "ldy": y.ld}
+        xn = recomputed.get(x_id)
+        if xn is None:
+            x = stored(x_id)
+            base["ldx"] = x.ld
+            if epilogues:
+                r = stored(r_id)
+                return Launch("gemv_add", dict(base, ldr=r.ld), [w0, x.ptr, r.ptr, y.ptr])
+            return Launch("gemv", base, [w0, x.ptr, y.ptr])
+        if xn.op.kind == "RmsNorm" and not epilogues:
+            eps, factor, has_gamma = xn.op.args
+            x = stored(xn.op.values[0])
+            gamma = b.weights[p.source(xn.op.sources[0]).name]
+            return Launch("gemv_rmsnorm", dict(base, ldx=x.ld, eps=eps, factor=factor), [w0, x.ptr, gamma, y.ptr])
+        if xn.op.kind == "SiluMul":
+            g, u = (stored(v) for v in xn.op.values)
+            if g.buf is not u.buf or g.ld != u.ld:
+                raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: SiLU-gate's halves are not one row.")
+            base = dict(base, ldx=g.ld, up_off=u.col - g.col)
+            if epilogues:
+                r = stored(r_id)
+                return Launch("gemv_silu_add", dict(base, ldr=r.ld), [w0, g.ptr, r.ptr, y.ptr])
+            return Launch("gemv_silu", base, [w0, g.ptr, y.ptr])
+        raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: no kernel runs {_work_text(p, step)}")
+
+    if len(anchors) == 1 and anchors[0].op.kind == "Attend":
+        att = anchors[0]
+        spec = att.op.args[0]
+        qn = recomputed.get(att.op.values[0])
+        if qn is None or qn.op.kind != "Rope":
+            raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: attention without its query's rotation.")
+        q = stored(qn.op.values[0])
+        kc, vc, pos, slot = (p.source(s).name for s in att.op.sources[:4])
+        layout = p.source(att.op.sources[0]).kind.layout
+        part = attn["partials"]
+        return Launch("attend_split",
+                      {"m": b.m, "heads": spec.heads, "kv_heads": spec.kv_heads, "d": spec.head_dim,
+                       "length": layout.length, "rotated": qn.op.args[0].rotated, "chunk": attn["chunk"],
+                       "max_splits": attn["max_splits"], "ldq": q.ld, "q_off": q.col, "scale": spec.scale},
+                      [q.base, tables["cos"], tables["sin"], b.ints[pos], b.ints[slot],
+                       b.caches[kc], b.caches[vc], part[0], part[1], part[2]])
+
+    kinds = [k for k, _ in work]
+    if kinds == ["Combine"]:
+        att = work[0][1]
+        spec = att.op.args[0]
+        out = stored(att.outputs[0])
+        pos = p.source(att.op.sources[2]).name
+        part = attn["partials"]
+        return Launch("attend_combine",
+                      {"m": b.m, "heads": spec.heads, "d": spec.head_dim, "chunk": attn["chunk"],
+                       "max_splits": attn["max_splits"], "ldo": out.ld},
+                      [part[0], part[1], part[2], b.ints[pos], out.ptr])
+
+    effects = [n for k, n in work if k == "Effect"]
+    if effects and all(n.op.kind == "KvStore" for n in effects) and len(effects) == 2:
+        sk, sv = effects
+        kn = recomputed.get(sk.op.values[0])
+        if kn is None or kn.op.kind != "Rope":
+            raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: keys stored without their rotation.")
+        kview, vview = stored(kn.op.values[0]), stored(sv.op.values[0])
+        if kview.buf is not vview.buf:
+            raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: keys and values are not one row.")
+        layout = p.source(sk.op.sources[0]).kind.layout
+        pos, slot = (p.source(s).name for s in sk.op.sources[1:3])
+        return Launch("kv_store_ring",
+                      {"m": b.m, "kv_heads": layout.kv_heads, "d": layout.head_dim, "length": layout.length,
+                       "rotated": kn.op.args[0].rotated, "ldq": kview.ld, "k_off": kview.col, "v_off": vview.col},
+                      [kview.base, tables["cos"], tables["sin"], b.ints[pos], b.ints[slot],
+                       b.caches[p.source(sk.op.sources[0]).name], b.caches[p.source(sv.op.sources[0]).name]])
+
+    if kinds == ["Recompute"] and work[0][1].op.kind == "Gather":
+        g = work[0][1]
+        table, tok = (p.source(s) for s in g.op.sources)
+        y = stored(g.outputs[0])
+        return Launch("gather", {"width": table.kind.dims[1], "m": b.m, "factor": g.op.args[0]},
+                      [b.weights[table.name], b.ints[tok.name], y.ptr])
+
+    if kinds == ["Recompute"] and work[0][1].op.kind == "ArgMax":
+        a = work[0][1]
+        x = stored(a.op.values[0])
+        y = stored(a.outputs[0])
+        return Launch("argmax", {"m": b.m, "n": x.width, "ldx": x.ld}, [x.ptr, y.ptr])
+
+    raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: no kernel runs {_work_text(p, step)}")
+
+
+def split_for(n_rows: int, k: int, sms: int) -> int:
+    """Split-K for a GEMV of n rows of k: enough warps to fill the device
+    with whole rows where possible (one warp streams a row's split)."""
+    for s in (1, 2, 4, 8):
+        if (n_rows * s) >= sms * 48 or k // s < 1024:
+            return s
+    return 8
+
+
+class Llama:
+    """A Llama-shaped f32 model on one device, or one rank of a Megatron-style
+    tensor-parallel group: the weights (seeded on the device, or given), the
+    Ring KV arena, the plans of the embedding, a layer and the head, and the
+    captured decode step.
+
+    With `world` ranks, each holds heads/world query and KV heads with their
+    rows of q/k/v and columns of o, ffn/world rows of gate and up with their
+    columns of down (column then row parallel), and vocab/world rows of the
+    tied LM head; the embedding table is whole on every rank. The
+    row-parallel projections (o, down) leave partial sums that an NCCL
+    allreduce adds before their residual epilogue runs; the head's greedy
+    candidates, one a shard, are gathered and picked.
+    """
+
+    def __init__(self, ctx: N.Context, shape: LlamaShape, batch: int, seed: int = 2026, chunk: int = 128,
+                 pdl: bool = True, prefill_kv: float | None = None, rank: int = 0, world: int = 1,
+                 host_weights=None):
+        import dataclasses
+
+        full = shape
+        for what, n in (("heads", full.heads), ("kv_heads", full.kv_heads), ("ffn", full.ffn),
+                        ("vocab", full.vocab)):
+            if n % world:
+                raise N.Refused(N.FKC_ERR_ARGUMENT, f"{what} {n} does not split over {world} ranks.")
+        s = dataclasses.replace(full, heads=full.heads // world, kv_heads=full.kv_heads // world,
+                                ffn=full.ffn // world)
+        self.ctx, self.full, self.s, self.m = ctx, full, s, batch
+        self.rank, self.world = rank, world
+        self.vocab_local = full.vocab // world
+        self.plans = {
+            "embed": PL.plan(PL.DEFAULT, embed_program(full)),
+            "layer": PL.plan(PL.PlanOptions(sequence_rows=batch if s.slots == 1 else 1), layer_program(s)),
+            "head": PL.plan(PL.DEFAULT, head_program(dataclasses.replace(full, vocab=self.vocab_local))),
+        }
+        # Weights: per layer [q;k;v], o, [gate;up], down, two norms; then the
+        # tied embedding/LM head and the final norm. N(0, 0.02), the norm
+        # gains too (the configs give no other law for them).
+        d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
+        self.layer_elems = (qw + 2 * kvw) * d + d * qw + 2 * f * d + d * f + 2 * d
+        self.arena = ctx.alloc(4 * (s.layers * self.layer_elems + full.vocab * d + d))
+        if host_weights is None:
+            # A rank's layer shards from its own seed; the embedding and the
+            # norms alike on every rank.
+            layers = N.DeviceBuffer(ctx, self.arena.ptr, 4 * s.layers * self.layer_elems)
+            ctx.fill_normal(layers, seed + 7919 * rank, 0.0, 0.02)
+            rest = N.DeviceBuffer(ctx, self.embed_ptr(), 4 * (full.vocab * d + d))
+            ctx.fill_normal(rest, seed + 104729, 0.0, 0.02)
+            for l in range(s.layers):
+                w = self.layer_weights(l)
+                ctx.fill_normal(N.DeviceBuffer(ctx, w["attn_norm"], 8 * d), seed + 3 * l + 1, 0.0, 0.02)
+        else:
+            self.arena.upload(host_weights)
+        self.cos, self.sin = ctx.rope_tables(s.theta, s.head_dim, s.head_dim // 2, s.positions)
+        self.kbase, self.vbase = self._kv_arena()
+        if prefill_kv is not None:
+            kv = s.layers * s.slots * s.kv_heads * s.length * s.head_dim
+            ctx.fill_normal(N.DeviceBuffer(ctx, self.kbase, 4 * kv), seed + 1 + 17 * rank, 0.0, prefill_kv)
+            ctx.fill_normal(N.DeviceBuffer(ctx, self.vbase, 4 * kv), seed + 2 + 17 * rank, 0.0, prefill_kv)
+        m = batch
+        # A step's row inputs in one buffer, so that one copy brings them in:
+        # the tokens, the positions, the slots, each part on a 16-byte
+        # boundary as every buffer a kernel binds (leastAlign,
+        # src/FuryKernel/Type.hs:66-71).
+        self.row_stride = (m + 3) // 4 * 4
+        self.rows = ctx.zeros(3 * self.row_stride, np.uint32)
+        rs = 4 * self.row_stride
+        self.tokens = N.DeviceBuffer(ctx, self.rows.ptr, 4 * m, np.uint32, (m,))
+        self.pos = N.DeviceBuffer(ctx, self.rows.ptr + rs, 4 * m, np.uint32, (m,))
+        self.slot = N.DeviceBuffer(ctx, self.rows.ptr + 2 * rs, 4 * m, np.uint32, (m,))
+        self.out_ids = ctx.zeros(m, np.uint32)
+        self.x = ctx.zeros((m, d))
+        self.x1 = ctx.zeros((m, d))
+        self.partial = ctx.zeros((m, d))
+        self.qkv = ctx.zeros((m, qw + 2 * kvw))
+        self.att = ctx.zeros((m, qw))
+        self.gu = ctx.zeros((m, 2 * f))
+        self.logits = ctx.zeros((m, self.vocab_local))
+        self.pairs = ctx.zeros(2 * m, np.uint32)
+        self.pairs_all = ctx.zeros(2 * m * world, np.uint32)
+        self.chunk = chunk
+        self.max_splits = (s.positions + chunk - 1) // chunk
+        self.part = [ctx.zeros(m * s.heads * self.max_splits), ctx.zeros(m * s.heads * self.max_splits),
+                     ctx.zeros(m * s.heads * self.max_splits * s.head_dim)]
+        self.pdl = pdl
+        self.launches = self._launches()
+        self.graph = None
+
+    # -- layout
+    def _kv_arena(self):
+        import ctypes
+
+        k, v = ctypes.c_void_p(), ctypes.c_void_p()
+        s = self.s
+        N.check(N.lib().fkc_kv_arena(self.ctx.handle, s.layers, s.slots, s.kv_heads, s.length, s.head_dim,
+                                     ctypes.byref(k), ctypes.byref(v)))
+        return k.value, v.value
+
+    LAYER_ORDER = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj", "attn_norm",
+                   "mlp_norm")
+
+    def layer_sizes(self) -> list:
+        s = self.s
+        d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
+        return [qw * d, kvw * d, kvw * d, d * qw, f * d, f * d, d * f, d, d]
+
+    def layer_weights(self, l: int) -> dict:
+        base = self.arena.ptr + 4 * l * self.layer_elems
+        off, at = {}, 0
+        for name, n in zip(self.LAYER_ORDER, self.layer_sizes()):
+            off[name] = base + 4 * at
+            at += n
+        return off
+
+    def embed_ptr(self) -> int:
+        return self.arena.ptr + 4 * self.s.layers * self.layer_elems
+
+    def final_norm_ptr(self) -> int:
+        return self.embed_ptr() + 4 * self.full.vocab * self.full.d_model
+
+    def kv_layer(self, l: int):
+        s = self.s
+        per = 4 * s.slots * s.kv_heads * s.length * s.head_dim
+        return self.kbase + l * per, self.vbase + l * per
+
+    # -- the step's launches
+    def _launches(self) -> list:
+        s, m = self.s, self.m
+        d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
+        tables = {"cos": self.cos.ptr, "sin": self.sin.ptr}
+        ints = {"token": self.tokens.ptr, "position": self.pos.ptr, "slot": self.slot.ptr}
+        attn = {"chunk": self.chunk, "max_splits": self.max_splits, "partials": [b.ptr for b in self.part]}
+        out = []
+        eb = Binding(weights={"embed": self.embed_ptr()}, ints=ints, m=m, values={"x": View(self.x, 0, d, d)})
+        p = self.plans["embed"].program
+        for st in self.plans["embed"].steps:
+            out.append(lower_step(p, st, eb, tables, attn))
+        p = self.plans["layer"].program
+        for l in range(s.layers):
+            kc, vc = self.kv_layer(l)
+            values = {"x": View(self.x, 0, d, d), "q": View(self.qkv, 0, qw + 2 * kvw, qw),
+                      "k": View(self.qkv, qw, qw + 2 * kvw, kvw), "v": View(self.qkv, qw + kvw, qw + 2 * kvw, kvw),
+                      "attended": View(self.att, 0, qw, qw), "x1": View(self.x1, 0, d, d),
+                      "gate": View(self.gu, 0, 2 * f, f), "up": View(self.gu, f, 2 * f, f),
+                      "x2": View(self.x, 0, d, d)}
+            b = Binding(weights=self.layer_weights(l), ints=ints, caches={"k_cache": kc, "v_cache": vc},
+                        values=values, m=m)
+            for st in self.plans["layer"].steps:
+                out.append(lower_step(p, st, b, tables, attn))
+        p = self.plans["head"].program
+        head_rows = self.embed_ptr() + 4 * self.rank * self.vocab_local * d
+        hb = Binding(weights={"embed": head_rows, "final_norm": self.final_norm_ptr()}, ints=ints, m=m,
+                     values={"x": View(self.x, 0, d, d),
+                             "logits": View(self.logits, 0, self.vocab_local, self.vocab_local),
+                             "token": View(self.out_ids, 0, 1, 1)})
+        for st in self.plans["head"].steps:
+            out.append(lower_step(p, st, hb, tables, attn))
+        if self.world > 1:
+            out = self._tensor_parallel(out)
+        # The engine's greedy feedback: the ids become the next step's
+        # tokens and the positions advance, so replays decode on their own.
+        out.append(Launch("advance", {"m": m}, [self.out_ids.ptr, self.tokens.ptr, self.pos.ptr]))
+        for L in out:  # split-K per GEMV shape
+            if L.kernel.startswith("gemv"):
+                L.params["split"] = split_for(L.params["n"], L.params["k"], self.ctx.sms)
+        return out
+
+    def _tensor_parallel(self, launches: list) -> list:
+        """The row-parallel projections' residual epilogues move after the
+        allreduce of their partial sums; the greedy pick gathers the shards'
+        candidates."""
+        m, d = self.m, self.s.d_model
+        P = self.partial.ptr
+        out = []
+        for L in launches:
+            if L.kernel in ("gemv_add", "gemv_silu_add"):
+                w, x, r, y = L.bufs
+                params = {k: v for k, v in L.params.items() if k != "ldr"}
+                if params["ldy"] != d or L.params["ldr"] != d:
+                    raise Unlowerable(N.FKC_ERR_ARGUMENT, "a row-parallel output that is not a whole row.")
+                out.append(Launch(L.kernel[:-4], params, [w, x, P]))
+                out.append(Launch("__allreduce__", {"count": m * d}, [P]))
+                out.append(Launch("add", {"n": m * d}, [r, P, y]))
+            elif L.kernel == "argmax":
+                x, ids = L.bufs
+                out.append(Launch("argmax_pairs", dict(L.params, offset=self.rank * self.vocab_local),
+                                  [x, self.pairs.ptr]))
+                out.append(Launch("__allgather__", {"count": 2 * m}, [self.pairs.ptr, self.pairs_all.ptr]))
+                out.append(Launch("argmax_pick", {"shards": self.world, "m": m}, [self.pairs_all.ptr, ids]))
+            else:
+                out.append(L)
+        return out
+
+    def _run(self, L: Launch) -> None:
+        if L.kernel == "__allreduce__":
+            N.check(N.lib().fkc_allreduce_sum_f32(self.ctx.handle, L.bufs[0], L.params["count"]))
+        elif L.kernel == "__allgather__":
+            N.check(N.lib().fkc_allgather_u32(self.ctx.handle, L.bufs[0], L.bufs[1], L.params["count"]))
+        else:
+            L.run(self.ctx)
+
+    def run_eager(self) -> None:
+        self.ctx.set_pdl(False)
+        for L in self.launches:
+            self._run(L)
+
+    def capture(self) -> N.Graph:
+        if self.graph is None:
+            self.ctx.set_pdl(self.pdl)
+            self.ctx.capture_begin()
+            try:
+                for L in self.launches:
+                    self._run(L)
+            finally:
+                g = self.ctx.capture_end()
+                self.ctx.set_pdl(False)
+            self.graph = g
+        return self.graph
+
+    def set_rows(self, tokens, positions, slots=None) -> None:
+        self.tokens.upload(np.asarray(tokens, np.uint32))
+        self.pos.upload(np.asarray(positions, np.uint32))
+        self.slot.upload(np.asarray(slots if slots is not None else np.arange(self.m), np.uint32))
+
+    def step(self) -> np.ndarray:
+        self.capture().launch()
+        self.ctx.sync()
+        return self.out_ids.download()
+
+    def launch_count(self) -> int:
+        """Kernels of this library a step launches (collectives excluded)."""
+        return sum(1 for L in self.launches if not L.kernel.startswith("__"))
+
+    def weight_bytes(self) -> int:
+        """The weights a step streams on this rank: the layers' shards, the
+        LM head's vocabulary rows and the final norm."""
+        s = self.s
+        return 4 * (s.layers * self.layer_elems + self.vocab_local * s.d_model + s.d_model)
+
+    def algorithmic_bytes(self, contexts) -> int:
+        """Bytes a decode step must move on this rank: every weight once, each
+        row's keys and values over its context, per layer."""
+        s = self.s
+        kv = sum(2 * s.kv_heads * s.head_dim * 4 * (int(c) + 1) for c in contexts) * s.layers
+        return self.weight_bytes() + kv
+
+
+def shard_weights(full: LlamaShape, layers: list, embed: np.ndarray, final_norm: np.ndarray, rank: int,
+                  world: int) -> np.ndarray:
+    """One rank's weight arena from the whole model's host weights, in the
+    engine's layout: per layer q/k/v rows of its heads, o's columns of its
+    heads, gate/up rows of its ffn slice, down's columns of that slice,
+    the norms; then the whole embedding and the final norm.
+
+    `layers` holds per layer the f32 arrays q [H*hd, d], k and v
+    [KV*hd, d], o [d, H*hd], gate and up [F, d], down [d, F], attn_norm and
+    mlp_norm [d]."""
+    hd, d = full.head_dim, full.d_model
+    hq, hk, fl = full.heads // world, full.kv_heads // world, full.ffn // world
+    qs = slice(rank * hq * hd, (rank + 1) * hq * hd)
+    ks = slice(rank * hk * hd, (rank + 1) * hk * hd)
+    fs = slice(rank * fl, (rank + 1) * fl)
+    parts = []
+    for w in layers:
+        parts += [w["q"][qs], w["k"][ks], w["v"][ks], np.ascontiguousarray(w["o"][:, qs]), w["gate"][fs],
+                  w["up"][fs], np.ascontiguousarray(w["down"][:, fs]), w["attn_norm"], w["mlp_norm"]]
+    parts += [embed, final_norm]
+    return np.concatenate([np.ascontiguousarray(a, np.float32).ravel() for a in parts])

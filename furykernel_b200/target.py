@@ -131,6 +131,10 @@ SPEC_KERNELS = {
         KernelSig("rope", [_f32("x"), _u32("pos"), _f32("cos"), _f32("sin"), _f32("y", "write")],
                   [_dim("m", 1, 65535), _dim("heads", 1, 65535), _dim("d", 2, 2048, 2), _u("rotated"), _u("ldx"),
                    _u("ldy")], threads=64),
+        KernelSig("argmax_pairs", [_f32("x"), _u32("pairs", "write")],
+                  [_dim("m", 1, 65535), _dim("n", 1, _MAX), _u("ldx"), _u("offset")], threads=1024),
+        KernelSig("argmax_pick", [_u32("pairs"), _u32("ids", "write")], [_dim("shards", 1, 64), _dim("m", 1, 65535)]),
+        KernelSig("advance", [_u32("ids"), _u32("tokens", "write"), _u32("pos", "read_write")], [_dim("m", 1, 65535)]),
         KernelSig("add", [_f32("a"), _f32("b"), _f32("y", "write")], [_dim("n", 1, _MAX)]),
         KernelSig("silu_mul", [_f32("a"), _f32("b"), _f32("y", "write")], [_dim("n", 1, _MAX)]),
     ]

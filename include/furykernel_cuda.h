@@ -136,6 +136,11 @@ int fkc_time_graph(fkc_ctx *ctx, fkc_graph *g, int warmup, int iters, float *ms)
 int fkc_comm_unique_id(void *id128);
 int fkc_comm_init(fkc_ctx *ctx, int nranks, int rank, const void *id128);
 int fkc_allreduce_sum_f32(fkc_ctx *ctx, void *dptr, size_t count);
+/* Each rank's `count` 32-bit words, gathered in rank order into recv
+ * (nranks * count words): the vocabulary shards' greedy candidates. */
+int fkc_allgather_u32(fkc_ctx *ctx, const void *send, void *recv, size_t count);
+/* The context's rank and number of ranks (1 and 0 without a communicator). */
+int fkc_comm_rank(fkc_ctx *ctx, int *rank, int *nranks);
 int fkc_comm_destroy(fkc_ctx *ctx);
 
 #ifdef __cplusplus

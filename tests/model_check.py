@@ -1,0 +1,118 @@
+"""Test infrastructure: a decode step of the Llama-shaped model recomputed by
+the oracle -- bit for bit in the CPU target's arithmetic (fko_*), and in f64
+with binary32 bounds (fkr_*, the reference's evaluator) -- from the weights
+and caches the device holds."""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+from oracle import oracle as O
+
+
+def host_model(eng):
+    """The engine's weights, per layer, as the device holds them."""
+    s = eng.s
+    d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
+    flat = eng.arena.download()
+    layers = []
+    for l in range(s.layers):
+        base = l * eng.layer_elems
+        at = base
+        w = {}
+        for name, rows, cols in [("qkv", qw + 2 * kvw, d), ("o", d, qw), ("gu", 2 * f, d), ("down", d, f),
+                                 ("attn_norm", 1, d), ("mlp_norm", 1, d)]:
+            w[name] = flat[at:at + rows * cols].reshape(rows, cols) if rows > 1 else flat[at:at + cols].copy()
+            at += rows * cols
+        layers.append(w)
+    e0 = s.layers * eng.layer_elems
+    embed = flat[e0:e0 + s.vocab * d].reshape(s.vocab, d)
+    final_norm = flat[e0 + s.vocab * d:e0 + s.vocab * d + d].copy()
+    return layers, embed, final_norm
+
+
+def host_caches(eng):
+    s = eng.s
+    n = s.layers * s.slots * s.kv_heads * s.length * s.head_dim
+    import ctypes
+
+    from furykernel_b200 import _native as N
+
+    k = np.empty(n, np.float32)
+    v = np.empty(n, np.float32)
+    N.check(N.lib().fkc_buf_download(eng.ctx.handle, k.ctypes.data, eng.kbase, k.nbytes))
+    N.check(N.lib().fkc_buf_download(eng.ctx.handle, v.ctypes.data, eng.vbase, v.nbytes))
+    shp = (s.layers, s.slots, s.kv_heads, s.length, s.head_dim)
+    return k.reshape(shp), v.reshape(shp)
+
+
+def splits_of(eng):
+    """The split-K of each GEMV launch, in launch order."""
+    return [L.params["split"] for L in eng.launches if L.kernel.startswith("gemv")]
+
+
+def oracle_decode(eng, layers, embed, final_norm, kcache, vcache, tokens, pos, slot, threads=0):
+    """The CPU target's bits for one decode step; the caches are updated in
+    place as the step's stores leave them. Returns (ids, logits, x)."""
+    s = eng.s
+    threads = threads or O.threads_default()
+    d, qw, kvw, f, hd = s.d_model, s.q_width, s.kv_width, s.ffn, s.head_dim
+    cos_t, sin_t = O.rope_tables(s.theta, hd, hd // 2, s.positions)
+    splits = iter(splits_of(eng))
+    scale = np.float32(1.0 / math.sqrt(hd))
+    eps = np.float32(s.eps)
+    x = O.gather(embed, tokens)
+    for l, w in enumerate(layers):
+        a = O.rmsnorm_rows(x, w["attn_norm"], eps, 1.0, threads)
+        qkv = O.gemv(w["qkv"], a, next(splits), threads)
+        q, k, v = qkv[:, :qw], qkv[:, qw:qw + kvw], qkv[:, qw + kvw:]
+        kr = O.rope(k, s.kv_heads, hd, hd // 2, pos, cos_t, sin_t)
+        kc, vc = kcache[l], vcache[l]
+        O.kv_store_ring(kr, s.kv_heads, hd, s.length, pos, slot, kc)
+        O.kv_store_ring(np.ascontiguousarray(v), s.kv_heads, hd, s.length, pos, slot, vc)
+        qr = O.rope(q, s.heads, hd, hd // 2, pos, cos_t, sin_t)
+        att, _ = O.attend(qr, s.heads, s.kv_heads, hd, s.length, pos, slot, kc, vc, scale, eng.chunk, 4,
+                          eng.max_splits, threads)
+        x1 = O.add(x, O.gemv(w["o"], att, next(splits), threads))
+        gu = O.gemv(w["gu"], O.rmsnorm_rows(x1, w["mlp_norm"], eps, 1.0, threads), next(splits), threads)
+        act = O.silu_mul(gu[:, :f], gu[:, f:])
+        x = O.add(x1, O.gemv(w["down"], act, next(splits), threads))
+    logits = O.gemv(embed, O.rmsnorm_rows(x, final_norm, eps, 1.0, threads), next(splits), threads)
+    return O.argmax(logits), logits, x
+
+
+def referee_decode(eng, layers, embed, final_norm, kcache_after, vcache_after, tokens, pos, slot):
+    """The f64 evaluator's values and bounds for the same step, attention
+    reading the caches as the kernels left them (evaluateStored,
+    Eval.hs:186-198). Returns ((logits, bounds), (ids, decided), kv checks)."""
+    s = eng.s
+    d, qw, kvw, f, hd = s.d_model, s.q_width, s.kv_width, s.ffn, s.head_dim
+    x = O.r_gather(embed, tokens)
+    stored_ok = True
+    for l, w in enumerate(layers):
+        a = O.r_rmsnorm(x, d, w["attn_norm"], s.eps)
+        qkv = O.r_linear(w["qkv"], a)
+        q = (qkv[0][:, :qw], qkv[1][:, :qw])
+        k = (qkv[0][:, qw:qw + kvw], qkv[1][:, qw:qw + kvw])
+        v = (qkv[0][:, qw + kvw:], qkv[1][:, qw + kvw:])
+        kr = O.r_rope(k, hd, hd // 2, s.theta, pos)
+        kc, vc = kcache_after[l], vcache_after[l]
+        for r in range(len(pos)):  # the stores the kernels made lie within their bounds
+            for h in range(s.kv_heads):
+                at = (slot[r], h, pos[r] % s.length)
+                for vals, cache in ((kr, kc), (v, vc)):
+                    exact = vals[0][r, h * hd:(h + 1) * hd]
+                    bound = vals[1][r, h * hd:(h + 1) * hd]
+                    got = cache[at].astype(np.float64)
+                    stored_ok &= bool(np.all(np.abs(got - exact) <= O.widened(bound)))
+        qr = O.r_rope(q, hd, hd // 2, s.theta, pos)
+        att = O.r_attend(qr, s.heads, s.kv_heads, hd, s.length, pos, slot, kc.astype(np.float64),
+                         vc.astype(np.float64), 1.0 / math.sqrt(hd))
+        x1 = O.r_add(x, O.r_linear(w["o"], att))
+        gu = O.r_linear(w["gu"], O.r_rmsnorm(x1, d, w["mlp_norm"], s.eps))
+        act = O.r_silu_mul((gu[0][:, :f], gu[1][:, :f]), (gu[0][:, f:], gu[1][:, f:]))
+        x = O.r_add(x1, O.r_linear(w["down"], act))
+    logits = O.r_linear(embed, O.r_rmsnorm(x, d, final_norm, s.eps))
+    return logits, O.r_argmax(logits), stored_ok
