@@ -42,6 +42,12 @@ static int cuda_fail(cudaError_t e, const char* what) {
   } while (0)
 
 extern "C" const char* fkc_last_error(void) { return g_last_error.c_str(); }
+
+// The no-allocation reduction's failures, reported through fkc_last_error.
+int fkc_noalloc_fail(int code, const char* msg) {
+  g_last_error = msg;
+  return code;
+}
 extern "C" int fkc_version(void) { return 1; }
 
 // ---------------------------------------------------------------------------

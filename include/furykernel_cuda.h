@@ -115,6 +115,27 @@ uint64_t fkc_fnv1a64(const void *bytes, size_t n);
  * dimensions are checked against their ranges first. */
 int fkc_launch(fkc_ctx *ctx, int kernel, const void *params, size_t params_len, void *const *bufs, int nbufs);
 
+/* ---- the tree reduction without allocation --------------------------------- */
+/* No counterpart in the reference. The sum of n f32 values at x into *y, with
+ * exactly the bits of the reduce_groups + reduce_final launches, for callers
+ * that cannot call cudaMalloc: code that runs inside a host whose allocator
+ * owns every byte of device memory (a serving engine's fixed arena, a memory
+ * pool with a hard budget), or on a path where an allocation's implicit
+ * synchronization or failure is not acceptable. The caller passes the input
+ * and the output; the scratch (the groups' partials, the final pass's sums
+ * and counter) is a static device array of the library, about 1 MiB, which
+ * every GPU that loads the library holds until the process exits; n may be
+ * at most 2^26 (67,108,864), larger n is refused with FKC_ERR_ARGUMENT.
+ * Runs on the current device, on `stream` (a cudaStream_t, NULL for the
+ * default stream). The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current: make that first
+ * call before any stream capture. Every call on a device shares the one
+ * array, which keeps the last call's contents; calls that overlap on the GPU
+ * (on different streams without ordering between them) race and must not
+ * be made. Nothing here calls cudaMalloc, cudaFree or any allocating
+ * routine. */
+int fkc_reduce_sum_f32_noalloc(const void *x, uint64_t n, void *y, void *stream);
+
 /* ---- a plan's launch sequence as one CUDA graph ---------------------------- */
 /* Launches between begin and end are captured, not run; replay runs them all
  * (the steps of src/FuryKernel/Program/Plan.hs:109-121, one launch each). */
