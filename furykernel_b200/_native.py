@@ -82,6 +82,9 @@ def lib() -> ctypes.CDLL:
             "fkc_comm_unique_id": (i32, [vp]),
             "fkc_comm_init": (i32, [vp, i32, i32, vp]),
             "fkc_allreduce_sum_f32": (i32, [vp, vp, sz]),
+            "fkc_allgather_u32": (i32, [vp, vp, vp, sz]),
+            "fkc_comm_rank": (i32, [vp, ctypes.POINTER(i32), ctypes.POINTER(i32)]),
+            "fkc_reduce_sum_f32_noalloc": (i32, [vp, u64, vp, vp]),
             "fkc_comm_destroy": (i32, [vp]),
         }
         for name, (res, args) in sig.items():

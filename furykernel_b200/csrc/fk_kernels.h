@@ -18,7 +18,8 @@ struct FkGemv {
   uint32_t up_off;  // SiLU-gate prologue: the up half's offset in a row of x
   int prologue;     // FK_PRO_*
   float eps, factor;
-  bool pdl;  // launch as a programmatic dependent of the previous kernel
+  bool pdl;        // launch as a programmatic dependent of the previous kernel
+  bool silu_pair;  // rows interleave gate and up: y_i = silu(row 2i) * row 2i+1
 };
 
 struct FkAttend {
@@ -68,6 +69,8 @@ cudaError_t fk_launch_rmsnorm_rows(const float* x, const float* gamma, float* y,
                                    float eps, float factor, cudaStream_t s);
 cudaError_t fk_launch_softmax_rows(const float* x, float* y, uint32_t rows, uint32_t h, cudaStream_t s);
 cudaError_t fk_launch_gemv(const FkGemv& g, cudaStream_t s);
+bool fk_gemv_streams(const FkGemv& g);
+cudaError_t fk_launch_gemv_stream(const FkGemv& g, int sms, cudaStream_t s);
 cudaError_t fk_launch_kv_store(const FkKvStore& a, cudaStream_t s);
 cudaError_t fk_launch_attend(const FkAttend& a, cudaStream_t s);
 cudaError_t fk_launch_combine(const FkCombine& a, cudaStream_t s);

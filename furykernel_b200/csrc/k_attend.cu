@@ -51,93 +51,112 @@ __global__ void kv_store_kernel(FkKvStore a) {
   a.vc[at + i + half] = vrow[i + half];
 }
 
-// The attention anchor: grid (max_splits, heads, m), 4 warps.
+// The attention anchor: persistent blocks of 4 warps over the step's items
+// (row, head, split), item i at block i mod G. A warp takes positions w,
+// w + 4, ... of its split, 8 rows of keys (then of values) in flight a lane.
 __global__ void __launch_bounds__(128) attend_split_kernel(FkAttend a) {
   __shared__ float qrot[kHeadDim];
   __shared__ float scores[kMaxChunk];
   __shared__ float4 accw[kAttWarps][kHeadDim / 4];
   __shared__ float lw[kAttWarps];
+  __shared__ uint32_t first[65];  // items before row r (rows <= 64 here)
 
   grid_wait();
   grid_launch_dependents();
-  const uint32_t j = blockIdx.x, h = blockIdx.y, r = blockIdx.z;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint32_t p = a.pos[r];
-  const uint32_t npos = p + 1;
-  const uint32_t splits = (npos + a.chunk - 1) / a.chunk;
-  if (j >= splits) return;
-  const uint32_t t0 = j * a.chunk;
-  const uint32_t t1 = min(npos, t0 + a.chunk);
-  const uint32_t kvh = h / (a.heads / a.kv_heads);
-  const size_t base = ((size_t)a.slot[r] * a.kv_heads + kvh) * a.length;
+  if (threadIdx.x == 0) {
+    uint32_t acc = 0;
+    for (uint32_t r = 0; r < a.m; ++r) {
+      first[r] = acc;
+      acc += a.heads * ((a.pos[r] + 1 + a.chunk - 1) / a.chunk);
+    }
+    first[a.m] = acc;
+  }
+  __syncthreads();
+  const uint32_t items = first[a.m];
   const float4* kc4 = reinterpret_cast<const float4*>(a.kc);
   const float4* vc4 = reinterpret_cast<const float4*>(a.vc);
+  constexpr int B = 8;  // positions in flight a warp
 
-  if (threadIdx.x < kHeadDim / 2)
-    rope_pair(a.qkv + (size_t)r * a.ldq + a.q_off + (size_t)h * kHeadDim, qrot, threadIdx.x, kHeadDim / 2,
-              a.rotated, a.cos_t + (size_t)p * a.rotated, a.sin_t + (size_t)p * a.rotated);
-  __syncthreads();
-  const float4 qv = reinterpret_cast<const float4*>(qrot)[lane];
+  for (uint32_t it = blockIdx.x; it < items; it += gridDim.x) {
+    uint32_t r = 0;
+    while (it >= first[r + 1]) ++r;
+    const uint32_t p = a.pos[r];
+    const uint32_t splits = (p + 1 + a.chunk - 1) / a.chunk;
+    const uint32_t local = it - first[r];
+    const uint32_t h = local / splits, j = local - h * splits;
+    const uint32_t t0 = j * a.chunk;
+    const uint32_t t1 = min(p + 1, t0 + a.chunk);
+    const uint32_t kvh = h / (a.heads / a.kv_heads);
+    const size_t base = ((size_t)a.slot[r] * a.kv_heads + kvh) * a.length;
 
-  // Scores: warp w takes positions t0 + w + 4 u, four at a time.
-  for (uint32_t t = t0 + warp; t < t1; t += 4 * kAttWarps) {
-    float4 kv[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const uint32_t tt = t + u * kAttWarps;
-      kv[u] = tt < t1 ? __ldcs(kc4 + (base + tt % a.length) * (kHeadDim / 4) + lane) : make_float4(0, 0, 0, 0);
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const float sc = __fmul_rn(warp_sum(__fadd_rn(0.0f, pack_dot(qv, kv[u]))), a.scale);
-      const uint32_t tt = t + u * kAttWarps;
-      if (lane == 0 && tt < t1) scores[tt - t0] = sc;
-    }
-  }
-  __syncthreads();
-  float mx = -INFINITY;
-  for (uint32_t i = lane; i < t1 - t0; i += 32) mx = max_number(mx, scores[i]);
-  mx = warp_max(mx);
+    __syncthreads();  // the previous item's shared arrays are free
+    if (threadIdx.x < kHeadDim / 2)
+      rope_pair(a.qkv + (size_t)r * a.ldq + a.q_off + (size_t)h * kHeadDim, qrot, threadIdx.x, kHeadDim / 2,
+                a.rotated, a.cos_t + (size_t)p * a.rotated, a.sin_t + (size_t)p * a.rotated);
+    __syncthreads();
+    const float4 qv = reinterpret_cast<const float4*>(qrot)[lane];
 
-  // Weighted sums: warp w over positions t0 + w, t0 + w + 4, ..., in order.
-  float l = 0.0f;
-  float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-  for (uint32_t t = t0 + warp; t < t1; t += 4 * kAttWarps) {
-    float4 vv[4];
+    // Scores: warp w takes positions t0 + w + 4 u, eight at a time.
+    for (uint32_t t = t0 + warp; t < t1; t += B * kAttWarps) {
+      float4 kv[B];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const uint32_t tt = t + u * kAttWarps;
-      vv[u] = tt < t1 ? __ldcs(vc4 + (base + tt % a.length) * (kHeadDim / 4) + lane) : make_float4(0, 0, 0, 0);
-    }
+      for (int u = 0; u < B; ++u) {
+        const uint32_t tt = t + u * kAttWarps;
+        kv[u] = tt < t1 ? __ldcs(kc4 + (base + tt % a.length) * (kHeadDim / 4) + lane) : make_float4(0, 0, 0, 0);
+      }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const uint32_t tt = t + u * kAttWarps;
-      if (tt < t1) {
-        const float e = exp_rounded(__fsub_rn(scores[tt - t0], mx));
-        l = __fadd_rn(l, e);
-        acc.x = __fadd_rn(acc.x, __fmul_rn(e, vv[u].x));
-        acc.y = __fadd_rn(acc.y, __fmul_rn(e, vv[u].y));
-        acc.z = __fadd_rn(acc.z, __fmul_rn(e, vv[u].z));
-        acc.w = __fadd_rn(acc.w, __fmul_rn(e, vv[u].w));
+      for (int u = 0; u < B; ++u) {
+        const float sc = __fmul_rn(warp_sum(__fadd_rn(0.0f, pack_dot(qv, kv[u]))), a.scale);
+        const uint32_t tt = t + u * kAttWarps;
+        if (lane == 0 && tt < t1) scores[tt - t0] = sc;
       }
     }
-  }
-  accw[warp][lane] = acc;
-  if (lane == 0) lw[warp] = l;
-  __syncthreads();
-  const size_t at = ((size_t)r * a.heads + h) * a.max_splits + j;
-  const float* accf = reinterpret_cast<const float*>(accw);
-  const uint32_t i = threadIdx.x;  // one dimension a thread
-  float o = accf[i];
+    __syncthreads();
+    float mx = -INFINITY;
+    for (uint32_t i = lane; i < t1 - t0; i += 32) mx = max_number(mx, scores[i]);
+    mx = warp_max(mx);
+
+    // Weighted sums: warp w over positions t0 + w, t0 + w + 4, ..., in order.
+    float l = 0.0f;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (uint32_t t = t0 + warp; t < t1; t += B * kAttWarps) {
+      float4 vv[B];
 #pragma unroll
-  for (int w = 1; w < kAttWarps; ++w) o = __fadd_rn(o, accf[w * kHeadDim + i]);
-  a.part_acc[at * kHeadDim + i] = o;
-  if (threadIdx.x == 0) {
-    float lt = lw[0];
+      for (int u = 0; u < B; ++u) {
+        const uint32_t tt = t + u * kAttWarps;
+        vv[u] = tt < t1 ? __ldcs(vc4 + (base + tt % a.length) * (kHeadDim / 4) + lane) : make_float4(0, 0, 0, 0);
+      }
 #pragma unroll
-    for (int w = 1; w < kAttWarps; ++w) lt = __fadd_rn(lt, lw[w]);
-    a.part_l[at] = lt;
-    a.part_m[at] = mx;
+      for (int u = 0; u < B; ++u) {
+        const uint32_t tt = t + u * kAttWarps;
+        if (tt < t1) {
+          const float e = exp_rounded(__fsub_rn(scores[tt - t0], mx));
+          l = __fadd_rn(l, e);
+          acc.x = __fadd_rn(acc.x, __fmul_rn(e, vv[u].x));
+          acc.y = __fadd_rn(acc.y, __fmul_rn(e, vv[u].y));
+          acc.z = __fadd_rn(acc.z, __fmul_rn(e, vv[u].z));
+          acc.w = __fadd_rn(acc.w, __fmul_rn(e, vv[u].w));
+        }
+      }
+    }
+    accw[warp][lane] = acc;
+    if (lane == 0) lw[warp] = l;
+    __syncthreads();
+    const size_t at = ((size_t)r * a.heads + h) * a.max_splits + j;
+    const float* accf = reinterpret_cast<const float*>(accw);
+    const uint32_t i = threadIdx.x;  // one dimension a thread
+    float o = accf[i];
+#pragma unroll
+    for (int w = 1; w < kAttWarps; ++w) o = __fadd_rn(o, accf[w * kHeadDim + i]);
+    a.part_acc[at * kHeadDim + i] = o;
+    if (threadIdx.x == 0) {
+      float lt = lw[0];
+#pragma unroll
+      for (int w = 1; w < kAttWarps; ++w) lt = __fadd_rn(lt, lw[w]);
+      a.part_l[at] = lt;
+      a.part_m[at] = mx;
+    }
   }
 }
 
@@ -180,9 +199,15 @@ cudaError_t fk_launch_kv_store(const FkKvStore& a, cudaStream_t s) {
 
 cudaError_t fk_launch_attend(const FkAttend& a, cudaStream_t s) {
   if (a.m == 0) return cudaSuccess;
-  if (a.d != fk::kHeadDim || a.chunk == 0 || a.chunk > fk::kMaxChunk || a.heads % a.kv_heads != 0)
+  if (a.d != fk::kHeadDim || a.chunk == 0 || a.chunk > fk::kMaxChunk || a.heads % a.kv_heads != 0 || a.m > 64)
     return cudaErrorInvalidValue;
-  return fk_launch_ex(fk::attend_split_kernel, dim3(a.max_splits, a.heads, a.m), dim3(128), 0, s, a.pdl, a);
+  // Blocks for the most items a step can have, at most 8 an SM; each loops.
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const uint64_t most = (uint64_t)a.m * a.heads * a.max_splits;
+  const uint32_t blocks = (uint32_t)(most < (uint64_t)sms * 8 ? most : (uint64_t)sms * 8);
+  return fk_launch_ex(fk::attend_split_kernel, dim3(blocks), dim3(128), 0, s, a.pdl, a);
 }
 
 cudaError_t fk_launch_combine(const FkCombine& a, cudaStream_t s) {

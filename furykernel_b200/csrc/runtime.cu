@@ -332,6 +332,12 @@ int l_softmax_rows(fkc_ctx* c, const Params& p, void* const* bufs) {
   return launched(fk_launch_softmax_rows(CF(0), F(1), p.u(0), p.u(1), c->stream), "softmax_rows");
 }
 
+// Decode batches of up to 4 rows stream through the persistent kernel; larger
+// batches take the chunked one. Both keep the GEMV order contract.
+cudaError_t run_gemv(fkc_ctx* c, const FkGemv& g) {
+  return fk_gemv_streams(g) ? fk_launch_gemv_stream(g, c->sms, c->stream) : fk_launch_gemv(g, c->stream);
+}
+
 FkGemv gemv_base(fkc_ctx* c, const Params& p) {
   FkGemv g = {};
   g.n = p.u(0);
@@ -350,7 +356,7 @@ int l_gemv(fkc_ctx* c, const Params& p, void* const* bufs) {
   FkGemv g = gemv_base(c, p);
   g.w = CF(0), g.x = CF(1), g.y = F(2);
   g.prologue = FK_PRO_NONE;
-  return launched(fk_launch_gemv(g, c->stream), "gemv");
+  return launched(run_gemv(c, g), "gemv");
 }
 // gemv_add: w, x, r, y | n k m split ldx ldy ldr
 int l_gemv_add(fkc_ctx* c, const Params& p, void* const* bufs) {
@@ -358,7 +364,7 @@ int l_gemv_add(fkc_ctx* c, const Params& p, void* const* bufs) {
   g.w = CF(0), g.x = CF(1), g.r = CF(2), g.y = F(3);
   g.ldr = p.u(6);
   g.prologue = FK_PRO_NONE;
-  return launched(fk_launch_gemv(g, c->stream), "gemv_add");
+  return launched(run_gemv(c, g), "gemv_add");
 }
 // gemv_rmsnorm: w, x, gamma, y | n k m split ldx ldy eps factor
 int l_gemv_rmsnorm(fkc_ctx* c, const Params& p, void* const* bufs) {
@@ -367,15 +373,31 @@ int l_gemv_rmsnorm(fkc_ctx* c, const Params& p, void* const* bufs) {
   g.eps = p.f(6);
   g.factor = p.f(7);
   g.prologue = FK_PRO_RMSNORM;
-  return launched(fk_launch_gemv(g, c->stream), "gemv_rmsnorm");
+  return launched(run_gemv(c, g), "gemv_rmsnorm");
 }
+// gemv_rmsnorm_silu: w, x, gamma, y | n k m split ldx ldy eps factor; rows
+// interleave gate and up, y gets n / 2 columns.
+int l_gemv_rmsnorm_silu(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkGemv g = gemv_base(c, p);
+  g.w = CF(0), g.x = CF(1), g.gamma = CF(2), g.y = F(3);
+  g.eps = p.f(6);
+  g.factor = p.f(7);
+  g.prologue = FK_PRO_RMSNORM;
+  g.silu_pair = true;
+  if (g.n % 2 != 0) return fail(FKC_ERR_ARGUMENT, "gemv_rmsnorm_silu: n %u is not a whole number of row pairs.", g.n);
+  if (!fk_gemv_streams(g))
+    return fail(FKC_ERR_ARGUMENT, "gemv_rmsnorm_silu: m %u and k %u are past what the streaming kernel stages.", g.m,
+                g.k);
+  return launched(fk_launch_gemv_stream(g, c->sms, c->stream), "gemv_rmsnorm_silu");
+}
+
 // gemv_silu: w, x, y | n k m split ldx ldy up_off
 int l_gemv_silu(fkc_ctx* c, const Params& p, void* const* bufs) {
   FkGemv g = gemv_base(c, p);
   g.w = CF(0), g.x = CF(1), g.y = F(2);
   g.up_off = p.u(6);
   g.prologue = FK_PRO_SILU;
-  return launched(fk_launch_gemv(g, c->stream), "gemv_silu");
+  return launched(run_gemv(c, g), "gemv_silu");
 }
 // gemv_silu_add: w, x, r, y | n k m split ldx ldy ldr up_off
 int l_gemv_silu_add(fkc_ctx* c, const Params& p, void* const* bufs) {
@@ -384,7 +406,7 @@ int l_gemv_silu_add(fkc_ctx* c, const Params& p, void* const* bufs) {
   g.ldr = p.u(6);
   g.up_off = p.u(7);
   g.prologue = FK_PRO_SILU;
-  return launched(fk_launch_gemv(g, c->stream), "gemv_silu_add");
+  return launched(run_gemv(c, g), "gemv_silu_add");
 }
 
 // kv_store_ring: qkv cos sin pos slot k_cache v_cache | m kv_heads d length rotated ldq k_off v_off
@@ -508,6 +530,11 @@ std::vector<KernelSpec> make_table() {
                {{"w", "read", "f32"}, {"x", "read", "f32"}, {"gamma", "read", "f32"}, {"y", "write", "f32"}},
                with(gemv_dims, {f32("eps"), f32("factor")}),
                l_gemv_rmsnorm});
+  t.push_back({"gemv_rmsnorm_silu",
+               512,
+               {{"w", "read", "f32"}, {"x", "read", "f32"}, {"gamma", "read", "f32"}, {"y", "write", "f32"}},
+               with(gemv_dims, {f32("eps"), f32("factor")}),
+               l_gemv_rmsnorm_silu});
   t.push_back({"gemv_silu",
                256,
                {{"w", "read", "f32"}, {"x", "read", "f32"}, {"y", "write", "f32"}},
@@ -542,7 +569,7 @@ std::vector<KernelSpec> make_table() {
                 {"part_m", "write", "f32"},
                 {"part_l", "write", "f32"},
                 {"part_acc", "write", "f32"}},
-               {dim("m", 1, 65535), dim("heads", 1, 1024), dim("kv_heads", 1, 1024), dim("d", 128, 128),
+               {dim("m", 1, 64), dim("heads", 1, 1024), dim("kv_heads", 1, 1024), dim("d", 128, 128),
                 dim("length", 1, kMax), u32("rotated"), dim("chunk", 1, 256), dim("max_splits", 1, 65535), u32("ldq"),
                 u32("q_off"), f32("scale")},
                l_attend});

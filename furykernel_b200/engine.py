@@ -229,7 +229,7 @@ class Llama:
     candidates, one a shard, are gathered and picked.
     """
 
-    def __init__(self, ctx: N.Context, shape: LlamaShape, batch: int, seed: int = 2026, chunk: int = 128,
+    def __init__(self, ctx: N.Context, shape: LlamaShape, batch: int, seed: int = 2026, chunk: int = 32,
                  pdl: bool = True, prefill_kv: float | None = None, rank: int = 0, world: int = 1,
                  host_weights=None):
         import dataclasses
@@ -243,6 +243,12 @@ class Llama:
                                 ffn=full.ffn // world)
         self.ctx, self.full, self.s, self.m = ctx, full, s, batch
         self.rank, self.world = rank, world
+        # For decode batches the streaming GEMV takes (up to 4 rows), the
+        # arena interleaves gate and up rows (gate_i at row 2i, up_i at
+        # 2i + 1), so that the [gate; up] step computes mlp_act = silu(gate) *
+        # up on its own tiles and stores it, and the down step reads it: the
+        # same bits as recomputing it in the down step, computed once.
+        self.gate_up_interleaved = batch <= 4
         self.vocab_local = full.vocab // world
         self.plans = {
             "embed": PL.plan(PL.DEFAULT, embed_program(full)),
@@ -291,6 +297,7 @@ class Llama:
         self.qkv = ctx.zeros((m, qw + 2 * kvw))
         self.att = ctx.zeros((m, qw))
         self.gu = ctx.zeros((m, 2 * f))
+        self.act = ctx.zeros((m, f))
         self.logits = ctx.zeros((m, self.vocab_local))
         self.pairs = ctx.zeros(2 * m, np.uint32)
         self.pairs_all = ctx.zeros(2 * m * world, np.uint32)
@@ -371,6 +378,8 @@ class Llama:
                              "token": View(self.out_ids, 0, 1, 1)})
         for st in self.plans["head"].steps:
             out.append(lower_step(p, st, hb, tables, attn))
+        if self.gate_up_interleaved:
+            out = self._silu_on_tiles(out)
         if self.world > 1:
             out = self._tensor_parallel(out)
         # The engine's greedy feedback: the ids become the next step's
@@ -378,7 +387,31 @@ class Llama:
         out.append(Launch("advance", {"m": m}, [self.out_ids.ptr, self.tokens.ptr, self.pos.ptr]))
         for L in out:  # split-K per GEMV shape
             if L.kernel.startswith("gemv"):
-                L.params["split"] = split_for(L.params["n"], L.params["k"], self.ctx.sms)
+                # The streaming kernel's parallelism is rows whatever the
+                # split, so it keeps one; the chunked kernel splits long rows.
+                L.params["split"] = 1 if m <= 4 else split_for(L.params["n"], L.params["k"], self.ctx.sms)
+        return out
+
+    def _silu_on_tiles(self, launches: list) -> list:
+        """The [gate; up] step followed by the down step that recomputes
+        silu(gate) * up from their stored rows becomes: the [gate; up] GEMV
+        on interleaved rows with the SiLU-gate epilogue, storing mlp_act;
+        the down GEMV reading it."""
+        f = self.s.ffn
+        gu = self.gu.ptr
+        out = list(launches)
+        for i in range(len(out) - 1):
+            a, b = out[i], out[i + 1]
+            if (a.kernel == "gemv_rmsnorm" and a.bufs[3] == gu and a.params["n"] == 2 * f
+                    and b.kernel in ("gemv_silu", "gemv_silu_add") and b.bufs[1] == gu and b.params["up_off"] == f):
+                out[i] = Launch("gemv_rmsnorm_silu", dict(a.params, ldy=f), [a.bufs[0], a.bufs[1], a.bufs[2],
+                                                                              self.act.ptr])
+                params = {k: v for k, v in b.params.items() if k != "up_off"}
+                params["ldx"] = f
+                if b.kernel == "gemv_silu_add":
+                    out[i + 1] = Launch("gemv_add", params, [b.bufs[0], self.act.ptr, b.bufs[2], b.bufs[3]])
+                else:
+                    out[i + 1] = Launch("gemv", params, [b.bufs[0], self.act.ptr, b.bufs[2]])
         return out
 
     def _tensor_parallel(self, launches: list) -> list:
@@ -462,7 +495,7 @@ class Llama:
 
 
 def shard_weights(full: LlamaShape, layers: list, embed: np.ndarray, final_norm: np.ndarray, rank: int,
-                  world: int) -> np.ndarray:
+                  world: int, interleave: bool = False) -> np.ndarray:
     """One rank's weight arena from the whole model's host weights, in the
     engine's layout: per layer q/k/v rows of its heads, o's columns of its
     heads, gate/up rows of its ffn slice, down's columns of that slice,
@@ -478,7 +511,10 @@ def shard_weights(full: LlamaShape, layers: list, embed: np.ndarray, final_norm:
     fs = slice(rank * fl, (rank + 1) * fl)
     parts = []
     for w in layers:
-        parts += [w["q"][qs], w["k"][ks], w["v"][ks], np.ascontiguousarray(w["o"][:, qs]), w["gate"][fs],
-                  w["up"][fs], np.ascontiguousarray(w["down"][:, fs]), w["attn_norm"], w["mlp_norm"]]
+        gate, up = w["gate"][fs], w["up"][fs]
+        gu = np.stack([gate, up], axis=1).reshape(2 * fl, d) if interleave else [gate, up]
+        parts += [w["q"][qs], w["k"][ks], w["v"][ks], np.ascontiguousarray(w["o"][:, qs])]
+        parts += [gu] if interleave else gu
+        parts += [np.ascontiguousarray(w["down"][:, fs]), w["attn_norm"], w["mlp_norm"]]
     parts += [embed, final_norm]
     return np.concatenate([np.ascontiguousarray(a, np.float32).ravel() for a in parts])

@@ -106,6 +106,8 @@ SPEC_KERNELS = {
         KernelSig("gemv_add", [_f32("w"), _f32("x"), _f32("r"), _f32("y", "write")], _GEMV + [_u("ldr")]),
         KernelSig("gemv_rmsnorm", [_f32("w"), _f32("x"), _f32("gamma"), _f32("y", "write")],
                   _GEMV + [_f("eps"), _f("factor")]),
+        KernelSig("gemv_rmsnorm_silu", [_f32("w"), _f32("x"), _f32("gamma"), _f32("y", "write")],
+                  _GEMV + [_f("eps"), _f("factor")], threads=512),
         KernelSig("gemv_silu", [_f32("w"), _f32("x"), _f32("y", "write")], _GEMV + [_u("up_off")]),
         KernelSig("gemv_silu_add", [_f32("w"), _f32("x"), _f32("r"), _f32("y", "write")],
                   _GEMV + [_u("ldr"), _u("up_off")]),
@@ -117,7 +119,7 @@ SPEC_KERNELS = {
         KernelSig("attend_split",
                   [_f32("qkv"), _f32("cos"), _f32("sin"), _u32("pos"), _u32("slot"), _f32("k_cache"),
                    _f32("v_cache"), _f32("part_m", "write"), _f32("part_l", "write"), _f32("part_acc", "write")],
-                  [_dim("m", 1, 65535), _dim("heads", 1, 1024), _dim("kv_heads", 1, 1024), _dim("d", 128, 128),
+                  [_dim("m", 1, 64), _dim("heads", 1, 1024), _dim("kv_heads", 1, 1024), _dim("d", 128, 128),
                    _dim("length", 1, _MAX), _u("rotated"), _dim("chunk", 1, 256), _dim("max_splits", 1, 65535),
                    _u("ldq"), _u("q_off"), _f("scale")], threads=128),
         KernelSig("attend_combine",

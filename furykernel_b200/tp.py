@@ -1,0 +1,127 @@
+"""Tensor parallelism across the GPUs of one box: one process per GPU.
+
+torch.distributed (NCCL) is the plumbing: the group's rendezvous, barriers,
+the exchange of the shim's NCCL unique id, and the max over ranks of a
+timing. The data path -- the allreduce after each row-parallel projection
+and the gather of the greedy candidates -- runs on the shim's own NCCL
+communicator, on the context's stream, inside the captured decode graph.
+"""
+
+from __future__ import annotations
+
+import datetime
+import json
+import os
+import time
+
+import numpy as np
+
+from . import _native as N
+
+
+def init(timeout_s: int = 120):
+    """(ctx, rank, world, local): the context of this rank's GPU with an NCCL
+    communicator over all ranks."""
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    if not dist.is_initialized():
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=timeout_s),
+                                device_id=torch.device("cuda", local))
+    ctx = N.Context(local)
+    uid = [N.Context.comm_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    ctx.comm_init(world, rank, uid[0])
+    return ctx, rank, world, local
+
+
+def finish(ctx, graphs=()) -> None:
+    """Graphs holding NCCL calls go first, then the communicator, then the group."""
+    import torch.distributed as dist
+
+    for g in graphs:
+        if g is not None:
+            g.destroy()
+    ctx.comm_destroy()
+    ctx.close()
+    if dist.is_initialized():
+        dist.destroy_process_group()
+
+
+def max_over_ranks(v: float) -> float:
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def bench_main(args, metric: str, prompt: int) -> None:
+    """The decode bench at N ranks: each rank replays its shard's captured
+    step; the step time is the max over ranks of the device-timed replays."""
+    import torch.distributed as dist
+
+    from .engine import Llama
+    from .program.llama import LlamaShape
+
+    ctx, rank, world, local = init()
+    b = args.batch
+    length = 4096 if b <= 4 else 1024
+    shape = LlamaShape(layers=args.layers, slots=b, length=length, positions=length)
+    eng = Llama(ctx, shape, b, seed=2026, chunk=32, prefill_kv=1.0, rank=rank, world=world)
+    tokens = np.arange(b, dtype=np.uint32) * 7 + 1
+    slots = np.arange(b, dtype=np.uint32)
+    eng.set_rows(tokens, np.full(b, prompt, np.uint32), slots)
+    graph = eng.capture()
+    for _ in range(args.warmup):
+        graph.launch()
+    ctx.sync()
+    eng.set_rows(tokens, np.full(b, prompt, np.uint32), slots)
+    dist.barrier()
+    ctx.sync()
+    ms = graph.time(0, args.steps)
+    dist.barrier()
+    ms = max_over_ranks(ms)
+    ms_step = ms / args.steps
+    value = b * args.steps / (ms / 1e3)
+
+    # End to end through the C ABI on every rank: the same host inputs in,
+    # the ids out, each step; the max over ranks of the wall time.
+    rs = eng.row_stride
+    host_in = N.pinned((3 * rs,), np.uint32)
+    host_out = N.pinned((b,), np.uint32)
+    host_in[:] = 0
+    host_in[:b] = tokens
+    host_in[rs:rs + b] = prompt
+    host_in[2 * rs:2 * rs + b] = slots
+    dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        N.check(N.lib().fkc_step(ctx.handle, graph.handle, host_in.ctypes.data, eng.rows.ptr, host_in.nbytes,
+                                 host_out.ctypes.data, eng.out_ids.ptr, host_out.nbytes))
+        host_in[:b] = host_out
+        host_in[rs:rs + b] += 1
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    per_rank = eng.algorithmic_bytes([prompt + args.steps / 2] * b)
+    if rank == 0:
+        line = {
+            "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: seeded N(0,0.02) weights made on the device, KV of a 512-position prompt seeded N(0,1)",
+            "config": {"workload": f"config 5 decode, batch {b}, context {prompt}..{prompt + args.steps}",
+                       "model": "llama-shaped 32 layers, d 4096, 32 heads x 128, ffn 11008, vocab 32000, tied head",
+                       "global_batch": b, "seq_len": prompt, "parallelism": f"tp{world}", "kv_length": length,
+                       "l2": "no flush: each step streams the shard's weights, > 126 MB L2"},
+            "hbm": {"per_gpu_step_bytes": per_rank, "per_gpu_achieved_gbs": per_rank / (ms_step / 1e3) / 1e9},
+            "e2e": {"value": b * args.steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(host_in.nbytes),
+                    "d2h_bytes_per_step": int(host_out.nbytes)},
+            "gpu_launches": eng.launch_count() * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    finish(ctx, [graph])

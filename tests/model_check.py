@@ -26,6 +26,8 @@ def host_model(eng):
                                  ("attn_norm", 1, d), ("mlp_norm", 1, d)]:
             w[name] = flat[at:at + rows * cols].reshape(rows, cols) if rows > 1 else flat[at:at + cols].copy()
             at += rows * cols
+        if eng.gate_up_interleaved:  # rows gate_0, up_0, gate_1, ...: back to [gate; up]
+            w["gu"] = np.ascontiguousarray(np.concatenate([w["gu"][0::2], w["gu"][1::2]]))
         layers.append(w)
     e0 = s.layers * eng.layer_elems
     embed = flat[e0:e0 + s.vocab * d].reshape(s.vocab, d)

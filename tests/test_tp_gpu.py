@@ -1,0 +1,79 @@
+"""Tensor parallelism on 2 GPUs: a small model's decode step sharded over two
+ranks (torchrun, one process a GPU), checked against the f64 evaluator's
+bounds over the whole model (the allreduce orders the row-parallel sums
+differently from one GPU, so TP is held to the bounds, not to bits), the
+ranks' hidden rows bit-identical, greedy ids equal to the referee's where
+its bounds decide them."""
+
+import math
+import os
+import socket
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests import model_check as MC
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def gpus() -> int:
+    try:
+        import torch
+
+        return torch.cuda.device_count()
+    except Exception:
+        return 0
+
+
+def free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.skipif(gpus() < 2, reason="needs 2 GPUs")
+def test_tp2_decode_step_within_bounds(tmp_path):
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=ROOT)
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(free_port()),
+           os.path.join(ROOT, "tests", "tp_worker.py"), str(tmp_path)]
+    r = subprocess.run(cmd, env=env, cwd=ROOT, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import tp_worker as W
+    from furykernel_b200.program.llama import LlamaShape
+
+    s = LlamaShape(d_model=512, heads=4, kv_heads=4, head_dim=128, ffn=1024, vocab=3000, layers=2, slots=2,
+                   length=64, positions=64)
+    layers, embed, final_norm = W.model(s)
+    ids = [np.load(tmp_path / f"ids_{r}.npy") for r in range(2)]
+    xs = [np.load(tmp_path / f"x_{r}.npy") for r in range(2)]
+    logits = np.concatenate([np.load(tmp_path / f"logits_{r}.npy") for r in range(2)], axis=1)
+    kc = np.concatenate([np.load(tmp_path / f"kc_{r}.npy") for r in range(2)], axis=2)
+    vc = np.concatenate([np.load(tmp_path / f"vc_{r}.npy") for r in range(2)], axis=2)
+    assert np.array_equal(ids[0], ids[1])
+    assert np.array_equal(xs[0].view(np.uint32), xs[1].view(np.uint32))
+
+    class Full:  # the referee reads only the whole model's shape
+        pass
+
+    full = Full()
+    full.s = s
+    lw = [{"qkv": np.concatenate([w["q"], w["k"], w["v"]]), "o": w["o"],
+           "gu": np.concatenate([w["gate"], w["up"]]), "down": w["down"], "attn_norm": w["attn_norm"],
+           "mlp_norm": w["mlp_norm"]} for w in layers]
+    tokens = np.array([5, 2999], np.uint32)
+    pos = np.array([3, 7], np.uint32)
+    slot = np.arange(2, dtype=np.uint32)
+    ref, (ref_ids, decided), stored_ok = MC.referee_decode(full, lw, embed, final_norm, kc, vc, tokens, pos, slot)
+    assert stored_ok
+    assert O.within(logits, ref).all()
+    rel = float(np.max(np.abs(logits - ref[0])) / np.max(np.abs(ref[0])))
+    assert rel <= 1e-4, rel
+    assert np.array_equal(ids[0][decided], ref_ids[decided])
