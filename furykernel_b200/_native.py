@@ -55,6 +55,7 @@ def lib() -> ctypes.CDLL:
             "fkc_sm_count": (i32, [vp, ctypes.POINTER(i32)]),
             "fkc_set_pdl": (i32, [vp, i32]),
             "fkc_sync": (i32, [vp]),
+            "fkc_status": (i32, [vp, ctypes.POINTER(i32)]),
             "fkc_buf_alloc": (i32, [vp, sz, pvp]),
             "fkc_buf_free": (i32, [vp, vp]),
             "fkc_buf_zero": (i32, [vp, vp, sz]),
@@ -266,6 +267,12 @@ class Context:
 
     def sync(self) -> None:
         check(lib().fkc_sync(self.handle))
+
+    def status(self) -> int:
+        """The device status word (0, or a bounded wait's code), then cleared."""
+        code = ctypes.c_int()
+        check(lib().fkc_status(self.handle, ctypes.byref(code)))
+        return code.value
 
     def alloc(self, nbytes: int, dtype=np.float32, shape=None) -> DeviceBuffer:
         p = ctypes.c_void_p()

@@ -89,6 +89,10 @@ cudaError_t fk_launch_argmax_pick(const uint32_t* pairs, uint32_t shards, uint32
                                   cudaStream_t s);
 cudaError_t fk_launch_advance(const uint32_t* ids, uint32_t* tokens, uint32_t* pos, uint32_t m, bool pdl,
                               cudaStream_t s);
+cudaError_t fk_launch_split_tf32(const float* x, float* hi, float* lo, uint64_t n, cudaStream_t s);
+cudaError_t fk_launch_gemm_tf32x3(const float* a_hi, const float* a_lo, const float* w_hi, const float* w_lo,
+                                  float* c, uint32_t M, uint32_t N, uint32_t K, uint32_t ldc, int* err,
+                                  cudaStream_t s);
 cudaError_t fk_launch_fill_normal(float* out, uint64_t n, uint64_t seed, double mu, double sigma, cudaStream_t s);
 cudaError_t fk_launch_fill_uniform(float* out, uint64_t n, uint64_t seed, double a, double b, cudaStream_t s);
 cudaError_t fk_launch_rope_tables(float* cos_t, float* sin_t, double theta, uint32_t d, uint32_t rotated,

@@ -81,7 +81,7 @@ __device__ __forceinline__ void row_totals(const float4* __restrict__ wr, const 
 }
 
 template <int M, int PRO, int EPI>
-__global__ void __launch_bounds__(512, 1) gemv_stream_kernel(StreamArgs a) {
+__global__ void __launch_bounds__(512, 2) gemv_stream_kernel(StreamArgs a) {
   extern __shared__ float4 xs4[];  // [m][k / 4]
   __shared__ float scales[M];
   __shared__ float slots[8];

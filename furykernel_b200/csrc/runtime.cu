@@ -62,6 +62,8 @@ struct fkc_ctx {
   // Scratch of reduce_final: the 256 chains' sums and a completion counter.
   float* red_chains = nullptr;
   unsigned int* red_done = nullptr;
+  // Where kernels with bounded waits record why they gave up (0: nothing).
+  int* status = nullptr;
   std::unordered_set<void*> allocs;
   ncclComm_t comm = nullptr;
   int nranks = 1, rank = 0;
@@ -92,6 +94,8 @@ extern "C" int fkc_open(int device, fkc_ctx** out) {
   if (e == cudaSuccess) e = cudaMalloc(&c->red_chains, 256 * sizeof(float));
   if (e == cudaSuccess) e = cudaMalloc(&c->red_done, sizeof(unsigned int));
   if (e == cudaSuccess) e = cudaMemset(c->red_done, 0, sizeof(unsigned int));
+  if (e == cudaSuccess) e = cudaMalloc(&c->status, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(c->status, 0, sizeof(int));
   if (e != cudaSuccess) {
     fkc_close(c);
     return cuda_fail(e, "fkc_open");
@@ -108,6 +112,7 @@ extern "C" int fkc_close(fkc_ctx* c) {
   for (void* p : c->allocs) cudaFree(p);
   if (c->red_chains) cudaFree(c->red_chains);
   if (c->red_done) cudaFree(c->red_done);
+  if (c->status) cudaFree(c->status);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
   return FKC_OK;
@@ -135,6 +140,15 @@ extern "C" int fkc_sync(fkc_ctx* c) {
   if (!c) return fail(FKC_ERR_ARGUMENT, "fkc_sync: null context.");
   cudaSetDevice(c->device);
   FKC_CUDA(cudaStreamSynchronize(c->stream), "fkc_sync");
+  return FKC_OK;
+}
+
+extern "C" int fkc_status(fkc_ctx* c, int* code) {
+  if (!c || !code) return fail(FKC_ERR_ARGUMENT, "fkc_status: null argument.");
+  cudaSetDevice(c->device);
+  FKC_CUDA(cudaStreamSynchronize(c->stream), "fkc_status");
+  FKC_CUDA(cudaMemcpy(code, c->status, sizeof(int), cudaMemcpyDeviceToHost), "fkc_status");
+  FKC_CUDA(cudaMemset(c->status, 0, sizeof(int)), "fkc_status");
   return FKC_OK;
 }
 
@@ -462,6 +476,21 @@ int l_rope(fkc_ctx* c, const Params& p, void* const* bufs) {
       "rope");
 }
 
+// split_tf32: x hi lo | n
+int l_split_tf32(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return launched(fk_launch_split_tf32(CF(0), F(1), F(2), p.u(0), c->stream), "split_tf32");
+}
+
+// gemm_tf32x3: a a_hi a_lo w_hi w_lo c | M N K ldc. A is split into the
+// caller's a_hi / a_lo first; W comes split (split_tf32, once).
+int l_gemm_tf32x3(fkc_ctx* c, const Params& p, void* const* bufs) {
+  const uint32_t M = p.u(0), N = p.u(1), K = p.u(2), ldc = p.u(3);
+  if (ldc < N) return fail(FKC_ERR_ARGUMENT, "gemm_tf32x3: ldc %u is less than N %u.", ldc, N);
+  cudaError_t e = fk_launch_split_tf32(CF(0), F(1), F(2), (uint64_t)M * K, c->stream);
+  if (e == cudaSuccess) e = fk_launch_gemm_tf32x3(CF(1), CF(2), CF(3), CF(4), F(5), M, N, K, ldc, c->status, c->stream);
+  return launched(e, "gemm_tf32x3");
+}
+
 // argmax_pairs: x pairs | m n ldx offset
 int l_argmax_pairs(fkc_ctx* c, const Params& p, void* const* bufs) {
   return launched(fk_launch_argmax_pairs(CF(0), p.u(0), p.u(1), p.u(2), p.u(3), U(1), c->pdl, c->stream),
@@ -600,6 +629,21 @@ std::vector<KernelSpec> make_table() {
                {dim("m", 1, 65535), dim("heads", 1, 65535), dim("d", 2, 2048, 2), u32("rotated"), u32("ldx"),
                 u32("ldy")},
                l_rope});
+  t.push_back({"split_tf32",
+               256,
+               {{"x", "read", "f32"}, {"hi", "write", "f32"}, {"lo", "write", "f32"}},
+               {dim("n", 1, kMax)},
+               l_split_tf32});
+  t.push_back({"gemm_tf32x3",
+               192,
+               {{"a", "read", "f32"},
+                {"a_hi", "read_write", "f32"},
+                {"a_lo", "read_write", "f32"},
+                {"w_hi", "read", "f32"},
+                {"w_lo", "read", "f32"},
+                {"c", "write", "f32"}},
+               {dim("M", 1, 1048576), dim("N", 1, 1048576), dim("K", 32, 1048576, 32), u32("ldc")},
+               l_gemm_tf32x3});
   t.push_back({"argmax_pairs",
                1024,
                {{"x", "read", "f32"}, {"pairs", "write", "u32"}},

@@ -133,6 +133,12 @@ SPEC_KERNELS = {
         KernelSig("rope", [_f32("x"), _u32("pos"), _f32("cos"), _f32("sin"), _f32("y", "write")],
                   [_dim("m", 1, 65535), _dim("heads", 1, 65535), _dim("d", 2, 2048, 2), _u("rotated"), _u("ldx"),
                    _u("ldy")], threads=64),
+        KernelSig("split_tf32", [_f32("x"), _f32("hi", "write"), _f32("lo", "write")], [_dim("n", 1, _MAX)]),
+        KernelSig("gemm_tf32x3",
+                  [_f32("a"), _f32("a_hi", "read_write"), _f32("a_lo", "read_write"), _f32("w_hi"), _f32("w_lo"),
+                   _f32("c", "write")],
+                  [_dim("M", 1, 1048576), _dim("N", 1, 1048576), _dim("K", 32, 1048576, 32), _u("ldc")],
+                  threads=192),
         KernelSig("argmax_pairs", [_f32("x"), _u32("pairs", "write")],
                   [_dim("m", 1, 65535), _dim("n", 1, _MAX), _u("ldx"), _u("offset")], threads=1024),
         KernelSig("argmax_pick", [_u32("pairs"), _u32("ids", "write")], [_dim("shards", 1, 64), _dim("m", 1, 65535)]),

@@ -66,6 +66,11 @@ int fkc_sm_count(fkc_ctx *ctx, int *sms);
  * (overlaps a launch's start with its predecessor's end). Default off. */
 int fkc_set_pdl(fkc_ctx *ctx, int enabled);
 int fkc_sync(fkc_ctx *ctx);
+/* Synchronizes, then reads and clears the context's device status word:
+ * 0, or the code a kernel with bounded waits recorded when one ran out
+ * (the tensor-core GEMM: 1 a stage never filled, 2 a stage never freed,
+ * 3 the accumulator never completed). */
+int fkc_status(fkc_ctx *ctx, int *code);
 
 /* ---- memory ------------------------------------------------------------- */
 /* Buffers the engine binds to kernels (the reference's caller-owned slices,

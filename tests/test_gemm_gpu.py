@@ -1,0 +1,54 @@
+"""The prefill GEMM on tcgen05 tensor cores (3xTF32) through the C ABI,
+against the f64 evaluator: every element within its binary32 bound
+(dotA, src/FuryKernel/Program/Eval.hs:747-754) and the normwise relative
+error max|C - C64| / max|C64| <= 1e-4 (the path's GEMM tolerance). The
+tensor cores sum in their own order, so no bit comparison."""
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    from furykernel_b200 import _native as N
+
+    c = N.Context(0)
+    yield c
+    c.close()
+
+
+def gemm(ctx, a, w):
+    M, K = a.shape
+    n = w.shape[0]
+    da, dw = ctx.to_device(a), ctx.to_device(w)
+    whi, wlo, ahi, alo = ctx.empty((n, K)), ctx.empty((n, K)), ctx.empty((M, K)), ctx.empty((M, K))
+    dc = ctx.zeros((M, n))
+    ctx.launch("split_tf32", {"n": n * K}, [dw, whi, wlo])
+    ctx.launch("gemm_tf32x3", {"M": M, "N": n, "K": K, "ldc": n}, [da, ahi, alo, whi, wlo, dc])
+    status = ctx.status()
+    c = dc.download()
+    hi, lo = whi.download(), wlo.download()
+    for b in (da, dw, whi, wlo, ahi, alo, dc):
+        b.free()
+    return c, status, hi, lo
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 384, 512), (200, 300, 4096), (129, 130, 96),
+                                   (512, 11008, 4096)])
+def test_gemm_tf32x3_within_bounds(ctx, M, N, K):
+    a = O.normal(3 + M, M * K).reshape(M, K)
+    w = O.normal(4 + N, N * K, 0.0, 0.02).reshape(N, K)
+    c, status, hi, lo = gemm(ctx, a, w)
+    assert status == 0
+    # The split: hi + lo represents w to within 2^-22 of |w|; both are TF32 values.
+    assert np.all(np.abs(hi.astype(np.float64) + lo - w) <= np.abs(w) * 2.0 ** -21)
+    assert np.all(hi.view(np.uint32) & 0x1FFF == 0) and np.all(lo.view(np.uint32) & 0x1FFF == 0)
+    exact = a.astype(np.float64) @ w.astype(np.float64).T
+    assert np.max(np.abs(c - exact)) / np.max(np.abs(exact)) <= 1e-4
+    rows = np.arange(0, M, max(1, M // 4))[:4]  # the referee's bounds on a sample of rows
+    ref = O.r_linear(w, O.r_input(a[rows]))
+    assert O.within(c[rows], ref).all()
