@@ -86,6 +86,10 @@ def lib() -> ctypes.CDLL:
             "fkc_allgather_u32": (i32, [vp, vp, vp, sz]),
             "fkc_comm_rank": (i32, [vp, ctypes.POINTER(i32), ctypes.POINTER(i32)]),
             "fkc_reduce_sum_f32_noalloc": (i32, [vp, u64, vp, vp]),
+            "fkc_peer_region_bytes": (sz, []),
+            "fkc_peer_alloc": (i32, [vp, sz, pvp, vp]),
+            "fkc_peer_open": (i32, [vp, vp, pvp]),
+            "fkc_peer_set": (i32, [vp, i32, i32, pvp]),
             "fkc_comm_destroy": (i32, [vp]),
         }
         for name, (res, args) in sig.items():

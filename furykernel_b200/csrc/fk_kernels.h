@@ -5,7 +5,25 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-enum { FK_PRO_NONE = 0, FK_PRO_RMSNORM = 1, FK_PRO_SILU = 2 };
+enum { FK_PRO_NONE = 0, FK_PRO_RMSNORM = 1, FK_PRO_SILU = 2, FK_PRO_REDUCE_RMSNORM = 3 };
+
+// Tensor-parallel exchange over NVLink peer memory. Every rank owns one
+// region, mapped into every other rank's process; by byte offset:
+//   0    u32 flags[FK_XBUFS][FK_MAX_PEERS]  the epoch rank q last signalled into this region, by buffer
+//   128  u32 epoch[FK_XBUFS]                this rank's own signals so far, by buffer
+//   160  u32 counter[FK_XBUFS]              blocks of the running producer that have finished
+//   256  f32 data[FK_XBUFS][FK_MAX_PEERS][FK_XSLOT]  rank q's partial rows, by buffer
+// Buffers: 0 the attention output projection's partials, 1 the down
+// projection's, 2 the vocabulary shards' greedy candidates.
+constexpr int FK_MAX_PEERS = 8;
+constexpr int FK_XBUFS = 3;
+constexpr unsigned FK_XSLOT = 65536;  // floats of a rank's slot: 4 rows of 16384
+constexpr size_t FK_XREGION = 256 + (size_t)FK_XBUFS * FK_MAX_PEERS * FK_XSLOT * 4;
+
+struct FkPeers {
+  char* base[FK_MAX_PEERS];  // each rank's region as this process maps it
+  unsigned world, rank;
+};
 
 struct FkGemv {
   const float* w;      // [n, k] out_in
@@ -20,6 +38,12 @@ struct FkGemv {
   float eps, factor;
   bool pdl;        // launch as a programmatic dependent of the previous kernel
   bool silu_pair;  // rows interleave gate and up: y_i = silu(row 2i) * row 2i+1
+  // Tensor parallelism over peer memory (streaming kernel only):
+  bool scatter;    // write the partial rows into every rank's exchange buffer xbuf
+  FkPeers peers;
+  unsigned xbuf;
+  float* xout;     // FK_PRO_REDUCE_RMSNORM: where block 0 stores the reduced rows
+  int* err;        // the context's status word
 };
 
 struct FkAttend {
@@ -84,9 +108,9 @@ cudaError_t fk_launch_rope(const float* x, uint32_t m, uint32_t heads, uint32_t 
 cudaError_t fk_launch_add(const float* a, const float* b, float* y, uint64_t n, cudaStream_t s);
 cudaError_t fk_launch_silu_mul(const float* a, const float* b, float* y, uint64_t n, cudaStream_t s);
 cudaError_t fk_launch_argmax_pairs(const float* x, uint32_t m, uint32_t n, uint32_t ldx, uint32_t offset,
-                                   uint32_t* pairs, bool pdl, cudaStream_t s);
-cudaError_t fk_launch_argmax_pick(const uint32_t* pairs, uint32_t shards, uint32_t m, uint32_t* ids, bool pdl,
-                                  cudaStream_t s);
+                                   uint32_t* pairs, const FkPeers* peers, bool pdl, cudaStream_t s);
+cudaError_t fk_launch_argmax_pick(const uint32_t* pairs, uint32_t shards, uint32_t m, uint32_t* ids,
+                                  const FkPeers* peers, int* err, bool pdl, cudaStream_t s);
 cudaError_t fk_launch_advance(const uint32_t* ids, uint32_t* tokens, uint32_t* pos, uint32_t m, bool pdl,
                               cudaStream_t s);
 cudaError_t fk_launch_split_tf32(const float* x, float* hi, float* lo, uint64_t n, cudaStream_t s);

@@ -4,6 +4,7 @@
 
 #include "fk_common.cuh"
 #include "fk_kernels.h"
+#include "fk_peers.cuh"
 
 namespace fk {
 
@@ -81,7 +82,8 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
 // that value's index plus the shard's offset, as argmax_kernel finds it
 // (first index of the maximum; a NaN first element wins). Grid m, 1024 threads.
 __global__ void __launch_bounds__(1024) argmax_pairs_kernel(const float* __restrict__ x, uint32_t n, uint32_t ldx,
-                                                            uint32_t offset, uint32_t* __restrict__ pairs) {
+                                                            uint32_t offset, uint32_t* __restrict__ pairs,
+                                                            FkPeers peers, int scatter) {
   __shared__ float sv[32];
   __shared__ uint32_t si[32];
   grid_wait();
@@ -131,26 +133,42 @@ __global__ void __launch_bounds__(1024) argmax_pairs_kernel(const float* __restr
         bv = xr[0];
         bi = 0;
       }
-      pairs[2 * r] = __float_as_uint(bv);
-      pairs[2 * r + 1] = bi == 0xffffffffu ? bi : bi + offset;
+      const uint32_t idx = bi == 0xffffffffu ? bi : bi + offset;
+      if (scatter) {  // into every rank's exchange buffer 2, this rank's slot
+        for (uint32_t q = 0; q < peers.world; ++q) {
+          uint32_t* slot = reinterpret_cast<uint32_t*>(xdata(peers.base[q], 2, peers.rank));
+          slot[2 * r] = __float_as_uint(bv);
+          slot[2 * r + 1] = idx;
+        }
+      } else {
+        pairs[2 * r] = __float_as_uint(bv);
+        pairs[2 * r + 1] = idx;
+      }
     }
   }
+  if (scatter) peers_signal(peers, 2);
 }
 
 // The greedy id from the shards' candidates, [shards][m][2], in shard order:
 // the fold over the whole row keeps the first shard's NaN-first candidate,
 // else the largest value, ties to the lower index.
 __global__ void argmax_pick_kernel(const uint32_t* __restrict__ pairs, uint32_t shards, uint32_t m,
-                                   uint32_t* __restrict__ ids) {
+                                   uint32_t* __restrict__ ids, FkPeers peers, int gather, int* err) {
   grid_wait();
   grid_launch_dependents();
+  if (gather) peers_wait(peers, 2, err);
+  // Shard s's candidates: gathered by NCCL at pairs + 2 s m, or in this
+  // rank's exchange buffer 2, slot s.
+  auto src = [&](uint32_t s) -> const uint32_t* {
+    return gather ? reinterpret_cast<const uint32_t*>(xdata(peers.base[peers.rank], 2, s)) : pairs + (size_t)s * m * 2;
+  };
   for (uint32_t r = threadIdx.x; r < m; r += blockDim.x) {
-    float bv = __uint_as_float(pairs[2 * r]);
-    uint32_t bi = pairs[2 * r + 1];
+    float bv = __uint_as_float(src(0)[2 * r]);
+    uint32_t bi = src(0)[2 * r + 1];
     if (!isnan(bv)) {
       for (uint32_t s = 1; s < shards; ++s) {
-        const float v = __uint_as_float(pairs[((size_t)s * m + r) * 2]);
-        const uint32_t i = pairs[((size_t)s * m + r) * 2 + 1];
+        const float v = __uint_as_float(src(s)[2 * r]);
+        const uint32_t i = src(s)[2 * r + 1];
         if (v > bv || (v == bv && i < bi)) {
           bv = v;
           bi = i;
@@ -222,16 +240,21 @@ __global__ void advance_kernel(const uint32_t* __restrict__ ids, uint32_t* __res
 }  // namespace fk
 
 cudaError_t fk_launch_argmax_pairs(const float* x, uint32_t m, uint32_t n, uint32_t ldx, uint32_t offset,
-                                   uint32_t* pairs, bool pdl, cudaStream_t s) {
+                                   uint32_t* pairs, const FkPeers* peers, bool pdl, cudaStream_t s) {
   if (m == 0) return cudaSuccess;
-  if (n == 0) return cudaErrorInvalidValue;
-  return fk_launch_ex(fk::argmax_pairs_kernel, dim3(m), dim3(1024), 0, s, pdl, x, n, ldx, offset, pairs);
+  if (n == 0 || (peers && 2 * (size_t)m > FK_XSLOT)) return cudaErrorInvalidValue;
+  FkPeers none = {};
+  return fk_launch_ex(fk::argmax_pairs_kernel, dim3(m), dim3(1024), 0, s, pdl, x, n, ldx, offset, pairs,
+                      peers ? *peers : none, peers ? 1 : 0);
 }
 
-cudaError_t fk_launch_argmax_pick(const uint32_t* pairs, uint32_t shards, uint32_t m, uint32_t* ids, bool pdl,
-                                  cudaStream_t s) {
+cudaError_t fk_launch_argmax_pick(const uint32_t* pairs, uint32_t shards, uint32_t m, uint32_t* ids,
+                                  const FkPeers* peers, int* err, bool pdl, cudaStream_t s) {
   if (m == 0) return cudaSuccess;
-  return fk_launch_ex(fk::argmax_pick_kernel, dim3(1), dim3(256), 0, s, pdl, pairs, shards, m, ids);
+  if (peers && shards != peers->world) return cudaErrorInvalidValue;
+  FkPeers none = {};
+  return fk_launch_ex(fk::argmax_pick_kernel, dim3(1), dim3(256), 0, s, pdl, pairs, shards, m, ids,
+                      peers ? *peers : none, peers ? 1 : 0, err);
 }
 
 cudaError_t fk_launch_advance(const uint32_t* ids, uint32_t* tokens, uint32_t* pos, uint32_t m, bool pdl,

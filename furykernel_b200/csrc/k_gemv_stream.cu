@@ -19,8 +19,16 @@
 // SiLU-gate of a row pair, for weights whose rows interleave gate and up
 // (row 2i gate_i, row 2i+1 up_i): y_i = silu(gate_i) * up_i, computed on the
 // pair's tile instead of in the next step's prologue (the same bits, once).
+//
+// Tensor parallelism (fk_peers.cuh): the row-parallel projections scatter
+// their partial rows into every rank's exchange region (SEPI_SCATTER); the
+// next GEMV's prologue (SPRO_REDUCE_RMSNORM) waits for every rank's partial,
+// forms the residual row x_new = r + (((P_0 + P_1) + P_2) + ...), ranks in
+// order, so that every rank holds the same bits, stores it (block 0), and
+// normalizes it as SPRO_RMSNORM does.
 #include "fk_common.cuh"
 #include "fk_kernels.h"
+#include "fk_peers.cuh"
 
 namespace fk {
 
@@ -34,10 +42,14 @@ struct StreamArgs {
   uint32_t ldx, ldr, ldy;
   uint32_t up_off;
   float eps, factor;
+  FkPeers peers;
+  uint32_t xbuf;  // the exchange buffer scattered into, or reduced from
+  float* xout;    // the reduced residual rows [m, k], stored by block 0
+  int* err;
 };
 
-enum { SPRO_NONE = 0, SPRO_RMSNORM = 1, SPRO_SILU = 2 };
-enum { SEPI_NONE = 0, SEPI_ADD = 1, SEPI_SILU_PAIR = 2 };
+enum { SPRO_NONE = 0, SPRO_RMSNORM = 1, SPRO_SILU = 2, SPRO_REDUCE_RMSNORM = 3 };
+enum { SEPI_NONE = 0, SEPI_ADD = 1, SEPI_SILU_PAIR = 2, SEPI_SCATTER = 3 };
 constexpr int kStreamWarps = 16;
 
 __device__ __forceinline__ float silu_of(float a, float b) {
@@ -105,15 +117,39 @@ __global__ void __launch_bounds__(512, 2) gemv_stream_kernel(StreamArgs a) {
   grid_wait();
   grid_launch_dependents();
 
-  if (PRO == SPRO_RMSNORM) {
-    // RMSNorm's scale of each staged row: threads 0..255 are the spec's 256
-    // lanes, each over packs t, t + 256, ... (src/FuryKernel/Reduce.hs:59-85).
+  constexpr bool NORM = PRO == SPRO_RMSNORM || PRO == SPRO_REDUCE_RMSNORM;
+  if (PRO == SPRO_REDUCE_RMSNORM) peers_wait(a.peers, a.xbuf, a.err);
+  // Stage x: as given, the SiLU-gate of a gate/up row, or the residual plus
+  // every rank's partial, in rank order.
+  for (uint32_t idx = threadIdx.x; idx < a.m * packs; idx += blockDim.x) {
+    const uint32_t i = idx / packs, j = idx - i * packs;
+    const float* xr = a.x + (size_t)i * a.ldx;
+    float4 v = __ldg(reinterpret_cast<const float4*>(xr) + j);
+    if (PRO == SPRO_SILU) {
+      const float4 u = __ldg(reinterpret_cast<const float4*>(xr + a.up_off) + j);
+      v = make_float4(silu_of(v.x, u.x), silu_of(v.y, u.y), silu_of(v.z, u.z), silu_of(v.w, u.w));
+    } else if (PRO == SPRO_REDUCE_RMSNORM) {
+      char* me = a.peers.base[a.peers.rank];
+      float4 s = reinterpret_cast<const float4*>(xdata(me, a.xbuf, 0) + (size_t)i * a.k)[j];
+      for (uint32_t q = 1; q < a.peers.world; ++q) {
+        const float4 p = reinterpret_cast<const float4*>(xdata(me, a.xbuf, q) + (size_t)i * a.k)[j];
+        s = make_float4(__fadd_rn(s.x, p.x), __fadd_rn(s.y, p.y), __fadd_rn(s.z, p.z), __fadd_rn(s.w, p.w));
+      }
+      v = make_float4(__fadd_rn(v.x, s.x), __fadd_rn(v.y, s.y), __fadd_rn(v.z, s.z), __fadd_rn(v.w, s.w));
+      if (blockIdx.x == 0) reinterpret_cast<float4*>(a.xout + (size_t)i * a.k)[j] = v;
+    }
+    xs4[(size_t)i * packs + j] = v;
+  }
+  __syncthreads();
+  if (NORM) {
+    // RMSNorm of each staged row: threads 0..255 are the spec's 256 lanes,
+    // each over packs t, t + 256, ... (src/FuryKernel/Reduce.hs:59-85); then
+    // x * scale * gamma (* factor) in place.
     for (uint32_t i = 0; i < a.m; ++i) {
       if (threadIdx.x < 256) {
-        const float4* x4 = reinterpret_cast<const float4*>(a.x + (size_t)i * a.ldx);
         float acc = 0.0f;
         for (uint32_t j = threadIdx.x; j < packs; j += 256u) {
-          const float4 v = __ldg(x4 + j);
+          const float4 v = xs4[(size_t)i * packs + j];
           acc = __fadd_rn(acc, __fmul_rn(v.x, v.x));
           acc = __fadd_rn(acc, __fmul_rn(v.y, v.y));
           acc = __fadd_rn(acc, __fmul_rn(v.z, v.z));
@@ -126,12 +162,9 @@ __global__ void __launch_bounds__(512, 2) gemv_stream_kernel(StreamArgs a) {
       if (threadIdx.x == 0) scales[i] = rsqrt_rounded(__fadd_rn(__fdiv_rn(tg_sum8(slots), (float)a.k), a.eps));
       __syncthreads();
     }
-  }
-  for (uint32_t idx = threadIdx.x; idx < a.m * packs; idx += blockDim.x) {
-    const uint32_t i = idx / packs, j = idx - i * packs;
-    const float* xr = a.x + (size_t)i * a.ldx;
-    float4 v = __ldg(reinterpret_cast<const float4*>(xr) + j);
-    if (PRO == SPRO_RMSNORM) {
+    for (uint32_t idx = threadIdx.x; idx < a.m * packs; idx += blockDim.x) {
+      const uint32_t i = idx / packs, j = idx - i * packs;
+      float4 v = xs4[(size_t)i * packs + j];
       const float sc = scales[i];
       v = make_float4(__fmul_rn(v.x, sc), __fmul_rn(v.y, sc), __fmul_rn(v.z, sc), __fmul_rn(v.w, sc));
       if (a.gamma) {
@@ -141,13 +174,10 @@ __global__ void __launch_bounds__(512, 2) gemv_stream_kernel(StreamArgs a) {
       if (a.factor != 1.0f)
         v = make_float4(__fmul_rn(v.x, a.factor), __fmul_rn(v.y, a.factor), __fmul_rn(v.z, a.factor),
                         __fmul_rn(v.w, a.factor));
-    } else if (PRO == SPRO_SILU) {
-      const float4 u = __ldg(reinterpret_cast<const float4*>(xr + a.up_off) + j);
-      v = make_float4(silu_of(v.x, u.x), silu_of(v.y, u.y), silu_of(v.z, u.z), silu_of(v.w, u.w));
+      xs4[(size_t)i * packs + j] = v;
     }
-    xs4[(size_t)i * packs + j] = v;
+    __syncthreads();
   }
-  __syncthreads();
 
   for (uint32_t slot = (uint32_t)warp;; slot += kStreamWarps) {
     const uint32_t u = blockIdx.x + slot * G;
@@ -162,6 +192,12 @@ __global__ void __launch_bounds__(512, 2) gemv_stream_kernel(StreamArgs a) {
 #pragma unroll
       for (int i = 0; i < M; ++i) {
         if (i >= (int)a.m) break;
+        if (EPI == SEPI_SCATTER) {
+          // This rank's partial of output u, into every rank's slot for it.
+          for (uint32_t q = 0; q < a.peers.world; ++q)
+            xdata(a.peers.base[q], a.xbuf, a.peers.rank)[(size_t)i * a.n + u] = t0[i];
+          continue;
+        }
         float v;
         if (EPI == SEPI_SILU_PAIR)
           v = silu_of(t0[i], t1[i]);
@@ -173,6 +209,7 @@ __global__ void __launch_bounds__(512, 2) gemv_stream_kernel(StreamArgs a) {
       }
     }
   }
+  if (EPI == SEPI_SCATTER) peers_signal(a.peers, a.xbuf);
 }
 
 template <int M, int PRO, int EPI>
@@ -229,15 +266,27 @@ cudaError_t fk_launch_gemv_stream(const FkGemv& g, int sms, cudaStream_t st) {
   a.up_off = g.up_off;
   a.eps = g.eps;
   a.factor = g.factor;
+  a.peers = g.peers;
+  a.xbuf = g.xbuf;
+  a.xout = g.xout;
+  a.err = g.err;
   using namespace fk;
-  const int epi = g.silu_pair ? SEPI_SILU_PAIR : (g.r ? SEPI_ADD : SEPI_NONE);
-  switch (g.prologue * 3 + epi) {
-    case FK_PRO_NONE * 3 + SEPI_NONE: return stream_m<SPRO_NONE, SEPI_NONE>(a, sms, st, g.pdl);
-    case FK_PRO_NONE * 3 + SEPI_ADD: return stream_m<SPRO_NONE, SEPI_ADD>(a, sms, st, g.pdl);
-    case FK_PRO_RMSNORM * 3 + SEPI_NONE: return stream_m<SPRO_RMSNORM, SEPI_NONE>(a, sms, st, g.pdl);
-    case FK_PRO_RMSNORM * 3 + SEPI_SILU_PAIR: return stream_m<SPRO_RMSNORM, SEPI_SILU_PAIR>(a, sms, st, g.pdl);
-    case FK_PRO_SILU * 3 + SEPI_NONE: return stream_m<SPRO_SILU, SEPI_NONE>(a, sms, st, g.pdl);
-    case FK_PRO_SILU * 3 + SEPI_ADD: return stream_m<SPRO_SILU, SEPI_ADD>(a, sms, st, g.pdl);
+  const bool peer = g.scatter || g.prologue == FK_PRO_REDUCE_RMSNORM;
+  if (peer && (g.peers.world < 1 || g.xbuf >= FK_XBUFS || (size_t)g.m * (g.scatter ? g.n : g.k) > FK_XSLOT ||
+               (g.prologue == FK_PRO_REDUCE_RMSNORM && !g.xout)))
+    return cudaErrorInvalidValue;
+  const int epi = g.scatter ? SEPI_SCATTER : g.silu_pair ? SEPI_SILU_PAIR : (g.r ? SEPI_ADD : SEPI_NONE);
+  switch (g.prologue * 4 + epi) {
+    case FK_PRO_NONE * 4 + SEPI_NONE: return stream_m<SPRO_NONE, SEPI_NONE>(a, sms, st, g.pdl);
+    case FK_PRO_NONE * 4 + SEPI_ADD: return stream_m<SPRO_NONE, SEPI_ADD>(a, sms, st, g.pdl);
+    case FK_PRO_NONE * 4 + SEPI_SCATTER: return stream_m<SPRO_NONE, SEPI_SCATTER>(a, sms, st, g.pdl);
+    case FK_PRO_RMSNORM * 4 + SEPI_NONE: return stream_m<SPRO_RMSNORM, SEPI_NONE>(a, sms, st, g.pdl);
+    case FK_PRO_RMSNORM * 4 + SEPI_SILU_PAIR: return stream_m<SPRO_RMSNORM, SEPI_SILU_PAIR>(a, sms, st, g.pdl);
+    case FK_PRO_SILU * 4 + SEPI_NONE: return stream_m<SPRO_SILU, SEPI_NONE>(a, sms, st, g.pdl);
+    case FK_PRO_SILU * 4 + SEPI_ADD: return stream_m<SPRO_SILU, SEPI_ADD>(a, sms, st, g.pdl);
+    case FK_PRO_REDUCE_RMSNORM * 4 + SEPI_NONE: return stream_m<SPRO_REDUCE_RMSNORM, SEPI_NONE>(a, sms, st, g.pdl);
+    case FK_PRO_REDUCE_RMSNORM * 4 + SEPI_SILU_PAIR:
+      return stream_m<SPRO_REDUCE_RMSNORM, SEPI_SILU_PAIR>(a, sms, st, g.pdl);
     default: return cudaErrorInvalidValue;
   }
 }

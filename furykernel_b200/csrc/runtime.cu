@@ -67,6 +67,10 @@ struct fkc_ctx {
   std::unordered_set<void*> allocs;
   ncclComm_t comm = nullptr;
   int nranks = 1, rank = 0;
+  // The peer set: every rank's exchange region, this rank's own included,
+  // by rank (fkc_peer_set).
+  FkPeers peers = {};
+  std::unordered_set<void*> opened;  // peers' regions mapped here
 };
 
 struct fkc_graph {
@@ -109,6 +113,7 @@ extern "C" int fkc_close(fkc_ctx* c) {
   cudaSetDevice(c->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
   if (c->comm) ncclCommDestroy(c->comm);
+  for (void* p : c->opened) cudaIpcCloseMemHandle(p);
   for (void* p : c->allocs) cudaFree(p);
   if (c->red_chains) cudaFree(c->red_chains);
   if (c->red_done) cudaFree(c->red_done);
@@ -493,13 +498,74 @@ int l_gemm_tf32x3(fkc_ctx* c, const Params& p, void* const* bufs) {
 
 // argmax_pairs: x pairs | m n ldx offset
 int l_argmax_pairs(fkc_ctx* c, const Params& p, void* const* bufs) {
-  return launched(fk_launch_argmax_pairs(CF(0), p.u(0), p.u(1), p.u(2), p.u(3), U(1), c->pdl, c->stream),
+  return launched(fk_launch_argmax_pairs(CF(0), p.u(0), p.u(1), p.u(2), p.u(3), U(1), nullptr, c->pdl, c->stream),
                   "argmax_pairs");
+}
+
+bool have_peers(fkc_ctx* c) { return c->peers.world >= 1 && c->peers.base[0] != nullptr; }
+
+// argmax_scatter: x | m n ldx offset: the candidates into every rank's buffer 2.
+int l_argmax_scatter(fkc_ctx* c, const Params& p, void* const* bufs) {
+  if (!have_peers(c)) return fail(FKC_ERR_STATE, "argmax_scatter: the context has no peer set.");
+  return launched(fk_launch_argmax_pairs(CF(0), p.u(0), p.u(1), p.u(2), p.u(3), nullptr, &c->peers, c->pdl,
+                                         c->stream),
+                  "argmax_scatter");
+}
+
+// argmax_gather_pick: ids | m: the ranks' candidates from this rank's buffer 2.
+int l_argmax_gather_pick(fkc_ctx* c, const Params& p, void* const* bufs) {
+  if (!have_peers(c)) return fail(FKC_ERR_STATE, "argmax_gather_pick: the context has no peer set.");
+  return launched(fk_launch_argmax_pick(nullptr, c->peers.world, p.u(0), U(0), &c->peers, c->status, c->pdl,
+                                        c->stream),
+                  "argmax_gather_pick");
+}
+
+// gemv_scatter: w x | n k m split ldx xbuf: this rank's partial rows into
+// every rank's exchange buffer xbuf.
+int l_gemv_scatter(fkc_ctx* c, const Params& p, void* const* bufs) {
+  if (!have_peers(c)) return fail(FKC_ERR_STATE, "gemv_scatter: the context has no peer set.");
+  FkGemv g = {};
+  g.w = CF(0), g.x = CF(1);
+  g.n = p.u(0), g.k = p.u(1), g.m = p.u(2), g.split = p.u(3), g.ldx = p.u(4), g.xbuf = p.u(5);
+  g.factor = 1.0f;
+  g.pdl = c->pdl;
+  g.prologue = FK_PRO_NONE;
+  g.scatter = true;
+  g.peers = c->peers;
+  g.err = c->status;
+  if (!fk_gemv_streams(g)) return fail(FKC_ERR_ARGUMENT, "gemv_scatter: m %u is past the streaming kernel's 4.", g.m);
+  return launched(fk_launch_gemv_stream(g, c->sms, c->stream), "gemv_scatter");
+}
+
+// gemv_reduce_rmsnorm(_silu): w r gamma xout y | n k m split ldr ldy eps factor
+// xbuf: x = r + the ranks' partials in buffer xbuf, in rank order, stored to
+// xout; then RMSNorm and the GEMV (SiLU-gate of row pairs for _silu).
+int reduce_gemv(fkc_ctx* c, const Params& p, void* const* bufs, bool silu, const char* name) {
+  if (!have_peers(c)) return fail(FKC_ERR_STATE, "%s: the context has no peer set.", name);
+  FkGemv g = {};
+  g.w = CF(0), g.x = CF(1), g.gamma = CF(2), g.xout = F(3), g.y = F(4);
+  g.n = p.u(0), g.k = p.u(1), g.m = p.u(2), g.split = p.u(3), g.ldx = p.u(4), g.ldy = p.u(5);
+  g.eps = p.f(6), g.factor = p.f(7), g.xbuf = p.u(8);
+  g.pdl = c->pdl;
+  g.prologue = FK_PRO_REDUCE_RMSNORM;
+  g.silu_pair = silu;
+  g.peers = c->peers;
+  g.err = c->status;
+  if (g.ldx != g.k) return fail(FKC_ERR_ARGUMENT, "%s: the residual rows must be whole (ldr %u, k %u).", name, g.ldx, g.k);
+  if (!fk_gemv_streams(g)) return fail(FKC_ERR_ARGUMENT, "%s: m %u is past the streaming kernel's 4.", name, g.m);
+  return launched(fk_launch_gemv_stream(g, c->sms, c->stream), name);
+}
+int l_gemv_reduce_rmsnorm(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return reduce_gemv(c, p, bufs, false, "gemv_reduce_rmsnorm");
+}
+int l_gemv_reduce_rmsnorm_silu(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return reduce_gemv(c, p, bufs, true, "gemv_reduce_rmsnorm_silu");
 }
 
 // argmax_pick: pairs ids | shards m
 int l_argmax_pick(fkc_ctx* c, const Params& p, void* const* bufs) {
-  return launched(fk_launch_argmax_pick(CU(0), p.u(0), p.u(1), U(1), c->pdl, c->stream), "argmax_pick");
+  return launched(fk_launch_argmax_pick(CU(0), p.u(0), p.u(1), U(1), nullptr, nullptr, c->pdl, c->stream),
+                  "argmax_pick");
 }
 
 // advance: ids tokens pos | m
@@ -654,6 +720,29 @@ std::vector<KernelSpec> make_table() {
                {{"pairs", "read", "u32"}, {"ids", "write", "u32"}},
                {dim("shards", 1, 64), dim("m", 1, 65535)},
                l_argmax_pick});
+  t.push_back({"argmax_scatter",
+               1024,
+               {{"x", "read", "f32"}},
+               {dim("m", 1, 4), dim("n", 1, kMax), u32("ldx"), u32("offset")},
+               l_argmax_scatter});
+  t.push_back({"argmax_gather_pick", 256, {{"ids", "write", "u32"}}, {dim("m", 1, 4)}, l_argmax_gather_pick});
+  t.push_back({"gemv_scatter",
+               512,
+               {{"w", "read", "f32"}, {"x", "read", "f32"}},
+               {dim("n", 1, 65536), dim("k", 4, 65536, 4), dim("m", 1, 4), dim("split", 1, 8), u32("ldx"),
+                dim("xbuf", 0, 1)},
+               l_gemv_scatter});
+  for (int silu = 0; silu < 2; ++silu)
+    t.push_back({silu ? "gemv_reduce_rmsnorm_silu" : "gemv_reduce_rmsnorm",
+                 512,
+                 {{"w", "read", "f32"},
+                  {"r", "read", "f32"},
+                  {"gamma", "read", "f32"},
+                  {"xout", "write", "f32"},
+                  {"y", "write", "f32"}},
+                 {dim("n", 1, 1048576), dim("k", 4, 16384, 4), dim("m", 1, 4), dim("split", 1, 8), u32("ldr"),
+                  u32("ldy"), f32("eps"), f32("factor"), dim("xbuf", 0, 1)},
+                 silu ? l_gemv_reduce_rmsnorm_silu : l_gemv_reduce_rmsnorm});
   t.push_back({"advance",
                256,
                {{"ids", "read", "u32"}, {"tokens", "write", "u32"}, {"pos", "read_write", "u32"}},
@@ -901,6 +990,49 @@ extern "C" int fkc_comm_rank(fkc_ctx* c, int* rank, int* nranks) {
   if (!c || !rank || !nranks) return fail(FKC_ERR_ARGUMENT, "fkc_comm_rank: null argument.");
   *rank = c->rank;
   *nranks = c->nranks;
+  return FKC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Peer memory over NVLink: exchange regions mapped between the processes
+
+extern "C" size_t fkc_peer_region_bytes(void) { return FK_XREGION; }
+
+extern "C" int fkc_peer_alloc(fkc_ctx* c, size_t bytes, void** local, void* handle64) {
+  if (!c || !local || !handle64) return fail(FKC_ERR_ARGUMENT, "fkc_peer_alloc: null argument.");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "an IPC handle is 64 bytes");
+  int rc = fkc_buf_alloc(c, bytes, local);
+  if (rc) return rc;
+  rc = fkc_buf_zero(c, *local, bytes);
+  if (rc) return rc;
+  FKC_CUDA(cudaStreamSynchronize(c->stream), "fkc_peer_alloc");
+  cudaIpcMemHandle_t h;
+  FKC_CUDA(cudaIpcGetMemHandle(&h, *local), "fkc_peer_alloc: cudaIpcGetMemHandle");
+  memcpy(handle64, &h, sizeof h);
+  return FKC_OK;
+}
+
+extern "C" int fkc_peer_open(fkc_ctx* c, const void* handle64, void** peer) {
+  if (!c || !handle64 || !peer) return fail(FKC_ERR_ARGUMENT, "fkc_peer_open: null argument.");
+  cudaSetDevice(c->device);
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof h);
+  void* p = nullptr;
+  FKC_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "fkc_peer_open: cudaIpcOpenMemHandle");
+  c->opened.insert(p);
+  *peer = p;
+  return FKC_OK;
+}
+
+extern "C" int fkc_peer_set(fkc_ctx* c, int world, int rank, void* const* regions) {
+  if (!c || !regions || world < 1 || world > FK_MAX_PEERS || rank < 0 || rank >= world)
+    return fail(FKC_ERR_ARGUMENT, "fkc_peer_set: %d ranks (at most %d), rank %d.", world, FK_MAX_PEERS, rank);
+  for (int q = 0; q < world; ++q) {
+    if (!regions[q]) return fail(FKC_ERR_ARGUMENT, "fkc_peer_set: no region for rank %d.", q);
+    c->peers.base[q] = (char*)regions[q];
+  }
+  c->peers.world = (uint32_t)world;
+  c->peers.rank = (uint32_t)rank;
   return FKC_OK;
 }
 

@@ -231,7 +231,7 @@ class Llama:
 
     def __init__(self, ctx: N.Context, shape: LlamaShape, batch: int, seed: int = 2026, chunk: int = 32,
                  pdl: bool = True, prefill_kv: float | None = None, rank: int = 0, world: int = 1,
-                 host_weights=None):
+                 host_weights=None, peer_exchange: bool = True):
         import dataclasses
 
         full = shape
@@ -249,6 +249,10 @@ class Llama:
         # up on its own tiles and stores it, and the down step reads it: the
         # same bits as recomputing it in the down step, computed once.
         self.gate_up_interleaved = batch <= 4
+        # Tensor parallelism's sums travel through peer memory (the context's
+        # peer set, tp.init) for the batches the streaming GEMV takes; larger
+        # batches use NCCL.
+        self.peer_exchange = world > 1 and batch <= 4 and peer_exchange
         self.vocab_local = full.vocab // world
         self.plans = {
             "embed": PL.plan(PL.DEFAULT, embed_program(full)),
@@ -415,9 +419,48 @@ class Llama:
         return out
 
     def _tensor_parallel(self, launches: list) -> list:
-        """The row-parallel projections' residual epilogues move after the
-        allreduce of their partial sums; the greedy pick gathers the shards'
-        candidates."""
+        if self.peer_exchange:
+            return self._tensor_parallel_peers(launches)
+        return self._tensor_parallel_nccl(launches)
+
+    def _tensor_parallel_peers(self, launches: list) -> list:
+        """Over NVLink peer memory: a row-parallel projection scatters its
+        partial rows into every rank's exchange buffer (o: 0, down: 1) and
+        leaves its residual epilogue to the next GEMV, whose prologue adds
+        the ranks' partials in rank order to the residual, stores the new
+        residual row and normalizes it; the greedy candidates travel the
+        same way. The same launches as on one GPU, no collective."""
+        out, pending = [], None  # pending: (buffer, residual, where the sum goes)
+        for L in launches:
+            if L.kernel == "gemv_add":
+                w, x, r, y = L.bufs
+                xbuf = 0 if pending is None or pending[0] == 1 else 1
+                p = L.params
+                if p["ldy"] != self.s.d_model or p["ldr"] != self.s.d_model:
+                    raise Unlowerable(N.FKC_ERR_ARGUMENT, "a row-parallel output that is not a whole row.")
+                out.append(Launch("gemv_scatter", {"n": p["n"], "k": p["k"], "m": p["m"], "split": p["split"],
+                                                   "ldx": p["ldx"], "xbuf": xbuf}, [w, x]))
+                pending = (xbuf, r, y)
+            elif pending is not None and L.kernel in ("gemv_rmsnorm", "gemv_rmsnorm_silu") and L.bufs[1] == pending[2]:
+                w, x, gamma, y = L.bufs
+                p = dict(L.params)
+                p.pop("ldx")
+                p.update(ldr=self.s.d_model, xbuf=pending[0])
+                name = "gemv_reduce_rmsnorm_silu" if L.kernel == "gemv_rmsnorm_silu" else "gemv_reduce_rmsnorm"
+                out.append(Launch(name, p, [w, pending[1], gamma, pending[2], y]))
+                pending = (pending[0], None, None)  # consumed; the buffer alternates on
+            elif L.kernel == "argmax":
+                x, ids = L.bufs
+                out.append(Launch("argmax_scatter", dict(L.params, offset=self.rank * self.vocab_local), [x]))
+                out.append(Launch("argmax_gather_pick", {"m": self.m}, [ids]))
+            else:
+                out.append(L)
+        return out
+
+    def _tensor_parallel_nccl(self, launches: list) -> list:
+        """With NCCL: the row-parallel projections' residual epilogues move
+        after the allreduce of their partial sums; the greedy pick gathers
+        the shards' candidates."""
         m, d = self.m, self.s.d_model
         P = self.partial.ptr
         out = []

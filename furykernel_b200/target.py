@@ -142,6 +142,16 @@ SPEC_KERNELS = {
         KernelSig("argmax_pairs", [_f32("x"), _u32("pairs", "write")],
                   [_dim("m", 1, 65535), _dim("n", 1, _MAX), _u("ldx"), _u("offset")], threads=1024),
         KernelSig("argmax_pick", [_u32("pairs"), _u32("ids", "write")], [_dim("shards", 1, 64), _dim("m", 1, 65535)]),
+        KernelSig("argmax_scatter", [_f32("x")], [_dim("m", 1, 4), _dim("n", 1, _MAX), _u("ldx"), _u("offset")],
+                  threads=1024),
+        KernelSig("argmax_gather_pick", [_u32("ids", "write")], [_dim("m", 1, 4)]),
+        KernelSig("gemv_scatter", [_f32("w"), _f32("x")],
+                  [_dim("n", 1, 65536), _dim("k", 4, 65536, 4), _dim("m", 1, 4), _dim("split", 1, 8), _u("ldx"),
+                   _dim("xbuf", 0, 1)], threads=512),
+        *[KernelSig(name, [_f32("w"), _f32("r"), _f32("gamma"), _f32("xout", "write"), _f32("y", "write")],
+                    [_dim("n", 1, 1048576), _dim("k", 4, 16384, 4), _dim("m", 1, 4), _dim("split", 1, 8), _u("ldr"),
+                     _u("ldy"), _f("eps"), _f("factor"), _dim("xbuf", 0, 1)], threads=512)
+          for name in ("gemv_reduce_rmsnorm", "gemv_reduce_rmsnorm_silu")],
         KernelSig("advance", [_u32("ids"), _u32("tokens", "write"), _u32("pos", "read_write")], [_dim("m", 1, 65535)]),
         KernelSig("add", [_f32("a"), _f32("b"), _f32("y", "write")], [_dim("n", 1, _MAX)]),
         KernelSig("silu_mul", [_f32("a"), _f32("b"), _f32("y", "write")], [_dim("n", 1, _MAX)]),

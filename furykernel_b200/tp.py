@@ -36,7 +36,33 @@ def init(timeout_s: int = 120):
     uid = [N.Context.comm_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(uid, src=0)
     ctx.comm_init(world, rank, uid[0])
+    peer_set(ctx, rank, world)
     return ctx, rank, world, local
+
+
+def peer_set(ctx, rank: int, world: int) -> None:
+    """Every rank's exchange region mapped into this process (IPC handles
+    gathered over the process group), registered with the context."""
+    import ctypes
+
+    import torch.distributed as dist
+
+    L = N.lib()
+    local = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(64)
+    N.check(L.fkc_peer_alloc(ctx.handle, L.fkc_peer_region_bytes(), ctypes.byref(local), handle))
+    handles = [None] * world
+    dist.all_gather_object(handles, handle.raw)
+    regions = (ctypes.c_void_p * world)()
+    for q in range(world):
+        if q == rank:
+            regions[q] = local.value
+        else:
+            p = ctypes.c_void_p()
+            N.check(L.fkc_peer_open(ctx.handle, ctypes.create_string_buffer(handles[q], 64), ctypes.byref(p)))
+            regions[q] = p.value
+    N.check(L.fkc_peer_set(ctx.handle, world, rank, regions))
+    dist.barrier()
 
 
 def finish(ctx, graphs=()) -> None:

@@ -165,8 +165,23 @@ int fkc_allreduce_sum_f32(fkc_ctx *ctx, void *dptr, size_t count);
 /* Each rank's `count` 32-bit words, gathered in rank order into recv
  * (nranks * count words): the vocabulary shards' greedy candidates. */
 int fkc_allgather_u32(fkc_ctx *ctx, const void *send, void *recv, size_t count);
-/* The context's rank and number of ranks (1 and 0 without a communicator). */
+/* The context's rank and number of ranks (0 and 1 without a communicator). */
 int fkc_comm_rank(fkc_ctx *ctx, int *rank, int *nranks);
+
+/* ---- tensor parallelism over NVLink peer memory ---------------------------- */
+/* The row-parallel projections' partial sums travel by stores into every
+ * rank's exchange region, and the next GEMV's prologue adds them in rank
+ * order: every rank gets the same bits, with no collective launch.
+ * fkc_peer_alloc: this rank's region (bytes: the library's region size,
+ * fkc_peer_region_bytes) and its 64-byte IPC handle; fkc_peer_open: a peer's
+ * region from its handle; fkc_peer_set: every rank's region as this process
+ * maps it, by rank (this rank's own included). The table's gemv_scatter,
+ * gemv_reduce_rmsnorm(_silu), argmax_scatter and argmax_gather_pick use the
+ * set; their waits are bounded and report through fkc_status. */
+size_t fkc_peer_region_bytes(void);
+int fkc_peer_alloc(fkc_ctx *ctx, size_t bytes, void **local, void *handle64);
+int fkc_peer_open(fkc_ctx *ctx, const void *handle64, void **peer);
+int fkc_peer_set(fkc_ctx *ctx, int world, int rank, void *const *regions);
 int fkc_comm_destroy(fkc_ctx *ctx);
 
 #ifdef __cplusplus

@@ -85,6 +85,60 @@ def oracle_decode(eng, layers, embed, final_norm, kcache, vcache, tokens, pos, s
     return O.argmax(logits), logits, x
 
 
+def oracle_decode_tp(s, world, layers, embed, final_norm, kcache, vcache, tokens, pos, slot, chunk, max_splits,
+                     threads=0):
+    """The CPU target's bits for one tensor-parallel decode step over the
+    peer exchange: each rank's shard GEMVs in the contract's order over its
+    own slice, the row-parallel partials added in rank order, then the
+    residual: x1 = x + (((P_0 + P_1) + ...)). `layers` holds the whole
+    model (q, k, v, o, gate, up, down, attn_norm, mlp_norm per layer); the
+    caches [layers, slots, kv_heads, length, hd] are updated in place.
+    Returns (ids, logits, x)."""
+    threads = threads or O.threads_default()
+    d, hd = s.d_model, s.head_dim
+    hq, hk, fl, vl = s.heads // world, s.kv_heads // world, s.ffn // world, s.vocab // world
+    cos_t, sin_t = O.rope_tables(s.theta, hd, hd // 2, s.positions)
+    scale = np.float32(1.0 / math.sqrt(hd))
+    eps = np.float32(s.eps)
+    x = O.gather(embed, tokens)
+
+    def ranked_sum(parts):
+        total = parts[0]
+        for p in parts[1:]:
+            total = O.add(total, p)
+        return total
+
+    for l, w in enumerate(layers):
+        a = O.rmsnorm_rows(x, w["attn_norm"], eps, 1.0, threads)
+        parts = []
+        for r in range(world):
+            qs, ks = slice(r * hq * hd, (r + 1) * hq * hd), slice(r * hk * hd, (r + 1) * hk * hd)
+            wqkv = np.concatenate([w["q"][qs], w["k"][ks], w["v"][ks]])
+            qkv = O.gemv(wqkv, a, 1, threads)
+            q, k, v = qkv[:, :hq * hd], qkv[:, hq * hd:(hq + hk) * hd], qkv[:, (hq + hk) * hd:]
+            kc = np.ascontiguousarray(kcache[l][:, r * hk:(r + 1) * hk])
+            vc = np.ascontiguousarray(vcache[l][:, r * hk:(r + 1) * hk])
+            O.kv_store_ring(O.rope(k, hk, hd, hd // 2, pos, cos_t, sin_t), hk, hd, s.length, pos, slot, kc)
+            O.kv_store_ring(np.ascontiguousarray(v), hk, hd, s.length, pos, slot, vc)
+            kcache[l][:, r * hk:(r + 1) * hk] = kc
+            vcache[l][:, r * hk:(r + 1) * hk] = vc
+            qr = O.rope(q, hq, hd, hd // 2, pos, cos_t, sin_t)
+            att, _ = O.attend(qr, hq, hk, hd, s.length, pos, slot, kc, vc, scale, chunk, 4, max_splits, threads)
+            parts.append(O.gemv(np.ascontiguousarray(w["o"][:, qs]), att, 1, threads))
+        x1 = O.add(x, ranked_sum(parts))
+        m2 = O.rmsnorm_rows(x1, w["mlp_norm"], eps, 1.0, threads)
+        parts = []
+        for r in range(world):
+            fs = slice(r * fl, (r + 1) * fl)
+            g = O.gemv(w["gate"][fs], m2, 1, threads)
+            u = O.gemv(w["up"][fs], m2, 1, threads)
+            parts.append(O.gemv(np.ascontiguousarray(w["down"][:, fs]), O.silu_mul(g, u), 1, threads))
+        x = O.add(x1, ranked_sum(parts))
+    n = O.rmsnorm_rows(x, final_norm, eps, 1.0, threads)
+    logits = np.concatenate([O.gemv(embed[r * vl:(r + 1) * vl], n, 1, threads) for r in range(world)], axis=1)
+    return O.argmax(logits), logits, x
+
+
 def referee_decode(eng, layers, embed, final_norm, kcache_after, vcache_after, tokens, pos, slot):
     """The f64 evaluator's values and bounds for the same step, attention
     reading the caches as the kernels left them (evaluateStored,

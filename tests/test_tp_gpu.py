@@ -59,6 +59,20 @@ def test_tp2_decode_step_within_bounds(tmp_path):
     vc = np.concatenate([np.load(tmp_path / f"vc_{r}.npy") for r in range(2)], axis=2)
     assert np.array_equal(ids[0], ids[1])
     assert np.array_equal(xs[0].view(np.uint32), xs[1].view(np.uint32))
+    # Bit for bit with the CPU restatement of the tensor-parallel arithmetic
+    # (shard GEMVs, partials added in rank order, then the residual).
+    tokens = np.array([5, 2999], np.uint32)
+    pos = np.array([3, 7], np.uint32)
+    slot = np.arange(2, dtype=np.uint32)
+    kc0 = np.zeros_like(kc)
+    vc0 = np.zeros_like(vc)
+    want_ids, want_logits, want_x = MC.oracle_decode_tp(s, 2, layers, embed, final_norm, kc0, vc0, tokens, pos, slot,
+                                                        16, 4)
+    assert np.array_equal(kc0.view(np.uint32), kc.view(np.uint32))
+    assert np.array_equal(vc0.view(np.uint32), vc.view(np.uint32))
+    assert np.array_equal(xs[0].view(np.uint32), want_x.view(np.uint32))
+    assert np.array_equal(logits.view(np.uint32), want_logits.view(np.uint32))
+    assert np.array_equal(ids[0], want_ids)
 
     class Full:  # the referee reads only the whole model's shape
         pass
