@@ -43,8 +43,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", default="5", choices=["5", "3c"],
-                    help="5: the decode step (default); 3c: the prefill GEMM alone")
+    ap.add_argument("--config", default="5", choices=["5", "1", "2", "3a", "3b", "3c", "4"],
+                    help="5: the 32-layer decode step (default); 1, 2, 3a, 3b, 3c, 4: BASELINE's other configs")
     return ap.parse_args()
 
 
@@ -411,10 +411,135 @@ def run_gemm(args):
         dist.destroy_process_group()
 
 
+def time_graph(ctx, launches, steps, warmup, rotate=None):
+    """Device time (ms) of one replay of the launches captured as a graph,
+    averaged over `steps` replays after `warmup`. With `rotate`, a list of
+    launch lists over distinct input copies, each replay takes the next
+    (inputs then come from HBM, not L2)."""
+    graphs = []
+    for ls in rotate or [launches]:
+        ctx.capture_begin()
+        for L in ls:
+            L.run(ctx)
+        graphs.append(ctx.capture_end())
+    import torch
+
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    for i in range(warmup):
+        graphs[i % len(graphs)].launch()
+    ctx.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        graphs[i % len(graphs)].launch()
+    e1.record(stream)
+    e1.synchronize()
+    for g in graphs:
+        g.destroy()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_kernel_config(args):
+    """Configs 1, 2, 3a, 3b and 4, one GPU: device time a launch sequence,
+    HBM bytes against the measured peak, and the CPU target's arithmetic
+    (oracle) timed on one core over the same input."""
+    import numpy as np
+    import torch
+
+    from furykernel_b200 import _native as N
+    from furykernel_b200.engine import Launch, Llama
+    from furykernel_b200.program.llama import LlamaShape
+    from oracle import oracle as O
+
+    torch.cuda.set_device(0)
+    ctx = N.Context(0)
+    peak, kind = peaks()
+    cfg = args.config
+    cpu_ms, cpu_sample_text = None, ""
+    if cfg == "1":
+        n = 16_777_216
+        xs = [ctx.empty(n) for _ in range(4)]
+        for i, x in enumerate(xs):
+            ctx.fill_uniform(x, 100 + i, -1.0, 1.0)
+        part, y = ctx.empty(n // 256), ctx.empty(1)
+        rot = [[Launch("reduce_groups", {"n": n}, [x.ptr, part.ptr]),
+                Launch("reduce_final", {"count": n // 256}, [part.ptr, y.ptr])] for x in xs]
+        ms = time_graph(ctx, None, args.steps, args.warmup, rotate=rot)
+        nbytes, workload, unit_label = 4 * n, "config 1: tree reduction of 16,777,216 f32 (4 rotating copies)", "sums/s"
+        host = O.uniform(100, n, -1.0, 1.0)
+        t0 = time.perf_counter()
+        O.reduce_sum(host, 1)
+        cpu_ms = (time.perf_counter() - t0) * 1e3
+        cpu_sample_text = "one whole sum, fko_reduce_sum, 1 thread"
+    elif cfg == "2":
+        rows = h = 4096
+        x, g, y, z = ctx.empty((rows, h)), ctx.empty(h), ctx.empty((rows, h)), ctx.empty((rows, h))
+        ctx.fill_normal(x, 11, 0.0, 1.0)
+        ctx.fill_uniform(g, 12, 0.5, 1.5)
+        ls = [Launch("rmsnorm_rows", {"rows": rows, "h": h, "eps": 1e-5, "factor": 1.0}, [x.ptr, g.ptr, y.ptr]),
+              Launch("softmax_rows", {"rows": rows, "h": h}, [y.ptr, z.ptr])]
+        ms = time_graph(ctx, ls, args.steps, args.warmup)
+        nbytes, workload, unit_label = 2 * 2 * 4 * rows * h + 4 * h, "config 2: RMSNorm then softmax, 4096 x 4096 f32", "passes/s"
+        hx = O.normal(11, rows * h).reshape(rows, h)
+        hg = O.uniform(12, h, 0.5, 1.5)
+        t0 = time.perf_counter()
+        O.softmax_rows(O.rmsnorm_rows(hx, hg, 1e-5, 1.0, 1), 1)
+        cpu_ms = (time.perf_counter() - t0) * 1e3
+        cpu_sample_text = "the whole pass, fko_rmsnorm_rows + fko_softmax_rows, 1 thread"
+    elif cfg in ("3a", "3b"):
+        m = 1 if cfg == "3a" else 16
+        n, k = 11008, 4096
+        w, x, y = ctx.empty((n, k)), ctx.empty((m, k)), ctx.empty((m, n))
+        ctx.fill_normal(w, 21, 0.0, 0.02)
+        ctx.fill_normal(x, 22, 0.0, 1.0)
+        split = 1  # the streaming (m <= 4) and batched (m <= 64) kernels keep one
+        ls = [Launch("gemv", {"n": n, "k": k, "m": m, "split": split, "ldx": k, "ldy": n}, [w.ptr, x.ptr, y.ptr])]
+        ms = time_graph(ctx, ls, args.steps, args.warmup)
+        nbytes = 4 * (n * k + m * k + m * n)
+        workload, unit_label = f"config 3{'a' if m == 1 else 'b'}: GEMV 11008 x 4096 f32, batch {m}", "GEMVs/s"
+        hw = O.normal(21, n * k, 0.0, 0.02).reshape(n, k)
+        hx = O.normal(22, m * k).reshape(m, k)
+        rows = 1024 if m > 1 else n
+        t0 = time.perf_counter()
+        O.gemv(hw[:rows], hx, split, 1)
+        cpu_ms = (time.perf_counter() - t0) * 1e3 * n / rows
+        cpu_sample_text = f"fko_gemv over {rows} of the 11008 rows, 1 thread, scaled to all rows"
+    else:  # config 4: one layer, context 2048
+        b = args.batch
+        s = LlamaShape(layers=1, slots=b, length=2304, positions=2304)
+        eng = Llama(ctx, s, b, seed=2026, chunk=32, prefill_kv=1.0)
+        eng.set_rows(np.arange(b, dtype=np.uint32) + 1, np.full(b, 2048, np.uint32), np.arange(b, dtype=np.uint32))
+        eng.run_eager()
+        ctx.sync()
+        layer = eng.launches[1:8]
+        assert [L.kernel for L in layer][2:4] == ["attend_split", "attend_combine"], [L.kernel for L in layer]
+        ctx.set_pdl(True)
+        ms = time_graph(ctx, layer, args.steps, args.warmup)
+        ctx.set_pdl(False)
+        nbytes = eng.weight_bytes() - 4 * (eng.vocab_local * s.d_model + s.d_model) + \
+            b * 2 * s.kv_heads * s.head_dim * 4 * 2049
+        workload, unit_label = f"config 4: one Llama-shaped layer, decode at context 2048, batch {b}", "tokens/s"
+    gbs = nbytes / (ms / 1e3) / 1e9
+    value = (args.batch if cfg == "4" else 1) / (ms / 1e3)
+    line = {"metric": workload, "value": value, "unit": unit_label, "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic, seeded on the device",
+            "config": {"workload": workload},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                         "traffic": None, "algorithmic_bytes": nbytes, "peak_kind": kind}}
+    if cpu_ms is not None:
+        line["cpu_baseline"] = {"value": 1e3 / cpu_ms, "unit": unit_label, "cores": 1, "kind": "port",
+                                "sample": cpu_sample_text, "ms": cpu_ms}
+    print(json.dumps(line), flush=True)
+    ctx.close()
+
+
 def main():
     args = parse()
     if args.config == "3c":
         return run_gemm(args)
+    if args.config in ("1", "2", "3a", "3b", "4"):
+        return run_kernel_config(args)
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -95,6 +95,8 @@ cudaError_t fk_launch_softmax_rows(const float* x, float* y, uint32_t rows, uint
 cudaError_t fk_launch_gemv(const FkGemv& g, cudaStream_t s);
 bool fk_gemv_streams(const FkGemv& g);
 cudaError_t fk_launch_gemv_stream(const FkGemv& g, int sms, cudaStream_t s);
+bool fk_gemv_batches(const FkGemv& g);
+cudaError_t fk_launch_gemv_batch(const FkGemv& g, int sms, cudaStream_t s);
 cudaError_t fk_launch_kv_store(const FkKvStore& a, cudaStream_t s);
 cudaError_t fk_launch_attend(const FkAttend& a, cudaStream_t s);
 cudaError_t fk_launch_combine(const FkCombine& a, cudaStream_t s);

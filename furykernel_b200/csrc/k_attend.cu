@@ -53,8 +53,11 @@ __global__ void kv_store_kernel(FkKvStore a) {
 
 // The attention anchor: persistent blocks of 4 warps over the step's items
 // (row, head, split), item i at block i mod G. A warp takes positions w,
-// w + 4, ... of its split, 8 rows of keys (then of values) in flight a lane.
-__global__ void __launch_bounds__(128) attend_split_kernel(FkAttend a) {
+// w + 4, ... of its split, 8 at a time. The first 8 keys and values are
+// requested before q is rotated, so that their latency hides the rotation's;
+// a split's weights exp(s - max) are computed once a position, 32 positions
+// across the lanes, and handed to the warp that adds them by shuffle.
+__global__ void __launch_bounds__(128, 4) attend_split_kernel(FkAttend a) {
   __shared__ float qrot[kHeadDim];
   __shared__ float scores[kMaxChunk];
   __shared__ float4 accw[kAttWarps][kHeadDim / 4];
@@ -77,6 +80,7 @@ __global__ void __launch_bounds__(128) attend_split_kernel(FkAttend a) {
   const float4* kc4 = reinterpret_cast<const float4*>(a.kc);
   const float4* vc4 = reinterpret_cast<const float4*>(a.vc);
   constexpr int B = 8;  // positions in flight a warp
+  constexpr uint32_t kStep = B * kAttWarps;
 
   for (uint32_t it = blockIdx.x; it < items; it += gridDim.x) {
     uint32_t r = 0;
@@ -90,6 +94,16 @@ __global__ void __launch_bounds__(128) attend_split_kernel(FkAttend a) {
     const uint32_t kvh = h / (a.heads / a.kv_heads);
     const size_t base = ((size_t)a.slot[r] * a.kv_heads + kvh) * a.length;
 
+    // This warp's first keys and values: they depend on nothing below.
+    float4 kv[B], vv[B];
+#pragma unroll
+    for (int u = 0; u < B; ++u) {
+      const uint32_t tt = t0 + warp + u * kAttWarps;
+      const size_t at = (base + tt % a.length) * (kHeadDim / 4) + lane;
+      kv[u] = tt < t1 ? __ldcs(kc4 + at) : make_float4(0, 0, 0, 0);
+      vv[u] = tt < t1 ? __ldcs(vc4 + at) : make_float4(0, 0, 0, 0);
+    }
+
     __syncthreads();  // the previous item's shared arrays are free
     if (threadIdx.x < kHeadDim / 2)
       rope_pair(a.qkv + (size_t)r * a.ldq + a.q_off + (size_t)h * kHeadDim, qrot, threadIdx.x, kHeadDim / 2,
@@ -98,12 +112,13 @@ __global__ void __launch_bounds__(128) attend_split_kernel(FkAttend a) {
     const float4 qv = reinterpret_cast<const float4*>(qrot)[lane];
 
     // Scores: warp w takes positions t0 + w + 4 u, eight at a time.
-    for (uint32_t t = t0 + warp; t < t1; t += B * kAttWarps) {
-      float4 kv[B];
+    for (uint32_t t = t0 + warp; t < t1; t += kStep) {
+      if (t != t0 + warp) {
 #pragma unroll
-      for (int u = 0; u < B; ++u) {
-        const uint32_t tt = t + u * kAttWarps;
-        kv[u] = tt < t1 ? __ldcs(kc4 + (base + tt % a.length) * (kHeadDim / 4) + lane) : make_float4(0, 0, 0, 0);
+        for (int u = 0; u < B; ++u) {
+          const uint32_t tt = t + u * kAttWarps;
+          kv[u] = tt < t1 ? __ldcs(kc4 + (base + tt % a.length) * (kHeadDim / 4) + lane) : make_float4(0, 0, 0, 0);
+        }
       }
 #pragma unroll
       for (int u = 0; u < B; ++u) {
@@ -120,18 +135,22 @@ __global__ void __launch_bounds__(128) attend_split_kernel(FkAttend a) {
     // Weighted sums: warp w over positions t0 + w, t0 + w + 4, ..., in order.
     float l = 0.0f;
     float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    for (uint32_t t = t0 + warp; t < t1; t += B * kAttWarps) {
-      float4 vv[B];
+    for (uint32_t t = t0 + warp; t < t1; t += kStep) {
+      if (t != t0 + warp) {
 #pragma unroll
-      for (int u = 0; u < B; ++u) {
-        const uint32_t tt = t + u * kAttWarps;
-        vv[u] = tt < t1 ? __ldcs(vc4 + (base + tt % a.length) * (kHeadDim / 4) + lane) : make_float4(0, 0, 0, 0);
+        for (int u = 0; u < B; ++u) {
+          const uint32_t tt = t + u * kAttWarps;
+          vv[u] = tt < t1 ? __ldcs(vc4 + (base + tt % a.length) * (kHeadDim / 4) + lane) : make_float4(0, 0, 0, 0);
+        }
       }
+      // The 32 positions from t - warp: lane i's weight is position i's.
+      const uint32_t g0 = t - (uint32_t)warp - t0;
+      const float e_lane = g0 + lane < t1 - t0 ? exp_rounded(__fsub_rn(scores[g0 + lane], mx)) : 0.0f;
 #pragma unroll
       for (int u = 0; u < B; ++u) {
         const uint32_t tt = t + u * kAttWarps;
+        const float e = __shfl_sync(0xffffffffu, e_lane, warp + u * kAttWarps);
         if (tt < t1) {
-          const float e = exp_rounded(__fsub_rn(scores[tt - t0], mx));
           l = __fadd_rn(l, e);
           acc.x = __fadd_rn(acc.x, __fmul_rn(e, vv[u].x));
           acc.y = __fadd_rn(acc.y, __fmul_rn(e, vv[u].y));
@@ -160,20 +179,33 @@ __global__ void __launch_bounds__(128) attend_split_kernel(FkAttend a) {
   }
 }
 
-// The combine step: grid (heads, m), d threads.
+// The combine step: grid (heads, m), d threads. The largest maximum M (the
+// maximum is exact in any order) and each split's weight exp(m_j - M) are
+// computed once a block, into shared memory; every thread then adds the
+// splits in order for its dimension.
 __global__ void combine_kernel(FkCombine a) {
+  extern __shared__ float wsplit[];  // [max_splits]
+  __shared__ float top_s;
   grid_wait();
   grid_launch_dependents();
   const uint32_t h = blockIdx.x, r = blockIdx.y, i = threadIdx.x;
   const uint32_t splits = (a.pos[r] + 1 + a.chunk - 1) / a.chunk;
   const size_t at = ((size_t)r * a.heads + h) * a.max_splits;
-  float top = -INFINITY;
-  for (uint32_t j = 0; j < splits; ++j) top = max_number(top, a.part_m[at + j]);
-  float w0 = exp_rounded(__fsub_rn(a.part_m[at], top));
+  if (threadIdx.x < 32) {
+    float top = -INFINITY;
+    for (uint32_t j = threadIdx.x; j < splits; j += 32) top = max_number(top, a.part_m[at + j]);
+    top = warp_max(top);
+    if (threadIdx.x == 0) top_s = top;
+  }
+  __syncthreads();
+  const float top = top_s;
+  for (uint32_t j = threadIdx.x; j < splits; j += blockDim.x) wsplit[j] = exp_rounded(__fsub_rn(a.part_m[at + j], top));
+  __syncthreads();
+  const float w0 = wsplit[0];
   float l = __fmul_rn(a.part_l[at], w0);
   float o = __fmul_rn(a.part_acc[at * a.d + i], w0);
   for (uint32_t j = 1; j < splits; ++j) {
-    const float w = exp_rounded(__fsub_rn(a.part_m[at + j], top));
+    const float w = wsplit[j];
     l = __fadd_rn(l, __fmul_rn(a.part_l[at + j], w));
     o = __fadd_rn(o, __fmul_rn(a.part_acc[(at + j) * a.d + i], w));
   }
@@ -201,19 +233,25 @@ cudaError_t fk_launch_attend(const FkAttend& a, cudaStream_t s) {
   if (a.m == 0) return cudaSuccess;
   if (a.d != fk::kHeadDim || a.chunk == 0 || a.chunk > fk::kMaxChunk || a.heads % a.kv_heads != 0 || a.m > 64)
     return cudaErrorInvalidValue;
-  // Blocks for the most items a step can have, at most 8 an SM; each loops.
-  int dev = 0, sms = 148;
+  // Blocks for the most items a step can have, as many as are resident at
+  // once; each loops over its items.
+  int dev = 0, sms = 148, per_sm = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fk::attend_split_kernel, 128, 0);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) return cudaErrorInvalidConfiguration;
   const uint64_t most = (uint64_t)a.m * a.heads * a.max_splits;
-  const uint32_t blocks = (uint32_t)(most < (uint64_t)sms * 8 ? most : (uint64_t)sms * 8);
+  const uint64_t resident = (uint64_t)sms * per_sm;
+  const uint32_t blocks = (uint32_t)(most < resident ? most : resident);
   return fk_launch_ex(fk::attend_split_kernel, dim3(blocks), dim3(128), 0, s, a.pdl, a);
 }
 
 cudaError_t fk_launch_combine(const FkCombine& a, cudaStream_t s) {
   if (a.m == 0) return cudaSuccess;
-  if (a.d > 1024) return cudaErrorInvalidValue;
-  return fk_launch_ex(fk::combine_kernel, dim3(a.heads, a.m), dim3(a.d), 0, s, a.pdl, a);
+  if (a.d > 1024 || a.d < 32 || a.max_splits == 0 || a.max_splits > 12288) return cudaErrorInvalidValue;
+  return fk_launch_ex(fk::combine_kernel, dim3(a.heads, a.m), dim3(a.d), (size_t)a.max_splits * sizeof(float), s,
+                      a.pdl, a);
 }
 
 cudaError_t fk_launch_rope(const float* x, uint32_t m, uint32_t heads, uint32_t d, uint32_t rotated, uint32_t ldx,

@@ -210,8 +210,20 @@ static cudaError_t launch_pro(const GemvArgs& a, cudaStream_t st, bool pdl) {
 
 cudaError_t fk_launch_gemv(const FkGemv& g, cudaStream_t st) {
   if (g.n == 0 || g.m == 0) return cudaSuccess;
-  if (g.k % 4 != 0 || g.m > 32 || !(g.split == 1 || g.split == 2 || g.split == 4 || g.split == 8))
-    return cudaErrorInvalidValue;
+  if (g.k % 4 != 0 || !(g.split == 1 || g.split == 2 || g.split == 4 || g.split == 8)) return cudaErrorInvalidValue;
+  if (g.m > 32) {
+    // Batch rows are independent: 32 at a time.
+    for (uint32_t i0 = 0; i0 < g.m; i0 += 32) {
+      FkGemv part = g;
+      part.m = g.m - i0 < 32 ? g.m - i0 : 32;
+      part.x = g.x + (size_t)i0 * g.ldx;
+      part.y = g.y + (size_t)i0 * g.ldy;
+      if (g.r) part.r = g.r + (size_t)i0 * g.ldr;
+      cudaError_t e = fk_launch_gemv(part, st);
+      if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+  }
   fk::GemvArgs a;
   a.w = g.w;
   a.x = g.x;

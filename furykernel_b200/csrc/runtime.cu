@@ -354,7 +354,9 @@ int l_softmax_rows(fkc_ctx* c, const Params& p, void* const* bufs) {
 // Decode batches of up to 4 rows stream through the persistent kernel; larger
 // batches take the chunked one. Both keep the GEMV order contract.
 cudaError_t run_gemv(fkc_ctx* c, const FkGemv& g) {
-  return fk_gemv_streams(g) ? fk_launch_gemv_stream(g, c->sms, c->stream) : fk_launch_gemv(g, c->stream);
+  if (fk_gemv_streams(g)) return fk_launch_gemv_stream(g, c->sms, c->stream);
+  if (fk_gemv_batches(g)) return fk_launch_gemv_batch(g, c->sms, c->stream);
+  return fk_launch_gemv(g, c->stream);
 }
 
 FkGemv gemv_base(fkc_ctx* c, const Params& p) {
@@ -404,10 +406,12 @@ int l_gemv_rmsnorm_silu(fkc_ctx* c, const Params& p, void* const* bufs) {
   g.prologue = FK_PRO_RMSNORM;
   g.silu_pair = true;
   if (g.n % 2 != 0) return fail(FKC_ERR_ARGUMENT, "gemv_rmsnorm_silu: n %u is not a whole number of row pairs.", g.n);
-  if (!fk_gemv_streams(g))
-    return fail(FKC_ERR_ARGUMENT, "gemv_rmsnorm_silu: m %u and k %u are past what the streaming kernel stages.", g.m,
-                g.k);
-  return launched(fk_launch_gemv_stream(g, c->sms, c->stream), "gemv_rmsnorm_silu");
+  if (!fk_gemv_streams(g) && !fk_gemv_batches(g))
+    return fail(FKC_ERR_ARGUMENT,
+                "gemv_rmsnorm_silu: m %u, k %u and split %u are past what the row-pair kernels take (m at most 64, "
+                "split 1 past m 4).",
+                g.m, g.k, g.split);
+  return launched(run_gemv(c, g), "gemv_rmsnorm_silu");
 }
 
 // gemv_silu: w, x, y | n k m split ldx ldy up_off
@@ -594,7 +598,7 @@ ParamSpec f32(const char* n) { return {n, "f32", false, 0, 0, 0}; }
 
 std::vector<KernelSpec> make_table() {
   std::vector<KernelSpec> t;
-  auto gemv_dims = std::vector<ParamSpec>{dim("n", 1, 1048576), dim("k", 4, 65536, 4), dim("m", 1, 32),
+  auto gemv_dims = std::vector<ParamSpec>{dim("n", 1, 1048576), dim("k", 4, 65536, 4), dim("m", 1, 64),
                                           dim("split", 1, 8),   u32("ldx"),           u32("ldy")};
   auto with = [](std::vector<ParamSpec> a, std::initializer_list<ParamSpec> b) {
     a.insert(a.end(), b.begin(), b.end());

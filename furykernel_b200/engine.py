@@ -243,12 +243,12 @@ class Llama:
                                 ffn=full.ffn // world)
         self.ctx, self.full, self.s, self.m = ctx, full, s, batch
         self.rank, self.world = rank, world
-        # For decode batches the streaming GEMV takes (up to 4 rows), the
-        # arena interleaves gate and up rows (gate_i at row 2i, up_i at
+        # For decode batches the streaming and batched GEMVs take (up to 64
+        # rows), the arena interleaves gate and up rows (gate_i at row 2i, up_i at
         # 2i + 1), so that the [gate; up] step computes mlp_act = silu(gate) *
         # up on its own tiles and stores it, and the down step reads it: the
         # same bits as recomputing it in the down step, computed once.
-        self.gate_up_interleaved = batch <= 4
+        self.gate_up_interleaved = batch <= 64
         # Tensor parallelism's sums travel through peer memory (the context's
         # peer set, tp.init) for the batches the streaming GEMV takes; larger
         # batches use NCCL.
@@ -391,9 +391,10 @@ class Llama:
         out.append(Launch("advance", {"m": m}, [self.out_ids.ptr, self.tokens.ptr, self.pos.ptr]))
         for L in out:  # split-K per GEMV shape
             if L.kernel.startswith("gemv"):
-                # The streaming kernel's parallelism is rows whatever the
-                # split, so it keeps one; the chunked kernel splits long rows.
-                L.params["split"] = 1 if m <= 4 else split_for(L.params["n"], L.params["k"], self.ctx.sms)
+                # The streaming (m <= 4) and batched (m <= 64) kernels'
+                # parallelism is rows whatever the split, so they keep one;
+                # the chunked kernel splits long rows.
+                L.params["split"] = 1 if m <= 64 else split_for(L.params["n"], L.params["k"], self.ctx.sms)
         return out
 
     def _silu_on_tiles(self, launches: list) -> list:

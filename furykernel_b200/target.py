@@ -91,7 +91,7 @@ def _f(name):
     return Param(name, "f32")
 
 
-_GEMV = [_dim("n", 1, 1048576), _dim("k", 4, 65536, 4), _dim("m", 1, 32), _dim("split", 1, 8), _u("ldx"), _u("ldy")]
+_GEMV = [_dim("n", 1, 1048576), _dim("k", 4, 65536, 4), _dim("m", 1, 64), _dim("split", 1, 8), _u("ldx"), _u("ldy")]
 _MAX = 4294967295
 
 SPEC_KERNELS = {

@@ -28,14 +28,14 @@ def small_shape(batch, layers=2, d=512, heads=4, ffn=1024, vocab=3000, length=96
                       slots=batch, length=length, positions=length)
 
 
-@pytest.mark.parametrize("batch,graph", [(1, True), (3, True), (2, False)])
+@pytest.mark.parametrize("batch,graph", [(1, True), (3, True), (2, False), (5, True), (9, True), (20, False)])
 def test_small_model_decode_step(ctx, batch, graph):
     from furykernel_b200.engine import Llama
 
     s = small_shape(batch)
     eng = Llama(ctx, s, batch, seed=100 + batch, chunk=32, prefill_kv=1.0)
     tokens = O.ints(5 + batch, batch, s.vocab)
-    pos = np.array([40, 95, 7][:batch], np.uint32)
+    pos = np.array([40, 95, 7][:batch] if batch <= 3 else (np.arange(batch) * 37 + 5) % 96, np.uint32)
     slot = np.arange(batch, dtype=np.uint32)[::-1].copy()
     layers, embed, final_norm = MC.host_model(eng)
     kc0, vc0 = MC.host_caches(eng)

@@ -119,7 +119,9 @@ def test_rmsnorm_softmax_rows(ctx, rows, h):
 
 
 @pytest.mark.parametrize("n,k,m,split", [(11008, 4096, 1, 1), (11008, 4096, 16, 1), (4096, 11008, 1, 2),
-                                         (300, 1000, 3, 4), (257, 4096, 32, 8)])
+                                         (300, 1000, 3, 4), (257, 4096, 32, 8), (11008, 4096, 5, 1),
+                                         (4096, 11008, 32, 1), (1001, 1000, 64, 1), (22, 4100, 9, 1),
+                                         (3, 256, 17, 1)])
 def test_gemv_bit_exact(ctx, n, k, m, split):
     w = O.normal(21, n * k, 0.0, 0.02).reshape(n, k)
     x = O.normal(22, m * k).reshape(m, k)
@@ -159,6 +161,33 @@ def test_gemv_prologues_and_epilogue(ctx):
     ctx.launch("gemv_silu", dict(base, ldx=2 * k, up_off=k), [wd, gud, yd])
     assert same_bits(yd.download(), O.gemv(w, act, 2, THREADS))
     for b in (wd, xd, gd, rd, gud, yd):
+        b.free()
+
+
+@pytest.mark.parametrize("m", [6, 12, 40])
+def test_batched_gemv_prologue_and_epilogues(ctx, m):
+    """The batched kernel (5 to 64 rows, split 1): RMSNorm before the
+    anchor, the residual on the tile, and the SiLU-gate of interleaved
+    gate/up rows on the pair's tile."""
+    n, k = 1002, 2048
+    w = O.normal(41, n * k, 0.0, 0.02).reshape(n, k)
+    x = O.normal(42, m * k).reshape(m, k)
+    g = O.uniform(43, k, 0.5, 1.5)
+    r = O.normal(44, m * n).reshape(m, n)
+    wd, xd, gd, rd = (ctx.to_device(a) for a in (w, x, g, r))
+    yd = ctx.empty((m, n))
+    base = {"n": n, "k": k, "m": m, "split": 1, "ldx": k, "ldy": n}
+    ctx.launch("gemv_rmsnorm", dict(base, eps=1e-5, factor=1.0), [wd, xd, gd, yd])
+    normed = O.rmsnorm_rows(x, g, 1e-5)
+    assert same_bits(yd.download(), O.gemv(w, normed, 1, THREADS))
+    ctx.launch("gemv_add", dict(base, ldr=n), [wd, xd, rd, yd])
+    assert same_bits(yd.download(), O.add(r, O.gemv(w, x, 1, THREADS)))
+    ad = ctx.empty((m, n // 2))
+    ctx.launch("gemv_rmsnorm_silu", dict(base, ldy=n // 2, eps=1e-5, factor=1.0), [wd, xd, gd, ad])
+    want = O.silu_mul(O.gemv(np.ascontiguousarray(w[0::2]), normed, 1, THREADS),
+                      O.gemv(np.ascontiguousarray(w[1::2]), normed, 1, THREADS))
+    assert same_bits(ad.download(), want)
+    for b in (wd, xd, gd, rd, yd, ad):
         b.free()
 
 
@@ -302,14 +331,16 @@ def test_rope_kernel(ctx):
 def test_dimension_refusal_text(ctx):
     from furykernel_b200 import _native as N
 
-    x = ctx.empty(16)
-    y = ctx.empty(16)
+    # Buffers large enough for the refused shapes, so that nothing could
+    # reach past them even if a check were missing.
+    x = ctx.empty(65 * 8)
+    y = ctx.empty(65 * 8)
     with pytest.raises(N.Refused) as e:
         ctx.launch("softmax_rows", {"rows": 1, "h": 6}, [x, y])
     assert str(e.value) == "softmax_rows: the dimension h is 6, outside its range 4..16384 multiple of 4."
     with pytest.raises(N.Refused) as e:
-        ctx.launch("gemv", {"n": 4, "k": 4, "m": 33, "split": 1, "ldx": 4, "ldy": 4}, [x, x, y])
-    assert str(e.value) == "gemv: the dimension m is 33, outside its range 1..32."
+        ctx.launch("gemv", {"n": 4, "k": 4, "m": 65, "split": 1, "ldx": 4, "ldy": 4}, [x, x, y])
+    assert str(e.value) == "gemv: the dimension m is 65, outside its range 1..64."
     x.free()
     y.free()
 
