@@ -4,21 +4,26 @@
 // summed pairwise, neighbours first -- so its outputs are the bits of the
 // other GEMV kernels and of the CPU target.
 //
-// At a batch past 4 the f32 arithmetic outweighs the weight stream (two
-// rounded operations per multiply-add, no fused form under the contract), so
-// the kernel is built to keep the FP32 pipes issuing: a warp owns 4 weight
-// rows and M batch rows at once (4 M chains a lane, every x pack read from
-// shared memory used 4 times, every weight pack M times).
+// Past a batch of 4 the f32 arithmetic outweighs the weight stream (two
+// rounded operations a multiply-add, no fused form under the contract). The
+// kernel computes two batch rows at once with sm_100's packed f32x2
+// arithmetic, which rounds each half as the scalar instructions do and
+// issues at twice their rate: batch rows 2p and 2p + 1 sit interleaved in shared
+// memory ({x0 of 2p, x0 of 2p+1, x1 of 2p, x1 of 2p+1}, then x2, x3), so one
+// 128-bit load gives two packed operands; a weight element is paired with
+// itself.
 //
-// Persistent blocks of 16 warps, one a SM. The units (4 consecutive rows)
-// are cut into one contiguous range a block; a block takes its range 16
-// units at a time, warp w the unit w of each round. Within a round the block
-// walks k in chunks of 256 packs: the chunk of every batch row in the pass is
-// copied to shared memory with cp.async (the next chunk's copies in flight
-// while this one is used), RMSNorm's scale and gain applied in place by the
-// thread that copied it; every warp's lanes then stream their rows' packs
-// with 128-bit loads that skip L1, one step ahead. Batches past M run as
-// passes of M rows over the same weight rows.
+// Work: persistent blocks of W warps, one a SM. The units (4 consecutive
+// weight rows) are cut into one contiguous range a block; a block takes its
+// range W units at a time, warp w the unit w of each round; a warp keeps its
+// 4 rows' chains for M batch rows (2 M packed accumulators a lane). Within a
+// round the block walks k in chunks of 256 packs: the chunk of the pass's
+// batch rows is copied into a raw buffer with cp.async while the previous
+// chunk is being used, then rewritten interleaved (RMSNorm's scale and gain
+// applied on the way) into one of two compute buffers. Lanes stream their
+// rows' packs with 128-bit loads that skip L1, one step ahead, behind an L2
+// prefetch four steps ahead. Batches past M run as passes of M rows over the
+// same weight rows.
 #include "fk_common.cuh"
 #include "fk_kernels.h"
 
@@ -33,75 +38,115 @@ struct BatchArgs {
   uint32_t n, k, m;
   uint32_t ldx, ldr, ldy;
   float eps, factor;
+  float negzero;  // -0.0, unknown to the compiler (see prod2)
 };
 
 enum { BPRO_NONE = 0, BPRO_RMSNORM = 1 };
 enum { BEPI_NONE = 0, BEPI_ADD = 1, BEPI_SILU_PAIR = 2 };
 template <int M>
-__host__ __device__ constexpr int batch_warps() { return M <= 8 ? 16 : 12; }
+__host__ __device__ constexpr int batch_warps() {
+  return M <= 8 ? 16 : 12;
+}
 constexpr int kBatchRows = 4;     // weight rows a warp
 constexpr uint32_t kChunk = 256;  // packs of x a chunk
 constexpr uint32_t kMaxBatch = 64;
+constexpr uint32_t kAhead = 4;  // steps of L2 prefetch ahead of the loads
 
 __device__ __forceinline__ float silu_pair_of(float a, float b) {
   const float e = exp_rounded(-a);
   return __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, e)), b);
 }
 
+// Packed binary32 pairs (PTX .f32x2, sm_100a): each half rounded to nearest
+// even, as add.rn.f32 / mul.rn.f32 on its own.
+__device__ __forceinline__ uint64_t pair(float lo, float hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// A packed product, rounded once, that the code generator cannot fuse into
+// the add it feeds: ptxas contracts mul.rn.f32x2 followed by add.rn.f32x2
+// into one fused multiply-add (measured on sm_100a, --fmad=false
+// notwithstanding), which would skip the product's rounding. As
+// fma(a, b, -0) with the -0 known only at run time it is a * b rounded once,
+// signed zeros included (+0 + -0 = +0, -0 + -0 = -0).
+__device__ __forceinline__ uint64_t prod2(uint64_t a, uint64_t b, uint64_t negzero) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(negzero));
+  return d;
+}
+__device__ __forceinline__ float lo_of(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float hi_of(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-// Copy chunk c of batch rows [row0, row0 + mp) into buffer xs; rows mp..M-1
-// of the buffer (computed on, never stored) are zero.
-template <int M>
-__device__ __forceinline__ void stage_chunk(const BatchArgs& a, float4* xs, uint32_t row0, uint32_t mp, uint32_t c,
-                                            uint32_t packs) {
-  const uint32_t base = c * kChunk;
-  const uint32_t len = min(kChunk, packs - base);
-  for (uint32_t idx = threadIdx.x; idx < M * kChunk; idx += blockDim.x) {
-    const uint32_t i = idx / kChunk, j = idx % kChunk;
-    if (i >= mp)
-      xs[idx] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    else if (j < len)
-      cp_async16(xs + idx, a.x + (size_t)(row0 + i) * a.ldx + 4 * (size_t)(base + j));
-  }
-}
-
-// RMSNorm of the copies this thread made: x * scale * gamma (* factor), each
-// product rounded, as the RmsNorm op's epilogue.
-__device__ __forceinline__ void normalize_chunk(const BatchArgs& a, float4* xs, const float* scales, uint32_t row0,
-                                                uint32_t mp, uint32_t c, uint32_t packs) {
+// Copy chunk c of batch rows [row0, row0 + mp) into the raw buffer [M][kChunk].
+__device__ __forceinline__ void copy_chunk(const BatchArgs& a, float4* raw, uint32_t row0, uint32_t mp, uint32_t c,
+                                           uint32_t packs) {
   const uint32_t base = c * kChunk;
   const uint32_t len = min(kChunk, packs - base);
   for (uint32_t idx = threadIdx.x; idx < mp * kChunk; idx += blockDim.x) {
     const uint32_t i = idx / kChunk, j = idx % kChunk;
-    if (j >= len) continue;
-    float4 v = xs[idx];
-    const float sc = scales[row0 + i];
+    if (j < len) cp_async16(raw + idx, a.x + (size_t)(row0 + i) * a.ldx + 4 * (size_t)(base + j));
+  }
+}
+
+// RMSNorm's epilogue on one pack: x * scale * gamma (* factor), each product
+// rounded, as the RmsNorm op computes it.
+template <int PRO>
+__device__ __forceinline__ float4 prologue(const BatchArgs& a, float4 v, float sc, float4 g) {
+  if (PRO == BPRO_RMSNORM) {
     v = make_float4(__fmul_rn(v.x, sc), __fmul_rn(v.y, sc), __fmul_rn(v.z, sc), __fmul_rn(v.w, sc));
-    if (a.gamma) {
-      const float4 g = __ldg(reinterpret_cast<const float4*>(a.gamma) + base + j);
-      v = make_float4(__fmul_rn(v.x, g.x), __fmul_rn(v.y, g.y), __fmul_rn(v.z, g.z), __fmul_rn(v.w, g.w));
-    }
+    if (a.gamma) v = make_float4(__fmul_rn(v.x, g.x), __fmul_rn(v.y, g.y), __fmul_rn(v.z, g.z), __fmul_rn(v.w, g.w));
     if (a.factor != 1.0f)
       v = make_float4(__fmul_rn(v.x, a.factor), __fmul_rn(v.y, a.factor), __fmul_rn(v.z, a.factor),
                       __fmul_rn(v.w, a.factor));
-    xs[idx] = v;
+  }
+  return v;
+}
+
+// Raw chunk -> compute buffer: plane 2p holds {x0, x0', x1, x1'} and plane
+// 2p + 1 {x2, x2', x3, x3'} of batch rows 2p and 2p + 1 (rows past mp zero).
+template <int M, int PRO>
+__device__ __forceinline__ void interleave_chunk(const BatchArgs& a, const float4* raw, float4* xs,
+                                                 const float* scales, uint32_t row0, uint32_t mp, uint32_t c,
+                                                 uint32_t packs) {
+  const uint32_t base = c * kChunk;
+  const uint32_t len = min(kChunk, packs - base);
+  for (uint32_t idx = threadIdx.x; idx < (M / 2) * kChunk; idx += blockDim.x) {
+    const uint32_t p = idx / kChunk, j = idx % kChunk;
+    if (j >= len) continue;
+    const uint32_t i0 = 2 * p, i1 = 2 * p + 1;
+    float4 g = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (PRO == BPRO_RMSNORM && a.gamma) g = __ldg(reinterpret_cast<const float4*>(a.gamma) + base + j);
+    const float4 zero = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const float4 u = i0 < mp ? prologue<PRO>(a, raw[i0 * kChunk + j], PRO == BPRO_RMSNORM ? scales[row0 + i0] : 0.0f, g)
+                             : zero;
+    const float4 v = i1 < mp ? prologue<PRO>(a, raw[i1 * kChunk + j], PRO == BPRO_RMSNORM ? scales[row0 + i1] : 0.0f, g)
+                             : zero;
+    xs[(2 * p) * kChunk + j] = make_float4(u.x, v.x, u.y, v.y);
+    xs[(2 * p + 1) * kChunk + j] = make_float4(u.z, v.z, u.w, v.w);
   }
 }
 
 template <int M, int PRO, int EPI>
 __global__ void __launch_bounds__(batch_warps<M>() * 32, 1) gemv_batch_kernel(BatchArgs a) {
-  extern __shared__ float4 xbuf[];  // [2][M][kChunk]
+  extern __shared__ float4 smem4[];  // raw [M][kChunk], then compute [2][M][kChunk]
+  float4* raw = smem4;
+  float4* comp = smem4 + (size_t)M * kChunk;
   __shared__ float scales[kMaxBatch];
   __shared__ float slots[kMaxBatch][8];
+  constexpr int P = M / 2;  // packed batch-row pairs
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t packs = a.k >> 2;
   const uint32_t units = (a.n + kBatchRows - 1) / kBatchRows;
@@ -147,6 +192,7 @@ __global__ void __launch_bounds__(batch_warps<M>() * 32, 1) gemv_batch_kernel(Ba
   }
 
   const float4* w4 = reinterpret_cast<const float4*>(a.w);
+  const uint64_t nz = pair(a.negzero, a.negzero);
   for (uint32_t u0 = u_lo; u0 < u_hi; u0 += batch_warps<M>()) {
     const uint32_t u = u0 + (uint32_t)warp;
     const bool active = u < u_hi;
@@ -156,57 +202,76 @@ __global__ void __launch_bounds__(batch_warps<M>() * 32, 1) gemv_batch_kernel(Ba
     uint32_t roff[kBatchRows];
 #pragma unroll
     for (int r = 0; r < kBatchRows; ++r) roff[r] = (min(row0 + r, a.n - 1) - min(row0, a.n - 1)) * packs;
+    // The L2 prefetch a step issues: lane l < 16 takes line l & 3 (of 128
+    // bytes) of row l >> 2's packs kAhead steps on.
+    const uint32_t pf_row = (min(row0 + ((uint32_t)lane >> 2 & 3u), a.n - 1) - min(row0, a.n - 1)) * packs;
+    const uint32_t pf_line = ((uint32_t)lane & 3u) * 8u;
 
     for (uint32_t p0 = 0; p0 < a.m; p0 += M) {
       const uint32_t mp = min((uint32_t)M, a.m - p0);
-      float acc[kBatchRows][M];
+      uint64_t acc[kBatchRows][P];
 #pragma unroll
       for (int r = 0; r < kBatchRows; ++r)
 #pragma unroll
-        for (int i = 0; i < M; ++i) acc[r][i] = 0.0f;
+        for (int q = 0; q < P; ++q) acc[r][q] = 0;  // +0.0 in both halves
 
-      stage_chunk<M>(a, xbuf, p0, mp, 0, packs);
+      copy_chunk(a, raw, p0, mp, 0, packs);
       cp_async_commit();
       float4 wv[kBatchRows];
       uint32_t g = (uint32_t)lane;
-      if (active && g < packs) {
+      if (active) {
+        const uint32_t g0 = min(g, packs - 1);
 #pragma unroll
-        for (int r = 0; r < kBatchRows; ++r) wv[r] = ld_stream(wrow + roff[r] + g);
+        for (int r = 0; r < kBatchRows; ++r) wv[r] = ld_stream(wrow + roff[r] + g0);
       }
       for (uint32_t c = 0; c < chunks; ++c) {
-        float4* xs = xbuf + (size_t)(c & 1) * M * kChunk;
+        float4* xs = comp + (size_t)(c & 1) * M * kChunk;
+        cp_async_wait_all();
+        __syncthreads();  // chunk c's copies are in; compute buffer c & 1 is free
+        interleave_chunk<M, PRO>(a, raw, xs, scales, p0, mp, c, packs);
+        __syncthreads();  // the raw buffer is free, chunk c is interleaved
         if (c + 1 < chunks) {
-          stage_chunk<M>(a, xbuf + (size_t)((c + 1) & 1) * M * kChunk, p0, mp, c + 1, packs);
+          copy_chunk(a, raw, p0, mp, c + 1, packs);
           cp_async_commit();
-          cp_async_wait<1>();
-        } else {
-          cp_async_wait<0>();
         }
-        if (PRO == BPRO_RMSNORM) normalize_chunk(a, xs, scales, p0, mp, c, packs);
-        __syncthreads();
         if (active) {
           const uint32_t end = min(packs, (c + 1) * kChunk);
           for (; g < end; g += 32) {
-            // The next step's packs (the last step reloads its own: no branch).
-            const uint32_t gn = min(g + 32, packs - 1);
-            float4 wn[kBatchRows];
+            uint64_t wd[kBatchRows][4];  // each weight element paired with itself
 #pragma unroll
-            for (int r = 0; r < kBatchRows; ++r) wn[r] = ld_stream(wrow + roff[r] + gn);
-            // Every row of the pass's buffer, the zero rows past mp included:
-            // no branch between the loads and the arithmetic.
-            const float4* xc = xs + (g - c * kChunk);
-#pragma unroll
-            for (int i = 0; i < M; ++i) {
-              const float4 xv = xc[i * kChunk];
-#pragma unroll
-              for (int r = 0; r < kBatchRows; ++r) acc[r][i] = __fadd_rn(acc[r][i], pack_dot(xv, wv[r]));
+            for (int r = 0; r < kBatchRows; ++r) {
+              wd[r][0] = pair(wv[r].x, wv[r].x);
+              wd[r][1] = pair(wv[r].y, wv[r].y);
+              wd[r][2] = pair(wv[r].z, wv[r].z);
+              wd[r][3] = pair(wv[r].w, wv[r].w);
             }
+            // Weights kAhead steps on toward L2, then the next step's packs
+            // into registers (the last step reloads its own: no branch).
+            {
+              const uint32_t gp = g - (uint32_t)lane + 32u * kAhead + pf_line;
+              if (lane < 16 && gp < packs) asm volatile("prefetch.global.L2 [%0];" ::"l"(wrow + pf_row + gp));
+            }
+            const uint32_t gn = min(g + 32, packs - 1);
 #pragma unroll
-            for (int r = 0; r < kBatchRows; ++r) wv[r] = wn[r];
+            for (int r = 0; r < kBatchRows; ++r) wv[r] = ld_stream(wrow + roff[r] + gn);
+            // Each 128-bit load is two packed operands as they lie.
+            const ulonglong2* xc = reinterpret_cast<const ulonglong2*>(xs) + (g - c * kChunk);
+#pragma unroll
+            for (int q = 0; q < P; ++q) {
+              const ulonglong2 e = xc[(2 * q) * kChunk], f = xc[(2 * q + 1) * kChunk];
+              const uint64_t x0 = e.x, x1 = e.y, x2 = f.x, x3 = f.y;
+#pragma unroll
+              for (int r = 0; r < kBatchRows; ++r) {
+                // ((x0 w0 + x1 w1) + (x2 w2 + x3 w3)) added to the chain.
+                const uint64_t s01 = add2(prod2(x0, wd[r][0], nz), prod2(x1, wd[r][1], nz));
+                const uint64_t s23 = add2(prod2(x2, wd[r][2], nz), prod2(x3, wd[r][3], nz));
+                acc[r][q] = add2(acc[r][q], add2(s01, s23));
+              }
+            }
           }
         }
-        __syncthreads();
       }
+      __syncthreads();  // every warp is done with the compute buffers
 
       if (active) {
         // Lanes summed pairwise; lane i keeps batch row p0 + i's totals.
@@ -215,9 +280,10 @@ __global__ void __launch_bounds__(batch_warps<M>() * 32, 1) gemv_batch_kernel(Ba
         for (int r = 0; r < kBatchRows; ++r) {
           mine[r] = 0.0f;
 #pragma unroll
-          for (int i = 0; i < M; ++i) {
-            const float t = warp_sum(acc[r][i]);
-            if (lane == i) mine[r] = t;
+          for (int q = 0; q < P; ++q) {
+            const float t0 = warp_sum(lo_of(acc[r][q])), t1 = warp_sum(hi_of(acc[r][q]));
+            if (lane == 2 * q) mine[r] = t0;
+            if (lane == 2 * q + 1) mine[r] = t1;
           }
         }
         if ((uint32_t)lane < mp) {
@@ -245,7 +311,7 @@ __global__ void __launch_bounds__(batch_warps<M>() * 32, 1) gemv_batch_kernel(Ba
 template <int M, int PRO, int EPI>
 static cudaError_t launch_batch(const BatchArgs& a, int sms, cudaStream_t st, bool pdl) {
   auto kern = gemv_batch_kernel<M, PRO, EPI>;
-  const size_t smem = 2 * (size_t)M * kChunk * sizeof(float4);
+  const size_t smem = 3 * (size_t)M * kChunk * sizeof(float4);
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -289,6 +355,7 @@ cudaError_t fk_launch_gemv_batch(const FkGemv& g, int sms, cudaStream_t st) {
   a.ldy = g.ldy;
   a.eps = g.eps;
   a.factor = g.factor;
+  a.negzero = -0.0f;
   using namespace fk;
   const int epi = g.silu_pair ? BEPI_SILU_PAIR : (g.r ? BEPI_ADD : BEPI_NONE);
   switch (g.prologue * 4 + epi) {

@@ -191,6 +191,31 @@ def test_batched_gemv_prologue_and_epilogues(ctx, m):
         b.free()
 
 
+def test_batched_gemv_subnormal_and_special_values(ctx):
+    """The packed f32x2 arithmetic keeps subnormal products and sums (no
+    flush to zero) and carries infinities and NaNs as the scalar one does."""
+    n, k, m = 64, 512, 10
+    w = O.normal(51, n * k, 0.0, 0.02).reshape(n, k)
+    x = O.normal(52, m * k).reshape(m, k)
+    x[1] *= np.float32(1e-38)   # products and sums in the subnormal range
+    x[2] *= np.float32(1e-30)
+    x[3, 7] = np.float32(np.inf)
+    x[4, 9] = np.float32(np.nan)
+    x[5, 11] = np.float32(-np.inf)
+    x[5, 12] = np.float32(np.inf)
+    wd, xd, yd = ctx.to_device(w), ctx.to_device(x), ctx.empty((m, n))
+    ctx.launch("gemv", {"n": n, "k": k, "m": m, "split": 1, "ldx": k, "ldy": n}, [wd, xd, yd])
+    y = yd.download()
+    want = O.gemv(w, x, 1, THREADS)
+    assert np.any((y[1] != 0) & (np.abs(y[1]) < np.finfo(np.float32).tiny))
+    # NaN payloads aside, the same values bit for bit.
+    nan = np.isnan(want)
+    assert np.array_equal(np.isnan(y), nan)
+    assert same_bits(np.where(nan, 0, y), np.where(nan, 0, want))
+    for b in (wd, xd, yd):
+        b.free()
+
+
 # ---------------------------------------------------------------------------
 # The decode attention path: KV store, split attention, combine
 
