@@ -146,7 +146,7 @@ __global__ void __launch_bounds__(1024) argmax_pairs_kernel(const float* __restr
       }
     }
   }
-  if (scatter) peers_signal(peers, 2);
+  if (scatter) peers_signal(peers, 2, (threadIdx.x & 31) == 0);
 }
 
 // The greedy id from the shards' candidates, [shards][m][2], in shard order:

@@ -21,7 +21,10 @@
 // pair's tile instead of in the next step's prologue (the same bits, once).
 //
 // Tensor parallelism (fk_peers.cuh): the row-parallel projections scatter
-// their partial rows into every rank's exchange region (SEPI_SCATTER); the
+// their partial rows into every rank's exchange region (SEPI_SCATTER: a
+// block owns a contiguous run of rows, stages them in shared memory and
+// writes them into this rank's own slot; the grid's last block copies the
+// slot to every other rank with 128-bit stores and releases it); the
 // next GEMV's prologue (SPRO_REDUCE_RMSNORM) waits for every rank's partial,
 // forms the residual row x_new = r + (((P_0 + P_1) + P_2) + ...), ranks in
 // order, so that every rank holds the same bits, stores it (block 0), and
@@ -51,6 +54,7 @@ struct StreamArgs {
 enum { SPRO_NONE = 0, SPRO_RMSNORM = 1, SPRO_SILU = 2, SPRO_REDUCE_RMSNORM = 3 };
 enum { SEPI_NONE = 0, SEPI_ADD = 1, SEPI_SILU_PAIR = 2, SEPI_SCATTER = 3 };
 constexpr int kStreamWarps = 16;
+constexpr uint32_t kScatterRows = 128;  // a scattering block's most output rows
 
 __device__ __forceinline__ float silu_of(float a, float b) {
   const float e = exp_rounded(-a);
@@ -179,9 +183,14 @@ __global__ void __launch_bounds__(512, 2) gemv_stream_kernel(StreamArgs a) {
     __syncthreads();
   }
 
+  // Scattering blocks own contiguous output rows [s_lo, s_hi), staged in
+  // shared memory and written to every rank in contiguous runs.
+  __shared__ float outs[EPI == SEPI_SCATTER ? M : 1][EPI == SEPI_SCATTER ? kScatterRows : 1];
+  const uint32_t s_lo = (uint32_t)((uint64_t)units * blockIdx.x / G);
+  const uint32_t s_hi = (uint32_t)((uint64_t)units * (blockIdx.x + 1) / G);
   for (uint32_t slot = (uint32_t)warp;; slot += kStreamWarps) {
-    const uint32_t u = blockIdx.x + slot * G;
-    if (u >= units) break;
+    const uint32_t u = EPI == SEPI_SCATTER ? s_lo + slot : blockIdx.x + slot * G;
+    if (EPI == SEPI_SCATTER ? u >= s_hi : u >= units) break;
     float t0[M], t1[M];
     row_totals<M>(reinterpret_cast<const float4*>(a.w + (size_t)u * per_unit * a.k), xs4, packs, a.m, a.split,
                   lane, t0);
@@ -193,9 +202,7 @@ __global__ void __launch_bounds__(512, 2) gemv_stream_kernel(StreamArgs a) {
       for (int i = 0; i < M; ++i) {
         if (i >= (int)a.m) break;
         if (EPI == SEPI_SCATTER) {
-          // This rank's partial of output u, into every rank's slot for it.
-          for (uint32_t q = 0; q < a.peers.world; ++q)
-            xdata(a.peers.base[q], a.xbuf, a.peers.rank)[(size_t)i * a.n + u] = t0[i];
+          outs[i][u - s_lo] = t0[i];
           continue;
         }
         float v;
@@ -209,7 +216,18 @@ __global__ void __launch_bounds__(512, 2) gemv_stream_kernel(StreamArgs a) {
       }
     }
   }
-  if (EPI == SEPI_SCATTER) peers_signal(a.peers, a.xbuf);
+  if (EPI == SEPI_SCATTER) {
+    // This rank's partial rows [s_lo, s_hi) into its own slot of its own
+    // region; the last block broadcasts the slot to every rank.
+    __syncthreads();
+    const uint32_t cnt = s_hi - s_lo;
+    float* dst = xdata(a.peers.base[a.peers.rank], a.xbuf, a.peers.rank);
+    for (uint32_t idx = threadIdx.x; idx < a.m * cnt; idx += blockDim.x) {
+      const uint32_t i = idx / cnt, j = idx - i * cnt;
+      dst[(size_t)i * a.n + s_lo + j] = outs[i][j];
+    }
+    peers_broadcast(a.peers, a.xbuf, a.m * a.n, threadIdx.x < a.m * cnt);
+  }
 }
 
 template <int M, int PRO, int EPI>
@@ -230,6 +248,7 @@ static cudaError_t launch_stream(const StreamArgs& a, int sms, cudaStream_t st, 
   const uint32_t units = EPI == SEPI_SILU_PAIR ? a.n / 2 : a.n;
   uint32_t blocks = (uint32_t)(sms * per_sm);
   if (blocks > units) blocks = units;
+  if (EPI == SEPI_SCATTER && (units + blocks - 1) / blocks > kScatterRows) return cudaErrorInvalidValue;
   return fk_launch_ex(kern, dim3(blocks), dim3(512), smem, st, pdl, a);
 }
 

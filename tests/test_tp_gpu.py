@@ -1,9 +1,9 @@
-"""Tensor parallelism on 2 GPUs: a small model's decode step sharded over two
-ranks (torchrun, one process a GPU), checked against the f64 evaluator's
-bounds over the whole model (the allreduce orders the row-parallel sums
-differently from one GPU, so TP is held to the bounds, not to bits), the
-ranks' hidden rows bit-identical, greedy ids equal to the referee's where
-its bounds decide them."""
+"""Tensor parallelism on 2, 4 and 8 GPUs: a small model's decode step sharded
+over the ranks (torchrun, one process a GPU), checked bit for bit against the
+CPU restatement of the tensor-parallel arithmetic (each shard's sums, the
+row-parallel partials added in rank order) and, over the whole model, within
+the f64 evaluator's bounds; the ranks' hidden rows bit-identical, greedy ids
+equal to the referee's where its bounds decide them."""
 
 import math
 import os
@@ -37,28 +37,28 @@ def free_port() -> int:
         return s.getsockname()[1]
 
 
-@pytest.mark.skipif(gpus() < 2, reason="needs 2 GPUs")
-def test_tp2_decode_step_within_bounds(tmp_path):
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_decode_step_within_bounds(tmp_path, world):
+    if gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=ROOT)
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(free_port()),
+           "--nproc-per-node", str(world), "--master-addr", "127.0.0.1", "--master-port", str(free_port()),
            os.path.join(ROOT, "tests", "tp_worker.py"), str(tmp_path)]
     r = subprocess.run(cmd, env=env, cwd=ROOT, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import tp_worker as W
-    from furykernel_b200.program.llama import LlamaShape
-
-    s = LlamaShape(d_model=512, heads=4, kv_heads=4, head_dim=128, ffn=1024, vocab=3000, layers=2, slots=2,
-                   length=64, positions=64)
+    s = W.shape()
     layers, embed, final_norm = W.model(s)
-    ids = [np.load(tmp_path / f"ids_{r}.npy") for r in range(2)]
-    xs = [np.load(tmp_path / f"x_{r}.npy") for r in range(2)]
-    logits = np.concatenate([np.load(tmp_path / f"logits_{r}.npy") for r in range(2)], axis=1)
-    kc = np.concatenate([np.load(tmp_path / f"kc_{r}.npy") for r in range(2)], axis=2)
-    vc = np.concatenate([np.load(tmp_path / f"vc_{r}.npy") for r in range(2)], axis=2)
-    assert np.array_equal(ids[0], ids[1])
-    assert np.array_equal(xs[0].view(np.uint32), xs[1].view(np.uint32))
+    ids = [np.load(tmp_path / f"ids_{r}.npy") for r in range(world)]
+    xs = [np.load(tmp_path / f"x_{r}.npy") for r in range(world)]
+    logits = np.concatenate([np.load(tmp_path / f"logits_{r}.npy") for r in range(world)], axis=1)
+    kc = np.concatenate([np.load(tmp_path / f"kc_{r}.npy") for r in range(world)], axis=2)
+    vc = np.concatenate([np.load(tmp_path / f"vc_{r}.npy") for r in range(world)], axis=2)
+    for r in range(1, world):
+        assert np.array_equal(ids[0], ids[r])
+        assert np.array_equal(xs[0].view(np.uint32), xs[r].view(np.uint32))
     # Bit for bit with the CPU restatement of the tensor-parallel arithmetic
     # (shard GEMVs, partials added in rank order, then the residual).
     tokens = np.array([5, 2999], np.uint32)
@@ -66,8 +66,8 @@ def test_tp2_decode_step_within_bounds(tmp_path):
     slot = np.arange(2, dtype=np.uint32)
     kc0 = np.zeros_like(kc)
     vc0 = np.zeros_like(vc)
-    want_ids, want_logits, want_x = MC.oracle_decode_tp(s, 2, layers, embed, final_norm, kc0, vc0, tokens, pos, slot,
-                                                        16, 4)
+    want_ids, want_logits, want_x = MC.oracle_decode_tp(s, world, layers, embed, final_norm, kc0, vc0, tokens, pos,
+                                                        slot, 16, 4)
     assert np.array_equal(kc0.view(np.uint32), kc.view(np.uint32))
     assert np.array_equal(vc0.view(np.uint32), vc.view(np.uint32))
     assert np.array_equal(xs[0].view(np.uint32), want_x.view(np.uint32))

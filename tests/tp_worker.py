@@ -35,16 +35,22 @@ def model(s):
     return layers, embed, final_norm
 
 
+def shape(batch=2):
+    """The test model: 8 heads, so that it shards over 2, 4 or 8 ranks."""
+    from furykernel_b200.program.llama import LlamaShape
+
+    return LlamaShape(d_model=512, heads=8, kv_heads=8, head_dim=128, ffn=1024, vocab=3000, layers=2, slots=batch,
+                      length=64, positions=64)
+
+
 def main():
     out_dir = sys.argv[1]
     from furykernel_b200 import tp
     from furykernel_b200.engine import Llama, shard_weights
-    from furykernel_b200.program.llama import LlamaShape
 
     ctx, rank, world, local = tp.init()
     batch = 2
-    s = LlamaShape(d_model=512, heads=4, kv_heads=4, head_dim=128, ffn=1024, vocab=3000, layers=2, slots=batch,
-                   length=64, positions=64)
+    s = shape(batch)
     layers, embed, final_norm = model(s)
     arena = shard_weights(s, layers, embed, final_norm, rank, world, interleave=batch <= 4)
     eng = Llama(ctx, s, batch, chunk=16, rank=rank, world=world, host_weights=arena)
