@@ -20,6 +20,7 @@ namespace fk {
 constexpr int kAttWarps = 4;
 constexpr int kHeadDim = 128;  // one float4 pack a lane
 constexpr int kMaxChunk = 256;
+constexpr uint32_t kMaxAttendRows = 16384;  // rows of one launch (prefill), first[] in shared memory
 
 // RoPE of one head (halves pairing, Eval.hs:634-645): thread i < d/2 turns
 // pair (i, i + d/2) by the position's table entry; pairs past `rotated` stay.
@@ -62,7 +63,7 @@ __global__ void __launch_bounds__(128, 4) attend_split_kernel(FkAttend a) {
   __shared__ float scores[kMaxChunk];
   __shared__ float4 accw[kAttWarps][kHeadDim / 4];
   __shared__ float lw[kAttWarps];
-  __shared__ uint32_t first[65];  // items before row r (rows <= 64 here)
+  extern __shared__ uint32_t first[];  // [m + 1]: items before row r
 
   grid_wait();
   grid_launch_dependents();
@@ -83,8 +84,13 @@ __global__ void __launch_bounds__(128, 4) attend_split_kernel(FkAttend a) {
   constexpr uint32_t kStep = B * kAttWarps;
 
   for (uint32_t it = blockIdx.x; it < items; it += gridDim.x) {
-    uint32_t r = 0;
-    while (it >= first[r + 1]) ++r;
+    // The row whose items hold it: the last r with first[r] <= it.
+    uint32_t lo = 0, hi = a.m - 1;
+    while (lo < hi) {
+      const uint32_t mid = (lo + hi + 1) / 2;
+      if (first[mid] <= it) lo = mid; else hi = mid - 1;
+    }
+    const uint32_t r = lo;
     const uint32_t p = a.pos[r];
     const uint32_t splits = (p + 1 + a.chunk - 1) / a.chunk;
     const uint32_t local = it - first[r];
@@ -231,20 +237,28 @@ cudaError_t fk_launch_kv_store(const FkKvStore& a, cudaStream_t s) {
 
 cudaError_t fk_launch_attend(const FkAttend& a, cudaStream_t s) {
   if (a.m == 0) return cudaSuccess;
-  if (a.d != fk::kHeadDim || a.chunk == 0 || a.chunk > fk::kMaxChunk || a.heads % a.kv_heads != 0 || a.m > 64)
+  if (a.d != fk::kHeadDim || a.chunk == 0 || a.chunk > fk::kMaxChunk || a.heads % a.kv_heads != 0 ||
+      a.m > fk::kMaxAttendRows || (uint64_t)a.m * a.heads * a.max_splits >= (1ull << 32))
     return cudaErrorInvalidValue;
   // Blocks for the most items a step can have, as many as are resident at
   // once; each loops over its items.
   int dev = 0, sms = 148, per_sm = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fk::attend_split_kernel, 128, 0);
+  const size_t smem = ((size_t)a.m + 1) * sizeof(uint32_t);
+  static size_t configured = 0;
+  if (smem > 48 * 1024 && smem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(fk::attend_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = smem;
+  }
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fk::attend_split_kernel, 128, smem);
   if (e != cudaSuccess) return e;
   if (per_sm < 1) return cudaErrorInvalidConfiguration;
   const uint64_t most = (uint64_t)a.m * a.heads * a.max_splits;
   const uint64_t resident = (uint64_t)sms * per_sm;
   const uint32_t blocks = (uint32_t)(most < resident ? most : resident);
-  return fk_launch_ex(fk::attend_split_kernel, dim3(blocks), dim3(128), 0, s, a.pdl, a);
+  return fk_launch_ex(fk::attend_split_kernel, dim3(blocks), dim3(128), smem, s, a.pdl, a);
 }
 
 cudaError_t fk_launch_combine(const FkCombine& a, cudaStream_t s) {

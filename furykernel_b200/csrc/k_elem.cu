@@ -194,6 +194,16 @@ __global__ void silu_mul_kernel(const float* __restrict__ a, const float* __rest
   }
 }
 
+// The SiLU-gate of interleaved (gate, up) pairs, as silu_mul computes it:
+// y[i] = silu(x[2i]) * x[2i + 1] (a GEMM over gate/up rows interleaved).
+__global__ void silu_pairs_kernel(const float2* __restrict__ x, float* __restrict__ y, uint64_t n) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+    const float2 gu = x[i];
+    const float e = exp_rounded(-gu.x);
+    y[i] = __fmul_rn(__fdiv_rn(gu.x, __fadd_rn(1.0f, e)), gu.y);
+  }
+}
+
 // Seeded inputs: SplitMix's finaliser of seed * golden + i, i from 1
 // (test/cpu/Cases.hs:885-892). N(mu, sigma) by Box-Muller on consecutive
 // words, in binary64 rounded once; U(a, b) from the top 24 bits.
@@ -292,6 +302,13 @@ cudaError_t fk_launch_add(const float* a, const float* b, float* y, uint64_t n, 
 cudaError_t fk_launch_silu_mul(const float* a, const float* b, float* y, uint64_t n, cudaStream_t s) {
   if (n == 0) return cudaSuccess;
   fk::silu_mul_kernel<<<grid_for(n), 256, 0, s>>>(a, b, y, n);
+  return cudaGetLastError();
+}
+
+cudaError_t fk_launch_silu_pairs(const float* x, float* y, uint64_t n, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  if (reinterpret_cast<uintptr_t>(x) & 7) return cudaErrorInvalidValue;
+  fk::silu_pairs_kernel<<<grid_for(n), 256, 0, s>>>(reinterpret_cast<const float2*>(x), y, n);
   return cudaGetLastError();
 }
 

@@ -584,6 +584,10 @@ int l_add(fkc_ctx* c, const Params& p, void* const* bufs) {
 int l_silu_mul(fkc_ctx* c, const Params& p, void* const* bufs) {
   return launched(fk_launch_silu_mul(CF(0), CF(1), F(2), p.u(0), c->stream), "silu_mul");
 }
+// silu_pairs: x y | n: y[i] = silu(x[2i]) * x[2i + 1].
+int l_silu_pairs(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return launched(fk_launch_silu_pairs(CF(0), F(1), p.u(0), c->stream), "silu_pairs");
+}
 
 #undef F
 #undef CF
@@ -668,7 +672,7 @@ std::vector<KernelSpec> make_table() {
                 {"part_m", "write", "f32"},
                 {"part_l", "write", "f32"},
                 {"part_acc", "write", "f32"}},
-               {dim("m", 1, 64), dim("heads", 1, 1024), dim("kv_heads", 1, 1024), dim("d", 128, 128),
+               {dim("m", 1, 16384), dim("heads", 1, 1024), dim("kv_heads", 1, 1024), dim("d", 128, 128),
                 dim("length", 1, kMax), u32("rotated"), dim("chunk", 1, 256), dim("max_splits", 1, 65535), u32("ldq"),
                 u32("q_off"), f32("scale")},
                l_attend});
@@ -762,6 +766,7 @@ std::vector<KernelSpec> make_table() {
                {{"a", "read", "f32"}, {"b", "read", "f32"}, {"y", "write", "f32"}},
                {dim("n", 1, kMax)},
                l_silu_mul});
+  t.push_back({"silu_pairs", 256, {{"x", "read", "f32"}, {"y", "write", "f32"}}, {dim("n", 1, kMax)}, l_silu_pairs});
   // The C layout (Abi.hs:113-133) and the canonical text (Abi.hs:136-159).
   for (auto& k : t) {
     uint32_t off = 0, align = 1;

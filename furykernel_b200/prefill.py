@@ -1,0 +1,197 @@
+"""Prompt prefill for the Llama engine: every prompt row through the layers
+at once, the projections as tcgen05 3xTF32 GEMMs (`gemm_tf32x3`), which
+store each row's keys and values in the Ring caches; then the engine's
+decode step continues from the last prompt row.
+
+The plan is the decode layer's (src/FuryKernel/Program/Plan.hs: RMSNorm
+before each anchor, the KV store before the attention, the residual Adds),
+run over R rows with the linears as tiles instead of GEMVs:
+
+    x  = gather(embed, tokens)
+    per layer:
+      a    = rmsnorm_rows(x, attn_norm)
+      qkv  = a [q;k;v]^T                      (GEMM)
+      kv_store_ring(qkv rows at their positions)
+      att  = attend_split + attend_combine     (each row over positions <= its own)
+      x1   = x + att o^T                       (GEMM, then add; TP: allreduce first)
+      m    = rmsnorm_rows(x1, mlp_norm)
+      act  = silu(m gate^T) * (m up^T)         (GEMM over the arena's gate/up rows)
+      x    = x1 + act down^T                   (GEMM, then add; TP: allreduce first)
+
+The GEMMs are 3xTF32 (a_hi b_hi + a_hi b_lo + a_lo b_hi, f32 accumulation
+in TMEM), so prefill agrees with the binary32 contract within the f64
+evaluator's bounds, not bit for bit; the decode steps after it are the
+contract's bits given the caches prefill left. The weights' TF32 halves
+are split once, into two arenas laid out as the weight arena.
+
+With tensor parallelism each rank runs its shard's GEMMs; the row-parallel
+partials (o, down) are summed by an NCCL allreduce before the residual add.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from . import _native as N
+from .engine import Launch, Llama
+
+
+class Prefill:
+    """Prefill of up to `rows` prompt rows for an engine (any batch, any
+    rank). `run(tokens, positions, slots)` stores the rows' keys and values
+    and leaves the last layer's rows in `x`."""
+
+    def __init__(self, eng: Llama, rows: int, chunk: int | None = None):
+        ctx, s = eng.ctx, eng.s
+        self.eng, self.ctx, self.R = eng, ctx, rows
+        d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
+        for what, k in (("d_model", d), ("q width", qw), ("ffn", f)):
+            if k % 32:
+                raise N.Refused(N.FKC_ERR_ARGUMENT, f"prefill: the GEMM's K ({what} {k}) is not a multiple of 32.")
+        # The layers' TF32 halves, laid out as the weight arena, a layer a
+        # launch.
+        per = eng.layer_elems
+        self.w_hi = ctx.alloc(4 * s.layers * per)
+        self.w_lo = ctx.alloc(4 * s.layers * per)
+        for l in range(s.layers):
+            at = 4 * l * per
+            ctx.launch("split_tf32", {"n": per}, [eng.arena.ptr + at, self.w_hi.ptr + at, self.w_lo.ptr + at])
+        R = rows
+        kmax = max(d, qw, f)
+        self.rs = (R + 3) // 4 * 4
+        self.rows_buf = ctx.zeros(3 * self.rs, np.uint32)
+        self.x = ctx.zeros((R, d))
+        self.a = ctx.zeros((R, d))
+        self.a_hi = ctx.zeros((R, kmax))
+        self.a_lo = ctx.zeros((R, kmax))
+        self.qkv = ctx.zeros((R, qw + 2 * kvw))
+        self.att = ctx.zeros((R, qw))
+        self.tmp = ctx.zeros((R, d))
+        self.x1 = ctx.zeros((R, d))
+        self.gu = ctx.zeros((R, 2 * f))
+        self.act = ctx.zeros((R, f))
+        self.chunk = chunk or eng.chunk
+        self.max_splits = (s.positions + self.chunk - 1) // self.chunk
+        ms = R * s.heads * self.max_splits
+        self.part = [ctx.zeros(ms), ctx.zeros(ms), ctx.zeros(ms * s.head_dim)]
+        self.graphs: dict = {}
+
+    def _hi(self, ptr: int) -> int:
+        return self.w_hi.ptr + (ptr - self.eng.arena.ptr)
+
+    def _lo(self, ptr: int) -> int:
+        return self.w_lo.ptr + (ptr - self.eng.arena.ptr)
+
+    def _gemm(self, a, K: int, w: int, N: int, c, ldc: int) -> Launch:
+        return Launch("gemm_tf32x3", {"M": self.m, "N": N, "K": K, "ldc": ldc},
+                      [a, self.a_hi.ptr, self.a_lo.ptr, self._hi(w), self._lo(w), c])
+
+    def launches(self, m: int) -> list:
+        """The launch list over the first m rows of the row buffers."""
+        eng, s = self.eng, self.eng.s
+        if not 1 <= m <= self.R:
+            raise N.Refused(N.FKC_ERR_ARGUMENT, f"prefill: {m} rows, outside 1..{self.R}.")
+        self.m = m
+        d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
+        rs4 = 4 * self.rs
+        tok, pos, slot = self.rows_buf.ptr, self.rows_buf.ptr + rs4, self.rows_buf.ptr + 2 * rs4
+        # The decode step's own launches are the templates of the gather,
+        # the KV stores and the attention (their shapes and tables).
+        by = {}
+        for L in eng.launches:
+            by.setdefault(L.kernel, []).append(L)
+        g0 = by["gather"][0]
+        out = [Launch("gather", dict(g0.params, m=m), [g0.bufs[0], tok, self.x.ptr])]
+        eps = None
+        for L in eng.launches:
+            if L.kernel.startswith("gemv") and "eps" in L.params:
+                eps = L.params["eps"]
+                break
+        nq = qw + 2 * kvw
+        for l in range(s.layers):
+            w = eng.layer_weights(l)
+            kv, at, cb = by["kv_store_ring"][l], by["attend_split"][l], by["attend_combine"][l]
+            out.append(Launch("rmsnorm_rows", {"rows": m, "h": d, "eps": eps, "factor": 1.0},
+                              [self.x.ptr, w["attn_norm"], self.a.ptr]))
+            out.append(self._gemm(self.a.ptr, d, w["q_proj"], nq, self.qkv.ptr, nq))
+            out.append(Launch("kv_store_ring", dict(kv.params, m=m, ldq=nq),
+                              [self.qkv.ptr, kv.bufs[1], kv.bufs[2], pos, slot, kv.bufs[5], kv.bufs[6]]))
+            out.append(Launch("attend_split", dict(at.params, m=m, ldq=nq, chunk=self.chunk,
+                                                   max_splits=self.max_splits),
+                              [self.qkv.ptr, at.bufs[1], at.bufs[2], pos, slot, at.bufs[5], at.bufs[6],
+                               self.part[0].ptr, self.part[1].ptr, self.part[2].ptr]))
+            out.append(Launch("attend_combine", dict(cb.params, m=m, chunk=self.chunk, max_splits=self.max_splits,
+                                                     ldo=qw),
+                              [self.part[0].ptr, self.part[1].ptr, self.part[2].ptr, pos, self.att.ptr]))
+            out.append(self._gemm(self.att.ptr, qw, w["o_proj"], d, self.tmp.ptr, d))
+            if eng.world > 1:
+                out.append(Launch("__allreduce__", {"count": m * d}, [self.tmp.ptr]))
+            out.append(Launch("add", {"n": m * d}, [self.x.ptr, self.tmp.ptr, self.x1.ptr]))
+            out.append(Launch("rmsnorm_rows", {"rows": m, "h": d, "eps": eps, "factor": 1.0},
+                              [self.x1.ptr, w["mlp_norm"], self.a.ptr]))
+            if eng.gate_up_interleaved:  # rows gate_0, up_0, ...: columns likewise
+                out.append(self._gemm(self.a.ptr, d, w["gate_proj"], 2 * f, self.gu.ptr, 2 * f))
+                out.append(Launch("silu_pairs", {"n": m * f}, [self.gu.ptr, self.act.ptr]))
+            else:  # gate rows, then up rows: one GEMM each, then the gate
+                up = self.gu.ptr + 4 * m * f
+                out.append(self._gemm(self.a.ptr, d, w["gate_proj"], f, self.gu.ptr, f))
+                out.append(self._gemm(self.a.ptr, d, w["up_proj"], f, up, f))
+                out.append(Launch("silu_mul", {"n": m * f}, [self.gu.ptr, up, self.act.ptr]))
+            out.append(self._gemm(self.act.ptr, f, w["down_proj"], d, self.tmp.ptr, d))
+            if eng.world > 1:
+                out.append(Launch("__allreduce__", {"count": m * d}, [self.tmp.ptr]))
+            out.append(Launch("add", {"n": m * d}, [self.x1.ptr, self.tmp.ptr, self.x.ptr]))
+        return out
+
+    def set_rows(self, tokens, positions, slots) -> int:
+        tokens = np.asarray(tokens, np.uint32)
+        m = len(tokens)
+        if m > self.R:
+            raise N.Refused(N.FKC_ERR_ARGUMENT, f"prefill: {m} rows, more than {self.R}.")
+        host = np.zeros(3 * self.rs, np.uint32)
+        host[:m] = tokens
+        host[self.rs:self.rs + m] = np.asarray(positions, np.uint32)
+        host[2 * self.rs:2 * self.rs + m] = np.asarray(slots, np.uint32)
+        self.rows_buf.upload(host)
+        return m
+
+    def graph(self, m: int) -> N.Graph:
+        """The captured prefill of m rows (one graph a row count)."""
+        g = self.graphs.get(m)
+        if g is None:
+            launches = self.launches(m)
+            self.ctx.set_pdl(False)
+            self.ctx.capture_begin()
+            try:
+                for L in launches:
+                    self.eng._run(L)
+            finally:
+                g = self.ctx.capture_end()
+            self.graphs[m] = g
+        return g
+
+    def run(self, tokens, positions, slots) -> None:
+        m = self.set_rows(tokens, positions, slots)
+        self.graph(m).launch()
+
+    def close(self) -> None:
+        for g in self.graphs.values():
+            g.destroy()
+        self.graphs = {}
+
+
+def prompt_then_decode(eng: Llama, pre: Prefill, prompts, slots) -> np.ndarray:
+    """Prefill each prompt's rows but its last into its slot (all prompts'
+    rows at once, R rows at a time), then one decode step over the batch
+    from each prompt's last token: the first generated ids."""
+    prompts = [np.asarray(p, np.uint32) for p in prompts]
+    toks, poss, sl = [], [], []
+    for p, s in zip(prompts, slots):
+        toks.append(p[:-1])
+        poss.append(np.arange(len(p) - 1, dtype=np.uint32))
+        sl.append(np.full(len(p) - 1, s, np.uint32))
+    toks, poss, sl = np.concatenate(toks), np.concatenate(poss), np.concatenate(sl)
+    for i in range(0, len(toks), pre.R):
+        pre.run(toks[i:i + pre.R], poss[i:i + pre.R], sl[i:i + pre.R])
+    eng.set_rows([p[-1] for p in prompts], [len(p) - 1 for p in prompts], slots)
+    return eng.step()

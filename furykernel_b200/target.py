@@ -119,7 +119,7 @@ SPEC_KERNELS = {
         KernelSig("attend_split",
                   [_f32("qkv"), _f32("cos"), _f32("sin"), _u32("pos"), _u32("slot"), _f32("k_cache"),
                    _f32("v_cache"), _f32("part_m", "write"), _f32("part_l", "write"), _f32("part_acc", "write")],
-                  [_dim("m", 1, 64), _dim("heads", 1, 1024), _dim("kv_heads", 1, 1024), _dim("d", 128, 128),
+                  [_dim("m", 1, 16384), _dim("heads", 1, 1024), _dim("kv_heads", 1, 1024), _dim("d", 128, 128),
                    _dim("length", 1, _MAX), _u("rotated"), _dim("chunk", 1, 256), _dim("max_splits", 1, 65535),
                    _u("ldq"), _u("q_off"), _f("scale")], threads=128),
         KernelSig("attend_combine",
@@ -155,6 +155,7 @@ SPEC_KERNELS = {
         KernelSig("advance", [_u32("ids"), _u32("tokens", "write"), _u32("pos", "read_write")], [_dim("m", 1, 65535)]),
         KernelSig("add", [_f32("a"), _f32("b"), _f32("y", "write")], [_dim("n", 1, _MAX)]),
         KernelSig("silu_mul", [_f32("a"), _f32("b"), _f32("y", "write")], [_dim("n", 1, _MAX)]),
+        KernelSig("silu_pairs", [_f32("x"), _f32("y", "write")], [_dim("n", 1, _MAX)]),
     ]
 }
 
