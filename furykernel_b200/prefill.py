@@ -41,7 +41,7 @@ class Prefill:
     rank). `run(tokens, positions, slots)` stores the rows' keys and values
     and leaves the last layer's rows in `x`."""
 
-    def __init__(self, eng: Llama, rows: int, chunk: int | None = None):
+    def __init__(self, eng: Llama, rows: int, chunk: int | None = None, positions: int | None = None):
         ctx, s = eng.ctx, eng.s
         self.eng, self.ctx, self.R = eng, ctx, rows
         d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
@@ -71,7 +71,10 @@ class Prefill:
         self.gu = ctx.zeros((R, 2 * f))
         self.act = ctx.zeros((R, f))
         self.chunk = chunk or eng.chunk
-        self.max_splits = (s.positions + self.chunk - 1) // self.chunk
+        # Splits a row's attention can have: up to the largest position a
+        # prefill here stores (the engine's positions unless given).
+        self.positions = positions or s.positions
+        self.max_splits = (self.positions + self.chunk - 1) // self.chunk
         ms = R * s.heads * self.max_splits
         self.part = [ctx.zeros(ms), ctx.zeros(ms), ctx.zeros(ms * s.head_dim)]
         self.graphs: dict = {}
@@ -148,6 +151,9 @@ class Prefill:
         m = len(tokens)
         if m > self.R:
             raise N.Refused(N.FKC_ERR_ARGUMENT, f"prefill: {m} rows, more than {self.R}.")
+        if m and int(np.max(positions)) >= self.positions:
+            raise N.Refused(N.FKC_ERR_ARGUMENT,
+                            f"prefill: position {int(np.max(positions))} is past the {self.positions} it was sized for.")
         host = np.zeros(3 * self.rs, np.uint32)
         host[:m] = tokens
         host[self.rs:self.rs + m] = np.asarray(positions, np.uint32)
@@ -174,23 +180,35 @@ class Prefill:
         m = self.set_rows(tokens, positions, slots)
         self.graph(m).launch()
 
+    def gemm_flops(self, rows: int) -> int:
+        """Useful flops of the GEMMs over `rows` rows (2 a multiply-add)."""
+        s = self.eng.s
+        return 2 * rows * s.layers * (self.eng.layer_elems - 2 * s.d_model)
+
     def close(self) -> None:
+        """Destroys the graphs and frees the TF32 halves and scratch."""
         for g in self.graphs.values():
             g.destroy()
         self.graphs = {}
+        for b in [self.w_hi, self.w_lo, self.rows_buf, self.x, self.a, self.a_hi, self.a_lo, self.qkv, self.att,
+                  self.tmp, self.x1, self.gu, self.act] + self.part:
+            b.free()
+
+
+def prompt_rows(prompts, slots):
+    """Every prompt's rows but its last: (tokens, positions, slots)."""
+    prompts = [np.asarray(p, np.uint32) for p in prompts]
+    toks = np.concatenate([p[:-1] for p in prompts])
+    poss = np.concatenate([np.arange(len(p) - 1, dtype=np.uint32) for p in prompts])
+    sl = np.concatenate([np.full(len(p) - 1, s, np.uint32) for p, s in zip(prompts, slots)])
+    return toks, poss, sl
 
 
 def prompt_then_decode(eng: Llama, pre: Prefill, prompts, slots) -> np.ndarray:
     """Prefill each prompt's rows but its last into its slot (all prompts'
     rows at once, R rows at a time), then one decode step over the batch
     from each prompt's last token: the first generated ids."""
-    prompts = [np.asarray(p, np.uint32) for p in prompts]
-    toks, poss, sl = [], [], []
-    for p, s in zip(prompts, slots):
-        toks.append(p[:-1])
-        poss.append(np.arange(len(p) - 1, dtype=np.uint32))
-        sl.append(np.full(len(p) - 1, s, np.uint32))
-    toks, poss, sl = np.concatenate(toks), np.concatenate(poss), np.concatenate(sl)
+    toks, poss, sl = prompt_rows(prompts, slots)
     for i in range(0, len(toks), pre.R):
         pre.run(toks[i:i + pre.R], poss[i:i + pre.R], sl[i:i + pre.R])
     eng.set_rows([p[-1] for p in prompts], [len(p) - 1 for p in prompts], slots)

@@ -87,7 +87,7 @@ def max_over_ranks(v: float) -> float:
     return float(t.item())
 
 
-def bench_main(args, metric: str, prompt: int) -> None:
+def bench_main(args, metric: str, prompt: int, prefill_fn) -> None:
     """The decode bench at N ranks: each rank replays its shard's captured
     step; the step time is the max over ranks of the device-timed replays."""
     import torch.distributed as dist
@@ -99,8 +99,11 @@ def bench_main(args, metric: str, prompt: int) -> None:
     b = args.batch
     length = 4096 if b <= 4 else 1024
     shape = LlamaShape(layers=args.layers, slots=b, length=length, positions=length)
-    eng = Llama(ctx, shape, b, seed=2026, chunk=32, prefill_kv=1.0, rank=rank, world=world)
-    tokens = np.arange(b, dtype=np.uint32) * 7 + 1
+    eng = Llama(ctx, shape, b, seed=2026, chunk=32, rank=rank, world=world)
+    tokens, prefill = prefill_fn(ctx, eng, b, local)
+    prefill["ms"] = max_over_ranks(prefill["ms"])
+    prefill["tokens_per_s"] = prefill["rows"] / (prefill["ms"] / 1e3)
+    prefill["gemm_tflops_per_gpu"] = prefill["gemm_flops_per_gpu"] / (prefill["ms"] / 1e3) / 1e12
     slots = np.arange(b, dtype=np.uint32)
     eng.set_rows(tokens, np.full(b, prompt, np.uint32), slots)
     graph = eng.capture()
@@ -139,7 +142,8 @@ def bench_main(args, metric: str, prompt: int) -> None:
             "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic: seeded N(0,0.02) weights made on the device, KV of a 512-position prompt seeded N(0,1)",
+            "data": "synthetic: seeded N(0,0.02) weights made on the device; prompts of 512 ids U[0,32000) (numpy "
+                    "PCG64 seed 512) prefilled through the model",
             "config": {"workload": f"config 5 decode, batch {b}, context {prompt}..{prompt + args.steps}",
                        "model": "llama-shaped 32 layers, d 4096, 32 heads x 128, ffn 11008, vocab 32000, tied head",
                        "global_batch": b, "seq_len": prompt, "parallelism": f"tp{world}", "kv_length": length,
@@ -148,6 +152,7 @@ def bench_main(args, metric: str, prompt: int) -> None:
             "e2e": {"value": b * args.steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(host_in.nbytes),
                     "d2h_bytes_per_step": int(host_out.nbytes)},
             "gpu_launches": eng.launch_count() * args.steps,
+            "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
     finish(ctx, [graph])
