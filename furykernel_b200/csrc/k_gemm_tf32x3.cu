@@ -140,7 +140,10 @@ __global__ void __launch_bounds__(192, 1)
   __shared__ int aborted;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t m0 = blockIdx.y * kGM, n0 = blockIdx.x * kGN;
+  // M tiles vary fastest: the CTAs that share a weight tile (one N tile,
+  // every M tile) run together, so the tile crosses HBM once and is reused
+  // from L2.
+  const uint32_t m0 = blockIdx.x * kGM, n0 = blockIdx.y * kGN;
   const uint32_t kblocks = K / kGK;
 
   if (threadIdx.x == 0) {
@@ -315,7 +318,8 @@ cudaError_t fk_launch_gemm_tf32x3(const float* a_hi, const float* a_lo, const fl
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  dim3 grid((N + fk::kGN - 1) / fk::kGN, (M + fk::kGM - 1) / fk::kGM);
+  if ((N + fk::kGN - 1) / fk::kGN > 65535) return cudaErrorInvalidValue;
+  dim3 grid((M + fk::kGM - 1) / fk::kGM, (N + fk::kGN - 1) / fk::kGN);
   fk::gemm_tf32x3_kernel<<<grid, 192, fk::kGemmSmem, s>>>(ma_hi, ma_lo, mw_hi, mw_lo, c, M, N, K, ldc, err);
   return cudaGetLastError();
 }
