@@ -554,8 +554,10 @@ def run_kernel_config(args):
         eng.set_rows(np.arange(b, dtype=np.uint32) + 1, np.full(b, 2048, np.uint32), np.arange(b, dtype=np.uint32))
         eng.run_eager()
         ctx.sync()
-        layer = eng.launches[1:8]
-        assert [L.kernel for L in layer][2:4] == ["attend_split", "attend_combine"], [L.kernel for L in layer]
+        per_layer = (len(eng.launches) - 4) // s.layers  # gather | layers | head, argmax, advance
+        layer = eng.launches[1:1 + per_layer]
+        assert "attend_decode" in [L.kernel for L in layer] or "attend_split" in [L.kernel for L in layer], \
+            [L.kernel for L in layer]
         ctx.set_pdl(True)
         ms = time_graph(ctx, layer, args.steps, args.warmup)
         ctx.set_pdl(False)

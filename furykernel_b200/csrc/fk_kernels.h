@@ -63,6 +63,16 @@ struct FkAttend {
   bool pdl;
 };
 
+// The decode step's KV store and attention in one launch (rows in distinct
+// slots): FkAttend plus where the new key and value sit in a qkv row and the
+// caches to write.
+struct FkAttendDecode {
+  FkAttend a;
+  uint32_t k_off, v_off;  // columns of k and v in a qkv row (ld = a.ldq)
+  float* kc_w;
+  float* vc_w;  // the caches a.kc / a.vc, written
+};
+
 struct FkKvStore {
   const float* qkv;  // k at column k_off, v at column v_off, ld = ldq
   const float* cos_t;
@@ -99,6 +109,7 @@ bool fk_gemv_batches(const FkGemv& g);
 cudaError_t fk_launch_gemv_batch(const FkGemv& g, int sms, cudaStream_t s);
 cudaError_t fk_launch_kv_store(const FkKvStore& a, cudaStream_t s);
 cudaError_t fk_launch_attend(const FkAttend& a, cudaStream_t s);
+cudaError_t fk_launch_attend_decode(const FkAttendDecode& f, cudaStream_t s);
 cudaError_t fk_launch_combine(const FkCombine& a, cudaStream_t s);
 cudaError_t fk_launch_gather(const float* table, uint32_t width, const uint32_t* tokens, uint32_t m, float factor,
                              float* y, bool pdl, cudaStream_t s);

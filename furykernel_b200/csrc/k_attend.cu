@@ -58,8 +58,22 @@ __global__ void kv_store_kernel(FkKvStore a) {
 // requested before q is rotated, so that their latency hides the rotation's;
 // a split's weights exp(s - max) are computed once a position, 32 positions
 // across the lanes, and handed to the warp that adds them by shuffle.
-__global__ void __launch_bounds__(128, 4) attend_split_kernel(FkAttend a) {
+//
+// FUSED (attend_decode, a decode step's rows in distinct slots): the plan's
+// KV store step and its attention in one launch. An item whose positions
+// land on the ring slot of its row's position p rotates the row's new key
+// (and reads its new value) itself and uses them there, so no item waits
+// for the store; one item a (row, KV head) -- the last split, the group's
+// first head -- writes them to the caches. The same arithmetic, so the
+// same bits, as the two kernels. (Counting items in for an in-kernel
+// combine cost more, a release-acquire atomic an item, than the combine
+// launch it saved.)
+template <bool FUSED>
+__global__ void __launch_bounds__(128, 4) attend_kernel(FkAttendDecode f) {
+  const FkAttend& a = f.a;
   __shared__ float qrot[kHeadDim];
+  __shared__ float krot[FUSED ? kHeadDim : 1];
+  __shared__ float vnew[FUSED ? kHeadDim : 1];
   __shared__ float scores[kMaxChunk];
   __shared__ float4 accw[kAttWarps][kHeadDim / 4];
   __shared__ float lw[kAttWarps];
@@ -82,6 +96,7 @@ __global__ void __launch_bounds__(128, 4) attend_split_kernel(FkAttend a) {
   const float4* vc4 = reinterpret_cast<const float4*>(a.vc);
   constexpr int B = 8;  // positions in flight a warp
   constexpr uint32_t kStep = B * kAttWarps;
+  const uint32_t group = a.heads / a.kv_heads;
 
   for (uint32_t it = blockIdx.x; it < items; it += gridDim.x) {
     // The row whose items hold it: the last r with first[r] <= it.
@@ -97,8 +112,13 @@ __global__ void __launch_bounds__(128, 4) attend_split_kernel(FkAttend a) {
     const uint32_t h = local / splits, j = local - h * splits;
     const uint32_t t0 = j * a.chunk;
     const uint32_t t1 = min(p + 1, t0 + a.chunk);
-    const uint32_t kvh = h / (a.heads / a.kv_heads);
+    const uint32_t kvh = h / group;
     const size_t base = ((size_t)a.slot[r] * a.kv_heads + kvh) * a.length;
+    const uint32_t pslot = p % a.length;  // where the row's new key and value land
+    // Whether one of this item's positions lands on that ring slot (the
+    // last split always; earlier ones only once the ring has wrapped).
+    const uint32_t alias = t0 + (pslot + a.length - t0 % a.length) % a.length;
+    const bool fresh = FUSED && alias < t1;
 
     // This warp's first keys and values: they depend on nothing below.
     float4 kv[B], vv[B];
@@ -111,10 +131,24 @@ __global__ void __launch_bounds__(128, 4) attend_split_kernel(FkAttend a) {
     }
 
     __syncthreads();  // the previous item's shared arrays are free
+    const float* cos_row = a.cos_t + (size_t)p * a.rotated;
+    const float* sin_row = a.sin_t + (size_t)p * a.rotated;
     if (threadIdx.x < kHeadDim / 2)
       rope_pair(a.qkv + (size_t)r * a.ldq + a.q_off + (size_t)h * kHeadDim, qrot, threadIdx.x, kHeadDim / 2,
-                a.rotated, a.cos_t + (size_t)p * a.rotated, a.sin_t + (size_t)p * a.rotated);
+                a.rotated, cos_row, sin_row);
+    if (fresh) {
+      const float* krow = a.qkv + (size_t)r * a.ldq + f.k_off + (size_t)kvh * kHeadDim;
+      const float* vrow = a.qkv + (size_t)r * a.ldq + f.v_off + (size_t)kvh * kHeadDim;
+      if (threadIdx.x >= kHeadDim / 2)
+        rope_pair(krow, krot, threadIdx.x - kHeadDim / 2, kHeadDim / 2, a.rotated, cos_row, sin_row);
+      vnew[threadIdx.x] = vrow[threadIdx.x];
+    }
     __syncthreads();
+    if (FUSED && j == splits - 1 && h % group == 0) {  // the KV store step, once a (row, KV head)
+      const size_t at = (base + pslot) * kHeadDim + threadIdx.x;
+      f.kc_w[at] = krot[threadIdx.x];
+      f.vc_w[at] = vnew[threadIdx.x];
+    }
     const float4 qv = reinterpret_cast<const float4*>(qrot)[lane];
 
     // Scores: warp w takes positions t0 + w + 4 u, eight at a time.
@@ -128,8 +162,10 @@ __global__ void __launch_bounds__(128, 4) attend_split_kernel(FkAttend a) {
       }
 #pragma unroll
       for (int u = 0; u < B; ++u) {
-        const float sc = __fmul_rn(warp_sum(__fadd_rn(0.0f, pack_dot(qv, kv[u]))), a.scale);
         const uint32_t tt = t + u * kAttWarps;
+        float4 kk = kv[u];
+        if (fresh && tt < t1 && tt % a.length == pslot) kk = reinterpret_cast<const float4*>(krot)[lane];
+        const float sc = __fmul_rn(warp_sum(__fadd_rn(0.0f, pack_dot(qv, kk))), a.scale);
         if (lane == 0 && tt < t1) scores[tt - t0] = sc;
       }
     }
@@ -157,11 +193,13 @@ __global__ void __launch_bounds__(128, 4) attend_split_kernel(FkAttend a) {
         const uint32_t tt = t + u * kAttWarps;
         const float e = __shfl_sync(0xffffffffu, e_lane, warp + u * kAttWarps);
         if (tt < t1) {
+          float4 v4 = vv[u];
+          if (fresh && tt % a.length == pslot) v4 = reinterpret_cast<const float4*>(vnew)[lane];
           l = __fadd_rn(l, e);
-          acc.x = __fadd_rn(acc.x, __fmul_rn(e, vv[u].x));
-          acc.y = __fadd_rn(acc.y, __fmul_rn(e, vv[u].y));
-          acc.z = __fadd_rn(acc.z, __fmul_rn(e, vv[u].z));
-          acc.w = __fadd_rn(acc.w, __fmul_rn(e, vv[u].w));
+          acc.x = __fadd_rn(acc.x, __fmul_rn(e, v4.x));
+          acc.y = __fadd_rn(acc.y, __fmul_rn(e, v4.y));
+          acc.z = __fadd_rn(acc.z, __fmul_rn(e, v4.z));
+          acc.w = __fadd_rn(acc.w, __fmul_rn(e, v4.w));
         }
       }
     }
@@ -182,6 +220,7 @@ __global__ void __launch_bounds__(128, 4) attend_split_kernel(FkAttend a) {
       a.part_l[at] = lt;
       a.part_m[at] = mx;
     }
+
   }
 }
 
@@ -235,31 +274,45 @@ cudaError_t fk_launch_kv_store(const FkKvStore& a, cudaStream_t s) {
   return fk_launch_ex(fk::kv_store_kernel, dim3(a.kv_heads, a.m), dim3(a.d / 2), 0, s, a.pdl, a);
 }
 
-cudaError_t fk_launch_attend(const FkAttend& a, cudaStream_t s) {
+namespace {
+template <bool FUSED>
+cudaError_t launch_attend(const FkAttendDecode& f, cudaStream_t s) {
+  const FkAttend& a = f.a;
   if (a.m == 0) return cudaSuccess;
-  if (a.d != fk::kHeadDim || a.chunk == 0 || a.chunk > fk::kMaxChunk || a.heads % a.kv_heads != 0 ||
-      a.m > fk::kMaxAttendRows || (uint64_t)a.m * a.heads * a.max_splits >= (1ull << 32))
+  if (a.d != fk::kHeadDim || a.chunk == 0 || a.chunk > fk::kMaxChunk || a.kv_heads == 0 ||
+      a.heads % a.kv_heads != 0 || a.m > fk::kMaxAttendRows || (uint64_t)a.m * a.heads * a.max_splits >= (1ull << 32))
     return cudaErrorInvalidValue;
+  if (FUSED && (!f.kc_w || !f.vc_w)) return cudaErrorInvalidValue;
   // Blocks for the most items a step can have, as many as are resident at
   // once; each loops over its items.
+  auto kern = fk::attend_kernel<FUSED>;
   int dev = 0, sms = 148, per_sm = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const size_t smem = ((size_t)a.m + 1) * sizeof(uint32_t);
   static size_t configured = 0;
   if (smem > 48 * 1024 && smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(fk::attend_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     configured = smem;
   }
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fk::attend_split_kernel, 128, smem);
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, smem);
   if (e != cudaSuccess) return e;
   if (per_sm < 1) return cudaErrorInvalidConfiguration;
   const uint64_t most = (uint64_t)a.m * a.heads * a.max_splits;
   const uint64_t resident = (uint64_t)sms * per_sm;
   const uint32_t blocks = (uint32_t)(most < resident ? most : resident);
-  return fk_launch_ex(fk::attend_split_kernel, dim3(blocks), dim3(128), smem, s, a.pdl, a);
+  return fk_launch_ex(kern, dim3(blocks), dim3(128), smem, s, a.pdl, f);
 }
+}  // namespace
+
+cudaError_t fk_launch_attend(const FkAttend& a, cudaStream_t s) {
+  FkAttendDecode f = {};
+  f.a = a;
+  return launch_attend<false>(f, s);
+}
+
+cudaError_t fk_launch_attend_decode(const FkAttendDecode& f, cudaStream_t s) { return launch_attend<true>(f, s); }
 
 cudaError_t fk_launch_combine(const FkCombine& a, cudaStream_t s) {
   if (a.m == 0) return cudaSuccess;

@@ -458,6 +458,27 @@ int l_attend(fkc_ctx* c, const Params& p, void* const* bufs) {
   return launched(fk_launch_attend(a, c->stream), "attend_split");
 }
 
+// attend_decode: qkv cos sin pos slot k_cache v_cache part_m part_l part_acc
+//   | m heads kv_heads d length rotated chunk max_splits ldq q_off k_off v_off scale
+// The KV store and attention steps of a decode step whose rows sit in
+// distinct slots, in one launch (attend_combine follows).
+int l_attend_decode(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkAttendDecode f = {};
+  FkAttend& a = f.a;
+  a.qkv = CF(0), a.cos_t = CF(1), a.sin_t = CF(2), a.pos = CU(3), a.slot = CU(4), a.kc = CF(5), a.vc = CF(6);
+  a.part_m = F(7), a.part_l = F(8), a.part_acc = F(9);
+  f.kc_w = F(5), f.vc_w = F(6);
+  a.m = p.u(0), a.heads = p.u(1), a.kv_heads = p.u(2), a.d = p.u(3), a.length = p.u(4), a.rotated = p.u(5);
+  a.chunk = p.u(6), a.max_splits = p.u(7), a.ldq = p.u(8), a.q_off = p.u(9);
+  f.k_off = p.u(10), f.v_off = p.u(11);
+  a.scale = p.f(12);
+  a.pdl = c->pdl;
+  if (a.kv_heads == 0 || a.heads % a.kv_heads != 0)
+    return fail(FKC_ERR_ARGUMENT, "attend_decode: %u heads do not share %u KV heads in groups.", a.heads, a.kv_heads);
+  if (a.rotated > a.d / 2) return fail(FKC_ERR_ARGUMENT, "attend_decode: rotated %u is more than d/2.", a.rotated);
+  return launched(fk_launch_attend_decode(f, c->stream), "attend_decode");
+}
+
 // attend_combine: part_m part_l part_acc pos out | m heads d chunk max_splits ldo
 int l_combine(fkc_ctx* c, const Params& p, void* const* bufs) {
   FkCombine a = {};
@@ -676,6 +697,22 @@ std::vector<KernelSpec> make_table() {
                 dim("length", 1, kMax), u32("rotated"), dim("chunk", 1, 256), dim("max_splits", 1, 65535), u32("ldq"),
                 u32("q_off"), f32("scale")},
                l_attend});
+  t.push_back({"attend_decode",
+               128,
+               {{"qkv", "read", "f32"},
+                {"cos", "read", "f32"},
+                {"sin", "read", "f32"},
+                {"pos", "read", "u32"},
+                {"slot", "read", "u32"},
+                {"k_cache", "read_write", "f32"},
+                {"v_cache", "read_write", "f32"},
+                {"part_m", "write", "f32"},
+                {"part_l", "write", "f32"},
+                {"part_acc", "write", "f32"}},
+               {dim("m", 1, 64), dim("heads", 1, 1024), dim("kv_heads", 1, 1024), dim("d", 128, 128),
+                dim("length", 1, kMax), u32("rotated"), dim("chunk", 1, 256), dim("max_splits", 1, 65535), u32("ldq"),
+                u32("q_off"), u32("k_off"), u32("v_off"), f32("scale")},
+               l_attend_decode});
   t.push_back({"attend_combine",
                128,
                {{"part_m", "read", "f32"},

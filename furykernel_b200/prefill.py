@@ -105,6 +105,16 @@ class Prefill:
             by.setdefault(L.kernel, []).append(L)
         g0 = by["gather"][0]
         out = [Launch("gather", dict(g0.params, m=m), [g0.bufs[0], tok, self.x.ptr])]
+        if "attend_decode" in by:  # the decode step fused them: split its launches back into the two steps
+            for L in by["attend_decode"]:
+                p = L.params
+                by.setdefault("kv_store_ring", []).append(Launch("kv_store_ring", {
+                    "m": p["m"], "kv_heads": p["kv_heads"], "d": p["d"], "length": p["length"],
+                    "rotated": p["rotated"], "ldq": p["ldq"], "k_off": p["k_off"], "v_off": p["v_off"]},
+                    L.bufs[:7]))
+                by.setdefault("attend_split", []).append(Launch("attend_split", {
+                    k: p[k] for k in ("m", "heads", "kv_heads", "d", "length", "rotated", "chunk", "max_splits",
+                                      "ldq", "q_off", "scale")}, L.bufs[:10]))
         eps = None
         for L in eng.launches:
             if L.kernel.startswith("gemv") and "eps" in L.params:

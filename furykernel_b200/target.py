@@ -122,6 +122,13 @@ SPEC_KERNELS = {
                   [_dim("m", 1, 16384), _dim("heads", 1, 1024), _dim("kv_heads", 1, 1024), _dim("d", 128, 128),
                    _dim("length", 1, _MAX), _u("rotated"), _dim("chunk", 1, 256), _dim("max_splits", 1, 65535),
                    _u("ldq"), _u("q_off"), _f("scale")], threads=128),
+        KernelSig("attend_decode",
+                  [_f32("qkv"), _f32("cos"), _f32("sin"), _u32("pos"), _u32("slot"), _f32("k_cache", "read_write"),
+                   _f32("v_cache", "read_write"), _f32("part_m", "write"), _f32("part_l", "write"),
+                   _f32("part_acc", "write")],
+                  [_dim("m", 1, 64), _dim("heads", 1, 1024), _dim("kv_heads", 1, 1024), _dim("d", 128, 128),
+                   _dim("length", 1, _MAX), _u("rotated"), _dim("chunk", 1, 256), _dim("max_splits", 1, 65535),
+                   _u("ldq"), _u("q_off"), _u("k_off"), _u("v_off"), _f("scale")], threads=128),
         KernelSig("attend_combine",
                   [_f32("part_m"), _f32("part_l"), _f32("part_acc"), _u32("pos"), _f32("out", "write")],
                   [_dim("m", 1, 65535), _dim("heads", 1, 1024), _dim("d", 1, 1024), _dim("chunk", 1, 256),

@@ -28,12 +28,14 @@ def small_shape(batch, layers=2, d=512, heads=4, ffn=1024, vocab=3000, length=96
                       slots=batch, length=length, positions=length)
 
 
-@pytest.mark.parametrize("batch,graph", [(1, True), (3, True), (2, False), (5, True), (9, True), (20, False)])
-def test_small_model_decode_step(ctx, batch, graph):
+@pytest.mark.parametrize("batch,graph,fused", [(1, True, True), (3, True, True), (2, False, True), (5, True, True),
+                                               (9, True, True), (20, False, True), (3, True, False),
+                                               (9, False, False)])
+def test_small_model_decode_step(ctx, batch, graph, fused):
     from furykernel_b200.engine import Llama
 
     s = small_shape(batch)
-    eng = Llama(ctx, s, batch, seed=100 + batch, chunk=32, prefill_kv=1.0)
+    eng = Llama(ctx, s, batch, seed=100 + batch, chunk=32, prefill_kv=1.0, fuse_attention=fused)
     tokens = O.ints(5 + batch, batch, s.vocab)
     pos = np.array([40, 95, 7][:batch] if batch <= 3 else (np.arange(batch) * 37 + 5) % 96, np.uint32)
     slot = np.arange(batch, dtype=np.uint32)[::-1].copy()
@@ -62,7 +64,9 @@ def test_small_model_decode_step(ctx, batch, graph):
     rel = float(np.max(np.abs(logits - ref[0])) / np.max(np.abs(ref[0])))
     assert rel <= 1e-4, rel
     assert np.array_equal(ids[decided], ref_ids[decided])
-    assert eng.launch_count() == 1 + 7 * s.layers + 2 + 1
+    # gather; per layer q/k/v, store, attend, combine, o, gate/up, down (the
+    # store and attention fused: one launch fewer); head, argmax; advance.
+    assert eng.launch_count() == 1 + (6 if fused else 7) * s.layers + 2 + 1
 
 
 def test_repeated_steps_advance_the_cache(ctx):

@@ -267,6 +267,21 @@ def test_attention_path(ctx, m, heads, kv_heads, length, positions, chunk):
                        np.float32(1.0 / math.sqrt(d)), chunk, 4, max_splits, THREADS)
     got = out.download()
     assert same_bits(got, want)
+    # The store and the attention as one launch (rows in distinct slots),
+    # then the combine: the same bits, the same caches.
+    dkc.upload(kc)
+    dvc.upload(vc)
+    out2 = ctx.empty((m, heads * d))
+    ctx.launch("attend_decode", {"m": m, "heads": heads, "kv_heads": kv_heads, "d": d, "length": length,
+                                 "rotated": d // 2, "chunk": chunk, "max_splits": max_splits, "ldq": width,
+                                 "q_off": 0, "k_off": heads * d, "v_off": (heads + kv_heads) * d,
+                                 "scale": 1.0 / math.sqrt(d)},
+               [dq, dcos, dsin, dpos, dslot, dkc, dvc, pm, pl, pa])
+    ctx.launch("attend_combine", {"m": m, "heads": heads, "d": d, "chunk": chunk, "max_splits": max_splits,
+                                  "ldo": heads * d}, [pm, pl, pa, dpos, out2])
+    assert same_bits(out2.download(), want)
+    assert same_bits(dkc.download(), kcache) and same_bits(dvc.download(), vcache)
+    out2.free()
     # The referee: attention over the caches as the kernels left them
     # (evaluateStored), positions <= pos; rows never wrap past `length` here
     # except the wrapping case, which reads the ring as stored.
