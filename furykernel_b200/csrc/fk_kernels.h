@@ -9,8 +9,9 @@ enum { FK_PRO_NONE = 0, FK_PRO_RMSNORM = 1, FK_PRO_SILU = 2, FK_PRO_REDUCE_RMSNO
 
 // Tensor-parallel exchange over NVLink peer memory. Every rank owns one
 // region, mapped into every other rank's process; by byte offset:
-//   0    u32 flags[FK_XBUFS][FK_MAX_PEERS]  the epoch rank q last signalled into this region, by buffer
-//   128  u32 epoch[FK_XBUFS]                this rank's own signals so far, by buffer
+//   0    u32 flags[FK_XBUFS][FK_MAX_PEERS]  buffers 0, 1: the rows rank q has written here, all uses;
+//                                            buffer 2: the epoch rank q last signalled into this region
+//   128  u32 epoch[FK_XBUFS]                this rank's uses of each buffer so far
 //   160  u32 counter[FK_XBUFS]              blocks of the running producer that have finished
 //   256  f32 data[FK_XBUFS][FK_MAX_PEERS][FK_XSLOT]  rank q's partial rows, by buffer
 // Buffers: 0 the attention output projection's partials, 1 the down

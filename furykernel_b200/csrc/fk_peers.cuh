@@ -1,8 +1,11 @@
 // Device side of the tensor-parallel exchange (the region layout is in
-// fk_kernels.h): a producer grid writes its partial rows into every rank's
-// region, then its last block releases the buffer's next epoch into every
-// rank's flags; a consumer waits, with a bound, until every rank's flag in
-// its own region has reached its own epoch, then reads the partials locally.
+// fk_kernels.h). Buffers 0 and 1 (the row-parallel partials) use counted
+// rows: producer blocks write their rows into every rank's region and add
+// the rows to that rank's count for them, a consumer waits until every
+// rank's count reaches the rows of all uses so far. Buffer 2 (the greedy
+// candidates) uses epochs: the producer's last block releases the buffer's
+// next epoch into every rank's flags, a consumer waits for its own epoch.
+// Every wait is bounded and records why it gave up.
 #pragma once
 
 #include "fk_common.cuh"
@@ -56,42 +59,54 @@ __device__ __forceinline__ void peers_signal(const FkPeers& P, uint32_t buf, boo
   }
 }
 
-// The producer's broadcast of a partial it has written into its own slot
-// of its own region (m_n floats, 16-byte aligned): every block of the grid
-// calls this once its part of the slot is written. Blocks fence at GPU
-// scope and count themselves in; the last one in copies the whole slot
-// into this rank's slot of every other rank's region with 128-bit stores,
-// fences at system scope and releases the buffer's next epoch into every
-// rank's flags. One block, not every writer, pays for system scope.
-__device__ __forceinline__ void peers_broadcast(const FkPeers& P, uint32_t buf, uint32_t count, bool wrote) {
-  __shared__ uint32_t last;
-  if (wrote) __threadfence();
+// The counted exchange of the row-parallel partials (buffers 0 and 1): a
+// buffer's flag word for rank q counts the rows rank q has written into its
+// slot of this region, all uses of the buffer together (u32, compared
+// modulo 2^32). Every producer block writes its run of rows straight into
+// every rank's slot, then its threads q < world add the run's length to rank
+// q's count with one release add each -- in parallel, after the block's
+// barrier (which the release makes cumulative over the block's stores); no
+// block waits for another. The last block to finish bumps this rank's use
+// count of the buffer (local), which the consumer multiplies by the rows a
+// use brings.
+__device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void peers_count_rows(const FkPeers& P, uint32_t buf, uint32_t rows) {
   __syncthreads();
-  char* me = P.base[P.rank];
-  if (threadIdx.x == 0) last = atomicAdd(xcounter(me) + buf, 1u) == gridDim.x - 1;
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  const float4* src = reinterpret_cast<const float4*>(xdata(me, buf, P.rank));
-  const uint32_t n4 = (count + 3) / 4;
-  for (uint32_t q = 0; q < P.world; ++q) {
-    if (q == P.rank) continue;
-    float4* dst = reinterpret_cast<float4*>(xdata(P.base[q], buf, P.rank));
-    for (uint32_t i = threadIdx.x; i < n4; i += blockDim.x) dst[i] = __ldcg(src + i);
-  }
-  fence_acq_rel_sys();
-  __syncthreads();
-  // Thread q stores rank q's flag: one fence above, no fence a flag.
-  const uint32_t e = xepoch(me)[buf] + 1;
-  if (threadIdx.x < P.world) {
-    fence_acq_rel_sys();  // orders the block's copies (seen through the barrier) before the flag
-    st_relaxed_sys(xflags(P.base[threadIdx.x]) + buf * FK_MAX_PEERS + P.rank, e);
-  }
-  __syncthreads();
+  if (threadIdx.x < P.world) red_release_sys_add(xflags(P.base[threadIdx.x]) + buf * FK_MAX_PEERS + P.rank, rows);
   if (threadIdx.x == 0) {
-    xcounter(me)[buf] = 0;
-    xepoch(me)[buf] = e;
+    char* me = P.base[P.rank];
+    if (atomicAdd(xcounter(me) + buf, 1u) == gridDim.x - 1) {
+      xcounter(me)[buf] = 0;
+      xepoch(me)[buf] += 1;
+    }
   }
+}
+
+// The consumer side: thread 0 waits, with a bound, until every rank's count
+// has reached (uses so far) x (rows a use). False when one did not come
+// within the bound (recorded in *err as 10 + buf).
+__device__ __forceinline__ bool peers_wait_rows(const FkPeers& P, uint32_t buf, uint32_t rows, int* err) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    char* me = P.base[P.rank];
+    const uint32_t target = *reinterpret_cast<volatile uint32_t*>(xepoch(me) + buf) * rows;
+    ok = 1;
+    for (uint32_t q = 0; q < P.world && ok; ++q) {
+      const long long t0 = clock64();
+      while ((int32_t)(ld_acquire_sys(xflags(me) + buf * FK_MAX_PEERS + q) - target) < 0) {
+        if (clock64() - t0 > kPeerWaitCycles) {
+          if (err) atomicCAS(err, 0, 10 + (int)buf);
+          ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  return ok != 0;
 }
 
 // Every thread of a consumer block calls this; thread 0 waits. False when

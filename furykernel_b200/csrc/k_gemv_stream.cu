@@ -22,10 +22,10 @@
 //
 // Tensor parallelism (fk_peers.cuh): the row-parallel projections scatter
 // their partial rows into every rank's exchange region (SEPI_SCATTER: a
-// block owns a contiguous run of rows, stages them in shared memory and
-// writes them into this rank's own slot; the grid's last block copies the
-// slot to every other rank with 128-bit stores and releases it); the
-// next GEMV's prologue (SPRO_REDUCE_RMSNORM) waits for every rank's partial,
+// block owns a contiguous run of rows, stages them in shared memory, writes
+// the run into this rank's slot of every region and counts its rows in with
+// a release add a rank); the
+// next GEMV's prologue (SPRO_REDUCE_RMSNORM) waits for every rank's rows,
 // forms the residual row x_new = r + (((P_0 + P_1) + P_2) + ...), ranks in
 // order, so that every rank holds the same bits, stores it (block 0), and
 // normalizes it as SPRO_RMSNORM does.
@@ -122,7 +122,7 @@ __global__ void __launch_bounds__(512, 2) gemv_stream_kernel(StreamArgs a) {
   grid_launch_dependents();
 
   constexpr bool NORM = PRO == SPRO_RMSNORM || PRO == SPRO_REDUCE_RMSNORM;
-  if (PRO == SPRO_REDUCE_RMSNORM) peers_wait(a.peers, a.xbuf, a.err);
+  if (PRO == SPRO_REDUCE_RMSNORM) peers_wait_rows(a.peers, a.xbuf, a.k, a.err);
   // Stage x: as given, the SiLU-gate of a gate/up row, or the residual plus
   // every rank's partial, in rank order.
   for (uint32_t idx = threadIdx.x; idx < a.m * packs; idx += blockDim.x) {
@@ -217,16 +217,18 @@ __global__ void __launch_bounds__(512, 2) gemv_stream_kernel(StreamArgs a) {
     }
   }
   if (EPI == SEPI_SCATTER) {
-    // This rank's partial rows [s_lo, s_hi) into its own slot of its own
-    // region; the last block broadcasts the slot to every rank.
+    // This rank's partial rows [s_lo, s_hi) into its slot of every rank's
+    // region (contiguous runs), counted in (fk_peers.cuh).
     __syncthreads();
     const uint32_t cnt = s_hi - s_lo;
-    float* dst = xdata(a.peers.base[a.peers.rank], a.xbuf, a.peers.rank);
-    for (uint32_t idx = threadIdx.x; idx < a.m * cnt; idx += blockDim.x) {
-      const uint32_t i = idx / cnt, j = idx - i * cnt;
-      dst[(size_t)i * a.n + s_lo + j] = outs[i][j];
+    for (uint32_t q = 0; q < a.peers.world; ++q) {
+      float* dst = xdata(a.peers.base[q], a.xbuf, a.peers.rank);
+      for (uint32_t idx = threadIdx.x; idx < a.m * cnt; idx += blockDim.x) {
+        const uint32_t i = idx / cnt, j = idx - i * cnt;
+        dst[(size_t)i * a.n + s_lo + j] = outs[i][j];
+      }
     }
-    peers_broadcast(a.peers, a.xbuf, a.m * a.n, threadIdx.x < a.m * cnt);
+    peers_count_rows(a.peers, a.xbuf, cnt);
   }
 }
 
