@@ -196,8 +196,11 @@ def prompt_prefill(ctx, eng, b: int, local: int):
     R = min(len(toks), 2048)
     pre = Prefill(eng, rows=R, positions=PROMPT)
     chunks = [(i, min(R, len(toks) - i)) for i in range(0, len(toks), R)]
-    for i, m in chunks:  # capture first: the timed region replays graphs
-        pre.graph(m)
+    # Capture, then one untimed pass (a graph's first replay uploads it, and
+    # NCCL's first captured collectives set up): prefill writes the same
+    # keys and values again in the timed pass.
+    for i, m in chunks:
+        pre.run(toks[i:i + m], poss[i:i + m], sl[i:i + m])
     ctx.sync()
     torch.cuda.set_device(local)
     stream = torch.cuda.ExternalStream(ctx.stream())

@@ -50,26 +50,29 @@ __global__ void __launch_bounds__(256) reduce_final_kernel(const float* __restri
                                                            uint32_t count, float* __restrict__ chains,
                                                            unsigned int* __restrict__ done,
                                                            float* __restrict__ y) {
-  // Block b computes chains [32 b, 32 b + 32): thread t takes chain 32 b + (t & 31)
-  // over the terms k = t >> 5, t >> 5 + 8, ... of that chain, staged in smem
-  // so that the chain's additions run in order.
-  __shared__ float terms[8][32];
+  // Block b computes chains [32 b, 32 b + 32). The chains' terms come in
+  // 64 at a time (warp w loads terms k0 + w + 8 i, i < 8, all in flight),
+  // staged in shared memory; warp 0's lane l then adds chain 32 b + l's 64
+  // terms in order.
+  constexpr int kRows = 64;
+  __shared__ float terms[kRows][32];
   __shared__ bool last;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t chain = blockIdx.x * 32 + lane;
   float acc = -0.0f;
   const uint32_t per_chain = (count + 255) / 256;
-  for (uint32_t k0 = 0; k0 < per_chain; k0 += 8) {
-    uint32_t k = k0 + warp;
-    uint32_t at = chain + 256 * k;
-    terms[warp][lane] = (k < per_chain && at < count) ? partials[at] : 0.0f;
+  for (uint32_t k0 = 0; k0 < per_chain; k0 += kRows) {
+#pragma unroll
+    for (int i = 0; i < kRows / 8; ++i) {
+      const uint32_t k = k0 + warp + 8 * i;
+      const uint32_t at = chain + 256 * k;
+      terms[warp + 8 * i][lane] = (k < per_chain && at < count) ? __ldcg(partials + at) : 0.0f;
+    }
     __syncthreads();
     if (warp == 0) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        uint32_t kk = k0 + j;
-        if (kk < per_chain && chain + 256 * kk < count) acc = __fadd_rn(acc, terms[j][lane]);
-      }
+      const uint32_t rows = min((uint32_t)kRows, per_chain - k0);
+      for (uint32_t j = 0; j < rows; ++j)
+        if (chain + 256 * (k0 + j) < count) acc = __fadd_rn(acc, terms[j][lane]);
     }
     __syncthreads();
   }
