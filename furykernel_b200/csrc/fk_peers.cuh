@@ -22,9 +22,6 @@ __device__ __forceinline__ float* xdata(char* base, uint32_t buf, uint32_t src) 
   return reinterpret_cast<float*>(base + 256) + ((size_t)buf * FK_MAX_PEERS + src) * FK_XSLOT;
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 
 // A flag store after the caller's own system-scope fence: relaxed, so that
 // a thread storing to several ranks does not pay one release fence a rank.
