@@ -229,7 +229,8 @@ __global__ void __launch_bounds__(128, 4) attend_kernel(FkAttendDecode f) {
 // computed once a block, into shared memory; every thread then adds the
 // splits in order for its dimension.
 __global__ void combine_kernel(FkCombine a) {
-  extern __shared__ float wsplit[];  // [max_splits]
+  extern __shared__ float wsplit[];  // [max_splits] weights, then [max_splits] sums
+  float* lsplit = wsplit + a.max_splits;
   __shared__ float top_s;
   grid_wait();
   grid_launch_dependents();
@@ -244,14 +245,29 @@ __global__ void combine_kernel(FkCombine a) {
   }
   __syncthreads();
   const float top = top_s;
-  for (uint32_t j = threadIdx.x; j < splits; j += blockDim.x) wsplit[j] = exp_rounded(__fsub_rn(a.part_m[at + j], top));
+  for (uint32_t j = threadIdx.x; j < splits; j += blockDim.x) {
+    wsplit[j] = exp_rounded(__fsub_rn(a.part_m[at + j], top));
+    lsplit[j] = a.part_l[at + j];
+  }
   __syncthreads();
   const float w0 = wsplit[0];
-  float l = __fmul_rn(a.part_l[at], w0);
+  float l = __fmul_rn(lsplit[0], w0);
   float o = __fmul_rn(a.part_acc[at * a.d + i], w0);
-  for (uint32_t j = 1; j < splits; ++j) {
+  // The splits in order; their accumulators 8 loads at a time in flight.
+  uint32_t j = 1;
+  for (; j + 8 <= splits; j += 8) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = a.part_acc[(at + j + u) * a.d + i];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      l = __fadd_rn(l, __fmul_rn(lsplit[j + u], wsplit[j + u]));
+      o = __fadd_rn(o, __fmul_rn(v[u], wsplit[j + u]));
+    }
+  }
+  for (; j < splits; ++j) {
     const float w = wsplit[j];
-    l = __fadd_rn(l, __fmul_rn(a.part_l[at + j], w));
+    l = __fadd_rn(l, __fmul_rn(lsplit[j], w));
     o = __fadd_rn(o, __fmul_rn(a.part_acc[(at + j) * a.d + i], w));
   }
   a.out[(size_t)r * a.ldo + (size_t)h * a.d + i] = __fdiv_rn(o, l);
@@ -316,9 +332,15 @@ cudaError_t fk_launch_attend_decode(const FkAttendDecode& f, cudaStream_t s) { r
 
 cudaError_t fk_launch_combine(const FkCombine& a, cudaStream_t s) {
   if (a.m == 0) return cudaSuccess;
-  if (a.d > 1024 || a.d < 32 || a.max_splits == 0 || a.max_splits > 12288) return cudaErrorInvalidValue;
-  return fk_launch_ex(fk::combine_kernel, dim3(a.heads, a.m), dim3(a.d), (size_t)a.max_splits * sizeof(float), s,
-                      a.pdl, a);
+  if (a.d > 1024 || a.d < 32 || a.max_splits == 0 || a.max_splits > 24576) return cudaErrorInvalidValue;
+  const size_t smem = 2 * (size_t)a.max_splits * sizeof(float);
+  static size_t configured = 0;
+  if (smem > 48 * 1024 && smem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(fk::combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = smem;
+  }
+  return fk_launch_ex(fk::combine_kernel, dim3(a.heads, a.m), dim3(a.d), smem, s, a.pdl, a);
 }
 
 cudaError_t fk_launch_rope(const float* x, uint32_t m, uint32_t heads, uint32_t d, uint32_t rotated, uint32_t ldx,
