@@ -180,6 +180,15 @@ def cpu_sample(threads: int, batch: int, w: dict, min_seconds: float = 10.0):
     return per_step, desc
 
 
+# DRAM bytes (read + write) of one launch, from ncu captures of the same
+# kernel and shape (dram__bytes_read.sum + dram__bytes_write.sum, one
+# capture each; the summaries under profiles/ give the commands).
+NCU_TRAFFIC = {
+    ("gemv_rmsnorm", 32000, 4096, 1): (524.35e6 + 3.43e6, "profiles/gemv_stream_lm_head_b1.md"),
+    ("gemv", 11008, 4096, 16): (180.90e6 + 3.87e6, "profiles/gemv_batch_b16.md"),
+}
+
+
 def prompt_prefill(ctx, eng, b: int, local: int):
     """Config 5's prompt: b prompts of PROMPT ids U[0, vocab) (numpy PCG64,
     seed 512, the same on every rank), every row but the last prefilled
@@ -360,7 +369,9 @@ def run_ours(args):
         "roofline": {"kernel": "%s %d x %d (the largest weight stream of a step, one launch, batch %d)"
                                % (L.kernel, p["n"], p["k"], b), "bound": "hbm",
                      "achieved": k_gbs, "peak": hbm_peak, "unit": "GB/s", "frac": k_gbs / hbm_peak,
-                     "traffic": None, "algorithmic_bytes": k_bytes, "launch_ms": k_ms, "peak_kind": peak_kind},
+                     "traffic": NCU_TRAFFIC.get((L.kernel, p["n"], p["k"], p["m"]), (None,))[0],
+                     "traffic_source": NCU_TRAFFIC.get((L.kernel, p["n"], p["k"], p["m"]), (None, None))[1],
+                     "algorithmic_bytes": k_bytes, "launch_ms": k_ms, "peak_kind": peak_kind},
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": int(host_in.nbytes),
                 "d2h_bytes_per_step": int(host_out.nbytes)},
         "gpu_launches": eng.launch_count() * args.steps,
@@ -574,7 +585,8 @@ def run_kernel_config(args):
             "vs_baseline": None, "dtype": "f32", "data": "synthetic, seeded on the device",
             "config": {"workload": workload},
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
-                         "traffic": None, "algorithmic_bytes": nbytes, "peak_kind": kind}}
+                         "traffic": NCU_TRAFFIC[("gemv", 11008, 4096, 16)][0] if cfg == "3b" else None,
+                         "algorithmic_bytes": nbytes, "peak_kind": kind}}
     if cpu_ms is not None:
         line["cpu_baseline"] = {"value": 1e3 / cpu_ms, "unit": unit_label, "cores": 1, "kind": "port",
                                 "sample": cpu_sample_text, "ms": cpu_ms}
