@@ -197,14 +197,14 @@ def prompt_prefill(ctx, eng, b: int, local: int):
     import numpy as np
     import torch
 
-    from furykernel_b200.prefill import Prefill, prompt_rows
+    from furykernel_b200.prefill import Prefill, prompt_chunks, prompt_rows
 
     prompts = np.random.default_rng(512).integers(0, eng.full.vocab, size=(b, PROMPT), dtype=np.uint32)
     slots = np.arange(b, dtype=np.uint32)
     toks, poss, sl = prompt_rows(prompts, slots)
-    R = min(len(toks), 2048)
-    pre = Prefill(eng, rows=R, positions=PROMPT)
-    chunks = [(i, min(R, len(toks) - i)) for i in range(0, len(toks), R)]
+    R = PROMPT - 1  # one prompt a run: the query-tiled prompt attention
+    pre = Prefill(eng, rows=R, positions=PROMPT, one_slot=True)
+    chunks = prompt_chunks(pre, toks, poss, sl)
     # Capture, then one untimed pass (a graph's first replay uploads it, and
     # NCCL's first captured collectives set up): prefill writes the same
     # keys and values again in the timed pass.

@@ -111,6 +111,7 @@ cudaError_t fk_launch_gemv_batch(const FkGemv& g, int sms, cudaStream_t s);
 cudaError_t fk_launch_kv_store(const FkKvStore& a, cudaStream_t s);
 cudaError_t fk_launch_attend(const FkAttend& a, cudaStream_t s);
 cudaError_t fk_launch_attend_decode(const FkAttendDecode& f, cudaStream_t s);
+cudaError_t fk_launch_attend_prompt(const FkAttend& a, float* out, uint32_t ldo, uint32_t max_pos, cudaStream_t s);
 cudaError_t fk_launch_combine(const FkCombine& a, cudaStream_t s);
 cudaError_t fk_launch_gather(const float* table, uint32_t width, const uint32_t* tokens, uint32_t m, float factor,
                              float* y, bool pdl, cudaStream_t s);

@@ -479,6 +479,24 @@ int l_attend_decode(fkc_ctx* c, const Params& p, void* const* bufs) {
   return launched(fk_launch_attend_decode(f, c->stream), "attend_decode");
 }
 
+// attend_prompt: qkv cos sin pos slot k_cache v_cache out
+//   | m heads kv_heads d length rotated ldq q_off ldo max_pos scale
+// A prompt's rows in one slot (slot[0]), positions <= max_pos < length.
+int l_attend_prompt(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkAttend a = {};
+  a.qkv = CF(0), a.cos_t = CF(1), a.sin_t = CF(2), a.pos = CU(3), a.slot = CU(4), a.kc = CF(5), a.vc = CF(6);
+  a.m = p.u(0), a.heads = p.u(1), a.kv_heads = p.u(2), a.d = p.u(3), a.length = p.u(4), a.rotated = p.u(5);
+  a.ldq = p.u(6), a.q_off = p.u(7);
+  a.scale = p.f(10);
+  a.pdl = c->pdl;
+  if (a.kv_heads == 0 || a.heads % a.kv_heads != 0)
+    return fail(FKC_ERR_ARGUMENT, "attend_prompt: %u heads do not share %u KV heads in groups.", a.heads, a.kv_heads);
+  if (a.rotated > a.d / 2) return fail(FKC_ERR_ARGUMENT, "attend_prompt: rotated %u is more than d/2.", a.rotated);
+  if (p.u(9) >= a.length)
+    return fail(FKC_ERR_ARGUMENT, "attend_prompt: max_pos %u is not within the ring's length %u.", p.u(9), a.length);
+  return launched(fk_launch_attend_prompt(a, F(7), p.u(8), p.u(9), c->stream), "attend_prompt");
+}
+
 // attend_combine: part_m part_l part_acc pos out | m heads d chunk max_splits ldo
 int l_combine(fkc_ctx* c, const Params& p, void* const* bufs) {
   FkCombine a = {};
@@ -713,6 +731,20 @@ std::vector<KernelSpec> make_table() {
                 dim("length", 1, kMax), u32("rotated"), dim("chunk", 1, 256), dim("max_splits", 1, 65535), u32("ldq"),
                 u32("q_off"), u32("k_off"), u32("v_off"), f32("scale")},
                l_attend_decode});
+  t.push_back({"attend_prompt",
+               128,
+               {{"qkv", "read", "f32"},
+                {"cos", "read", "f32"},
+                {"sin", "read", "f32"},
+                {"pos", "read", "u32"},
+                {"slot", "read", "u32"},
+                {"k_cache", "read", "f32"},
+                {"v_cache", "read", "f32"},
+                {"out", "write", "f32"}},
+               {dim("m", 1, 65535), dim("heads", 1, 1024), dim("kv_heads", 1, 1024), dim("d", 128, 128),
+                dim("length", 1, kMax), u32("rotated"), u32("ldq"), u32("q_off"), u32("ldo"), dim("max_pos", 0, 1407),
+                f32("scale")},
+               l_attend_prompt});
   t.push_back({"attend_combine",
                128,
                {{"part_m", "read", "f32"},

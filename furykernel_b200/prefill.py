@@ -41,7 +41,8 @@ class Prefill:
     rank). `run(tokens, positions, slots)` stores the rows' keys and values
     and leaves the last layer's rows in `x`."""
 
-    def __init__(self, eng: Llama, rows: int, chunk: int | None = None, positions: int | None = None):
+    def __init__(self, eng: Llama, rows: int, chunk: int | None = None, positions: int | None = None,
+                 one_slot: bool = False):
         ctx, s = eng.ctx, eng.s
         self.eng, self.ctx, self.R = eng, ctx, rows
         d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
@@ -75,6 +76,10 @@ class Prefill:
         # prefill here stores (the engine's positions unless given).
         self.positions = positions or s.positions
         self.max_splits = (self.positions + self.chunk - 1) // self.chunk
+        # One prompt (one slot) a run: the attention tiled by queries
+        # (attend_prompt), keys shared by 32 rows, instead of the decode
+        # attention over every row.
+        self.one_slot = one_slot and self.positions <= min(s.length, 1408)
         ms = R * s.heads * self.max_splits
         self.part = [ctx.zeros(ms), ctx.zeros(ms), ctx.zeros(ms * s.head_dim)]
         self.graphs: dict = {}
@@ -129,13 +134,21 @@ class Prefill:
             out.append(self._gemm(self.a.ptr, d, w["q_proj"], nq, self.qkv.ptr, nq))
             out.append(Launch("kv_store_ring", dict(kv.params, m=m, ldq=nq),
                               [self.qkv.ptr, kv.bufs[1], kv.bufs[2], pos, slot, kv.bufs[5], kv.bufs[6]]))
-            out.append(Launch("attend_split", dict(at.params, m=m, ldq=nq, chunk=self.chunk,
-                                                   max_splits=self.max_splits),
-                              [self.qkv.ptr, at.bufs[1], at.bufs[2], pos, slot, at.bufs[5], at.bufs[6],
-                               self.part[0].ptr, self.part[1].ptr, self.part[2].ptr]))
-            out.append(Launch("attend_combine", dict(cb.params, m=m, chunk=self.chunk, max_splits=self.max_splits,
-                                                     ldo=qw),
-                              [self.part[0].ptr, self.part[1].ptr, self.part[2].ptr, pos, self.att.ptr]))
+            if self.one_slot:
+                ap = at.params
+                out.append(Launch("attend_prompt", {
+                    "m": m, "heads": ap["heads"], "kv_heads": ap["kv_heads"], "d": ap["d"], "length": ap["length"],
+                    "rotated": ap["rotated"], "ldq": nq, "q_off": ap["q_off"], "ldo": qw,
+                    "max_pos": self.positions - 1, "scale": ap["scale"]},
+                    [self.qkv.ptr, at.bufs[1], at.bufs[2], pos, slot, at.bufs[5], at.bufs[6], self.att.ptr]))
+            else:
+                out.append(Launch("attend_split", dict(at.params, m=m, ldq=nq, chunk=self.chunk,
+                                                       max_splits=self.max_splits),
+                                  [self.qkv.ptr, at.bufs[1], at.bufs[2], pos, slot, at.bufs[5], at.bufs[6],
+                                   self.part[0].ptr, self.part[1].ptr, self.part[2].ptr]))
+                out.append(Launch("attend_combine", dict(cb.params, m=m, chunk=self.chunk,
+                                                         max_splits=self.max_splits, ldo=qw),
+                                  [self.part[0].ptr, self.part[1].ptr, self.part[2].ptr, pos, self.att.ptr]))
             out.append(self._gemm(self.att.ptr, qw, w["o_proj"], d, self.tmp.ptr, d))
             if eng.world > 1:
                 out.append(Launch("__allreduce__", {"count": m * d}, [self.tmp.ptr]))
@@ -164,6 +177,8 @@ class Prefill:
         if m and int(np.max(positions)) >= self.positions:
             raise N.Refused(N.FKC_ERR_ARGUMENT,
                             f"prefill: position {int(np.max(positions))} is past the {self.positions} it was sized for.")
+        if self.one_slot and m and len(np.unique(np.asarray(slots))) != 1:
+            raise N.Refused(N.FKC_ERR_ARGUMENT, "prefill: a one-slot prefill's rows sit in more than one slot.")
         host = np.zeros(3 * self.rs, np.uint32)
         host[:m] = tokens
         host[self.rs:self.rs + m] = np.asarray(positions, np.uint32)
@@ -214,12 +229,25 @@ def prompt_rows(prompts, slots):
     return toks, poss, sl
 
 
+def prompt_chunks(pre: Prefill, toks, poss, sl) -> list:
+    """The (start, rows) runs a prefill takes the rows in: R at a time, and
+    for a one-slot prefill never across a slot."""
+    out, i = [], 0
+    while i < len(toks):
+        j = min(i + pre.R, len(toks))
+        if pre.one_slot:
+            j = i + int(np.argmax(np.append(sl[i:j] != sl[i], True)))
+        out.append((i, j - i))
+        i = j
+    return out
+
+
 def prompt_then_decode(eng: Llama, pre: Prefill, prompts, slots) -> np.ndarray:
-    """Prefill each prompt's rows but its last into its slot (all prompts'
-    rows at once, R rows at a time), then one decode step over the batch
-    from each prompt's last token: the first generated ids."""
+    """Prefill each prompt's rows but its last into its slot (R rows at a
+    time; one prompt a run for a one-slot prefill), then one decode step over
+    the batch from each prompt's last token: the first generated ids."""
     toks, poss, sl = prompt_rows(prompts, slots)
-    for i in range(0, len(toks), pre.R):
-        pre.run(toks[i:i + pre.R], poss[i:i + pre.R], sl[i:i + pre.R])
+    for i, m in prompt_chunks(pre, toks, poss, sl):
+        pre.run(toks[i:i + m], poss[i:i + m], sl[i:i + m])
     eng.set_rows([p[-1] for p in prompts], [len(p) - 1 for p in prompts], slots)
     return eng.step()

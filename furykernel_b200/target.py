@@ -129,6 +129,12 @@ SPEC_KERNELS = {
                   [_dim("m", 1, 64), _dim("heads", 1, 1024), _dim("kv_heads", 1, 1024), _dim("d", 128, 128),
                    _dim("length", 1, _MAX), _u("rotated"), _dim("chunk", 1, 256), _dim("max_splits", 1, 65535),
                    _u("ldq"), _u("q_off"), _u("k_off"), _u("v_off"), _f("scale")], threads=128),
+        KernelSig("attend_prompt",
+                  [_f32("qkv"), _f32("cos"), _f32("sin"), _u32("pos"), _u32("slot"), _f32("k_cache"),
+                   _f32("v_cache"), _f32("out", "write")],
+                  [_dim("m", 1, 65535), _dim("heads", 1, 1024), _dim("kv_heads", 1, 1024), _dim("d", 128, 128),
+                   _dim("length", 1, _MAX), _u("rotated"), _u("ldq"), _u("q_off"), _u("ldo"),
+                   _dim("max_pos", 0, 1407), _f("scale")], threads=128),
         KernelSig("attend_combine",
                   [_f32("part_m"), _f32("part_l"), _f32("part_acc"), _u32("pos"), _f32("out", "write")],
                   [_dim("m", 1, 65535), _dim("heads", 1, 1024), _dim("d", 1, 1024), _dim("chunk", 1, 256),

@@ -44,6 +44,35 @@ def test_silu_pairs_bits(ctx):
     dy.free()
 
 
+def test_prompt_attention_within_bounds(ctx):
+    """attend_prompt (query-tiled, for prefill): 70 rows of one prompt at
+    positions 0..69 over the stored keys and values, within the f64
+    evaluator's bounds and 1e-4 normwise (its orders differ from the split
+    kernel's)."""
+    m, heads, kv_heads, length, d = 70, 4, 2, 96, 128
+    width = (heads + 2 * kv_heads) * d
+    qkv = O.normal(91, m * width).reshape(m, width)
+    pos = np.arange(m, dtype=np.uint32)
+    slot = np.full(m, 1, np.uint32)
+    kc = O.normal(92, 2 * kv_heads * length * d).reshape(2, kv_heads, length, d)
+    vc = O.normal(93, 2 * kv_heads * length * d).reshape(2, kv_heads, length, d)
+    dq, dkc, dvc, dpos, dslot = (ctx.to_device(a) for a in (qkv, kc, vc, pos, slot))
+    dcos, dsin = ctx.rope_tables(10000.0, d, d // 2, length)
+    out = ctx.empty((m, heads * d))
+    ctx.launch("attend_prompt", {"m": m, "heads": heads, "kv_heads": kv_heads, "d": d, "length": length,
+                                 "rotated": d // 2, "ldq": width, "q_off": 0, "ldo": heads * d, "max_pos": m - 1,
+                                 "scale": 1.0 / math.sqrt(d)}, [dq, dcos, dsin, dpos, dslot, dkc, dvc, out])
+    got = out.download()
+    qref = O.r_rope(O.r_input(qkv[:, :heads * d]), d, d // 2, 10000.0, pos)
+    ref = O.r_attend(qref, heads, kv_heads, d, length, pos, slot, kc.astype(np.float64), vc.astype(np.float64),
+                     1.0 / math.sqrt(d))
+    assert O.within(got, ref).all()
+    rel = float(np.max(np.abs(got - ref[0])) / np.max(np.abs(ref[0])))
+    assert rel <= 1e-4, rel
+    for b in (dq, dkc, dvc, dpos, dslot, dcos, dsin, out):
+        b.free()
+
+
 def test_attention_over_prompt_rows(ctx):
     """100 rows of one prompt in one slot, positions 0..99: every row's keys
     and values stored first, then each row over the positions <= its own."""
@@ -82,8 +111,8 @@ def test_attention_over_prompt_rows(ctx):
         b.free()
 
 
-@pytest.mark.parametrize("batch", [1, 3])
-def test_prefill_then_decode(ctx, batch):
+@pytest.mark.parametrize("batch,one_slot", [(1, False), (3, False), (1, True), (3, True)])
+def test_prefill_then_decode(ctx, batch, one_slot):
     from furykernel_b200.engine import Llama
     from furykernel_b200.prefill import Prefill
     from furykernel_b200.program.llama import LlamaShape
@@ -91,7 +120,7 @@ def test_prefill_then_decode(ctx, batch):
     s = LlamaShape(d_model=512, heads=4, kv_heads=4, head_dim=128, ffn=1024, vocab=3000, layers=2, slots=batch,
                    length=96, positions=96)
     eng = Llama(ctx, s, batch, seed=300 + batch, chunk=16)
-    pre = Prefill(eng, rows=128)
+    pre = Prefill(eng, rows=128, one_slot=one_slot)
     layers, embed, final_norm = MC.host_model(eng)
     lens = [40, 23, 31][:batch]
     prompts = [O.ints(80 + i, n, s.vocab) for i, n in enumerate(lens)]
@@ -100,7 +129,10 @@ def test_prefill_then_decode(ctx, batch):
     toks = np.concatenate([p[:-1] for p in prompts])
     poss = np.concatenate([np.arange(n - 1, dtype=np.uint32) for n in lens])
     sl = np.concatenate([np.full(n - 1, i, np.uint32) for i, n in enumerate(lens)])
-    pre.run(toks, poss, sl)
+    from furykernel_b200.prefill import prompt_chunks
+
+    for i, n in prompt_chunks(pre, toks, poss, sl):
+        pre.run(toks[i:i + n], poss[i:i + n], sl[i:i + n])
     ctx.sync()
     kc_p, vc_p = MC.host_caches(eng)
     # Prefill's stores lie within the f64 evaluator's bounds.
