@@ -539,8 +539,20 @@ class Llama:
             self.graph = g
         return self.graph
 
+    def check_rows(self, tokens, positions, slots) -> None:
+        """Refuses row inputs the kernels would index past their buffers
+        with: ids past the vocabulary, positions past the RoPE tables, slots
+        past the KV arena."""
+        s = self.s
+        for what, v, bound in (("token", tokens, self.full.vocab), ("position", positions, s.positions),
+                               ("slot", slots, s.slots)):
+            v = np.asarray(v)
+            if v.size and int(v.max()) >= bound:
+                raise N.Refused(N.FKC_ERR_ARGUMENT, f"a {what} {int(v.max())} is past the engine's {bound}.")
+
     def set_rows(self, tokens, positions, slots=None) -> None:
         slots = np.asarray(slots if slots is not None else np.arange(self.m), np.uint32)
+        self.check_rows(tokens, positions, slots)
         if self.fuse_attention and len(np.unique(slots)) != len(slots):
             raise N.Refused(N.FKC_ERR_ARGUMENT, "a decode step's rows must sit in distinct slots (the fused "
                                                 "attention stores a row's key while the others read).")

@@ -177,6 +177,7 @@ class Prefill:
         if m and int(np.max(positions)) >= self.positions:
             raise N.Refused(N.FKC_ERR_ARGUMENT,
                             f"prefill: position {int(np.max(positions))} is past the {self.positions} it was sized for.")
+        self.eng.check_rows(tokens, positions, slots)
         if self.one_slot and m and len(np.unique(np.asarray(slots))) != 1:
             raise N.Refused(N.FKC_ERR_ARGUMENT, "prefill: a one-slot prefill's rows sit in more than one slot.")
         host = np.zeros(3 * self.rs, np.uint32)

@@ -57,3 +57,18 @@ def test_prompt_chunks_respect_the_row_budget_and_slots():
     for i, m in runs:
         assert len(set(sl[i:i + m].tolist())) == 1
     assert sum(m for _, m in runs) == len(toks)
+
+
+def test_row_inputs_past_the_engine_s_tables_are_refused():
+    from furykernel_b200 import _native as N
+
+    eng = SimpleNamespace(s=SimpleNamespace(positions=64, slots=2), full=SimpleNamespace(vocab=100))
+    Llama.check_rows(eng, [1, 99], [0, 63], [0, 1])
+    for tokens, pos, slots, what in (([100], [0], [0], "token 100"), ([1], [64], [0], "position 64"),
+                                     ([1], [0], [2], "slot 2")):
+        try:
+            Llama.check_rows(eng, tokens, pos, slots)
+        except N.Refused as e:
+            assert what in str(e)
+        else:
+            raise AssertionError(what)
