@@ -298,6 +298,66 @@ void fko_gemv(const float *w, uint32_t n, uint32_t k, const float *x, uint32_t m
 }
 
 /* ------------------------------------------------------------------------ */
+/* The bf16 GEMV family itself (test/Test/FuryKernel/Gemv.hs:118-191): x, W  */
+/* and y bf16, widened exactly to binary32 (a NaN quieted, Numerics.hs:      */
+/* 33-38); pack width p (4, 8, 16): a lane's pack goes four elements to a    */
+/* chain, chain c adding ((x0 w0 + x1 w1) + (x2 w2 + x3 w3)) from 0; a       */
+/* lane's chains added left to right (inOrder, Gemv.hs:214-217), then the    */
+/* SIMD sum; the splits' partials in split order; y narrowed to bf16 by     */
+/* round-to-nearest-even (narrowBF16, Numerics.hs:41-48).                    */
+
+float fko_widen_bf16(uint16_t b) {
+  uint32_t w = (uint32_t)b << 16;
+  if ((w & 0x7F800000u) == 0x7F800000u && (w & 0x007FFFFFu)) w |= 0x00400000u;
+  float f;
+  memcpy(&f, &w, 4);
+  return f;
+}
+
+uint16_t fko_narrow_bf16(float x) {
+  uint32_t w;
+  memcpy(&w, &x, 4);
+  if (x != x) return (uint16_t)((w >> 16) | 0x0040u);
+  const uint32_t lsb = (w >> 16) & 1u;
+  return (uint16_t)((w + 0x7FFFu + lsb) >> 16);
+}
+
+void fko_gemv_bf16(const uint16_t *w, uint32_t n, uint32_t k, const uint16_t *x, uint32_t m, uint32_t pack,
+                   uint32_t split, uint16_t *y, int threads) {
+  const uint32_t packs = k / pack, chains = pack / 4;
+  const uint32_t stride = 32 * split;
+#pragma omp parallel for schedule(static) num_threads(threads > 0 ? threads : 1)
+  for (int64_t o = 0; o < (int64_t)n; ++o) {
+    const uint16_t *wr = w + (size_t)o * k;
+    for (uint32_t i = 0; i < m; ++i) {
+      const uint16_t *xr = x + (size_t)i * k;
+      float total = 0.0f;
+      for (uint32_t q = 0; q < split; ++q) {
+        float lanes[32];
+        for (uint32_t l = 0; l < 32; ++l) {
+          float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+          for (uint32_t j = q * 32 + l; j < packs; j += stride)
+            for (uint32_t c = 0; c < chains; ++c) {
+              const size_t at = (size_t)j * pack + 4 * c;
+              float x0 = fko_widen_bf16(xr[at]), x1 = fko_widen_bf16(xr[at + 1]);
+              float x2 = fko_widen_bf16(xr[at + 2]), x3 = fko_widen_bf16(xr[at + 3]);
+              float w0 = fko_widen_bf16(wr[at]), w1 = fko_widen_bf16(wr[at + 1]);
+              float w2 = fko_widen_bf16(wr[at + 2]), w3 = fko_widen_bf16(wr[at + 3]);
+              acc[c] = acc[c] + ((x0 * w0 + x1 * w1) + (x2 * w2 + x3 * w3));
+            }
+          float t = acc[0];
+          for (uint32_t c = 1; c < chains; ++c) t = t + acc[c];
+          lanes[l] = t;
+        }
+        float part = fko_simd_sum(lanes, 32);
+        total = q == 0 ? part : total + part;
+      }
+      y[(size_t)i * n + (size_t)o] = fko_narrow_bf16(total);
+    }
+  }
+}
+
+/* ------------------------------------------------------------------------ */
 /* RoPE, halves pairing (Eval.hs:634-645): tables of each position's cosine  */
 /* and sine of p * theta^(-2i/d), rounded once from binary64; each pair      */
 /* (i, i + d/2), i < rotated, turned as x_i c - x_{i+d/2} s and              */

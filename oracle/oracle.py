@@ -31,6 +31,7 @@ _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _f64p = np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")
 _u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
 _i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
 _u64 = ctypes.c_uint64
 _u32 = ctypes.c_uint32
 _int = ctypes.c_int
@@ -67,6 +68,9 @@ def lib():
             "fko_rmsnorm_rows": (None, [_f32p, _u32, _u32, ctypes.c_void_p, _f32, _f32, _f32p, _int]),
             "fko_softmax_rows": (None, [_f32p, _u32, _u32, _f32p, _int]),
             "fko_gemv": (None, [_f32p, _u32, _u32, _f32p, _u32, _u32, _f32p, _int]),
+            "fko_gemv_bf16": (None, [_u16p, _u32, _u32, _u16p, _u32, _u32, _u32, _u16p, _int]),
+            "fko_widen_bf16": (_f32, [ctypes.c_uint16]),
+            "fko_narrow_bf16": (ctypes.c_uint16, [_f32]),
             "fko_rope_tables": (None, [_f64, _u32, _u32, _u32, _f32p, _f32p]),
             "fko_rope": (None, [_f32p, _u32, _u32, _u32, _u32, _u32p, _f32p, _f32p, _f32p]),
             "fko_kv_store_ring": (None, [_f32p, _u32, _u32, _u32, _u32, _u32p, _u32p, _f32p]),
@@ -170,6 +174,39 @@ def gemv(w, x, split: int = 1, threads: int = 1) -> np.ndarray:
     y = np.empty((x2.shape[0], n), np.float32)
     lib().fko_gemv(w, n, k, x2, x2.shape[0], split, y, threads)
     return y
+
+
+def gemv_bf16(w, x, pack: int = 8, split: int = 1, threads: int = 1) -> np.ndarray:
+    """The reference's bf16 GEMV family (test/Test/FuryKernel/Gemv.hs):
+    w [n, k] and x [m, k] as bf16 bits (uint16), y [m, n] bf16 bits."""
+    w = _c(w, np.uint16)
+    x = _c(x, np.uint16)
+    n, k = w.shape
+    x2 = x.reshape(-1, k)
+    y = np.empty((x2.shape[0], n), np.uint16)
+    lib().fko_gemv_bf16(w, n, k, x2, x2.shape[0], pack, split, y, threads)
+    return y
+
+
+def narrow_bf16(a) -> np.ndarray:
+    """binary32 -> bf16 bits, round to nearest even, NaN quieted
+    (narrowBF16, src/FuryKernel/Numerics.hs:41-48), vectorised."""
+    a = np.ascontiguousarray(a, np.float32)
+    w = a.view(np.uint32).astype(np.uint64)
+    lsb = (w >> 16) & 1
+    out = ((w + 0x7FFF + lsb) >> 16).astype(np.uint16)
+    nan = np.isnan(a)
+    out[nan] = ((w[nan] >> 16) | 0x0040).astype(np.uint16)
+    return out
+
+
+def widen_bf16(b) -> np.ndarray:
+    """bf16 bits -> binary32, exact, NaN quieted (widenBF16,
+    Numerics.hs:33-38), vectorised."""
+    w = np.ascontiguousarray(b, np.uint16).astype(np.uint32) << 16
+    nan = ((w & 0x7F800000) == 0x7F800000) & ((w & 0x007FFFFF) != 0)
+    w[nan] |= 0x00400000
+    return w.view(np.float32)
 
 
 def rope_tables(theta: float, d: int, rotated: int, positions: int):
