@@ -123,6 +123,9 @@ cudaError_t fk_launch_rope(const float* x, uint32_t m, uint32_t heads, uint32_t 
 cudaError_t fk_launch_add(const float* a, const float* b, float* y, uint64_t n, cudaStream_t s);
 cudaError_t fk_launch_silu_mul(const float* a, const float* b, float* y, uint64_t n, cudaStream_t s);
 cudaError_t fk_launch_silu_pairs(const float* x, float* y, uint64_t n, cudaStream_t s);
+cudaError_t fk_launch_gemv_bf16(const uint16_t* w, const uint16_t* x, uint16_t* y, uint32_t n, uint32_t k,
+                                uint32_t m, uint32_t pack, uint32_t split, uint32_t ldx, uint32_t ldy, int sms,
+                                bool pdl, cudaStream_t s);
 cudaError_t fk_launch_argmax_pairs(const float* x, uint32_t m, uint32_t n, uint32_t ldx, uint32_t offset,
                                    uint32_t* pairs, const FkPeers* peers, bool pdl, cudaStream_t s);
 cudaError_t fk_launch_argmax_pick(const uint32_t* pairs, uint32_t shards, uint32_t m, uint32_t* ids,

@@ -623,6 +623,20 @@ int l_add(fkc_ctx* c, const Params& p, void* const* bufs) {
 int l_silu_mul(fkc_ctx* c, const Params& p, void* const* bufs) {
   return launched(fk_launch_silu_mul(CF(0), CF(1), F(2), p.u(0), c->stream), "silu_mul");
 }
+// gemv_bf16: w x y | n k m pack split ldx ldy: the reference's bf16 GEMV
+// family (test/Test/FuryKernel/Gemv.hs), pack width 4, 8 or 16.
+int l_gemv_bf16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  const uint32_t pack = p.u(3);
+  if (pack != 4 && pack != 8 && pack != 16)
+    return fail(FKC_ERR_ARGUMENT, "gemv_bf16: the pack width %u is not 4, 8 or 16.", pack);
+  if (p.u(1) % pack != 0 || p.u(5) % pack != 0)
+    return fail(FKC_ERR_ARGUMENT, "gemv_bf16: k %u and ldx %u are not multiples of the pack width %u.", p.u(1),
+                p.u(5), pack);
+  return launched(fk_launch_gemv_bf16((const uint16_t*)bufs[0], (const uint16_t*)bufs[1], (uint16_t*)bufs[2], p.u(0),
+                                      p.u(1), p.u(2), pack, p.u(4), p.u(5), p.u(6), c->sms, c->pdl, c->stream),
+                  "gemv_bf16");
+}
+
 // silu_pairs: x y | n: y[i] = silu(x[2i]) * x[2i + 1].
 int l_silu_pairs(fkc_ctx* c, const Params& p, void* const* bufs) {
   return launched(fk_launch_silu_pairs(CF(0), F(1), p.u(0), c->stream), "silu_pairs");
@@ -836,6 +850,12 @@ std::vector<KernelSpec> make_table() {
                {dim("n", 1, kMax)},
                l_silu_mul});
   t.push_back({"silu_pairs", 256, {{"x", "read", "f32"}, {"y", "write", "f32"}}, {dim("n", 1, kMax)}, l_silu_pairs});
+  t.push_back({"gemv_bf16",
+               512,
+               {{"w", "read", "bf16"}, {"x", "read", "bf16"}, {"y", "write", "bf16"}},
+               {dim("n", 1, 1048576), dim("k", 4, 65536, 4), dim("m", 1, 16), dim("pack", 4, 16, 4), dim("split", 1, 16),
+                u32("ldx"), u32("ldy")},
+               l_gemv_bf16});
   // The C layout (Abi.hs:113-133) and the canonical text (Abi.hs:136-159).
   for (auto& k : t) {
     uint32_t off = 0, align = 1;

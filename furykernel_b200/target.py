@@ -79,6 +79,10 @@ def _u32(name, access="read"):
     return Buffer(name, access, "u32")
 
 
+def _bf16(name, access="read"):
+    return Buffer(name, access, "bf16")
+
+
 def _dim(name, lo, hi, mult=1):
     return Param(name, "u32", DimRange(lo, hi, mult))
 
@@ -169,6 +173,9 @@ SPEC_KERNELS = {
         KernelSig("add", [_f32("a"), _f32("b"), _f32("y", "write")], [_dim("n", 1, _MAX)]),
         KernelSig("silu_mul", [_f32("a"), _f32("b"), _f32("y", "write")], [_dim("n", 1, _MAX)]),
         KernelSig("silu_pairs", [_f32("x"), _f32("y", "write")], [_dim("n", 1, _MAX)]),
+        KernelSig("gemv_bf16", [_bf16("w"), _bf16("x"), _bf16("y", "write")],
+                  [_dim("n", 1, 1048576), _dim("k", 4, 65536, 4), _dim("m", 1, 16), _dim("pack", 4, 16, 4),
+                   _dim("split", 1, 16), _u("ldx"), _u("ldy")], threads=512),
     ]
 }
 

@@ -216,6 +216,39 @@ def test_batched_gemv_subnormal_and_special_values(ctx):
         b.free()
 
 
+@pytest.mark.parametrize("n,k,m,pack,split", [(11008, 4096, 1, 8, 1), (4096, 11008, 4, 8, 2), (300, 1024, 3, 4, 4),
+                                              (257, 2048, 16, 16, 1), (64, 512, 7, 16, 8), (33, 96, 2, 4, 16)])
+def test_gemv_bf16_family_bit_exact(ctx, n, k, m, pack, split):
+    """The reference's bf16 GEMV family (Gemv.hs): bf16 in and out, f32
+    chains, the oracle's bits for every pack width and split."""
+    w = O.narrow_bf16(O.normal(81, n * k, 0.0, 0.02)).reshape(n, k)
+    x = O.narrow_bf16(O.normal(82, m * k)).reshape(m, k)
+    wd, xd = ctx.to_device(w), ctx.to_device(x)
+    yd = ctx.empty((m, n), np.uint16)
+    ctx.launch("gemv_bf16", {"n": n, "k": k, "m": m, "pack": pack, "split": split, "ldx": k, "ldy": n}, [wd, xd, yd])
+    assert np.array_equal(yd.download(), O.gemv_bf16(w, x, pack, split, THREADS))
+    for b in (wd, xd, yd):
+        b.free()
+
+
+def test_gemv_bf16_special_values(ctx):
+    n, k, m = 40, 256, 3
+    w = O.narrow_bf16(O.normal(83, n * k, 0.0, 0.02)).reshape(n, k)
+    x = O.narrow_bf16(O.normal(84, m * k)).reshape(m, k)
+    x[0, 5] = 0x7F80  # +inf
+    x[1, 9] = 0x7FC1  # a NaN
+    x[2] = O.narrow_bf16(O.widen_bf16(x[2]) * np.float32(1e-38))  # subnormal products
+    wd, xd = ctx.to_device(w), ctx.to_device(x)
+    yd = ctx.empty((m, n), np.uint16)
+    ctx.launch("gemv_bf16", {"n": n, "k": k, "m": m, "pack": 8, "split": 1, "ldx": k, "ldy": n}, [wd, xd, yd])
+    got, want = yd.download(), O.gemv_bf16(w, x, 8, 1)
+    nan = np.isnan(O.widen_bf16(want))
+    assert np.array_equal(np.isnan(O.widen_bf16(got)), nan)  # NaN payloads aside
+    assert np.array_equal(got[~nan], want[~nan])
+    for b in (wd, xd, yd):
+        b.free()
+
+
 # ---------------------------------------------------------------------------
 # The decode attention path: KV store, split attention, combine
 
