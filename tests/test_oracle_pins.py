@@ -152,3 +152,31 @@ def test_attention_over_one_position_returns_its_value():
     y, yb = O.r_attend((q, np.zeros_like(q)), heads, 1, d, length, np.array([0], np.uint32),
                        np.array([0], np.uint32), kc, vc, 1.0 / math.sqrt(d))
     assert np.allclose(y[0], vc[0, 0, 0])
+
+
+def _ulps_bf16(a, b):
+    """Distance in bf16 steps, across zero too (ReduceTest.hs:91-96)."""
+    def ordered(u):
+        u = u.astype(np.int64)
+        return np.where(u & 0x8000, -(u & 0x7FFF), u)
+    return np.abs(ordered(a) - ordered(b))
+
+
+@pytest.mark.parametrize("h", [64, 256, 1000, 4096])
+def test_rmsnorm_within_one_bf16_ulp_of_its_f64_spec(h):
+    """The reference's RMSNorm property (test/Test/FuryKernel/ReduceTest.hs:
+    40-42, 96-107), for the f32 row kernel: its result, narrowed to bf16, is
+    within one bf16 ulp of the f64 specification narrowed once; and a row's
+    bits do not depend on the rows beside it (:109-119)."""
+    rng = np.random.default_rng(h)
+    rows = 3
+    x = O.widen_bf16(O.narrow_bf16(rng.uniform(-8, 8, size=(rows, h)).astype(np.float32)))
+    g = O.widen_bf16(O.narrow_bf16(rng.uniform(-2, 2, size=h).astype(np.float32)))
+    eps = np.float32(1e-6)
+    got = O.rmsnorm_rows(x, g, eps)
+    d = x.astype(np.float64)
+    s = 1.0 / np.sqrt((d * d).sum(axis=1, keepdims=True) / h + float(eps))
+    spec = (d * s * g.astype(np.float64)).astype(np.float32)
+    assert _ulps_bf16(O.narrow_bf16(got), O.narrow_bf16(spec)).max() <= 1
+    alone = O.rmsnorm_rows(x[1:2], g, eps)
+    assert np.array_equal(alone.view(np.uint32), got[1:2].view(np.uint32))
