@@ -462,10 +462,28 @@ def run_gemm(args):
                          "note": "achieved counts the 3 TF32 products the tensor pipe runs"},
             "gpu_launches": 2 * args.steps, "clocks": clk.summary(),
         }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = gemm_cpu_baseline(M, K, NN)
         print(json.dumps(line), flush=True)
     ctx.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def gemm_cpu_baseline(M: int, K: int, N: int, rows: int = 4) -> dict:
+    """Config 3c on the host as the CPU target computes it (gemmTile: each
+    element a sequential binary32 sum over k, oracle/fko_gemm_tile), one
+    thread, on `rows` of A's M rows, scaled to the whole product."""
+    from oracle import oracle as O
+
+    a = O.normal(31, rows * K).reshape(rows, K)
+    w = O.normal(32, N * K, 0.0, 0.02).reshape(N, K)
+    t0 = time.perf_counter()
+    O.gemm_tile(a, w, 1)
+    s = (time.perf_counter() - t0) * M / rows
+    return {"value": 2.0 * M * N * K / s / 1e12, "unit": "TFLOP/s", "cores": 1, "kind": "port",
+            "sample": f"{rows} of the {M} rows of A against all of W, gemmTile's order (k in order), 1 thread, "
+                      "scaled to all rows", "ms": s * 1e3}
 
 
 def time_graph(ctx, launches, steps, warmup, rotate=None):

@@ -56,6 +56,7 @@ void fko_rmsnorm_rows(const float *x, uint32_t rows, uint32_t h, const float *ga
                       float eps, float factor, float *y, int threads);
 void fko_softmax_rows(const float *x, uint32_t rows, uint32_t h, float *y, int threads);
 
+void fko_gemm_tile(const float *a, uint32_t M, uint32_t K, const float *b, uint32_t N, float *c, int threads);
 float fko_widen_bf16(uint16_t b);
 uint16_t fko_narrow_bf16(float x);
 void fko_gemv_bf16(const uint16_t *w, uint32_t n, uint32_t k, const uint16_t *x, uint32_t m, uint32_t pack,

@@ -298,6 +298,25 @@ void fko_gemv(const float *w, uint32_t n, uint32_t k, const float *x, uint32_t m
 }
 
 /* ------------------------------------------------------------------------ */
+/* gemmTile (src/FuryKernel/Tile.hs:76-157) as the CPU target runs it:      */
+/* C = A B^T, an element's sum over k in order, 8 at a time through the     */
+/* fragment product (Cpu.hs:549-560: acc = acc + a * b, each product and    */
+/* sum rounded), from 0 -- so a sequential binary32 dot over k.             */
+
+void fko_gemm_tile(const float *a, uint32_t M, uint32_t K, const float *b, uint32_t N, float *c, int threads) {
+#pragma omp parallel for schedule(static) num_threads(threads > 0 ? threads : 1)
+  for (int64_t i = 0; i < (int64_t)M; ++i) {
+    const float *ar = a + (size_t)i * K;
+    for (uint32_t j = 0; j < N; ++j) {
+      const float *br = b + (size_t)j * K;
+      float acc = 0.0f;
+      for (uint32_t k = 0; k < K; ++k) acc = acc + ar[k] * br[k];
+      c[(size_t)i * N + j] = acc;
+    }
+  }
+}
+
+/* ------------------------------------------------------------------------ */
 /* The bf16 GEMV family itself (test/Test/FuryKernel/Gemv.hs:118-191): x, W  */
 /* and y bf16, widened exactly to binary32 (a NaN quieted, Numerics.hs:      */
 /* 33-38); pack width p (4, 8, 16): a lane's pack goes four elements to a    */

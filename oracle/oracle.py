@@ -69,6 +69,7 @@ def lib():
             "fko_softmax_rows": (None, [_f32p, _u32, _u32, _f32p, _int]),
             "fko_gemv": (None, [_f32p, _u32, _u32, _f32p, _u32, _u32, _f32p, _int]),
             "fko_gemv_bf16": (None, [_u16p, _u32, _u32, _u16p, _u32, _u32, _u32, _u16p, _int]),
+            "fko_gemm_tile": (None, [_f32p, _u32, _u32, _f32p, _u32, _f32p, _int]),
             "fko_widen_bf16": (_f32, [ctypes.c_uint16]),
             "fko_narrow_bf16": (ctypes.c_uint16, [_f32]),
             "fko_rope_tables": (None, [_f64, _u32, _u32, _u32, _f32p, _f32p]),
@@ -174,6 +175,17 @@ def gemv(w, x, split: int = 1, threads: int = 1) -> np.ndarray:
     y = np.empty((x2.shape[0], n), np.float32)
     lib().fko_gemv(w, n, k, x2, x2.shape[0], split, y, threads)
     return y
+
+
+def gemm_tile(a, b, threads: int = 1) -> np.ndarray:
+    """C = A B^T as the CPU target's gemmTile sums it (k in order)."""
+    a = _c(a, np.float32)
+    b = _c(b, np.float32)
+    M, K = a.shape
+    N = b.shape[0]
+    c = np.empty((M, N), np.float32)
+    lib().fko_gemm_tile(a, M, K, b, N, c, threads)
+    return c
 
 
 def gemv_bf16(w, x, pack: int = 8, split: int = 1, threads: int = 1) -> np.ndarray:

@@ -180,3 +180,19 @@ def test_rmsnorm_within_one_bf16_ulp_of_its_f64_spec(h):
     assert _ulps_bf16(O.narrow_bf16(got), O.narrow_bf16(spec)).max() <= 1
     alone = O.rmsnorm_rows(x[1:2], g, eps)
     assert np.array_equal(alone.view(np.uint32), got[1:2].view(np.uint32))
+
+
+def test_gemm_tile_sums_k_in_order():
+    """gemmTile's element sums k in order (Tile.hs:19-23), the fragment
+    product adding a rounded product at a time (Cpu.hs:549-560): with
+    1e8, 1, -1e8, 1 along k the in-order sum is 1 (pairwise would be 0 or
+    2); and every element within the f64 evaluator's bound of A B^T
+    (TileTest.hs:33-47)."""
+    a = np.array([[1e8, 1.0, -1e8, 1.0] + [0.0] * 4], np.float32)
+    b = np.ones((1, 8), np.float32)
+    assert O.gemm_tile(a, b)[0, 0] == np.float32(1.0)
+    rng = np.random.default_rng(5)
+    A = rng.standard_normal((9, 96)).astype(np.float32)
+    B = (0.02 * rng.standard_normal((7, 96))).astype(np.float32)
+    got = O.gemm_tile(A, B)
+    assert O.within(got, O.r_linear(B, O.r_input(A))).all()
