@@ -5,6 +5,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 enum { FK_PRO_NONE = 0, FK_PRO_RMSNORM = 1, FK_PRO_SILU = 2, FK_PRO_REDUCE_RMSNORM = 3 };
 
 // Tensor-parallel exchange over NVLink peer memory. Every rank owns one
@@ -140,6 +144,25 @@ cudaError_t fk_launch_fill_normal(float* out, uint64_t n, uint64_t seed, double 
 cudaError_t fk_launch_fill_uniform(float* out, uint64_t n, uint64_t seed, double a, double b, cudaStream_t s);
 cudaError_t fk_launch_rope_tables(float* cos_t, float* sin_t, double theta, uint32_t d, uint32_t rotated,
                                   uint32_t positions, cudaStream_t s);
+
+// Lets `func` take `bytes` of dynamic shared memory on the current device:
+// cudaFuncSetAttribute is per device, so it is set once per (function,
+// device) and raised when a launch asks for more.
+template <typename F>
+inline cudaError_t fk_allow_smem(F func, size_t bytes) {
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, size_t> allowed;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  size_t& have = allowed[{reinterpret_cast<const void*>(func), dev}];
+  if (bytes <= have) return cudaSuccess;
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess) have = bytes;
+  return e;
+}
 
 // Launch helper for kernels that take part in programmatic dependent launch.
 template <typename... KArgs, typename... Args>

@@ -422,13 +422,9 @@ cudaError_t launch_attend(const FkAttendDecode& f, cudaStream_t s) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const size_t smem = ((size_t)a.m + 1) * sizeof(uint32_t);
-  static size_t configured = 0;
-  if (smem > 48 * 1024 && smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    configured = smem;
-  }
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, smem);
+  cudaError_t e = fk_allow_smem(kern, smem);
+  if (e != cudaSuccess) return e;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, smem);
   if (e != cudaSuccess) return e;
   if (per_sm < 1) return cudaErrorInvalidConfiguration;
   const uint64_t most = (uint64_t)a.m * a.heads * a.max_splits;
@@ -451,13 +447,8 @@ cudaError_t fk_launch_attend_prompt(const FkAttend& a, float* out, uint32_t ldo,
   if (a.d != fk::kHeadDim || a.kv_heads == 0 || a.heads % a.kv_heads != 0 || max_pos >= a.length) return cudaErrorInvalidValue;
   const size_t smem = (3 * (size_t)fk::kPromptTile * fk::kHeadDim + (size_t)fk::kPromptTile * (max_pos + 1)) * 4;
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  static size_t configured = 0;
-  if (smem > 48 * 1024 && smem > configured) {
-    cudaError_t e =
-        cudaFuncSetAttribute(fk::attend_prompt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    configured = smem;
-  }
+  cudaError_t e = fk_allow_smem(fk::attend_prompt_kernel, smem);
+  if (e != cudaSuccess) return e;
   const dim3 grid((a.m + fk::kPromptTile - 1) / fk::kPromptTile, a.heads);
   return fk_launch_ex(fk::attend_prompt_kernel, grid, dim3(128), smem, s, a.pdl, a, out, ldo, max_pos);
 }
@@ -466,12 +457,8 @@ cudaError_t fk_launch_combine(const FkCombine& a, cudaStream_t s) {
   if (a.m == 0) return cudaSuccess;
   if (a.d > 1024 || a.d < 32 || a.max_splits == 0 || a.max_splits > 24576) return cudaErrorInvalidValue;
   const size_t smem = 2 * (size_t)a.max_splits * sizeof(float);
-  static size_t configured = 0;
-  if (smem > 48 * 1024 && smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(fk::combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    configured = smem;
-  }
+  cudaError_t e = fk_allow_smem(fk::combine_kernel, smem);
+  if (e != cudaSuccess) return e;
   return fk_launch_ex(fk::combine_kernel, dim3(a.heads, a.m), dim3(a.d), smem, s, a.pdl, a);
 }
 

@@ -311,12 +311,9 @@ cudaError_t fk_launch_gemm_tf32x3(const float* a_hi, const float* a_lo, const fl
   if (!make_map(&ma_hi, a_hi, M, K, fk::kGM) || !make_map(&ma_lo, a_lo, M, K, fk::kGM) ||
       !make_map(&mw_hi, w_hi, N, K, fk::kGN) || !make_map(&mw_lo, w_lo, N, K, fk::kGN))
     return cudaErrorInvalidValue;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e =
-        cudaFuncSetAttribute(fk::gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fk::kGemmSmem);
+  {
+    cudaError_t e = fk_allow_smem(fk::gemm_tf32x3_kernel, fk::kGemmSmem);
     if (e != cudaSuccess) return e;
-    configured = true;
   }
   if ((N + fk::kGN - 1) / fk::kGN > 65535) return cudaErrorInvalidValue;
   dim3 grid((M + fk::kGM - 1) / fk::kGM, (N + fk::kGN - 1) / fk::kGN);

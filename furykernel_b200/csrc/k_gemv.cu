@@ -178,8 +178,8 @@ static cudaError_t launch_m(const GemvArgs& a, cudaStream_t st, bool pdl) {
   const uint32_t blocks = (a.n + rows_per_block - 1) / rows_per_block;
   const size_t smem = (size_t)a.m * a.kc * sizeof(float);
   auto kern = gemv_kernel<M, PRO, ADD>;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  {
+    cudaError_t e = fk_allow_smem(kern, smem);
     if (e != cudaSuccess) return e;
   }
   cudaLaunchConfig_t cfg = {};

@@ -312,12 +312,8 @@ template <int M, int PRO, int EPI>
 static cudaError_t launch_batch(const BatchArgs& a, int sms, cudaStream_t st, bool pdl) {
   auto kern = gemv_batch_kernel<M, PRO, EPI>;
   const size_t smem = 3 * (size_t)M * kChunk * sizeof(float4);
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  cudaError_t e = fk_allow_smem(kern, smem);
+  if (e != cudaSuccess) return e;
   const uint32_t units = (a.n + kBatchRows - 1) / kBatchRows;
   uint32_t blocks = (uint32_t)sms;
   if (blocks > units) blocks = units;

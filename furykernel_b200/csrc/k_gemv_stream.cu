@@ -236,14 +236,10 @@ template <int M, int PRO, int EPI>
 static cudaError_t launch_stream(const StreamArgs& a, int sms, cudaStream_t st, bool pdl) {
   auto kern = gemv_stream_kernel<M, PRO, EPI>;
   const size_t smem = (size_t)a.m * a.k * sizeof(float);
-  static size_t configured = 0;  // dynamic shared memory this instantiation allows
-  if (smem > 48 * 1024 && smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    configured = smem;
-  }
+  cudaError_t e = fk_allow_smem(kern, smem);
+  if (e != cudaSuccess) return e;
   int per_sm = 0;
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 512, smem);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 512, smem);
   if (e != cudaSuccess) return e;
   if (per_sm < 1) return cudaErrorInvalidValue;
   if (per_sm > 2) per_sm = 2;
