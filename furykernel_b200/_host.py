@@ -1,0 +1,155 @@
+"""ctypes binding of libfurykernel_host.so (include/furykernel_host.h): the
+programs, the planner and the lowering in C++. The Llama engine takes its
+launch list from here; the Python restatement in `program/` and `engine.py`
+is the same algorithm, kept as the checker the tests compare against."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+from . import _native as N
+
+_LIB = None
+_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_build", "libfurykernel_host.so")
+
+FKH_OK, FKH_ERR_ARGUMENT, FKH_ERR_SPACE, FKH_ERR_INTERNAL = 0, 1, 2, 3
+ABI_VERSION = 1
+
+
+class Shape(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint64) for n in ("d_model", "heads", "kv_heads", "head_dim", "ffn", "vocab",
+                                                "layers")] + \
+               [("theta", ctypes.c_double), ("eps", ctypes.c_double)] + \
+               [(n, ctypes.c_uint64) for n in ("slots", "length", "positions")]
+
+
+class PlanOptions(ctypes.Structure):
+    _fields_ = [("horizontal", ctypes.c_int), ("gated", ctypes.c_int), ("store_gelus", ctypes.c_int),
+                ("sequence_rows", ctypes.c_uint64)]
+
+
+DESC_ADDRS = ("arena", "kbase", "vbase", "cos_t", "sin_t", "tokens", "pos", "slot", "x", "x1", "qkv", "att", "gu",
+              "act", "logits", "out_ids", "partial", "pairs", "pairs_all")
+
+
+class Desc(ctypes.Structure):
+    _fields_ = [("full", Shape)] + \
+               [(n, ctypes.c_uint64) for n in ("batch", "rank", "world", "sms", "chunk")] + \
+               [(n, ctypes.c_int) for n in ("gate_up_interleaved", "peer_exchange", "fuse_attention")] + \
+               [(n, ctypes.c_uint64) for n in DESC_ADDRS] + [("part", ctypes.c_uint64 * 3)]
+
+
+def lib():
+    """The loaded library, rebuilt first (g++, no CUDA) when a source is
+    newer; a failed build or load raises."""
+    global _LIB
+    if _LIB is None:
+        from . import build as B
+
+        B.build_host()  # a no-op unless a source is newer than the library
+        L = ctypes.CDLL(_PATH)
+        L.fkh_abi_version.restype = ctypes.c_int
+        if L.fkh_abi_version() != ABI_VERSION:
+            raise RuntimeError(f"libfurykernel_host.so has ABI {L.fkh_abi_version()}, this binding {ABI_VERSION}")
+        text_args = [ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t), ctypes.c_char_p,
+                     ctypes.c_size_t]
+        L.fkh_llama_program_text.argtypes = [ctypes.POINTER(Shape), ctypes.c_int] + text_args
+        L.fkh_program_roundtrip.argtypes = [ctypes.c_char_p] + text_args
+        L.fkh_plan_text.argtypes = [ctypes.c_char_p, ctypes.POINTER(PlanOptions)] + text_args
+        L.fkh_llama_launches.argtypes = [ctypes.POINTER(Desc), ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p,
+                                         ctypes.c_size_t]
+        L.fkh_launches_count.argtypes = [ctypes.c_void_p]
+        L.fkh_launches_count.restype = ctypes.c_size_t
+        for f in ("fkh_launch_param_count", "fkh_launch_buf_count"):
+            getattr(L, f).argtypes = [ctypes.c_void_p, ctypes.c_size_t]
+            getattr(L, f).restype = ctypes.c_size_t
+        L.fkh_launch_kernel.argtypes = [ctypes.c_void_p, ctypes.c_size_t]
+        L.fkh_launch_kernel.restype = ctypes.c_char_p
+        L.fkh_launch_param_name.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t]
+        L.fkh_launch_param_name.restype = ctypes.c_char_p
+        L.fkh_launch_param_value.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t]
+        L.fkh_launch_param_value.restype = ctypes.c_double
+        L.fkh_launch_buf.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t]
+        L.fkh_launch_buf.restype = ctypes.c_uint64
+        L.fkh_launches_free.argtypes = [ctypes.c_void_p]
+        L.fkh_split_for.argtypes = [ctypes.c_uint64] * 3
+        L.fkh_split_for.restype = ctypes.c_uint64
+        _LIB = L
+    return _LIB
+
+
+def _check(rc: int, err) -> None:
+    if rc == FKH_ERR_ARGUMENT:
+        raise N.Refused(N.FKC_ERR_ARGUMENT, err.value.decode())
+    if rc != FKH_OK:
+        raise N.FkcError(N.FKC_ERR_STATE, f"libfurykernel_host.so: {err.value.decode()} (code {rc})")
+
+
+def _text(call, *args) -> str:
+    err = ctypes.create_string_buffer(1024)
+    n = ctypes.c_size_t(0)
+    rc = call(*args, None, 0, ctypes.byref(n), err, len(err))
+    if rc != FKH_ERR_SPACE:
+        _check(rc, err)
+    buf = ctypes.create_string_buffer(n.value + 1)
+    _check(call(*args, buf, len(buf), ctypes.byref(n), err, len(err)), err)
+    return buf.value.decode()
+
+
+def shape(s) -> Shape:
+    """A LlamaShape (program.llama) as the C struct."""
+    return Shape(s.d_model, s.heads, s.kv_heads, s.head_dim, s.ffn, s.vocab, s.layers, s.theta, s.eps, s.slots,
+                 s.length, s.positions)
+
+
+def llama_program_text(s, which: str) -> str:
+    """The rendered embed, layer or head program of a LlamaShape."""
+    w = {"embed": 0, "layer": 1, "head": 2}[which]
+    sh = shape(s)
+    return _text(lib().fkh_llama_program_text, ctypes.byref(sh), w)
+
+
+def program_roundtrip(text: str) -> str:
+    return _text(lib().fkh_program_roundtrip, text.encode())
+
+
+def plan_text(program_text: str, horizontal=True, gated=False, store_gelus=False, sequence_rows=1) -> str:
+    """Plans a rendered program and renders the plan."""
+    o = PlanOptions(int(horizontal), int(gated), int(store_gelus), sequence_rows)
+    return _text(lib().fkh_plan_text, program_text.encode(), ctypes.byref(o))
+
+
+def split_for(n_rows: int, k: int, sms: int) -> int:
+    return int(lib().fkh_split_for(n_rows, k, sms))
+
+
+def llama_launches(full, batch: int, rank: int, world: int, sms: int, chunk: int, gate_up_interleaved: bool,
+                   peer_exchange: bool, fuse_attention: bool, addrs: dict) -> list:
+    """The decode step's launch list: (kernel, params dict, bufs list)
+    triples, params as ints where they are integers."""
+    d = Desc()
+    d.full = shape(full)
+    d.batch, d.rank, d.world, d.sms, d.chunk = batch, rank, world, sms, chunk
+    d.gate_up_interleaved, d.peer_exchange, d.fuse_attention = (int(gate_up_interleaved), int(peer_exchange),
+                                                                 int(fuse_attention))
+    for n in DESC_ADDRS:
+        setattr(d, n, int(addrs.get(n, 0)))
+    for i, p in enumerate(addrs["part"]):
+        d.part[i] = int(p)
+    L = lib()
+    h = ctypes.c_void_p()
+    err = ctypes.create_string_buffer(1024)
+    _check(L.fkh_llama_launches(ctypes.byref(d), ctypes.byref(h), err, len(err)), err)
+    try:
+        out = []
+        for i in range(L.fkh_launches_count(h)):
+            params = {}
+            for j in range(L.fkh_launch_param_count(h, i)):
+                v = L.fkh_launch_param_value(h, i, j)
+                params[L.fkh_launch_param_name(h, i, j).decode()] = int(v) if float(v).is_integer() else v
+            bufs = [int(L.fkh_launch_buf(h, i, j)) for j in range(L.fkh_launch_buf_count(h, i))]
+            out.append((L.fkh_launch_kernel(h, i).decode(), params, bufs))
+        return out
+    finally:
+        L.fkh_launches_free(h)

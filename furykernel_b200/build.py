@@ -73,5 +73,26 @@ def build(verbose: bool = False, ptxas_v: bool = False) -> str:
     return LIB
 
 
+HOST = os.path.join(HERE, "host")
+HOST_LIB = os.path.join(OUT_DIR, "libfurykernel_host.so")
+
+
+def build_host(verbose: bool = False) -> str:
+    """libfurykernel_host.so: the programs, the planner and the lowering in
+    C++ (g++, no CUDA), behind include/furykernel_host.h."""
+    os.makedirs(OUT_DIR, exist_ok=True)
+    srcs = sorted(glob.glob(os.path.join(HOST, "*.cc")))
+    deps = srcs + glob.glob(os.path.join(HOST, "*.h")) + [os.path.join(HERE, "..", "include", "furykernel_host.h")]
+    if os.path.exists(HOST_LIB) and all(os.path.getmtime(d) <= os.path.getmtime(HOST_LIB) for d in deps):
+        return HOST_LIB
+    cmd = ["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra", "-Wno-unused-parameter",
+           "-fvisibility=hidden", *srcs, "-o", HOST_LIB]
+    if verbose:
+        print(" ".join(cmd), file=sys.stderr)
+    subprocess.run(cmd, check=True)
+    return HOST_LIB
+
+
 if __name__ == "__main__":
     print(build(verbose=True, ptxas_v="-v" in sys.argv))
+    print(build_host(verbose=True))

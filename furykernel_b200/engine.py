@@ -14,7 +14,11 @@ over the concatenated rows. KV caches are Ring arenas per layer.
 
 `Llama` builds a whole decode step -- the embedding gather, every layer's
 plan, the head's plan -- captures it as one CUDA graph, and replays it per
-step: host token ids in, greedy ids out.
+step: host token ids in, greedy ids out. Its launch list comes from the C++
+host library (libfurykernel_host.so: the same programs, planner and
+lowering); `lower_step` and `Llama._launches_restated` state the same
+algorithm in Python, and the tests hold the library to them launch for
+launch.
 """
 
 from __future__ import annotations
@@ -359,7 +363,29 @@ class Llama:
         return self.kbase + l * per, self.vbase + l * per
 
     # -- the step's launches
+    def launch_addresses(self) -> dict:
+        """The device addresses the decode step's launches bind (the C++
+        host library's fkh_llama_desc)."""
+        return {"arena": self.arena.ptr, "kbase": self.kbase, "vbase": self.vbase, "cos_t": self.cos.ptr,
+                "sin_t": self.sin.ptr, "tokens": self.tokens.ptr, "pos": self.pos.ptr, "slot": self.slot.ptr,
+                "x": self.x.ptr, "x1": self.x1.ptr, "qkv": self.qkv.ptr, "att": self.att.ptr, "gu": self.gu.ptr,
+                "act": self.act.ptr, "logits": self.logits.ptr, "out_ids": self.out_ids.ptr,
+                "partial": self.partial.ptr, "pairs": self.pairs.ptr, "pairs_all": self.pairs_all.ptr,
+                "part": [b.ptr for b in self.part]}
+
     def _launches(self) -> list:
+        """The decode step's launches, from libfurykernel_host.so
+        (fkh_llama_launches): the plans of the embedding, a layer and the
+        head lowered to table launches, then the rewrites below."""
+        from . import _host
+
+        return [Launch(k, p, b) for k, p, b in _host.llama_launches(
+            self.full, self.m, self.rank, self.world, self.ctx.sms, self.chunk, self.gate_up_interleaved,
+            self.peer_exchange, self.fuse_attention, self.launch_addresses())]
+
+    def _launches_restated(self) -> list:
+        """The same launch list in Python (the restatement the host
+        library is checked against)."""
         s, m = self.s, self.m
         d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
         tables = {"cos": self.cos.ptr, "sin": self.sin.ptr}

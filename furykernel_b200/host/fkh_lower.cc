@@ -1,0 +1,538 @@
+// A plan's steps as launches of the CUDA target's kernel table (the step
+// shapes of the Llama-shaped programs), and the whole decode step of the
+// Llama engine: the embedding, every layer, the head, then the engine's
+// rewrites (the SiLU-gate on interleaved gate/up tiles, tensor parallelism
+// over peer memory or NCCL, the decode step's KV store folded into its
+// attention) and the split-K of each GEMV.
+#include <algorithm>
+
+#include "fkh.h"
+
+namespace fkh {
+
+double Launch::param(const std::string& n) const {
+  for (const auto& [k, v] : params)
+    if (k == n) return v;
+  throw Refusal(kernel + ": no parameter " + n + ".");
+}
+bool Launch::has(const std::string& n) const {
+  for (const auto& kv : params)
+    if (kv.first == n) return true;
+  return false;
+}
+void Launch::set(const std::string& n, double v) {
+  for (auto& kv : params)
+    if (kv.first == n) {
+      kv.second = v;
+      return;
+    }
+  params.emplace_back(n, v);
+}
+
+namespace {
+
+std::string work_text(const Program& p, const Step& step) {
+  std::string s;
+  for (size_t i = 0; i < step.work.size(); ++i) {
+    std::string k = step.work[i].kind;
+    std::transform(k.begin(), k.end(), k.begin(), ::tolower);
+    s += (i ? "; " : "") + k + " " + p.nodes[step.work[i].node].name;
+  }
+  return s;
+}
+
+template <typename M>
+typename M::mapped_type at(const M& m, const std::string& key, const std::string& what) {
+  auto it = m.find(key);
+  if (it == m.end()) throw Refusal(what + ": nothing is bound to " + key + ".");
+  return it->second;
+}
+
+}  // namespace
+
+Launch lower_step(const Program& p, const Step& step, const Binding& b, uint64_t cos_t, uint64_t sin_t,
+                  const AttnBufs& attn) {
+  std::vector<const Node*> anchors, epilogues, effects;
+  std::map<int, const Node*> recomputed;
+  std::vector<std::string> kinds;
+  for (const Work& w : step.work) {
+    const Node* n = &p.nodes[w.node];
+    kinds.push_back(w.kind);
+    if (w.kind == "Anchor") anchors.push_back(n);
+    if (w.kind == "Recompute") recomputed[n->outputs[0]] = n;
+    if (w.kind == "Epilogue") epilogues.push_back(n);
+    if (w.kind == "Effect") effects.push_back(n);
+  }
+  auto vname = [&](int v) { return p.values[v].name; };
+  auto stored = [&](int v) -> View {
+    auto it = b.values.find(vname(v));
+    if (it == b.values.end()) throw Refusal(step.name + ": " + vname(v) + " is not stored where the step reads it.");
+    return it->second;
+  };
+  auto src_name = [&](int s) { return p.sources[s].name; };
+  auto recomputed_of = [&](int v) -> const Node* {
+    auto it = recomputed.find(v);
+    return it == recomputed.end() ? nullptr : it->second;
+  };
+  const double m = (double)b.m;
+
+  bool all_linear = !anchors.empty();
+  for (const Node* n : anchors)
+    if (n->op.kind != "Linear") all_linear = false;
+  if (all_linear) {
+    const int x_id = anchors[0]->op.values[0];
+    for (const Node* n : anchors)
+      if (n->op.values[0] != x_id)
+        throw Refusal(step.name + ": anchors of different inputs: " + work_text(p, step));
+    const uint64_t w0 = at(b.weights, src_name(anchors[0]->op.sources[0]), step.name);
+    uint64_t n_total = 0;
+    const uint64_t k = p.sources[anchors[0]->op.sources[0]].kind.dims[1];
+    uint64_t addr = w0;
+    for (const Node* n : anchors) {  // the anchors' weights must lie adjacent
+      const Source& w = p.sources[n->op.sources[0]];
+      if (at(b.weights, w.name, step.name) != addr)
+        throw Refusal(step.name + ": the weights of its anchors are not adjacent.");
+      addr += 4 * w.kind.dims[0] * k;
+      n_total += w.kind.dims[0];
+    }
+    View y;
+    int r_id = -1;
+    if (!epilogues.empty()) {
+      const Node* ep = epilogues[0];
+      if (epilogues.size() != 1 || ep->op.kind != "Add" || anchors.size() != 1)
+        throw Refusal(step.name + ": epilogue " + ep->name + " is not one residual add.");
+      const int tile = anchors[0]->outputs[0];
+      r_id = ep->op.values[1] == tile ? ep->op.values[0] : ep->op.values[1];
+      y = stored(ep->outputs[0]);
+    } else {
+      y = at(b.values, vname(anchors[0]->outputs[0]), step.name);
+      for (size_t i = 1; i < anchors.size(); ++i) {  // adjacent columns
+        const View nxt = at(b.values, vname(anchors[i]->outputs[0]), step.name);
+        if (nxt.base != y.base) throw Refusal(step.name + ": its anchors' outputs are not adjacent.");
+      }
+    }
+    Launch L;
+    L.params = {{"n", (double)n_total}, {"k", (double)k}, {"m", m}, {"split", 1.0}, {"ldy", (double)y.ld}};
+    const Node* xn = recomputed_of(x_id);
+    if (!xn) {
+      const View x = stored(x_id);
+      L.set("ldx", (double)x.ld);
+      if (!epilogues.empty()) {
+        const View r = stored(r_id);
+        L.kernel = "gemv_add";
+        L.set("ldr", (double)r.ld);
+        L.bufs = {w0, x.ptr(), r.ptr(), y.ptr()};
+        return L;
+      }
+      L.kernel = "gemv";
+      L.bufs = {w0, x.ptr(), y.ptr()};
+      return L;
+    }
+    if (xn->op.kind == "RmsNorm" && epilogues.empty()) {
+      const View x = stored(xn->op.values[0]);
+      const uint64_t gamma = at(b.weights, src_name(xn->op.sources[0]), step.name);
+      L.kernel = "gemv_rmsnorm";
+      L.set("ldx", (double)x.ld);
+      L.set("eps", xn->op.eps);
+      L.set("factor", xn->op.factor);
+      L.bufs = {w0, x.ptr(), gamma, y.ptr()};
+      return L;
+    }
+    if (xn->op.kind == "SiluMul") {
+      const View g = stored(xn->op.values[0]), u = stored(xn->op.values[1]);
+      if (g.base != u.base || g.ld != u.ld) throw Refusal(step.name + ": SiLU-gate's halves are not one row.");
+      L.set("ldx", (double)g.ld);
+      L.set("up_off", (double)(u.col - g.col));
+      if (!epilogues.empty()) {
+        const View r = stored(r_id);
+        L.kernel = "gemv_silu_add";
+        L.set("ldr", (double)r.ld);
+        L.bufs = {w0, g.ptr(), r.ptr(), y.ptr()};
+        return L;
+      }
+      L.kernel = "gemv_silu";
+      L.bufs = {w0, g.ptr(), y.ptr()};
+      return L;
+    }
+    throw Refusal(step.name + ": no kernel runs " + work_text(p, step));
+  }
+
+  if (anchors.size() == 1 && anchors[0]->op.kind == "Attend") {
+    const Node* att = anchors[0];
+    const AttnSpec& spec = att->op.attn;
+    const Node* qn = recomputed_of(att->op.values[0]);
+    if (!qn || qn->op.kind != "Rope") throw Refusal(step.name + ": attention without its query's rotation.");
+    const View q = stored(qn->op.values[0]);
+    const Source& kc = p.sources[att->op.sources[0]];
+    Launch L;
+    L.kernel = "attend_split";
+    L.params = {{"m", m},
+                {"heads", (double)spec.heads},
+                {"kv_heads", (double)spec.kv_heads},
+                {"d", (double)spec.head_dim},
+                {"length", (double)kc.kind.r.length},
+                {"rotated", (double)qn->op.rope.rotated},
+                {"chunk", (double)attn.chunk},
+                {"max_splits", (double)attn.max_splits},
+                {"ldq", (double)q.ld},
+                {"q_off", (double)q.col},
+                {"scale", spec.scale}};
+    L.bufs = {q.base,
+              cos_t,
+              sin_t,
+              at(b.ints, src_name(att->op.sources[2]), step.name),
+              at(b.ints, src_name(att->op.sources[3]), step.name),
+              at(b.caches, kc.name, step.name),
+              at(b.caches, src_name(att->op.sources[1]), step.name),
+              attn.partials[0],
+              attn.partials[1],
+              attn.partials[2]};
+    return L;
+  }
+
+  if (kinds == std::vector<std::string>{"Combine"}) {
+    const Node* att = &p.nodes[step.work[0].node];
+    const AttnSpec& spec = att->op.attn;
+    const View out = stored(att->outputs[0]);
+    Launch L;
+    L.kernel = "attend_combine";
+    L.params = {{"m", m},
+                {"heads", (double)spec.heads},
+                {"d", (double)spec.head_dim},
+                {"chunk", (double)attn.chunk},
+                {"max_splits", (double)attn.max_splits},
+                {"ldo", (double)out.ld}};
+    L.bufs = {attn.partials[0], attn.partials[1], attn.partials[2],
+              at(b.ints, src_name(att->op.sources[2]), step.name), out.ptr()};
+    return L;
+  }
+
+  bool all_stores = !effects.empty();
+  for (const Node* n : effects)
+    if (n->op.kind != "KvStore") all_stores = false;
+  if (all_stores && effects.size() == 2) {
+    const Node* sk = effects[0];
+    const Node* sv = effects[1];
+    const Node* kn = recomputed_of(sk->op.values[0]);
+    if (!kn || kn->op.kind != "Rope") throw Refusal(step.name + ": keys stored without their rotation.");
+    const View kview = stored(kn->op.values[0]), vview = stored(sv->op.values[0]);
+    if (kview.base != vview.base) throw Refusal(step.name + ": keys and values are not one row.");
+    const Source& kc = p.sources[sk->op.sources[0]];
+    Launch L;
+    L.kernel = "kv_store_ring";
+    L.params = {{"m", m},
+                {"kv_heads", (double)kc.kind.r.kv_heads},
+                {"d", (double)kc.kind.r.head_dim},
+                {"length", (double)kc.kind.r.length},
+                {"rotated", (double)kn->op.rope.rotated},
+                {"ldq", (double)kview.ld},
+                {"k_off", (double)kview.col},
+                {"v_off", (double)vview.col}};
+    L.bufs = {kview.base,
+              cos_t,
+              sin_t,
+              at(b.ints, src_name(sk->op.sources[1]), step.name),
+              at(b.ints, src_name(sk->op.sources[2]), step.name),
+              at(b.caches, kc.name, step.name),
+              at(b.caches, src_name(sv->op.sources[0]), step.name)};
+    return L;
+  }
+
+  if (kinds == std::vector<std::string>{"Recompute"}) {
+    const Node* n = &p.nodes[step.work[0].node];
+    if (n->op.kind == "Gather") {
+      const Source& table = p.sources[n->op.sources[0]];
+      const Source& tok = p.sources[n->op.sources[1]];
+      const View y = stored(n->outputs[0]);
+      Launch L;
+      L.kernel = "gather";
+      L.params = {{"width", (double)table.kind.dims[1]}, {"m", m}, {"factor", n->op.f}};
+      L.bufs = {at(b.weights, table.name, step.name), at(b.ints, tok.name, step.name), y.ptr()};
+      return L;
+    }
+    if (n->op.kind == "ArgMax") {
+      const View x = stored(n->op.values[0]);
+      const View y = stored(n->outputs[0]);
+      Launch L;
+      L.kernel = "argmax";
+      L.params = {{"m", m}, {"n", (double)x.width}, {"ldx", (double)x.ld}};
+      L.bufs = {x.ptr(), y.ptr()};
+      return L;
+    }
+  }
+  throw Refusal(step.name + ": no kernel runs " + work_text(p, step));
+}
+
+uint64_t split_for(uint64_t n_rows, uint64_t k, uint64_t sms) {
+  for (uint64_t s : {1, 2, 4, 8})
+    if (n_rows * s >= sms * 48 || k / s < 1024) return s;
+  return 8;
+}
+
+namespace {
+
+// The [gate; up] step followed by the down step that recomputes
+// silu(gate) * up from their stored rows becomes the [gate; up] GEMV on
+// interleaved rows with the SiLU-gate epilogue, storing mlp_act, and the
+// down GEMV reading it.
+void silu_on_tiles(std::vector<Launch>& out, uint64_t f, uint64_t gu, uint64_t act) {
+  for (size_t i = 0; i + 1 < out.size(); ++i) {
+    Launch& a = out[i];
+    Launch& b = out[i + 1];
+    if (a.kernel == "gemv_rmsnorm" && a.bufs[3] == gu && a.param("n") == 2.0 * f &&
+        (b.kernel == "gemv_silu" || b.kernel == "gemv_silu_add") && b.bufs[1] == gu && b.param("up_off") == f) {
+      Launch na;
+      na.kernel = "gemv_rmsnorm_silu";
+      na.params = a.params;
+      na.set("ldy", (double)f);
+      na.bufs = {a.bufs[0], a.bufs[1], a.bufs[2], act};
+      Launch nb;
+      for (const auto& kv : b.params)
+        if (kv.first != "up_off") nb.params.push_back(kv);
+      nb.set("ldx", (double)f);
+      if (b.kernel == "gemv_silu_add") {
+        nb.kernel = "gemv_add";
+        nb.bufs = {b.bufs[0], act, b.bufs[2], b.bufs[3]};
+      } else {
+        nb.kernel = "gemv";
+        nb.bufs = {b.bufs[0], act, b.bufs[2]};
+      }
+      a = na;
+      b = nb;
+    }
+  }
+}
+
+// Over NVLink peer memory: a row-parallel projection scatters its partial
+// rows into every rank's exchange buffer (o: 0, down: 1) and leaves its
+// residual epilogue to the next GEMV, whose prologue adds the ranks'
+// partials in rank order to the residual, stores the new residual row and
+// normalizes it; the greedy candidates travel the same way.
+std::vector<Launch> tensor_parallel_peers(const std::vector<Launch>& in, const LlamaLaunchDesc& d,
+                                          uint64_t vocab_local) {
+  std::vector<Launch> out;
+  struct Pending {
+    int buf;
+    uint64_t r, y;
+    bool live;
+  };
+  std::optional<Pending> pending;
+  const uint64_t dm = d.full.d_model;
+  for (const Launch& L : in) {
+    if (L.kernel == "gemv_add") {
+      const int xbuf = !pending || pending->buf == 1 ? 0 : 1;
+      if (L.param("ldy") != dm || L.param("ldr") != dm)
+        throw Refusal("a row-parallel output that is not a whole row.");
+      Launch s;
+      s.kernel = "gemv_scatter";
+      s.params = {{"n", L.param("n")}, {"k", L.param("k")}, {"m", L.param("m")}, {"split", L.param("split")},
+                  {"ldx", L.param("ldx")}, {"xbuf", (double)xbuf}};
+      s.bufs = {L.bufs[0], L.bufs[1]};
+      out.push_back(s);
+      pending = Pending{xbuf, L.bufs[2], L.bufs[3], true};
+    } else if (pending && pending->live && (L.kernel == "gemv_rmsnorm" || L.kernel == "gemv_rmsnorm_silu") &&
+               L.bufs[1] == pending->y) {
+      Launch r;
+      r.kernel = L.kernel == "gemv_rmsnorm_silu" ? "gemv_reduce_rmsnorm_silu" : "gemv_reduce_rmsnorm";
+      for (const auto& kv : L.params)
+        if (kv.first != "ldx") r.params.push_back(kv);
+      r.set("ldr", (double)dm);
+      r.set("xbuf", (double)pending->buf);
+      r.bufs = {L.bufs[0], pending->r, L.bufs[2], pending->y, L.bufs[3]};
+      out.push_back(r);
+      pending->live = false;  // consumed; the buffer alternates on
+    } else if (L.kernel == "argmax") {
+      Launch s;
+      s.kernel = "argmax_scatter";
+      s.params = L.params;
+      s.set("offset", (double)(d.rank * vocab_local));
+      s.bufs = {L.bufs[0]};
+      out.push_back(s);
+      Launch g;
+      g.kernel = "argmax_gather_pick";
+      g.params = {{"m", (double)d.batch}};
+      g.bufs = {L.bufs[1]};
+      out.push_back(g);
+    } else {
+      out.push_back(L);
+    }
+  }
+  return out;
+}
+
+// With NCCL: the row-parallel projections' residual epilogues move after the
+// allreduce of their partial sums; the greedy pick gathers the shards'
+// candidates.
+std::vector<Launch> tensor_parallel_nccl(const std::vector<Launch>& in, const LlamaLaunchDesc& d,
+                                         uint64_t vocab_local) {
+  std::vector<Launch> out;
+  const uint64_t dm = d.full.d_model, m = d.batch;
+  for (const Launch& L : in) {
+    if (L.kernel == "gemv_add" || L.kernel == "gemv_silu_add") {
+      if (L.param("ldy") != dm || L.param("ldr") != dm)
+        throw Refusal("a row-parallel output that is not a whole row.");
+      Launch g;
+      g.kernel = L.kernel.substr(0, L.kernel.size() - 4);
+      for (const auto& kv : L.params)
+        if (kv.first != "ldr") g.params.push_back(kv);
+      g.bufs = {L.bufs[0], L.bufs[1], d.partial};
+      out.push_back(g);
+      Launch ar;
+      ar.kernel = "__allreduce__";
+      ar.params = {{"count", (double)(m * dm)}};
+      ar.bufs = {d.partial};
+      out.push_back(ar);
+      Launch add;
+      add.kernel = "add";
+      add.params = {{"n", (double)(m * dm)}};
+      add.bufs = {L.bufs[2], d.partial, L.bufs[3]};
+      out.push_back(add);
+    } else if (L.kernel == "argmax") {
+      Launch a;
+      a.kernel = "argmax_pairs";
+      a.params = L.params;
+      a.set("offset", (double)(d.rank * vocab_local));
+      a.bufs = {L.bufs[0], d.pairs};
+      out.push_back(a);
+      Launch g;
+      g.kernel = "__allgather__";
+      g.params = {{"count", (double)(2 * m)}};
+      g.bufs = {d.pairs, d.pairs_all};
+      out.push_back(g);
+      Launch p;
+      p.kernel = "argmax_pick";
+      p.params = {{"shards", (double)d.world}, {"m", (double)m}};
+      p.bufs = {d.pairs_all, L.bufs[1]};
+      out.push_back(p);
+    } else {
+      out.push_back(L);
+    }
+  }
+  return out;
+}
+
+// Each layer's KV store and split attention, when they bind the same row of
+// q/k/v, positions, slots and caches, become one attend_decode launch.
+std::vector<Launch> fuse_attention(const std::vector<Launch>& in) {
+  std::vector<Launch> out;
+  for (size_t i = 0; i < in.size(); ++i) {
+    if (i + 1 < in.size() && in[i].kernel == "kv_store_ring" && in[i + 1].kernel == "attend_split") {
+      const Launch& kv = in[i];
+      const Launch& at = in[i + 1];
+      bool same = kv.bufs[0] == at.bufs[0] &&
+                  std::equal(kv.bufs.begin() + 3, kv.bufs.begin() + 7, at.bufs.begin() + 3);
+      for (const char* k : {"ldq", "rotated", "d", "kv_heads", "length"})
+        if (kv.param(k) != at.param(k)) same = false;
+      if (same) {
+        Launch f;
+        f.kernel = "attend_decode";
+        f.params = at.params;
+        f.set("k_off", kv.param("k_off"));
+        f.set("v_off", kv.param("v_off"));
+        f.bufs = at.bufs;
+        out.push_back(f);
+        ++i;
+        continue;
+      }
+    }
+    out.push_back(in[i]);
+  }
+  return out;
+}
+
+}  // namespace
+
+std::vector<Launch> llama_launches(const LlamaLaunchDesc& d) {
+  const LlamaShape& full = d.full;
+  if (d.world == 0 || full.heads % d.world || full.kv_heads % d.world || full.ffn % d.world ||
+      full.vocab % d.world)
+    throw Refusal("the model does not split over " + std::to_string(d.world) + " ranks.");
+  LlamaShape s = full;  // this rank's shard
+  s.heads = full.heads / d.world;
+  s.kv_heads = full.kv_heads / d.world;
+  s.ffn = full.ffn / d.world;
+  const uint64_t m = d.batch, dm = s.d_model, qw = s.q_width(), kvw = s.kv_width(), f = s.ffn;
+  const uint64_t vocab_local = full.vocab / d.world;
+  const uint64_t layer_elems = (qw + 2 * kvw) * dm + dm * qw + 2 * f * dm + dm * f + 2 * dm;
+  const uint64_t embed_ptr = d.arena + 4 * s.layers * layer_elems;
+  const uint64_t final_norm_ptr = embed_ptr + 4 * full.vocab * full.d_model;
+
+  PlanOptions layer_opts;
+  layer_opts.sequence_rows = s.slots == 1 ? m : 1;
+  LlamaShape head_shape = full;
+  head_shape.vocab = vocab_local;
+  const Plan embed_plan = plan(PlanOptions{}, embed_program(full));
+  const Plan layer_plan = plan(layer_opts, layer_program(s));
+  const Plan head_plan = plan(PlanOptions{}, head_program(head_shape));
+
+  AttnBufs attn;
+  attn.chunk = d.chunk;
+  attn.max_splits = (s.positions + d.chunk - 1) / d.chunk;
+  for (int i = 0; i < 3; ++i) attn.partials[i] = d.part[i];
+  const std::map<std::string, uint64_t> ints = {{"token", d.tokens}, {"position", d.pos}, {"slot", d.slot}};
+
+  std::vector<Launch> out;
+  {
+    Binding eb;
+    eb.weights = {{"embed", embed_ptr}};
+    eb.ints = ints;
+    eb.m = m;
+    eb.values = {{"x", View{d.x, 0, dm, dm}}};
+    for (const Step& st : embed_plan.steps)
+      out.push_back(lower_step(embed_plan.program, st, eb, d.cos_t, d.sin_t, attn));
+  }
+  const uint64_t per_cache = 4 * s.slots * s.kv_heads * s.length * s.head_dim;
+  const uint64_t sizes[9] = {qw * dm, kvw * dm, kvw * dm, dm * qw, f * dm, f * dm, dm * f, dm, dm};
+  const char* names[9] = {"q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj", "attn_norm",
+                          "mlp_norm"};
+  for (uint64_t l = 0; l < s.layers; ++l) {
+    Binding b;
+    uint64_t at = d.arena + 4 * l * layer_elems;
+    for (int i = 0; i < 9; ++i) {
+      b.weights[names[i]] = at;
+      at += 4 * sizes[i];
+    }
+    b.ints = ints;
+    b.caches = {{"k_cache", d.kbase + l * per_cache}, {"v_cache", d.vbase + l * per_cache}};
+    b.m = m;
+    b.values = {{"x", View{d.x, 0, dm, dm}},
+                {"q", View{d.qkv, 0, qw + 2 * kvw, qw}},
+                {"k", View{d.qkv, qw, qw + 2 * kvw, kvw}},
+                {"v", View{d.qkv, qw + kvw, qw + 2 * kvw, kvw}},
+                {"attended", View{d.att, 0, qw, qw}},
+                {"x1", View{d.x1, 0, dm, dm}},
+                {"gate", View{d.gu, 0, 2 * f, f}},
+                {"up", View{d.gu, f, 2 * f, f}},
+                {"x2", View{d.x, 0, dm, dm}}};
+    for (const Step& st : layer_plan.steps)
+      out.push_back(lower_step(layer_plan.program, st, b, d.cos_t, d.sin_t, attn));
+  }
+  {
+    Binding hb;
+    hb.weights = {{"embed", embed_ptr + 4 * d.rank * vocab_local * full.d_model}, {"final_norm", final_norm_ptr}};
+    hb.ints = ints;
+    hb.m = m;
+    hb.values = {{"x", View{d.x, 0, dm, dm}},
+                 {"logits", View{d.logits, 0, vocab_local, vocab_local}},
+                 {"token", View{d.out_ids, 0, 1, 1}}};
+    for (const Step& st : head_plan.steps)
+      out.push_back(lower_step(head_plan.program, st, hb, d.cos_t, d.sin_t, attn));
+  }
+  if (d.gate_up_interleaved) silu_on_tiles(out, f, d.gu, d.act);
+  if (d.world > 1)
+    out = d.peer_exchange ? tensor_parallel_peers(out, d, vocab_local) : tensor_parallel_nccl(out, d, vocab_local);
+  if (d.fuse_attention) out = fuse_attention(out);
+  // The engine's greedy feedback: the ids become the next step's tokens and
+  // the positions advance, so replays decode on their own.
+  Launch adv;
+  adv.kernel = "advance";
+  adv.params = {{"m", (double)m}};
+  adv.bufs = {d.out_ids, d.tokens, d.pos};
+  out.push_back(adv);
+  for (Launch& L : out)  // split-K a GEMV: the streaming and batched kernels keep one
+    if (L.kernel.rfind("gemv", 0) == 0)
+      L.set("split", (double)(m <= 64 ? 1 : split_for((uint64_t)L.param("n"), (uint64_t)L.param("k"), d.sms)));
+  return out;
+}
+
+}  // namespace fkh

@@ -1,0 +1,114 @@
+/* furykernel-cuda's host side in C++ (libfurykernel_host.so): FuryKernel's
+ * programs, its planner and the lowering of a plan to launches of the CUDA
+ * target's kernel table, behind a C ABI.
+ *
+ * The reference computes these in Haskell before its target runs anything:
+ * the program a model is written as (FuryKernel.Program.Graph, Build:
+ * src/FuryKernel/Program/Graph.hs:299-360, Build.hs), the plan
+ * (FuryKernel.Program.Plan.plan, src/FuryKernel/Program/Plan.hs), and a
+ * backend's launches for the plan's steps (Backend.hs:203-228, the
+ * LoweredKernel list a backend runs). A FuryKernel.Cuda module binds the
+ * entries below where it would otherwise call its own planner on a program
+ * the CUDA target runs; the launch list it gets back names entries of
+ * libfurykernel_cuda.so's kernel table (fkc_kernel_find) with their
+ * parameters and buffers, ready for fkc_launch or a captured graph.
+ *
+ * Errors: every entry returns 0 (FKH_OK) or a nonzero code, and writes the
+ * refusal's text (the planner's or the lowering's words) into `err`
+ * (NUL-terminated, truncated to `err_cap` bytes) when `err` is not NULL. */
+#ifndef FURYKERNEL_HOST_H
+#define FURYKERNEL_HOST_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FKH_API __attribute__((visibility("default")))
+#else
+#define FKH_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  FKH_OK = 0,
+  FKH_ERR_ARGUMENT = 1, /* a refusal: the text says why */
+  FKH_ERR_SPACE = 2,    /* an output buffer too small: *len holds the size */
+  FKH_ERR_INTERNAL = 3
+};
+
+/* The library's ABI version (this header's FKH_ABI_VERSION). */
+#define FKH_ABI_VERSION 1
+FKH_API int fkh_abi_version(void);
+
+/* A Llama-shaped model (the shapes of the programs the engine plans). */
+typedef struct {
+  uint64_t d_model, heads, kv_heads, head_dim, ffn, vocab, layers;
+  double theta, eps;
+  uint64_t slots, length, positions;
+} fkh_llama_shape;
+
+/* The planner's options (PlanOptions, src/FuryKernel/Program/Plan.hs:243-268). */
+typedef struct {
+  int horizontal, gated, store_gelus;
+  uint64_t sequence_rows;
+} fkh_plan_options;
+
+/* Texts: a program as the reference's renderProgram lays it out
+ * (Graph.hs:445-528) and a plan as renderPlan does (Plan.hs:815-843). The
+ * text is written to buf (NUL-terminated) when cap is large enough; *len is
+ * its length without the NUL either way (FKH_ERR_SPACE when it did not fit).
+ * which: 0 the embedding, 1 one decoder layer, 2 the head. */
+FKH_API int fkh_llama_program_text(const fkh_llama_shape *shape, int which, char *buf, size_t cap, size_t *len, char *err,
+                           size_t err_cap);
+/* Parses a program text (the renderer's layout) and renders it back. */
+FKH_API int fkh_program_roundtrip(const char *program_text, char *buf, size_t cap, size_t *len, char *err, size_t err_cap);
+/* Parses a program text, plans it with the options and renders the plan. */
+FKH_API int fkh_plan_text(const char *program_text, const fkh_plan_options *opts, char *buf, size_t cap, size_t *len,
+                  char *err, size_t err_cap);
+
+/* The Llama engine's decode step: the shape, the batch, this rank of the
+ * tensor-parallel group, the choices, and the device addresses of every
+ * buffer the launches bind (furykernel_b200/engine.py's Llama holds the
+ * same fields). */
+typedef struct {
+  fkh_llama_shape full; /* the whole model; each rank holds heads, kv_heads, ffn and vocab / world */
+  uint64_t batch, rank, world, sms, chunk;
+  int gate_up_interleaved, peer_exchange, fuse_attention;
+  /* the weight arena: per layer q k v o gate up down attn_norm mlp_norm,
+   * then the whole embedding table and the final norm; the Ring KV arena's
+   * key and value bases (fkc_kv_arena) */
+  uint64_t arena, kbase, vbase;
+  uint64_t cos_t, sin_t;           /* fkc_rope_tables */
+  uint64_t tokens, pos, slot;      /* [batch] u32 each */
+  uint64_t x, x1, qkv, att, gu, act, logits, out_ids;
+  uint64_t partial, pairs, pairs_all; /* NCCL tensor parallelism */
+  uint64_t part[3];                   /* split attention's partials */
+} fkh_llama_desc;
+
+/* A launch list: kernel names of the CUDA target's table, parameters by
+ * name (numbers as double: every table parameter is an integer below 2^53
+ * or an f32), buffers as device addresses in declaration order. Two
+ * pseudo-kernels stand for NCCL calls: "__allreduce__" (count; the buffer
+ * summed in place) and "__allgather__" (count; send, receive). */
+typedef struct fkh_launches fkh_launches;
+
+FKH_API int fkh_llama_launches(const fkh_llama_desc *desc, fkh_launches **out, char *err, size_t err_cap);
+FKH_API size_t fkh_launches_count(const fkh_launches *l);
+FKH_API const char *fkh_launch_kernel(const fkh_launches *l, size_t i);
+FKH_API size_t fkh_launch_param_count(const fkh_launches *l, size_t i);
+FKH_API const char *fkh_launch_param_name(const fkh_launches *l, size_t i, size_t j);
+FKH_API double fkh_launch_param_value(const fkh_launches *l, size_t i, size_t j);
+FKH_API size_t fkh_launch_buf_count(const fkh_launches *l, size_t i);
+FKH_API uint64_t fkh_launch_buf(const fkh_launches *l, size_t i, size_t j);
+FKH_API void fkh_launches_free(fkh_launches *l);
+
+/* Split-K for a GEMV of n rows of k on `sms` SMs (the chunked kernel's). */
+FKH_API uint64_t fkh_split_for(uint64_t n_rows, uint64_t k, uint64_t sms);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

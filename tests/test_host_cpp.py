@@ -1,0 +1,230 @@
+"""The C++ host library (libfurykernel_host.so, include/furykernel_host.h)
+against the Python restatement of the same programs, planner and lowering,
+on the CPU: the rendered programs, the plans of the reference's golden
+programs (test/Test/FuryKernel/ProgramTest.hs) under every option set, and
+the Llama engine's whole decode-step launch list for every configuration
+the tests and the bench run (addresses are stand-ins; nothing runs)."""
+
+import ctypes
+import dataclasses
+import math
+from types import SimpleNamespace
+
+import pytest
+
+from furykernel_b200 import _host as H
+from furykernel_b200 import _native as N
+from furykernel_b200.engine import Llama
+from furykernel_b200.program import plan as PL
+from furykernel_b200.program.build import program
+from furykernel_b200.program.graph import render_program, whole_row
+from furykernel_b200.program.llama import LlamaShape, embed_program, head_program, layer_program
+
+from tests.test_program import LAYER_PLAN, OPTION_SETS, two_tiles
+from tests.test_program import head_program as golden_head
+from tests.test_program import layer as golden_layer
+
+SHAPES = [
+    LlamaShape(),
+    LlamaShape(d_model=512, heads=4, kv_heads=4, head_dim=128, ffn=1024, vocab=3000, layers=2, slots=3, length=96,
+               positions=96),
+    LlamaShape(d_model=64, heads=4, kv_heads=2, head_dim=8, ffn=48, vocab=40, layers=2, slots=1, length=16,
+               positions=16),
+    LlamaShape(d_model=128, heads=8, kv_heads=8, head_dim=16, ffn=344, vocab=512, layers=1, theta=500000.0,
+               eps=1e-6, slots=2, length=40, positions=64),
+]
+
+
+def doubled():
+    b = program("doubled")
+    x = b.input("x", whole_row(4))
+    w = b.weight("w", [4, 4])
+    y = x
+    for k in range(1, 41):
+        y = b.add(f"d{k}", y, y)
+    b.output("y", b.linear("y", w, 0, y))
+    return b.done()
+
+
+GOLDEN_PROGRAMS = [golden_layer(False), golden_layer(True), golden_head(), two_tiles(), doubled()]
+
+
+def test_library_exports_the_header():
+    L = H.lib()
+    header = open(__file__.rsplit("/tests/", 1)[0] + "/include/furykernel_host.h").read()
+    import re
+
+    names = re.findall(r"\b(fkh_[a-z_0-9]+)\s*\(", header)
+    assert len(names) >= 14
+    for n in names:
+        assert hasattr(L, n), n
+    assert L.fkh_abi_version() == H.ABI_VERSION
+
+
+@pytest.mark.parametrize("s", SHAPES, ids=range(len(SHAPES)))
+@pytest.mark.parametrize("which,build", [("embed", embed_program), ("layer", layer_program),
+                                         ("head", head_program)])
+def test_llama_programs_render_alike(s, which, build):
+    assert H.llama_program_text(s, which) == render_program(build(s))
+
+
+@pytest.mark.parametrize("i", range(len(GOLDEN_PROGRAMS)))
+def test_golden_programs_parse_back(i):
+    text = render_program(GOLDEN_PROGRAMS[i])
+    assert H.program_roundtrip(text) == text
+
+
+def test_layer_plan_golden():
+    # ProgramTest.hs:559-640, planned by the library.
+    assert H.plan_text(render_program(golden_layer(False))) == LAYER_PLAN
+
+
+@pytest.mark.parametrize("opts", OPTION_SETS, ids=lambda o: f"h{int(o.horizontal)}g{int(o.gated)}"
+                         f"s{int(o.store_gelus)}r{o.sequence_rows}")
+@pytest.mark.parametrize("i", range(len(GOLDEN_PROGRAMS)))
+def test_golden_programs_plan_alike(i, opts):
+    p = GOLDEN_PROGRAMS[i]
+    got = H.plan_text(render_program(p), opts.horizontal, opts.gated, opts.store_gelus, opts.sequence_rows)
+    assert got == PL.render_plan(PL.plan(opts, p))
+
+
+@pytest.mark.parametrize("s", SHAPES, ids=range(len(SHAPES)))
+@pytest.mark.parametrize("rows", [1, 4, 64])
+def test_llama_programs_plan_alike(s, rows):
+    for build in (embed_program, layer_program, head_program):
+        p = build(s)
+        assert H.plan_text(render_program(p), sequence_rows=rows) == \
+            PL.render_plan(PL.plan(PL.PlanOptions(sequence_rows=rows), p))
+
+
+def test_refusals_carry_text():
+    with pytest.raises(N.Refused, match="expected .program"):
+        H.program_roundtrip("nonsense")
+    with pytest.raises(N.Refused):
+        H.plan_text(render_program(two_tiles()), sequence_rows=0)
+
+
+def test_text_entry_reports_the_size_it_needs():
+    L = H.lib()
+    text = render_program(two_tiles()).encode()
+    n = ctypes.c_size_t(0)
+    buf = ctypes.create_string_buffer(8)
+    rc = L.fkh_program_roundtrip(text, buf, 8, ctypes.byref(n), None, 0)
+    assert rc == H.FKH_ERR_SPACE and n.value == len(text)
+
+
+def test_split_for_alike():
+    from furykernel_b200.engine import split_for
+
+    for n in (1, 512, 4096, 12288, 22016, 32000):
+        for k in (64, 1024, 4096, 11008):
+            for sms in (132, 148):
+                assert H.split_for(n, k, sms) == split_for(n, k, sms)
+
+
+class Buf:
+    """A stand-in device buffer: an address."""
+
+    def __init__(self, ptr):
+        self.ptr = ptr
+
+    def __int__(self):
+        return self.ptr
+
+
+def fake_engine(full, batch, rank=0, world=1, peer_exchange=True, fuse_attention=None, sms=148, chunk=32):
+    """A Llama with the attributes its launch lists read, at stand-in
+    addresses (no device): the same decisions as its constructor."""
+    e = object.__new__(Llama)
+    s = dataclasses.replace(full, heads=full.heads // world, kv_heads=full.kv_heads // world,
+                            ffn=full.ffn // world)
+    e.full, e.s, e.m, e.rank, e.world = full, s, batch, rank, world
+    e.ctx = SimpleNamespace(sms=sms)
+    e.gate_up_interleaved = batch <= 64
+    e.peer_exchange = world > 1 and batch <= 4 and peer_exchange
+    e.vocab_local = full.vocab // world
+    e.plans = {
+        "embed": PL.plan(PL.DEFAULT, embed_program(full)),
+        "layer": PL.plan(PL.PlanOptions(sequence_rows=batch if s.slots == 1 else 1), layer_program(s)),
+        "head": PL.plan(PL.DEFAULT, head_program(dataclasses.replace(full, vocab=e.vocab_local))),
+    }
+    d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
+    e.layer_elems = (qw + 2 * kvw) * d + d * qw + 2 * f * d + d * f + 2 * d
+    at = iter(range(1, 100))
+    e.arena = Buf(1 << 44)
+    e.kbase, e.vbase = 2 << 44, 3 << 44
+    for name in ("cos", "sin", "tokens", "pos", "slot", "out_ids", "x", "x1", "partial", "qkv", "att", "gu",
+                 "act", "logits", "pairs", "pairs_all"):
+        setattr(e, name, Buf((4 << 44) + (next(at) << 32)))
+    e.chunk = chunk
+    e.max_splits = (s.positions + chunk - 1) // chunk
+    e.part = [Buf((5 << 44) + (i << 32)) for i in range(3)]
+    if fuse_attention is None:
+        fuse_attention = batch <= 4
+    e.fuse_attention = fuse_attention and batch <= 64
+    return e
+
+
+def small(batch, layers=2, d=512, heads=4, ffn=1024, vocab=3000, length=96):
+    return LlamaShape(d_model=d, heads=heads, kv_heads=heads, head_dim=128, ffn=ffn, vocab=vocab, layers=layers,
+                      slots=batch, length=length, positions=length)
+
+
+def tp_shape(batch):
+    return LlamaShape(d_model=512, heads=8, kv_heads=8, head_dim=128, ffn=1024, vocab=3000, layers=2, slots=batch,
+                      length=96, positions=96)
+
+
+CASES = (
+    # the engine's decode tests: batch, fused
+    [(small(b), b, 0, 1, True, f) for b, f in ((1, True), (3, True), (2, True), (5, True), (9, True), (20, True),
+                                               (3, False), (9, False), (64, None), (65, None), (100, None))]
+    # smoke
+    + [(LlamaShape(d_model=256, heads=2, kv_heads=2, head_dim=128, ffn=512, vocab=500, layers=2, slots=b,
+                   length=64, positions=64), b, 0, 1, True, None) for b in (1, 5)]
+    # tensor parallelism: every rank, over peer memory and over NCCL
+    + [(tp_shape(b), b, r, w, peer, None) for w in (2, 4, 8) for r in range(w) for b in (1, 3, 16)
+       for peer in (True, False)]
+    # the bench's configs: the 7B-shaped model at its batches, one and eight ranks
+    + [(LlamaShape(layers=32, slots=b, length=2304, positions=2304), b, 0, 1, True, None) for b in (1, 4, 16, 64)]
+    + [(LlamaShape(layers=32, slots=1, length=4096, positions=4096), 1, r, 8, True, None) for r in (0, 7)]
+    + [(LlamaShape(layers=1, slots=b, length=2304, positions=2304), b, 0, 1, True, f) for b in (1, 16)
+       for f in (True, False)]
+    # a GQA model over a ring of one slot
+    + [(SHAPES[2], 1, 0, 1, True, None),
+       (dataclasses.replace(SHAPES[2], slots=4), 4, 0, 1, True, None)]
+    + [(SHAPES[2], 1, r, 2, p, None) for r in (0, 1) for p in (True, False)]
+)
+
+
+@pytest.mark.parametrize("case", range(len(CASES)))
+def test_decode_launches_alike(case):
+    full, batch, rank, world, peer, fuse = CASES[case]
+    e = fake_engine(full, batch, rank, world, peer, fuse)
+    want = e._launches_restated()
+    got = e._launches()
+    assert [L.kernel for L in got] == [L.kernel for L in want]
+    for g, w in zip(got, want):
+        assert g.bufs == w.bufs, (g.kernel, g.bufs, w.bufs)
+        assert g.params == w.params, (g.kernel, g.params, w.params)
+        for k, v in w.params.items():  # floats keep their bits (f32 parameters)
+            if isinstance(v, float):
+                assert math.isclose(g.params[k], v, rel_tol=0, abs_tol=0) or g.params[k] == v
+
+
+def test_unlowerable_steps_are_refused_alike():
+    # A ring of one slot shorter than a batch's rows has staged stores: no kernel.
+    full = LlamaShape(d_model=64, heads=4, kv_heads=2, head_dim=8, ffn=48, vocab=40, layers=1, slots=1, length=4,
+                      positions=16)
+    e = fake_engine(full, 8)
+    with pytest.raises(N.Refused):
+        e._launches_restated()
+    with pytest.raises(N.Refused, match="no kernel runs"):
+        e._launches()
+
+
+def test_uneven_shards_are_refused():
+    with pytest.raises(N.Refused, match="does not split over 3 ranks"):
+        e = fake_engine(tp_shape(1), 1, 0, 1)
+        e.world = 3
+        e._launches()
