@@ -85,11 +85,20 @@ def build_host(verbose: bool = False) -> str:
     deps = srcs + glob.glob(os.path.join(HOST, "*.h")) + [os.path.join(HERE, "..", "include", "furykernel_host.h")]
     if os.path.exists(HOST_LIB) and all(os.path.getmtime(d) <= os.path.getmtime(HOST_LIB) for d in deps):
         return HOST_LIB
+    # Several processes (the ranks of a tensor-parallel run) may find the
+    # library stale at once: each builds its own file and renames it into
+    # place, so that no process loads a half-written library.
+    tmp = f"{HOST_LIB}.{os.getpid()}.tmp"
     cmd = ["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra", "-Wno-unused-parameter",
-           "-fvisibility=hidden", *srcs, "-o", HOST_LIB]
+           "-fvisibility=hidden", *srcs, "-o", tmp]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
-    subprocess.run(cmd, check=True)
+    try:
+        subprocess.run(cmd, check=True)
+        os.replace(tmp, HOST_LIB)
+    finally:
+        if os.path.exists(tmp):
+            os.remove(tmp)
     return HOST_LIB
 
 
