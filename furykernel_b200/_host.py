@@ -59,6 +59,8 @@ def lib():
         L.fkh_plan_text.argtypes = [ctypes.c_char_p, ctypes.POINTER(PlanOptions)] + text_args
         L.fkh_llama_launches.argtypes = [ctypes.POINTER(Desc), ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p,
                                          ctypes.c_size_t]
+        L.fkh_llama_prefill_launches.argtypes = [ctypes.POINTER(Desc), ctypes.POINTER(PrefillDesc), ctypes.c_uint64,
+                                                 ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p, ctypes.c_size_t]
         L.fkh_launches_count.argtypes = [ctypes.c_void_p]
         L.fkh_launches_count.restype = ctypes.c_size_t
         for f in ("fkh_launch_param_count", "fkh_launch_buf_count"):
@@ -124,10 +126,7 @@ def split_for(n_rows: int, k: int, sms: int) -> int:
     return int(lib().fkh_split_for(n_rows, k, sms))
 
 
-def llama_launches(full, batch: int, rank: int, world: int, sms: int, chunk: int, gate_up_interleaved: bool,
-                   peer_exchange: bool, fuse_attention: bool, addrs: dict) -> list:
-    """The decode step's launch list: (kernel, params dict, bufs list)
-    triples, params as ints where they are integers."""
+def _desc(full, batch, rank, world, sms, chunk, gate_up_interleaved, peer_exchange, fuse_attention, addrs) -> Desc:
     d = Desc()
     d.full = shape(full)
     d.batch, d.rank, d.world, d.sms, d.chunk = batch, rank, world, sms, chunk
@@ -137,10 +136,16 @@ def llama_launches(full, batch: int, rank: int, world: int, sms: int, chunk: int
         setattr(d, n, int(addrs.get(n, 0)))
     for i, p in enumerate(addrs["part"]):
         d.part[i] = int(p)
+    return d
+
+
+def _collect(call, *args) -> list:
+    """A launch list from an entry that makes one: (kernel, params dict,
+    bufs list) triples, params as ints where they are integers."""
     L = lib()
     h = ctypes.c_void_p()
     err = ctypes.create_string_buffer(1024)
-    _check(L.fkh_llama_launches(ctypes.byref(d), ctypes.byref(h), err, len(err)), err)
+    _check(call(*args, ctypes.byref(h), err, len(err)), err)
     try:
         out = []
         for i in range(L.fkh_launches_count(h)):
@@ -153,3 +158,33 @@ def llama_launches(full, batch: int, rank: int, world: int, sms: int, chunk: int
         return out
     finally:
         L.fkh_launches_free(h)
+
+
+def llama_launches(full, batch: int, rank: int, world: int, sms: int, chunk: int, gate_up_interleaved: bool,
+                   peer_exchange: bool, fuse_attention: bool, addrs: dict) -> list:
+    """The decode step's launch list (fkh_llama_launches)."""
+    d = _desc(full, batch, rank, world, sms, chunk, gate_up_interleaved, peer_exchange, fuse_attention, addrs)
+    return _collect(lib().fkh_llama_launches, ctypes.byref(d))
+
+
+PREFILL_ADDRS = ("w_hi", "w_lo", "tokens", "pos", "slot", "x", "a", "a_hi", "a_lo", "qkv", "att", "tmp", "x1",
+                 "gu", "act")
+
+
+class PrefillDesc(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint64) for n in ("rows", "chunk", "positions")] + [("one_slot", ctypes.c_int)] + \
+               [(n, ctypes.c_uint64) for n in PREFILL_ADDRS] + [("part", ctypes.c_uint64 * 3)]
+
+
+def prefill_launches(decode: tuple, rows: int, chunk: int, positions: int, one_slot: bool, addrs: dict,
+                     m: int) -> list:
+    """The prefill of m rows (fkh_llama_prefill_launches); `decode` holds
+    llama_launches' arguments for the engine in front of it."""
+    d = _desc(*decode)
+    p = PrefillDesc()
+    p.rows, p.chunk, p.positions, p.one_slot = rows, chunk, positions, int(one_slot)
+    for n in PREFILL_ADDRS:
+        setattr(p, n, int(addrs[n]))
+    for i, a in enumerate(addrs["part"]):
+        p.part[i] = int(a)
+    return _collect(lib().fkh_llama_prefill_launches, ctypes.byref(d), ctypes.byref(p), m)

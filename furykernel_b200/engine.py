@@ -379,9 +379,13 @@ class Llama:
         head lowered to table launches, then the rewrites below."""
         from . import _host
 
-        return [Launch(k, p, b) for k, p, b in _host.llama_launches(
-            self.full, self.m, self.rank, self.world, self.ctx.sms, self.chunk, self.gate_up_interleaved,
-            self.peer_exchange, self.fuse_attention, self.launch_addresses())]
+        return [Launch(k, p, b) for k, p, b in _host.llama_launches(*self.launch_args())]
+
+    def launch_args(self) -> tuple:
+        """fkh_llama_desc's fields: the shape, the batch, the rank, the
+        choices and the addresses."""
+        return (self.full, self.m, self.rank, self.world, self.ctx.sms, self.chunk, self.gate_up_interleaved,
+                self.peer_exchange, self.fuse_attention, self.launch_addresses())
 
     def _launches_restated(self) -> list:
         """The same launch list in Python (the restatement the host

@@ -268,6 +268,27 @@ struct LlamaLaunchDesc {
 };
 
 std::vector<Launch> llama_launches(const LlamaLaunchDesc& d);
+// This rank's shard of the model (heads, KV heads and ffn over the ranks),
+// refused when the model does not split evenly.
+LlamaShape shard_of(const LlamaLaunchDesc& d);
+// A layer's floats in the weight arena, and the addresses of its weights
+// (q k v o gate up down attn_norm mlp_norm, in that order).
+uint64_t layer_elems(const LlamaShape& s);
+std::map<std::string, uint64_t> layer_weights(const LlamaShape& s, uint64_t arena, uint64_t l);
 uint64_t split_for(uint64_t n_rows, uint64_t k, uint64_t sms);
+
+// The prompt prefill of up to `rows` rows in front of a decode step
+// (furykernel_b200/prefill.py): its row buffers, the weights' TF32 halves
+// (two arenas laid out as the weight arena) and its choices.
+struct PrefillDesc {
+  uint64_t rows = 1, chunk = 32, positions = 1;
+  bool one_slot = false;  // every run's rows in one slot: the query-tiled prompt attention
+  uint64_t w_hi = 0, w_lo = 0;
+  uint64_t tokens = 0, pos = 0, slot = 0;
+  uint64_t x = 0, a = 0, a_hi = 0, a_lo = 0, qkv = 0, att = 0, tmp = 0, x1 = 0, gu = 0, act = 0;
+  uint64_t part[3] = {0, 0, 0};
+};
+
+std::vector<Launch> prefill_launches(const LlamaLaunchDesc& decode, const PrefillDesc& p, uint64_t m);
 
 }  // namespace fkh

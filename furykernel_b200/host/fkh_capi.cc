@@ -67,6 +67,42 @@ fkh::LlamaShape shape_of(const fkh_llama_shape& s) {
 
 bool valid(const fkh_launches* l, size_t i) { return l && i < l->list.size(); }
 
+fkh::LlamaLaunchDesc desc_of(const fkh_llama_desc& desc) {
+  fkh::LlamaLaunchDesc d;
+  d.full = shape_of(desc.full);
+  d.batch = desc.batch;
+  d.rank = desc.rank;
+  d.world = desc.world;
+  d.sms = desc.sms;
+  d.chunk = desc.chunk;
+  if (!d.batch || !d.world || d.rank >= d.world || !d.sms || !d.chunk)
+    throw fkh::Refusal("batch, world, sms and chunk must be positive and rank below world.");
+  d.gate_up_interleaved = desc.gate_up_interleaved != 0;
+  d.peer_exchange = desc.peer_exchange != 0;
+  d.fuse_attention = desc.fuse_attention != 0;
+  d.arena = desc.arena;
+  d.kbase = desc.kbase;
+  d.vbase = desc.vbase;
+  d.cos_t = desc.cos_t;
+  d.sin_t = desc.sin_t;
+  d.tokens = desc.tokens;
+  d.pos = desc.pos;
+  d.slot = desc.slot;
+  d.x = desc.x;
+  d.x1 = desc.x1;
+  d.qkv = desc.qkv;
+  d.att = desc.att;
+  d.gu = desc.gu;
+  d.act = desc.act;
+  d.logits = desc.logits;
+  d.out_ids = desc.out_ids;
+  d.partial = desc.partial;
+  d.pairs = desc.pairs;
+  d.pairs_all = desc.pairs_all;
+  for (int i = 0; i < 3; ++i) d.part[i] = desc.part[i];
+  return d;
+}
+
 }  // namespace
 
 extern "C" {
@@ -116,40 +152,42 @@ int fkh_llama_launches(const fkh_llama_desc* desc, fkh_launches** out, char* err
   return guarded(err, err_cap, [&] {
     if (!desc || !out) throw fkh::Refusal("no descriptor or no place for the launches.");
     *out = nullptr;
-    fkh::LlamaLaunchDesc d;
-    d.full = shape_of(desc->full);
-    d.batch = desc->batch;
-    d.rank = desc->rank;
-    d.world = desc->world;
-    d.sms = desc->sms;
-    d.chunk = desc->chunk;
-    if (!d.batch || !d.world || d.rank >= d.world || !d.sms || !d.chunk)
-      throw fkh::Refusal("batch, world, sms and chunk must be positive and rank below world.");
-    d.gate_up_interleaved = desc->gate_up_interleaved != 0;
-    d.peer_exchange = desc->peer_exchange != 0;
-    d.fuse_attention = desc->fuse_attention != 0;
-    d.arena = desc->arena;
-    d.kbase = desc->kbase;
-    d.vbase = desc->vbase;
-    d.cos_t = desc->cos_t;
-    d.sin_t = desc->sin_t;
-    d.tokens = desc->tokens;
-    d.pos = desc->pos;
-    d.slot = desc->slot;
-    d.x = desc->x;
-    d.x1 = desc->x1;
-    d.qkv = desc->qkv;
-    d.att = desc->att;
-    d.gu = desc->gu;
-    d.act = desc->act;
-    d.logits = desc->logits;
-    d.out_ids = desc->out_ids;
-    d.partial = desc->partial;
-    d.pairs = desc->pairs;
-    d.pairs_all = desc->pairs_all;
-    for (int i = 0; i < 3; ++i) d.part[i] = desc->part[i];
     auto l = std::make_unique<fkh_launches>();
-    l->list = fkh::llama_launches(d);
+    l->list = fkh::llama_launches(desc_of(*desc));
+    *out = l.release();
+    return FKH_OK;
+  });
+}
+
+int fkh_llama_prefill_launches(const fkh_llama_desc* desc, const fkh_prefill_desc* prefill, uint64_t m,
+                               fkh_launches** out, char* err, size_t err_cap) {
+  return guarded(err, err_cap, [&] {
+    if (!desc || !prefill || !out) throw fkh::Refusal("no descriptor or no place for the launches.");
+    *out = nullptr;
+    fkh::PrefillDesc p;
+    p.rows = prefill->rows;
+    p.chunk = prefill->chunk;
+    p.positions = prefill->positions;
+    if (!p.rows || !p.chunk || !p.positions) throw fkh::Refusal("prefill: rows, chunk and positions must be positive.");
+    p.one_slot = prefill->one_slot != 0;
+    p.w_hi = prefill->w_hi;
+    p.w_lo = prefill->w_lo;
+    p.tokens = prefill->tokens;
+    p.pos = prefill->pos;
+    p.slot = prefill->slot;
+    p.x = prefill->x;
+    p.a = prefill->a;
+    p.a_hi = prefill->a_hi;
+    p.a_lo = prefill->a_lo;
+    p.qkv = prefill->qkv;
+    p.att = prefill->att;
+    p.tmp = prefill->tmp;
+    p.x1 = prefill->x1;
+    p.gu = prefill->gu;
+    p.act = prefill->act;
+    for (int i = 0; i < 3; ++i) p.part[i] = prefill->part[i];
+    auto l = std::make_unique<fkh_launches>();
+    l->list = fkh::prefill_launches(desc_of(*desc), p, m);
     *out = l.release();
     return FKH_OK;
   });

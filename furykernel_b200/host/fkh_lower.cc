@@ -442,7 +442,7 @@ std::vector<Launch> fuse_attention(const std::vector<Launch>& in) {
 
 }  // namespace
 
-std::vector<Launch> llama_launches(const LlamaLaunchDesc& d) {
+LlamaShape shard_of(const LlamaLaunchDesc& d) {
   const LlamaShape& full = d.full;
   if (d.world == 0 || full.heads % d.world || full.kv_heads % d.world || full.ffn % d.world ||
       full.vocab % d.world)
@@ -451,10 +451,34 @@ std::vector<Launch> llama_launches(const LlamaLaunchDesc& d) {
   s.heads = full.heads / d.world;
   s.kv_heads = full.kv_heads / d.world;
   s.ffn = full.ffn / d.world;
+  return s;
+}
+
+uint64_t layer_elems(const LlamaShape& s) {
+  const uint64_t dm = s.d_model, qw = s.q_width(), kvw = s.kv_width(), f = s.ffn;
+  return (qw + 2 * kvw) * dm + dm * qw + 2 * f * dm + dm * f + 2 * dm;
+}
+
+std::map<std::string, uint64_t> layer_weights(const LlamaShape& s, uint64_t arena, uint64_t l) {
+  const uint64_t dm = s.d_model, qw = s.q_width(), kvw = s.kv_width(), f = s.ffn;
+  const uint64_t sizes[9] = {qw * dm, kvw * dm, kvw * dm, dm * qw, f * dm, f * dm, dm * f, dm, dm};
+  const char* names[9] = {"q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj", "attn_norm",
+                          "mlp_norm"};
+  std::map<std::string, uint64_t> w;
+  uint64_t at = arena + 4 * l * layer_elems(s);
+  for (int i = 0; i < 9; ++i) {
+    w[names[i]] = at;
+    at += 4 * sizes[i];
+  }
+  return w;
+}
+
+std::vector<Launch> llama_launches(const LlamaLaunchDesc& d) {
+  const LlamaShape& full = d.full;
+  const LlamaShape s = shard_of(d);
   const uint64_t m = d.batch, dm = s.d_model, qw = s.q_width(), kvw = s.kv_width(), f = s.ffn;
   const uint64_t vocab_local = full.vocab / d.world;
-  const uint64_t layer_elems = (qw + 2 * kvw) * dm + dm * qw + 2 * f * dm + dm * f + 2 * dm;
-  const uint64_t embed_ptr = d.arena + 4 * s.layers * layer_elems;
+  const uint64_t embed_ptr = d.arena + 4 * s.layers * layer_elems(s);
   const uint64_t final_norm_ptr = embed_ptr + 4 * full.vocab * full.d_model;
 
   PlanOptions layer_opts;
@@ -482,16 +506,9 @@ std::vector<Launch> llama_launches(const LlamaLaunchDesc& d) {
       out.push_back(lower_step(embed_plan.program, st, eb, d.cos_t, d.sin_t, attn));
   }
   const uint64_t per_cache = 4 * s.slots * s.kv_heads * s.length * s.head_dim;
-  const uint64_t sizes[9] = {qw * dm, kvw * dm, kvw * dm, dm * qw, f * dm, f * dm, dm * f, dm, dm};
-  const char* names[9] = {"q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj", "attn_norm",
-                          "mlp_norm"};
   for (uint64_t l = 0; l < s.layers; ++l) {
     Binding b;
-    uint64_t at = d.arena + 4 * l * layer_elems;
-    for (int i = 0; i < 9; ++i) {
-      b.weights[names[i]] = at;
-      at += 4 * sizes[i];
-    }
+    b.weights = layer_weights(s, d.arena, l);
     b.ints = ints;
     b.caches = {{"k_cache", d.kbase + l * per_cache}, {"v_cache", d.vbase + l * per_cache}};
     b.m = m;

@@ -1,0 +1,149 @@
+// The prompt prefill's launch list: every prompt row through the layers at
+// once, the decode layer's plan run over m rows with the linears as
+// tcgen05 3xTF32 GEMM tiles (gemm_tf32x3) instead of GEMVs. The decode
+// step's own launches are the templates of the gather, the KV stores and
+// the attention (their shapes, tables and caches).
+#include "fkh.h"
+
+namespace fkh {
+
+namespace {
+
+Launch make(const std::string& kernel, std::vector<std::pair<std::string, double>> params,
+            std::vector<uint64_t> bufs) {
+  Launch L;
+  L.kernel = kernel;
+  L.params = std::move(params);
+  L.bufs = std::move(bufs);
+  return L;
+}
+
+// A launch's parameters with some replaced (the rest keep their order).
+Launch with(const Launch& t, const std::vector<std::pair<std::string, double>>& changes, std::vector<uint64_t> bufs) {
+  Launch L = t;
+  for (const auto& [k, v] : changes) L.set(k, v);
+  L.bufs = std::move(bufs);
+  return L;
+}
+
+}  // namespace
+
+std::vector<Launch> prefill_launches(const LlamaLaunchDesc& d, const PrefillDesc& p, uint64_t m) {
+  if (m < 1 || m > p.rows)
+    throw Refusal("prefill: " + std::to_string(m) + " rows, outside 1.." + std::to_string(p.rows) + ".");
+  const LlamaShape s = shard_of(d);
+  const uint64_t dm = s.d_model, qw = s.q_width(), kvw = s.kv_width(), f = s.ffn, nq = qw + 2 * kvw;
+  const uint64_t max_splits = (p.positions + p.chunk - 1) / p.chunk;
+  const std::vector<Launch> decode = llama_launches(d);
+
+  std::map<std::string, std::vector<const Launch*>> by;
+  for (const Launch& L : decode) by[L.kernel].push_back(&L);
+  auto need = [&](const std::string& k, uint64_t i) -> const Launch& {
+    auto it = by.find(k);
+    if (it == by.end() || it->second.size() <= i) throw Refusal("prefill: the decode step has no " + k + " launch.");
+    return *it->second[i];
+  };
+  // Where the decode step folded each layer's store into its attention,
+  // split the launches back into the two steps.
+  std::vector<Launch> unfused;
+  if (by.count("attend_decode")) {
+    unfused.reserve(2 * by["attend_decode"].size());
+    for (const Launch* L : by["attend_decode"]) {
+      unfused.push_back(make("kv_store_ring",
+                             {{"m", L->param("m")},
+                              {"kv_heads", L->param("kv_heads")},
+                              {"d", L->param("d")},
+                              {"length", L->param("length")},
+                              {"rotated", L->param("rotated")},
+                              {"ldq", L->param("ldq")},
+                              {"k_off", L->param("k_off")},
+                              {"v_off", L->param("v_off")}},
+                             {L->bufs.begin(), L->bufs.begin() + 7}));
+      std::vector<std::pair<std::string, double>> ap;
+      for (const char* k : {"m", "heads", "kv_heads", "d", "length", "rotated", "chunk", "max_splits", "ldq", "q_off",
+                            "scale"})
+        ap.emplace_back(k, L->param(k));
+      unfused.push_back(make("attend_split", ap, {L->bufs.begin(), L->bufs.begin() + 10}));
+    }
+    for (const Launch& L : unfused) by[L.kernel].push_back(&L);
+  }
+  double eps = 0;
+  bool have_eps = false;
+  for (const Launch& L : decode)
+    if (L.kernel.rfind("gemv", 0) == 0 && L.has("eps")) {
+      eps = L.param("eps");
+      have_eps = true;
+      break;
+    }
+  if (!have_eps) throw Refusal("prefill: the decode step normalizes nothing.");
+
+  auto hi = [&](uint64_t w) { return p.w_hi + (w - d.arena); };
+  auto lo = [&](uint64_t w) { return p.w_lo + (w - d.arena); };
+  auto gemm = [&](uint64_t a, uint64_t K, uint64_t w, uint64_t N, uint64_t c, uint64_t ldc) {
+    return make("gemm_tf32x3", {{"M", (double)m}, {"N", (double)N}, {"K", (double)K}, {"ldc", (double)ldc}},
+                {a, p.a_hi, p.a_lo, hi(w), lo(w), c});
+  };
+  const double md = (double)m;
+
+  std::vector<Launch> out;
+  const Launch& g0 = need("gather", 0);
+  out.push_back(with(g0, {{"m", md}}, {g0.bufs[0], p.tokens, p.x}));
+  for (uint64_t l = 0; l < s.layers; ++l) {
+    const auto w = layer_weights(s, d.arena, l);
+    const Launch& kv = need("kv_store_ring", l);
+    const Launch& at = need("attend_split", l);
+    const Launch& cb = need("attend_combine", l);
+    out.push_back(make("rmsnorm_rows", {{"rows", md}, {"h", (double)dm}, {"eps", eps}, {"factor", 1.0}},
+                       {p.x, w.at("attn_norm"), p.a}));
+    out.push_back(gemm(p.a, dm, w.at("q_proj"), nq, p.qkv, nq));
+    out.push_back(with(kv, {{"m", md}, {"ldq", (double)nq}},
+                       {p.qkv, kv.bufs[1], kv.bufs[2], p.pos, p.slot, kv.bufs[5], kv.bufs[6]}));
+    if (p.one_slot) {
+      out.push_back(make("attend_prompt",
+                         {{"m", md},
+                          {"heads", at.param("heads")},
+                          {"kv_heads", at.param("kv_heads")},
+                          {"d", at.param("d")},
+                          {"length", at.param("length")},
+                          {"rotated", at.param("rotated")},
+                          {"ldq", (double)nq},
+                          {"q_off", at.param("q_off")},
+                          {"ldo", (double)qw},
+                          {"max_pos", (double)(p.positions - 1)},
+                          {"scale", at.param("scale")}},
+                         {p.qkv, at.bufs[1], at.bufs[2], p.pos, p.slot, at.bufs[5], at.bufs[6], p.att}));
+    } else {
+      out.push_back(with(at,
+                         {{"m", md}, {"ldq", (double)nq}, {"chunk", (double)p.chunk},
+                          {"max_splits", (double)max_splits}},
+                         {p.qkv, at.bufs[1], at.bufs[2], p.pos, p.slot, at.bufs[5], at.bufs[6], p.part[0], p.part[1],
+                          p.part[2]}));
+      out.push_back(with(cb,
+                         {{"m", md}, {"chunk", (double)p.chunk}, {"max_splits", (double)max_splits},
+                          {"ldo", (double)qw}},
+                         {p.part[0], p.part[1], p.part[2], p.pos, p.att}));
+    }
+    // The row-parallel projections' partial sums are added across the
+    // ranks before the residual add.
+    out.push_back(gemm(p.att, qw, w.at("o_proj"), dm, p.tmp, dm));
+    if (d.world > 1) out.push_back(make("__allreduce__", {{"count", (double)(m * dm)}}, {p.tmp}));
+    out.push_back(make("add", {{"n", (double)(m * dm)}}, {p.x, p.tmp, p.x1}));
+    out.push_back(make("rmsnorm_rows", {{"rows", md}, {"h", (double)dm}, {"eps", eps}, {"factor", 1.0}},
+                       {p.x1, w.at("mlp_norm"), p.a}));
+    if (d.gate_up_interleaved) {  // rows gate_0, up_0, ...: the GEMM's columns likewise
+      out.push_back(gemm(p.a, dm, w.at("gate_proj"), 2 * f, p.gu, 2 * f));
+      out.push_back(make("silu_pairs", {{"n", (double)(m * f)}}, {p.gu, p.act}));
+    } else {  // gate rows, then up rows: a GEMM each, then the gate
+      const uint64_t up = p.gu + 4 * m * f;
+      out.push_back(gemm(p.a, dm, w.at("gate_proj"), f, p.gu, f));
+      out.push_back(gemm(p.a, dm, w.at("up_proj"), f, up, f));
+      out.push_back(make("silu_mul", {{"n", (double)(m * f)}}, {p.gu, up, p.act}));
+    }
+    out.push_back(gemm(p.act, f, w.at("down_proj"), dm, p.tmp, dm));
+    if (d.world > 1) out.push_back(make("__allreduce__", {{"count", (double)(m * dm)}}, {p.tmp}));
+    out.push_back(make("add", {{"n", (double)(m * dm)}}, {p.x1, p.tmp, p.x}));
+  }
+  return out;
+}
+
+}  // namespace fkh

@@ -95,7 +95,24 @@ class Prefill:
                       [a, self.a_hi.ptr, self.a_lo.ptr, self._hi(w), self._lo(w), c])
 
     def launches(self, m: int) -> list:
-        """The launch list over the first m rows of the row buffers."""
+        """The launch list over the first m rows of the row buffers, from
+        libfurykernel_host.so (fkh_llama_prefill_launches)."""
+        from . import _host
+
+        if not 1 <= m <= self.R:
+            raise N.Refused(N.FKC_ERR_ARGUMENT, f"prefill: {m} rows, outside 1..{self.R}.")
+        self.m = m
+        addrs = {n: getattr(self, n).ptr for n in ("w_hi", "w_lo", "x", "a", "a_hi", "a_lo", "qkv", "att", "tmp",
+                                                   "x1", "gu", "act")}
+        rs4 = 4 * self.rs
+        addrs.update(tokens=self.rows_buf.ptr, pos=self.rows_buf.ptr + rs4, slot=self.rows_buf.ptr + 2 * rs4,
+                     part=[b.ptr for b in self.part])
+        return [Launch(k, p, b) for k, p, b in _host.prefill_launches(
+            self.eng.launch_args(), self.R, self.chunk, self.positions, self.one_slot, addrs, m)]
+
+    def _launches_restated(self, m: int) -> list:
+        """The same launch list in Python (the restatement the host
+        library is checked against)."""
         eng, s = self.eng, self.eng.s
         if not 1 <= m <= self.R:
             raise N.Refused(N.FKC_ERR_ARGUMENT, f"prefill: {m} rows, outside 1..{self.R}.")

@@ -105,6 +105,27 @@ FKH_API size_t fkh_launch_buf_count(const fkh_launches *l, size_t i);
 FKH_API uint64_t fkh_launch_buf(const fkh_launches *l, size_t i, size_t j);
 FKH_API void fkh_launches_free(fkh_launches *l);
 
+/* The prompt prefill in front of a decode step: every prompt row through
+ * the layers at once, the linears as tcgen05 3xTF32 GEMM tiles
+ * (gemm_tf32x3, the reference's gemmTile: src/FuryKernel/Tile.hs:76-157),
+ * each row's keys and values stored in the Ring caches
+ * (furykernel_b200/prefill.py holds the same fields). */
+typedef struct {
+  uint64_t rows;      /* the most rows a launch list takes */
+  uint64_t chunk;     /* attention positions a split covers */
+  uint64_t positions; /* the bound of the positions a prefill stores */
+  int one_slot;       /* every run's rows in one slot: the query-tiled attend_prompt */
+  uint64_t w_hi, w_lo; /* the weights' TF32 halves, laid out as the weight arena */
+  uint64_t tokens, pos, slot; /* [rows] u32 each */
+  uint64_t x, a, a_hi, a_lo, qkv, att, tmp, x1, gu, act;
+  uint64_t part[3];
+} fkh_prefill_desc;
+
+/* The prefill of m rows (1..rows); `desc` is the decode step's, whose own
+ * launches are the templates of the gather, the KV stores and the attention. */
+FKH_API int fkh_llama_prefill_launches(const fkh_llama_desc *desc, const fkh_prefill_desc *prefill, uint64_t m,
+                                       fkh_launches **out, char *err, size_t err_cap);
+
 /* Split-K for a GEMV of n rows of k on `sms` SMs (the chunked kernel's). */
 FKH_API uint64_t fkh_split_for(uint64_t n_rows, uint64_t k, uint64_t sms);
 

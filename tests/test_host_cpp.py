@@ -228,3 +228,62 @@ def test_uneven_shards_are_refused():
         e = fake_engine(tp_shape(1), 1, 0, 1)
         e.world = 3
         e._launches()
+
+
+def fake_prefill(eng, rows, chunk=None, positions=None, one_slot=False):
+    """A Prefill with the attributes its launch lists read, at stand-in
+    addresses: the same decisions as its constructor."""
+    from furykernel_b200.prefill import Prefill
+
+    p = object.__new__(Prefill)
+    s = eng.s
+    p.eng, p.ctx, p.R = eng, eng.ctx, rows
+    at = iter(range(1, 100))
+    for name in ("w_hi", "w_lo", "rows_buf", "x", "a", "a_hi", "a_lo", "qkv", "att", "tmp", "x1", "gu", "act"):
+        setattr(p, name, Buf((6 << 44) + (next(at) << 36)))
+    p.rs = (rows + 3) // 4 * 4
+    p.chunk = chunk or eng.chunk
+    p.positions = positions or s.positions
+    p.max_splits = (p.positions + p.chunk - 1) // p.chunk
+    p.one_slot = one_slot and p.positions <= min(s.length, 1408)
+    p.part = [Buf((7 << 44) + (i << 36)) for i in range(3)]
+    return p
+
+
+PREFILL_CASES = (
+    # the prefill tests: batch, rows, one slot
+    [(small(b), b, 0, 1, True, rows, one, m) for b, rows, one, m in ((1, 128, False, 100), (3, 128, False, 128),
+                                                                     (1, 128, True, 64), (3, 128, True, 7))]
+    # the bench's prompt prefill (config 5), one and two ranks, and a batch past the interleaved arena
+    + [(LlamaShape(layers=4, slots=1, length=4096, positions=4096), 1, r, w, True, 512, True, 512)
+       for w in (1, 2) for r in range(w)]
+    + [(LlamaShape(layers=2, slots=1, length=4096, positions=4096), 1, 0, 1, True, 512, False, 512)]
+    + [(small(65, layers=1), 65, 0, 1, True, 64, False, 33)]
+    # tensor parallelism over NCCL and over peer memory
+    + [(tp_shape(b), b, r, 4, peer, 32, False, 32) for b in (1, 16) for r in (0, 3) for peer in (True, False)]
+)
+
+
+@pytest.mark.parametrize("case", range(len(PREFILL_CASES)))
+def test_prefill_launches_alike(case):
+    full, batch, rank, world, peer, rows, one_slot, m = PREFILL_CASES[case]
+    e = fake_engine(full, batch, rank, world, peer)
+    e.launches = e._launches_restated()
+    # as the bench sizes it: positions up to the prompt's rows
+    p = fake_prefill(e, rows, positions=rows if rows == 512 else None, one_slot=one_slot)
+    assert p.one_slot == one_slot
+    want = p._launches_restated(m)
+    got = p.launches(m)
+    assert [L.kernel for L in got] == [L.kernel for L in want]
+    for g, w in zip(got, want):
+        assert (g.kernel, g.bufs) == (w.kernel, w.bufs)
+        assert g.params == w.params, (g.kernel, g.params, w.params)
+
+
+def test_prefill_rows_are_bounded():
+    e = fake_engine(small(1), 1)
+    e.launches = e._launches_restated()
+    p = fake_prefill(e, 16)
+    for m in (0, 17):
+        with pytest.raises(N.Refused, match="outside 1..16"):
+            p.launches(m)
