@@ -14,14 +14,15 @@ _LIB = None
 _PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_build", "libfurykernel_host.so")
 
 FKH_OK, FKH_ERR_ARGUMENT, FKH_ERR_SPACE, FKH_ERR_INTERNAL = 0, 1, 2, 3
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 
 class Shape(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint64) for n in ("d_model", "heads", "kv_heads", "head_dim", "ffn", "vocab",
                                                 "layers")] + \
                [("theta", ctypes.c_double), ("eps", ctypes.c_double)] + \
-               [(n, ctypes.c_uint64) for n in ("slots", "length", "positions")]
+               [(n, ctypes.c_uint64) for n in ("slots", "length", "positions")] + \
+               [("weights_bf16", ctypes.c_int), ("cache_bf16", ctypes.c_int)]
 
 
 class PlanOptions(ctypes.Structure):
@@ -101,8 +102,11 @@ def _text(call, *args) -> str:
 
 def shape(s) -> Shape:
     """A LlamaShape (program.llama) as the C struct."""
+    for what, t in (("weights", s.weights), ("cache", s.cache)):
+        if t not in ("f32", "bf16"):
+            raise N.Refused(N.FKC_ERR_ARGUMENT, f"the {what}' element type {t} is not f32 or bf16.")
     return Shape(s.d_model, s.heads, s.kv_heads, s.head_dim, s.ffn, s.vocab, s.layers, s.theta, s.eps, s.slots,
-                 s.length, s.positions)
+                 s.length, s.positions, int(s.weights == "bf16"), int(s.cache == "bf16"))
 
 
 def llama_program_text(s, which: str) -> str:

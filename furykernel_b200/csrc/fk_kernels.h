@@ -142,6 +142,22 @@ cudaError_t fk_launch_gemm_tf32x3(const float* a_hi, const float* a_lo, const fl
                                   cudaStream_t s);
 cudaError_t fk_launch_fill_normal(float* out, uint64_t n, uint64_t seed, double mu, double sigma, cudaStream_t s);
 cudaError_t fk_launch_fill_uniform(float* out, uint64_t n, uint64_t seed, double a, double b, cudaStream_t s);
+// bf16 weights (k_w16.cu): the f32 kernels' arithmetic over widened weights.
+cudaError_t fk_launch_gemv_w16(const FkGemv& g, const uint16_t* w, const uint16_t* gamma, int sms, cudaStream_t s);
+cudaError_t fk_launch_gather_w16(const uint16_t* table, uint32_t width, const uint32_t* tokens, uint32_t m,
+                                 float factor, float* y, bool pdl, cudaStream_t s);
+cudaError_t fk_launch_rmsnorm_rows_w16(const float* x, const uint16_t* gamma, float* y, uint32_t rows, uint32_t h,
+                                       float eps, float factor, cudaStream_t s);
+cudaError_t fk_launch_split_tf32_w16(const uint16_t* x, float* hi, float* lo, uint64_t n, cudaStream_t s);
+cudaError_t fk_launch_fill_normal_w16(uint16_t* out, uint64_t n, uint64_t seed, double mu, double sigma,
+                                      cudaStream_t s);
+// bf16 KV caches (k_attend_kv16.cu): stores rounded to bf16, reads widened.
+cudaError_t fk_launch_kv_store16(const FkKvStore& a, uint16_t* kc, uint16_t* vc, cudaStream_t s);
+cudaError_t fk_launch_attend16(const FkAttend& a, const uint16_t* kc, const uint16_t* vc, cudaStream_t s);
+cudaError_t fk_launch_attend_decode16(const FkAttend& a, uint32_t k_off, uint32_t v_off, uint16_t* kc, uint16_t* vc,
+                                      cudaStream_t s);
+cudaError_t fk_launch_attend_prompt16(const FkAttend& a, const uint16_t* kc, const uint16_t* vc, float* out,
+                                      uint32_t ldo, uint32_t max_pos, cudaStream_t s);
 cudaError_t fk_launch_rope_tables(float* cos_t, float* sin_t, double theta, uint32_t d, uint32_t rotated,
                                   uint32_t positions, cudaStream_t s);
 

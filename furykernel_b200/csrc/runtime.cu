@@ -229,6 +229,23 @@ extern "C" int fkc_kv_arena(fkc_ctx* c, uint32_t layers, uint32_t slots, uint32_
   return fkc_buf_zero(c, *v_base, total);
 }
 
+extern "C" int fkc_kv_arena_elem(fkc_ctx* c, uint32_t layers, uint32_t slots, uint32_t kv_heads, uint32_t length,
+                                 uint32_t head_dim, uint32_t elem_bytes, void** k_base, void** v_base) {
+  if (!c || !k_base || !v_base) return fail(FKC_ERR_ARGUMENT, "fkc_kv_arena_elem: null argument.");
+  if (elem_bytes != 2 && elem_bytes != 4)
+    return fail(FKC_ERR_ARGUMENT, "fkc_kv_arena_elem: elements of %u bytes; a cache holds 2 (bf16) or 4 (f32).",
+                elem_bytes);
+  const size_t per = (size_t)slots * kv_heads * length * head_dim * elem_bytes;
+  const size_t total = per * layers;
+  int rc = fkc_buf_alloc(c, total, k_base);
+  if (rc) return rc;
+  rc = fkc_buf_alloc(c, total, v_base);
+  if (rc) return rc;
+  rc = fkc_buf_zero(c, *k_base, total);
+  if (rc) return rc;
+  return fkc_buf_zero(c, *v_base, total);
+}
+
 extern "C" int fkc_rope_tables(fkc_ctx* c, double theta, uint32_t d, uint32_t rotated, uint32_t positions,
                                void** cos_t, void** sin_t) {
   if (!c || !cos_t || !sin_t || d == 0) return fail(FKC_ERR_ARGUMENT, "fkc_rope_tables: bad argument.");
@@ -253,6 +270,13 @@ extern "C" int fkc_fill_normal(fkc_ctx* c, void* dptr, uint64_t n, uint64_t seed
   if (!c || (n && !dptr)) return fail(FKC_ERR_ARGUMENT, "fkc_fill_normal: null argument.");
   cudaSetDevice(c->device);
   FKC_CUDA(fk_launch_fill_normal((float*)dptr, n, seed, mu, sigma, c->stream), "fkc_fill_normal");
+  return FKC_OK;
+}
+
+extern "C" int fkc_fill_normal_bf16(fkc_ctx* c, void* dptr, uint64_t n, uint64_t seed, double mu, double sigma) {
+  if (!c || (n && !dptr)) return fail(FKC_ERR_ARGUMENT, "fkc_fill_normal_bf16: null argument.");
+  cudaSetDevice(c->device);
+  FKC_CUDA(fk_launch_fill_normal_w16((uint16_t*)dptr, n, seed, mu, sigma, c->stream), "fkc_fill_normal_bf16");
   return FKC_OK;
 }
 
@@ -642,6 +666,166 @@ int l_silu_pairs(fkc_ctx* c, const Params& p, void* const* bufs) {
   return launched(fk_launch_silu_pairs(CF(0), F(1), p.u(0), c->stream), "silu_pairs");
 }
 
+// ---- bf16 weights (the entries' `w`, `gamma`, `table` buffers are bf16) ----
+#define W16(i) ((const uint16_t*)bufs[i])
+#define M16(i) ((uint16_t*)bufs[i])
+
+int gemv_w16(fkc_ctx* c, const FkGemv& g, const uint16_t* w, const uint16_t* gamma, const char* name) {
+  return launched(fk_launch_gemv_w16(g, w, gamma, c->sms, c->stream), name);
+}
+int l_gemv_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkGemv g = gemv_base(c, p);
+  g.x = CF(1), g.y = F(2);
+  g.prologue = FK_PRO_NONE;
+  return gemv_w16(c, g, W16(0), nullptr, "gemv_wbf16");
+}
+int l_gemv_add_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkGemv g = gemv_base(c, p);
+  g.x = CF(1), g.r = CF(2), g.y = F(3);
+  g.ldr = p.u(6);
+  g.prologue = FK_PRO_NONE;
+  return gemv_w16(c, g, W16(0), nullptr, "gemv_add_wbf16");
+}
+int l_gemv_rmsnorm_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkGemv g = gemv_base(c, p);
+  g.x = CF(1), g.y = F(3);
+  g.eps = p.f(6);
+  g.factor = p.f(7);
+  g.prologue = FK_PRO_RMSNORM;
+  return gemv_w16(c, g, W16(0), W16(2), "gemv_rmsnorm_wbf16");
+}
+int l_gemv_rmsnorm_silu_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkGemv g = gemv_base(c, p);
+  g.x = CF(1), g.y = F(3);
+  g.eps = p.f(6);
+  g.factor = p.f(7);
+  g.prologue = FK_PRO_RMSNORM;
+  g.silu_pair = true;
+  if (g.n % 2 != 0)
+    return fail(FKC_ERR_ARGUMENT, "gemv_rmsnorm_silu_wbf16: n %u is not a whole number of row pairs.", g.n);
+  if (!fk_gemv_streams(g))
+    return fail(FKC_ERR_ARGUMENT, "gemv_rmsnorm_silu_wbf16: m %u is past the streaming kernel's 4.", g.m);
+  return gemv_w16(c, g, W16(0), W16(2), "gemv_rmsnorm_silu_wbf16");
+}
+int l_gemv_silu_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkGemv g = gemv_base(c, p);
+  g.x = CF(1), g.y = F(2);
+  g.up_off = p.u(6);
+  g.prologue = FK_PRO_SILU;
+  return gemv_w16(c, g, W16(0), nullptr, "gemv_silu_wbf16");
+}
+int l_gemv_silu_add_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkGemv g = gemv_base(c, p);
+  g.x = CF(1), g.r = CF(2), g.y = F(3);
+  g.ldr = p.u(6);
+  g.up_off = p.u(7);
+  g.prologue = FK_PRO_SILU;
+  return gemv_w16(c, g, W16(0), nullptr, "gemv_silu_add_wbf16");
+}
+int l_gemv_scatter_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  if (!have_peers(c)) return fail(FKC_ERR_STATE, "gemv_scatter_wbf16: the context has no peer set.");
+  FkGemv g = {};
+  g.x = CF(1);
+  g.n = p.u(0), g.k = p.u(1), g.m = p.u(2), g.split = p.u(3), g.ldx = p.u(4), g.xbuf = p.u(5);
+  g.factor = 1.0f;
+  g.pdl = c->pdl;
+  g.prologue = FK_PRO_NONE;
+  g.scatter = true;
+  g.peers = c->peers;
+  g.err = c->status;
+  if (!fk_gemv_streams(g))
+    return fail(FKC_ERR_ARGUMENT, "gemv_scatter_wbf16: m %u is past the streaming kernel's 4.", g.m);
+  return gemv_w16(c, g, W16(0), nullptr, "gemv_scatter_wbf16");
+}
+int reduce_gemv_w16(fkc_ctx* c, const Params& p, void* const* bufs, bool silu, const char* name) {
+  if (!have_peers(c)) return fail(FKC_ERR_STATE, "%s: the context has no peer set.", name);
+  FkGemv g = {};
+  g.x = CF(1), g.xout = F(3), g.y = F(4);
+  g.n = p.u(0), g.k = p.u(1), g.m = p.u(2), g.split = p.u(3), g.ldx = p.u(4), g.ldy = p.u(5);
+  g.eps = p.f(6), g.factor = p.f(7), g.xbuf = p.u(8);
+  g.pdl = c->pdl;
+  g.prologue = FK_PRO_REDUCE_RMSNORM;
+  g.silu_pair = silu;
+  g.peers = c->peers;
+  g.err = c->status;
+  if (g.ldx != g.k) return fail(FKC_ERR_ARGUMENT, "%s: the residual rows must be whole (ldr %u, k %u).", name, g.ldx, g.k);
+  if (!fk_gemv_streams(g)) return fail(FKC_ERR_ARGUMENT, "%s: m %u is past the streaming kernel's 4.", name, g.m);
+  return gemv_w16(c, g, W16(0), W16(2), name);
+}
+int l_gemv_reduce_rmsnorm_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return reduce_gemv_w16(c, p, bufs, false, "gemv_reduce_rmsnorm_wbf16");
+}
+int l_gemv_reduce_rmsnorm_silu_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return reduce_gemv_w16(c, p, bufs, true, "gemv_reduce_rmsnorm_silu_wbf16");
+}
+int l_gather_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return launched(fk_launch_gather_w16(W16(0), p.u(0), CU(1), p.u(1), p.f(2), F(2), c->pdl, c->stream),
+                  "gather_wbf16");
+}
+int l_rmsnorm_rows_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return launched(fk_launch_rmsnorm_rows_w16(CF(0), W16(1), F(2), p.u(0), p.u(1), p.f(2), p.f(3), c->stream),
+                  "rmsnorm_rows_wbf16");
+}
+int l_split_tf32_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return launched(fk_launch_split_tf32_w16(W16(0), F(1), F(2), p.u(0), c->stream), "split_tf32_wbf16");
+}
+
+// ---- bf16 KV caches (the entries' `k_cache`, `v_cache` buffers are bf16) ----
+int l_kv_store_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkKvStore a = {};
+  a.qkv = CF(0), a.cos_t = CF(1), a.sin_t = CF(2), a.pos = CU(3), a.slot = CU(4);
+  a.m = p.u(0), a.kv_heads = p.u(1), a.d = p.u(2), a.length = p.u(3), a.rotated = p.u(4);
+  a.ldq = p.u(5), a.k_off = p.u(6), a.v_off = p.u(7);
+  a.pdl = c->pdl;
+  if (a.rotated > a.d / 2) return fail(FKC_ERR_ARGUMENT, "kv_store_ring_kvbf16: rotated %u is more than d/2.", a.rotated);
+  return launched(fk_launch_kv_store16(a, M16(5), M16(6), c->stream), "kv_store_ring_kvbf16");
+}
+FkAttend attend_base(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkAttend a = {};
+  a.qkv = CF(0), a.cos_t = CF(1), a.sin_t = CF(2), a.pos = CU(3), a.slot = CU(4);
+  a.m = p.u(0), a.heads = p.u(1), a.kv_heads = p.u(2), a.d = p.u(3), a.length = p.u(4), a.rotated = p.u(5);
+  a.pdl = c->pdl;
+  return a;
+}
+int l_attend_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkAttend a = attend_base(c, p, bufs);
+  a.part_m = F(7), a.part_l = F(8), a.part_acc = F(9);
+  a.chunk = p.u(6), a.max_splits = p.u(7), a.ldq = p.u(8), a.q_off = p.u(9);
+  a.scale = p.f(10);
+  if (a.kv_heads == 0 || a.heads % a.kv_heads != 0)
+    return fail(FKC_ERR_ARGUMENT, "attend_split_kvbf16: %u heads do not share %u KV heads in groups.", a.heads,
+                a.kv_heads);
+  return launched(fk_launch_attend16(a, W16(5), W16(6), c->stream), "attend_split_kvbf16");
+}
+int l_attend_decode_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkAttend a = attend_base(c, p, bufs);
+  a.part_m = F(7), a.part_l = F(8), a.part_acc = F(9);
+  a.chunk = p.u(6), a.max_splits = p.u(7), a.ldq = p.u(8), a.q_off = p.u(9);
+  a.scale = p.f(12);
+  if (a.kv_heads == 0 || a.heads % a.kv_heads != 0)
+    return fail(FKC_ERR_ARGUMENT, "attend_decode_kvbf16: %u heads do not share %u KV heads in groups.", a.heads,
+                a.kv_heads);
+  if (a.rotated > a.d / 2) return fail(FKC_ERR_ARGUMENT, "attend_decode_kvbf16: rotated %u is more than d/2.", a.rotated);
+  return launched(fk_launch_attend_decode16(a, p.u(10), p.u(11), M16(5), M16(6), c->stream), "attend_decode_kvbf16");
+}
+int l_attend_prompt_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  FkAttend a = attend_base(c, p, bufs);
+  a.ldq = p.u(6), a.q_off = p.u(7);
+  a.scale = p.f(10);
+  if (a.kv_heads == 0 || a.heads % a.kv_heads != 0)
+    return fail(FKC_ERR_ARGUMENT, "attend_prompt_kvbf16: %u heads do not share %u KV heads in groups.", a.heads,
+                a.kv_heads);
+  if (a.rotated > a.d / 2) return fail(FKC_ERR_ARGUMENT, "attend_prompt_kvbf16: rotated %u is more than d/2.", a.rotated);
+  if (p.u(9) >= a.length)
+    return fail(FKC_ERR_ARGUMENT, "attend_prompt_kvbf16: max_pos %u is not within the ring's length %u.", p.u(9),
+                a.length);
+  return launched(fk_launch_attend_prompt16(a, W16(5), W16(6), F(7), p.u(8), p.u(9), c->stream),
+                  "attend_prompt_kvbf16");
+}
+
+#undef W16
+#undef M16
+
 #undef F
 #undef CF
 #undef CU
@@ -856,6 +1040,48 @@ std::vector<KernelSpec> make_table() {
                {dim("n", 1, 1048576), dim("k", 4, 65536, 4), dim("m", 1, 16), dim("pack", 4, 16, 4), dim("split", 1, 16),
                 u32("ldx"), u32("ldy")},
                l_gemv_bf16});
+  // The bf16 forms: an f32 entry's parameters with some buffers bf16 (the
+  // model's weights, or its KV caches) and their own launchers.
+  struct Variant {
+    const char* base;
+    const char* name;
+    std::vector<const char*> retyped;
+    LaunchFn launch;
+  };
+  const std::vector<Variant> variants = {
+      {"gemv", "gemv_wbf16", {"w"}, l_gemv_w16},
+      {"gemv_add", "gemv_add_wbf16", {"w"}, l_gemv_add_w16},
+      {"gemv_rmsnorm", "gemv_rmsnorm_wbf16", {"w", "gamma"}, l_gemv_rmsnorm_w16},
+      {"gemv_rmsnorm_silu", "gemv_rmsnorm_silu_wbf16", {"w", "gamma"}, l_gemv_rmsnorm_silu_w16},
+      {"gemv_silu", "gemv_silu_wbf16", {"w"}, l_gemv_silu_w16},
+      {"gemv_silu_add", "gemv_silu_add_wbf16", {"w"}, l_gemv_silu_add_w16},
+      {"gemv_scatter", "gemv_scatter_wbf16", {"w"}, l_gemv_scatter_w16},
+      {"gemv_reduce_rmsnorm", "gemv_reduce_rmsnorm_wbf16", {"w", "gamma"}, l_gemv_reduce_rmsnorm_w16},
+      {"gemv_reduce_rmsnorm_silu", "gemv_reduce_rmsnorm_silu_wbf16", {"w", "gamma"}, l_gemv_reduce_rmsnorm_silu_w16},
+      {"gather", "gather_wbf16", {"table"}, l_gather_w16},
+      {"rmsnorm_rows", "rmsnorm_rows_wbf16", {"gamma"}, l_rmsnorm_rows_w16},
+      {"split_tf32", "split_tf32_wbf16", {"x"}, l_split_tf32_w16},
+      {"kv_store_ring", "kv_store_ring_kvbf16", {"k_cache", "v_cache"}, l_kv_store_kv16},
+      {"attend_split", "attend_split_kvbf16", {"k_cache", "v_cache"}, l_attend_kv16},
+      {"attend_decode", "attend_decode_kvbf16", {"k_cache", "v_cache"}, l_attend_decode_kv16},
+      {"attend_prompt", "attend_prompt_kvbf16", {"k_cache", "v_cache"}, l_attend_prompt_kv16},
+  };
+  for (const Variant& v : variants) {
+    KernelSpec k;
+    bool found = false;
+    for (const KernelSpec& b : t)
+      if (strcmp(b.name, v.base) == 0) {
+        k = b;
+        found = true;
+      }
+    if (!found) continue;
+    k.name = v.name;
+    k.launch = v.launch;
+    for (BufSpec& b : k.bufs)
+      for (const char* r : v.retyped)
+        if (strcmp(b.name, r) == 0) b.type = "bf16";
+    t.push_back(k);
+  }
   // The C layout (Abi.hs:113-133) and the canonical text (Abi.hs:136-159).
   for (auto& k : t) {
     uint32_t off = 0, align = 1;

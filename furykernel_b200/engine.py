@@ -81,6 +81,35 @@ def _work_text(p, step) -> str:
     return "; ".join(f"{w.kind.lower()} {p.node(w.node).name}" for w in step.work)
 
 
+# A kernel's element-type form: the f32 entry's name, or with the suffix of
+# its bf16 weights or its bf16 KV caches.
+W16, KV16 = "_wbf16", "_kvbf16"
+
+
+def kernel_form(kernel: str) -> tuple:
+    """(the f32 entry's name, the suffix of the form)."""
+    for suffix in (W16, KV16):
+        if kernel.endswith(suffix):
+            return kernel[:-len(suffix)], suffix
+    return kernel, ""
+
+
+def _weight_suffix(step, t: str) -> str:
+    if t == "f32":
+        return ""
+    if t == "bf16":
+        return W16
+    raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: no kernel reads {t} weights.")
+
+
+def _cache_suffix(step, elem: str) -> str:
+    if elem == "f32":
+        return ""
+    if elem == "bf16":
+        return KV16
+    raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: no kernel reads {elem} caches.")
+
+
 def lower_step(p, step, b: Binding, tables: dict, attn: dict) -> Launch:
     """One step of a plan as one launch (the step shapes of the Llama plans)."""
     work = [(w.kind, p.node(w.node)) for w in step.work]
@@ -100,6 +129,10 @@ def lower_step(p, step, b: Binding, tables: dict, attn: dict) -> Launch:
         if any(n.op.values[0] != x_id for n in anchors):
             raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: anchors of different inputs: {_work_text(p, step)}")
         ws = [p.source(n.op.sources[0]) for n in anchors]
+        if any(w.kind.type != ws[0].kind.type for w in ws):
+            raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: its anchors' weights differ in type.")
+        wt = _weight_suffix(step, ws[0].kind.type)
+        esz = 2 if wt else 4
         w0 = b.weights[ws[0].name]
         n_total = sum(w.kind.dims[0] for w in ws)
         k = ws[0].kind.dims[1]
@@ -107,7 +140,7 @@ def lower_step(p, step, b: Binding, tables: dict, attn: dict) -> Launch:
         for w in ws:  # the anchors' weights must lie adjacent
             if b.weights[w.name] != addr:
                 raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: the weights of its anchors are not adjacent.")
-            addr += 4 * w.kind.dims[0] * k
+            addr += esz * w.kind.dims[0] * k
         if epilogues:
             (ep,) = epilogues
             if ep.op.kind != "Add" or len(anchors) != 1:
@@ -129,13 +162,17 @@ def lower_step(p, step, b: Binding, tables: dict, attn: dict) -> Launch:
             base["ldx"] = x.ld
             if epilogues:
                 r = stored(r_id)
-                return Launch("gemv_add", dict(base, ldr=r.ld), [w0, x.ptr, r.ptr, y.ptr])
-            return Launch("gemv", base, [w0, x.ptr, y.ptr])
+                return Launch("gemv_add" + wt, dict(base, ldr=r.ld), [w0, x.ptr, r.ptr, y.ptr])
+            return Launch("gemv" + wt, base, [w0, x.ptr, y.ptr])
         if xn.op.kind == "RmsNorm" and not epilogues:
             eps, factor, has_gamma = xn.op.args
             x = stored(xn.op.values[0])
-            gamma = b.weights[p.source(xn.op.sources[0]).name]
-            return Launch("gemv_rmsnorm", dict(base, ldx=x.ld, eps=eps, factor=factor), [w0, x.ptr, gamma, y.ptr])
+            g = p.source(xn.op.sources[0])
+            if g.kind.type != ws[0].kind.type:
+                raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: the norm's gain and the weights differ in type.")
+            gamma = b.weights[g.name]
+            return Launch("gemv_rmsnorm" + wt, dict(base, ldx=x.ld, eps=eps, factor=factor),
+                          [w0, x.ptr, gamma, y.ptr])
         if xn.op.kind == "SiluMul":
             g, u = (stored(v) for v in xn.op.values)
             if g.buf is not u.buf or g.ld != u.ld:
@@ -143,8 +180,8 @@ def lower_step(p, step, b: Binding, tables: dict, attn: dict) -> Launch:
             base = dict(base, ldx=g.ld, up_off=u.col - g.col)
             if epilogues:
                 r = stored(r_id)
-                return Launch("gemv_silu_add", dict(base, ldr=r.ld), [w0, g.ptr, r.ptr, y.ptr])
-            return Launch("gemv_silu", base, [w0, g.ptr, y.ptr])
+                return Launch("gemv_silu_add" + wt, dict(base, ldr=r.ld), [w0, g.ptr, r.ptr, y.ptr])
+            return Launch("gemv_silu" + wt, base, [w0, g.ptr, y.ptr])
         raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: no kernel runs {_work_text(p, step)}")
 
     if len(anchors) == 1 and anchors[0].op.kind == "Attend":
@@ -156,8 +193,9 @@ def lower_step(p, step, b: Binding, tables: dict, attn: dict) -> Launch:
         q = stored(qn.op.values[0])
         kc, vc, pos, slot = (p.source(s).name for s in att.op.sources[:4])
         layout = p.source(att.op.sources[0]).kind.layout
+        ct = _cache_suffix(step, p.source(att.op.sources[0]).kind.elem)
         part = attn["partials"]
-        return Launch("attend_split",
+        return Launch("attend_split" + ct,
                       {"m": b.m, "heads": spec.heads, "kv_heads": spec.kv_heads, "d": spec.head_dim,
                        "length": layout.length, "rotated": qn.op.args[0].rotated, "chunk": attn["chunk"],
                        "max_splits": attn["max_splits"], "ldq": q.ld, "q_off": q.col, "scale": spec.scale},
@@ -186,8 +224,9 @@ def lower_step(p, step, b: Binding, tables: dict, attn: dict) -> Launch:
         if kview.buf is not vview.buf:
             raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: keys and values are not one row.")
         layout = p.source(sk.op.sources[0]).kind.layout
+        ct = _cache_suffix(step, p.source(sk.op.sources[0]).kind.elem)
         pos, slot = (p.source(s).name for s in sk.op.sources[1:3])
-        return Launch("kv_store_ring",
+        return Launch("kv_store_ring" + ct,
                       {"m": b.m, "kv_heads": layout.kv_heads, "d": layout.head_dim, "length": layout.length,
                        "rotated": kn.op.args[0].rotated, "ldq": kview.ld, "k_off": kview.col, "v_off": vview.col},
                       [kview.base, tables["cos"], tables["sin"], b.ints[pos], b.ints[slot],
@@ -197,7 +236,8 @@ def lower_step(p, step, b: Binding, tables: dict, attn: dict) -> Launch:
         g = work[0][1]
         table, tok = (p.source(s) for s in g.op.sources)
         y = stored(g.outputs[0])
-        return Launch("gather", {"width": table.kind.dims[1], "m": b.m, "factor": g.op.args[0]},
+        return Launch("gather" + _weight_suffix(step, table.kind.type),
+                      {"width": table.kind.dims[1], "m": b.m, "factor": g.op.args[0]},
                       [b.weights[table.name], b.ints[tok.name], y.ptr])
 
     if kinds == ["Recompute"] and work[0][1].op.kind == "ArgMax":
@@ -219,10 +259,11 @@ def split_for(n_rows: int, k: int, sms: int) -> int:
 
 
 class Llama:
-    """A Llama-shaped f32 model on one device, or one rank of a Megatron-style
+    """A Llama-shaped model on one device, or one rank of a Megatron-style
     tensor-parallel group: the weights (seeded on the device, or given), the
     Ring KV arena, the plans of the embedding, a layer and the head, and the
-    captured decode step.
+    captured decode step. Activations are f32; the weights and the caches
+    are f32 or bf16, as the shape says (`weights`, `cache`).
 
     With `world` ranks, each holds heads/world query and KV heads with their
     rows of q/k/v and columns of o, ffn/world rows of gate and up with their
@@ -247,12 +288,21 @@ class Llama:
                                 ffn=full.ffn // world)
         self.ctx, self.full, self.s, self.m = ctx, full, s, batch
         self.rank, self.world = rank, world
+        # Bytes of a weight and of a cache element.
+        self.wb = {"f32": 4, "bf16": 2}.get(s.weights)
+        self.cb = {"f32": 4, "bf16": 2}.get(s.cache)
+        if self.wb is None or self.cb is None:
+            raise N.Refused(N.FKC_ERR_ARGUMENT, f"no kernels for {s.weights} weights and {s.cache} caches.")
+        if self.wb == 2 and any(n % 8 for n in (s.d_model, s.q_width, s.kv_width, s.ffn)):
+            raise N.Refused(N.FKC_ERR_ARGUMENT, "bf16 weights: d_model, the q and kv widths and ffn must be multiples "
+                            "of 8, so that every weight starts on a 16-byte boundary.")
         # For decode batches the streaming and batched GEMVs take (up to 64
         # rows), the arena interleaves gate and up rows (gate_i at row 2i, up_i at
         # 2i + 1), so that the [gate; up] step computes mlp_act = silu(gate) *
         # up on its own tiles and stores it, and the down step reads it: the
         # same bits as recomputing it in the down step, computed once.
-        self.gate_up_interleaved = batch <= 64
+        # (bf16 weights: the streaming kernel's batches, up to 4 rows).
+        self.gate_up_interleaved = batch <= (4 if self.wb == 2 else 64)
         # Tensor parallelism's sums travel through peer memory (the context's
         # peer set, tp.init) for the batches the streaming GEMV takes; larger
         # batches use NCCL.
@@ -268,25 +318,28 @@ class Llama:
         # gains too (the configs give no other law for them).
         d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
         self.layer_elems = (qw + 2 * kvw) * d + d * qw + 2 * f * d + d * f + 2 * d
-        self.arena = ctx.alloc(4 * (s.layers * self.layer_elems + full.vocab * d + d))
+        wb = self.wb
+        self.arena = ctx.alloc(wb * (s.layers * self.layer_elems + full.vocab * d + d))
+        fill = ctx.fill_normal if wb == 4 else ctx.fill_normal_bf16
         if host_weights is None:
             # A rank's layer shards from its own seed; the embedding and the
-            # norms alike on every rank.
-            layers = N.DeviceBuffer(ctx, self.arena.ptr, 4 * s.layers * self.layer_elems)
-            ctx.fill_normal(layers, seed + 7919 * rank, 0.0, 0.02)
-            rest = N.DeviceBuffer(ctx, self.embed_ptr(), 4 * (full.vocab * d + d))
-            ctx.fill_normal(rest, seed + 104729, 0.0, 0.02)
+            # norms alike on every rank (bf16: the same values, rounded).
+            layers = N.DeviceBuffer(ctx, self.arena.ptr, wb * s.layers * self.layer_elems)
+            fill(layers, seed + 7919 * rank, 0.0, 0.02)
+            rest = N.DeviceBuffer(ctx, self.embed_ptr(), wb * (full.vocab * d + d))
+            fill(rest, seed + 104729, 0.0, 0.02)
             for l in range(s.layers):
                 w = self.layer_weights(l)
-                ctx.fill_normal(N.DeviceBuffer(ctx, w["attn_norm"], 8 * d), seed + 3 * l + 1, 0.0, 0.02)
+                fill(N.DeviceBuffer(ctx, w["attn_norm"], 2 * wb * d), seed + 3 * l + 1, 0.0, 0.02)
         else:
             self.arena.upload(host_weights)
         self.cos, self.sin = ctx.rope_tables(s.theta, s.head_dim, s.head_dim // 2, s.positions)
         self.kbase, self.vbase = self._kv_arena()
         if prefill_kv is not None:
             kv = s.layers * s.slots * s.kv_heads * s.length * s.head_dim
-            ctx.fill_normal(N.DeviceBuffer(ctx, self.kbase, 4 * kv), seed + 1 + 17 * rank, 0.0, prefill_kv)
-            ctx.fill_normal(N.DeviceBuffer(ctx, self.vbase, 4 * kv), seed + 2 + 17 * rank, 0.0, prefill_kv)
+            cfill = ctx.fill_normal if self.cb == 4 else ctx.fill_normal_bf16
+            cfill(N.DeviceBuffer(ctx, self.kbase, self.cb * kv), seed + 1 + 17 * rank, 0.0, prefill_kv)
+            cfill(N.DeviceBuffer(ctx, self.vbase, self.cb * kv), seed + 2 + 17 * rank, 0.0, prefill_kv)
         m = batch
         # A step's row inputs in one buffer, so that one copy brings them in:
         # the tokens, the positions, the slots, each part on a 16-byte
@@ -331,8 +384,8 @@ class Llama:
 
         k, v = ctypes.c_void_p(), ctypes.c_void_p()
         s = self.s
-        N.check(N.lib().fkc_kv_arena(self.ctx.handle, s.layers, s.slots, s.kv_heads, s.length, s.head_dim,
-                                     ctypes.byref(k), ctypes.byref(v)))
+        N.check(N.lib().fkc_kv_arena_elem(self.ctx.handle, s.layers, s.slots, s.kv_heads, s.length, s.head_dim,
+                                          self.cb, ctypes.byref(k), ctypes.byref(v)))
         return k.value, v.value
 
     LAYER_ORDER = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj", "attn_norm",
@@ -344,22 +397,22 @@ class Llama:
         return [qw * d, kvw * d, kvw * d, d * qw, f * d, f * d, d * f, d, d]
 
     def layer_weights(self, l: int) -> dict:
-        base = self.arena.ptr + 4 * l * self.layer_elems
+        base = self.arena.ptr + self.wb * l * self.layer_elems
         off, at = {}, 0
         for name, n in zip(self.LAYER_ORDER, self.layer_sizes()):
-            off[name] = base + 4 * at
+            off[name] = base + self.wb * at
             at += n
         return off
 
     def embed_ptr(self) -> int:
-        return self.arena.ptr + 4 * self.s.layers * self.layer_elems
+        return self.arena.ptr + self.wb * self.s.layers * self.layer_elems
 
     def final_norm_ptr(self) -> int:
-        return self.embed_ptr() + 4 * self.full.vocab * self.full.d_model
+        return self.embed_ptr() + self.wb * self.full.vocab * self.full.d_model
 
     def kv_layer(self, l: int):
         s = self.s
-        per = 4 * s.slots * s.kv_heads * s.length * s.head_dim
+        per = self.cb * s.slots * s.kv_heads * s.length * s.head_dim
         return self.kbase + l * per, self.vbase + l * per
 
     # -- the step's launches
@@ -413,7 +466,7 @@ class Llama:
             for st in self.plans["layer"].steps:
                 out.append(lower_step(p, st, b, tables, attn))
         p = self.plans["head"].program
-        head_rows = self.embed_ptr() + 4 * self.rank * self.vocab_local * d
+        head_rows = self.embed_ptr() + self.wb * self.rank * self.vocab_local * d
         hb = Binding(weights={"embed": head_rows, "final_norm": self.final_norm_ptr()}, ints=ints, m=m,
                      values={"x": View(self.x, 0, d, d),
                              "logits": View(self.logits, 0, self.vocab_local, self.vocab_local),
@@ -443,13 +496,15 @@ class Llama:
         attend_decode launch (the same bits); the combine follows."""
         out, i = [], 0
         while i < len(launches):
-            if i + 1 < len(launches) and [L.kernel for L in launches[i:i + 2]] == ["kv_store_ring", "attend_split"]:
+            pair = [kernel_form(L.kernel) for L in launches[i:i + 2]]
+            if (i + 1 < len(launches) and [b for b, _ in pair] == ["kv_store_ring", "attend_split"]
+                    and pair[0][1] == pair[1][1]):
                 kv, at = launches[i:i + 2]
                 same = (kv.bufs[0] == at.bufs[0] and list(kv.bufs[3:7]) == list(at.bufs[3:7])
                         and all(kv.params[k] == at.params[k] for k in ("ldq", "rotated", "d", "kv_heads", "length")))
                 if same:
                     p = dict(at.params, k_off=kv.params["k_off"], v_off=kv.params["v_off"])
-                    out.append(Launch("attend_decode", p, list(at.bufs)))
+                    out.append(Launch("attend_decode" + pair[0][1], p, list(at.bufs)))
                     i += 2
                     continue
             out.append(launches[i])
@@ -466,16 +521,17 @@ class Llama:
         out = list(launches)
         for i in range(len(out) - 1):
             a, b = out[i], out[i + 1]
-            if (a.kernel == "gemv_rmsnorm" and a.bufs[3] == gu and a.params["n"] == 2 * f
-                    and b.kernel in ("gemv_silu", "gemv_silu_add") and b.bufs[1] == gu and b.params["up_off"] == f):
-                out[i] = Launch("gemv_rmsnorm_silu", dict(a.params, ldy=f), [a.bufs[0], a.bufs[1], a.bufs[2],
-                                                                              self.act.ptr])
+            (ab, asuf), (bb, bsuf) = kernel_form(a.kernel), kernel_form(b.kernel)
+            if (ab == "gemv_rmsnorm" and a.bufs[3] == gu and a.params["n"] == 2 * f
+                    and bb in ("gemv_silu", "gemv_silu_add") and b.bufs[1] == gu and b.params["up_off"] == f):
+                out[i] = Launch("gemv_rmsnorm_silu" + asuf, dict(a.params, ldy=f),
+                                [a.bufs[0], a.bufs[1], a.bufs[2], self.act.ptr])
                 params = {k: v for k, v in b.params.items() if k != "up_off"}
                 params["ldx"] = f
-                if b.kernel == "gemv_silu_add":
-                    out[i + 1] = Launch("gemv_add", params, [b.bufs[0], self.act.ptr, b.bufs[2], b.bufs[3]])
+                if bb == "gemv_silu_add":
+                    out[i + 1] = Launch("gemv_add" + bsuf, params, [b.bufs[0], self.act.ptr, b.bufs[2], b.bufs[3]])
                 else:
-                    out[i + 1] = Launch("gemv", params, [b.bufs[0], self.act.ptr, b.bufs[2]])
+                    out[i + 1] = Launch("gemv" + bsuf, params, [b.bufs[0], self.act.ptr, b.bufs[2]])
         return out
 
     def _tensor_parallel(self, launches: list) -> list:
@@ -492,22 +548,23 @@ class Llama:
         same way. The same launches as on one GPU, no collective."""
         out, pending = [], None  # pending: (buffer, residual, where the sum goes)
         for L in launches:
-            if L.kernel == "gemv_add":
+            base, suf = kernel_form(L.kernel)
+            if base == "gemv_add":
                 w, x, r, y = L.bufs
                 xbuf = 0 if pending is None or pending[0] == 1 else 1
                 p = L.params
                 if p["ldy"] != self.s.d_model or p["ldr"] != self.s.d_model:
                     raise Unlowerable(N.FKC_ERR_ARGUMENT, "a row-parallel output that is not a whole row.")
-                out.append(Launch("gemv_scatter", {"n": p["n"], "k": p["k"], "m": p["m"], "split": p["split"],
-                                                   "ldx": p["ldx"], "xbuf": xbuf}, [w, x]))
+                out.append(Launch("gemv_scatter" + suf, {"n": p["n"], "k": p["k"], "m": p["m"], "split": p["split"],
+                                                         "ldx": p["ldx"], "xbuf": xbuf}, [w, x]))
                 pending = (xbuf, r, y)
-            elif pending is not None and L.kernel in ("gemv_rmsnorm", "gemv_rmsnorm_silu") and L.bufs[1] == pending[2]:
+            elif pending is not None and base in ("gemv_rmsnorm", "gemv_rmsnorm_silu") and L.bufs[1] == pending[2]:
                 w, x, gamma, y = L.bufs
                 p = dict(L.params)
                 p.pop("ldx")
                 p.update(ldr=self.s.d_model, xbuf=pending[0])
-                name = "gemv_reduce_rmsnorm_silu" if L.kernel == "gemv_rmsnorm_silu" else "gemv_reduce_rmsnorm"
-                out.append(Launch(name, p, [w, pending[1], gamma, pending[2], y]))
+                name = "gemv_reduce_rmsnorm_silu" if base == "gemv_rmsnorm_silu" else "gemv_reduce_rmsnorm"
+                out.append(Launch(name + suf, p, [w, pending[1], gamma, pending[2], y]))
                 pending = (pending[0], None, None)  # consumed; the buffer alternates on
             elif L.kernel == "argmax":
                 x, ids = L.bufs
@@ -525,12 +582,13 @@ class Llama:
         P = self.partial.ptr
         out = []
         for L in launches:
-            if L.kernel in ("gemv_add", "gemv_silu_add"):
+            base, suf = kernel_form(L.kernel)
+            if base in ("gemv_add", "gemv_silu_add"):
                 w, x, r, y = L.bufs
                 params = {k: v for k, v in L.params.items() if k != "ldr"}
                 if params["ldy"] != d or L.params["ldr"] != d:
                     raise Unlowerable(N.FKC_ERR_ARGUMENT, "a row-parallel output that is not a whole row.")
-                out.append(Launch(L.kernel[:-4], params, [w, x, P]))
+                out.append(Launch(base[:-4] + suf, params, [w, x, P]))
                 out.append(Launch("__allreduce__", {"count": m * d}, [P]))
                 out.append(Launch("add", {"n": m * d}, [r, P, y]))
             elif L.kernel == "argmax":
@@ -603,13 +661,13 @@ class Llama:
         """The weights a step streams on this rank: the layers' shards, the
         LM head's vocabulary rows and the final norm."""
         s = self.s
-        return 4 * (s.layers * self.layer_elems + self.vocab_local * s.d_model + s.d_model)
+        return self.wb * (s.layers * self.layer_elems + self.vocab_local * s.d_model + s.d_model)
 
     def algorithmic_bytes(self, contexts) -> int:
         """Bytes a decode step must move on this rank: every weight once, each
         row's keys and values over its context, per layer."""
         s = self.s
-        kv = sum(2 * s.kv_heads * s.head_dim * 4 * (int(c) + 1) for c in contexts) * s.layers
+        kv = sum(2 * s.kv_heads * s.head_dim * self.cb * (int(c) + 1) for c in contexts) * s.layers
         return self.weight_bytes() + kv
 
 

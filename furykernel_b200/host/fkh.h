@@ -161,11 +161,15 @@ class Builder {
 };
 
 // The Llama-shaped programs of this path (one decoder layer, the embedding,
-// the head), all f32 (furykernel_b200/program/llama.py states them too).
+// the head): f32 activations; f32 or bf16 weights and KV caches
+// (furykernel_b200/program/llama.py states them too).
 struct LlamaShape {
   uint64_t d_model = 4096, heads = 32, kv_heads = 32, head_dim = 128, ffn = 11008, vocab = 32000, layers = 32;
   double theta = 10000.0, eps = 1e-5;
   uint64_t slots = 1, length = 4096, positions = 4096;
+  std::string weights = "f32", cache = "f32";  // element types: "f32" or "bf16"
+  uint64_t weight_bytes() const { return weights == "bf16" ? 2 : 4; }
+  uint64_t cache_bytes() const { return cache == "bf16" ? 2 : 4; }
   uint64_t q_width() const { return heads * head_dim; }
   uint64_t kv_width() const { return kv_heads * head_dim; }
 };
@@ -250,6 +254,12 @@ struct AttnBufs {
 
 Launch lower_step(const Program& p, const Step& step, const Binding& b, uint64_t cos_t, uint64_t sin_t,
                   const AttnBufs& attn);
+
+// A kernel's element-type form: the f32 entry's name, or with the suffix of
+// its bf16 weights (kW16) or its bf16 KV caches (kKV16).
+constexpr const char* kW16 = "_wbf16";
+constexpr const char* kKV16 = "_kvbf16";
+std::pair<std::string, std::string> kernel_form(const std::string& kernel);
 
 // The whole decode step of the Llama engine (furykernel_b200/engine.py):
 // every address the launches bind, the shape and the choices.

@@ -59,6 +59,8 @@ fkh::LlamaShape shape_of(const fkh_llama_shape& s) {
   o.slots = s.slots;
   o.length = s.length;
   o.positions = s.positions;
+  o.weights = s.weights_bf16 ? "bf16" : "f32";
+  o.cache = s.cache_bf16 ? "bf16" : "f32";
   if (!o.heads || !o.kv_heads || o.heads % o.kv_heads || !o.head_dim || o.head_dim % 2 || !o.d_model ||
       !o.ffn || !o.vocab || !o.slots || !o.length || !o.positions)
     throw fkh::Refusal("the Llama shape has an empty or uneven dimension.");

@@ -48,7 +48,28 @@ typename M::mapped_type at(const M& m, const std::string& key, const std::string
   return it->second;
 }
 
+std::string weight_suffix(const Step& step, const std::string& t) {
+  if (t == "f32") return "";
+  if (t == "bf16") return kW16;
+  throw Refusal(step.name + ": no kernel reads " + t + " weights.");
+}
+
+std::string cache_suffix(const Step& step, const std::string& elem) {
+  if (elem == "f32") return "";
+  if (elem == "bf16") return kKV16;
+  throw Refusal(step.name + ": no kernel reads " + elem + " caches.");
+}
+
 }  // namespace
+
+std::pair<std::string, std::string> kernel_form(const std::string& kernel) {
+  for (const char* suffix : {kW16, kKV16}) {
+    const size_t n = std::char_traits<char>::length(suffix);
+    if (kernel.size() > n && kernel.compare(kernel.size() - n, n, suffix) == 0)
+      return {kernel.substr(0, kernel.size() - n), suffix};
+  }
+  return {kernel, ""};
+}
 
 Launch lower_step(const Program& p, const Step& step, const Binding& b, uint64_t cos_t, uint64_t sin_t,
                   const AttnBufs& attn) {
@@ -84,6 +105,12 @@ Launch lower_step(const Program& p, const Step& step, const Binding& b, uint64_t
     for (const Node* n : anchors)
       if (n->op.values[0] != x_id)
         throw Refusal(step.name + ": anchors of different inputs: " + work_text(p, step));
+    const std::string& wtype = p.sources[anchors[0]->op.sources[0]].kind.type;
+    for (const Node* n : anchors)
+      if (p.sources[n->op.sources[0]].kind.type != wtype)
+        throw Refusal(step.name + ": its anchors' weights differ in type.");
+    const std::string wt = weight_suffix(step, wtype);
+    const uint64_t esz = wt.empty() ? 4 : 2;
     const uint64_t w0 = at(b.weights, src_name(anchors[0]->op.sources[0]), step.name);
     uint64_t n_total = 0;
     const uint64_t k = p.sources[anchors[0]->op.sources[0]].kind.dims[1];
@@ -92,7 +119,7 @@ Launch lower_step(const Program& p, const Step& step, const Binding& b, uint64_t
       const Source& w = p.sources[n->op.sources[0]];
       if (at(b.weights, w.name, step.name) != addr)
         throw Refusal(step.name + ": the weights of its anchors are not adjacent.");
-      addr += 4 * w.kind.dims[0] * k;
+      addr += esz * w.kind.dims[0] * k;
       n_total += w.kind.dims[0];
     }
     View y;
@@ -119,19 +146,21 @@ Launch lower_step(const Program& p, const Step& step, const Binding& b, uint64_t
       L.set("ldx", (double)x.ld);
       if (!epilogues.empty()) {
         const View r = stored(r_id);
-        L.kernel = "gemv_add";
+        L.kernel = "gemv_add" + wt;
         L.set("ldr", (double)r.ld);
         L.bufs = {w0, x.ptr(), r.ptr(), y.ptr()};
         return L;
       }
-      L.kernel = "gemv";
+      L.kernel = "gemv" + wt;
       L.bufs = {w0, x.ptr(), y.ptr()};
       return L;
     }
     if (xn->op.kind == "RmsNorm" && epilogues.empty()) {
       const View x = stored(xn->op.values[0]);
+      if (p.sources[xn->op.sources[0]].kind.type != wtype)
+        throw Refusal(step.name + ": the norm's gain and the weights differ in type.");
       const uint64_t gamma = at(b.weights, src_name(xn->op.sources[0]), step.name);
-      L.kernel = "gemv_rmsnorm";
+      L.kernel = "gemv_rmsnorm" + wt;
       L.set("ldx", (double)x.ld);
       L.set("eps", xn->op.eps);
       L.set("factor", xn->op.factor);
@@ -145,12 +174,12 @@ Launch lower_step(const Program& p, const Step& step, const Binding& b, uint64_t
       L.set("up_off", (double)(u.col - g.col));
       if (!epilogues.empty()) {
         const View r = stored(r_id);
-        L.kernel = "gemv_silu_add";
+        L.kernel = "gemv_silu_add" + wt;
         L.set("ldr", (double)r.ld);
         L.bufs = {w0, g.ptr(), r.ptr(), y.ptr()};
         return L;
       }
-      L.kernel = "gemv_silu";
+      L.kernel = "gemv_silu" + wt;
       L.bufs = {w0, g.ptr(), y.ptr()};
       return L;
     }
@@ -165,7 +194,7 @@ Launch lower_step(const Program& p, const Step& step, const Binding& b, uint64_t
     const View q = stored(qn->op.values[0]);
     const Source& kc = p.sources[att->op.sources[0]];
     Launch L;
-    L.kernel = "attend_split";
+    L.kernel = "attend_split" + cache_suffix(step, kc.kind.elem);
     L.params = {{"m", m},
                 {"heads", (double)spec.heads},
                 {"kv_heads", (double)spec.kv_heads},
@@ -219,7 +248,7 @@ Launch lower_step(const Program& p, const Step& step, const Binding& b, uint64_t
     if (kview.base != vview.base) throw Refusal(step.name + ": keys and values are not one row.");
     const Source& kc = p.sources[sk->op.sources[0]];
     Launch L;
-    L.kernel = "kv_store_ring";
+    L.kernel = "kv_store_ring" + cache_suffix(step, kc.kind.elem);
     L.params = {{"m", m},
                 {"kv_heads", (double)kc.kind.r.kv_heads},
                 {"d", (double)kc.kind.r.head_dim},
@@ -245,7 +274,7 @@ Launch lower_step(const Program& p, const Step& step, const Binding& b, uint64_t
       const Source& tok = p.sources[n->op.sources[1]];
       const View y = stored(n->outputs[0]);
       Launch L;
-      L.kernel = "gather";
+      L.kernel = "gather" + weight_suffix(step, table.kind.type);
       L.params = {{"width", (double)table.kind.dims[1]}, {"m", m}, {"factor", n->op.f}};
       L.bufs = {at(b.weights, table.name, step.name), at(b.ints, tok.name, step.name), y.ptr()};
       return L;
@@ -279,10 +308,12 @@ void silu_on_tiles(std::vector<Launch>& out, uint64_t f, uint64_t gu, uint64_t a
   for (size_t i = 0; i + 1 < out.size(); ++i) {
     Launch& a = out[i];
     Launch& b = out[i + 1];
-    if (a.kernel == "gemv_rmsnorm" && a.bufs[3] == gu && a.param("n") == 2.0 * f &&
-        (b.kernel == "gemv_silu" || b.kernel == "gemv_silu_add") && b.bufs[1] == gu && b.param("up_off") == f) {
+    const auto [ab, asuf] = kernel_form(a.kernel);
+    const auto [bb, bsuf] = kernel_form(b.kernel);
+    if (ab == "gemv_rmsnorm" && a.bufs[3] == gu && a.param("n") == 2.0 * f &&
+        (bb == "gemv_silu" || bb == "gemv_silu_add") && b.bufs[1] == gu && b.param("up_off") == f) {
       Launch na;
-      na.kernel = "gemv_rmsnorm_silu";
+      na.kernel = "gemv_rmsnorm_silu" + asuf;
       na.params = a.params;
       na.set("ldy", (double)f);
       na.bufs = {a.bufs[0], a.bufs[1], a.bufs[2], act};
@@ -290,11 +321,11 @@ void silu_on_tiles(std::vector<Launch>& out, uint64_t f, uint64_t gu, uint64_t a
       for (const auto& kv : b.params)
         if (kv.first != "up_off") nb.params.push_back(kv);
       nb.set("ldx", (double)f);
-      if (b.kernel == "gemv_silu_add") {
-        nb.kernel = "gemv_add";
+      if (bb == "gemv_silu_add") {
+        nb.kernel = "gemv_add" + bsuf;
         nb.bufs = {b.bufs[0], act, b.bufs[2], b.bufs[3]};
       } else {
-        nb.kernel = "gemv";
+        nb.kernel = "gemv" + bsuf;
         nb.bufs = {b.bufs[0], act, b.bufs[2]};
       }
       a = na;
@@ -319,21 +350,22 @@ std::vector<Launch> tensor_parallel_peers(const std::vector<Launch>& in, const L
   std::optional<Pending> pending;
   const uint64_t dm = d.full.d_model;
   for (const Launch& L : in) {
-    if (L.kernel == "gemv_add") {
+    const auto [base, suf] = kernel_form(L.kernel);
+    if (base == "gemv_add") {
       const int xbuf = !pending || pending->buf == 1 ? 0 : 1;
       if (L.param("ldy") != dm || L.param("ldr") != dm)
         throw Refusal("a row-parallel output that is not a whole row.");
       Launch s;
-      s.kernel = "gemv_scatter";
+      s.kernel = "gemv_scatter" + suf;
       s.params = {{"n", L.param("n")}, {"k", L.param("k")}, {"m", L.param("m")}, {"split", L.param("split")},
                   {"ldx", L.param("ldx")}, {"xbuf", (double)xbuf}};
       s.bufs = {L.bufs[0], L.bufs[1]};
       out.push_back(s);
       pending = Pending{xbuf, L.bufs[2], L.bufs[3], true};
-    } else if (pending && pending->live && (L.kernel == "gemv_rmsnorm" || L.kernel == "gemv_rmsnorm_silu") &&
+    } else if (pending && pending->live && (base == "gemv_rmsnorm" || base == "gemv_rmsnorm_silu") &&
                L.bufs[1] == pending->y) {
       Launch r;
-      r.kernel = L.kernel == "gemv_rmsnorm_silu" ? "gemv_reduce_rmsnorm_silu" : "gemv_reduce_rmsnorm";
+      r.kernel = (base == "gemv_rmsnorm_silu" ? "gemv_reduce_rmsnorm_silu" : "gemv_reduce_rmsnorm") + suf;
       for (const auto& kv : L.params)
         if (kv.first != "ldx") r.params.push_back(kv);
       r.set("ldr", (double)dm);
@@ -368,11 +400,12 @@ std::vector<Launch> tensor_parallel_nccl(const std::vector<Launch>& in, const Ll
   std::vector<Launch> out;
   const uint64_t dm = d.full.d_model, m = d.batch;
   for (const Launch& L : in) {
-    if (L.kernel == "gemv_add" || L.kernel == "gemv_silu_add") {
+    const auto [base, suf] = kernel_form(L.kernel);
+    if (base == "gemv_add" || base == "gemv_silu_add") {
       if (L.param("ldy") != dm || L.param("ldr") != dm)
         throw Refusal("a row-parallel output that is not a whole row.");
       Launch g;
-      g.kernel = L.kernel.substr(0, L.kernel.size() - 4);
+      g.kernel = base.substr(0, base.size() - 4) + suf;
       for (const auto& kv : L.params)
         if (kv.first != "ldr") g.params.push_back(kv);
       g.bufs = {L.bufs[0], L.bufs[1], d.partial};
@@ -416,7 +449,9 @@ std::vector<Launch> tensor_parallel_nccl(const std::vector<Launch>& in, const Ll
 std::vector<Launch> fuse_attention(const std::vector<Launch>& in) {
   std::vector<Launch> out;
   for (size_t i = 0; i < in.size(); ++i) {
-    if (i + 1 < in.size() && in[i].kernel == "kv_store_ring" && in[i + 1].kernel == "attend_split") {
+    const auto kvf = kernel_form(in[i].kernel);
+    const auto atf = i + 1 < in.size() ? kernel_form(in[i + 1].kernel) : std::pair<std::string, std::string>{};
+    if (i + 1 < in.size() && kvf.first == "kv_store_ring" && atf.first == "attend_split" && kvf.second == atf.second) {
       const Launch& kv = in[i];
       const Launch& at = in[i + 1];
       bool same = kv.bufs[0] == at.bufs[0] &&
@@ -425,7 +460,7 @@ std::vector<Launch> fuse_attention(const std::vector<Launch>& in) {
         if (kv.param(k) != at.param(k)) same = false;
       if (same) {
         Launch f;
-        f.kernel = "attend_decode";
+        f.kernel = "attend_decode" + kvf.second;
         f.params = at.params;
         f.set("k_off", kv.param("k_off"));
         f.set("v_off", kv.param("v_off"));
@@ -465,10 +500,11 @@ std::map<std::string, uint64_t> layer_weights(const LlamaShape& s, uint64_t aren
   const char* names[9] = {"q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj", "attn_norm",
                           "mlp_norm"};
   std::map<std::string, uint64_t> w;
-  uint64_t at = arena + 4 * l * layer_elems(s);
+  const uint64_t wb = s.weight_bytes();
+  uint64_t at = arena + wb * l * layer_elems(s);
   for (int i = 0; i < 9; ++i) {
     w[names[i]] = at;
-    at += 4 * sizes[i];
+    at += wb * sizes[i];
   }
   return w;
 }
@@ -478,8 +514,9 @@ std::vector<Launch> llama_launches(const LlamaLaunchDesc& d) {
   const LlamaShape s = shard_of(d);
   const uint64_t m = d.batch, dm = s.d_model, qw = s.q_width(), kvw = s.kv_width(), f = s.ffn;
   const uint64_t vocab_local = full.vocab / d.world;
-  const uint64_t embed_ptr = d.arena + 4 * s.layers * layer_elems(s);
-  const uint64_t final_norm_ptr = embed_ptr + 4 * full.vocab * full.d_model;
+  const uint64_t wb = s.weight_bytes();
+  const uint64_t embed_ptr = d.arena + wb * s.layers * layer_elems(s);
+  const uint64_t final_norm_ptr = embed_ptr + wb * full.vocab * full.d_model;
 
   PlanOptions layer_opts;
   layer_opts.sequence_rows = s.slots == 1 ? m : 1;
@@ -505,7 +542,7 @@ std::vector<Launch> llama_launches(const LlamaLaunchDesc& d) {
     for (const Step& st : embed_plan.steps)
       out.push_back(lower_step(embed_plan.program, st, eb, d.cos_t, d.sin_t, attn));
   }
-  const uint64_t per_cache = 4 * s.slots * s.kv_heads * s.length * s.head_dim;
+  const uint64_t per_cache = s.cache_bytes() * s.slots * s.kv_heads * s.length * s.head_dim;
   for (uint64_t l = 0; l < s.layers; ++l) {
     Binding b;
     b.weights = layer_weights(s, d.arena, l);
@@ -526,7 +563,7 @@ std::vector<Launch> llama_launches(const LlamaLaunchDesc& d) {
   }
   {
     Binding hb;
-    hb.weights = {{"embed", embed_ptr + 4 * d.rank * vocab_local * full.d_model}, {"final_norm", final_norm_ptr}};
+    hb.weights = {{"embed", embed_ptr + wb * d.rank * vocab_local * full.d_model}, {"final_norm", final_norm_ptr}};
     hb.ints = ints;
     hb.m = m;
     hb.values = {{"x", View{d.x, 0, dm, dm}},

@@ -36,8 +36,12 @@ std::vector<Launch> prefill_launches(const LlamaLaunchDesc& d, const PrefillDesc
   const uint64_t max_splits = (p.positions + p.chunk - 1) / p.chunk;
   const std::vector<Launch> decode = llama_launches(d);
 
+  // The decode launches by their f32 entries' names; the forms follow the
+  // model's element types.
   std::map<std::string, std::vector<const Launch*>> by;
-  for (const Launch& L : decode) by[L.kernel].push_back(&L);
+  for (const Launch& L : decode) by[kernel_form(L.kernel).first].push_back(&L);
+  const std::string wsuf = s.weights == "bf16" ? kW16 : "";
+  const std::string csuf = s.cache == "bf16" ? kKV16 : "";
   auto need = [&](const std::string& k, uint64_t i) -> const Launch& {
     auto it = by.find(k);
     if (it == by.end() || it->second.size() <= i) throw Refusal("prefill: the decode step has no " + k + " launch.");
@@ -49,7 +53,7 @@ std::vector<Launch> prefill_launches(const LlamaLaunchDesc& d, const PrefillDesc
   if (by.count("attend_decode")) {
     unfused.reserve(2 * by["attend_decode"].size());
     for (const Launch* L : by["attend_decode"]) {
-      unfused.push_back(make("kv_store_ring",
+      unfused.push_back(make("kv_store_ring" + csuf,
                              {{"m", L->param("m")},
                               {"kv_heads", L->param("kv_heads")},
                               {"d", L->param("d")},
@@ -63,9 +67,9 @@ std::vector<Launch> prefill_launches(const LlamaLaunchDesc& d, const PrefillDesc
       for (const char* k : {"m", "heads", "kv_heads", "d", "length", "rotated", "chunk", "max_splits", "ldq", "q_off",
                             "scale"})
         ap.emplace_back(k, L->param(k));
-      unfused.push_back(make("attend_split", ap, {L->bufs.begin(), L->bufs.begin() + 10}));
+      unfused.push_back(make("attend_split" + csuf, ap, {L->bufs.begin(), L->bufs.begin() + 10}));
     }
-    for (const Launch& L : unfused) by[L.kernel].push_back(&L);
+    for (const Launch& L : unfused) by[kernel_form(L.kernel).first].push_back(&L);
   }
   double eps = 0;
   bool have_eps = false;
@@ -77,8 +81,10 @@ std::vector<Launch> prefill_launches(const LlamaLaunchDesc& d, const PrefillDesc
     }
   if (!have_eps) throw Refusal("prefill: the decode step normalizes nothing.");
 
-  auto hi = [&](uint64_t w) { return p.w_hi + (w - d.arena); };
-  auto lo = [&](uint64_t w) { return p.w_lo + (w - d.arena); };
+  // The TF32 halves are f32 arenas laid out as the weight arena.
+  const uint64_t wb = s.weight_bytes();
+  auto hi = [&](uint64_t w) { return p.w_hi + (w - d.arena) * 4 / wb; };
+  auto lo = [&](uint64_t w) { return p.w_lo + (w - d.arena) * 4 / wb; };
   auto gemm = [&](uint64_t a, uint64_t K, uint64_t w, uint64_t N, uint64_t c, uint64_t ldc) {
     return make("gemm_tf32x3", {{"M", (double)m}, {"N", (double)N}, {"K", (double)K}, {"ldc", (double)ldc}},
                 {a, p.a_hi, p.a_lo, hi(w), lo(w), c});
@@ -93,13 +99,13 @@ std::vector<Launch> prefill_launches(const LlamaLaunchDesc& d, const PrefillDesc
     const Launch& kv = need("kv_store_ring", l);
     const Launch& at = need("attend_split", l);
     const Launch& cb = need("attend_combine", l);
-    out.push_back(make("rmsnorm_rows", {{"rows", md}, {"h", (double)dm}, {"eps", eps}, {"factor", 1.0}},
+    out.push_back(make("rmsnorm_rows" + wsuf, {{"rows", md}, {"h", (double)dm}, {"eps", eps}, {"factor", 1.0}},
                        {p.x, w.at("attn_norm"), p.a}));
     out.push_back(gemm(p.a, dm, w.at("q_proj"), nq, p.qkv, nq));
     out.push_back(with(kv, {{"m", md}, {"ldq", (double)nq}},
                        {p.qkv, kv.bufs[1], kv.bufs[2], p.pos, p.slot, kv.bufs[5], kv.bufs[6]}));
     if (p.one_slot) {
-      out.push_back(make("attend_prompt",
+      out.push_back(make("attend_prompt" + csuf,
                          {{"m", md},
                           {"heads", at.param("heads")},
                           {"kv_heads", at.param("kv_heads")},
@@ -128,7 +134,7 @@ std::vector<Launch> prefill_launches(const LlamaLaunchDesc& d, const PrefillDesc
     out.push_back(gemm(p.att, qw, w.at("o_proj"), dm, p.tmp, dm));
     if (d.world > 1) out.push_back(make("__allreduce__", {{"count", (double)(m * dm)}}, {p.tmp}));
     out.push_back(make("add", {{"n", (double)(m * dm)}}, {p.x, p.tmp, p.x1}));
-    out.push_back(make("rmsnorm_rows", {{"rows", md}, {"h", (double)dm}, {"eps", eps}, {"factor", 1.0}},
+    out.push_back(make("rmsnorm_rows" + wsuf, {{"rows", md}, {"h", (double)dm}, {"eps", eps}, {"factor", 1.0}},
                        {p.x1, w.at("mlp_norm"), p.a}));
     if (d.gate_up_interleaved) {  // rows gate_0, up_0, ...: the GEMM's columns likewise
       out.push_back(gemm(p.a, dm, w.at("gate_proj"), 2 * f, p.gu, 2 * f));

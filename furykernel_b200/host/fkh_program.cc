@@ -208,18 +208,18 @@ Program layer_program(const LlamaShape& s, const std::string& name) {
   const int x = b.input("x", whole_row(s.d_model));
   const int pos = b.row_ints("position", 1, s.positions);
   const int slot = b.row_ints("slot", 1, s.slots);
-  const int attn_norm = b.weight("attn_norm", {s.d_model}, "f32");
-  const int wq = b.weight("q_proj", {s.q_width(), s.d_model}, "f32");
-  const int wk = b.weight("k_proj", {s.kv_width(), s.d_model}, "f32");
-  const int wv = b.weight("v_proj", {s.kv_width(), s.d_model}, "f32");
-  const int wo = b.weight("o_proj", {s.d_model, s.q_width()}, "f32");
-  const int mlp_norm = b.weight("mlp_norm", {s.d_model}, "f32");
-  const int wg = b.weight("gate_proj", {s.ffn, s.d_model}, "f32");
-  const int wu = b.weight("up_proj", {s.ffn, s.d_model}, "f32");
-  const int wd = b.weight("down_proj", {s.d_model, s.ffn}, "f32");
+  const int attn_norm = b.weight("attn_norm", {s.d_model}, s.weights);
+  const int wq = b.weight("q_proj", {s.q_width(), s.d_model}, s.weights);
+  const int wk = b.weight("k_proj", {s.kv_width(), s.d_model}, s.weights);
+  const int wv = b.weight("v_proj", {s.kv_width(), s.d_model}, s.weights);
+  const int wo = b.weight("o_proj", {s.d_model, s.q_width()}, s.weights);
+  const int mlp_norm = b.weight("mlp_norm", {s.d_model}, s.weights);
+  const int wg = b.weight("gate_proj", {s.ffn, s.d_model}, s.weights);
+  const int wu = b.weight("up_proj", {s.ffn, s.d_model}, s.weights);
+  const int wd = b.weight("down_proj", {s.d_model, s.ffn}, s.weights);
   const Ring ring{s.slots, s.kv_heads, s.length, s.head_dim};
-  const int kc = b.cache("k_cache", ring, "f32");
-  const int vc = b.cache("v_cache", ring, "f32");
+  const int kc = b.cache("k_cache", ring, s.cache);
+  const int vc = b.cache("v_cache", ring, s.cache);
   const int a = b.rmsnorm("attn_in", s.eps, attn_norm, 1.0, x);
   const int q = b.linear("q", wq, s.head_dim, a);
   const int k = b.linear("k", wk, s.head_dim, a);
@@ -250,7 +250,7 @@ Program layer_program(const LlamaShape& s, const std::string& name) {
 Program embed_program(const LlamaShape& s) {
   Builder b("embed");
   const int tok = b.row_ints("token", 1, s.vocab);
-  const int table = b.weight("embed", {s.vocab, s.d_model}, "f32");
+  const int table = b.weight("embed", {s.vocab, s.d_model}, s.weights);
   const int x = b.gather("x", table, tok, 1.0);
   b.output("x", x);
   return b.done();
@@ -259,8 +259,8 @@ Program embed_program(const LlamaShape& s) {
 Program head_program(const LlamaShape& s) {
   Builder b("head");
   const int x = b.input("x", whole_row(s.d_model));
-  const int norm = b.weight("final_norm", {s.d_model}, "f32");
-  const int embed = b.weight("embed", {s.vocab, s.d_model}, "f32");
+  const int norm = b.weight("final_norm", {s.d_model}, s.weights);
+  const int embed = b.weight("embed", {s.vocab, s.d_model}, s.weights);
   const int n = b.rmsnorm("final_normed", s.eps, norm, 1.0, x);
   const int logits = b.linear("logits", embed, 0, n);
   const int token = b.argmax("token", logits);

@@ -33,7 +33,7 @@ from __future__ import annotations
 import numpy as np
 
 from . import _native as N
-from .engine import Launch, Llama
+from .engine import KV16, W16, Launch, Llama, kernel_form
 
 
 class Prefill:
@@ -51,12 +51,14 @@ class Prefill:
                 raise N.Refused(N.FKC_ERR_ARGUMENT, f"prefill: the GEMM's K ({what} {k}) is not a multiple of 32.")
         # The layers' TF32 halves, laid out as the weight arena, a layer a
         # launch.
+        # (bf16 weights: the widened weight is the high half, the low half 0.)
         per = eng.layer_elems
         self.w_hi = ctx.alloc(4 * s.layers * per)
         self.w_lo = ctx.alloc(4 * s.layers * per)
+        split = "split_tf32" + (W16 if eng.wb == 2 else "")
         for l in range(s.layers):
             at = 4 * l * per
-            ctx.launch("split_tf32", {"n": per}, [eng.arena.ptr + at, self.w_hi.ptr + at, self.w_lo.ptr + at])
+            ctx.launch(split, {"n": per}, [eng.arena.ptr + eng.wb * l * per, self.w_hi.ptr + at, self.w_lo.ptr + at])
         R = rows
         kmax = max(d, qw, f)
         self.rs = (R + 3) // 4 * 4
@@ -85,10 +87,10 @@ class Prefill:
         self.graphs: dict = {}
 
     def _hi(self, ptr: int) -> int:
-        return self.w_hi.ptr + (ptr - self.eng.arena.ptr)
+        return self.w_hi.ptr + (ptr - self.eng.arena.ptr) * 4 // self.eng.wb
 
     def _lo(self, ptr: int) -> int:
-        return self.w_lo.ptr + (ptr - self.eng.arena.ptr)
+        return self.w_lo.ptr + (ptr - self.eng.arena.ptr) * 4 // self.eng.wb
 
     def _gemm(self, a, K: int, w: int, N: int, c, ldc: int) -> Launch:
         return Launch("gemm_tf32x3", {"M": self.m, "N": N, "K": K, "ldc": ldc},
@@ -124,17 +126,19 @@ class Prefill:
         # the KV stores and the attention (their shapes and tables).
         by = {}
         for L in eng.launches:
-            by.setdefault(L.kernel, []).append(L)
+            by.setdefault(kernel_form(L.kernel)[0], []).append(L)
+        wsuf = W16 if eng.wb == 2 else ""
+        csuf = KV16 if eng.cb == 2 else ""
         g0 = by["gather"][0]
-        out = [Launch("gather", dict(g0.params, m=m), [g0.bufs[0], tok, self.x.ptr])]
+        out = [Launch(g0.kernel, dict(g0.params, m=m), [g0.bufs[0], tok, self.x.ptr])]
         if "attend_decode" in by:  # the decode step fused them: split its launches back into the two steps
             for L in by["attend_decode"]:
                 p = L.params
-                by.setdefault("kv_store_ring", []).append(Launch("kv_store_ring", {
+                by.setdefault("kv_store_ring", []).append(Launch("kv_store_ring" + csuf, {
                     "m": p["m"], "kv_heads": p["kv_heads"], "d": p["d"], "length": p["length"],
                     "rotated": p["rotated"], "ldq": p["ldq"], "k_off": p["k_off"], "v_off": p["v_off"]},
                     L.bufs[:7]))
-                by.setdefault("attend_split", []).append(Launch("attend_split", {
+                by.setdefault("attend_split", []).append(Launch("attend_split" + csuf, {
                     k: p[k] for k in ("m", "heads", "kv_heads", "d", "length", "rotated", "chunk", "max_splits",
                                       "ldq", "q_off", "scale")}, L.bufs[:10]))
         eps = None
@@ -146,20 +150,20 @@ class Prefill:
         for l in range(s.layers):
             w = eng.layer_weights(l)
             kv, at, cb = by["kv_store_ring"][l], by["attend_split"][l], by["attend_combine"][l]
-            out.append(Launch("rmsnorm_rows", {"rows": m, "h": d, "eps": eps, "factor": 1.0},
+            out.append(Launch("rmsnorm_rows" + wsuf, {"rows": m, "h": d, "eps": eps, "factor": 1.0},
                               [self.x.ptr, w["attn_norm"], self.a.ptr]))
             out.append(self._gemm(self.a.ptr, d, w["q_proj"], nq, self.qkv.ptr, nq))
-            out.append(Launch("kv_store_ring", dict(kv.params, m=m, ldq=nq),
+            out.append(Launch(kv.kernel, dict(kv.params, m=m, ldq=nq),
                               [self.qkv.ptr, kv.bufs[1], kv.bufs[2], pos, slot, kv.bufs[5], kv.bufs[6]]))
             if self.one_slot:
                 ap = at.params
-                out.append(Launch("attend_prompt", {
+                out.append(Launch("attend_prompt" + csuf, {
                     "m": m, "heads": ap["heads"], "kv_heads": ap["kv_heads"], "d": ap["d"], "length": ap["length"],
                     "rotated": ap["rotated"], "ldq": nq, "q_off": ap["q_off"], "ldo": qw,
                     "max_pos": self.positions - 1, "scale": ap["scale"]},
                     [self.qkv.ptr, at.bufs[1], at.bufs[2], pos, slot, at.bufs[5], at.bufs[6], self.att.ptr]))
             else:
-                out.append(Launch("attend_split", dict(at.params, m=m, ldq=nq, chunk=self.chunk,
+                out.append(Launch(at.kernel, dict(at.params, m=m, ldq=nq, chunk=self.chunk,
                                                        max_splits=self.max_splits),
                                   [self.qkv.ptr, at.bufs[1], at.bufs[2], pos, slot, at.bufs[5], at.bufs[6],
                                    self.part[0].ptr, self.part[1].ptr, self.part[2].ptr]))
@@ -170,7 +174,7 @@ class Prefill:
             if eng.world > 1:
                 out.append(Launch("__allreduce__", {"count": m * d}, [self.tmp.ptr]))
             out.append(Launch("add", {"n": m * d}, [self.x.ptr, self.tmp.ptr, self.x1.ptr]))
-            out.append(Launch("rmsnorm_rows", {"rows": m, "h": d, "eps": eps, "factor": 1.0},
+            out.append(Launch("rmsnorm_rows" + wsuf, {"rows": m, "h": d, "eps": eps, "factor": 1.0},
                               [self.x1.ptr, w["mlp_norm"], self.a.ptr]))
             if eng.gate_up_interleaved:  # rows gate_0, up_0, ...: columns likewise
                 out.append(self._gemm(self.a.ptr, d, w["gate_proj"], 2 * f, self.gu.ptr, 2 * f))

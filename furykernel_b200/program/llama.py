@@ -1,8 +1,9 @@
 """The Llama-shaped decoder programs of this path, written with the program
 builder: one layer (RMSNorm, q/k/v, RoPE, KV store, attention, o, residual,
 RMSNorm, SiLU-gated FFN, residual), the embedding, and the head (final
-norm, tied LM head, greedy token). All f32: weights, activations and the
-Ring KV caches."""
+norm, tied LM head, greedy token). Activations are f32; the weights and the
+Ring KV caches are f32 (the BASELINE configurations) or bf16 (the
+reference's own element types)."""
 
 from __future__ import annotations
 
@@ -10,7 +11,7 @@ import math
 from dataclasses import dataclass
 
 from .build import program
-from .graph import CACHE_F32, AttendTo, AttnSpec, Ring, RopeSpec, StoreAt, whole_row
+from .graph import AttendTo, AttnSpec, Ring, RopeSpec, StoreAt, whole_row
 
 
 @dataclass(frozen=True)
@@ -27,6 +28,8 @@ class LlamaShape:
     slots: int = 1  # sequences the ring holds
     length: int = 4096  # ring length
     positions: int = 4096  # bound of the positions a row may have
+    weights: str = "f32"  # every weight's element type: "f32", or "bf16" (the reference's, Build.hs:171-175)
+    cache: str = "f32"  # the KV caches' element type: "f32", or "bf16" (CacheBF16, Graph.hs:165-180)
 
     @property
     def q_width(self):
@@ -44,17 +47,17 @@ def layer_program(s: LlamaShape, name: str = "layer"):
     x = b.input("x", whole_row(s.d_model))
     pos = b.row_ints("position", 1, s.positions)
     slot = b.row_ints("slot", 1, s.slots)
-    attn_norm = b.weight("attn_norm", [s.d_model], "f32")
-    wq = b.weight("q_proj", [s.q_width, s.d_model], "f32")
-    wk = b.weight("k_proj", [s.kv_width, s.d_model], "f32")
-    wv = b.weight("v_proj", [s.kv_width, s.d_model], "f32")
-    wo = b.weight("o_proj", [s.d_model, s.q_width], "f32")
-    mlp_norm = b.weight("mlp_norm", [s.d_model], "f32")
-    wg = b.weight("gate_proj", [s.ffn, s.d_model], "f32")
-    wu = b.weight("up_proj", [s.ffn, s.d_model], "f32")
-    wd = b.weight("down_proj", [s.d_model, s.ffn], "f32")
-    kc = b.cache("k_cache", Ring(s.slots, s.kv_heads, s.length, s.head_dim), CACHE_F32)
-    vc = b.cache("v_cache", Ring(s.slots, s.kv_heads, s.length, s.head_dim), CACHE_F32)
+    attn_norm = b.weight("attn_norm", [s.d_model], s.weights)
+    wq = b.weight("q_proj", [s.q_width, s.d_model], s.weights)
+    wk = b.weight("k_proj", [s.kv_width, s.d_model], s.weights)
+    wv = b.weight("v_proj", [s.kv_width, s.d_model], s.weights)
+    wo = b.weight("o_proj", [s.d_model, s.q_width], s.weights)
+    mlp_norm = b.weight("mlp_norm", [s.d_model], s.weights)
+    wg = b.weight("gate_proj", [s.ffn, s.d_model], s.weights)
+    wu = b.weight("up_proj", [s.ffn, s.d_model], s.weights)
+    wd = b.weight("down_proj", [s.d_model, s.ffn], s.weights)
+    kc = b.cache("k_cache", Ring(s.slots, s.kv_heads, s.length, s.head_dim), s.cache)
+    vc = b.cache("v_cache", Ring(s.slots, s.kv_heads, s.length, s.head_dim), s.cache)
     a = b.rmsnorm("attn_in", s.eps, attn_norm, 1.0, x)
     q = b.linear("q", wq, s.head_dim, a)
     k = b.linear("k", wk, s.head_dim, a)
@@ -81,7 +84,7 @@ def layer_program(s: LlamaShape, name: str = "layer"):
 def embed_program(s: LlamaShape):
     b = program("embed")
     tok = b.row_ints("token", 1, s.vocab)
-    table = b.weight("embed", [s.vocab, s.d_model], "f32")
+    table = b.weight("embed", [s.vocab, s.d_model], s.weights)
     x = b.gather("x", table, tok, 1.0)
     b.output("x", x)
     return b.done()
@@ -91,8 +94,8 @@ def head_program(s: LlamaShape):
     """The final norm, the tied LM head and the greedy token."""
     b = program("head")
     x = b.input("x", whole_row(s.d_model))
-    norm = b.weight("final_norm", [s.d_model], "f32")
-    embed = b.weight("embed", [s.vocab, s.d_model], "f32")
+    norm = b.weight("final_norm", [s.d_model], s.weights)
+    embed = b.weight("embed", [s.vocab, s.d_model], s.weights)
     n = b.rmsnorm("final_normed", s.eps, norm, 1.0, x)
     logits = b.linear("logits", embed, 0, n)
     token = b.argmax("token", logits)

@@ -180,6 +180,26 @@ SPEC_KERNELS = {
 }
 
 
+# The bf16 forms (the model's weights, or its KV caches, in bf16: the
+# reference's element types, Build.hs:171-194): an f32 entry's parameters
+# with the named buffers bf16.
+_VARIANTS = [
+    *[(base, base + "_wbf16", {"w", "gamma"})
+      for base in ("gemv", "gemv_add", "gemv_rmsnorm", "gemv_rmsnorm_silu", "gemv_silu", "gemv_silu_add",
+                   "gemv_scatter", "gemv_reduce_rmsnorm", "gemv_reduce_rmsnorm_silu")],
+    ("gather", "gather_wbf16", {"table"}),
+    ("rmsnorm_rows", "rmsnorm_rows_wbf16", {"gamma"}),
+    ("split_tf32", "split_tf32_wbf16", {"x"}),
+    *[(base, base + "_kvbf16", {"k_cache", "v_cache"})
+      for base in ("kv_store_ring", "attend_split", "attend_decode", "attend_prompt")],
+]
+for _base, _name, _retyped in _VARIANTS:
+    _k = SPEC_KERNELS[_base]
+    SPEC_KERNELS[_name] = KernelSig(_name, [Buffer(b.name, b.access, "bf16" if b.name in _retyped else b.type)
+                                            for b in _k.buffers], _k.params, threads=_k.threads)
+W16_SUFFIX, KV16_SUFFIX = "_wbf16", "_kvbf16"
+
+
 class CudaBackend:
     """`cuda :: Backend Cuda`: the name and the lowering."""
 

@@ -90,6 +90,12 @@ int fkc_host_free(void *host);
  * is slots * kv_heads * length * head_dim elements. */
 int fkc_kv_arena(fkc_ctx *ctx, uint32_t layers, uint32_t slots, uint32_t kv_heads, uint32_t length,
                  uint32_t head_dim, void **k_base, void **v_base);
+/* The same arena with elements of elem_bytes: 4 (f32) or 2 (bf16, the
+ * element type the reference gives a cache, CacheBF16, Graph.hs:165-180;
+ * the *_kvbf16 table entries read and write it). The layer stride is
+ * slots * kv_heads * length * head_dim elements of that size. */
+int fkc_kv_arena_elem(fkc_ctx *ctx, uint32_t layers, uint32_t slots, uint32_t kv_heads, uint32_t length,
+                      uint32_t head_dim, uint32_t elem_bytes, void **k_base, void **v_base);
 /* RoPE tables: the cosine and sine of p * theta^(-2i/d) for p < positions,
  * i < rotated, each rounded once from binary64 (the engine's tables that
  * Eval.hs:36-68 allows), [positions, rotated] f32 each. */
@@ -99,6 +105,9 @@ int fkc_rope_tables(fkc_ctx *ctx, double theta, uint32_t d, uint32_t rotated, ui
  * (test/cpu/Cases.hs:885-892), normals by Box-Muller in binary64. */
 int fkc_fill_normal(fkc_ctx *ctx, void *dptr, uint64_t n, uint64_t seed, double mu, double sigma);
 int fkc_fill_uniform(fkc_ctx *ctx, void *dptr, uint64_t n, uint64_t seed, double a, double b);
+/* fkc_fill_normal's values rounded to bf16 (nearest, ties to even: narrowBF16,
+ * src/FuryKernel/Numerics.hs:41-48), n bf16 elements at dptr. */
+int fkc_fill_normal_bf16(fkc_ctx *ctx, void *dptr, uint64_t n, uint64_t seed, double mu, double sigma);
 
 /* ---- the kernel table (LoweredKernel, Backend.hs:203-228) ----------------- */
 int fkc_kernel_count(void);

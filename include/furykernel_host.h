@@ -40,7 +40,7 @@ enum {
 };
 
 /* The library's ABI version (this header's FKH_ABI_VERSION). */
-#define FKH_ABI_VERSION 1
+#define FKH_ABI_VERSION 2
 FKH_API int fkh_abi_version(void);
 
 /* A Llama-shaped model (the shapes of the programs the engine plans). */
@@ -48,6 +48,8 @@ typedef struct {
   uint64_t d_model, heads, kv_heads, head_dim, ffn, vocab, layers;
   double theta, eps;
   uint64_t slots, length, positions;
+  int weights_bf16; /* every weight bf16 (the reference's element type), else f32 */
+  int cache_bf16;   /* the KV caches bf16 (CacheBF16), else f32 */
 } fkh_llama_shape;
 
 /* The planner's options (PlanOptions, src/FuryKernel/Program/Plan.hs:243-268). */

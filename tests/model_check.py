@@ -12,11 +12,22 @@ import numpy as np
 from oracle import oracle as O
 
 
+def download_f32(eng, ptr, n, elem_bytes):
+    """n elements at a device address as f32: bf16 ones widened (exact)."""
+    from furykernel_b200 import _native as N
+
+    raw = np.empty(n, np.float32 if elem_bytes == 4 else np.uint16)
+    N.check(N.lib().fkc_buf_download(eng.ctx.handle, raw.ctypes.data, ptr, raw.nbytes))
+    return raw if elem_bytes == 4 else O.widen_bf16(raw)
+
+
 def host_model(eng):
-    """The engine's weights, per layer, as the device holds them."""
+    """The engine's weights, per layer, as the device holds them (bf16
+    weights widened to f32, exactly)."""
     s = eng.s
     d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
-    flat = eng.arena.download()
+    wb = getattr(eng, "wb", 4)
+    flat = download_f32(eng, eng.arena.ptr, eng.arena.nbytes // wb, wb)
     layers = []
     for l in range(s.layers):
         base = l * eng.layer_elems
@@ -36,16 +47,12 @@ def host_model(eng):
 
 
 def host_caches(eng):
+    """The KV caches as the device holds them, as f32 (bf16 widened)."""
     s = eng.s
     n = s.layers * s.slots * s.kv_heads * s.length * s.head_dim
-    import ctypes
-
-    from furykernel_b200 import _native as N
-
-    k = np.empty(n, np.float32)
-    v = np.empty(n, np.float32)
-    N.check(N.lib().fkc_buf_download(eng.ctx.handle, k.ctypes.data, eng.kbase, k.nbytes))
-    N.check(N.lib().fkc_buf_download(eng.ctx.handle, v.ctypes.data, eng.vbase, v.nbytes))
+    cb = getattr(eng, "cb", 4)
+    k = download_f32(eng, eng.kbase, n, cb)
+    v = download_f32(eng, eng.vbase, n, cb)
     shp = (s.layers, s.slots, s.kv_heads, s.length, s.head_dim)
     return k.reshape(shp), v.reshape(shp)
 
@@ -57,8 +64,11 @@ def splits_of(eng):
 
 def oracle_decode(eng, layers, embed, final_norm, kcache, vcache, tokens, pos, slot, threads=0):
     """The CPU target's bits for one decode step; the caches are updated in
-    place as the step's stores leave them. Returns (ids, logits, x)."""
+    place as the step's stores leave them (bf16 caches: each stored element
+    rounded to bf16, Eval.hs:9). Returns (ids, logits, x)."""
     s = eng.s
+    as_stored = (lambda a: O.widen_bf16(O.narrow_bf16(a)).reshape(a.shape)) if getattr(eng, "cb", 4) == 2 \
+        else (lambda a: a)
     threads = threads or O.threads_default()
     d, qw, kvw, f, hd = s.d_model, s.q_width, s.kv_width, s.ffn, s.head_dim
     cos_t, sin_t = O.rope_tables(s.theta, hd, hd // 2, s.positions)
@@ -72,8 +82,8 @@ def oracle_decode(eng, layers, embed, final_norm, kcache, vcache, tokens, pos, s
         q, k, v = qkv[:, :qw], qkv[:, qw:qw + kvw], qkv[:, qw + kvw:]
         kr = O.rope(k, s.kv_heads, hd, hd // 2, pos, cos_t, sin_t)
         kc, vc = kcache[l], vcache[l]
-        O.kv_store_ring(kr, s.kv_heads, hd, s.length, pos, slot, kc)
-        O.kv_store_ring(np.ascontiguousarray(v), s.kv_heads, hd, s.length, pos, slot, vc)
+        O.kv_store_ring(as_stored(kr), s.kv_heads, hd, s.length, pos, slot, kc)
+        O.kv_store_ring(as_stored(np.ascontiguousarray(v)), s.kv_heads, hd, s.length, pos, slot, vc)
         qr = O.rope(q, s.heads, hd, hd // 2, pos, cos_t, sin_t)
         att, _ = O.attend(qr, s.heads, s.kv_heads, hd, s.length, pos, slot, kc, vc, scale, eng.chunk, 4,
                           eng.max_splits, threads)

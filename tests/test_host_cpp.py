@@ -32,6 +32,9 @@ SHAPES = [
                positions=16),
     LlamaShape(d_model=128, heads=8, kv_heads=8, head_dim=16, ffn=344, vocab=512, layers=1, theta=500000.0,
                eps=1e-6, slots=2, length=40, positions=64),
+    LlamaShape(weights="bf16", cache="bf16"),
+    LlamaShape(d_model=512, heads=4, kv_heads=2, head_dim=128, ffn=1024, vocab=3000, layers=2, slots=3, length=96,
+               positions=96, weights="bf16", cache="f32"),
 ]
 
 
@@ -140,7 +143,8 @@ def fake_engine(full, batch, rank=0, world=1, peer_exchange=True, fuse_attention
                             ffn=full.ffn // world)
     e.full, e.s, e.m, e.rank, e.world = full, s, batch, rank, world
     e.ctx = SimpleNamespace(sms=sms)
-    e.gate_up_interleaved = batch <= 64
+    e.wb, e.cb = (2 if full.weights == "bf16" else 4), (2 if full.cache == "bf16" else 4)
+    e.gate_up_interleaved = batch <= (4 if e.wb == 2 else 64)
     e.peer_exchange = world > 1 and batch <= 4 and peer_exchange
     e.vocab_local = full.vocab // world
     e.plans = {
@@ -194,6 +198,15 @@ CASES = (
     + [(SHAPES[2], 1, 0, 1, True, None),
        (dataclasses.replace(SHAPES[2], slots=4), 4, 0, 1, True, None)]
     + [(SHAPES[2], 1, r, 2, p, None) for r in (0, 1) for p in (True, False)]
+    # bf16 weights and bf16 caches: every batch form, fused or not, and tensor parallelism
+    + [(dataclasses.replace(small(b), weights="bf16", cache="bf16"), b, 0, 1, True, f)
+       for b, f in ((1, None), (3, False), (4, None), (5, None), (9, True), (33, None), (65, None))]
+    + [(dataclasses.replace(tp_shape(b), weights="bf16", cache="bf16"), b, r, 4, peer, None) for b in (1, 16)
+       for r in (0, 3) for peer in (True, False)]
+    + [(dataclasses.replace(small(b), weights=w, cache=c), b, 0, 1, True, None) for b in (1, 8)
+       for w, c in (("bf16", "f32"), ("f32", "bf16"))]
+    + [(LlamaShape(layers=32, slots=1, length=4096, positions=4096, weights="bf16", cache="bf16"), 1, 0, 1, True,
+        None)]
 )
 
 
@@ -261,6 +274,10 @@ PREFILL_CASES = (
     + [(small(65, layers=1), 65, 0, 1, True, 64, False, 33)]
     # tensor parallelism over NCCL and over peer memory
     + [(tp_shape(b), b, r, 4, peer, 32, False, 32) for b in (1, 16) for r in (0, 3) for peer in (True, False)]
+    # bf16 weights and caches
+    + [(dataclasses.replace(small(b), weights="bf16", cache="bf16"), b, 0, 1, True, 128, one, m)
+       for b, one, m in ((1, False, 100), (1, True, 64), (8, False, 128))]
+    + [(dataclasses.replace(tp_shape(1), weights="bf16", cache="bf16"), 1, 1, 2, True, 32, False, 32)]
 )
 
 
