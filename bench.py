@@ -45,7 +45,19 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--config", default="5", choices=["5", "1", "2", "3a", "3b", "3c", "4"],
                     help="5: the 32-layer decode step (default); 1, 2, 3a, 3b, 3c, 4: BASELINE's other configs")
+    ap.add_argument("--weights", default="f32", choices=["f32", "bf16"],
+                    help="config 5: the model's weights (f32, the BASELINE configuration; bf16, the reference's "
+                         "own element type)")
+    ap.add_argument("--cache", default="f32", choices=["f32", "bf16"], help="config 5: the KV caches' element type")
     return ap.parse_args()
+
+
+def model_types(args) -> tuple:
+    """Config 5's metric and dtype for the element types asked for."""
+    if args.weights == "f32" and args.cache == "f32":
+        return METRIC, "f32"
+    kind = f"{args.weights} weights, {args.cache} KV caches, f32 activations"
+    return f"decode tokens/s, 32-layer Llama-shaped, {kind} (config 5's shape)", kind
 
 
 def peaks():
@@ -252,13 +264,16 @@ def run_reference(args):
     per_step = sum(times) / len(times)
     value = args.batch / per_step
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "impl": "reference", "metric": model_types(args)[0], "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": model_types(args)[1],
+        "data": "synthetic (seeded)",
         "config": {"workload": f"config 5 decode, batch {args.batch}, context {PROMPT}", "global_batch": args.batch,
                    "seq_len": PROMPT, "parallelism": "cpu"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": desc + "; per step one sample, OpenMP over rows and heads"},
+                         "sample": desc + "; per step one sample, OpenMP over rows and heads"
+                                   + ("" if model_types(args)[1] == "f32" else
+                                      "; bf16 weights and caches are the same arithmetic over widened values")},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -283,11 +298,13 @@ def run_ours(args):
     if world > 1:
         from furykernel_b200 import tp
 
-        return tp.bench_main(args, METRIC, PROMPT, prompt_prefill)
+        return tp.bench_main(args, model_types(args)[0], PROMPT, prompt_prefill)
 
+    metric, dtype = model_types(args)
     b = args.batch
     length = 4096 if b <= 4 else 1024
-    shape = LlamaShape(layers=args.layers, slots=b, length=length, positions=length)
+    shape = LlamaShape(layers=args.layers, slots=b, length=length, positions=length, weights=args.weights,
+                       cache=args.cache)
     ctx = N.Context(local)
     eng = Llama(ctx, shape, b, seed=2026, chunk=32)
     tokens, prefill = prompt_prefill(ctx, eng, b, local)
@@ -327,7 +344,7 @@ def run_ours(args):
     e1.synchronize()
     k_ms = e0.elapsed_time(e1) / reps
     p = L.params
-    k_bytes = 4 * (p["n"] * p["k"] + p["m"] * p["k"] + p["k"] + p["m"] * p["n"])
+    k_bytes = eng.wb * (p["n"] * p["k"] + p["k"]) + 4 * (p["m"] * p["k"] + p["m"] * p["n"])
     k_gbs = k_bytes / (k_ms / 1e3) / 1e9
 
     # End to end through the C ABI: host token ids and positions in (pinned),
@@ -354,15 +371,15 @@ def run_ours(args):
     e2e = b * args.steps / e2e_s
 
     line = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "f32",
+        "vs_baseline": None, "dtype": dtype,
         "data": "synthetic: seeded N(0,0.02) weights made on the device; prompts of 512 ids U[0,32000) (numpy "
                 "PCG64 seed 512) prefilled through the model",
         "config": {"workload": f"config 5 decode, batch {b}, context {PROMPT}..{PROMPT + args.steps}",
                    "model": "llama-shaped 32 layers, d 4096, 32 heads x 128, ffn 11008, vocab 32000, tied head",
                    "global_batch": b, "seq_len": PROMPT, "parallelism": "tp1", "kv_length": length,
-                   "l2": "no flush: each step streams 26.4 GB of weights, > 126 MB L2"},
+                   "l2": "no flush: each step streams %.1f GB of weights, > 126 MB L2" % (eng.weight_bytes() / 1e9)},
         "hbm": {"step_algorithmic_bytes": step_bytes, "achieved_gbs": step_gbs,
                 "frac_of_8tbs": step_gbs / 8000.0, "frac_of_peak": step_gbs / hbm_peak, "peak": hbm_peak,
                 "peak_kind": peak_kind},

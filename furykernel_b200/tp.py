@@ -98,7 +98,8 @@ def bench_main(args, metric: str, prompt: int, prefill_fn) -> None:
     ctx, rank, world, local = init()
     b = args.batch
     length = 4096 if b <= 4 else 1024
-    shape = LlamaShape(layers=args.layers, slots=b, length=length, positions=length)
+    wt, ct = getattr(args, "weights", "f32"), getattr(args, "cache", "f32")
+    shape = LlamaShape(layers=args.layers, slots=b, length=length, positions=length, weights=wt, cache=ct)
     eng = Llama(ctx, shape, b, seed=2026, chunk=32, rank=rank, world=world)
     tokens, prefill = prefill_fn(ctx, eng, b, local)
     prefill["ms"] = max_over_ranks(prefill["ms"])
@@ -141,7 +142,8 @@ def bench_main(args, metric: str, prompt: int, prefill_fn) -> None:
         line = {
             "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32",
+            "vs_baseline": None,
+            "dtype": "f32" if (wt, ct) == ("f32", "f32") else f"{wt} weights, {ct} KV caches, f32 activations",
             "data": "synthetic: seeded N(0,0.02) weights made on the device; prompts of 512 ids U[0,32000) (numpy "
                     "PCG64 seed 512) prefilled through the model",
             "config": {"workload": f"config 5 decode, batch {b}, context {prompt}..{prompt + args.steps}",
