@@ -14,7 +14,7 @@ _LIB = None
 _PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_build", "libfurykernel_host.so")
 
 FKH_OK, FKH_ERR_ARGUMENT, FKH_ERR_SPACE, FKH_ERR_INTERNAL = 0, 1, 2, 3
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 
 class Shape(ctypes.Structure):
@@ -22,7 +22,8 @@ class Shape(ctypes.Structure):
                                                 "layers")] + \
                [("theta", ctypes.c_double), ("eps", ctypes.c_double)] + \
                [(n, ctypes.c_uint64) for n in ("slots", "length", "positions")] + \
-               [("weights_bf16", ctypes.c_int), ("cache_bf16", ctypes.c_int)]
+               [("weights_bf16", ctypes.c_int), ("cache_bf16", ctypes.c_int)] + \
+               [("blocks", ctypes.c_uint64), ("block_size", ctypes.c_uint64)]
 
 
 class PlanOptions(ctypes.Structure):
@@ -106,7 +107,7 @@ def shape(s) -> Shape:
         if t not in ("f32", "bf16"):
             raise N.Refused(N.FKC_ERR_ARGUMENT, f"the {what}' element type {t} is not f32 or bf16.")
     return Shape(s.d_model, s.heads, s.kv_heads, s.head_dim, s.ffn, s.vocab, s.layers, s.theta, s.eps, s.slots,
-                 s.length, s.positions, int(s.weights == "bf16"), int(s.cache == "bf16"))
+                 s.length, s.positions, int(s.weights == "bf16"), int(s.cache == "bf16"), s.blocks, s.block_size)
 
 
 def llama_program_text(s, which: str) -> str:

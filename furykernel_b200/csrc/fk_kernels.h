@@ -91,6 +91,13 @@ struct FkKvStore {
   bool pdl;
 };
 
+// A paged cache's block tables: row r's entries at table + r * table_len,
+// each a block of the pool (< blocks) of block_size positions.
+struct FkPaged {
+  const uint32_t* table;
+  uint32_t block_size, table_len, blocks;
+};
+
 struct FkCombine {
   const float* part_m;
   const float* part_l;
@@ -158,6 +165,13 @@ cudaError_t fk_launch_attend_decode16(const FkAttend& a, uint32_t k_off, uint32_
                                       cudaStream_t s);
 cudaError_t fk_launch_attend_prompt16(const FkAttend& a, const uint16_t* kc, const uint16_t* vc, float* out,
                                       uint32_t ldo, uint32_t max_pos, cudaStream_t s);
+// Paged KV caches (k_attend_paged.cu), f32 or bf16 elements.
+cudaError_t fk_launch_kv_store_paged(const FkKvStore& a, const FkPaged& pg, void* kc, void* vc, bool bf16,
+                                     cudaStream_t s);
+cudaError_t fk_launch_attend_paged(const FkAttend& a, const FkPaged& pg, const void* kc, const void* vc, bool bf16,
+                                   cudaStream_t s);
+cudaError_t fk_launch_attend_prompt_paged(const FkAttend& a, const FkPaged& pg, const void* kc, const void* vc,
+                                          bool bf16, float* out, uint32_t ldo, uint32_t max_pos, cudaStream_t s);
 cudaError_t fk_launch_rope_tables(float* cos_t, float* sin_t, double theta, uint32_t d, uint32_t rotated,
                                   uint32_t positions, cudaStream_t s);
 

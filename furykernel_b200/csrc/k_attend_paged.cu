@@ -1,0 +1,448 @@
+// Attention over paged KV caches (Paged blocks blockSize kvHeads headDim,
+// src/FuryKernel/Program/Graph.hs:144-152): each layer's keys and values
+// live in a pool of blocks of `block_size` positions, and each row lists its
+// sequence's blocks in a block table of `table_len` u32 entries. Position p,
+// KV head h of a row is at element (h * block_size + p mod block_size) * d
+// of block table[p / block_size] (cacheIndex, src/FuryKernel/Program/
+// Eval.hs:592-602); the pool holds its blocks back to back, so block b
+// starts at element b * kv_heads * block_size * d.
+//
+// Arithmetic: the ring kernels' (k_attend.cu), position for position -- the
+// KV store rotates each key and stores it and the value at the row's
+// position; a score is a chain over the lanes' packs summed pairwise, times
+// the scale; a split's weights exp(s - max) in binary64 rounded once, the
+// warps' sums in warp order; the prompt attention's two passes. Only where
+// a position's key and value live differs, so the oracle's ring attention
+// over the blocks gathered in table order gives the bits. Elements are f32
+// or bf16 (stores rounded to nearest even, reads widened: Eval.hs:9).
+//
+// A table entry at or past the pool's `blocks` is not read or written: its
+// keys and values read as 0 and its stores are dropped (the engine checks
+// the tables it uploads; this keeps a bad entry from reaching past the pool).
+#include "fk_common.cuh"
+#include "fk_kernels.h"
+
+namespace fk {
+namespace paged {
+
+constexpr int kAttWarps = 4;
+constexpr int kHeadDim = 128;
+constexpr int kMaxChunk = 256;
+constexpr uint32_t kMaxAttendRows = 16384;
+constexpr int kPromptTile = 32;
+
+// The element forms: a pack of four elements widened to f32, an element
+// stored (bf16: rounded to nearest even, narrowBF16,
+// src/FuryKernel/Numerics.hs:41-48), a value as the cache holds it.
+__device__ __forceinline__ float4 ld_pack(const float* p) { return __ldcs(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ float4 ld_pack(const uint16_t* p) {
+  const uint2 r = __ldcs(reinterpret_cast<const uint2*>(p));
+  return make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xFFFF0000u), __uint_as_float(r.y << 16),
+                     __uint_as_float(r.y & 0xFFFF0000u));
+}
+__device__ __forceinline__ float ld_elem(const float* p) { return *p; }
+__device__ __forceinline__ float ld_elem(const uint16_t* p) { return __uint_as_float((uint32_t)*p << 16); }
+__device__ __forceinline__ uint16_t narrow(float v) {
+  const uint32_t w = __float_as_uint(v);
+  if ((w & 0x7F800000u) == 0x7F800000u && (w & 0x007FFFFFu)) return (uint16_t)((w >> 16) | 0x0040u);
+  return (uint16_t)((w + 0x7FFFu + ((w >> 16) & 1u)) >> 16);
+}
+__device__ __forceinline__ void st_elem(float* p, float v) { *p = v; }
+__device__ __forceinline__ void st_elem(uint16_t* p, float v) { *p = narrow(v); }
+
+// RoPE of pair (i, i + half) of one head (halves pairing, Eval.hs:634-645),
+// k_attend.cu's rope_pair arithmetic.
+__device__ __forceinline__ void rope2(const float* __restrict__ src, uint32_t i, uint32_t half, uint32_t rotated,
+                                      const float* __restrict__ cos_row, const float* __restrict__ sin_row,
+                                      float& lo, float& hi) {
+  const float a = src[i], b = src[i + half];
+  if (i < rotated) {
+    const float c = __ldg(cos_row + i), s = __ldg(sin_row + i);
+    lo = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+    hi = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+  } else {
+    lo = a;
+    hi = b;
+  }
+}
+
+struct Pool {
+  const uint32_t* table;  // [m, table_len]
+  uint32_t block_size, table_len, blocks;
+};
+
+// The element index of (row r, position t, KV head h, element 0), or
+// UINT64_MAX where the row's table has no block there.
+__device__ __forceinline__ uint64_t at_of(const Pool& P, uint32_t r, uint32_t t, uint32_t h, uint32_t kv_heads,
+                                          uint32_t d) {
+  const uint32_t slot = t / P.block_size;
+  if (slot >= P.table_len) return ~0ull;
+  const uint32_t block = __ldg(P.table + (size_t)r * P.table_len + slot);
+  if (block >= P.blocks) return ~0ull;
+  return (((uint64_t)block * kv_heads + h) * P.block_size + t % P.block_size) * d;
+}
+
+template <typename E>
+struct StoreArgs {
+  FkKvStore a;  // a.slot, a.kc, a.vc, a.length unused
+  Pool P;
+  E* kc;
+  E* vc;
+};
+
+// The KV store step: grid (kv_heads, m), d / 2 threads.
+template <typename E>
+__global__ void kv_store_paged_kernel(StoreArgs<E> s) {
+  const FkKvStore& a = s.a;
+  grid_wait();
+  grid_launch_dependents();
+  const uint32_t h = blockIdx.x, r = blockIdx.y, i = threadIdx.x, half = a.d / 2;
+  const uint32_t p = a.pos[r];
+  const uint64_t at = at_of(s.P, r, p, h, a.kv_heads, a.d);
+  if (at == ~0ull) return;
+  const float* krow = a.qkv + (size_t)r * a.ldq + a.k_off + (size_t)h * a.d;
+  const float* vrow = a.qkv + (size_t)r * a.ldq + a.v_off + (size_t)h * a.d;
+  float lo, hi;
+  rope2(krow, i, half, a.rotated, a.cos_t + (size_t)p * a.rotated, a.sin_t + (size_t)p * a.rotated, lo, hi);
+  st_elem(s.kc + at + i, lo);
+  st_elem(s.kc + at + i + half, hi);
+  st_elem(s.vc + at + i, vrow[i]);
+  st_elem(s.vc + at + i + half, vrow[i + half]);
+}
+
+template <typename E>
+struct AttendArgs {
+  FkAttend a;  // a.slot, a.kc, a.vc, a.length unused
+  Pool P;
+  const E* kc;
+  const E* vc;
+};
+
+// The attention anchor: persistent blocks of 4 warps over the step's items
+// (row, head, split), item i at block i mod G; warp w takes positions w,
+// w + 4, ... of its split, 8 at a time (the ring kernel's order).
+template <typename E>
+__global__ void __launch_bounds__(128, 4) attend_paged_kernel(AttendArgs<E> f) {
+  const FkAttend& a = f.a;
+  __shared__ float qrot[kHeadDim];
+  __shared__ float scores[kMaxChunk];
+  __shared__ float4 accw[kAttWarps][kHeadDim / 4];
+  __shared__ float lw[kAttWarps];
+  extern __shared__ uint32_t first[];  // [m + 1]: items before row r
+
+  grid_wait();
+  grid_launch_dependents();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    uint32_t acc = 0;
+    for (uint32_t r = 0; r < a.m; ++r) {
+      first[r] = acc;
+      acc += a.heads * ((a.pos[r] + 1 + a.chunk - 1) / a.chunk);
+    }
+    first[a.m] = acc;
+  }
+  __syncthreads();
+  const uint32_t items = first[a.m];
+  constexpr int B = 8;
+  constexpr uint32_t kStep = B * kAttWarps;
+  const uint32_t group = a.heads / a.kv_heads;
+  const float4 zero4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+
+  for (uint32_t it = blockIdx.x; it < items; it += gridDim.x) {
+    uint32_t lo = 0, hi = a.m - 1;
+    while (lo < hi) {
+      const uint32_t mid = (lo + hi + 1) / 2;
+      if (first[mid] <= it) lo = mid; else hi = mid - 1;
+    }
+    const uint32_t r = lo;
+    const uint32_t p = a.pos[r];
+    const uint32_t splits = (p + 1 + a.chunk - 1) / a.chunk;
+    const uint32_t local = it - first[r];
+    const uint32_t h = local / splits, j = local - h * splits;
+    const uint32_t t0 = j * a.chunk;
+    const uint32_t t1 = min(p + 1, t0 + a.chunk);
+    const uint32_t kvh = h / group;
+
+    float4 kv[B], vv[B];
+#pragma unroll
+    for (int u = 0; u < B; ++u) {
+      const uint32_t tt = t0 + warp + u * kAttWarps;
+      const uint64_t at = tt < t1 ? at_of(f.P, r, tt, kvh, a.kv_heads, kHeadDim) : ~0ull;
+      kv[u] = at != ~0ull ? ld_pack(f.kc + at + 4 * lane) : zero4;
+      vv[u] = at != ~0ull ? ld_pack(f.vc + at + 4 * lane) : zero4;
+    }
+
+    __syncthreads();  // the previous item's shared arrays are free
+    if (threadIdx.x < kHeadDim / 2) {
+      float q0, q1;
+      rope2(a.qkv + (size_t)r * a.ldq + a.q_off + (size_t)h * kHeadDim, threadIdx.x, kHeadDim / 2, a.rotated,
+            a.cos_t + (size_t)p * a.rotated, a.sin_t + (size_t)p * a.rotated, q0, q1);
+      qrot[threadIdx.x] = q0;
+      qrot[threadIdx.x + kHeadDim / 2] = q1;
+    }
+    __syncthreads();
+    const float4 qv = reinterpret_cast<const float4*>(qrot)[lane];
+
+    for (uint32_t t = t0 + warp; t < t1; t += kStep) {
+      if (t != t0 + warp) {
+#pragma unroll
+        for (int u = 0; u < B; ++u) {
+          const uint32_t tt = t + u * kAttWarps;
+          const uint64_t at = tt < t1 ? at_of(f.P, r, tt, kvh, a.kv_heads, kHeadDim) : ~0ull;
+          kv[u] = at != ~0ull ? ld_pack(f.kc + at + 4 * lane) : zero4;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < B; ++u) {
+        const uint32_t tt = t + u * kAttWarps;
+        const float sc = __fmul_rn(warp_sum(__fadd_rn(0.0f, pack_dot(qv, kv[u]))), a.scale);
+        if (lane == 0 && tt < t1) scores[tt - t0] = sc;
+      }
+    }
+    __syncthreads();
+    float mx = -INFINITY;
+    for (uint32_t i = lane; i < t1 - t0; i += 32) mx = max_number(mx, scores[i]);
+    mx = warp_max(mx);
+
+    float l = 0.0f;
+    float4 acc = zero4;
+    for (uint32_t t = t0 + warp; t < t1; t += kStep) {
+      if (t != t0 + warp) {
+#pragma unroll
+        for (int u = 0; u < B; ++u) {
+          const uint32_t tt = t + u * kAttWarps;
+          const uint64_t at = tt < t1 ? at_of(f.P, r, tt, kvh, a.kv_heads, kHeadDim) : ~0ull;
+          vv[u] = at != ~0ull ? ld_pack(f.vc + at + 4 * lane) : zero4;
+        }
+      }
+      const uint32_t g0 = t - (uint32_t)warp - t0;
+      const float e_lane = g0 + lane < t1 - t0 ? exp_rounded(__fsub_rn(scores[g0 + lane], mx)) : 0.0f;
+#pragma unroll
+      for (int u = 0; u < B; ++u) {
+        const uint32_t tt = t + u * kAttWarps;
+        const float e = __shfl_sync(0xffffffffu, e_lane, warp + u * kAttWarps);
+        if (tt < t1) {
+          const float4 v4 = vv[u];
+          l = __fadd_rn(l, e);
+          acc.x = __fadd_rn(acc.x, __fmul_rn(e, v4.x));
+          acc.y = __fadd_rn(acc.y, __fmul_rn(e, v4.y));
+          acc.z = __fadd_rn(acc.z, __fmul_rn(e, v4.z));
+          acc.w = __fadd_rn(acc.w, __fmul_rn(e, v4.w));
+        }
+      }
+    }
+    accw[warp][lane] = acc;
+    if (lane == 0) lw[warp] = l;
+    __syncthreads();
+    const size_t at = ((size_t)r * a.heads + h) * a.max_splits + j;
+    const float* accf = reinterpret_cast<const float*>(accw);
+    const uint32_t i = threadIdx.x;
+    float o = accf[i];
+#pragma unroll
+    for (int w = 1; w < kAttWarps; ++w) o = __fadd_rn(o, accf[w * kHeadDim + i]);
+    a.part_acc[at * kHeadDim + i] = o;
+    if (threadIdx.x == 0) {
+      float lt = lw[0];
+#pragma unroll
+      for (int w = 1; w < kAttWarps; ++w) lt = __fadd_rn(lt, lw[w]);
+      a.part_l[at] = lt;
+      a.part_m[at] = mx;
+    }
+  }
+}
+
+// Attention over a prompt's rows of one sequence (prefill), the ring
+// prompt kernel's two passes (k_attend.cu): a block a (32 query rows,
+// head); keys and values 32 positions at a time into shared memory, through
+// row 0's block table (the prompt's rows share their sequence's table).
+template <typename E>
+__global__ void __launch_bounds__(128) attend_prompt_paged_kernel(AttendArgs<E> f, float* __restrict__ out,
+                                                                  uint32_t ldo, uint32_t max_pos) {
+  const FkAttend& a = f.a;
+  extern __shared__ float psm[];
+  float* qs = psm;                          // [32][128] the tile's rotated queries
+  float* kt = qs + kPromptTile * kHeadDim;  // [128][32] keys, transposed
+  float* vt = kt + kHeadDim * kPromptTile;  // [32][128] values
+  float* sc = vt + kPromptTile * kHeadDim;  // [32][max_pos + 1] scores
+  const uint32_t ncols = max_pos + 1;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t r0 = blockIdx.x * kPromptTile, h = blockIdx.y;
+  const uint32_t rows = min((uint32_t)kPromptTile, a.m - r0);
+  const uint32_t kvh = h / (a.heads / a.kv_heads);
+  grid_wait();
+  grid_launch_dependents();
+
+  for (uint32_t i = warp; i < kPromptTile; i += 4) {
+    if (i < rows) {
+      const uint32_t r = r0 + i, p = a.pos[r];
+      for (uint32_t c = lane; c < kHeadDim / 2; c += 32) {
+        float q0, q1;
+        rope2(a.qkv + (size_t)r * a.ldq + a.q_off + (size_t)h * kHeadDim, c, kHeadDim / 2, a.rotated,
+              a.cos_t + (size_t)p * a.rotated, a.sin_t + (size_t)p * a.rotated, q0, q1);
+        qs[i * kHeadDim + c] = q0;
+        qs[i * kHeadDim + c + kHeadDim / 2] = q1;
+      }
+    }
+  }
+  uint32_t tile_max = 0;
+  for (uint32_t i = 0; i < rows; ++i) tile_max = max(tile_max, a.pos[r0 + i]);
+  const uint32_t keys = min(tile_max + 1, ncols);
+  __syncthreads();
+
+  float mx[kPromptTile / 4];
+#pragma unroll
+  for (int u = 0; u < kPromptTile / 4; ++u) mx[u] = -INFINITY;
+  for (uint32_t t0 = 0; t0 < keys; t0 += kPromptTile) {
+    for (uint32_t e = threadIdx.x; e < kPromptTile * kHeadDim; e += blockDim.x) {
+      const uint32_t k = e / kHeadDim, dd = e % kHeadDim;
+      const uint64_t at = t0 + k < keys ? at_of(f.P, 0, t0 + k, kvh, a.kv_heads, kHeadDim) : ~0ull;
+      kt[dd * kPromptTile + k] = at != ~0ull ? ld_elem(f.kc + at + dd) : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < kPromptTile / 4; ++u) {
+      const uint32_t i = warp + 4 * u;
+      if (i < rows) {
+        const float* q = qs + i * kHeadDim;
+        float dot = 0.0f;
+        for (uint32_t dd = 0; dd < kHeadDim; ++dd) dot = __fadd_rn(dot, __fmul_rn(q[dd], kt[dd * kPromptTile + lane]));
+        const uint32_t t = t0 + lane;
+        const float s = __fmul_rn(dot, a.scale);
+        if (t <= a.pos[r0 + i] && t < ncols) {
+          sc[i * ncols + t] = s;
+          mx[u] = max_number(mx[u], s);
+        }
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int u = 0; u < kPromptTile / 4; ++u) mx[u] = warp_max(mx[u]);
+
+  float l[kPromptTile / 4];
+  float acc[kPromptTile / 4][4];
+#pragma unroll
+  for (int u = 0; u < kPromptTile / 4; ++u) {
+    l[u] = 0.0f;
+#pragma unroll
+    for (int jd = 0; jd < 4; ++jd) acc[u][jd] = 0.0f;
+  }
+  for (uint32_t t0 = 0; t0 < keys; t0 += kPromptTile) {
+    for (uint32_t e = threadIdx.x; e < kPromptTile * kHeadDim; e += blockDim.x) {
+      const uint32_t k = e / kHeadDim, dd = e % kHeadDim;
+      const uint64_t at = t0 + k < keys ? at_of(f.P, 0, t0 + k, kvh, a.kv_heads, kHeadDim) : ~0ull;
+      vt[e] = at != ~0ull ? ld_elem(f.vc + at + dd) : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < kPromptTile / 4; ++u) {
+      const uint32_t i = warp + 4 * u;
+      if (i < rows) {
+        const uint32_t t = t0 + lane;
+        const float e = t <= a.pos[r0 + i] && t < ncols ? exp_rounded(__fsub_rn(sc[i * ncols + t], mx[u])) : 0.0f;
+        l[u] = __fadd_rn(l[u], e);
+        for (uint32_t k = 0; k < kPromptTile; ++k) {
+          const float ek = __shfl_sync(0xffffffffu, e, k);
+#pragma unroll
+          for (int jd = 0; jd < 4; ++jd)
+            acc[u][jd] = __fadd_rn(acc[u][jd], __fmul_rn(ek, vt[k * kHeadDim + lane + 32 * jd]));
+        }
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int u = 0; u < kPromptTile / 4; ++u) {
+    const uint32_t i = warp + 4 * u;
+    const float lt = warp_sum(l[u]);
+    if (i < rows) {
+#pragma unroll
+      for (int jd = 0; jd < 4; ++jd)
+        out[(size_t)(r0 + i) * ldo + (size_t)h * kHeadDim + lane + 32 * jd] = __fdiv_rn(acc[u][jd], lt);
+    }
+  }
+}
+
+template <typename E>
+cudaError_t launch_store(const FkKvStore& a, const FkPaged& pg, E* kc, E* vc, cudaStream_t s) {
+  if (a.m == 0) return cudaSuccess;
+  if (a.d % 2 != 0 || a.d > 2048 || pg.block_size == 0 || pg.table_len == 0 || !pg.table || !kc || !vc)
+    return cudaErrorInvalidValue;
+  StoreArgs<E> st;
+  st.a = a;
+  st.P = Pool{pg.table, pg.block_size, pg.table_len, pg.blocks};
+  st.kc = kc;
+  st.vc = vc;
+  return fk_launch_ex(kv_store_paged_kernel<E>, dim3(a.kv_heads, a.m), dim3(a.d / 2), 0, s, a.pdl, st);
+}
+
+template <typename E>
+cudaError_t launch_attend(const FkAttend& a, const FkPaged& pg, const E* kc, const E* vc, cudaStream_t s) {
+  if (a.m == 0) return cudaSuccess;
+  if (a.d != kHeadDim || a.chunk == 0 || a.chunk > kMaxChunk || a.kv_heads == 0 || a.heads % a.kv_heads != 0 ||
+      a.m > kMaxAttendRows || (uint64_t)a.m * a.heads * a.max_splits >= (1ull << 32) || pg.block_size == 0 ||
+      pg.table_len == 0 || !pg.table || !kc || !vc)
+    return cudaErrorInvalidValue;
+  AttendArgs<E> f;
+  f.a = a;
+  f.P = Pool{pg.table, pg.block_size, pg.table_len, pg.blocks};
+  f.kc = kc;
+  f.vc = vc;
+  auto kern = attend_paged_kernel<E>;
+  int dev = 0, sms = 148, per_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const size_t smem = ((size_t)a.m + 1) * sizeof(uint32_t);
+  cudaError_t e = fk_allow_smem(kern, smem);
+  if (e != cudaSuccess) return e;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, smem);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) return cudaErrorInvalidConfiguration;
+  const uint64_t most = (uint64_t)a.m * a.heads * a.max_splits;
+  const uint64_t resident = (uint64_t)sms * per_sm;
+  const uint32_t blocks = (uint32_t)(most < resident ? most : resident);
+  return fk_launch_ex(kern, dim3(blocks), dim3(128), smem, s, a.pdl, f);
+}
+
+template <typename E>
+cudaError_t launch_prompt(const FkAttend& a, const FkPaged& pg, const E* kc, const E* vc, float* out, uint32_t ldo,
+                          uint32_t max_pos, cudaStream_t s) {
+  if (a.m == 0) return cudaSuccess;
+  if (a.d != kHeadDim || a.kv_heads == 0 || a.heads % a.kv_heads != 0 || pg.block_size == 0 ||
+      pg.table_len == 0 || !pg.table || !kc || !vc || (uint64_t)max_pos >= (uint64_t)pg.table_len * pg.block_size)
+    return cudaErrorInvalidValue;
+  const size_t smem = (3 * (size_t)kPromptTile * kHeadDim + (size_t)kPromptTile * (max_pos + 1)) * 4;
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  auto kern = attend_prompt_paged_kernel<E>;
+  cudaError_t e = fk_allow_smem(kern, smem);
+  if (e != cudaSuccess) return e;
+  AttendArgs<E> f;
+  f.a = a;
+  f.P = Pool{pg.table, pg.block_size, pg.table_len, pg.blocks};
+  f.kc = kc;
+  f.vc = vc;
+  const dim3 grid((a.m + kPromptTile - 1) / kPromptTile, a.heads);
+  return fk_launch_ex(kern, grid, dim3(128), smem, s, a.pdl, f, out, ldo, max_pos);
+}
+
+}  // namespace paged
+}  // namespace fk
+
+cudaError_t fk_launch_kv_store_paged(const FkKvStore& a, const FkPaged& pg, void* kc, void* vc, bool bf16,
+                                     cudaStream_t s) {
+  return bf16 ? fk::paged::launch_store<uint16_t>(a, pg, (uint16_t*)kc, (uint16_t*)vc, s)
+              : fk::paged::launch_store<float>(a, pg, (float*)kc, (float*)vc, s);
+}
+
+cudaError_t fk_launch_attend_paged(const FkAttend& a, const FkPaged& pg, const void* kc, const void* vc, bool bf16,
+                                   cudaStream_t s) {
+  return bf16 ? fk::paged::launch_attend<uint16_t>(a, pg, (const uint16_t*)kc, (const uint16_t*)vc, s)
+              : fk::paged::launch_attend<float>(a, pg, (const float*)kc, (const float*)vc, s);
+}
+
+cudaError_t fk_launch_attend_prompt_paged(const FkAttend& a, const FkPaged& pg, const void* kc, const void* vc,
+                                          bool bf16, float* out, uint32_t ldo, uint32_t max_pos, cudaStream_t s) {
+  return bf16 ? fk::paged::launch_prompt<uint16_t>(a, pg, (const uint16_t*)kc, (const uint16_t*)vc, out, ldo,
+                                                   max_pos, s)
+              : fk::paged::launch_prompt<float>(a, pg, (const float*)kc, (const float*)vc, out, ldo, max_pos, s);
+}

@@ -823,6 +823,74 @@ int l_attend_prompt_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
                   "attend_prompt_kvbf16");
 }
 
+// ---- paged KV caches: block tables into pools of blocks --------------------
+// kv_store_paged: qkv cos sin pos table k_cache v_cache
+//   | m kv_heads d block_size table_len blocks rotated ldq k_off v_off
+int kv_store_paged(fkc_ctx* c, const Params& p, void* const* bufs, bool bf16, const char* name) {
+  FkKvStore a = {};
+  a.qkv = CF(0), a.cos_t = CF(1), a.sin_t = CF(2), a.pos = CU(3);
+  a.m = p.u(0), a.kv_heads = p.u(1), a.d = p.u(2), a.rotated = p.u(6);
+  a.ldq = p.u(7), a.k_off = p.u(8), a.v_off = p.u(9);
+  a.pdl = c->pdl;
+  const FkPaged pg = {CU(4), p.u(3), p.u(4), p.u(5)};
+  if (a.rotated > a.d / 2) return fail(FKC_ERR_ARGUMENT, "%s: rotated %u is more than d/2.", name, a.rotated);
+  return launched(fk_launch_kv_store_paged(a, pg, bufs[5], bufs[6], bf16, c->stream), name);
+}
+int l_kv_store_paged(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return kv_store_paged(c, p, bufs, false, "kv_store_paged");
+}
+int l_kv_store_paged_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return kv_store_paged(c, p, bufs, true, "kv_store_paged_kvbf16");
+}
+// attend_split_paged: qkv cos sin pos table k_cache v_cache part_m part_l part_acc
+//   | m heads kv_heads d block_size table_len blocks rotated chunk max_splits ldq q_off scale
+int attend_paged(fkc_ctx* c, const Params& p, void* const* bufs, bool bf16, const char* name) {
+  FkAttend a = {};
+  a.qkv = CF(0), a.cos_t = CF(1), a.sin_t = CF(2), a.pos = CU(3);
+  a.part_m = F(7), a.part_l = F(8), a.part_acc = F(9);
+  a.m = p.u(0), a.heads = p.u(1), a.kv_heads = p.u(2), a.d = p.u(3), a.rotated = p.u(7);
+  a.chunk = p.u(8), a.max_splits = p.u(9), a.ldq = p.u(10), a.q_off = p.u(11);
+  a.scale = p.f(12);
+  a.pdl = c->pdl;
+  const FkPaged pg = {CU(4), p.u(4), p.u(5), p.u(6)};
+  if (a.kv_heads == 0 || a.heads % a.kv_heads != 0)
+    return fail(FKC_ERR_ARGUMENT, "%s: %u heads do not share %u KV heads in groups.", name, a.heads, a.kv_heads);
+  if (a.rotated > a.d / 2) return fail(FKC_ERR_ARGUMENT, "%s: rotated %u is more than d/2.", name, a.rotated);
+  return launched(fk_launch_attend_paged(a, pg, bufs[5], bufs[6], bf16, c->stream), name);
+}
+int l_attend_paged(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return attend_paged(c, p, bufs, false, "attend_split_paged");
+}
+int l_attend_paged_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return attend_paged(c, p, bufs, true, "attend_split_paged_kvbf16");
+}
+// attend_prompt_paged: qkv cos sin pos table k_cache v_cache out
+//   | m heads kv_heads d block_size table_len blocks rotated ldq q_off ldo max_pos scale
+// A prompt's rows of one sequence: row 0's block table serves them all.
+int attend_prompt_paged(fkc_ctx* c, const Params& p, void* const* bufs, bool bf16, const char* name) {
+  FkAttend a = {};
+  a.qkv = CF(0), a.cos_t = CF(1), a.sin_t = CF(2), a.pos = CU(3);
+  a.m = p.u(0), a.heads = p.u(1), a.kv_heads = p.u(2), a.d = p.u(3), a.rotated = p.u(7);
+  a.ldq = p.u(8), a.q_off = p.u(9);
+  a.scale = p.f(12);
+  a.pdl = c->pdl;
+  const FkPaged pg = {CU(4), p.u(4), p.u(5), p.u(6)};
+  if (a.kv_heads == 0 || a.heads % a.kv_heads != 0)
+    return fail(FKC_ERR_ARGUMENT, "%s: %u heads do not share %u KV heads in groups.", name, a.heads, a.kv_heads);
+  if (a.rotated > a.d / 2) return fail(FKC_ERR_ARGUMENT, "%s: rotated %u is more than d/2.", name, a.rotated);
+  if ((uint64_t)p.u(11) >= (uint64_t)pg.table_len * pg.block_size)
+    return fail(FKC_ERR_ARGUMENT, "%s: max_pos %u is past the block table's %u positions.", name, p.u(11),
+                pg.table_len * pg.block_size);
+  return launched(fk_launch_attend_prompt_paged(a, pg, bufs[5], bufs[6], bf16, F(7), p.u(10), p.u(11), c->stream),
+                  name);
+}
+int l_attend_prompt_paged(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return attend_prompt_paged(c, p, bufs, false, "attend_prompt_paged");
+}
+int l_attend_prompt_paged_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return attend_prompt_paged(c, p, bufs, true, "attend_prompt_paged_kvbf16");
+}
+
 #undef W16
 #undef M16
 
@@ -1040,6 +1108,50 @@ std::vector<KernelSpec> make_table() {
                {dim("n", 1, 1048576), dim("k", 4, 65536, 4), dim("m", 1, 16), dim("pack", 4, 16, 4), dim("split", 1, 16),
                 u32("ldx"), u32("ldy")},
                l_gemv_bf16});
+  // Paged caches (Graph.hs:144-152): a row's block table instead of its slot.
+  t.push_back({"kv_store_paged",
+               64,
+               {{"qkv", "read", "f32"},
+                {"cos", "read", "f32"},
+                {"sin", "read", "f32"},
+                {"pos", "read", "u32"},
+                {"table", "read", "u32"},
+                {"k_cache", "read_write", "f32"},
+                {"v_cache", "read_write", "f32"}},
+               {dim("m", 1, 65535), dim("kv_heads", 1, 1024), dim("d", 2, 2048, 2), dim("block_size", 1, 65536),
+                dim("table_len", 1, kMax), dim("blocks", 1, kMax), u32("rotated"), u32("ldq"), u32("k_off"),
+                u32("v_off")},
+               l_kv_store_paged});
+  t.push_back({"attend_split_paged",
+               128,
+               {{"qkv", "read", "f32"},
+                {"cos", "read", "f32"},
+                {"sin", "read", "f32"},
+                {"pos", "read", "u32"},
+                {"table", "read", "u32"},
+                {"k_cache", "read", "f32"},
+                {"v_cache", "read", "f32"},
+                {"part_m", "write", "f32"},
+                {"part_l", "write", "f32"},
+                {"part_acc", "write", "f32"}},
+               {dim("m", 1, 16384), dim("heads", 1, 1024), dim("kv_heads", 1, 1024), dim("d", 128, 128),
+                dim("block_size", 1, 65536), dim("table_len", 1, kMax), dim("blocks", 1, kMax), u32("rotated"),
+                dim("chunk", 1, 256), dim("max_splits", 1, 65535), u32("ldq"), u32("q_off"), f32("scale")},
+               l_attend_paged});
+  t.push_back({"attend_prompt_paged",
+               128,
+               {{"qkv", "read", "f32"},
+                {"cos", "read", "f32"},
+                {"sin", "read", "f32"},
+                {"pos", "read", "u32"},
+                {"table", "read", "u32"},
+                {"k_cache", "read", "f32"},
+                {"v_cache", "read", "f32"},
+                {"out", "write", "f32"}},
+               {dim("m", 1, 65535), dim("heads", 1, 1024), dim("kv_heads", 1, 1024), dim("d", 128, 128),
+                dim("block_size", 1, 65536), dim("table_len", 1, kMax), dim("blocks", 1, kMax), u32("rotated"),
+                u32("ldq"), u32("q_off"), u32("ldo"), dim("max_pos", 0, 1407), f32("scale")},
+               l_attend_prompt_paged});
   // The bf16 forms: an f32 entry's parameters with some buffers bf16 (the
   // model's weights, or its KV caches) and their own launchers.
   struct Variant {
@@ -1065,6 +1177,9 @@ std::vector<KernelSpec> make_table() {
       {"attend_split", "attend_split_kvbf16", {"k_cache", "v_cache"}, l_attend_kv16},
       {"attend_decode", "attend_decode_kvbf16", {"k_cache", "v_cache"}, l_attend_decode_kv16},
       {"attend_prompt", "attend_prompt_kvbf16", {"k_cache", "v_cache"}, l_attend_prompt_kv16},
+      {"kv_store_paged", "kv_store_paged_kvbf16", {"k_cache", "v_cache"}, l_kv_store_paged_kv16},
+      {"attend_split_paged", "attend_split_paged_kvbf16", {"k_cache", "v_cache"}, l_attend_paged_kv16},
+      {"attend_prompt_paged", "attend_prompt_paged_kvbf16", {"k_cache", "v_cache"}, l_attend_prompt_paged_kv16},
   };
   for (const Variant& v : variants) {
     KernelSpec k;

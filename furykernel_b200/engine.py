@@ -30,7 +30,7 @@ import numpy as np
 
 from . import _native as N
 from .program import plan as PL
-from .program.graph import SCache, SRowInts, SWeight
+from .program.graph import Paged, SCache, SRowInts, SWeight
 from .program.llama import LlamaShape, embed_program, head_program, layer_program
 
 
@@ -195,6 +195,14 @@ def lower_step(p, step, b: Binding, tables: dict, attn: dict) -> Launch:
         layout = p.source(att.op.sources[0]).kind.layout
         ct = _cache_suffix(step, p.source(att.op.sources[0]).kind.elem)
         part = attn["partials"]
+        if isinstance(layout, Paged):  # through the rows' block tables
+            return Launch("attend_split_paged" + ct,
+                          {"m": b.m, "heads": spec.heads, "kv_heads": spec.kv_heads, "d": spec.head_dim,
+                           "block_size": layout.block_size, "table_len": p.source(att.op.sources[3]).kind.count,
+                           "blocks": layout.blocks, "rotated": qn.op.args[0].rotated, "chunk": attn["chunk"],
+                           "max_splits": attn["max_splits"], "ldq": q.ld, "q_off": q.col, "scale": spec.scale},
+                          [q.base, tables["cos"], tables["sin"], b.ints[pos], b.ints[slot],
+                           b.caches[kc], b.caches[vc], part[0], part[1], part[2]])
         return Launch("attend_split" + ct,
                       {"m": b.m, "heads": spec.heads, "kv_heads": spec.kv_heads, "d": spec.head_dim,
                        "length": layout.length, "rotated": qn.op.args[0].rotated, "chunk": attn["chunk"],
@@ -226,6 +234,14 @@ def lower_step(p, step, b: Binding, tables: dict, attn: dict) -> Launch:
         layout = p.source(sk.op.sources[0]).kind.layout
         ct = _cache_suffix(step, p.source(sk.op.sources[0]).kind.elem)
         pos, slot = (p.source(s).name for s in sk.op.sources[1:3])
+        if isinstance(layout, Paged):  # through the rows' block tables
+            return Launch("kv_store_paged" + ct,
+                          {"m": b.m, "kv_heads": layout.kv_heads, "d": layout.head_dim,
+                           "block_size": layout.block_size, "table_len": p.source(sk.op.sources[2]).kind.count,
+                           "blocks": layout.blocks, "rotated": kn.op.args[0].rotated, "ldq": kview.ld,
+                           "k_off": kview.col, "v_off": vview.col},
+                          [kview.base, tables["cos"], tables["sin"], b.ints[pos], b.ints[slot],
+                           b.caches[p.source(sk.op.sources[0]).name], b.caches[p.source(sv.op.sources[0]).name]])
         return Launch("kv_store_ring" + ct,
                       {"m": b.m, "kv_heads": layout.kv_heads, "d": layout.head_dim, "length": layout.length,
                        "rotated": kn.op.args[0].rotated, "ldq": kview.ld, "k_off": kview.col, "v_off": vview.col},
@@ -336,7 +352,7 @@ class Llama:
         self.cos, self.sin = ctx.rope_tables(s.theta, s.head_dim, s.head_dim // 2, s.positions)
         self.kbase, self.vbase = self._kv_arena()
         if prefill_kv is not None:
-            kv = s.layers * s.slots * s.kv_heads * s.length * s.head_dim
+            kv = s.layers * self._kv_units() * s.kv_heads * self._kv_unit_len() * s.head_dim
             cfill = ctx.fill_normal if self.cb == 4 else ctx.fill_normal_bf16
             cfill(N.DeviceBuffer(ctx, self.kbase, self.cb * kv), seed + 1 + 17 * rank, 0.0, prefill_kv)
             cfill(N.DeviceBuffer(ctx, self.vbase, self.cb * kv), seed + 2 + 17 * rank, 0.0, prefill_kv)
@@ -345,12 +361,17 @@ class Llama:
         # the tokens, the positions, the slots, each part on a 16-byte
         # boundary as every buffer a kernel binds (leastAlign,
         # src/FuryKernel/Type.hs:66-71).
+        # With a paged cache the third part is the rows' block tables
+        # [m, table_len] instead of their slots.
         self.row_stride = (m + 3) // 4 * 4
-        self.rows = ctx.zeros(3 * self.row_stride, np.uint32)
+        seq = s.table_len if s.paged else 1
+        self.rows_words = 2 * self.row_stride + (m * seq + 3) // 4 * 4
+        self.rows = ctx.zeros(self.rows_words, np.uint32)
         rs = 4 * self.row_stride
         self.tokens = N.DeviceBuffer(ctx, self.rows.ptr, 4 * m, np.uint32, (m,))
         self.pos = N.DeviceBuffer(ctx, self.rows.ptr + rs, 4 * m, np.uint32, (m,))
-        self.slot = N.DeviceBuffer(ctx, self.rows.ptr + 2 * rs, 4 * m, np.uint32, (m,))
+        self.slot = N.DeviceBuffer(ctx, self.rows.ptr + 2 * rs, 4 * m * seq, np.uint32,
+                                   (m, seq) if s.paged else (m,))
         self.out_ids = ctx.zeros(m, np.uint32)
         self.x = ctx.zeros((m, d))
         self.x1 = ctx.zeros((m, d))
@@ -372,20 +393,30 @@ class Llama:
         # default for the small batches whose steps are launch-bound (one
         # launch a layer fewer); at batch 16 the separate store measured
         # faster (0.617 against 0.658 ms a layer at context 2048).
+        # (No fused form reads a paged cache.)
         if fuse_attention is None:
             fuse_attention = m <= 4
-        self.fuse_attention = fuse_attention and m <= 64
+        self.fuse_attention = fuse_attention and m <= 64 and not s.paged
         self.launches = self._launches()
         self.graph = None
 
     # -- layout
+    def _kv_units(self) -> int:
+        """A layer's ring slots, or its pool's blocks."""
+        return self.s.blocks if self.s.paged else self.s.slots
+
+    def _kv_unit_len(self) -> int:
+        """Positions a slot or a block holds."""
+        return self.s.block_size if self.s.paged else self.s.length
+
     def _kv_arena(self):
         import ctypes
 
         k, v = ctypes.c_void_p(), ctypes.c_void_p()
         s = self.s
-        N.check(N.lib().fkc_kv_arena_elem(self.ctx.handle, s.layers, s.slots, s.kv_heads, s.length, s.head_dim,
-                                          self.cb, ctypes.byref(k), ctypes.byref(v)))
+        N.check(N.lib().fkc_kv_arena_elem(self.ctx.handle, s.layers, self._kv_units(), s.kv_heads,
+                                          self._kv_unit_len(), s.head_dim, self.cb, ctypes.byref(k),
+                                          ctypes.byref(v)))
         return k.value, v.value
 
     LAYER_ORDER = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj", "attn_norm",
@@ -412,7 +443,7 @@ class Llama:
 
     def kv_layer(self, l: int):
         s = self.s
-        per = self.cb * s.slots * s.kv_heads * s.length * s.head_dim
+        per = self.cb * self._kv_units() * s.kv_heads * self._kv_unit_len() * s.head_dim
         return self.kbase + l * per, self.vbase + l * per
 
     # -- the step's launches
@@ -446,7 +477,8 @@ class Llama:
         s, m = self.s, self.m
         d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
         tables = {"cos": self.cos.ptr, "sin": self.sin.ptr}
-        ints = {"token": self.tokens.ptr, "position": self.pos.ptr, "slot": self.slot.ptr}
+        ints = {"token": self.tokens.ptr, "position": self.pos.ptr,
+                ("block_table" if s.paged else "slot"): self.slot.ptr}
         attn = {"chunk": self.chunk, "max_splits": self.max_splits, "partials": [b.ptr for b in self.part]}
         out = []
         eb = Binding(weights={"embed": self.embed_ptr()}, ints=ints, m=m, values={"x": View(self.x, 0, d, d)})
@@ -630,15 +662,24 @@ class Llama:
     def check_rows(self, tokens, positions, slots) -> None:
         """Refuses row inputs the kernels would index past their buffers
         with: ids past the vocabulary, positions past the RoPE tables, slots
-        past the KV arena."""
+        past the KV arena (or, paged, block-table entries past the pool)."""
         s = self.s
-        for what, v, bound in (("token", tokens, self.full.vocab), ("position", positions, s.positions),
-                               ("slot", slots, s.slots)):
+        seq = ("block", slots, s.blocks) if s.paged else ("slot", slots, s.slots)
+        for what, v, bound in (("token", tokens, self.full.vocab), ("position", positions, s.positions), seq):
             v = np.asarray(v)
             if v.size and int(v.max()) >= bound:
                 raise N.Refused(N.FKC_ERR_ARGUMENT, f"a {what} {int(v.max())} is past the engine's {bound}.")
 
     def set_rows(self, tokens, positions, slots=None) -> None:
+        """A step's rows: tokens, positions, and each row's ring slot or,
+        with a paged cache, its block table [m, table_len]."""
+        if self.s.paged:
+            if slots is None:
+                raise N.Refused(N.FKC_ERR_ARGUMENT, "a paged cache's rows need their block tables.")
+            slots = np.asarray(slots, np.uint32)
+            if slots.shape != (self.m, self.s.table_len):
+                raise N.Refused(N.FKC_ERR_ARGUMENT, f"block tables of shape {slots.shape}, not "
+                                                    f"({self.m}, {self.s.table_len}).")
         slots = np.asarray(slots if slots is not None else np.arange(self.m), np.uint32)
         self.check_rows(tokens, positions, slots)
         if self.fuse_attention and len(np.unique(slots)) != len(slots):

@@ -135,6 +135,7 @@ class Builder {
   int row_ints(const std::string& name, uint64_t n, uint64_t bound);
   int weight(const std::string& name, std::vector<uint64_t> dims, const std::string& type);
   int cache(const std::string& name, Ring layout, const std::string& elem);
+  int cache(const std::string& name, Paged layout, const std::string& elem);
   int linear(const std::string& name, int w, uint64_t seg, int x);
   int rmsnorm(const std::string& name, double eps, std::optional<int> gamma, double factor, int x);
   int add(const std::string& name, int a, int b);
@@ -168,6 +169,12 @@ struct LlamaShape {
   double theta = 10000.0, eps = 1e-5;
   uint64_t slots = 1, length = 4096, positions = 4096;
   std::string weights = "f32", cache = "f32";  // element types: "f32" or "bf16"
+  // A paged cache (Graph.hs:144-152) instead of the ring: a pool of `blocks`
+  // blocks of `block_size` positions a layer, each row's block table of
+  // table_len() entries. block_size 0: the ring of `slots` and `length`.
+  uint64_t blocks = 0, block_size = 0;
+  bool paged() const { return block_size > 0; }
+  uint64_t table_len() const { return paged() ? (positions + block_size - 1) / block_size : 0; }
   uint64_t weight_bytes() const { return weights == "bf16" ? 2 : 4; }
   uint64_t cache_bytes() const { return cache == "bf16" ? 2 : 4; }
   uint64_t q_width() const { return heads * head_dim; }

@@ -61,6 +61,9 @@ fkh::LlamaShape shape_of(const fkh_llama_shape& s) {
   o.positions = s.positions;
   o.weights = s.weights_bf16 ? "bf16" : "f32";
   o.cache = s.cache_bf16 ? "bf16" : "f32";
+  o.blocks = s.blocks;
+  o.block_size = s.block_size;
+  if (o.paged() && !o.blocks) throw fkh::Refusal("a paged cache of no blocks.");
   if (!o.heads || !o.kv_heads || o.heads % o.kv_heads || !o.head_dim || o.head_dim % 2 || !o.d_model ||
       !o.ffn || !o.vocab || !o.slots || !o.length || !o.positions)
     throw fkh::Refusal("the Llama shape has an empty or uneven dimension.");

@@ -194,18 +194,35 @@ Launch lower_step(const Program& p, const Step& step, const Binding& b, uint64_t
     const View q = stored(qn->op.values[0]);
     const Source& kc = p.sources[att->op.sources[0]];
     Launch L;
-    L.kernel = "attend_split" + cache_suffix(step, kc.kind.elem);
-    L.params = {{"m", m},
-                {"heads", (double)spec.heads},
-                {"kv_heads", (double)spec.kv_heads},
-                {"d", (double)spec.head_dim},
-                {"length", (double)kc.kind.r.length},
-                {"rotated", (double)qn->op.rope.rotated},
-                {"chunk", (double)attn.chunk},
-                {"max_splits", (double)attn.max_splits},
-                {"ldq", (double)q.ld},
-                {"q_off", (double)q.col},
-                {"scale", spec.scale}};
+    if (!kc.kind.ring) {  // through the rows' block tables
+      L.kernel = "attend_split_paged" + cache_suffix(step, kc.kind.elem);
+      L.params = {{"m", m},
+                  {"heads", (double)spec.heads},
+                  {"kv_heads", (double)spec.kv_heads},
+                  {"d", (double)spec.head_dim},
+                  {"block_size", (double)kc.kind.pg.block_size},
+                  {"table_len", (double)p.sources[att->op.sources[3]].kind.count},
+                  {"blocks", (double)kc.kind.pg.blocks},
+                  {"rotated", (double)qn->op.rope.rotated},
+                  {"chunk", (double)attn.chunk},
+                  {"max_splits", (double)attn.max_splits},
+                  {"ldq", (double)q.ld},
+                  {"q_off", (double)q.col},
+                  {"scale", spec.scale}};
+    } else {
+      L.kernel = "attend_split" + cache_suffix(step, kc.kind.elem);
+      L.params = {{"m", m},
+                  {"heads", (double)spec.heads},
+                  {"kv_heads", (double)spec.kv_heads},
+                  {"d", (double)spec.head_dim},
+                  {"length", (double)kc.kind.r.length},
+                  {"rotated", (double)qn->op.rope.rotated},
+                  {"chunk", (double)attn.chunk},
+                  {"max_splits", (double)attn.max_splits},
+                  {"ldq", (double)q.ld},
+                  {"q_off", (double)q.col},
+                  {"scale", spec.scale}};
+    }
     L.bufs = {q.base,
               cos_t,
               sin_t,
@@ -248,15 +265,29 @@ Launch lower_step(const Program& p, const Step& step, const Binding& b, uint64_t
     if (kview.base != vview.base) throw Refusal(step.name + ": keys and values are not one row.");
     const Source& kc = p.sources[sk->op.sources[0]];
     Launch L;
-    L.kernel = "kv_store_ring" + cache_suffix(step, kc.kind.elem);
-    L.params = {{"m", m},
-                {"kv_heads", (double)kc.kind.r.kv_heads},
-                {"d", (double)kc.kind.r.head_dim},
-                {"length", (double)kc.kind.r.length},
-                {"rotated", (double)kn->op.rope.rotated},
-                {"ldq", (double)kview.ld},
-                {"k_off", (double)kview.col},
-                {"v_off", (double)vview.col}};
+    if (!kc.kind.ring) {  // through the rows' block tables
+      L.kernel = "kv_store_paged" + cache_suffix(step, kc.kind.elem);
+      L.params = {{"m", m},
+                  {"kv_heads", (double)kc.kind.pg.kv_heads},
+                  {"d", (double)kc.kind.pg.head_dim},
+                  {"block_size", (double)kc.kind.pg.block_size},
+                  {"table_len", (double)p.sources[sk->op.sources[2]].kind.count},
+                  {"blocks", (double)kc.kind.pg.blocks},
+                  {"rotated", (double)kn->op.rope.rotated},
+                  {"ldq", (double)kview.ld},
+                  {"k_off", (double)kview.col},
+                  {"v_off", (double)vview.col}};
+    } else {
+      L.kernel = "kv_store_ring" + cache_suffix(step, kc.kind.elem);
+      L.params = {{"m", m},
+                  {"kv_heads", (double)kc.kind.r.kv_heads},
+                  {"d", (double)kc.kind.r.head_dim},
+                  {"length", (double)kc.kind.r.length},
+                  {"rotated", (double)kn->op.rope.rotated},
+                  {"ldq", (double)kview.ld},
+                  {"k_off", (double)kview.col},
+                  {"v_off", (double)vview.col}};
+    }
     L.bufs = {kview.base,
               cos_t,
               sin_t,
@@ -530,7 +561,9 @@ std::vector<Launch> llama_launches(const LlamaLaunchDesc& d) {
   attn.chunk = d.chunk;
   attn.max_splits = (s.positions + d.chunk - 1) / d.chunk;
   for (int i = 0; i < 3; ++i) attn.partials[i] = d.part[i];
-  const std::map<std::string, uint64_t> ints = {{"token", d.tokens}, {"position", d.pos}, {"slot", d.slot}};
+  // A row's sequence: its ring slot, or its block table of the paged pool.
+  const std::map<std::string, uint64_t> ints = {
+      {"token", d.tokens}, {"position", d.pos}, {s.paged() ? "block_table" : "slot", d.slot}};
 
   std::vector<Launch> out;
   {
@@ -542,7 +575,9 @@ std::vector<Launch> llama_launches(const LlamaLaunchDesc& d) {
     for (const Step& st : embed_plan.steps)
       out.push_back(lower_step(embed_plan.program, st, eb, d.cos_t, d.sin_t, attn));
   }
-  const uint64_t per_cache = s.cache_bytes() * s.slots * s.kv_heads * s.length * s.head_dim;
+  // A layer's caches: its ring's slots, or its pool's blocks.
+  const uint64_t units = s.paged() ? s.blocks : s.slots, unit_len = s.paged() ? s.block_size : s.length;
+  const uint64_t per_cache = s.cache_bytes() * units * s.kv_heads * unit_len * s.head_dim;
   for (uint64_t l = 0; l < s.layers; ++l) {
     Binding b;
     b.weights = layer_weights(s, d.arena, l);

@@ -96,15 +96,32 @@ std::vector<Launch> prefill_launches(const LlamaLaunchDesc& d, const PrefillDesc
   out.push_back(with(g0, {{"m", md}}, {g0.bufs[0], p.tokens, p.x}));
   for (uint64_t l = 0; l < s.layers; ++l) {
     const auto w = layer_weights(s, d.arena, l);
-    const Launch& kv = need("kv_store_ring", l);
-    const Launch& at = need("attend_split", l);
+    const bool paged = s.paged();
+    const Launch& kv = need(paged ? "kv_store_paged" : "kv_store_ring", l);
+    const Launch& at = need(paged ? "attend_split_paged" : "attend_split", l);
     const Launch& cb = need("attend_combine", l);
     out.push_back(make("rmsnorm_rows" + wsuf, {{"rows", md}, {"h", (double)dm}, {"eps", eps}, {"factor", 1.0}},
                        {p.x, w.at("attn_norm"), p.a}));
     out.push_back(gemm(p.a, dm, w.at("q_proj"), nq, p.qkv, nq));
     out.push_back(with(kv, {{"m", md}, {"ldq", (double)nq}},
                        {p.qkv, kv.bufs[1], kv.bufs[2], p.pos, p.slot, kv.bufs[5], kv.bufs[6]}));
-    if (p.one_slot) {
+    if (p.one_slot && paged) {
+      out.push_back(make("attend_prompt_paged" + csuf,
+                         {{"m", md},
+                          {"heads", at.param("heads")},
+                          {"kv_heads", at.param("kv_heads")},
+                          {"d", at.param("d")},
+                          {"block_size", at.param("block_size")},
+                          {"table_len", at.param("table_len")},
+                          {"blocks", at.param("blocks")},
+                          {"rotated", at.param("rotated")},
+                          {"ldq", (double)nq},
+                          {"q_off", at.param("q_off")},
+                          {"ldo", (double)qw},
+                          {"max_pos", (double)(p.positions - 1)},
+                          {"scale", at.param("scale")}},
+                         {p.qkv, at.bufs[1], at.bufs[2], p.pos, p.slot, at.bufs[5], at.bufs[6], p.att}));
+    } else if (p.one_slot) {
       out.push_back(make("attend_prompt" + csuf,
                          {{"m", md},
                           {"heads", at.param("heads")},

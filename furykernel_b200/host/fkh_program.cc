@@ -118,6 +118,15 @@ int Builder::cache(const std::string& name, Ring layout, const std::string& elem
   return source(name, k);
 }
 
+int Builder::cache(const std::string& name, Paged layout, const std::string& elem) {
+  SourceKind k;
+  k.kind = SrcKind::Cache;
+  k.ring = false;
+  k.pg = layout;
+  k.elem = elem;
+  return source(name, k);
+}
+
 int Builder::linear(const std::string& name, int w, uint64_t seg, int x) {
   const uint64_t n = rows_of(w);
   Op op;
@@ -207,7 +216,8 @@ Program layer_program(const LlamaShape& s, const std::string& name) {
   Builder b(name);
   const int x = b.input("x", whole_row(s.d_model));
   const int pos = b.row_ints("position", 1, s.positions);
-  const int slot = b.row_ints("slot", 1, s.slots);
+  // A row's sequence: its slot of the ring, or its block table of the pool.
+  const int slot = s.paged() ? b.row_ints("block_table", s.table_len(), s.blocks) : b.row_ints("slot", 1, s.slots);
   const int attn_norm = b.weight("attn_norm", {s.d_model}, s.weights);
   const int wq = b.weight("q_proj", {s.q_width(), s.d_model}, s.weights);
   const int wk = b.weight("k_proj", {s.kv_width(), s.d_model}, s.weights);
@@ -218,8 +228,9 @@ Program layer_program(const LlamaShape& s, const std::string& name) {
   const int wu = b.weight("up_proj", {s.ffn, s.d_model}, s.weights);
   const int wd = b.weight("down_proj", {s.d_model, s.ffn}, s.weights);
   const Ring ring{s.slots, s.kv_heads, s.length, s.head_dim};
-  const int kc = b.cache("k_cache", ring, s.cache);
-  const int vc = b.cache("v_cache", ring, s.cache);
+  const Paged pool{s.blocks, s.block_size, s.kv_heads, s.head_dim};
+  const int kc = s.paged() ? b.cache("k_cache", pool, s.cache) : b.cache("k_cache", ring, s.cache);
+  const int vc = s.paged() ? b.cache("v_cache", pool, s.cache) : b.cache("v_cache", ring, s.cache);
   const int a = b.rmsnorm("attn_in", s.eps, attn_norm, 1.0, x);
   const int q = b.linear("q", wq, s.head_dim, a);
   const int k = b.linear("k", wk, s.head_dim, a);

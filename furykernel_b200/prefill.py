@@ -61,8 +61,11 @@ class Prefill:
             ctx.launch(split, {"n": per}, [eng.arena.ptr + eng.wb * l * per, self.w_hi.ptr + at, self.w_lo.ptr + at])
         R = rows
         kmax = max(d, qw, f)
+        # Tokens, positions, then each row's slot or (paged) block table.
         self.rs = (R + 3) // 4 * 4
-        self.rows_buf = ctx.zeros(3 * self.rs, np.uint32)
+        self.seq = s.table_len if s.paged else 1
+        self.rows_words = 2 * self.rs + (R * self.seq + 3) // 4 * 4
+        self.rows_buf = ctx.zeros(self.rows_words, np.uint32)
         self.x = ctx.zeros((R, d))
         self.a = ctx.zeros((R, d))
         self.a_hi = ctx.zeros((R, kmax))
@@ -81,7 +84,8 @@ class Prefill:
         # One prompt (one slot) a run: the attention tiled by queries
         # (attend_prompt), keys shared by 32 rows, instead of the decode
         # attention over every row.
-        self.one_slot = one_slot and self.positions <= min(s.length, 1408)
+        span = s.table_len * s.block_size if s.paged else s.length
+        self.one_slot = one_slot and self.positions <= min(span, 1408)
         ms = R * s.heads * self.max_splits
         self.part = [ctx.zeros(ms), ctx.zeros(ms), ctx.zeros(ms * s.head_dim)]
         self.graphs: dict = {}
@@ -149,13 +153,24 @@ class Prefill:
         nq = qw + 2 * kvw
         for l in range(s.layers):
             w = eng.layer_weights(l)
-            kv, at, cb = by["kv_store_ring"][l], by["attend_split"][l], by["attend_combine"][l]
+            paged = "kv_store_paged" in by
+            kv = by["kv_store_paged" if paged else "kv_store_ring"][l]
+            at = by["attend_split_paged" if paged else "attend_split"][l]
+            cb = by["attend_combine"][l]
             out.append(Launch("rmsnorm_rows" + wsuf, {"rows": m, "h": d, "eps": eps, "factor": 1.0},
                               [self.x.ptr, w["attn_norm"], self.a.ptr]))
             out.append(self._gemm(self.a.ptr, d, w["q_proj"], nq, self.qkv.ptr, nq))
             out.append(Launch(kv.kernel, dict(kv.params, m=m, ldq=nq),
                               [self.qkv.ptr, kv.bufs[1], kv.bufs[2], pos, slot, kv.bufs[5], kv.bufs[6]]))
-            if self.one_slot:
+            if self.one_slot and paged:
+                ap = at.params
+                out.append(Launch("attend_prompt_paged" + csuf, {
+                    "m": m, "heads": ap["heads"], "kv_heads": ap["kv_heads"], "d": ap["d"],
+                    "block_size": ap["block_size"], "table_len": ap["table_len"], "blocks": ap["blocks"],
+                    "rotated": ap["rotated"], "ldq": nq, "q_off": ap["q_off"], "ldo": qw,
+                    "max_pos": self.positions - 1, "scale": ap["scale"]},
+                    [self.qkv.ptr, at.bufs[1], at.bufs[2], pos, slot, at.bufs[5], at.bufs[6], self.att.ptr]))
+            elif self.one_slot:
                 ap = at.params
                 out.append(Launch("attend_prompt" + csuf, {
                     "m": m, "heads": ap["heads"], "kv_heads": ap["kv_heads"], "d": ap["d"], "length": ap["length"],
@@ -191,20 +206,25 @@ class Prefill:
         return out
 
     def set_rows(self, tokens, positions, slots) -> int:
+        """The rows of a run: tokens, positions, and each row's slot or,
+        with a paged cache, its block table [m, table_len]."""
         tokens = np.asarray(tokens, np.uint32)
         m = len(tokens)
+        slots = np.asarray(slots, np.uint32)
+        if self.eng.s.paged and slots.shape != (m, self.seq):
+            raise N.Refused(N.FKC_ERR_ARGUMENT, f"prefill: block tables of shape {slots.shape}, not ({m}, {self.seq}).")
         if m > self.R:
             raise N.Refused(N.FKC_ERR_ARGUMENT, f"prefill: {m} rows, more than {self.R}.")
         if m and int(np.max(positions)) >= self.positions:
             raise N.Refused(N.FKC_ERR_ARGUMENT,
                             f"prefill: position {int(np.max(positions))} is past the {self.positions} it was sized for.")
         self.eng.check_rows(tokens, positions, slots)
-        if self.one_slot and m and len(np.unique(np.asarray(slots))) != 1:
+        if self.one_slot and m and len(np.unique(slots.reshape(m, -1), axis=0)) != 1:
             raise N.Refused(N.FKC_ERR_ARGUMENT, "prefill: a one-slot prefill's rows sit in more than one slot.")
-        host = np.zeros(3 * self.rs, np.uint32)
+        host = np.zeros(self.rows_words, np.uint32)
         host[:m] = tokens
         host[self.rs:self.rs + m] = np.asarray(positions, np.uint32)
-        host[2 * self.rs:2 * self.rs + m] = np.asarray(slots, np.uint32)
+        host[2 * self.rs:2 * self.rs + m * self.seq] = slots.reshape(-1)
         self.rows_buf.upload(host)
         return m
 

@@ -11,7 +11,7 @@ import math
 from dataclasses import dataclass
 
 from .build import program
-from .graph import AttendTo, AttnSpec, Ring, RopeSpec, StoreAt, whole_row
+from .graph import AttendTo, AttnSpec, Paged, Ring, RopeSpec, StoreAt, whole_row
 
 
 @dataclass(frozen=True)
@@ -30,6 +30,11 @@ class LlamaShape:
     positions: int = 4096  # bound of the positions a row may have
     weights: str = "f32"  # every weight's element type: "f32", or "bf16" (the reference's, Build.hs:171-175)
     cache: str = "f32"  # the KV caches' element type: "f32", or "bf16" (CacheBF16, Graph.hs:165-180)
+    # A paged cache (Graph.hs:144-152) instead of the ring: a pool of `blocks`
+    # blocks of `block_size` positions a layer, which each row lists in its
+    # block table of table_len entries. 0: the ring of `slots` and `length`.
+    blocks: int = 0
+    block_size: int = 0
 
     @property
     def q_width(self):
@@ -39,6 +44,15 @@ class LlamaShape:
     def kv_width(self):
         return self.kv_heads * self.head_dim
 
+    @property
+    def paged(self):
+        return self.block_size > 0
+
+    @property
+    def table_len(self):
+        """Block-table entries a row has: enough blocks for every position."""
+        return (self.positions + self.block_size - 1) // self.block_size if self.paged else 0
+
 
 def layer_program(s: LlamaShape, name: str = "layer"):
     """One decoder layer, as a program: the input row x and its position and
@@ -46,7 +60,8 @@ def layer_program(s: LlamaShape, name: str = "layer"):
     b = program(name)
     x = b.input("x", whole_row(s.d_model))
     pos = b.row_ints("position", 1, s.positions)
-    slot = b.row_ints("slot", 1, s.slots)
+    # A row's sequence: its slot of the ring, or its block table of the pool.
+    slot = b.row_ints("block_table", s.table_len, s.blocks) if s.paged else b.row_ints("slot", 1, s.slots)
     attn_norm = b.weight("attn_norm", [s.d_model], s.weights)
     wq = b.weight("q_proj", [s.q_width, s.d_model], s.weights)
     wk = b.weight("k_proj", [s.kv_width, s.d_model], s.weights)
@@ -56,8 +71,10 @@ def layer_program(s: LlamaShape, name: str = "layer"):
     wg = b.weight("gate_proj", [s.ffn, s.d_model], s.weights)
     wu = b.weight("up_proj", [s.ffn, s.d_model], s.weights)
     wd = b.weight("down_proj", [s.d_model, s.ffn], s.weights)
-    kc = b.cache("k_cache", Ring(s.slots, s.kv_heads, s.length, s.head_dim), s.cache)
-    vc = b.cache("v_cache", Ring(s.slots, s.kv_heads, s.length, s.head_dim), s.cache)
+    layout = Paged(s.blocks, s.block_size, s.kv_heads, s.head_dim) if s.paged else \
+        Ring(s.slots, s.kv_heads, s.length, s.head_dim)
+    kc = b.cache("k_cache", layout, s.cache)
+    vc = b.cache("v_cache", layout, s.cache)
     a = b.rmsnorm("attn_in", s.eps, attn_norm, 1.0, x)
     q = b.linear("q", wq, s.head_dim, a)
     k = b.linear("k", wk, s.head_dim, a)

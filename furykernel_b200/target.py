@@ -176,6 +176,27 @@ SPEC_KERNELS = {
         KernelSig("gemv_bf16", [_bf16("w"), _bf16("x"), _bf16("y", "write")],
                   [_dim("n", 1, 1048576), _dim("k", 4, 65536, 4), _dim("m", 1, 16), _dim("pack", 4, 16, 4),
                    _dim("split", 1, 16), _u("ldx"), _u("ldy")], threads=512),
+        # Paged caches (Graph.hs:144-152): a row's block table instead of its slot.
+        KernelSig("kv_store_paged",
+                  [_f32("qkv"), _f32("cos"), _f32("sin"), _u32("pos"), _u32("table"), _f32("k_cache", "read_write"),
+                   _f32("v_cache", "read_write")],
+                  [_dim("m", 1, 65535), _dim("kv_heads", 1, 1024), _dim("d", 2, 2048, 2), _dim("block_size", 1, 65536),
+                   _dim("table_len", 1, _MAX), _dim("blocks", 1, _MAX), _u("rotated"), _u("ldq"), _u("k_off"),
+                   _u("v_off")], threads=64),
+        KernelSig("attend_split_paged",
+                  [_f32("qkv"), _f32("cos"), _f32("sin"), _u32("pos"), _u32("table"), _f32("k_cache"),
+                   _f32("v_cache"), _f32("part_m", "write"), _f32("part_l", "write"), _f32("part_acc", "write")],
+                  [_dim("m", 1, 16384), _dim("heads", 1, 1024), _dim("kv_heads", 1, 1024), _dim("d", 128, 128),
+                   _dim("block_size", 1, 65536), _dim("table_len", 1, _MAX), _dim("blocks", 1, _MAX), _u("rotated"),
+                   _dim("chunk", 1, 256), _dim("max_splits", 1, 65535), _u("ldq"), _u("q_off"), _f("scale")],
+                  threads=128),
+        KernelSig("attend_prompt_paged",
+                  [_f32("qkv"), _f32("cos"), _f32("sin"), _u32("pos"), _u32("table"), _f32("k_cache"),
+                   _f32("v_cache"), _f32("out", "write")],
+                  [_dim("m", 1, 65535), _dim("heads", 1, 1024), _dim("kv_heads", 1, 1024), _dim("d", 128, 128),
+                   _dim("block_size", 1, 65536), _dim("table_len", 1, _MAX), _dim("blocks", 1, _MAX),
+                   _u("rotated"), _u("ldq"), _u("q_off"), _u("ldo"), _dim("max_pos", 0, 1407), _f("scale")],
+                  threads=128),
     ]
 }
 
@@ -191,7 +212,8 @@ _VARIANTS = [
     ("rmsnorm_rows", "rmsnorm_rows_wbf16", {"gamma"}),
     ("split_tf32", "split_tf32_wbf16", {"x"}),
     *[(base, base + "_kvbf16", {"k_cache", "v_cache"})
-      for base in ("kv_store_ring", "attend_split", "attend_decode", "attend_prompt")],
+      for base in ("kv_store_ring", "attend_split", "attend_decode", "attend_prompt", "kv_store_paged",
+                   "attend_split_paged", "attend_prompt_paged")],
 ]
 for _base, _name, _retyped in _VARIANTS:
     _k = SPEC_KERNELS[_base]

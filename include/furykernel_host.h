@@ -40,7 +40,7 @@ enum {
 };
 
 /* The library's ABI version (this header's FKH_ABI_VERSION). */
-#define FKH_ABI_VERSION 2
+#define FKH_ABI_VERSION 3
 FKH_API int fkh_abi_version(void);
 
 /* A Llama-shaped model (the shapes of the programs the engine plans). */
@@ -50,6 +50,10 @@ typedef struct {
   uint64_t slots, length, positions;
   int weights_bf16; /* every weight bf16 (the reference's element type), else f32 */
   int cache_bf16;   /* the KV caches bf16 (CacheBF16), else f32 */
+  /* A paged cache (Paged, Graph.hs:144-152): a pool of `blocks` blocks of
+   * `block_size` positions a layer, each row's block table of
+   * ceil(positions / block_size) entries; block_size 0: the ring. */
+  uint64_t blocks, block_size;
 } fkh_llama_shape;
 
 /* The planner's options (PlanOptions, src/FuryKernel/Program/Plan.hs:243-268). */

@@ -47,14 +47,38 @@ def host_model(eng):
 
 
 def host_caches(eng):
-    """The KV caches as the device holds them, as f32 (bf16 widened)."""
+    """The KV caches as the device holds them, as f32 (bf16 widened):
+    [layers, slots, kv_heads, length, d] rings, or [layers, blocks,
+    kv_heads, block_size, d] pools."""
     s = eng.s
-    n = s.layers * s.slots * s.kv_heads * s.length * s.head_dim
+    units, unit_len = (s.blocks, s.block_size) if getattr(s, "paged", False) else (s.slots, s.length)
+    n = s.layers * units * s.kv_heads * unit_len * s.head_dim
     cb = getattr(eng, "cb", 4)
     k = download_f32(eng, eng.kbase, n, cb)
     v = download_f32(eng, eng.vbase, n, cb)
-    shp = (s.layers, s.slots, s.kv_heads, s.length, s.head_dim)
+    shp = (s.layers, units, s.kv_heads, unit_len, s.head_dim)
     return k.reshape(shp), v.reshape(shp)
+
+
+def pool_to_rings(pool, tables):
+    """A layer's paged pool [blocks, kv_heads, bs, d] as one ring a row
+    [m, kv_heads, table_len * bs, d]: row r's blocks in its table's order,
+    so that position t of the row is ring position t (cacheIndex,
+    src/FuryKernel/Program/Eval.hs:592-602)."""
+    tables = np.asarray(tables)
+    m, tl = tables.shape
+    _, kvh, bs, d = pool.shape
+    g = pool[tables.reshape(-1)].reshape(m, tl, kvh, bs, d)
+    return np.ascontiguousarray(g.transpose(0, 2, 1, 3, 4).reshape(m, kvh, tl * bs, d))
+
+
+def rings_to_pool(rings, tables, pool):
+    """The rows' rings written back into the pool through their tables."""
+    tables = np.asarray(tables)
+    m, tl = tables.shape
+    _, kvh, bs, d = pool.shape
+    blocks = rings.reshape(m, kvh, tl, bs, d).transpose(0, 2, 1, 3, 4).reshape(m * tl, kvh, bs, d)
+    pool[tables.reshape(-1)] = blocks
 
 
 def splits_of(eng):
@@ -81,11 +105,18 @@ def oracle_decode(eng, layers, embed, final_norm, kcache, vcache, tokens, pos, s
         qkv = O.gemv(w["qkv"], a, next(splits), threads)
         q, k, v = qkv[:, :qw], qkv[:, qw:qw + kvw], qkv[:, qw + kvw:]
         kr = O.rope(k, s.kv_heads, hd, hd // 2, pos, cos_t, sin_t)
-        kc, vc = kcache[l], vcache[l]
-        O.kv_store_ring(as_stored(kr), s.kv_heads, hd, s.length, pos, slot, kc)
-        O.kv_store_ring(as_stored(np.ascontiguousarray(v)), s.kv_heads, hd, s.length, pos, slot, vc)
+        if getattr(s, "paged", False):  # `slot` holds the rows' block tables
+            kc, vc = pool_to_rings(kcache[l], slot), pool_to_rings(vcache[l], slot)
+            length, rslot = s.table_len * s.block_size, np.arange(len(pos), dtype=np.uint32)
+        else:
+            kc, vc, length, rslot = kcache[l], vcache[l], s.length, slot
+        O.kv_store_ring(as_stored(kr), s.kv_heads, hd, length, pos, rslot, kc)
+        O.kv_store_ring(as_stored(np.ascontiguousarray(v)), s.kv_heads, hd, length, pos, rslot, vc)
+        if getattr(s, "paged", False):
+            rings_to_pool(kc, slot, kcache[l])
+            rings_to_pool(vc, slot, vcache[l])
         qr = O.rope(q, s.heads, hd, hd // 2, pos, cos_t, sin_t)
-        att, _ = O.attend(qr, s.heads, s.kv_heads, hd, s.length, pos, slot, kc, vc, scale, eng.chunk, 4,
+        att, _ = O.attend(qr, s.heads, s.kv_heads, hd, length, pos, rslot, kc, vc, scale, eng.chunk, 4,
                           eng.max_splits, threads)
         x1 = O.add(x, O.gemv(w["o"], att, next(splits), threads))
         gu = O.gemv(w["gu"], O.rmsnorm_rows(x1, w["mlp_norm"], eps, 1.0, threads), next(splits), threads)

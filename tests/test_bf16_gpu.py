@@ -8,7 +8,7 @@ itself bit-exact with the oracle -- and to the oracle directly; the decode
 step of a bf16 model to the oracle's decode over the widened model.
 
 These forms have not run on a B200 yet: the module runs only with
-FURYKERNEL_BF16_GPU=1 in the environment, so that a run of the GPU suite
+FURYKERNEL_NEW_KERNELS=1 in the environment, so that a run of the GPU suite
 exercises only kernels that have passed on a GPU before."""
 
 import math
@@ -20,8 +20,8 @@ import pytest
 from oracle import oracle as O
 
 pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("FURYKERNEL_BF16_GPU") != "1",
-                                 reason="the bf16 forms have not run on a B200 yet (FURYKERNEL_BF16_GPU=1 runs them)")]
+              pytest.mark.skipif(os.environ.get("FURYKERNEL_NEW_KERNELS") != "1",
+                                 reason="the bf16 forms have not run on a B200 yet (FURYKERNEL_NEW_KERNELS=1 runs them)")]
 
 THREADS = O.threads_default()
 

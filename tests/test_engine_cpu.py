@@ -62,7 +62,8 @@ def test_prompt_chunks_respect_the_row_budget_and_slots():
 def test_row_inputs_past_the_engine_s_tables_are_refused():
     from furykernel_b200 import _native as N
 
-    eng = SimpleNamespace(s=SimpleNamespace(positions=64, slots=2), full=SimpleNamespace(vocab=100))
+    eng = SimpleNamespace(s=SimpleNamespace(positions=64, slots=2, paged=False, blocks=0),
+                          full=SimpleNamespace(vocab=100))
     Llama.check_rows(eng, [1, 99], [0, 63], [0, 1])
     for tokens, pos, slots, what in (([100], [0], [0], "token 100"), ([1], [64], [0], "position 64"),
                                      ([1], [0], [2], "slot 2")):
@@ -72,3 +73,13 @@ def test_row_inputs_past_the_engine_s_tables_are_refused():
             assert what in str(e)
         else:
             raise AssertionError(what)
+    # A paged cache: every block-table entry within the pool.
+    paged = SimpleNamespace(s=SimpleNamespace(positions=64, slots=1, paged=True, blocks=8),
+                            full=SimpleNamespace(vocab=100))
+    Llama.check_rows(paged, [1, 2], [0, 63], [[0, 1, 2, 3], [7, 6, 5, 4]])
+    try:
+        Llama.check_rows(paged, [1], [0], [[0, 8, 1, 2]])
+    except N.Refused as e:
+        assert "block 8" in str(e)
+    else:
+        raise AssertionError("block 8")

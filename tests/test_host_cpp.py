@@ -35,6 +35,9 @@ SHAPES = [
     LlamaShape(weights="bf16", cache="bf16"),
     LlamaShape(d_model=512, heads=4, kv_heads=2, head_dim=128, ffn=1024, vocab=3000, layers=2, slots=3, length=96,
                positions=96, weights="bf16", cache="f32"),
+    LlamaShape(d_model=512, heads=4, kv_heads=2, head_dim=128, ffn=1024, vocab=3000, layers=2, positions=96,
+               blocks=64, block_size=16),
+    LlamaShape(layers=32, positions=4096, blocks=4096, block_size=16, weights="bf16", cache="bf16"),
 ]
 
 
@@ -165,7 +168,7 @@ def fake_engine(full, batch, rank=0, world=1, peer_exchange=True, fuse_attention
     e.part = [Buf((5 << 44) + (i << 32)) for i in range(3)]
     if fuse_attention is None:
         fuse_attention = batch <= 4
-    e.fuse_attention = fuse_attention and batch <= 64
+    e.fuse_attention = fuse_attention and batch <= 64 and not s.paged
     return e
 
 
@@ -207,6 +210,11 @@ CASES = (
        for w, c in (("bf16", "f32"), ("f32", "bf16"))]
     + [(LlamaShape(layers=32, slots=1, length=4096, positions=4096, weights="bf16", cache="bf16"), 1, 0, 1, True,
         None)]
+    # paged caches: f32 and bf16, batches of every GEMV form, tensor parallelism
+    + [(dataclasses.replace(small(b), blocks=64, block_size=16, cache=c), b, 0, 1, True, None)
+       for b in (1, 3, 9, 65) for c in ("f32", "bf16")]
+    + [(dataclasses.replace(tp_shape(b), blocks=32, block_size=8), b, r, 2, peer, None) for b in (1, 16)
+       for r in (0, 1) for peer in (True, False)]
 )
 
 
@@ -278,6 +286,10 @@ PREFILL_CASES = (
     + [(dataclasses.replace(small(b), weights="bf16", cache="bf16"), b, 0, 1, True, 128, one, m)
        for b, one, m in ((1, False, 100), (1, True, 64), (8, False, 128))]
     + [(dataclasses.replace(tp_shape(1), weights="bf16", cache="bf16"), 1, 1, 2, True, 32, False, 32)]
+    # paged caches: the split attention over rows, and one prompt through its table
+    + [(dataclasses.replace(small(b), blocks=64, block_size=16, cache=c), b, 0, 1, True, 96, one, m)
+       for b, one, m, c in ((1, False, 90, "f32"), (1, True, 96, "f32"), (4, True, 50, "bf16"), (8, False, 96, "bf16"))]
+    + [(dataclasses.replace(tp_shape(1), blocks=32, block_size=8), 1, 1, 2, True, 32, False, 32)]
 )
 
 

@@ -1,0 +1,181 @@
+"""Parity of the paged-cache kernels (`*_paged`, f32 and bf16 caches) on a
+B200, through the C ABI.
+
+A paged cache holds a row's position t in block table[t / block_size] of a
+pool (src/FuryKernel/Program/Eval.hs:592-602); the kernels keep the ring
+kernels' arithmetic position for position, so each is held bit for bit to
+the oracle's ring arithmetic over the row's blocks gathered in table order
+(tests/model_check.py: pool_to_rings), and the decode step of a model with
+paged caches to the oracle's decode.
+
+These kernels have not run on a B200 yet: the module runs only with
+FURYKERNEL_NEW_KERNELS=1 in the environment, so that a run of the GPU suite
+exercises only kernels that have passed on a GPU before."""
+
+import math
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests import model_check as MC
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(os.environ.get("FURYKERNEL_NEW_KERNELS") != "1",
+                                 reason="the paged kernels have not run on a B200 yet (FURYKERNEL_NEW_KERNELS=1 "
+                                        "runs them)")]
+
+THREADS = O.threads_default()
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    from furykernel_b200 import _native as N
+
+    c = N.Context(0)
+    yield c
+    c.close()
+
+
+def same_bits(a, b):
+    a = np.ascontiguousarray(a, np.float32).view(np.uint32)
+    b = np.ascontiguousarray(b, np.float32).view(np.uint32)
+    return a.shape == b.shape and np.array_equal(a, b)
+
+
+def disjoint_tables(seed, m, table_len, blocks):
+    """Each row its own blocks, in a shuffled order."""
+    perm = np.random.default_rng(seed).permutation(blocks)[:m * table_len]
+    return perm.reshape(m, table_len).astype(np.uint32)
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+@pytest.mark.parametrize("m,heads,kv_heads,block_size,positions,chunk", [
+    (2, 4, 2, 16, [5, 40], 16),
+    (3, 8, 8, 32, [0, 129, 191], 64),
+    (1, 32, 32, 16, [2047], 128),
+])
+def test_paged_store_and_attention(ctx, bf16, m, heads, kv_heads, block_size, positions, chunk):
+    d = 128
+    width = (heads + 2 * kv_heads) * d
+    qkv = O.normal(101, m * width).reshape(m, width)
+    pos = np.array(positions, np.uint32)
+    span = int(pos.max()) + 1
+    table_len = (span + block_size - 1) // block_size
+    blocks = m * table_len + 3
+    tables = disjoint_tables(102, m, table_len, blocks)
+    shape = (blocks, kv_heads, block_size, d)
+    kpool = O.normal(103, int(np.prod(shape))).reshape(shape)
+    vpool = O.normal(104, int(np.prod(shape))).reshape(shape)
+    if bf16:
+        kbits, vbits = O.narrow_bf16(kpool).reshape(shape), O.narrow_bf16(vpool).reshape(shape)
+        kpool, vpool = O.widen_bf16(kbits).reshape(shape), O.widen_bf16(vbits).reshape(shape)
+        dk, dv = ctx.to_device(kbits), ctx.to_device(vbits)
+    else:
+        dk, dv = ctx.to_device(kpool), ctx.to_device(vpool)
+    cos_t, sin_t = O.rope_tables(10000.0, d, d // 2, span)
+    max_splits = (span + chunk - 1) // chunk
+    dq, dpos, dtab = ctx.to_device(qkv), ctx.to_device(pos), ctx.to_device(tables)
+    dcos, dsin = ctx.rope_tables(10000.0, d, d // 2, span)
+    pm, pl = ctx.empty(m * heads * max_splits), ctx.empty(m * heads * max_splits)
+    pa = ctx.empty(m * heads * max_splits * d)
+    out = ctx.empty((m, heads * d))
+    suffix = "_kvbf16" if bf16 else ""
+    pg = {"block_size": block_size, "table_len": table_len, "blocks": blocks}
+    ctx.launch("kv_store_paged" + suffix,
+               dict(pg, m=m, kv_heads=kv_heads, d=d, rotated=d // 2, ldq=width, k_off=heads * d,
+                    v_off=(heads + kv_heads) * d), [dq, dcos, dsin, dpos, dtab, dk, dv])
+    ctx.launch("attend_split_paged" + suffix,
+               dict(pg, m=m, heads=heads, kv_heads=kv_heads, d=d, rotated=d // 2, chunk=chunk, max_splits=max_splits,
+                    ldq=width, q_off=0, scale=1.0 / math.sqrt(d)),
+               [dq, dcos, dsin, dpos, dtab, dk, dv, pm, pl, pa])
+    ctx.launch("attend_combine", {"m": m, "heads": heads, "d": d, "chunk": chunk, "max_splits": max_splits,
+                                  "ldo": heads * d}, [pm, pl, pa, dpos, out])
+
+    # The oracle: each row's blocks as a ring, the stores, the ring attention.
+    as_stored = (lambda a: O.widen_bf16(O.narrow_bf16(a)).reshape(a.shape)) if bf16 else (lambda a: a)
+    kr, vr = MC.pool_to_rings(kpool, tables), MC.pool_to_rings(vpool, tables)
+    length, rows = table_len * block_size, np.arange(m, dtype=np.uint32)
+    krot = O.rope(qkv[:, heads * d:(heads + kv_heads) * d], kv_heads, d, d // 2, pos, cos_t, sin_t)
+    O.kv_store_ring(as_stored(krot), kv_heads, d, length, pos, rows, kr)
+    O.kv_store_ring(as_stored(np.ascontiguousarray(qkv[:, (heads + kv_heads) * d:])), kv_heads, d, length, pos,
+                    rows, vr)
+    kwant, vwant = kpool.copy(), vpool.copy()
+    MC.rings_to_pool(kr, tables, kwant)
+    MC.rings_to_pool(vr, tables, vwant)
+    if bf16:
+        assert np.array_equal(dk.download(), O.narrow_bf16(kwant).reshape(shape))
+        assert np.array_equal(dv.download(), O.narrow_bf16(vwant).reshape(shape))
+    else:
+        assert same_bits(dk.download(), kwant) and same_bits(dv.download(), vwant)
+    qrot = O.rope(qkv[:, :heads * d], heads, d, d // 2, pos, cos_t, sin_t)
+    want, _ = O.attend(qrot, heads, kv_heads, d, length, pos, rows, kr, vr, np.float32(1.0 / math.sqrt(d)), chunk,
+                       4, max_splits, THREADS)
+    assert same_bits(out.download(), want)
+    for b in (dq, dpos, dtab, dk, dv, dcos, dsin, pm, pl, pa, out):
+        b.free()
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+def test_paged_prompt_attention_matches_the_ring_form(ctx, bf16):
+    """One prompt's rows through its block table: the same bits as the ring
+    prompt kernel over the blocks gathered into a slot."""
+    m, heads, kv_heads, d, block_size = 70, 4, 2, 128, 16
+    width = (heads + 2 * kv_heads) * d
+    table_len, blocks = 5, 12
+    qkv = O.normal(111, m * width).reshape(m, width)
+    pos = np.arange(m, dtype=np.uint32)
+    table = disjoint_tables(112, 1, table_len, blocks)
+    tables = np.repeat(table, m, axis=0)
+    shape = (blocks, kv_heads, block_size, d)
+    kpool = O.normal(113, int(np.prod(shape))).reshape(shape)
+    vpool = O.normal(114, int(np.prod(shape))).reshape(shape)
+    if bf16:
+        kbits, vbits = O.narrow_bf16(kpool).reshape(shape), O.narrow_bf16(vpool).reshape(shape)
+        kpool, vpool = O.widen_bf16(kbits).reshape(shape), O.widen_bf16(vbits).reshape(shape)
+        dk, dv = ctx.to_device(kbits), ctx.to_device(vbits)
+    else:
+        dk, dv = ctx.to_device(kpool), ctx.to_device(vpool)
+    length = table_len * block_size
+    ring_k = MC.pool_to_rings(kpool, table)  # [1, kv_heads, length, d]
+    ring_v = MC.pool_to_rings(vpool, table)
+    rk, rv = ctx.to_device(ring_k), ctx.to_device(ring_v)
+    dq, dpos, dtab, dslot = ctx.to_device(qkv), ctx.to_device(pos), ctx.to_device(tables), ctx.zeros(m, np.uint32)
+    dcos, dsin = ctx.rope_tables(10000.0, d, d // 2, length)
+    o_paged, o_ring = ctx.empty((m, heads * d)), ctx.empty((m, heads * d))
+    common = {"m": m, "heads": heads, "kv_heads": kv_heads, "d": d, "rotated": d // 2, "ldq": width, "q_off": 0,
+              "ldo": heads * d, "max_pos": m - 1, "scale": 1.0 / math.sqrt(d)}
+    ctx.launch("attend_prompt_paged" + ("_kvbf16" if bf16 else ""),
+               dict(common, block_size=block_size, table_len=table_len, blocks=blocks),
+               [dq, dcos, dsin, dpos, dtab, dk, dv, o_paged])
+    ctx.launch("attend_prompt", dict(common, length=length), [dq, dcos, dsin, dpos, dslot, rk, rv, o_ring])
+    assert same_bits(o_paged.download(), o_ring.download())
+    for b in (dk, dv, rk, rv, dq, dpos, dtab, dslot, dcos, dsin, o_paged, o_ring):
+        b.free()
+
+
+@pytest.mark.parametrize("batch,cache", [(1, "f32"), (3, "f32"), (9, "bf16"), (2, "bf16")])
+def test_paged_model_decode_step(ctx, batch, cache):
+    """A decode step of a model with paged caches, captured as a graph,
+    against the oracle's decode over the rows' blocks: the same ids, logits
+    and residual rows, bit for bit, and the same pools."""
+    from furykernel_b200.engine import Llama
+    from furykernel_b200.program.llama import LlamaShape
+
+    s = LlamaShape(d_model=512, heads=4, kv_heads=4, head_dim=128, ffn=1024, vocab=3000, layers=2, positions=96,
+                   blocks=6 * batch + 5, block_size=16, cache=cache)
+    eng = Llama(ctx, s, batch, seed=400 + batch, chunk=32, prefill_kv=1.0)
+    tokens = O.ints(19 + batch, batch, s.vocab)
+    pos = ((np.arange(batch) * 37 + 5) % 96).astype(np.uint32)
+    tables = disjoint_tables(120 + batch, batch, s.table_len, s.blocks)
+    layers, embed, final_norm = MC.host_model(eng)
+    kc, vc = MC.host_caches(eng)
+    eng.set_rows(tokens, pos, tables)
+    ids = eng.step()
+    want_ids, want_logits, want_x = MC.oracle_decode(eng, layers, embed, final_norm, kc, vc, tokens, pos, tables)
+    assert np.array_equal(ids, want_ids)
+    assert same_bits(eng.logits.download(), want_logits)
+    assert same_bits(eng.x.download(), want_x)
+    gk, gv = MC.host_caches(eng)
+    assert same_bits(gk, kc) and same_bits(gv, vc)
