@@ -14,7 +14,7 @@ _LIB = None
 _PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_build", "libfurykernel_host.so")
 
 FKH_OK, FKH_ERR_ARGUMENT, FKH_ERR_SPACE, FKH_ERR_INTERNAL = 0, 1, 2, 3
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 
 class Shape(ctypes.Structure):
@@ -39,7 +39,8 @@ class Desc(ctypes.Structure):
     _fields_ = [("full", Shape)] + \
                [(n, ctypes.c_uint64) for n in ("batch", "rank", "world", "sms", "chunk")] + \
                [(n, ctypes.c_int) for n in ("gate_up_interleaved", "peer_exchange", "fuse_attention")] + \
-               [(n, ctypes.c_uint64) for n in DESC_ADDRS] + [("part", ctypes.c_uint64 * 3)]
+               [(n, ctypes.c_uint64) for n in DESC_ADDRS] + [("part", ctypes.c_uint64 * 3)] + \
+               [("splits", ctypes.POINTER(ctypes.c_uint32)), ("nsplits", ctypes.c_size_t)]
 
 
 def lib():
@@ -131,8 +132,15 @@ def split_for(n_rows: int, k: int, sms: int) -> int:
     return int(lib().fkh_split_for(n_rows, k, sms))
 
 
-def _desc(full, batch, rank, world, sms, chunk, gate_up_interleaved, peer_exchange, fuse_attention, addrs) -> Desc:
+def _desc(full, batch, rank, world, sms, chunk, gate_up_interleaved, peer_exchange, fuse_attention, addrs,
+          splits=None) -> Desc:
+    """The descriptor; `splits` maps GEMV shapes (n, k) to a selection's
+    split-K (the array stays alive as the descriptor's `_keep`)."""
     d = Desc()
+    if splits:
+        flat = (ctypes.c_uint32 * (3 * len(splits)))(*[v for (n, k), s in sorted(splits.items()) for v in (n, k, s)])
+        d.splits, d.nsplits = ctypes.cast(flat, ctypes.POINTER(ctypes.c_uint32)), len(splits)
+        d._keep = flat
     d.full = shape(full)
     d.batch, d.rank, d.world, d.sms, d.chunk = batch, rank, world, sms, chunk
     d.gate_up_interleaved, d.peer_exchange, d.fuse_attention = (int(gate_up_interleaved), int(peer_exchange),
@@ -166,9 +174,10 @@ def _collect(call, *args) -> list:
 
 
 def llama_launches(full, batch: int, rank: int, world: int, sms: int, chunk: int, gate_up_interleaved: bool,
-                   peer_exchange: bool, fuse_attention: bool, addrs: dict) -> list:
+                   peer_exchange: bool, fuse_attention: bool, addrs: dict, splits=None) -> list:
     """The decode step's launch list (fkh_llama_launches)."""
-    d = _desc(full, batch, rank, world, sms, chunk, gate_up_interleaved, peer_exchange, fuse_attention, addrs)
+    d = _desc(full, batch, rank, world, sms, chunk, gate_up_interleaved, peer_exchange, fuse_attention, addrs,
+              splits)
     return _collect(lib().fkh_llama_launches, ctypes.byref(d))
 
 
@@ -193,3 +202,96 @@ def prefill_launches(decode: tuple, rows: int, chunk: int, positions: int, one_s
     for i, a in enumerate(addrs["part"]):
         p.part[i] = int(a)
     return _collect(lib().fkh_llama_prefill_launches, ctypes.byref(d), ctypes.byref(p), m)
+
+
+# ---- variant spaces and selections -----------------------------------------
+
+def _setup_select(L):
+    text = [ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t), ctypes.c_char_p, ctypes.c_size_t]
+    L.fkh_json_roundtrip.argtypes = [ctypes.c_char_p] + text
+    L.fkh_selection_roundtrip.argtypes = [ctypes.c_char_p] + text
+    L.fkh_space_check.argtypes = [ctypes.c_char_p] + text
+    L.fkh_space_parse_key.argtypes = [ctypes.c_char_p, ctypes.c_char_p] + text
+    L.fkh_space_names.argtypes = [ctypes.c_char_p] + text
+    L.fkh_split_join.argtypes = [ctypes.c_char_p, ctypes.c_char_p] + text
+    u32p = ctypes.POINTER(ctypes.c_uint32)
+    L.fkh_gemv_consider.argtypes = [ctypes.c_uint32] * 5 + [ctypes.POINTER(ctypes.c_int),
+                                                           ctypes.POINTER(ctypes.c_uint64),
+                                                           ctypes.POINTER(ctypes.c_uint64), ctypes.c_char_p,
+                                                           ctypes.c_size_t]
+    L.fkh_gemv_selection_render.argtypes = [u32p, u32p, ctypes.c_size_t, ctypes.c_uint32] + text
+    L.fkh_gemv_selection_validate.argtypes = [ctypes.c_char_p, u32p, ctypes.c_size_t, ctypes.c_uint32, u32p,
+                                              ctypes.c_char_p, ctypes.c_size_t]
+
+
+def _lib_select():
+    L = lib()
+    if not getattr(L, "_select_ready", False):
+        _setup_select(L)
+        L._select_ready = True
+    return L
+
+
+def json_roundtrip(text: str) -> str:
+    """JSON parsed and rendered as the reference renders it."""
+    return _text(_lib_select().fkh_json_roundtrip, text.encode())
+
+
+def selection_roundtrip(text: str) -> str:
+    """A selection's JSON parsed and rendered back (the format only)."""
+    return _text(_lib_select().fkh_selection_roundtrip, text.encode())
+
+
+def space_check(space_json: str) -> list:
+    """What checkSpace refuses of a space given as JSON."""
+    out = _text(_lib_select().fkh_space_check, space_json.encode())
+    return [p for p in out.split("\n") if p]
+
+
+def space_parse_key(space_json: str, key: str) -> str:
+    return _text(_lib_select().fkh_space_parse_key, space_json.encode(), key.encode())
+
+
+def space_names(space_json: str) -> list:
+    return [n for n in _text(_lib_select().fkh_space_names, space_json.encode()).split("\n") if n]
+
+
+def split_join(name: str, right_prefix: str):
+    out = _text(_lib_select().fkh_split_join, name.encode(), right_prefix.encode())
+    return tuple(out.split("\n")) if out else None
+
+
+GEMV_OUTCOMES = ("kept", "illegal", "indivisible", "too few")
+
+
+def gemv_consider(n: int, k: int, m: int, split: int, cores: int) -> tuple:
+    """What pruning makes of GEMV variant s<split> of class n_k_m:
+    (outcome, work units, kernel identity, reasons)."""
+    kind, groups, h = ctypes.c_int(), ctypes.c_uint64(), ctypes.c_uint64()
+    reasons = ctypes.create_string_buffer(512)
+    _check(_lib_select().fkh_gemv_consider(n, k, m, split, cores, ctypes.byref(kind), ctypes.byref(groups),
+                                           ctypes.byref(h), reasons, len(reasons)), reasons)
+    return GEMV_OUTCOMES[kind.value], groups.value, h.value, reasons.value.decode()
+
+
+def _classes(classes):
+    flat = (ctypes.c_uint32 * (3 * len(classes)))(*[int(v) for c in classes for v in c])
+    return flat, len(classes)
+
+
+def gemv_selection_render(classes, splits, cores: int) -> str:
+    """A selection of this target's GEMV family: classes (n, k, m), each
+    its split."""
+    flat, n = _classes(classes)
+    sp = (ctypes.c_uint32 * n)(*splits)
+    return _text(_lib_select().fkh_gemv_selection_render, flat, sp, n, cores)
+
+
+def gemv_selection_validate(text: str, classes, cores: int) -> list:
+    """Each class's split from a committed selection, or a Refused with
+    every problem, one a line."""
+    flat, n = _classes(classes)
+    out = (ctypes.c_uint32 * max(n, 1))()
+    err = ctypes.create_string_buffer(8192)
+    _check(_lib_select().fkh_gemv_selection_validate(text.encode(), flat, n, cores, out, err, len(err)), err)
+    return list(out[:n])

@@ -292,7 +292,8 @@ class Llama:
 
     def __init__(self, ctx: N.Context, shape: LlamaShape, batch: int, seed: int = 2026, chunk: int = 32,
                  pdl: bool = True, prefill_kv: float | None = None, rank: int = 0, world: int = 1,
-                 host_weights=None, peer_exchange: bool = True, fuse_attention: bool | None = None):
+                 host_weights=None, peer_exchange: bool = True, fuse_attention: bool | None = None,
+                 selection: str | None = None):
         import dataclasses
 
         full = shape
@@ -397,6 +398,13 @@ class Llama:
         if fuse_attention is None:
             fuse_attention = m <= 4
         self.fuse_attention = fuse_attention and m <= 64 and not s.paged
+        # A committed selection (furykernel_b200.select): each GEMV shape's
+        # split-K, the same at every batch.
+        self.splits = {}
+        if selection is not None:
+            from . import select
+
+            self.splits = select.splits_for(self, selection)
         self.launches = self._launches()
         self.graph = None
 
@@ -469,7 +477,7 @@ class Llama:
         """fkh_llama_desc's fields: the shape, the batch, the rank, the
         choices and the addresses."""
         return (self.full, self.m, self.rank, self.world, self.ctx.sms, self.chunk, self.gate_up_interleaved,
-                self.peer_exchange, self.fuse_attention, self.launch_addresses())
+                self.peer_exchange, self.fuse_attention, self.launch_addresses(), getattr(self, "splits", None))
 
     def _launches_restated(self) -> list:
         """The same launch list in Python (the restatement the host
@@ -516,10 +524,17 @@ class Llama:
         out.append(Launch("advance", {"m": m}, [self.out_ids.ptr, self.tokens.ptr, self.pos.ptr]))
         for L in out:  # split-K per GEMV shape
             if L.kernel.startswith("gemv"):
-                # The streaming (m <= 4) and batched (m <= 64) kernels'
-                # parallelism is rows whatever the split, so they keep one;
-                # the chunked kernel splits long rows.
-                L.params["split"] = 1 if m <= 64 else split_for(L.params["n"], L.params["k"], self.ctx.sms)
+                # A selection's pick for the shape, the same at every batch;
+                # else one, which the streaming (m <= 4) and batched
+                # (m <= 64) kernels keep (their parallelism is rows whatever
+                # the split); past 64 rows the chunked kernel splits long rows.
+                n, k = L.params["n"], L.params["k"]
+                split = getattr(self, "splits", {}).get((n, k), 1 if m <= 64 else split_for(n, k, self.ctx.sms))
+                if split != 1 and m > 4 and kernel_form(L.kernel)[0] in ("gemv_rmsnorm_silu",
+                                                                         "gemv_reduce_rmsnorm_silu"):
+                    raise N.Refused(N.FKC_ERR_ARGUMENT, f"{L.kernel}: the row-pair kernels take split 1 past batch 4, "
+                                                        f"not {split}.")
+                L.params["split"] = split
         return out
 
     def _fuse_attention(self, launches: list) -> list:

@@ -282,6 +282,9 @@ struct LlamaLaunchDesc {
   uint64_t x = 0, x1 = 0, qkv = 0, att = 0, gu = 0, act = 0, logits = 0, out_ids = 0;
   uint64_t partial = 0, pairs = 0, pairs_all = 0;
   uint64_t part[3] = {0, 0, 0};
+  // A committed selection's split-K for each GEMV shape (n, k), for every
+  // batch alike; shapes it does not list take the default.
+  std::map<std::pair<uint64_t, uint64_t>, uint64_t> splits;
 };
 
 std::vector<Launch> llama_launches(const LlamaLaunchDesc& d);

@@ -7,6 +7,7 @@
 
 #include "../../include/furykernel_host.h"
 #include "fkh.h"
+#include "fkh_select.h"
 
 struct fkh_launches {
   std::vector<fkh::Launch> list;
@@ -105,6 +106,12 @@ fkh::LlamaLaunchDesc desc_of(const fkh_llama_desc& desc) {
   d.pairs = desc.pairs;
   d.pairs_all = desc.pairs_all;
   for (int i = 0; i < 3; ++i) d.part[i] = desc.part[i];
+  if (desc.nsplits && !desc.splits) throw fkh::Refusal("nsplits without splits.");
+  for (size_t i = 0; i < desc.nsplits; ++i) {
+    const uint32_t s = desc.splits[3 * i + 2];
+    if (s != 1 && s != 2 && s != 4 && s != 8) throw fkh::Refusal("a split of " + std::to_string(s) + ", not 1, 2, 4 or 8.");
+    d.splits[{desc.splits[3 * i], desc.splits[3 * i + 1]}] = s;
+  }
   return d;
 }
 
@@ -223,5 +230,172 @@ uint64_t fkh_launch_buf(const fkh_launches* l, size_t i, size_t j) {
 void fkh_launches_free(fkh_launches* l) { delete l; }
 
 uint64_t fkh_split_for(uint64_t n_rows, uint64_t k, uint64_t sms) { return fkh::split_for(n_rows, k, sms); }
+
+// ---- JSON, variant spaces, selections -------------------------------------
+
+int fkh_json_roundtrip(const char* text, char* buf, size_t cap, size_t* len, char* err, size_t err_cap) {
+  return guarded(err, err_cap, [&] {
+    if (!text) throw fkh::Refusal("no text.");
+    return put_text(fkh::render_json(fkh::parse_json(text)), buf, cap, len);
+  });
+}
+
+int fkh_selection_roundtrip(const char* text, char* buf, size_t cap, size_t* len, char* err, size_t err_cap) {
+  return guarded(err, err_cap, [&] {
+    if (!text) throw fkh::Refusal("no text.");
+    return put_text(fkh::render_selection(fkh::parse_selection(text)), buf, cap, len);
+  });
+}
+
+namespace {
+
+std::vector<fkh::VShape> gemv_classes(const uint32_t* classes, size_t count) {
+  if (count && !classes) throw fkh::Refusal("no classes.");
+  std::vector<fkh::VShape> out;
+  for (size_t i = 0; i < count; ++i)
+    out.push_back({{"n", classes[3 * i]}, {"k", classes[3 * i + 1]}, {"m", classes[3 * i + 2]}});
+  return out;
+}
+
+// A space from its JSON description: {"family": ..., "axes": [{"name",
+// "prefix", "values": [...], "order"}], "classes": [{dim: value, ...} or
+// [[dim, value], ...]], "batch": [...]}; its points are all kept, each its
+// own kernel.
+fkh::Space space_of(const std::string& text) {
+  const fkh::Json j = fkh::parse_json(text);
+  auto get = [&](const fkh::Json& o, const std::string& k) -> const fkh::Json& {
+    for (const auto& m : o.members)
+      if (m.first == k) return m.second;
+    throw fkh::Refusal("the space has no " + k + ".");
+  };
+  fkh::Space sp;
+  sp.family = get(j, "family").s;
+  for (const fkh::Json& a : get(j, "axes").items) {
+    fkh::Axis ax{get(a, "name").s, get(a, "prefix").s, {}, get(a, "order").b};
+    for (const fkh::Json& v : get(a, "values").items) ax.values.push_back((uint64_t)v.i);
+    sp.axes.push_back(ax);
+  }
+  for (const fkh::Json& c : get(j, "classes").items) {  // an object, or a list of [dimension, value] pairs
+    fkh::VShape s;
+    if (c.kind == fkh::Json::Array) {
+      for (const fkh::Json& dv : c.items)
+        if (dv.kind == fkh::Json::Array && dv.items.size() == 2) s.emplace_back(dv.items[0].s, (uint64_t)dv.items[1].i);
+    } else {
+      for (const auto& [d, v] : c.members) s.emplace_back(d, (uint64_t)v.i);
+    }
+    sp.shapes.push_back(s);
+  }
+  for (const fkh::Json& b : get(j, "batch").items) sp.batch.push_back(b.s);
+  sp.consider = [](const fkh::VShape& s, const fkh::Point& p, uint64_t) {
+    fkh::Outcome o;
+    o.kind = fkh::Outcome::Kept;
+    o.hash = std::hash<std::string>{}(fkh::shape_key(s) + "/" + fkh::axis_key(p));
+    return o;
+  };
+  return sp;
+}
+
+}  // namespace
+
+int fkh_space_check(const char* space_json, char* buf, size_t cap, size_t* len, char* err, size_t err_cap) {
+  return guarded(err, err_cap, [&] {
+    if (!space_json) throw fkh::Refusal("no space.");
+    std::string out;
+    for (const std::string& p : fkh::check_space(space_of(space_json))) out += p + "\n";
+    return put_text(out, buf, cap, len);
+  });
+}
+
+int fkh_space_parse_key(const char* space_json, const char* key, char* buf, size_t cap, size_t* len, char* err,
+                        size_t err_cap) {
+  return guarded(err, err_cap, [&] {
+    if (!space_json || !key) throw fkh::Refusal("no space or no key.");
+    return put_text(fkh::axis_key(fkh::parse_axis_key(space_of(space_json).axes, key)), buf, cap, len);
+  });
+}
+
+int fkh_space_names(const char* space_json, char* buf, size_t cap, size_t* len, char* err, size_t err_cap) {
+  return guarded(err, err_cap, [&] {
+    if (!space_json) throw fkh::Refusal("no space.");
+    const fkh::Space sp = space_of(space_json);
+    std::string out;
+    for (const fkh::VShape& s : sp.shapes)
+      for (const fkh::Point& p : fkh::points(sp.axes)) {
+        const std::string name = fkh::variant_name(sp, s, p);
+        fkh::VShape back;
+        fkh::Point pb;
+        const bool ok = fkh::variant_of_name(sp, name, back, pb) && back == s && pb == p;
+        out += name + (ok ? "" : " (does not read back)") + "\n";
+      }
+    return put_text(out, buf, cap, len);
+  });
+}
+
+int fkh_split_join(const char* name, const char* right_prefix, char* buf, size_t cap, size_t* len, char* err,
+                   size_t err_cap) {
+  return guarded(err, err_cap, [&] {
+    if (!name || !right_prefix) throw fkh::Refusal("no name.");
+    const std::string pre = right_prefix;
+    // Valid: the prefix then one or more digits.
+    auto valid = [&](const std::string& r) {
+      if (r.compare(0, pre.size(), pre) != 0 || r.size() == pre.size()) return false;
+      for (size_t i = pre.size(); i < r.size(); ++i)
+        if (r[i] < '0' || r[i] > '9') return false;
+      return true;
+    };
+    std::string left, right;
+    if (!fkh::split_join(valid, name, left, right)) return put_text("", buf, cap, len);
+    return put_text(left + "\n" + right, buf, cap, len);
+  });
+}
+
+int fkh_gemv_consider(uint32_t n, uint32_t k, uint32_t m, uint32_t split, uint32_t cores, int* kind, uint64_t* groups,
+                      uint64_t* hash, char* reasons, size_t reasons_cap) {
+  return guarded(reasons, reasons_cap, [&] {
+    const fkh::Space sp = fkh::gemv_space({});
+    const fkh::Outcome o = sp.consider({{"n", n}, {"k", k}, {"m", m}}, {{"s", split}}, cores);
+    if (kind) *kind = (int)o.kind;
+    if (groups) *groups = o.groups;
+    if (hash) *hash = o.hash;
+    std::string r;
+    for (const std::string& x : o.reasons) r += (r.empty() ? "" : " ") + x;
+    put_err(reasons, reasons_cap, r.c_str());
+    return FKH_OK;
+  });
+}
+
+int fkh_gemv_selection_render(const uint32_t* classes, const uint32_t* splits, size_t count, uint32_t cores,
+                              char* buf, size_t cap, size_t* len, char* err, size_t err_cap) {
+  return guarded(err, err_cap, [&] {
+    if (count && !splits) throw fkh::Refusal("no splits.");
+    const std::vector<fkh::VShape> cls = gemv_classes(classes, count);
+    const fkh::Space sp = fkh::gemv_space(cls);
+    fkh::Selection sel;
+    sel.family = sp.family;
+    sel.target = fkh::kTargetName;
+    sel.cores = cores;
+    for (size_t i = 0; i < count; ++i) {
+      const fkh::Point p{{"s", splits[i]}};
+      const fkh::Outcome o = sp.consider(cls[i], p, cores);
+      if (o.kind != fkh::Outcome::Kept)
+        throw fkh::Refusal(fkh::variant_name(sp, cls[i], p) + " is not a kept variant of its class.");
+      sel.classes[fkh::shape_key(cls[i])] = fkh::Pick{fkh::axis_key(p), o.hash};
+    }
+    fkh::validate_selection(cores, fkh::kTargetName, sp, sel);
+    return put_text(fkh::render_selection(sel), buf, cap, len);
+  });
+}
+
+int fkh_gemv_selection_validate(const char* text, const uint32_t* classes, size_t count, uint32_t cores,
+                                uint32_t* splits, char* err, size_t err_cap) {
+  return guarded(err, err_cap, [&] {
+    if (!text || (count && !splits)) throw fkh::Refusal("no selection or no place for the splits.");
+    const fkh::Space sp = fkh::gemv_space(gemv_classes(classes, count));
+    const std::vector<fkh::Point> picks = fkh::validate_selection(cores, fkh::kTargetName, sp,
+                                                                  fkh::parse_selection(text));
+    for (size_t i = 0; i < picks.size(); ++i) splits[i] = (uint32_t)picks[i][0].second;
+    return FKH_OK;
+  });
+}
 
 }  // extern "C"

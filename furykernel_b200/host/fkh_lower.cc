@@ -618,9 +618,21 @@ std::vector<Launch> llama_launches(const LlamaLaunchDesc& d) {
   adv.params = {{"m", (double)m}};
   adv.bufs = {d.out_ids, d.tokens, d.pos};
   out.push_back(adv);
-  for (Launch& L : out)  // split-K a GEMV: the streaming and batched kernels keep one
-    if (L.kernel.rfind("gemv", 0) == 0)
-      L.set("split", (double)(m <= 64 ? 1 : split_for((uint64_t)L.param("n"), (uint64_t)L.param("k"), d.sms)));
+  // Split-K a GEMV: a selection's pick for its shape, the same at every
+  // batch (so that a row's bits do not depend on its batch); else one,
+  // which the streaming and batched kernels keep (past 64 rows, the
+  // chunked kernel's choice for the shape).
+  for (Launch& L : out) {
+    if (L.kernel.rfind("gemv", 0) != 0) continue;
+    const uint64_t n = (uint64_t)L.param("n"), k = (uint64_t)L.param("k");
+    auto it = d.splits.find({n, k});
+    const uint64_t split = it != d.splits.end() ? it->second : m <= 64 ? 1 : split_for(n, k, d.sms);
+    const std::string base = kernel_form(L.kernel).first;
+    if (split != 1 && m > 4 && (base == "gemv_rmsnorm_silu" || base == "gemv_reduce_rmsnorm_silu"))
+      throw Refusal(L.kernel + ": the row-pair kernels take split 1 past batch 4, not " + std::to_string(split) +
+                    ".");
+    L.set("split", (double)split);
+  }
   return out;
 }
 

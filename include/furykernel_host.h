@@ -40,7 +40,7 @@ enum {
 };
 
 /* The library's ABI version (this header's FKH_ABI_VERSION). */
-#define FKH_ABI_VERSION 3
+#define FKH_ABI_VERSION 4
 FKH_API int fkh_abi_version(void);
 
 /* A Llama-shaped model (the shapes of the programs the engine plans). */
@@ -92,6 +92,10 @@ typedef struct {
   uint64_t x, x1, qkv, att, gu, act, logits, out_ids;
   uint64_t partial, pairs, pairs_all; /* NCCL tensor parallelism */
   uint64_t part[3];                   /* split attention's partials */
+  /* A committed selection's split-K for GEMV shapes: nsplits triples
+   * (n, k, split), the same split at every batch; NULL for the default. */
+  const uint32_t *splits;
+  size_t nsplits;
 } fkh_llama_desc;
 
 /* A launch list: kernel names of the CUDA target's table, parameters by
@@ -134,6 +138,41 @@ FKH_API int fkh_llama_prefill_launches(const fkh_llama_desc *desc, const fkh_pre
 
 /* Split-K for a GEMV of n rows of k on `sms` SMs (the chunked kernel's). */
 FKH_API uint64_t fkh_split_for(uint64_t n_rows, uint64_t k, uint64_t sms);
+
+/* ---- variant spaces and selections ---------------------------------------
+ * JSON as the reference writes it (src/FuryKernel/Json.hs): parsed and
+ * rendered back, or the parse error and its character. */
+FKH_API int fkh_json_roundtrip(const char *text, char *buf, size_t cap, size_t *len, char *err, size_t err_cap);
+/* A selection (src/FuryKernel/Selection.hs:8-36, the format, version 1)
+ * parsed and rendered back, or what is wrong with its format. */
+FKH_API int fkh_selection_roundtrip(const char *text, char *buf, size_t cap, size_t *len, char *err,
+                                    size_t err_cap);
+/* A variant space given as JSON ({"family", "axes": [{"name", "prefix",
+ * "values", "order"}], "classes": [{dimension: value}], "batch"}): what
+ * checkSpace refuses (Variant.hs), one a line; an axis key read back (or
+ * parseAxisKey's message); every variant's name, each marked where it does
+ * not read back. */
+FKH_API int fkh_space_check(const char *space_json, char *buf, size_t cap, size_t *len, char *err, size_t err_cap);
+FKH_API int fkh_space_parse_key(const char *space_json, const char *key, char *buf, size_t cap, size_t *len,
+                                char *err, size_t err_cap);
+FKH_API int fkh_space_names(const char *space_json, char *buf, size_t cap, size_t *len, char *err, size_t err_cap);
+/* splitJoin (Variant.hs): a name split at the first _x_ whose right side is
+ * right_prefix and digits, as "left\nright"; empty where none is. */
+FKH_API int fkh_split_join(const char *name, const char *right_prefix, char *buf, size_t cap, size_t *len, char *err,
+                           size_t err_cap);
+/* This target's GEMV family (classes n_k_m, m the batch; one axis, the
+ * split-K s, which orders the reduction): what pruning makes of a point
+ * (kind: 0 kept, 1 illegal, 2 indivisible, 3 too few work units; the
+ * launch's work units; the kernel identity the selection records as its IR
+ * hash; the reasons); a selection of the given splits rendered; a
+ * selection validated against classes (n, k, m triples) on a GPU of `cores`
+ * SMs, giving each class's split, or every problem, one a line. */
+FKH_API int fkh_gemv_consider(uint32_t n, uint32_t k, uint32_t m, uint32_t split, uint32_t cores, int *kind,
+                              uint64_t *groups, uint64_t *hash, char *reasons, size_t reasons_cap);
+FKH_API int fkh_gemv_selection_render(const uint32_t *classes, const uint32_t *splits, size_t count, uint32_t cores,
+                                      char *buf, size_t cap, size_t *len, char *err, size_t err_cap);
+FKH_API int fkh_gemv_selection_validate(const char *text, const uint32_t *classes, size_t count, uint32_t cores,
+                                        uint32_t *splits, char *err, size_t err_cap);
 
 #ifdef __cplusplus
 }
