@@ -80,6 +80,14 @@ void fko_attend_combine(uint32_t m, uint32_t heads, uint32_t d, const uint32_t *
                         uint32_t chunk, uint32_t max_splits, const float *part_m,
                         const float *part_l, const float *part_acc, float *out);
 void fko_silu_mul(const float *a, const float *b, uint64_t n, float *y);
+float fko_gelu_tanh(float x);
+void fko_route_topk(const float *x, uint32_t m, uint32_t n, uint32_t k, const float *scale, uint32_t *ids,
+                    float *ws);
+void fko_gemv_routed(const float *table, uint32_t entries, uint32_t n, uint32_t kk, const uint32_t *ids, uint32_t m,
+                     uint32_t k, const float *x, uint32_t xw, uint32_t split, float *y, int threads);
+void fko_gated_gelu(const float *x, uint64_t segments, uint32_t f, float *y);
+void fko_combine_ranks_add(const float *r, const float *ws, const float *segs, uint32_t m, uint32_t k, uint32_t d,
+                           float *y);
 void fko_add(const float *a, const float *b, uint64_t n, float *y);
 void fko_gather(const float *table, uint32_t width, const uint32_t *tokens, uint32_t m,
                 float factor, float *y);

@@ -535,6 +535,123 @@ void fko_silu_mul(const float *a, const float *b, uint64_t n, float *y) {
   }
 }
 
+/* ------------------------------------------------------------------------ */
+/* Routed experts (Graph.hs:306-340; their meaning, Eval.hs:291-320, 356-416, */
+/* 648-656), in this target's binary32 order.                               */
+
+/* GELU, the tanh form (geluTanh, Eval.hs:658-659), evaluated as written,  */
+/* left to right in binary32: (0.5 x) (1 + tanh(c (x + ((0.044715 x) x) x))),*/
+/* c = sqrt(2/pi) rounded to binary32, tanh in binary64 rounded once.       */
+float fko_gelu_tanh(float x) {
+  const float c = (float)0.79788456080286535588;
+  float p = 0.044715f * x;
+  p = p * x;
+  p = p * x;
+  const float u = c * (x + p);
+  const float t = (float)tanh((double)u);
+  return (0.5f * x) * (1.0f + t);
+}
+
+/* Route (routeRow SoftmaxOfTopK, Eval.hs:648-656): each row's top k of its */
+/* n logits, ties to the lower index (a logit is taken where it is greater  */
+/* than the best so far); e_j = exp(x_j - best) (the difference in binary32,*/
+/* exp in binary64 rounded once), their sum in rank order, w_j = e_j / sum, */
+/* times scale[id] where an expert scale is given.                          */
+void fko_route_topk(const float *x, uint32_t m, uint32_t n, uint32_t k, const float *scale, uint32_t *ids,
+                    float *ws) {
+  for (uint32_t r = 0; r < m; ++r) {
+    const float *xr = x + (size_t)r * n;
+    uint32_t *ir = ids + (size_t)r * k;
+    float *wr = ws + (size_t)r * k;
+    for (uint32_t j = 0; j < k; ++j) {
+      uint32_t best = n;
+      for (uint32_t i = 0; i < n; ++i) {
+        int taken = 0;
+        for (uint32_t q = 0; q < j; ++q) taken |= ir[q] == i;
+        if (taken) continue;
+        if (best == n || xr[i] > xr[best]) best = i;
+      }
+      ir[j] = best;
+    }
+    float e[64];
+    const float top = xr[ir[0]];
+    float total = 0.0f;
+    for (uint32_t j = 0; j < k; ++j) {
+      e[j] = (float)exp((double)(xr[ir[j]] - top));
+      total = j == 0 ? e[j] : total + e[j];
+    }
+    for (uint32_t j = 0; j < k; ++j) {
+      float w = e[j] / total;
+      if (scale) w = w * scale[ir[j]];
+      wr[j] = w;
+    }
+  }
+}
+
+/* LinearRouted (Eval.hs:291-320): per row r and rank j, y[r, j n + o] =   */
+/* W[ids[r, j]] row o . x[r, base : base + kk], base 0 when every rank     */
+/* takes the row's one segment (xw == kk), else j kk; the GEMV order       */
+/* contract at pack 4 and split s, as fko_gemv.                             */
+void fko_gemv_routed(const float *table, uint32_t entries, uint32_t n, uint32_t kk, const uint32_t *ids, uint32_t m,
+                     uint32_t k, const float *x, uint32_t xw, uint32_t split, float *y, int threads) {
+  const uint32_t packs = kk / 4;
+  const uint32_t stride = 32 * split;
+#pragma omp parallel for schedule(static) num_threads(threads > 0 ? threads : 1)
+  for (int64_t rj = 0; rj < (int64_t)m * k; ++rj) {
+    const uint32_t r = (uint32_t)(rj / k), j = (uint32_t)(rj % k);
+    const uint32_t e = ids[(size_t)r * k + j];
+    const float *xr = x + (size_t)r * xw + (xw == kk ? 0 : (size_t)j * kk);
+    float *yr = y + (size_t)r * k * n + (size_t)j * n;
+    if (e >= entries) {
+      for (uint32_t o = 0; o < n; ++o) yr[o] = NAN;
+      continue;
+    }
+    for (uint32_t o = 0; o < n; ++o) {
+      const float *wr = table + ((size_t)e * n + o) * kk;
+      float total = 0.0f;
+      for (uint32_t q = 0; q < split; ++q) {
+        float lanes[32];
+        for (uint32_t l = 0; l < 32; ++l) {
+          float acc = 0.0f;
+          for (uint32_t jj = q * 32 + l; jj < packs; jj += stride) {
+            const float *xp = xr + 4 * (size_t)jj;
+            const float *wp = wr + 4 * (size_t)jj;
+            float c = (xp[0] * wp[0] + xp[1] * wp[1]) + (xp[2] * wp[2] + xp[3] * wp[3]);
+            acc = acc + c;
+          }
+          lanes[l] = acc;
+        }
+        float part = fko_simd_sum(lanes, 32);
+        total = q == 0 ? part : total + part;
+      }
+      yr[o] = total;
+    }
+  }
+}
+
+/* GatedGelu (Eval.hs:356-362): per segment of 2 f, gelu(a_i) b_i of its  */
+/* halves a and b; the output's segments are f wide.                       */
+void fko_gated_gelu(const float *x, uint64_t segments, uint32_t f, float *y) {
+  for (uint64_t s = 0; s < segments; ++s)
+    for (uint32_t i = 0; i < f; ++i) {
+      const float a = x[s * 2 * f + i], b = x[s * 2 * f + f + i];
+      y[s * f + i] = fko_gelu_tanh(a) * b;
+    }
+}
+
+/* CombineRanks then the residual Add (Eval.hs:405-416, 336-343): per row, */
+/* ((w_0 s_0 + w_1 s_1) + w_2 s_2) + ... in rank order, then r + that.     */
+void fko_combine_ranks_add(const float *r, const float *ws, const float *segs, uint32_t m, uint32_t k, uint32_t d,
+                           float *y) {
+  for (uint32_t row = 0; row < m; ++row)
+    for (uint32_t i = 0; i < d; ++i) {
+      float acc = ws[(size_t)row * k] * segs[(size_t)row * k * d + i];
+      for (uint32_t j = 1; j < k; ++j)
+        acc = acc + ws[(size_t)row * k + j] * segs[(size_t)row * k * d + (size_t)j * d + i];
+      y[(size_t)row * d + i] = r[(size_t)row * d + i] + acc;
+    }
+}
+
 void fko_add(const float *a, const float *b, uint64_t n, float *y) {
   for (uint64_t i = 0; i < n; ++i) y[i] = a[i] + b[i];
 }

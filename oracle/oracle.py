@@ -79,6 +79,11 @@ def lib():
                                         _f32, _u32, _u32, _u32, _f32p, _f32p, _f32p, _int]),
             "fko_attend_combine": (None, [_u32, _u32, _u32, _u32p, _u32, _u32, _f32p, _f32p, _f32p, _f32p]),
             "fko_silu_mul": (None, [_f32p, _f32p, _u64, _f32p]),
+            "fko_gelu_tanh": (ctypes.c_float, [_f32]),
+            "fko_route_topk": (None, [_f32p, _u32, _u32, _u32, ctypes.c_void_p, _u32p, _f32p]),
+            "fko_gemv_routed": (None, [_f32p, _u32, _u32, _u32, _u32p, _u32, _u32, _f32p, _u32, _u32, _f32p, _int]),
+            "fko_gated_gelu": (None, [_f32p, _u64, _u32, _f32p]),
+            "fko_combine_ranks_add": (None, [_f32p, _f32p, _f32p, _u32, _u32, _u32, _f32p]),
             "fko_add": (None, [_f32p, _f32p, _u64, _f32p]),
             "fko_gather": (None, [_f32p, _u32, _u32p, _u32, _f32, _f32p]),
             "fko_argmax": (None, [_f32p, _u32, _u32, _u32p]),
@@ -262,6 +267,56 @@ def silu_mul(a, b) -> np.ndarray:
     a = _c(a, np.float32)
     y = np.empty_like(a)
     lib().fko_silu_mul(a, _c(b, np.float32), a.size, y)
+    return y
+
+
+def gelu_tanh(x: float) -> np.float32:
+    """GELU, the tanh form, in this target's binary32 order (fko_gelu_tanh)."""
+    return np.float32(lib().fko_gelu_tanh(float(x)))
+
+
+def route_topk(x, k: int, scale=None):
+    """Each row's top k ids (ties to the lower index) and their softmax
+    weights (routeRow, Eval.hs:648-656), times the expert scale if given."""
+    x = _c(x, np.float32)
+    m, n = x.reshape(-1, x.shape[-1]).shape
+    ids = np.empty((m, k), np.uint32)
+    ws = np.empty((m, k), np.float32)
+    sc = _c(scale, np.float32) if scale is not None else None
+    lib().fko_route_topk(x, m, n, k, sc.ctypes.data if sc is not None else None, ids, ws)
+    return ids, ws
+
+
+def gemv_routed(table, ids, x, split: int = 1, threads: int = 1) -> np.ndarray:
+    """LinearRouted: table [entries, n, kk], ids [m, k], x [m, kk] (every
+    rank's input) or [m, k * kk] (a segment a rank); y [m, k * n]."""
+    table = _c(table, np.float32)
+    entries, n, kk = table.shape
+    ids = _c(ids, np.uint32)
+    m, k = ids.shape
+    x = _c(x, np.float32).reshape(m, -1)
+    y = np.empty((m, k * n), np.float32)
+    lib().fko_gemv_routed(table, entries, n, kk, ids, m, k, x, x.shape[1], split, y, threads)
+    return y
+
+
+def gated_gelu(x, f: int) -> np.ndarray:
+    """GatedGelu of segments of 2 f: gelu(first half) * second half."""
+    x = _c(x, np.float32)
+    segs = x.size // (2 * f)
+    y = np.empty(segs * f, np.float32)
+    lib().fko_gated_gelu(x, segs, f, y)
+    return y.reshape(x.shape[:-1] + (x.shape[-1] // 2,)) if x.ndim > 1 else y
+
+
+def combine_ranks_add(r, ws, segs) -> np.ndarray:
+    """r + the route-weighted sum of the ranks' segments, in rank order."""
+    r = _c(r, np.float32)
+    ws = _c(ws, np.float32)
+    m, k = ws.shape
+    d = r.shape[-1]
+    y = np.empty((m, d), np.float32)
+    lib().fko_combine_ranks_add(r, ws, _c(segs, np.float32), m, k, d, y)
     return y
 
 
