@@ -823,6 +823,33 @@ int l_attend_prompt_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
                   "attend_prompt_kvbf16");
 }
 
+// ---- routed experts ------------------------------------------------------
+// route_topk: x ids ws | m n k ldx; route_topk_scaled: x scale ids ws | m n k ldx
+int l_route_topk(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return launched(fk_launch_route_topk(CF(0), p.u(0), p.u(1), p.u(2), p.u(3), nullptr, U(1), F(2), c->pdl, c->stream),
+                  "route_topk");
+}
+int l_route_topk_scaled(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return launched(fk_launch_route_topk(CF(0), p.u(0), p.u(1), p.u(2), p.u(3), CF(1), U(2), F(3), c->pdl, c->stream),
+                  "route_topk_scaled");
+}
+// gemv_routed: table ids x y | entries n kk m k split ldx ldy per_rank
+int l_gemv_routed(fkc_ctx* c, const Params& p, void* const* bufs) {
+  if (p.u(8) > 1) return fail(FKC_ERR_ARGUMENT, "gemv_routed: per_rank is %u, not 0 or 1.", p.u(8));
+  return launched(fk_launch_gemv_routed(CF(0), p.u(0), p.u(1), p.u(2), CU(1), p.u(3), p.u(4), CF(2), p.u(6),
+                                        p.u(8) != 0, p.u(5), F(3), p.u(7), c->pdl, c->stream),
+                  "gemv_routed");
+}
+// gated_gelu: x y | segments f
+int l_gated_gelu(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return launched(fk_launch_gated_gelu(CF(0), p.u(0), p.u(1), F(1), c->pdl, c->stream), "gated_gelu");
+}
+// combine_ranks_add: r ws segs y | m k d
+int l_combine_ranks_add(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return launched(fk_launch_combine_ranks_add(CF(0), CF(1), CF(2), p.u(0), p.u(1), p.u(2), F(3), c->pdl, c->stream),
+                  "combine_ranks_add");
+}
+
 // ---- paged KV caches: block tables into pools of blocks --------------------
 // kv_store_paged: qkv cos sin pos table k_cache v_cache
 //   | m kv_heads d block_size table_len blocks rotated ldq k_off v_off
@@ -1152,6 +1179,30 @@ std::vector<KernelSpec> make_table() {
                 dim("block_size", 1, 65536), dim("table_len", 1, kMax), dim("blocks", 1, kMax), u32("rotated"),
                 u32("ldq"), u32("q_off"), u32("ldo"), dim("max_pos", 0, 1407), f32("scale")},
                l_attend_prompt_paged});
+  // Routed experts (Graph.hs:306-340).
+  t.push_back({"route_topk",
+               32,
+               {{"x", "read", "f32"}, {"ids", "write", "u32"}, {"ws", "write", "f32"}},
+               {dim("m", 1, 65535), dim("n", 1, 1024), dim("k", 1, 8), u32("ldx")},
+               l_route_topk});
+  t.push_back({"route_topk_scaled",
+               32,
+               {{"x", "read", "f32"}, {"scale", "read", "f32"}, {"ids", "write", "u32"}, {"ws", "write", "f32"}},
+               {dim("m", 1, 65535), dim("n", 1, 1024), dim("k", 1, 8), u32("ldx")},
+               l_route_topk_scaled});
+  t.push_back({"gemv_routed",
+               256,
+               {{"table", "read", "f32"}, {"ids", "read", "u32"}, {"x", "read", "f32"}, {"y", "write", "f32"}},
+               {dim("entries", 1, 4096), dim("n", 1, 1048576), dim("kk", 4, 65536, 4), dim("m", 1, 64),
+                dim("k", 1, 8), dim("split", 1, 8), u32("ldx"), u32("ldy"), u32("per_rank")},
+               l_gemv_routed});
+  t.push_back({"gated_gelu", 256, {{"x", "read", "f32"}, {"y", "write", "f32"}},
+               {dim("segments", 1, kMax), dim("f", 1, kMax)}, l_gated_gelu});
+  t.push_back({"combine_ranks_add",
+               256,
+               {{"r", "read", "f32"}, {"ws", "read", "f32"}, {"segs", "read", "f32"}, {"y", "write", "f32"}},
+               {dim("m", 1, 65535), dim("k", 1, 8), dim("d", 1, kMax)},
+               l_combine_ranks_add});
   // The bf16 forms: an f32 entry's parameters with some buffers bf16 (the
   // model's weights, or its KV caches) and their own launchers.
   struct Variant {

@@ -176,6 +176,17 @@ SPEC_KERNELS = {
         KernelSig("gemv_bf16", [_bf16("w"), _bf16("x"), _bf16("y", "write")],
                   [_dim("n", 1, 1048576), _dim("k", 4, 65536, 4), _dim("m", 1, 16), _dim("pack", 4, 16, 4),
                    _dim("split", 1, 16), _u("ldx"), _u("ldy")], threads=512),
+        # Routed experts (Graph.hs:306-340).
+        KernelSig("route_topk", [_f32("x"), _u32("ids", "write"), _f32("ws", "write")],
+                  [_dim("m", 1, 65535), _dim("n", 1, 1024), _dim("k", 1, 8), _u("ldx")], threads=32),
+        KernelSig("route_topk_scaled", [_f32("x"), _f32("scale"), _u32("ids", "write"), _f32("ws", "write")],
+                  [_dim("m", 1, 65535), _dim("n", 1, 1024), _dim("k", 1, 8), _u("ldx")], threads=32),
+        KernelSig("gemv_routed", [_f32("table"), _u32("ids"), _f32("x"), _f32("y", "write")],
+                  [_dim("entries", 1, 4096), _dim("n", 1, 1048576), _dim("kk", 4, 65536, 4), _dim("m", 1, 64),
+                   _dim("k", 1, 8), _dim("split", 1, 8), _u("ldx"), _u("ldy"), _u("per_rank")]),
+        KernelSig("gated_gelu", [_f32("x"), _f32("y", "write")], [_dim("segments", 1, _MAX), _dim("f", 1, _MAX)]),
+        KernelSig("combine_ranks_add", [_f32("r"), _f32("ws"), _f32("segs"), _f32("y", "write")],
+                  [_dim("m", 1, 65535), _dim("k", 1, 8), _dim("d", 1, _MAX)]),
         # Paged caches (Graph.hs:144-152): a row's block table instead of its slot.
         KernelSig("kv_store_paged",
                   [_f32("qkv"), _f32("cos"), _f32("sin"), _u32("pos"), _u32("table"), _f32("k_cache", "read_write"),
