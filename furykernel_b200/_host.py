@@ -14,7 +14,7 @@ _LIB = None
 _PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_build", "libfurykernel_host.so")
 
 FKH_OK, FKH_ERR_ARGUMENT, FKH_ERR_SPACE, FKH_ERR_INTERNAL = 0, 1, 2, 3
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 
 class Shape(ctypes.Structure):
@@ -23,7 +23,8 @@ class Shape(ctypes.Structure):
                [("theta", ctypes.c_double), ("eps", ctypes.c_double)] + \
                [(n, ctypes.c_uint64) for n in ("slots", "length", "positions")] + \
                [("weights_bf16", ctypes.c_int), ("cache_bf16", ctypes.c_int)] + \
-               [("blocks", ctypes.c_uint64), ("block_size", ctypes.c_uint64)]
+               [("blocks", ctypes.c_uint64), ("block_size", ctypes.c_uint64)] + \
+               [("experts", ctypes.c_uint64), ("top_k", ctypes.c_uint64)]
 
 
 class PlanOptions(ctypes.Structure):
@@ -35,12 +36,16 @@ DESC_ADDRS = ("arena", "kbase", "vbase", "cos_t", "sin_t", "tokens", "pos", "slo
               "act", "logits", "out_ids", "partial", "pairs", "pairs_all")
 
 
+MOE_ADDRS = ("mlp_in", "router_logits", "route_ids", "route_weights", "experts_gu", "experts_act", "experts_out")
+
+
 class Desc(ctypes.Structure):
     _fields_ = [("full", Shape)] + \
                [(n, ctypes.c_uint64) for n in ("batch", "rank", "world", "sms", "chunk")] + \
                [(n, ctypes.c_int) for n in ("gate_up_interleaved", "peer_exchange", "fuse_attention")] + \
                [(n, ctypes.c_uint64) for n in DESC_ADDRS] + [("part", ctypes.c_uint64 * 3)] + \
-               [("splits", ctypes.POINTER(ctypes.c_uint32)), ("nsplits", ctypes.c_size_t)]
+               [("splits", ctypes.POINTER(ctypes.c_uint32)), ("nsplits", ctypes.c_size_t)] + \
+               [(n, ctypes.c_uint64) for n in MOE_ADDRS]
 
 
 def lib():
@@ -108,7 +113,8 @@ def shape(s) -> Shape:
         if t not in ("f32", "bf16"):
             raise N.Refused(N.FKC_ERR_ARGUMENT, f"the {what}' element type {t} is not f32 or bf16.")
     return Shape(s.d_model, s.heads, s.kv_heads, s.head_dim, s.ffn, s.vocab, s.layers, s.theta, s.eps, s.slots,
-                 s.length, s.positions, int(s.weights == "bf16"), int(s.cache == "bf16"), s.blocks, s.block_size)
+                 s.length, s.positions, int(s.weights == "bf16"), int(s.cache == "bf16"), s.blocks, s.block_size,
+                 s.experts, s.top_k)
 
 
 def llama_program_text(s, which: str) -> str:
@@ -145,7 +151,7 @@ def _desc(full, batch, rank, world, sms, chunk, gate_up_interleaved, peer_exchan
     d.batch, d.rank, d.world, d.sms, d.chunk = batch, rank, world, sms, chunk
     d.gate_up_interleaved, d.peer_exchange, d.fuse_attention = (int(gate_up_interleaved), int(peer_exchange),
                                                                  int(fuse_attention))
-    for n in DESC_ADDRS:
+    for n in DESC_ADDRS + MOE_ADDRS:
         setattr(d, n, int(addrs.get(n, 0)))
     for i, p in enumerate(addrs["part"]):
         d.part[i] = int(p)

@@ -265,6 +265,79 @@ def lower_step(p, step, b: Binding, tables: dict, attn: dict) -> Launch:
     raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: no kernel runs {_work_text(p, step)}")
 
 
+def lower_steps(p, step, b: Binding, tables: dict, attn: dict) -> list:
+    """One step of a plan as its launches: the routed-experts steps as
+    several (their parts run as separate kernels), any other as
+    lower_step's one."""
+    work = [(w.kind, p.node(w.node)) for w in step.work]
+    kinds = sorted((k, n.op.kind) for k, n in work)
+    vname = lambda v: p.value(v).name  # noqa: E731
+
+    def stored(v) -> View:
+        view = b.values.get(vname(v))
+        if view is None:
+            raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: {vname(v)} is not stored where the step reads it.")
+        return view
+
+    def node(kind):
+        return next(n for _, n in work if n.op.kind == kind)
+
+    stored_values = {st.value for st in step.stores}
+    if kinds == [("Anchor", "Linear"), ("Recompute", "RmsNorm")] and node("RmsNorm").outputs[0] in stored_values:
+        # The norm's row is stored for a later step: the rows, then the GEMV of them.
+        nn, lin = node("RmsNorm"), node("Linear")
+        eps, factor, _ = nn.op.args
+        x, y, out = stored(nn.op.values[0]), stored(nn.outputs[0]), stored(lin.outputs[0])
+        if x.ld != x.width or y.ld != y.width:
+            raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: a stored norm of rows that are not whole.")
+        w = p.source(lin.op.sources[0])
+        wt = _weight_suffix(step, w.kind.type)
+        n, k = w.kind.dims
+        return [Launch("rmsnorm_rows" + wt, {"rows": b.m, "h": x.width, "eps": eps, "factor": factor},
+                       [x.ptr, b.weights[p.source(nn.op.sources[0]).name], y.ptr]),
+                Launch("gemv" + wt, {"n": n, "k": k, "m": b.m, "split": attn.get("split", 1), "ldx": y.ld,
+                                     "ldy": out.ld}, [b.weights[w.name], y.ptr, out.ptr])]
+    if kinds in ([("Anchor", "LinearRouted"), ("Recompute", "Route")],
+                 [("Anchor", "LinearRouted"), ("Recompute", "GatedGelu")]):
+        lr = node("LinearRouted")
+        t = p.source(lr.op.sources[0])
+        if t.kind.type != "f32":
+            raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: no routed kernel reads {t.kind.type} tables.")
+        n, kk = t.kind.dims
+        ids_v, x_id = lr.op.values
+        ids, y = stored(ids_v), stored(lr.outputs[0])
+        k = ids.width
+        out = []
+        if kinds[1][1] == "Route":
+            r = node("Route")
+            logits, ws = stored(r.op.values[0]), stored(r.outputs[1])
+            if r.op.args[0].expert_scale is not None:
+                raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: no kernel scales a route's experts here.")
+            out.append(Launch("route_topk", {"m": b.m, "n": logits.width, "k": k, "ldx": logits.ld},
+                              [logits.ptr, ids.ptr, ws.ptr]))
+            x = stored(x_id)
+        else:
+            g = node("GatedGelu")
+            gu, x = stored(g.op.values[0]), stored(g.outputs[0])
+            if gu.ld != gu.width or x.ld != x.width:
+                raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: a gate of rows that are not whole.")
+            out.append(Launch("gated_gelu", {"segments": b.m * k, "f": kk}, [gu.ptr, x.ptr]))
+        out.append(Launch("gemv_routed", {"entries": t.kind.entries, "n": n, "kk": kk, "m": b.m, "k": k,
+                                          "split": attn.get("split", 1), "ldx": x.ld, "ldy": y.ld,
+                                          "per_rank": int(x.width != kk)},
+                          [b.weights[t.name], ids.ptr, x.ptr, y.ptr]))
+        return out
+    if kinds == [("Recompute", "Add"), ("Recompute", "CombineRanks")]:
+        c, a = node("CombineRanks"), node("Add")
+        ws, segs, y = stored(c.op.values[0]), stored(c.op.values[1]), stored(a.outputs[0])
+        r_id = a.op.values[0] if a.op.values[1] == c.outputs[0] else a.op.values[1]
+        r = stored(r_id)
+        if any(v.ld != v.width for v in (ws, segs, y, r)):
+            raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: a combine of rows that are not whole.")
+        return [Launch("combine_ranks_add", {"m": b.m, "k": ws.width, "d": y.width}, [r.ptr, ws.ptr, segs.ptr, y.ptr])]
+    return [lower_step(p, step, b, tables, attn)]
+
+
 def split_for(n_rows: int, k: int, sms: int) -> int:
     """Split-K for a GEMV of n rows of k: enough warps to fill the device
     with whole rows where possible (one warp streams a row's split)."""
@@ -310,6 +383,9 @@ class Llama:
         self.cb = {"f32": 4, "bf16": 2}.get(s.cache)
         if self.wb is None or self.cb is None:
             raise N.Refused(N.FKC_ERR_ARGUMENT, f"no kernels for {s.weights} weights and {s.cache} caches.")
+        if s.experts and (world > 1 or self.wb != 4 or batch * s.top_k > 64 or s.experts > 1024):
+            raise N.Refused(N.FKC_ERR_ARGUMENT, "routed experts: one GPU, f32 weights, at most 64 (row, expert) "
+                                                "pairs a step and 1024 experts.")
         if self.wb == 2 and any(n % 8 for n in (s.d_model, s.q_width, s.kv_width, s.ffn)):
             raise N.Refused(N.FKC_ERR_ARGUMENT, "bf16 weights: d_model, the q and kv widths and ffn must be multiples "
                             "of 8, so that every weight starts on a 16-byte boundary.")
@@ -334,7 +410,7 @@ class Llama:
         # tied embedding/LM head and the final norm. N(0, 0.02), the norm
         # gains too (the configs give no other law for them).
         d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
-        self.layer_elems = (qw + 2 * kvw) * d + d * qw + 2 * f * d + d * f + 2 * d
+        self.layer_elems = sum(self.layer_sizes())
         wb = self.wb
         self.arena = ctx.alloc(wb * (s.layers * self.layer_elems + full.vocab * d + d))
         fill = ctx.fill_normal if wb == 4 else ctx.fill_normal_bf16
@@ -381,6 +457,12 @@ class Llama:
         self.att = ctx.zeros((m, qw))
         self.gu = ctx.zeros((m, 2 * f))
         self.act = ctx.zeros((m, f))
+        if s.experts:  # the routed FFN's rows: the normed row, logits, route, experts' in and out
+            e, k = s.experts, s.top_k
+            self.moe = {"mlp_in": ctx.zeros((m, d)), "router_logits": ctx.zeros((m, e)),
+                        "route_ids": ctx.zeros((m, k), np.uint32), "route_weights": ctx.zeros((m, k)),
+                        "experts_gu": ctx.zeros((m, k * 2 * f)), "experts_act": ctx.zeros((m, k * f)),
+                        "experts_out": ctx.zeros((m, k * d))}
         self.logits = ctx.zeros((m, self.vocab_local))
         self.pairs = ctx.zeros(2 * m, np.uint32)
         self.pairs_all = ctx.zeros(2 * m * world, np.uint32)
@@ -429,16 +511,25 @@ class Llama:
 
     LAYER_ORDER = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj", "attn_norm",
                    "mlp_norm")
+    # With routed experts: the router and the experts' tables (each entry
+    # [2 ffn, d] gate/up and [d, ffn] down) in place of the dense FFN.
+    MOE_ORDER = ("q_proj", "k_proj", "v_proj", "o_proj", "router", "experts_gate_up", "experts_down", "attn_norm",
+                 "mlp_norm")
+
+    def layer_order(self) -> tuple:
+        return self.MOE_ORDER if self.s.experts else self.LAYER_ORDER
 
     def layer_sizes(self) -> list:
         s = self.s
         d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
+        if s.experts:
+            return [qw * d, kvw * d, kvw * d, d * qw, s.experts * d, s.experts * 2 * f * d, s.experts * d * f, d, d]
         return [qw * d, kvw * d, kvw * d, d * qw, f * d, f * d, d * f, d, d]
 
     def layer_weights(self, l: int) -> dict:
         base = self.arena.ptr + self.wb * l * self.layer_elems
         off, at = {}, 0
-        for name, n in zip(self.LAYER_ORDER, self.layer_sizes()):
+        for name, n in zip(self.layer_order(), self.layer_sizes()):
             off[name] = base + self.wb * at
             at += n
         return off
@@ -463,7 +554,8 @@ class Llama:
                 "x": self.x.ptr, "x1": self.x1.ptr, "qkv": self.qkv.ptr, "att": self.att.ptr, "gu": self.gu.ptr,
                 "act": self.act.ptr, "logits": self.logits.ptr, "out_ids": self.out_ids.ptr,
                 "partial": self.partial.ptr, "pairs": self.pairs.ptr, "pairs_all": self.pairs_all.ptr,
-                "part": [b.ptr for b in self.part]}
+                "part": [b.ptr for b in self.part],
+                **{name: buf.ptr for name, buf in getattr(self, "moe", {}).items()}}
 
     def _launches(self) -> list:
         """The decode step's launches, from libfurykernel_host.so
@@ -501,10 +593,15 @@ class Llama:
                       "attended": View(self.att, 0, qw, qw), "x1": View(self.x1, 0, d, d),
                       "gate": View(self.gu, 0, 2 * f, f), "up": View(self.gu, f, 2 * f, f),
                       "x2": View(self.x, 0, d, d)}
+            if s.experts:
+                e, k = s.experts, s.top_k
+                for name, width in (("mlp_in", d), ("router_logits", e), ("route_ids", k), ("route_weights", k),
+                                    ("experts_gu", k * 2 * f), ("experts_act", k * f), ("experts_out", k * d)):
+                    values[name] = View(self.moe[name], 0, width, width)
             b = Binding(weights=self.layer_weights(l), ints=ints, caches={"k_cache": kc, "v_cache": vc},
                         values=values, m=m)
             for st in self.plans["layer"].steps:
-                out.append(lower_step(p, st, b, tables, attn))
+                out += lower_steps(p, st, b, tables, attn)
         p = self.plans["head"].program
         head_rows = self.embed_ptr() + self.wb * self.rank * self.vocab_local * d
         hb = Binding(weights={"embed": head_rows, "final_norm": self.final_norm_ptr()}, ints=ints, m=m,

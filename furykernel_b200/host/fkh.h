@@ -145,6 +145,11 @@ class Builder {
   int attend(const std::string& name, AttnSpec spec, int q, int keys, int vals, int positions, int sequences);
   int gather(const std::string& name, int table, int tokens, double factor);
   int argmax(const std::string& name, int x);
+  int table(const std::string& name, uint64_t entries, std::vector<uint64_t> dims, const std::string& type);
+  int linear_routed(const std::string& name, int table, int ids, int x);
+  std::pair<int, int> route(const std::string& name, uint64_t k, std::optional<int> scale, int x);
+  int gated_gelu(const std::string& name, int x);
+  int combine_ranks(const std::string& name, int w, int x);
   void output(const std::string& name, int v);
 
   const Program& program() const { return p_; }
@@ -169,6 +174,9 @@ struct LlamaShape {
   double theta = 10000.0, eps = 1e-5;
   uint64_t slots = 1, length = 4096, positions = 4096;
   std::string weights = "f32", cache = "f32";  // element types: "f32" or "bf16"
+  // Routed experts in place of the dense FFN: `experts` of ffn each, every
+  // row taking its top_k (experts 0: the dense SiLU-gated FFN).
+  uint64_t experts = 0, top_k = 2;
   // A paged cache (Graph.hs:144-152) instead of the ring: a pool of `blocks`
   // blocks of `block_size` positions a layer, each row's block table of
   // table_len() entries. block_size 0: the ring of `slots` and `length`.
@@ -261,6 +269,10 @@ struct AttnBufs {
 
 Launch lower_step(const Program& p, const Step& step, const Binding& b, uint64_t cos_t, uint64_t sin_t,
                   const AttnBufs& attn);
+// A step as its launches: the routed-experts steps as several, any other
+// as lower_step's one.
+std::vector<Launch> lower_steps(const Program& p, const Step& step, const Binding& b, uint64_t cos_t, uint64_t sin_t,
+                                const AttnBufs& attn);
 
 // A kernel's element-type form: the f32 entry's name, or with the suffix of
 // its bf16 weights (kW16) or its bf16 KV caches (kKV16).
@@ -285,6 +297,10 @@ struct LlamaLaunchDesc {
   // A committed selection's split-K for each GEMV shape (n, k), for every
   // batch alike; shapes it does not list take the default.
   std::map<std::pair<uint64_t, uint64_t>, uint64_t> splits;
+  // Routed experts: the normed row, the router's logits, the route's ids
+  // and weights, the experts' gate/up rows, their gate, their outputs.
+  uint64_t mlp_in = 0, router_logits = 0, route_ids = 0, route_weights = 0, experts_gu = 0, experts_act = 0,
+           experts_out = 0;
 };
 
 std::vector<Launch> llama_launches(const LlamaLaunchDesc& d);

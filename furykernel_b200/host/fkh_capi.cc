@@ -64,6 +64,9 @@ fkh::LlamaShape shape_of(const fkh_llama_shape& s) {
   o.cache = s.cache_bf16 ? "bf16" : "f32";
   o.blocks = s.blocks;
   o.block_size = s.block_size;
+  o.experts = s.experts;
+  o.top_k = s.top_k;
+  if (o.experts && (o.top_k == 0 || o.top_k > o.experts)) throw fkh::Refusal("top_k must be 1 to experts.");
   if (o.paged() && !o.blocks) throw fkh::Refusal("a paged cache of no blocks.");
   if (!o.heads || !o.kv_heads || o.heads % o.kv_heads || !o.head_dim || o.head_dim % 2 || !o.d_model ||
       !o.ffn || !o.vocab || !o.slots || !o.length || !o.positions)
@@ -106,6 +109,13 @@ fkh::LlamaLaunchDesc desc_of(const fkh_llama_desc& desc) {
   d.pairs = desc.pairs;
   d.pairs_all = desc.pairs_all;
   for (int i = 0; i < 3; ++i) d.part[i] = desc.part[i];
+  d.mlp_in = desc.mlp_in;
+  d.router_logits = desc.router_logits;
+  d.route_ids = desc.route_ids;
+  d.route_weights = desc.route_weights;
+  d.experts_gu = desc.experts_gu;
+  d.experts_act = desc.experts_act;
+  d.experts_out = desc.experts_out;
   if (desc.nsplits && !desc.splits) throw fkh::Refusal("nsplits without splits.");
   for (size_t i = 0; i < desc.nsplits; ++i) {
     const uint32_t s = desc.splits[3 * i + 2];

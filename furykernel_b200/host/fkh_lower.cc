@@ -323,6 +323,112 @@ Launch lower_step(const Program& p, const Step& step, const Binding& b, uint64_t
   throw Refusal(step.name + ": no kernel runs " + work_text(p, step));
 }
 
+std::vector<Launch> lower_steps(const Program& p, const Step& step, const Binding& b, uint64_t cos_t, uint64_t sin_t,
+                                const AttnBufs& attn) {
+  std::vector<std::pair<std::string, std::string>> kinds;
+  for (const Work& w : step.work) kinds.emplace_back(w.kind, p.nodes[w.node].op.kind);
+  std::sort(kinds.begin(), kinds.end());
+  auto node = [&](const std::string& kind) -> const Node& {
+    for (const Work& w : step.work)
+      if (p.nodes[w.node].op.kind == kind) return p.nodes[w.node];
+    throw Refusal(step.name + ": no " + kind + ".");
+  };
+  auto stored = [&](int v) -> View {
+    auto it = b.values.find(p.values[v].name);
+    if (it == b.values.end())
+      throw Refusal(step.name + ": " + p.values[v].name + " is not stored where the step reads it.");
+    return it->second;
+  };
+  auto weight = [&](const std::string& name) -> uint64_t {
+    auto it = b.weights.find(name);
+    if (it == b.weights.end()) throw Refusal(step.name + ": nothing is bound to " + name + ".");
+    return it->second;
+  };
+  auto make = [](const std::string& kernel, std::vector<std::pair<std::string, double>> params,
+                 std::vector<uint64_t> bufs) {
+    Launch L;
+    L.kernel = kernel;
+    L.params = std::move(params);
+    L.bufs = std::move(bufs);
+    return L;
+  };
+  using KP = std::vector<std::pair<std::string, std::string>>;
+  const double m = (double)b.m;
+  bool norm_stored = false;
+  if (kinds == KP{{"Anchor", "Linear"}, {"Recompute", "RmsNorm"}}) {
+    const int v = node("RmsNorm").outputs[0];
+    for (const Stored& st : step.stores)
+      if (st.value == v) norm_stored = true;
+  }
+  if (norm_stored) {  // the norm's row is stored for a later step: the rows, then their GEMV
+    const Node& nn = node("RmsNorm");
+    const Node& lin = node("Linear");
+    const View x = stored(nn.op.values[0]), y = stored(nn.outputs[0]), out = stored(lin.outputs[0]);
+    if (x.ld != x.width || y.ld != y.width) throw Refusal(step.name + ": a stored norm of rows that are not whole.");
+    const Source& w = p.sources[lin.op.sources[0]];
+    const std::string wt = w.kind.type == "bf16" ? kW16 : w.kind.type == "f32" ? "" : "?";
+    if (wt == "?") throw Refusal(step.name + ": no kernel reads " + w.kind.type + " weights.");
+    return {make("rmsnorm_rows" + wt,
+                 {{"rows", m}, {"h", (double)x.width}, {"eps", nn.op.eps}, {"factor", nn.op.factor}},
+                 {x.ptr(), weight(p.sources[nn.op.sources[0]].name), y.ptr()}),
+            make("gemv" + wt,
+                 {{"n", (double)w.kind.dims[0]}, {"k", (double)w.kind.dims[1]}, {"m", m}, {"split", 1.0},
+                  {"ldx", (double)y.ld}, {"ldy", (double)out.ld}},
+                 {weight(w.name), y.ptr(), out.ptr()})};
+  }
+  const bool routed_route = kinds == KP{{"Anchor", "LinearRouted"}, {"Recompute", "Route"}};
+  const bool routed_gate = kinds == KP{{"Anchor", "LinearRouted"}, {"Recompute", "GatedGelu"}};
+  if (routed_route || routed_gate) {
+    const Node& lr = node("LinearRouted");
+    const Source& t = p.sources[lr.op.sources[0]];
+    if (t.kind.type != "f32") throw Refusal(step.name + ": no routed kernel reads " + t.kind.type + " tables.");
+    const uint64_t n = t.kind.dims[0], kk = t.kind.dims[1];
+    const View ids = stored(lr.op.values[0]), y = stored(lr.outputs[0]);
+    const uint64_t k = ids.width;
+    std::vector<Launch> out;
+    View x;
+    if (routed_route) {
+      const Node& r = node("Route");
+      if (r.op.route.expert_scale) throw Refusal(step.name + ": no kernel scales a route's experts here.");
+      const View logits = stored(r.op.values[0]), ws = stored(r.outputs[1]);
+      out.push_back(make("route_topk",
+                         {{"m", m}, {"n", (double)logits.width}, {"k", (double)k}, {"ldx", (double)logits.ld}},
+                         {logits.ptr(), ids.ptr(), ws.ptr()}));
+      x = stored(lr.op.values[1]);
+    } else {
+      const Node& g = node("GatedGelu");
+      const View gu = stored(g.op.values[0]);
+      x = stored(g.outputs[0]);
+      if (gu.ld != gu.width || x.ld != x.width) throw Refusal(step.name + ": a gate of rows that are not whole.");
+      out.push_back(make("gated_gelu", {{"segments", m * (double)k}, {"f", (double)kk}}, {gu.ptr(), x.ptr()}));
+    }
+    out.push_back(make("gemv_routed",
+                       {{"entries", (double)t.kind.entries},
+                        {"n", (double)n},
+                        {"kk", (double)kk},
+                        {"m", m},
+                        {"k", (double)k},
+                        {"split", 1.0},
+                        {"ldx", (double)x.ld},
+                        {"ldy", (double)y.ld},
+                        {"per_rank", x.width != kk ? 1.0 : 0.0}},
+                       {weight(t.name), ids.ptr(), x.ptr(), y.ptr()}));
+    return out;
+  }
+  if (kinds == KP{{"Recompute", "Add"}, {"Recompute", "CombineRanks"}}) {
+    const Node& c = node("CombineRanks");
+    const Node& a = node("Add");
+    const View ws = stored(c.op.values[0]), segs = stored(c.op.values[1]), y = stored(a.outputs[0]);
+    const int r_id = a.op.values[1] == c.outputs[0] ? a.op.values[0] : a.op.values[1];
+    const View r = stored(r_id);
+    for (const View* v : {&ws, &segs, &y, &r})
+      if (v->ld != v->width) throw Refusal(step.name + ": a combine of rows that are not whole.");
+    return {make("combine_ranks_add", {{"m", m}, {"k", (double)ws.width}, {"d", (double)y.width}},
+                 {r.ptr(), ws.ptr(), segs.ptr(), y.ptr()})};
+  }
+  return {lower_step(p, step, b, cos_t, sin_t, attn)};
+}
+
 uint64_t split_for(uint64_t n_rows, uint64_t k, uint64_t sms) {
   for (uint64_t s : {1, 2, 4, 8})
     if (n_rows * s >= sms * 48 || k / s < 1024) return s;
@@ -520,16 +626,40 @@ LlamaShape shard_of(const LlamaLaunchDesc& d) {
   return s;
 }
 
+namespace {
+
+// A layer's weights in the arena, in order: q k v o, the dense FFN's gate
+// up down (or the router and the experts' gate/up and down tables), the
+// two norms.
+void layer_layout(const LlamaShape& s, uint64_t (&sizes)[9], const char* (&names)[9]) {
+  const uint64_t dm = s.d_model, qw = s.q_width(), kvw = s.kv_width(), f = s.ffn, e = s.experts;
+  const uint64_t dense[9] = {qw * dm, kvw * dm, kvw * dm, dm * qw, f * dm, f * dm, dm * f, dm, dm};
+  const uint64_t moe[9] = {qw * dm, kvw * dm, kvw * dm, dm * qw, e * dm, e * 2 * f * dm, e * dm * f, dm, dm};
+  const char* dn[9] = {"q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj", "attn_norm",
+                       "mlp_norm"};
+  const char* mn[9] = {"q_proj", "k_proj", "v_proj", "o_proj", "router", "experts_gate_up", "experts_down",
+                       "attn_norm", "mlp_norm"};
+  for (int i = 0; i < 9; ++i) {
+    sizes[i] = e ? moe[i] : dense[i];
+    names[i] = e ? mn[i] : dn[i];
+  }
+}
+
+}  // namespace
+
 uint64_t layer_elems(const LlamaShape& s) {
-  const uint64_t dm = s.d_model, qw = s.q_width(), kvw = s.kv_width(), f = s.ffn;
-  return (qw + 2 * kvw) * dm + dm * qw + 2 * f * dm + dm * f + 2 * dm;
+  uint64_t sizes[9];
+  const char* names[9];
+  layer_layout(s, sizes, names);
+  uint64_t t = 0;
+  for (uint64_t v : sizes) t += v;
+  return t;
 }
 
 std::map<std::string, uint64_t> layer_weights(const LlamaShape& s, uint64_t arena, uint64_t l) {
-  const uint64_t dm = s.d_model, qw = s.q_width(), kvw = s.kv_width(), f = s.ffn;
-  const uint64_t sizes[9] = {qw * dm, kvw * dm, kvw * dm, dm * qw, f * dm, f * dm, dm * f, dm, dm};
-  const char* names[9] = {"q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj", "attn_norm",
-                          "mlp_norm"};
+  uint64_t sizes[9];
+  const char* names[9];
+  layer_layout(s, sizes, names);
   std::map<std::string, uint64_t> w;
   const uint64_t wb = s.weight_bytes();
   uint64_t at = arena + wb * l * layer_elems(s);
@@ -593,8 +723,17 @@ std::vector<Launch> llama_launches(const LlamaLaunchDesc& d) {
                 {"gate", View{d.gu, 0, 2 * f, f}},
                 {"up", View{d.gu, f, 2 * f, f}},
                 {"x2", View{d.x, 0, dm, dm}}};
+    if (s.experts) {
+      const uint64_t e = s.experts, k = s.top_k;
+      const std::pair<const char*, std::pair<uint64_t, uint64_t>> moe[] = {
+          {"mlp_in", {d.mlp_in, dm}},           {"router_logits", {d.router_logits, e}},
+          {"route_ids", {d.route_ids, k}},      {"route_weights", {d.route_weights, k}},
+          {"experts_gu", {d.experts_gu, k * 2 * f}}, {"experts_act", {d.experts_act, k * f}},
+          {"experts_out", {d.experts_out, k * dm}}};
+      for (const auto& [name, bw] : moe) b.values[name] = View{bw.first, 0, bw.second, bw.second};
+    }
     for (const Step& st : layer_plan.steps)
-      out.push_back(lower_step(layer_plan.program, st, b, d.cos_t, d.sin_t, attn));
+      for (Launch& L : lower_steps(layer_plan.program, st, b, d.cos_t, d.sin_t, attn)) out.push_back(std::move(L));
   }
   {
     Binding hb;

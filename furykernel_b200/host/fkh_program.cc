@@ -207,6 +207,52 @@ int Builder::argmax(const std::string& name, int x) {
   return one(name, op, whole_row(1), "u32");
 }
 
+int Builder::table(const std::string& name, uint64_t entries, std::vector<uint64_t> dims, const std::string& type) {
+  SourceKind k;
+  k.kind = SrcKind::Table;
+  k.entries = entries;
+  k.dims = std::move(dims);
+  k.type = type;
+  k.layout = "out_in";
+  return source(name, k);
+}
+
+int Builder::linear_routed(const std::string& name, int table, int ids, int x) {
+  const uint64_t n = rows_of(table);
+  const uint64_t ranks = p_.values[ids].shape.width;
+  Op op;
+  op.kind = "LinearRouted";
+  op.values = {ids, x};
+  op.sources = {table};
+  return one(name, op, Shape{ranks * n, n});
+}
+
+std::pair<int, int> Builder::route(const std::string& name, uint64_t k, std::optional<int> scale, int x) {
+  Op op;
+  op.kind = "Route";
+  op.values = {x};
+  op.route.k = k;
+  op.route.expert_scale = scale;
+  if (scale) op.sources = {*scale};
+  const auto ids = node(name, op, {{name + "_ids", whole_row(k), "u32"}, {name + "_weights", whole_row(k), "f32"}});
+  return {ids[0], ids[1]};
+}
+
+int Builder::gated_gelu(const std::string& name, int x) {
+  const Shape in = p_.values[x].shape;
+  Op op;
+  op.kind = "GatedGelu";
+  op.values = {x};
+  return one(name, op, Shape{in.width / 2, in.segment / 2});
+}
+
+int Builder::combine_ranks(const std::string& name, int w, int x) {
+  Op op;
+  op.kind = "CombineRanks";
+  op.values = {w, x};
+  return one(name, op, whole_row(p_.values[x].shape.segment));
+}
+
 void Builder::output(const std::string& name, int v) { p_.outputs.push_back(Output{name, v}); }
 
 // ---------------------------------------------------------------------------
@@ -224,9 +270,17 @@ Program layer_program(const LlamaShape& s, const std::string& name) {
   const int wv = b.weight("v_proj", {s.kv_width(), s.d_model}, s.weights);
   const int wo = b.weight("o_proj", {s.d_model, s.q_width()}, s.weights);
   const int mlp_norm = b.weight("mlp_norm", {s.d_model}, s.weights);
-  const int wg = b.weight("gate_proj", {s.ffn, s.d_model}, s.weights);
-  const int wu = b.weight("up_proj", {s.ffn, s.d_model}, s.weights);
-  const int wd = b.weight("down_proj", {s.d_model, s.ffn}, s.weights);
+  // The dense FFN's weights, or the router and the experts' tables.
+  int wg = -1, wu = -1, wd = -1, router = -1, egu = -1, edn = -1;
+  if (s.experts) {
+    router = b.weight("router", {s.experts, s.d_model}, s.weights);
+    egu = b.table("experts_gate_up", s.experts, {2 * s.ffn, s.d_model}, s.weights);
+    edn = b.table("experts_down", s.experts, {s.d_model, s.ffn}, s.weights);
+  } else {
+    wg = b.weight("gate_proj", {s.ffn, s.d_model}, s.weights);
+    wu = b.weight("up_proj", {s.ffn, s.d_model}, s.weights);
+    wd = b.weight("down_proj", {s.d_model, s.ffn}, s.weights);
+  }
   const Ring ring{s.slots, s.kv_heads, s.length, s.head_dim};
   const Paged pool{s.blocks, s.block_size, s.kv_heads, s.head_dim};
   const int kc = s.paged() ? b.cache("k_cache", pool, s.cache) : b.cache("k_cache", ring, s.cache);
@@ -249,11 +303,21 @@ Program layer_program(const LlamaShape& s, const std::string& name) {
   const int out = b.linear("attn_out", wo, 0, o);
   const int x1 = b.add("x1", x, out);
   const int m = b.rmsnorm("mlp_in", s.eps, mlp_norm, 1.0, x1);
-  const int gate = b.linear("gate", wg, 0, m);
-  const int up = b.linear("up", wu, 0, m);
-  const int act = b.silu_mul("mlp_act", gate, up);
-  const int down = b.linear("mlp_out", wd, 0, act);
-  const int x2 = b.add("x2", x1, down);
+  int ffn_out;
+  if (s.experts) {  // each row's top_k experts, GELU-gated, weighted by the route
+    const int logits = b.linear("router_logits", router, 0, m);
+    const auto [ids, ws] = b.route("route", s.top_k, std::nullopt, logits);
+    const int gu = b.linear_routed("experts_gu", egu, ids, m);
+    const int act = b.gated_gelu("experts_act", gu);
+    const int eo = b.linear_routed("experts_out", edn, ids, act);
+    ffn_out = b.combine_ranks("experts_sum", ws, eo);
+  } else {
+    const int gate = b.linear("gate", wg, 0, m);
+    const int up = b.linear("up", wu, 0, m);
+    const int act = b.silu_mul("mlp_act", gate, up);
+    ffn_out = b.linear("mlp_out", wd, 0, act);
+  }
+  const int x2 = b.add("x2", x1, ffn_out);
   b.output("x", x2);
   return b.done();
 }

@@ -44,6 +44,9 @@ class Prefill:
     def __init__(self, eng: Llama, rows: int, chunk: int | None = None, positions: int | None = None,
                  one_slot: bool = False):
         ctx, s = eng.ctx, eng.s
+        if getattr(s, "experts", 0):
+            raise N.Refused(N.FKC_ERR_ARGUMENT, "prefill: routed experts run through the decode step's kernels; "
+                                                "no GEMM form of them is built.")
         self.eng, self.ctx, self.R = eng, ctx, rows
         d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
         for what, k in (("d_model", d), ("q width", qw), ("ffn", f)):

@@ -35,6 +35,10 @@ class LlamaShape:
     # block table of table_len entries. 0: the ring of `slots` and `length`.
     blocks: int = 0
     block_size: int = 0
+    # Routed experts in place of the dense FFN: `experts` of ffn each, every
+    # row taking its top_k (experts 0: the dense SiLU-gated FFN).
+    experts: int = 0
+    top_k: int = 2
 
     @property
     def q_width(self):
@@ -68,9 +72,15 @@ def layer_program(s: LlamaShape, name: str = "layer"):
     wv = b.weight("v_proj", [s.kv_width, s.d_model], s.weights)
     wo = b.weight("o_proj", [s.d_model, s.q_width], s.weights)
     mlp_norm = b.weight("mlp_norm", [s.d_model], s.weights)
-    wg = b.weight("gate_proj", [s.ffn, s.d_model], s.weights)
-    wu = b.weight("up_proj", [s.ffn, s.d_model], s.weights)
-    wd = b.weight("down_proj", [s.d_model, s.ffn], s.weights)
+    # The dense FFN's weights, or the router and the experts' tables.
+    if s.experts:
+        router = b.weight("router", [s.experts, s.d_model], s.weights)
+        egu = b.table("experts_gate_up", s.experts, [2 * s.ffn, s.d_model], s.weights)
+        edn = b.table("experts_down", s.experts, [s.d_model, s.ffn], s.weights)
+    else:
+        wg = b.weight("gate_proj", [s.ffn, s.d_model], s.weights)
+        wu = b.weight("up_proj", [s.ffn, s.d_model], s.weights)
+        wd = b.weight("down_proj", [s.d_model, s.ffn], s.weights)
     layout = Paged(s.blocks, s.block_size, s.kv_heads, s.head_dim) if s.paged else \
         Ring(s.slots, s.kv_heads, s.length, s.head_dim)
     kc = b.cache("k_cache", layout, s.cache)
@@ -89,11 +99,19 @@ def layer_program(s: LlamaShape, name: str = "layer"):
     out = b.linear("attn_out", wo, 0, o)
     x1 = b.add("x1", x, out)
     m = b.rmsnorm("mlp_in", s.eps, mlp_norm, 1.0, x1)
-    gate = b.linear("gate", wg, 0, m)
-    up = b.linear("up", wu, 0, m)
-    act = b.silu_mul("mlp_act", gate, up)
-    down = b.linear("mlp_out", wd, 0, act)
-    x2 = b.add("x2", x1, down)
+    if s.experts:  # each row's top_k experts, GELU-gated, weighted by the route
+        logits = b.linear("router_logits", router, 0, m)
+        ids, ws = b.route("route", s.top_k, None, logits)
+        gu = b.linear_routed("experts_gu", egu, ids, m)
+        act = b.gated_gelu("experts_act", gu)
+        eo = b.linear_routed("experts_out", edn, ids, act)
+        ffn_out = b.combine_ranks("experts_sum", ws, eo)
+    else:
+        gate = b.linear("gate", wg, 0, m)
+        up = b.linear("up", wu, 0, m)
+        act = b.silu_mul("mlp_act", gate, up)
+        ffn_out = b.linear("mlp_out", wd, 0, act)
+    x2 = b.add("x2", x1, ffn_out)
     b.output("x", x2)
     return b.done()
 

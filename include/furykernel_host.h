@@ -40,7 +40,7 @@ enum {
 };
 
 /* The library's ABI version (this header's FKH_ABI_VERSION). */
-#define FKH_ABI_VERSION 4
+#define FKH_ABI_VERSION 5
 FKH_API int fkh_abi_version(void);
 
 /* A Llama-shaped model (the shapes of the programs the engine plans). */
@@ -54,6 +54,9 @@ typedef struct {
    * `block_size` positions a layer, each row's block table of
    * ceil(positions / block_size) entries; block_size 0: the ring. */
   uint64_t blocks, block_size;
+  /* Routed experts in place of the dense FFN: `experts` of ffn each, every
+   * row its top_k (experts 0: the dense FFN). */
+  uint64_t experts, top_k;
 } fkh_llama_shape;
 
 /* The planner's options (PlanOptions, src/FuryKernel/Program/Plan.hs:243-268). */
@@ -96,6 +99,11 @@ typedef struct {
    * (n, k, split), the same split at every batch; NULL for the default. */
   const uint32_t *splits;
   size_t nsplits;
+  /* Routed experts: the normed row [batch, d], the router's logits
+   * [batch, experts], the route's ids (u32) and weights [batch, top_k], the
+   * experts' gate/up rows [batch, top_k * 2 ffn], their gate
+   * [batch, top_k * ffn], their outputs [batch, top_k * d]. */
+  uint64_t mlp_in, router_logits, route_ids, route_weights, experts_gu, experts_act, experts_out;
 } fkh_llama_desc;
 
 /* A launch list: kernel names of the CUDA target's table, parameters by

@@ -33,11 +33,16 @@ def host_model(eng):
         base = l * eng.layer_elems
         at = base
         w = {}
-        for name, rows, cols in [("qkv", qw + 2 * kvw, d), ("o", d, qw), ("gu", 2 * f, d), ("down", d, f),
-                                 ("attn_norm", 1, d), ("mlp_norm", 1, d)]:
+        e = getattr(s, "experts", 0)
+        ffn = [("router", e, d), ("egu", e * 2 * f, d), ("edn", e * d, f)] if e else [("gu", 2 * f, d), ("down", d, f)]
+        for name, rows, cols in [("qkv", qw + 2 * kvw, d), ("o", d, qw)] + ffn + [("attn_norm", 1, d),
+                                                                                   ("mlp_norm", 1, d)]:
             w[name] = flat[at:at + rows * cols].reshape(rows, cols) if rows > 1 else flat[at:at + cols].copy()
             at += rows * cols
-        if eng.gate_up_interleaved:  # rows gate_0, up_0, gate_1, ...: back to [gate; up]
+        if e:  # the experts' tables, an entry each
+            w["egu"] = w["egu"].reshape(e, 2 * f, d)
+            w["edn"] = w["edn"].reshape(e, d, f)
+        elif eng.gate_up_interleaved:  # rows gate_0, up_0, gate_1, ...: back to [gate; up]
             w["gu"] = np.ascontiguousarray(np.concatenate([w["gu"][0::2], w["gu"][1::2]]))
         layers.append(w)
     e0 = s.layers * eng.layer_elems
@@ -119,6 +124,14 @@ def oracle_decode(eng, layers, embed, final_norm, kcache, vcache, tokens, pos, s
         att, _ = O.attend(qr, s.heads, s.kv_heads, hd, length, pos, rslot, kc, vc, scale, eng.chunk, 4,
                           eng.max_splits, threads)
         x1 = O.add(x, O.gemv(w["o"], att, next(splits), threads))
+        if getattr(s, "experts", 0):  # the router, the top k, the experts' GELU-gated FFNs, their weighted sum
+            m_in = O.rmsnorm_rows(x1, w["mlp_norm"], eps, 1.0, threads)
+            logits = O.gemv(w["router"], m_in, next(splits), threads)
+            ids, ws = O.route_topk(logits, s.top_k)
+            gu = O.gemv_routed(w["egu"], ids, m_in, next(splits), threads)
+            eo = O.gemv_routed(w["edn"], ids, O.gated_gelu(gu, f), next(splits), threads)
+            x = O.combine_ranks_add(x1, ws, eo)
+            continue
         gu = O.gemv(w["gu"], O.rmsnorm_rows(x1, w["mlp_norm"], eps, 1.0, threads), next(splits), threads)
         act = O.silu_mul(gu[:, :f], gu[:, f:])
         x = O.add(x1, O.gemv(w["down"], act, next(splits), threads))

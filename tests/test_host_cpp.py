@@ -38,6 +38,8 @@ SHAPES = [
     LlamaShape(d_model=512, heads=4, kv_heads=2, head_dim=128, ffn=1024, vocab=3000, layers=2, positions=96,
                blocks=64, block_size=16),
     LlamaShape(layers=32, positions=4096, blocks=4096, block_size=16, weights="bf16", cache="bf16"),
+    LlamaShape(d_model=512, heads=4, kv_heads=4, head_dim=128, ffn=256, vocab=3000, layers=2, slots=2, length=96,
+               positions=96, experts=8, top_k=2),
 ]
 
 
@@ -156,13 +158,16 @@ def fake_engine(full, batch, rank=0, world=1, peer_exchange=True, fuse_attention
         "head": PL.plan(PL.DEFAULT, head_program(dataclasses.replace(full, vocab=e.vocab_local))),
     }
     d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
-    e.layer_elems = (qw + 2 * kvw) * d + d * qw + 2 * f * d + d * f + 2 * d
+    e.layer_elems = sum(e.layer_sizes())
     at = iter(range(1, 100))
     e.arena = Buf(1 << 44)
     e.kbase, e.vbase = 2 << 44, 3 << 44
     for name in ("cos", "sin", "tokens", "pos", "slot", "out_ids", "x", "x1", "partial", "qkv", "att", "gu",
                  "act", "logits", "pairs", "pairs_all"):
         setattr(e, name, Buf((4 << 44) + (next(at) << 32)))
+    if s.experts:
+        e.moe = {name: Buf((8 << 44) + (i << 36)) for i, name in enumerate(
+            ("mlp_in", "router_logits", "route_ids", "route_weights", "experts_gu", "experts_act", "experts_out"))}
     e.chunk = chunk
     e.max_splits = (s.positions + chunk - 1) // chunk
     e.part = [Buf((5 << 44) + (i << 32)) for i in range(3)]
@@ -215,6 +220,10 @@ CASES = (
        for b in (1, 3, 9, 65) for c in ("f32", "bf16")]
     + [(dataclasses.replace(tp_shape(b), blocks=32, block_size=8), b, r, 2, peer, None) for b in (1, 16)
        for r in (0, 1) for peer in (True, False)]
+    # routed experts: a Mixtral-shaped layer, top 2 of 8, and top 1 of 4 over a paged cache
+    + [(dataclasses.replace(small(b), experts=8, top_k=2), b, 0, 1, True, None) for b in (1, 3, 9, 32)]
+    + [(dataclasses.replace(small(b), experts=4, top_k=1, blocks=32, block_size=16), b, 0, 1, True, None)
+       for b in (1, 5)]
 )
 
 
