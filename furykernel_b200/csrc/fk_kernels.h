@@ -151,6 +151,9 @@ cudaError_t fk_launch_fill_normal(float* out, uint64_t n, uint64_t seed, double 
 cudaError_t fk_launch_fill_uniform(float* out, uint64_t n, uint64_t seed, double a, double b, cudaStream_t s);
 // bf16 weights (k_w16.cu): the f32 kernels' arithmetic over widened weights.
 cudaError_t fk_launch_gemv_w16(const FkGemv& g, const uint16_t* w, const uint16_t* gamma, int sms, cudaStream_t s);
+bool fk_gemv_w16_batches(const FkGemv& g, const uint16_t* w);
+cudaError_t fk_launch_gemv_batch_w16(const FkGemv& g, const uint16_t* w, const uint16_t* gamma, int sms,
+                                     cudaStream_t s);
 cudaError_t fk_launch_gather_w16(const uint16_t* table, uint32_t width, const uint32_t* tokens, uint32_t m,
                                  float factor, float* y, bool pdl, cudaStream_t s);
 cudaError_t fk_launch_rmsnorm_rows_w16(const float* x, const uint16_t* gamma, float* y, uint32_t rows, uint32_t h,

@@ -15,7 +15,8 @@
 // Kernels: the weight-streaming GEMV for batches of up to 4 rows
 // (gemv_stream_w16_kernel, persistent, x staged once a block with its
 // prologue, every epilogue including the tensor-parallel scatter and the
-// reduce-then-normalize prologue), the chunked GEMV for larger batches
+// reduce-then-normalize prologue), the packed batched GEMV for up to 64 rows
+// at split 1 (k_w16_batch.cu), the chunked GEMV for the rest
 // (gemv_chunk_w16_kernel, 32 rows a launch), the embedding gather, RMSNorm
 // rows with a bf16 gain, the TF32 split of bf16 weights (exact: a bf16
 // value has 8 significant bits, a TF32 value 11, so the low half is 0), and
@@ -600,8 +601,11 @@ cudaError_t fk_launch_gemv_w16(const FkGemv& g, const uint16_t* w, const uint16_
       default: return cudaErrorInvalidValue;
     }
   }
-  // Past the streaming kernel: the chunked one, which has no row-pair or
-  // peer forms, 32 batch rows a launch.
+  // Batches up to 64 rows at split 1: the packed batched kernel
+  // (k_w16_batch.cu), which has the row-pair form.
+  if (!peer && fk_gemv_w16_batches(g, w)) return fk_launch_gemv_batch_w16(g, w, gamma, sms, st);
+  // Past those: the chunked kernel, which has no row-pair or peer forms, 32
+  // batch rows a launch.
   if (g.silu_pair || peer || !(g.split == 1 || g.split == 2 || g.split == 4 || g.split == 8))
     return cudaErrorInvalidValue;
   for (uint32_t i0 = 0; i0 < g.m; i0 += 32) {

@@ -703,8 +703,11 @@ int l_gemv_rmsnorm_silu_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
   g.silu_pair = true;
   if (g.n % 2 != 0)
     return fail(FKC_ERR_ARGUMENT, "gemv_rmsnorm_silu_wbf16: n %u is not a whole number of row pairs.", g.n);
-  if (!fk_gemv_streams(g))
-    return fail(FKC_ERR_ARGUMENT, "gemv_rmsnorm_silu_wbf16: m %u is past the streaming kernel's 4.", g.m);
+  if (!fk_gemv_streams(g) && !fk_gemv_w16_batches(g, W16(0)))
+    return fail(FKC_ERR_ARGUMENT,
+                "gemv_rmsnorm_silu_wbf16: m %u, k %u and split %u are past what the row-pair kernels take (m at most "
+                "64, split 1 past m 4).",
+                g.m, g.k, g.split);
   return gemv_w16(c, g, W16(0), W16(2), "gemv_rmsnorm_silu_wbf16");
 }
 int l_gemv_silu_w16(fkc_ctx* c, const Params& p, void* const* bufs) {

@@ -394,8 +394,7 @@ class Llama:
         # 2i + 1), so that the [gate; up] step computes mlp_act = silu(gate) *
         # up on its own tiles and stores it, and the down step reads it: the
         # same bits as recomputing it in the down step, computed once.
-        # (bf16 weights: the streaming kernel's batches, up to 4 rows).
-        self.gate_up_interleaved = batch <= (4 if self.wb == 2 else 64)
+        self.gate_up_interleaved = batch <= 64
         # Tensor parallelism's sums travel through peer memory (the context's
         # peer set, tp.init) for the batches the streaming GEMV takes; larger
         # batches use NCCL.

@@ -149,7 +149,7 @@ def fake_engine(full, batch, rank=0, world=1, peer_exchange=True, fuse_attention
     e.full, e.s, e.m, e.rank, e.world = full, s, batch, rank, world
     e.ctx = SimpleNamespace(sms=sms)
     e.wb, e.cb = (2 if full.weights == "bf16" else 4), (2 if full.cache == "bf16" else 4)
-    e.gate_up_interleaved = batch <= (4 if e.wb == 2 else 64)
+    e.gate_up_interleaved = batch <= 64
     e.peer_exchange = world > 1 and batch <= 4 and peer_exchange
     e.vocab_local = full.vocab // world
     e.plans = {
