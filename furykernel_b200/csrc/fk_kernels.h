@@ -178,9 +178,9 @@ cudaError_t fk_launch_attend_prompt_paged(const FkAttend& a, const FkPaged& pg, 
 // Routed experts (k_moe.cu).
 cudaError_t fk_launch_route_topk(const float* x, uint32_t m, uint32_t n, uint32_t k, uint32_t ldx,
                                  const float* scale, uint32_t* ids, float* ws, bool pdl, cudaStream_t s);
-cudaError_t fk_launch_gemv_routed(const float* table, uint32_t entries, uint32_t n, uint32_t kk, const uint32_t* ids,
-                                  uint32_t m, uint32_t k, const float* x, uint32_t ldx, bool per_rank, uint32_t split,
-                                  float* y, uint32_t ldy, bool pdl, cudaStream_t s);
+cudaError_t fk_launch_gemv_routed(const void* table, bool bf16, uint32_t entries, uint32_t n, uint32_t kk,
+                                  const uint32_t* ids, uint32_t m, uint32_t k, const float* x, uint32_t ldx,
+                                  bool per_rank, uint32_t split, float* y, uint32_t ldy, bool pdl, cudaStream_t s);
 cudaError_t fk_launch_gated_gelu(const float* x, uint64_t segments, uint32_t f, float* y, bool pdl, cudaStream_t s);
 cudaError_t fk_launch_combine_ranks_add(const float* r, const float* ws, const float* segs, uint32_t m, uint32_t k,
                                         uint32_t d, float* y, bool pdl, cudaStream_t s);

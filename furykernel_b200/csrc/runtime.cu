@@ -837,11 +837,17 @@ int l_route_topk_scaled(fkc_ctx* c, const Params& p, void* const* bufs) {
                   "route_topk_scaled");
 }
 // gemv_routed: table ids x y | entries n kk m k split ldx ldy per_rank
-int l_gemv_routed(fkc_ctx* c, const Params& p, void* const* bufs) {
-  if (p.u(8) > 1) return fail(FKC_ERR_ARGUMENT, "gemv_routed: per_rank is %u, not 0 or 1.", p.u(8));
-  return launched(fk_launch_gemv_routed(CF(0), p.u(0), p.u(1), p.u(2), CU(1), p.u(3), p.u(4), CF(2), p.u(6),
+int gemv_routed(fkc_ctx* c, const Params& p, void* const* bufs, bool bf16, const char* name) {
+  if (p.u(8) > 1) return fail(FKC_ERR_ARGUMENT, "%s: per_rank is %u, not 0 or 1.", name, p.u(8));
+  return launched(fk_launch_gemv_routed(bufs[0], bf16, p.u(0), p.u(1), p.u(2), CU(1), p.u(3), p.u(4), CF(2), p.u(6),
                                         p.u(8) != 0, p.u(5), F(3), p.u(7), c->pdl, c->stream),
-                  "gemv_routed");
+                  name);
+}
+int l_gemv_routed(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return gemv_routed(c, p, bufs, false, "gemv_routed");
+}
+int l_gemv_routed_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return gemv_routed(c, p, bufs, true, "gemv_routed_wbf16");
 }
 // gated_gelu: x y | segments f
 int l_gated_gelu(fkc_ctx* c, const Params& p, void* const* bufs) {
@@ -1234,6 +1240,7 @@ std::vector<KernelSpec> make_table() {
       {"kv_store_paged", "kv_store_paged_kvbf16", {"k_cache", "v_cache"}, l_kv_store_paged_kv16},
       {"attend_split_paged", "attend_split_paged_kvbf16", {"k_cache", "v_cache"}, l_attend_paged_kv16},
       {"attend_prompt_paged", "attend_prompt_paged_kvbf16", {"k_cache", "v_cache"}, l_attend_prompt_paged_kv16},
+      {"gemv_routed", "gemv_routed_wbf16", {"table"}, l_gemv_routed_w16},
   };
   for (const Variant& v : variants) {
     KernelSpec k;

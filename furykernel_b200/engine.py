@@ -301,8 +301,7 @@ def lower_steps(p, step, b: Binding, tables: dict, attn: dict) -> list:
                  [("Anchor", "LinearRouted"), ("Recompute", "GatedGelu")]):
         lr = node("LinearRouted")
         t = p.source(lr.op.sources[0])
-        if t.kind.type != "f32":
-            raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: no routed kernel reads {t.kind.type} tables.")
+        tsuf = _weight_suffix(step, t.kind.type)
         n, kk = t.kind.dims
         ids_v, x_id = lr.op.values
         ids, y = stored(ids_v), stored(lr.outputs[0])
@@ -322,7 +321,7 @@ def lower_steps(p, step, b: Binding, tables: dict, attn: dict) -> list:
             if gu.ld != gu.width or x.ld != x.width:
                 raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: a gate of rows that are not whole.")
             out.append(Launch("gated_gelu", {"segments": b.m * k, "f": kk}, [gu.ptr, x.ptr]))
-        out.append(Launch("gemv_routed", {"entries": t.kind.entries, "n": n, "kk": kk, "m": b.m, "k": k,
+        out.append(Launch("gemv_routed" + tsuf, {"entries": t.kind.entries, "n": n, "kk": kk, "m": b.m, "k": k,
                                           "split": attn.get("split", 1), "ldx": x.ld, "ldy": y.ld,
                                           "per_rank": int(x.width != kk)},
                           [b.weights[t.name], ids.ptr, x.ptr, y.ptr]))
@@ -383,9 +382,9 @@ class Llama:
         self.cb = {"f32": 4, "bf16": 2}.get(s.cache)
         if self.wb is None or self.cb is None:
             raise N.Refused(N.FKC_ERR_ARGUMENT, f"no kernels for {s.weights} weights and {s.cache} caches.")
-        if s.experts and (world > 1 or self.wb != 4 or batch * s.top_k > 64 or s.experts > 1024):
-            raise N.Refused(N.FKC_ERR_ARGUMENT, "routed experts: one GPU, f32 weights, at most 64 (row, expert) "
-                                                "pairs a step and 1024 experts.")
+        if s.experts and (world > 1 or batch * s.top_k > 64 or s.experts > 1024):
+            raise N.Refused(N.FKC_ERR_ARGUMENT, "routed experts: one GPU, at most 64 (row, expert) pairs a step "
+                                                "and 1024 experts.")
         if self.wb == 2 and any(n % 8 for n in (s.d_model, s.q_width, s.kv_width, s.ffn)):
             raise N.Refused(N.FKC_ERR_ARGUMENT, "bf16 weights: d_model, the q and kv widths and ffn must be multiples "
                             "of 8, so that every weight starts on a 16-byte boundary.")

@@ -381,7 +381,8 @@ std::vector<Launch> lower_steps(const Program& p, const Step& step, const Bindin
   if (routed_route || routed_gate) {
     const Node& lr = node("LinearRouted");
     const Source& t = p.sources[lr.op.sources[0]];
-    if (t.kind.type != "f32") throw Refusal(step.name + ": no routed kernel reads " + t.kind.type + " tables.");
+    const std::string tsuf = t.kind.type == "bf16" ? kW16 : t.kind.type == "f32" ? "" : "?";
+    if (tsuf == "?") throw Refusal(step.name + ": no kernel reads " + t.kind.type + " weights.");
     const uint64_t n = t.kind.dims[0], kk = t.kind.dims[1];
     const View ids = stored(lr.op.values[0]), y = stored(lr.outputs[0]);
     const uint64_t k = ids.width;
@@ -402,7 +403,7 @@ std::vector<Launch> lower_steps(const Program& p, const Step& step, const Bindin
       if (gu.ld != gu.width || x.ld != x.width) throw Refusal(step.name + ": a gate of rows that are not whole.");
       out.push_back(make("gated_gelu", {{"segments", m * (double)k}, {"f", (double)kk}}, {gu.ptr(), x.ptr()}));
     }
-    out.push_back(make("gemv_routed",
+    out.push_back(make("gemv_routed" + tsuf,
                        {{"entries", (double)t.kind.entries},
                         {"n", (double)n},
                         {"kk", (double)kk},

@@ -222,6 +222,7 @@ _VARIANTS = [
     ("gather", "gather_wbf16", {"table"}),
     ("rmsnorm_rows", "rmsnorm_rows_wbf16", {"gamma"}),
     ("split_tf32", "split_tf32_wbf16", {"x"}),
+    ("gemv_routed", "gemv_routed_wbf16", {"table"}),
     *[(base, base + "_kvbf16", {"k_cache", "v_cache"})
       for base in ("kv_store_ring", "attend_split", "attend_decode", "attend_prompt", "kv_store_paged",
                    "attend_split_paged", "attend_prompt_paged")],

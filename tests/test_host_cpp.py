@@ -224,6 +224,8 @@ CASES = (
     + [(dataclasses.replace(small(b), experts=8, top_k=2), b, 0, 1, True, None) for b in (1, 3, 9, 32)]
     + [(dataclasses.replace(small(b), experts=4, top_k=1, blocks=32, block_size=16), b, 0, 1, True, None)
        for b in (1, 5)]
+    + [(dataclasses.replace(small(b), experts=8, top_k=2, weights="bf16", cache="bf16"), b, 0, 1, True, None)
+       for b in (1, 12)]
 )
 
 

@@ -70,8 +70,15 @@ def test_gemv_routed_shared_and_per_rank(ctx, entries, n, kk, m, k, split):
         ctx.launch("gemv_routed", {"entries": entries, "n": n, "kk": kk, "m": m, "k": k, "split": split, "ldx": xw,
                                    "ldy": k * n, "per_rank": per_rank}, [td, idd, xd, yd])
         assert same_bits(yd.download(), O.gemv_routed(table, ids, x, split, THREADS))
-        xd.free()
-        yd.free()
+        # The bf16 table form: the f32 arithmetic over the widened entries.
+        bits = O.narrow_bf16(table).reshape(table.shape)
+        bd = ctx.to_device(bits)
+        ctx.launch("gemv_routed_wbf16", {"entries": entries, "n": n, "kk": kk, "m": m, "k": k, "split": split,
+                                         "ldx": xw, "ldy": k * n, "per_rank": per_rank}, [bd, idd, xd, yd])
+        widened = O.widen_bf16(bits).reshape(table.shape)
+        assert same_bits(yd.download(), O.gemv_routed(widened, ids, x, split, THREADS))
+        for b in (xd, yd, bd):
+            b.free()
     td.free()
     idd.free()
 
@@ -92,8 +99,9 @@ def test_gated_gelu_and_combine(ctx):
         b.free()
 
 
-@pytest.mark.parametrize("batch,experts,top_k", [(1, 8, 2), (3, 8, 2), (9, 16, 4)])
-def test_moe_model_decode_step(ctx, batch, experts, top_k):
+@pytest.mark.parametrize("batch,experts,top_k,weights", [(1, 8, 2, "f32"), (3, 8, 2, "f32"), (9, 16, 4, "f32"),
+                                                         (2, 8, 2, "bf16"), (12, 8, 2, "bf16")])
+def test_moe_model_decode_step(ctx, batch, experts, top_k, weights):
     """A decode step of a model whose FFN is routed experts, captured as a
     graph, against the oracle's decode: the same ids, logits and residual
     rows, bit for bit."""
@@ -101,7 +109,7 @@ def test_moe_model_decode_step(ctx, batch, experts, top_k):
     from furykernel_b200.program.llama import LlamaShape
 
     s = LlamaShape(d_model=512, heads=4, kv_heads=4, head_dim=128, ffn=256, vocab=3000, layers=2, slots=batch,
-                   length=96, positions=96, experts=experts, top_k=top_k)
+                   length=96, positions=96, experts=experts, top_k=top_k, weights=weights)
     eng = Llama(ctx, s, batch, seed=500 + batch, chunk=32, prefill_kv=1.0)
     tokens = O.ints(29 + batch, batch, s.vocab)
     pos = ((np.arange(batch) * 37 + 5) % 96).astype(np.uint32)
