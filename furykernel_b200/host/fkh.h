@@ -233,6 +233,9 @@ struct PlanOptions {
 
 Plan plan(const PlanOptions& o, const Program& p);
 std::string render_plan(const Plan& pl);
+// A plan step's name: s, one or more digits, _, something
+// (src/FuryKernel/Program/Plan.hs:162-165).
+bool is_step_name(const std::string& t);
 
 // ---------------------------------------------------------------------------
 // Lowering: a step as one launch of the target's kernel table.

@@ -346,8 +346,9 @@ int fkh_split_join(const char* name, const char* right_prefix, char* buf, size_t
   return guarded(err, err_cap, [&] {
     if (!name || !right_prefix) throw fkh::Refusal("no name.");
     const std::string pre = right_prefix;
-    // Valid: the prefix then one or more digits.
+    // Valid: the prefix then one or more digits; with no prefix, a step's name.
     auto valid = [&](const std::string& r) {
+      if (pre.empty()) return fkh::is_step_name(r);
       if (r.compare(0, pre.size(), pre) != 0 || r.size() == pre.size()) return false;
       for (size_t i = pre.size(); i < r.size(); ++i)
         if (r[i] < '0' || r[i] > '9') return false;

@@ -615,6 +615,13 @@ class Planner {
 
 Plan plan(const PlanOptions& o, const Program& p) { return Planner(o, p).run(); }
 
+bool is_step_name(const std::string& t) {
+  if (t.empty() || t[0] != 's') return false;
+  size_t i = 1;
+  while (i < t.size() && t[i] >= '0' && t[i] <= '9') ++i;
+  return i > 1 && i + 1 < t.size() && t[i] == '_';
+}
+
 std::string render_plan(const Plan& pl) {
   const Program& p = pl.program;
   auto stored = [&](const Stored& st) -> std::string {

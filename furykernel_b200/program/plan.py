@@ -583,7 +583,7 @@ def render_plan(pl: Plan) -> str:
 
 
 def is_step_name(t: str) -> bool:
-    """Plan.hs:156-162."""
+    """src/FuryKernel/Program/Plan.hs:162-165."""
     if not t.startswith("s"):
         return False
     rest = t[1:]

@@ -165,7 +165,9 @@ FKH_API int fkh_space_parse_key(const char *space_json, const char *key, char *b
                                 char *err, size_t err_cap);
 FKH_API int fkh_space_names(const char *space_json, char *buf, size_t cap, size_t *len, char *err, size_t err_cap);
 /* splitJoin (Variant.hs): a name split at the first _x_ whose right side is
- * right_prefix and digits, as "left\nright"; empty where none is. */
+ * right_prefix and digits -- or, where right_prefix is "", a plan step's name
+ * (isStepName, Program/Plan.hs:162-165) -- as "left\nright"; empty where
+ * none is. */
 FKH_API int fkh_split_join(const char *name, const char *right_prefix, char *buf, size_t cap, size_t *len, char *err,
                            size_t err_cap);
 /* This target's GEMV family (classes n_k_m, m the batch; one axis, the

@@ -272,3 +272,117 @@ def test_render_program_golden():
 def test_step_names():
     assert PL.is_step_name("s0_x") and PL.is_step_name("s12_combine")
     assert not PL.is_step_name("s_x") and not PL.is_step_name("s0_") and not PL.is_step_name("x0_y")
+
+
+# ---------------------------------------------------------------------------
+# More of ProgramTest.hs's goldens (ProgramTest.hs:46-86, :113-127), for the
+# Python planner and the C++ host library's alike.
+
+
+def predicting():
+    """ProgramTest.hs:769-782: a route the program outputs beside the experts'."""
+    b = program("predicting")
+    x = b.input("x", whole_row(32))
+    router = b.weight("router_proj", [8, 32])
+    ahead = b.weight("ahead_proj", [8, 32])
+    experts = b.table("experts", 8, [16, 32])
+    logits = b.linear("router_logits", router, 0, x)
+    ahead_logits = b.linear("ahead_logits", ahead, 0, x)
+    ids, ws = b.route("route", 2, None, logits)
+    ahead_ids, _ = b.route("ahead", 2, None, ahead_logits)
+    y = b.linear_routed("experts_out", experts, ids, x)
+    s = b.combine_ranks("experts_sum", ws, y)
+    b.output("y", s)
+    b.output("ahead", ahead_ids)
+    return b.done()
+
+
+def embed_program():
+    """ProgramTest.hs:785-790: tokens to the residual stream, scaled."""
+    b = program("embed")
+    tokens = b.row_ints("tokens", 1, 64)
+    embed = b.weight("embed", [64, 32])
+    x = b.gather("x", embed, tokens, 5.65625)
+    b.output("x", x)
+    return b.done()
+
+
+def names_both(prog, opts):
+    from furykernel_b200 import _host as H
+    from furykernel_b200.program.graph import render_program
+
+    py = [s.name for s in PL.plan(opts, prog).steps]
+    text = H.plan_text(render_program(prog), opts.horizontal, opts.gated, opts.store_gelus, opts.sequence_rows)
+    cc = [ln.split()[1] for ln in text.splitlines() if ln.startswith("  step ")]
+    assert py == cc
+    return py
+
+
+def test_keys_as_values_plan_the_same_without_the_value_projection():
+    assert names_both(layer(True), PL.DEFAULT) == ["s0_gemv", "s1_store", "s2_attend", "s3_combine", "s4_gemv",
+                                                   "s5_gemv", "s6_gemv", "s7_gemv", "s8_x2"]
+
+
+def test_stored_gelus_and_gated_routes():
+    assert names_both(layer(False), PL.PlanOptions(store_gelus=True)) == [
+        "s0_gemv", "s1_store", "s2_attend", "s3_combine", "s4_gemv", "s5_gemv", "s6_mlp_act", "s7_gemv",
+        "s8_experts_act", "s9_gemv", "s10_x2"]
+    assert names_both(layer(False), PL.PlanOptions(gated=True, store_gelus=True)) == [
+        "s0_gemv", "s1_store", "s2_attend", "s3_combine", "s4_gemv", "s5_gemv", "s6_route_ids", "s7_gemv",
+        "s8_gemv", "s9_experts_act", "s10_gemv", "s11_x2"]
+    assert names_both(layer(False), PL.PlanOptions(gated=True)) == [
+        "s0_gemv", "s1_store", "s2_attend", "s3_combine", "s4_gemv", "s5_gemv", "s6_route_ids", "s7_gemv",
+        "s8_gemv", "s9_gemv", "s10_x2"]
+
+
+def test_gated_a_route_the_program_outputs_is_stored_beside_the_experts_route():
+    from furykernel_b200 import _host as H
+    from furykernel_b200.program.graph import render_program
+
+    want = [
+        "plan predicting",
+        "  step s0_gemv",
+        "    anchor router_logits",
+        "    anchor ahead_logits",
+        "    reads x f32",
+        "    stores router_logits f32",
+        "    stores ahead_logits f32",
+        "  step s1_route_ids",
+        "    recompute route_ids",
+        "    recompute ahead_ids",
+        "    reads router_logits f32",
+        "    reads ahead_logits f32",
+        "    stores route_ids u32",
+        "    stores route_weights f32",
+        "    stores ahead_ids u32",
+        "  step s2_gemv",
+        "    anchor experts_out",
+        "    reads x f32",
+        "    reads route_ids u32",
+        "    stores experts_out f32",
+        "  step s3_experts_sum",
+        "    recompute experts_sum",
+        "    reads route_weights f32",
+        "    reads experts_out f32",
+        "    stores experts_sum f32",
+    ]
+    opts = PL.PlanOptions(gated=True)
+    assert PL.render_plan(PL.plan(opts, predicting())).splitlines() == want
+    assert H.plan_text(render_program(predicting()), True, True, False, 1).splitlines() == want
+
+
+def test_the_embedding_one_light_step():
+    from furykernel_b200 import _host as H
+    from furykernel_b200.program.graph import render_program
+
+    want = ["plan embed", "  step s0_x", "    recompute x", "    stores x f32"]
+    assert PL.render_plan(PL.plan(PL.DEFAULT, embed_program())).splitlines() == want
+    assert H.plan_text(render_program(embed_program())).splitlines() == want
+    # A step's kernel name splits back at the first _x_ whose right side is
+    # a step's name (ProgramTest.hs:103-109); "" asks for that rule.
+    left, _ = H.split_join("embed_x_s0_x_x_m1", "m")
+    assert H.split_join(left, "") == ("embed", "s0_x")
+    assert H.split_join("embed_x_s0_x", "") == ("embed", "s0_x")
+    assert H.split_join("embed_x_x_s1_store", "") == ("embed_x", "s1_store")
+    assert [PL.is_step_name(t) for t in ["s0_x", "s12_attend", "s_x", "s0", "s0_", "x0_s"]] == \
+        [True, True, False, False, False, False]
