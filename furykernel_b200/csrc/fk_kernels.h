@@ -11,6 +11,9 @@
 
 enum { FK_PRO_NONE = 0, FK_PRO_RMSNORM = 1, FK_PRO_SILU = 2, FK_PRO_REDUCE_RMSNORM = 3 };
 
+// The element type of a model's weights or KV caches (fk_elem16.cuh).
+enum FkElem { FK_F32 = 0, FK_BF16 = 1, FK_F16 = 2 };
+
 // Tensor-parallel exchange over NVLink peer memory. Every rank owns one
 // region, mapped into every other rank's process; by byte offset:
 //   0    u32 flags[FK_XBUFS][FK_MAX_PEERS]  buffers 0, 1: the rows rank q has written here, all uses;
@@ -149,36 +152,39 @@ cudaError_t fk_launch_gemm_tf32x3(const float* a_hi, const float* a_lo, const fl
                                   cudaStream_t s);
 cudaError_t fk_launch_fill_normal(float* out, uint64_t n, uint64_t seed, double mu, double sigma, cudaStream_t s);
 cudaError_t fk_launch_fill_uniform(float* out, uint64_t n, uint64_t seed, double a, double b, cudaStream_t s);
-// bf16 weights (k_w16.cu): the f32 kernels' arithmetic over widened weights.
-cudaError_t fk_launch_gemv_w16(const FkGemv& g, const uint16_t* w, const uint16_t* gamma, int sms, cudaStream_t s);
+// 16-bit weights, bf16 or f16 (k_w16.cu): the f32 kernels' arithmetic over
+// widened weights.
+cudaError_t fk_launch_gemv_w16(const FkGemv& g, FkElem e, const uint16_t* w, const uint16_t* gamma, int sms,
+                               cudaStream_t s);
 bool fk_gemv_w16_batches(const FkGemv& g, const uint16_t* w);
-cudaError_t fk_launch_gemv_batch_w16(const FkGemv& g, const uint16_t* w, const uint16_t* gamma, int sms,
+cudaError_t fk_launch_gemv_batch_w16(const FkGemv& g, FkElem e, const uint16_t* w, const uint16_t* gamma, int sms,
                                      cudaStream_t s);
-cudaError_t fk_launch_gather_w16(const uint16_t* table, uint32_t width, const uint32_t* tokens, uint32_t m,
+cudaError_t fk_launch_gather_w16(FkElem e, const uint16_t* table, uint32_t width, const uint32_t* tokens, uint32_t m,
                                  float factor, float* y, bool pdl, cudaStream_t s);
-cudaError_t fk_launch_rmsnorm_rows_w16(const float* x, const uint16_t* gamma, float* y, uint32_t rows, uint32_t h,
-                                       float eps, float factor, cudaStream_t s);
-cudaError_t fk_launch_split_tf32_w16(const uint16_t* x, float* hi, float* lo, uint64_t n, cudaStream_t s);
-cudaError_t fk_launch_fill_normal_w16(uint16_t* out, uint64_t n, uint64_t seed, double mu, double sigma,
+cudaError_t fk_launch_rmsnorm_rows_w16(FkElem e, const float* x, const uint16_t* gamma, float* y, uint32_t rows,
+                                       uint32_t h, float eps, float factor, cudaStream_t s);
+cudaError_t fk_launch_split_tf32_w16(FkElem e, const uint16_t* x, float* hi, float* lo, uint64_t n, cudaStream_t s);
+cudaError_t fk_launch_fill_normal_w16(FkElem e, uint16_t* out, uint64_t n, uint64_t seed, double mu, double sigma,
                                       cudaStream_t s);
-// bf16 KV caches (k_attend_kv16.cu): stores rounded to bf16, reads widened.
-cudaError_t fk_launch_kv_store16(const FkKvStore& a, uint16_t* kc, uint16_t* vc, cudaStream_t s);
-cudaError_t fk_launch_attend16(const FkAttend& a, const uint16_t* kc, const uint16_t* vc, cudaStream_t s);
-cudaError_t fk_launch_attend_decode16(const FkAttend& a, uint32_t k_off, uint32_t v_off, uint16_t* kc, uint16_t* vc,
-                                      cudaStream_t s);
-cudaError_t fk_launch_attend_prompt16(const FkAttend& a, const uint16_t* kc, const uint16_t* vc, float* out,
+// 16-bit KV caches, bf16 or f16 (k_attend_kv16.cu): stores rounded to the
+// cache's type, reads widened.
+cudaError_t fk_launch_kv_store16(const FkKvStore& a, FkElem e, uint16_t* kc, uint16_t* vc, cudaStream_t s);
+cudaError_t fk_launch_attend16(const FkAttend& a, FkElem e, const uint16_t* kc, const uint16_t* vc, cudaStream_t s);
+cudaError_t fk_launch_attend_decode16(const FkAttend& a, FkElem e, uint32_t k_off, uint32_t v_off, uint16_t* kc,
+                                      uint16_t* vc, cudaStream_t s);
+cudaError_t fk_launch_attend_prompt16(const FkAttend& a, FkElem e, const uint16_t* kc, const uint16_t* vc, float* out,
                                       uint32_t ldo, uint32_t max_pos, cudaStream_t s);
-// Paged KV caches (k_attend_paged.cu), f32 or bf16 elements.
-cudaError_t fk_launch_kv_store_paged(const FkKvStore& a, const FkPaged& pg, void* kc, void* vc, bool bf16,
+// Paged KV caches (k_attend_paged.cu), f32, bf16 or f16 elements.
+cudaError_t fk_launch_kv_store_paged(const FkKvStore& a, const FkPaged& pg, void* kc, void* vc, FkElem e,
                                      cudaStream_t s);
-cudaError_t fk_launch_attend_paged(const FkAttend& a, const FkPaged& pg, const void* kc, const void* vc, bool bf16,
+cudaError_t fk_launch_attend_paged(const FkAttend& a, const FkPaged& pg, const void* kc, const void* vc, FkElem e,
                                    cudaStream_t s);
 cudaError_t fk_launch_attend_prompt_paged(const FkAttend& a, const FkPaged& pg, const void* kc, const void* vc,
-                                          bool bf16, float* out, uint32_t ldo, uint32_t max_pos, cudaStream_t s);
-// Routed experts (k_moe.cu).
+                                          FkElem e, float* out, uint32_t ldo, uint32_t max_pos, cudaStream_t s);
+// Routed experts (k_moe.cu); the experts' table f32, bf16 or f16.
 cudaError_t fk_launch_route_topk(const float* x, uint32_t m, uint32_t n, uint32_t k, uint32_t ldx,
                                  const float* scale, uint32_t* ids, float* ws, bool pdl, cudaStream_t s);
-cudaError_t fk_launch_gemv_routed(const void* table, bool bf16, uint32_t entries, uint32_t n, uint32_t kk,
+cudaError_t fk_launch_gemv_routed(const void* table, FkElem e, uint32_t entries, uint32_t n, uint32_t kk,
                                   const uint32_t* ids, uint32_t m, uint32_t k, const float* x, uint32_t ldx,
                                   bool per_rank, uint32_t split, float* y, uint32_t ldy, bool pdl, cudaStream_t s);
 cudaError_t fk_launch_gated_gelu(const float* x, uint64_t segments, uint32_t f, float* y, bool pdl, cudaStream_t s);

@@ -1,10 +1,11 @@
-// Decode attention over bf16 Ring KV caches, the element type the
+// Decode attention over 16-bit Ring KV caches: bf16, the element type the
 // reference's program builder gives a cache (`cache = cacheOf CacheBF16`,
-// src/FuryKernel/Program/Build.hs:188-194; CacheElem, Graph.hs:165-180):
-// "a KV cache holds each stored element rounded to its element type"
-// (src/FuryKernel/Program/Eval.hs:9). So the KV store rounds each rotated
-// key and each value to bf16 (narrowBF16: nearest, ties to even,
-// src/FuryKernel/Numerics.hs:41-48), and the attention reads them widened,
+// src/FuryKernel/Program/Build.hs:188-194), or f16 (CacheF16; CacheElem,
+// Graph.hs:165-180): "a KV cache holds each stored element rounded to its
+// element type" (src/FuryKernel/Program/Eval.hs:9). So the KV store rounds
+// each rotated key and each value to the cache's type (narrowBF16 or
+// narrowF16: nearest, ties to even, src/FuryKernel/Numerics.hs:41-48 and
+// :100-130; the type a tag, fk_elem16.cuh), and the attention reads them widened,
 // exactly; everything else -- RoPE, the scores' chains and lane sums, the
 // weights exp(s - max) in binary64 rounded once, the warps' sums in warp
 // order, the partials -- is the f32 kernels' arithmetic in the f32 kernels'
@@ -15,6 +16,7 @@
 // rounded as the store rounds them, which is what the two-kernel form reads
 // back from the cache: the same bits either way.
 #include "fk_common.cuh"
+#include "fk_elem16.cuh"
 #include "fk_kernels.h"
 
 namespace fk {
@@ -25,22 +27,11 @@ constexpr int kHeadDim = 128;  // one pack of 4 a lane
 constexpr int kMaxChunk = 256;
 constexpr uint32_t kMaxAttendRows = 16384;
 
-__device__ __forceinline__ float widen(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
-
-__device__ __forceinline__ float4 widen4(uint2 r) {
-  return make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xFFFF0000u), __uint_as_float(r.y << 16),
-                     __uint_as_float(r.y & 0xFFFF0000u));
-}
-
-// narrowBF16 (src/FuryKernel/Numerics.hs:41-48).
-__device__ __forceinline__ uint16_t narrow(float v) {
-  const uint32_t w = __float_as_uint(v);
-  if ((w & 0x7F800000u) == 0x7F800000u && (w & 0x007FFFFFu)) return (uint16_t)((w >> 16) | 0x0040u);
-  return (uint16_t)((w + 0x7FFFu + ((w >> 16) & 1u)) >> 16);
-}
-
 // A value as the cache holds it.
-__device__ __forceinline__ float rounded(float v) { return widen(narrow(v)); }
+template <class E>
+__device__ __forceinline__ float rounded(float v) {
+  return E::widen(E::narrow(v));
+}
 
 // RoPE of pair (i, i + half) of one head (halves pairing, Eval.hs:634-645),
 // as k_attend.cu's rope_pair computes it; pairs past `rotated` stay.
@@ -65,6 +56,7 @@ struct Store16 {
 };
 
 // The KV store step: grid (kv_heads, m), d / 2 threads.
+template <class E>
 __global__ void kv_store16_kernel(Store16 s) {
   const FkKvStore& a = s.a;
   grid_wait();
@@ -76,10 +68,10 @@ __global__ void kv_store16_kernel(Store16 s) {
   const float* vrow = a.qkv + (size_t)r * a.ldq + a.v_off + (size_t)h * a.d;
   float lo, hi;
   rope2(krow, i, half, a.rotated, a.cos_t + (size_t)p * a.rotated, a.sin_t + (size_t)p * a.rotated, lo, hi);
-  s.kc[at + i] = narrow(lo);
-  s.kc[at + i + half] = narrow(hi);
-  s.vc[at + i] = narrow(vrow[i]);
-  s.vc[at + i + half] = narrow(vrow[i + half]);
+  s.kc[at + i] = E::narrow(lo);
+  s.kc[at + i + half] = E::narrow(hi);
+  s.vc[at + i] = E::narrow(vrow[i]);
+  s.vc[at + i + half] = E::narrow(vrow[i + half]);
 }
 
 struct Attend16 {
@@ -95,7 +87,7 @@ struct Attend16 {
 // persistent blocks of 4 warps over the step's items (row, head, split),
 // item i at block i mod G; a warp takes positions w, w + 4, ... of its
 // split, 8 at a time, their raw bits requested before q is rotated.
-template <bool FUSED>
+template <class E, bool FUSED>
 __global__ void __launch_bounds__(128, 4) attend16_kernel(Attend16 f) {
   const FkAttend& a = f.a;
   __shared__ float qrot[kHeadDim];
@@ -171,16 +163,16 @@ __global__ void __launch_bounds__(128, 4) attend16_kernel(Attend16 f) {
         const uint32_t i = threadIdx.x - kHeadDim / 2;
         float k0, k1;
         rope2(krow, i, kHeadDim / 2, a.rotated, cos_row, sin_row, k0, k1);
-        krot[i] = rounded(k0);
-        krot[i + kHeadDim / 2] = rounded(k1);
+        krot[i] = rounded<E>(k0);
+        krot[i + kHeadDim / 2] = rounded<E>(k1);
       }
-      vnew[threadIdx.x] = rounded(vrow[threadIdx.x]);
+      vnew[threadIdx.x] = rounded<E>(vrow[threadIdx.x]);
     }
     __syncthreads();
     if (FUSED && j == splits - 1 && h % group == 0) {  // the KV store step, once a (row, KV head)
       const size_t at = (base + pslot) * kHeadDim + threadIdx.x;
-      f.kc_w[at] = narrow(krot[threadIdx.x]);
-      f.vc_w[at] = narrow(vnew[threadIdx.x]);
+      f.kc_w[at] = E::narrow(krot[threadIdx.x]);
+      f.vc_w[at] = E::narrow(vnew[threadIdx.x]);
     }
     const float4 qv = reinterpret_cast<const float4*>(qrot)[lane];
 
@@ -195,7 +187,7 @@ __global__ void __launch_bounds__(128, 4) attend16_kernel(Attend16 f) {
 #pragma unroll
       for (int u = 0; u < B; ++u) {
         const uint32_t tt = t + u * kAttWarps;
-        float4 kk = widen4(kv[u]);
+        float4 kk = E::widen4(kv[u]);
         if (fresh && tt < t1 && tt % a.length == pslot) kk = reinterpret_cast<const float4*>(krot)[lane];
         const float sc = __fmul_rn(warp_sum(__fadd_rn(0.0f, pack_dot(qv, kk))), a.scale);
         if (lane == 0 && tt < t1) scores[tt - t0] = sc;
@@ -223,7 +215,7 @@ __global__ void __launch_bounds__(128, 4) attend16_kernel(Attend16 f) {
         const uint32_t tt = t + u * kAttWarps;
         const float e = __shfl_sync(0xffffffffu, e_lane, warp + u * kAttWarps);
         if (tt < t1) {
-          float4 v4 = widen4(vv[u]);
+          float4 v4 = E::widen4(vv[u]);
           if (fresh && tt % a.length == pslot) v4 = reinterpret_cast<const float4*>(vnew)[lane];
           l = __fadd_rn(l, e);
           acc.x = __fadd_rn(acc.x, __fmul_rn(e, v4.x));
@@ -254,10 +246,11 @@ __global__ void __launch_bounds__(128, 4) attend16_kernel(Attend16 f) {
 }
 
 // Attention over a prompt's rows in one slot (prefill), k_attend.cu's
-// attend_prompt_kernel over bf16 caches: a block a (32 query rows, head);
+// attend_prompt_kernel over 16-bit caches: a block a (32 query rows, head);
 // keys and values 32 at a time into shared memory, widened.
 constexpr int kPromptTile = 32;
 
+template <class E>
 __global__ void __launch_bounds__(128) attend_prompt16_kernel(Attend16 f, float* __restrict__ out, uint32_t ldo,
                                                               uint32_t max_pos) {
   const FkAttend& a = f.a;
@@ -298,7 +291,7 @@ __global__ void __launch_bounds__(128) attend_prompt16_kernel(Attend16 f, float*
   for (uint32_t t0 = 0; t0 < keys; t0 += kPromptTile) {
     for (uint32_t e = threadIdx.x; e < kPromptTile * kHeadDim; e += blockDim.x) {
       const uint32_t k = e / kHeadDim, dd = e % kHeadDim;
-      kt[dd * kPromptTile + k] = t0 + k < keys ? widen(f.kc[(base + t0 + k) * kHeadDim + dd]) : 0.0f;
+      kt[dd * kPromptTile + k] = t0 + k < keys ? E::widen(f.kc[(base + t0 + k) * kHeadDim + dd]) : 0.0f;
     }
     __syncthreads();
 #pragma unroll
@@ -332,7 +325,7 @@ __global__ void __launch_bounds__(128) attend_prompt16_kernel(Attend16 f, float*
   for (uint32_t t0 = 0; t0 < keys; t0 += kPromptTile) {
     for (uint32_t e = threadIdx.x; e < kPromptTile * kHeadDim; e += blockDim.x) {
       const uint32_t k = e / kHeadDim, dd = e % kHeadDim;
-      vt[e] = t0 + k < keys ? widen(f.vc[(base + t0 + k) * kHeadDim + dd]) : 0.0f;
+      vt[e] = t0 + k < keys ? E::widen(f.vc[(base + t0 + k) * kHeadDim + dd]) : 0.0f;
     }
     __syncthreads();
 #pragma unroll
@@ -364,7 +357,7 @@ __global__ void __launch_bounds__(128) attend_prompt16_kernel(Attend16 f, float*
   }
 }
 
-template <bool FUSED>
+template <class E, bool FUSED>
 cudaError_t launch_attend16(const Attend16& f, cudaStream_t s) {
   const FkAttend& a = f.a;
   if (a.m == 0) return cudaSuccess;
@@ -372,7 +365,7 @@ cudaError_t launch_attend16(const Attend16& f, cudaStream_t s) {
       a.m > kMaxAttendRows || (uint64_t)a.m * a.heads * a.max_splits >= (1ull << 32) || !f.kc || !f.vc)
     return cudaErrorInvalidValue;
   if (FUSED && (!f.kc_w || !f.vc_w)) return cudaErrorInvalidValue;
-  auto kern = attend16_kernel<FUSED>;
+  auto kern = attend16_kernel<E, FUSED>;
   int dev = 0, sms = 148, per_sm = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -388,29 +381,41 @@ cudaError_t launch_attend16(const Attend16& f, cudaStream_t s) {
   return fk_launch_ex(kern, dim3(blocks), dim3(128), smem, s, a.pdl, f);
 }
 
+template <class E>
+cudaError_t launch_prompt16(const Attend16& f, float* out, uint32_t ldo, uint32_t max_pos, size_t smem, cudaStream_t s) {
+  cudaError_t e = fk_allow_smem(attend_prompt16_kernel<E>, smem);
+  if (e != cudaSuccess) return e;
+  const dim3 grid((f.a.m + kPromptTile - 1) / kPromptTile, f.a.heads);
+  return fk_launch_ex(attend_prompt16_kernel<E>, grid, dim3(128), smem, s, f.a.pdl, f, out, ldo, max_pos);
+}
+
 }  // namespace kv16
 }  // namespace fk
 
-cudaError_t fk_launch_kv_store16(const FkKvStore& a, uint16_t* kc, uint16_t* vc, cudaStream_t s) {
+cudaError_t fk_launch_kv_store16(const FkKvStore& a, FkElem e, uint16_t* kc, uint16_t* vc, cudaStream_t s) {
   if (a.m == 0) return cudaSuccess;
   if (a.d % 2 != 0 || a.d > 2048 || !kc || !vc) return cudaErrorInvalidValue;
   fk::kv16::Store16 st;
   st.a = a;
   st.kc = kc;
   st.vc = vc;
-  return fk_launch_ex(fk::kv16::kv_store16_kernel, dim3(a.kv_heads, a.m), dim3(a.d / 2), 0, s, a.pdl, st);
+#define CALL(E) fk_launch_ex(fk::kv16::kv_store16_kernel<E>, dim3(a.kv_heads, a.m), dim3(a.d / 2), 0, s, a.pdl, st)
+  return FK_BY_ELEM16(e, CALL);
+#undef CALL
 }
 
-cudaError_t fk_launch_attend16(const FkAttend& a, const uint16_t* kc, const uint16_t* vc, cudaStream_t s) {
+cudaError_t fk_launch_attend16(const FkAttend& a, FkElem e, const uint16_t* kc, const uint16_t* vc, cudaStream_t s) {
   fk::kv16::Attend16 f = {};
   f.a = a;
   f.kc = kc;
   f.vc = vc;
-  return fk::kv16::launch_attend16<false>(f, s);
+#define CALL(E) fk::kv16::launch_attend16<E, false>(f, s)
+  return FK_BY_ELEM16(e, CALL);
+#undef CALL
 }
 
-cudaError_t fk_launch_attend_decode16(const FkAttend& a, uint32_t k_off, uint32_t v_off, uint16_t* kc, uint16_t* vc,
-                                      cudaStream_t s) {
+cudaError_t fk_launch_attend_decode16(const FkAttend& a, FkElem e, uint32_t k_off, uint32_t v_off, uint16_t* kc,
+                                      uint16_t* vc, cudaStream_t s) {
   fk::kv16::Attend16 f = {};
   f.a = a;
   f.kc = kc;
@@ -419,10 +424,12 @@ cudaError_t fk_launch_attend_decode16(const FkAttend& a, uint32_t k_off, uint32_
   f.v_off = v_off;
   f.kc_w = kc;
   f.vc_w = vc;
-  return fk::kv16::launch_attend16<true>(f, s);
+#define CALL(E) fk::kv16::launch_attend16<E, true>(f, s)
+  return FK_BY_ELEM16(e, CALL);
+#undef CALL
 }
 
-cudaError_t fk_launch_attend_prompt16(const FkAttend& a, const uint16_t* kc, const uint16_t* vc, float* out,
+cudaError_t fk_launch_attend_prompt16(const FkAttend& a, FkElem e, const uint16_t* kc, const uint16_t* vc, float* out,
                                       uint32_t ldo, uint32_t max_pos, cudaStream_t s) {
   if (a.m == 0) return cudaSuccess;
   if (a.d != fk::kv16::kHeadDim || a.kv_heads == 0 || a.heads % a.kv_heads != 0 || max_pos >= a.length || !kc ||
@@ -431,12 +438,11 @@ cudaError_t fk_launch_attend_prompt16(const FkAttend& a, const uint16_t* kc, con
   const size_t smem =
       (3 * (size_t)fk::kv16::kPromptTile * fk::kv16::kHeadDim + (size_t)fk::kv16::kPromptTile * (max_pos + 1)) * 4;
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  cudaError_t e = fk_allow_smem(fk::kv16::attend_prompt16_kernel, smem);
-  if (e != cudaSuccess) return e;
   fk::kv16::Attend16 f = {};
   f.a = a;
   f.kc = kc;
   f.vc = vc;
-  const dim3 grid((a.m + fk::kv16::kPromptTile - 1) / fk::kv16::kPromptTile, a.heads);
-  return fk_launch_ex(fk::kv16::attend_prompt16_kernel, grid, dim3(128), smem, s, a.pdl, f, out, ldo, max_pos);
+#define CALL(E) fk::kv16::launch_prompt16<E>(f, out, ldo, max_pos, smem, s)
+  return FK_BY_ELEM16(e, CALL);
+#undef CALL
 }

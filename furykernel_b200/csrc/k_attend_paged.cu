@@ -13,13 +13,15 @@
 // the scale; a split's weights exp(s - max) in binary64 rounded once, the
 // warps' sums in warp order; the prompt attention's two passes. Only where
 // a position's key and value live differs, so the oracle's ring attention
-// over the blocks gathered in table order gives the bits. Elements are f32
-// or bf16 (stores rounded to nearest even, reads widened: Eval.hs:9).
+// over the blocks gathered in table order gives the bits. Elements are f32,
+// bf16 or f16 (stores rounded to the cache's type, nearest even, reads
+// widened: Eval.hs:9; the type a tag, fk_elem16.cuh).
 //
 // A table entry at or past the pool's `blocks` is not read or written: its
 // keys and values read as 0 and its stores are dropped (the engine checks
 // the tables it uploads; this keeps a bad entry from reaching past the pool).
 #include "fk_common.cuh"
+#include "fk_elem16.cuh"
 #include "fk_kernels.h"
 
 namespace fk {
@@ -31,24 +33,32 @@ constexpr int kMaxChunk = 256;
 constexpr uint32_t kMaxAttendRows = 16384;
 constexpr int kPromptTile = 32;
 
-// The element forms: a pack of four elements widened to f32, an element
-// stored (bf16: rounded to nearest even, narrowBF16,
-// src/FuryKernel/Numerics.hs:41-48), a value as the cache holds it.
-__device__ __forceinline__ float4 ld_pack(const float* p) { return __ldcs(reinterpret_cast<const float4*>(p)); }
-__device__ __forceinline__ float4 ld_pack(const uint16_t* p) {
-  const uint2 r = __ldcs(reinterpret_cast<const uint2*>(p));
-  return make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xFFFF0000u), __uint_as_float(r.y << 16),
-                     __uint_as_float(r.y & 0xFFFF0000u));
+// The element forms of a cache of type E: a pack of four elements widened
+// to f32, an element widened, an element stored (16-bit types: rounded to
+// nearest even).
+template <class E>
+using St = typename E::Storage;
+template <class E>
+__device__ __forceinline__ float4 ld_pack(const St<E>* p) {
+  if constexpr (E::kElem == FK_F32)
+    return __ldcs(reinterpret_cast<const float4*>(p));
+  else
+    return E::widen4(__ldcs(reinterpret_cast<const uint2*>(p)));
 }
-__device__ __forceinline__ float ld_elem(const float* p) { return *p; }
-__device__ __forceinline__ float ld_elem(const uint16_t* p) { return __uint_as_float((uint32_t)*p << 16); }
-__device__ __forceinline__ uint16_t narrow(float v) {
-  const uint32_t w = __float_as_uint(v);
-  if ((w & 0x7F800000u) == 0x7F800000u && (w & 0x007FFFFFu)) return (uint16_t)((w >> 16) | 0x0040u);
-  return (uint16_t)((w + 0x7FFFu + ((w >> 16) & 1u)) >> 16);
+template <class E>
+__device__ __forceinline__ float ld_elem(const St<E>* p) {
+  if constexpr (E::kElem == FK_F32)
+    return *p;
+  else
+    return E::widen(*p);
 }
-__device__ __forceinline__ void st_elem(float* p, float v) { *p = v; }
-__device__ __forceinline__ void st_elem(uint16_t* p, float v) { *p = narrow(v); }
+template <class E>
+__device__ __forceinline__ void st_elem(St<E>* p, float v) {
+  if constexpr (E::kElem == FK_F32)
+    *p = v;
+  else
+    *p = E::narrow(v);
+}
 
 // RoPE of pair (i, i + half) of one head (halves pairing, Eval.hs:634-645),
 // k_attend.cu's rope_pair arithmetic.
@@ -82,16 +92,16 @@ __device__ __forceinline__ uint64_t at_of(const Pool& P, uint32_t r, uint32_t t,
   return (((uint64_t)block * kv_heads + h) * P.block_size + t % P.block_size) * d;
 }
 
-template <typename E>
+template <class E>
 struct StoreArgs {
   FkKvStore a;  // a.slot, a.kc, a.vc, a.length unused
   Pool P;
-  E* kc;
-  E* vc;
+  St<E>* kc;
+  St<E>* vc;
 };
 
 // The KV store step: grid (kv_heads, m), d / 2 threads.
-template <typename E>
+template <class E>
 __global__ void kv_store_paged_kernel(StoreArgs<E> s) {
   const FkKvStore& a = s.a;
   grid_wait();
@@ -104,24 +114,24 @@ __global__ void kv_store_paged_kernel(StoreArgs<E> s) {
   const float* vrow = a.qkv + (size_t)r * a.ldq + a.v_off + (size_t)h * a.d;
   float lo, hi;
   rope2(krow, i, half, a.rotated, a.cos_t + (size_t)p * a.rotated, a.sin_t + (size_t)p * a.rotated, lo, hi);
-  st_elem(s.kc + at + i, lo);
-  st_elem(s.kc + at + i + half, hi);
-  st_elem(s.vc + at + i, vrow[i]);
-  st_elem(s.vc + at + i + half, vrow[i + half]);
+  st_elem<E>(s.kc + at + i, lo);
+  st_elem<E>(s.kc + at + i + half, hi);
+  st_elem<E>(s.vc + at + i, vrow[i]);
+  st_elem<E>(s.vc + at + i + half, vrow[i + half]);
 }
 
-template <typename E>
+template <class E>
 struct AttendArgs {
   FkAttend a;  // a.slot, a.kc, a.vc, a.length unused
   Pool P;
-  const E* kc;
-  const E* vc;
+  const St<E>* kc;
+  const St<E>* vc;
 };
 
 // The attention anchor: persistent blocks of 4 warps over the step's items
 // (row, head, split), item i at block i mod G; warp w takes positions w,
 // w + 4, ... of its split, 8 at a time (the ring kernel's order).
-template <typename E>
+template <class E>
 __global__ void __launch_bounds__(128, 4) attend_paged_kernel(AttendArgs<E> f) {
   const FkAttend& a = f.a;
   __shared__ float qrot[kHeadDim];
@@ -168,8 +178,8 @@ __global__ void __launch_bounds__(128, 4) attend_paged_kernel(AttendArgs<E> f) {
     for (int u = 0; u < B; ++u) {
       const uint32_t tt = t0 + warp + u * kAttWarps;
       const uint64_t at = tt < t1 ? at_of(f.P, r, tt, kvh, a.kv_heads, kHeadDim) : ~0ull;
-      kv[u] = at != ~0ull ? ld_pack(f.kc + at + 4 * lane) : zero4;
-      vv[u] = at != ~0ull ? ld_pack(f.vc + at + 4 * lane) : zero4;
+      kv[u] = at != ~0ull ? ld_pack<E>(f.kc + at + 4 * lane) : zero4;
+      vv[u] = at != ~0ull ? ld_pack<E>(f.vc + at + 4 * lane) : zero4;
     }
 
     __syncthreads();  // the previous item's shared arrays are free
@@ -189,7 +199,7 @@ __global__ void __launch_bounds__(128, 4) attend_paged_kernel(AttendArgs<E> f) {
         for (int u = 0; u < B; ++u) {
           const uint32_t tt = t + u * kAttWarps;
           const uint64_t at = tt < t1 ? at_of(f.P, r, tt, kvh, a.kv_heads, kHeadDim) : ~0ull;
-          kv[u] = at != ~0ull ? ld_pack(f.kc + at + 4 * lane) : zero4;
+          kv[u] = at != ~0ull ? ld_pack<E>(f.kc + at + 4 * lane) : zero4;
         }
       }
 #pragma unroll
@@ -212,7 +222,7 @@ __global__ void __launch_bounds__(128, 4) attend_paged_kernel(AttendArgs<E> f) {
         for (int u = 0; u < B; ++u) {
           const uint32_t tt = t + u * kAttWarps;
           const uint64_t at = tt < t1 ? at_of(f.P, r, tt, kvh, a.kv_heads, kHeadDim) : ~0ull;
-          vv[u] = at != ~0ull ? ld_pack(f.vc + at + 4 * lane) : zero4;
+          vv[u] = at != ~0ull ? ld_pack<E>(f.vc + at + 4 * lane) : zero4;
         }
       }
       const uint32_t g0 = t - (uint32_t)warp - t0;
@@ -255,7 +265,7 @@ __global__ void __launch_bounds__(128, 4) attend_paged_kernel(AttendArgs<E> f) {
 // prompt kernel's two passes (k_attend.cu): a block a (32 query rows,
 // head); keys and values 32 positions at a time into shared memory, through
 // row 0's block table (the prompt's rows share their sequence's table).
-template <typename E>
+template <class E>
 __global__ void __launch_bounds__(128) attend_prompt_paged_kernel(AttendArgs<E> f, float* __restrict__ out,
                                                                   uint32_t ldo, uint32_t max_pos) {
   const FkAttend& a = f.a;
@@ -296,7 +306,7 @@ __global__ void __launch_bounds__(128) attend_prompt_paged_kernel(AttendArgs<E> 
     for (uint32_t e = threadIdx.x; e < kPromptTile * kHeadDim; e += blockDim.x) {
       const uint32_t k = e / kHeadDim, dd = e % kHeadDim;
       const uint64_t at = t0 + k < keys ? at_of(f.P, 0, t0 + k, kvh, a.kv_heads, kHeadDim) : ~0ull;
-      kt[dd * kPromptTile + k] = at != ~0ull ? ld_elem(f.kc + at + dd) : 0.0f;
+      kt[dd * kPromptTile + k] = at != ~0ull ? ld_elem<E>(f.kc + at + dd) : 0.0f;
     }
     __syncthreads();
 #pragma unroll
@@ -331,7 +341,7 @@ __global__ void __launch_bounds__(128) attend_prompt_paged_kernel(AttendArgs<E> 
     for (uint32_t e = threadIdx.x; e < kPromptTile * kHeadDim; e += blockDim.x) {
       const uint32_t k = e / kHeadDim, dd = e % kHeadDim;
       const uint64_t at = t0 + k < keys ? at_of(f.P, 0, t0 + k, kvh, a.kv_heads, kHeadDim) : ~0ull;
-      vt[e] = at != ~0ull ? ld_elem(f.vc + at + dd) : 0.0f;
+      vt[e] = at != ~0ull ? ld_elem<E>(f.vc + at + dd) : 0.0f;
     }
     __syncthreads();
 #pragma unroll
@@ -363,21 +373,21 @@ __global__ void __launch_bounds__(128) attend_prompt_paged_kernel(AttendArgs<E> 
   }
 }
 
-template <typename E>
-cudaError_t launch_store(const FkKvStore& a, const FkPaged& pg, E* kc, E* vc, cudaStream_t s) {
+template <class E>
+cudaError_t launch_store(const FkKvStore& a, const FkPaged& pg, void* kc, void* vc, cudaStream_t s) {
   if (a.m == 0) return cudaSuccess;
   if (a.d % 2 != 0 || a.d > 2048 || pg.block_size == 0 || pg.table_len == 0 || !pg.table || !kc || !vc)
     return cudaErrorInvalidValue;
   StoreArgs<E> st;
   st.a = a;
   st.P = Pool{pg.table, pg.block_size, pg.table_len, pg.blocks};
-  st.kc = kc;
-  st.vc = vc;
+  st.kc = static_cast<St<E>*>(kc);
+  st.vc = static_cast<St<E>*>(vc);
   return fk_launch_ex(kv_store_paged_kernel<E>, dim3(a.kv_heads, a.m), dim3(a.d / 2), 0, s, a.pdl, st);
 }
 
-template <typename E>
-cudaError_t launch_attend(const FkAttend& a, const FkPaged& pg, const E* kc, const E* vc, cudaStream_t s) {
+template <class E>
+cudaError_t launch_attend(const FkAttend& a, const FkPaged& pg, const void* kc, const void* vc, cudaStream_t s) {
   if (a.m == 0) return cudaSuccess;
   if (a.d != kHeadDim || a.chunk == 0 || a.chunk > kMaxChunk || a.kv_heads == 0 || a.heads % a.kv_heads != 0 ||
       a.m > kMaxAttendRows || (uint64_t)a.m * a.heads * a.max_splits >= (1ull << 32) || pg.block_size == 0 ||
@@ -386,8 +396,8 @@ cudaError_t launch_attend(const FkAttend& a, const FkPaged& pg, const E* kc, con
   AttendArgs<E> f;
   f.a = a;
   f.P = Pool{pg.table, pg.block_size, pg.table_len, pg.blocks};
-  f.kc = kc;
-  f.vc = vc;
+  f.kc = static_cast<const St<E>*>(kc);
+  f.vc = static_cast<const St<E>*>(vc);
   auto kern = attend_paged_kernel<E>;
   int dev = 0, sms = 148, per_sm = 0;
   cudaGetDevice(&dev);
@@ -404,8 +414,8 @@ cudaError_t launch_attend(const FkAttend& a, const FkPaged& pg, const E* kc, con
   return fk_launch_ex(kern, dim3(blocks), dim3(128), smem, s, a.pdl, f);
 }
 
-template <typename E>
-cudaError_t launch_prompt(const FkAttend& a, const FkPaged& pg, const E* kc, const E* vc, float* out, uint32_t ldo,
+template <class E>
+cudaError_t launch_prompt(const FkAttend& a, const FkPaged& pg, const void* kc, const void* vc, float* out, uint32_t ldo,
                           uint32_t max_pos, cudaStream_t s) {
   if (a.m == 0) return cudaSuccess;
   if (a.d != kHeadDim || a.kv_heads == 0 || a.heads % a.kv_heads != 0 || pg.block_size == 0 ||
@@ -419,8 +429,8 @@ cudaError_t launch_prompt(const FkAttend& a, const FkPaged& pg, const E* kc, con
   AttendArgs<E> f;
   f.a = a;
   f.P = Pool{pg.table, pg.block_size, pg.table_len, pg.blocks};
-  f.kc = kc;
-  f.vc = vc;
+  f.kc = static_cast<const St<E>*>(kc);
+  f.vc = static_cast<const St<E>*>(vc);
   const dim3 grid((a.m + kPromptTile - 1) / kPromptTile, a.heads);
   return fk_launch_ex(kern, grid, dim3(128), smem, s, a.pdl, f, out, ldo, max_pos);
 }
@@ -428,21 +438,30 @@ cudaError_t launch_prompt(const FkAttend& a, const FkPaged& pg, const E* kc, con
 }  // namespace paged
 }  // namespace fk
 
-cudaError_t fk_launch_kv_store_paged(const FkKvStore& a, const FkPaged& pg, void* kc, void* vc, bool bf16,
+// The launch for a cache of element type e: f32, bf16 or f16.
+#define FK_BY_ELEM(e, CALL)                          \
+  ((e) == FK_F32    ? CALL(fk::F32)                  \
+   : (e) == FK_BF16 ? CALL(fk::Bf16)                 \
+   : (e) == FK_F16  ? CALL(fk::F16)                  \
+                    : cudaErrorInvalidValue)
+
+cudaError_t fk_launch_kv_store_paged(const FkKvStore& a, const FkPaged& pg, void* kc, void* vc, FkElem e,
                                      cudaStream_t s) {
-  return bf16 ? fk::paged::launch_store<uint16_t>(a, pg, (uint16_t*)kc, (uint16_t*)vc, s)
-              : fk::paged::launch_store<float>(a, pg, (float*)kc, (float*)vc, s);
+#define CALL(E) fk::paged::launch_store<E>(a, pg, kc, vc, s)
+  return FK_BY_ELEM(e, CALL);
+#undef CALL
 }
 
-cudaError_t fk_launch_attend_paged(const FkAttend& a, const FkPaged& pg, const void* kc, const void* vc, bool bf16,
+cudaError_t fk_launch_attend_paged(const FkAttend& a, const FkPaged& pg, const void* kc, const void* vc, FkElem e,
                                    cudaStream_t s) {
-  return bf16 ? fk::paged::launch_attend<uint16_t>(a, pg, (const uint16_t*)kc, (const uint16_t*)vc, s)
-              : fk::paged::launch_attend<float>(a, pg, (const float*)kc, (const float*)vc, s);
+#define CALL(E) fk::paged::launch_attend<E>(a, pg, kc, vc, s)
+  return FK_BY_ELEM(e, CALL);
+#undef CALL
 }
 
 cudaError_t fk_launch_attend_prompt_paged(const FkAttend& a, const FkPaged& pg, const void* kc, const void* vc,
-                                          bool bf16, float* out, uint32_t ldo, uint32_t max_pos, cudaStream_t s) {
-  return bf16 ? fk::paged::launch_prompt<uint16_t>(a, pg, (const uint16_t*)kc, (const uint16_t*)vc, out, ldo,
-                                                   max_pos, s)
-              : fk::paged::launch_prompt<float>(a, pg, (const float*)kc, (const float*)vc, out, ldo, max_pos, s);
+                                          FkElem e, float* out, uint32_t ldo, uint32_t max_pos, cudaStream_t s) {
+#define CALL(E) fk::paged::launch_prompt<E>(a, pg, kc, vc, out, ldo, max_pos, s)
+  return FK_BY_ELEM(e, CALL);
+#undef CALL
 }

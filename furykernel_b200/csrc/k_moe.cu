@@ -17,6 +17,7 @@
 //   in binary32, tanh in binary64 rounded once; the gate gelu(a) b;
 // - combine: ((w_0 s_0 + w_1 s_1) + ...) in rank order, then r + that.
 #include "fk_common.cuh"
+#include "fk_elem16.cuh"
 #include "fk_kernels.h"
 
 namespace fk {
@@ -84,7 +85,7 @@ __global__ void __launch_bounds__(32) route_topk_kernel(const float* __restrict_
 }
 
 struct RoutedArgs {
-  const void* table;   // [entries, n, kk], f32 or bf16
+  const void* table;   // [entries, n, kk], f32, bf16 or f16
   const uint32_t* ids; // [m, k]
   const float* x;      // [m, ldx]: one segment of kk every rank takes, or k of them
   float* y;            // [m, ldy]: a segment of n a rank
@@ -94,25 +95,27 @@ struct RoutedArgs {
 
 constexpr int kPairsAPass = 4;
 
-// A pack of four table weights: f32, or bf16 widened exactly.
-__device__ __forceinline__ float4 ld_pack(const float* row, uint32_t j) {
-  return ld_stream(reinterpret_cast<const float4*>(row) + j);
-}
-__device__ __forceinline__ float4 ld_pack(const uint16_t* row, uint32_t j) {
-  uint2 v;
-  asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
-      : "=r"(v.x), "=r"(v.y)
-      : "l"(reinterpret_cast<const uint2*>(row) + j));
-  return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u), __uint_as_float(v.y << 16),
-                     __uint_as_float(v.y & 0xFFFF0000u));
+// A pack of four table weights: f32, or a 16-bit type widened exactly.
+template <class E>
+__device__ __forceinline__ float4 ld_pack(const typename E::Storage* row, uint32_t j) {
+  if constexpr (E::kElem == FK_F32) {
+    return ld_stream(reinterpret_cast<const float4*>(row) + j);
+  } else {
+    uint2 v;
+    asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+        : "=r"(v.x), "=r"(v.y)
+        : "l"(reinterpret_cast<const uint2*>(row) + j));
+    return E::widen4(v);
+  }
 }
 
 // The routed GEMV: a block a (expert, 8 output rows), a warp a row. The
 // block lists the (row, rank) pairs whose route chose its expert and, for
 // up to 4 pairs at a time, streams the expert's row once for them, each
 // pair's dot in the GEMV contract's order. Experts no row chose read no
-// weights. T: the table's element, f32 or bf16 (widened where read).
-template <typename T>
+// weights. E: the table's element type, f32, bf16 or f16 (widened where
+// read).
+template <class E>
 __global__ void __launch_bounds__(256) gemv_routed_kernel(RoutedArgs a) {
   __shared__ uint32_t pairs[kMaxPairs];
   __shared__ uint32_t npairs;
@@ -132,7 +135,7 @@ __global__ void __launch_bounds__(256) gemv_routed_kernel(RoutedArgs a) {
   if (P == 0 || o >= a.n) return;
   const uint32_t packs = a.kk >> 2;
   const uint32_t stride = 32u * a.split;
-  const T* wr = reinterpret_cast<const T*>(a.table) + ((size_t)e * a.n + o) * a.kk;
+  const typename E::Storage* wr = reinterpret_cast<const typename E::Storage*>(a.table) + ((size_t)e * a.n + o) * a.kk;
   for (uint32_t p0 = 0; p0 < P; p0 += kPairsAPass) {
     const uint32_t np = min((uint32_t)kPairsAPass, P - p0);
     const float4* xs[kPairsAPass];
@@ -148,7 +151,7 @@ __global__ void __launch_bounds__(256) gemv_routed_kernel(RoutedArgs a) {
 #pragma unroll
       for (int q = 0; q < kPairsAPass; ++q) acc[q] = 0.0f;
       for (uint32_t jj = sq * 32u + (uint32_t)lane; jj < packs; jj += stride) {
-        const float4 wv = ld_pack(wr, jj);
+        const float4 wv = ld_pack<E>(wr, jj);
 #pragma unroll
         for (int q = 0; q < kPairsAPass; ++q)
           if ((uint32_t)q < np) acc[q] = __fadd_rn(acc[q], pack_dot(__ldg(xs[q] + jj), wv));
@@ -224,7 +227,7 @@ cudaError_t fk_launch_route_topk(const float* x, uint32_t m, uint32_t n, uint32_
   return fk_launch_ex(fk::moe::route_topk_kernel, dim3(m), dim3(32), 0, s, pdl, x, n, k, ldx, scale, ids, ws);
 }
 
-cudaError_t fk_launch_gemv_routed(const void* table, bool bf16, uint32_t entries, uint32_t n, uint32_t kk,
+cudaError_t fk_launch_gemv_routed(const void* table, FkElem el, uint32_t entries, uint32_t n, uint32_t kk,
                                   const uint32_t* ids, uint32_t m, uint32_t k, const float* x, uint32_t ldx,
                                   bool per_rank, uint32_t split, float* y, uint32_t ldy, bool pdl, cudaStream_t s) {
   if (m == 0 || n == 0) return cudaSuccess;
@@ -245,9 +248,13 @@ cudaError_t fk_launch_gemv_routed(const void* table, bool bf16, uint32_t entries
   a.ldx = ldx;
   a.ldy = ldy;
   a.per_rank = per_rank;
-  if (bf16)
-    return fk_launch_ex(fk::moe::gemv_routed_kernel<uint16_t>, dim3(entries, (n + 7) / 8), dim3(256), 0, s, pdl, a);
-  return fk_launch_ex(fk::moe::gemv_routed_kernel<float>, dim3(entries, (n + 7) / 8), dim3(256), 0, s, pdl, a);
+  const dim3 grid(entries, (n + 7) / 8);
+  switch (el) {
+    case FK_F32: return fk_launch_ex(fk::moe::gemv_routed_kernel<fk::F32>, grid, dim3(256), 0, s, pdl, a);
+    case FK_BF16: return fk_launch_ex(fk::moe::gemv_routed_kernel<fk::Bf16>, grid, dim3(256), 0, s, pdl, a);
+    case FK_F16: return fk_launch_ex(fk::moe::gemv_routed_kernel<fk::F16>, grid, dim3(256), 0, s, pdl, a);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t fk_launch_gated_gelu(const float* x, uint64_t segments, uint32_t f, float* y, bool pdl, cudaStream_t s) {

@@ -1,16 +1,19 @@
-// A decode step whose weights are bf16, the element type the reference's
-// program builder gives a model's weights (`weight`,
-// src/FuryKernel/Program/Build.hs:171-175): activations, sums and outputs
-// stay binary32, and every weight is widened to binary32 where it is read,
-// exactly (widenBF16, src/FuryKernel/Numerics.hs:33-38). So each kernel here
+// A decode step whose weights are 16-bit: bf16, the element type the
+// reference's program builder gives a model's weights (`weight`,
+// src/FuryKernel/Program/Build.hs:171-175), or f16, the other 16-bit type a
+// weight may hold (src/FuryKernel/Program/Check.hs:105-111). Activations,
+// sums and outputs stay binary32, and every weight is widened to binary32
+// where it is read, exactly (widenBF16 and widenF16,
+// src/FuryKernel/Numerics.hs:33-38 and :51-66; fk_elem16.cuh). So each kernel here
 // keeps the arithmetic and the order of its f32 counterpart over the widened
 // weights -- the GEMV order contract at pack 4 and split s
 // (test/Test/FuryKernel/Gemv.hs:9-26), RMSNorm's 256-lane order, the
 // SiLU-gate -- and the f32 oracle over the widened weights gives its bits,
 // while the weights' HBM bytes halve.
 //
-// Widening does not quiet a signalling NaN here (the reference's widening
-// does): a NaN weight makes a NaN sum either way.
+// Widening does not quiet a NaN here (the reference's widening does): a NaN
+// weight makes a NaN sum either way. Each kernel takes the element type as
+// a tag (fk::Bf16, fk::F16).
 //
 // Kernels: the weight-streaming GEMV for batches of up to 4 rows
 // (gemv_stream_w16_kernel, persistent, x staged once a block with its
@@ -18,22 +21,17 @@
 // reduce-then-normalize prologue), the packed batched GEMV for up to 64 rows
 // at split 1 (k_w16_batch.cu), the chunked GEMV for the rest
 // (gemv_chunk_w16_kernel, 32 rows a launch), the embedding gather, RMSNorm
-// rows with a bf16 gain, the TF32 split of bf16 weights (exact: a bf16
-// value has 8 significant bits, a TF32 value 11, so the low half is 0), and
-// the seeded normal fill rounded to bf16.
+// rows with a 16-bit gain, the TF32 split of 16-bit weights (exact: a bf16
+// value has 8 significant bits, an f16 value 11 and a TF32 value 11, and
+// f16's exponents are within TF32's, so the low half is 0), and the seeded
+// normal fill rounded to the weights' type.
 #include "fk_common.cuh"
+#include "fk_elem16.cuh"
 #include "fk_kernels.h"
 #include "fk_peers.cuh"
 
 namespace fk {
 namespace w16 {
-
-// Pack j's four weights of a row (8 bytes), widened: element 0 is the low
-// half of the first word.
-__device__ __forceinline__ float4 widen4(uint2 r) {
-  return make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xFFFF0000u), __uint_as_float(r.y << 16),
-                     __uint_as_float(r.y & 0xFFFF0000u));
-}
 
 // Streaming load of a pack's raw bits: read once, no L1 allocation.
 __device__ __forceinline__ uint2 ld_stream2(const uint2* p) {
@@ -42,17 +40,10 @@ __device__ __forceinline__ uint2 ld_stream2(const uint2* p) {
   return v;
 }
 
+// Pack j of a 16-bit gain, widened.
+template <class E>
 __device__ __forceinline__ float4 gain4(const uint16_t* gamma, uint32_t j) {
-  return widen4(__ldg(reinterpret_cast<const uint2*>(gamma) + j));
-}
-
-// binary32 -> bfloat16, round to nearest, ties to even; a NaN keeps its
-// sign and top payload bits and comes out quiet (narrowBF16,
-// src/FuryKernel/Numerics.hs:41-48).
-__device__ __forceinline__ uint16_t narrow(float v) {
-  const uint32_t w = __float_as_uint(v);
-  if ((w & 0x7F800000u) == 0x7F800000u && (w & 0x007FFFFFu)) return (uint16_t)((w >> 16) | 0x0040u);
-  return (uint16_t)((w + 0x7FFFu + ((w >> 16) & 1u)) >> 16);
+  return E::widen4(__ldg(reinterpret_cast<const uint2*>(gamma) + j));
 }
 
 struct StreamArgs {
@@ -85,7 +76,7 @@ __device__ __forceinline__ float silu_of(float a, float b) {
 // One row's totals for the staged rows of x, in the contract's order: split
 // q, lane l visits packs q*32 + l, + 32 s, ...; chains from 0; lanes summed
 // pairwise; splits added in order.
-template <int M>
+template <class E, int M>
 __device__ __forceinline__ void row_totals(const uint2* __restrict__ wr, const float4* __restrict__ xs4,
                                            uint32_t packs, uint32_t m, uint32_t s, int lane, float (&total)[M]) {
   const uint32_t stride = 32u * s;
@@ -100,14 +91,14 @@ __device__ __forceinline__ void row_totals(const uint2* __restrict__ wr, const f
       for (int u = 0; u < kInFlight; ++u) raw[u] = ld_stream2(wr + j + u * stride);
 #pragma unroll
       for (int u = 0; u < kInFlight; ++u) {
-        const float4 wv = widen4(raw[u]);
+        const float4 wv = E::widen4(raw[u]);
 #pragma unroll
         for (int i = 0; i < M; ++i)
           if (i < (int)m) acc[i] = __fadd_rn(acc[i], pack_dot(xs4[(size_t)i * packs + j + u * stride], wv));
       }
     }
     for (; j < packs; j += stride) {
-      const float4 wv = widen4(ld_stream2(wr + j));
+      const float4 wv = E::widen4(ld_stream2(wr + j));
 #pragma unroll
       for (int i = 0; i < M; ++i)
         if (i < (int)m) acc[i] = __fadd_rn(acc[i], pack_dot(xs4[(size_t)i * packs + j], wv));
@@ -123,7 +114,7 @@ __device__ __forceinline__ void row_totals(const uint2* __restrict__ wr, const f
 // Persistent blocks of 16 warps; unit u (a row, or a gate/up row pair) goes
 // to block u mod G and, within it, warp (u / G) mod 16; a scattering block
 // owns the contiguous rows [s_lo, s_hi) instead.
-template <int M, int PRO, int EPI>
+template <class E, int M, int PRO, int EPI>
 __global__ void __launch_bounds__(512, 2) gemv_stream_w16_kernel(StreamArgs a) {
   extern __shared__ float4 xs4[];  // [m][k / 4]
   __shared__ float scales[M];
@@ -198,7 +189,7 @@ __global__ void __launch_bounds__(512, 2) gemv_stream_w16_kernel(StreamArgs a) {
       const float sc = scales[i];
       v = make_float4(__fmul_rn(v.x, sc), __fmul_rn(v.y, sc), __fmul_rn(v.z, sc), __fmul_rn(v.w, sc));
       if (a.gamma) {
-        const float4 g = gain4(a.gamma, j);
+        const float4 g = gain4<E>(a.gamma, j);
         v = make_float4(__fmul_rn(v.x, g.x), __fmul_rn(v.y, g.y), __fmul_rn(v.z, g.z), __fmul_rn(v.w, g.w));
       }
       if (a.factor != 1.0f)
@@ -218,8 +209,8 @@ __global__ void __launch_bounds__(512, 2) gemv_stream_w16_kernel(StreamArgs a) {
     const uint32_t u = EPI == SEPI_SCATTER ? s_lo + slot : blockIdx.x + slot * G;
     if (EPI == SEPI_SCATTER ? u >= s_hi : u >= units) break;
     float t0[M], t1[M];
-    row_totals<M>(w2 + (size_t)u * per_unit * packs, xs4, packs, a.m, a.split, lane, t0);
-    if (EPI == SEPI_SILU_PAIR) row_totals<M>(w2 + ((size_t)u * 2 + 1) * packs, xs4, packs, a.m, a.split, lane, t1);
+    row_totals<E, M>(w2 + (size_t)u * per_unit * packs, xs4, packs, a.m, a.split, lane, t0);
+    if (EPI == SEPI_SILU_PAIR) row_totals<E, M>(w2 + ((size_t)u * 2 + 1) * packs, xs4, packs, a.m, a.split, lane, t1);
     if (lane == 0) {
 #pragma unroll
       for (int i = 0; i < M; ++i) {
@@ -255,9 +246,9 @@ __global__ void __launch_bounds__(512, 2) gemv_stream_w16_kernel(StreamArgs a) {
   }
 }
 
-template <int M, int PRO, int EPI>
+template <class E, int M, int PRO, int EPI>
 static cudaError_t launch_stream(const StreamArgs& a, int sms, cudaStream_t st, bool pdl) {
-  auto kern = gemv_stream_w16_kernel<M, PRO, EPI>;
+  auto kern = gemv_stream_w16_kernel<E, M, PRO, EPI>;
   const size_t smem = (size_t)a.m * a.k * sizeof(float);
   cudaError_t e = fk_allow_smem(kern, smem);
   if (e != cudaSuccess) return e;
@@ -273,11 +264,11 @@ static cudaError_t launch_stream(const StreamArgs& a, int sms, cudaStream_t st, 
   return fk_launch_ex(kern, dim3(blocks), dim3(512), smem, st, pdl, a);
 }
 
-template <int PRO, int EPI>
+template <class E, int PRO, int EPI>
 static cudaError_t stream_m(const StreamArgs& a, int sms, cudaStream_t st, bool pdl) {
-  if (a.m <= 1) return launch_stream<1, PRO, EPI>(a, sms, st, pdl);
-  if (a.m <= 2) return launch_stream<2, PRO, EPI>(a, sms, st, pdl);
-  return launch_stream<4, PRO, EPI>(a, sms, st, pdl);
+  if (a.m <= 1) return launch_stream<E, 1, PRO, EPI>(a, sms, st, pdl);
+  if (a.m <= 2) return launch_stream<E, 2, PRO, EPI>(a, sms, st, pdl);
+  return launch_stream<E, 4, PRO, EPI>(a, sms, st, pdl);
 }
 
 // ---------------------------------------------------------------------------
@@ -322,7 +313,7 @@ __device__ float rmsnorm_scale_warp(const float* __restrict__ xr, uint32_t k, fl
   return rsqrt_rounded(__fadd_rn(__fdiv_rn(tg_sum8(slots), (float)k), eps));
 }
 
-template <int M, int PRO, bool ADD>
+template <class E, int M, int PRO, bool ADD>
 __global__ void __launch_bounds__(256) gemv_chunk_w16_kernel(ChunkArgs a) {
   extern __shared__ float4 xs4[];  // [m][kc / 4]
   __shared__ float scales[M];
@@ -370,7 +361,7 @@ __global__ void __launch_bounds__(256) gemv_chunk_w16_kernel(ChunkArgs a) {
         const float sc = scales[i];
         xv = make_float4(__fmul_rn(xv.x, sc), __fmul_rn(xv.y, sc), __fmul_rn(xv.z, sc), __fmul_rn(xv.w, sc));
         if (a.gamma) {
-          const float4 g = gain4(a.gamma, j);
+          const float4 g = gain4<E>(a.gamma, j);
           xv = make_float4(__fmul_rn(xv.x, g.x), __fmul_rn(xv.y, g.y), __fmul_rn(xv.z, g.z), __fmul_rn(xv.w, g.w));
         }
         if (a.factor != 1.0f)
@@ -392,14 +383,14 @@ __global__ void __launch_bounds__(256) gemv_chunk_w16_kernel(ChunkArgs a) {
         for (int u = 0; u < kInFlight; ++u) raw[u] = ld_stream2(wr + j + u * stride);
 #pragma unroll
         for (int u = 0; u < kInFlight; ++u) {
-          const float4 wv = widen4(raw[u]);
+          const float4 wv = E::widen4(raw[u]);
 #pragma unroll
           for (int i = 0; i < M; ++i)
             if (i < (int)a.m) acc[i] = __fadd_rn(acc[i], pack_dot(xs4[(size_t)i * kc4 + (j + u * stride - c0)], wv));
         }
       }
       for (; j < c1; j += stride) {
-        const float4 wv = widen4(ld_stream2(wr + j));
+        const float4 wv = E::widen4(ld_stream2(wr + j));
 #pragma unroll
         for (int i = 0; i < M; ++i)
           if (i < (int)a.m) acc[i] = __fadd_rn(acc[i], pack_dot(xs4[(size_t)i * kc4 + (j - c0)], wv));
@@ -425,33 +416,34 @@ __global__ void __launch_bounds__(256) gemv_chunk_w16_kernel(ChunkArgs a) {
   }
 }
 
-template <int M, int PRO, bool ADD>
+template <class E, int M, int PRO, bool ADD>
 static cudaError_t launch_chunk_m(const ChunkArgs& a, cudaStream_t st, bool pdl) {
   const uint32_t rows_per_block = 8u / a.split;
   const uint32_t blocks = (a.n + rows_per_block - 1) / rows_per_block;
   const size_t smem = (size_t)a.m * a.kc * sizeof(float);
-  auto kern = gemv_chunk_w16_kernel<M, PRO, ADD>;
+  auto kern = gemv_chunk_w16_kernel<E, M, PRO, ADD>;
   cudaError_t e = fk_allow_smem(kern, smem);
   if (e != cudaSuccess) return e;
   return fk_launch_ex(kern, dim3(blocks), dim3(256), smem, st, pdl, a);
 }
 
-template <int PRO, bool ADD>
+template <class E, int PRO, bool ADD>
 static cudaError_t launch_chunk(const ChunkArgs& a, cudaStream_t st, bool pdl) {
-  if (a.m <= 1) return launch_chunk_m<1, PRO, ADD>(a, st, pdl);
-  if (a.m <= 2) return launch_chunk_m<2, PRO, ADD>(a, st, pdl);
-  if (a.m <= 4) return launch_chunk_m<4, PRO, ADD>(a, st, pdl);
-  if (a.m <= 8) return launch_chunk_m<8, PRO, ADD>(a, st, pdl);
-  if (a.m <= 16) return launch_chunk_m<16, PRO, ADD>(a, st, pdl);
-  if (a.m <= 32) return launch_chunk_m<32, PRO, ADD>(a, st, pdl);
+  if (a.m <= 1) return launch_chunk_m<E, 1, PRO, ADD>(a, st, pdl);
+  if (a.m <= 2) return launch_chunk_m<E, 2, PRO, ADD>(a, st, pdl);
+  if (a.m <= 4) return launch_chunk_m<E, 4, PRO, ADD>(a, st, pdl);
+  if (a.m <= 8) return launch_chunk_m<E, 8, PRO, ADD>(a, st, pdl);
+  if (a.m <= 16) return launch_chunk_m<E, 16, PRO, ADD>(a, st, pdl);
+  if (a.m <= 32) return launch_chunk_m<E, 32, PRO, ADD>(a, st, pdl);
   return cudaErrorInvalidValue;
 }
 
 // ---------------------------------------------------------------------------
 // Elementwise.
 
-// The embedding gather: row tokens[r] of a bf16 table, widened, times the
+// The embedding gather: row tokens[r] of a 16-bit table, widened, times the
 // factor. Grid (width / 4 / 256, m).
+template <class E>
 __global__ void gather_w16_kernel(const uint16_t* __restrict__ table, uint32_t width,
                                   const uint32_t* __restrict__ tokens, float factor, float* __restrict__ y) {
   grid_wait();
@@ -460,15 +452,15 @@ __global__ void gather_w16_kernel(const uint16_t* __restrict__ table, uint32_t w
   const uint32_t j = blockIdx.x * 256u + threadIdx.x;
   if (4 * j >= width) return;
   const uint2* src = reinterpret_cast<const uint2*>(table + (size_t)tokens[r] * width);
-  float4 v = widen4(__ldg(src + j));
+  float4 v = E::widen4(__ldg(src + j));
   if (factor != 1.0f)
     v = make_float4(__fmul_rn(v.x, factor), __fmul_rn(v.y, factor), __fmul_rn(v.z, factor), __fmul_rn(v.w, factor));
   reinterpret_cast<float4*>(y + (size_t)r * width)[j] = v;
 }
 
-// RMSNorm rows (prefill) with a bf16 gain: the 256 spec lanes over packs
+// RMSNorm rows (prefill) with a 16-bit gain: the 256 spec lanes over packs
 // t, t + 256, ...; y = x * scale * gamma (* factor). A block a row.
-template <int PK>
+template <class E, int PK>
 __global__ void __launch_bounds__(256) rmsnorm_rows_w16_kernel(const float* __restrict__ x,
                                                                const uint16_t* __restrict__ gamma,
                                                                float* __restrict__ y, uint32_t h, float eps,
@@ -501,7 +493,7 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_w16_kernel(const float* __re
     if (j < packs) {
       float4 o = make_float4(__fmul_rn(v[i].x, scale), __fmul_rn(v[i].y, scale), __fmul_rn(v[i].z, scale),
                              __fmul_rn(v[i].w, scale));
-      const float4 g = gain4(gamma, j);
+      const float4 g = gain4<E>(gamma, j);
       o = make_float4(__fmul_rn(o.x, g.x), __fmul_rn(o.y, g.y), __fmul_rn(o.z, g.z), __fmul_rn(o.w, g.w));
       if (factor != 1.0f)
         o = make_float4(__fmul_rn(o.x, factor), __fmul_rn(o.y, factor), __fmul_rn(o.z, factor),
@@ -511,12 +503,13 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_w16_kernel(const float* __re
   }
 }
 
-// The TF32 halves of bf16 weights for the prefill GEMM: the widened value
+// The TF32 halves of 16-bit weights for the prefill GEMM: the widened value
 // is a TF32 value, so hi is it and lo is 0.
+template <class E>
 __global__ void split_tf32_w16_kernel(const uint16_t* __restrict__ x, float* __restrict__ hi, float* __restrict__ lo,
                                       uint64_t n) {
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
-    hi[i] = __uint_as_float((uint32_t)x[i] << 16);
+    hi[i] = E::widen(x[i]);
     lo[i] = 0.0f;
   }
 }
@@ -524,7 +517,7 @@ __global__ void split_tf32_w16_kernel(const uint16_t* __restrict__ x, float* __r
 // Seeded normals as the f32 fill draws them (SplitMix's finaliser of
 // seed * golden + i, i from 1, test/cpu/Cases.hs:885-892; Box-Muller on
 // consecutive words in binary64, rounded once to binary32), then rounded to
-// bf16: the f32 fill's values, narrowed.
+// the 16-bit type: the f32 fill's values, narrowed.
 __device__ __forceinline__ uint64_t splitmix(uint64_t seed, uint64_t i) {
   uint64_t z = seed * 0x9E3779B97F4A7C15ULL + i;
   z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
@@ -532,6 +525,7 @@ __device__ __forceinline__ uint64_t splitmix(uint64_t seed, uint64_t i) {
   return z ^ (z >> 31);
 }
 
+template <class E>
 __global__ void fill_normal_w16_kernel(uint16_t* __restrict__ out, uint64_t n, uint64_t seed, double mu,
                                        double sigma) {
   const uint64_t pairs = (n + 1) / 2;
@@ -542,8 +536,8 @@ __global__ void fill_normal_w16_kernel(uint16_t* __restrict__ out, uint64_t n, u
     const double u2 = (double)(w2 >> 11) * 0x1p-53;
     const double rr = sqrt(-2.0 * log(u1));
     const double t = 6.283185307179586 * u2;
-    out[2 * p] = narrow((float)(mu + sigma * (rr * cos(t))));
-    if (2 * p + 1 < n) out[2 * p + 1] = narrow((float)(mu + sigma * (rr * sin(t))));
+    out[2 * p] = E::narrow((float)(mu + sigma * (rr * cos(t))));
+    if (2 * p + 1 < n) out[2 * p + 1] = E::narrow((float)(mu + sigma * (rr * sin(t))));
   }
 }
 
@@ -552,12 +546,8 @@ static unsigned grid_for(uint64_t n) {
   return (unsigned)(b > 148ull * 64 ? 148ull * 64 : (b == 0 ? 1 : b));
 }
 
-}  // namespace w16
-}  // namespace fk
-
-cudaError_t fk_launch_gemv_w16(const FkGemv& g, const uint16_t* w, const uint16_t* gamma, int sms, cudaStream_t st) {
-  using namespace fk::w16;
-  if (g.n == 0 || g.m == 0) return cudaSuccess;
+template <class E>
+static cudaError_t gemv(const FkGemv& g, const uint16_t* w, const uint16_t* gamma, int sms, cudaStream_t st) {
   if (g.k % 4 != 0 || g.split == 0 || !w) return cudaErrorInvalidValue;
   const bool peer = g.scatter || g.prologue == FK_PRO_REDUCE_RMSNORM;
   if (fk_gemv_streams(g)) {
@@ -587,23 +577,23 @@ cudaError_t fk_launch_gemv_w16(const FkGemv& g, const uint16_t* w, const uint16_
     a.err = g.err;
     const int epi = g.scatter ? SEPI_SCATTER : g.silu_pair ? SEPI_SILU_PAIR : (g.r ? SEPI_ADD : SEPI_NONE);
     switch (g.prologue * 4 + epi) {
-      case FK_PRO_NONE * 4 + SEPI_NONE: return stream_m<SPRO_NONE, SEPI_NONE>(a, sms, st, g.pdl);
-      case FK_PRO_NONE * 4 + SEPI_ADD: return stream_m<SPRO_NONE, SEPI_ADD>(a, sms, st, g.pdl);
-      case FK_PRO_NONE * 4 + SEPI_SCATTER: return stream_m<SPRO_NONE, SEPI_SCATTER>(a, sms, st, g.pdl);
-      case FK_PRO_RMSNORM * 4 + SEPI_NONE: return stream_m<SPRO_RMSNORM, SEPI_NONE>(a, sms, st, g.pdl);
-      case FK_PRO_RMSNORM * 4 + SEPI_SILU_PAIR: return stream_m<SPRO_RMSNORM, SEPI_SILU_PAIR>(a, sms, st, g.pdl);
-      case FK_PRO_SILU * 4 + SEPI_NONE: return stream_m<SPRO_SILU, SEPI_NONE>(a, sms, st, g.pdl);
-      case FK_PRO_SILU * 4 + SEPI_ADD: return stream_m<SPRO_SILU, SEPI_ADD>(a, sms, st, g.pdl);
+      case FK_PRO_NONE * 4 + SEPI_NONE: return stream_m<E, SPRO_NONE, SEPI_NONE>(a, sms, st, g.pdl);
+      case FK_PRO_NONE * 4 + SEPI_ADD: return stream_m<E, SPRO_NONE, SEPI_ADD>(a, sms, st, g.pdl);
+      case FK_PRO_NONE * 4 + SEPI_SCATTER: return stream_m<E, SPRO_NONE, SEPI_SCATTER>(a, sms, st, g.pdl);
+      case FK_PRO_RMSNORM * 4 + SEPI_NONE: return stream_m<E, SPRO_RMSNORM, SEPI_NONE>(a, sms, st, g.pdl);
+      case FK_PRO_RMSNORM * 4 + SEPI_SILU_PAIR: return stream_m<E, SPRO_RMSNORM, SEPI_SILU_PAIR>(a, sms, st, g.pdl);
+      case FK_PRO_SILU * 4 + SEPI_NONE: return stream_m<E, SPRO_SILU, SEPI_NONE>(a, sms, st, g.pdl);
+      case FK_PRO_SILU * 4 + SEPI_ADD: return stream_m<E, SPRO_SILU, SEPI_ADD>(a, sms, st, g.pdl);
       case FK_PRO_REDUCE_RMSNORM * 4 + SEPI_NONE:
-        return stream_m<SPRO_REDUCE_RMSNORM, SEPI_NONE>(a, sms, st, g.pdl);
+        return stream_m<E, SPRO_REDUCE_RMSNORM, SEPI_NONE>(a, sms, st, g.pdl);
       case FK_PRO_REDUCE_RMSNORM * 4 + SEPI_SILU_PAIR:
-        return stream_m<SPRO_REDUCE_RMSNORM, SEPI_SILU_PAIR>(a, sms, st, g.pdl);
+        return stream_m<E, SPRO_REDUCE_RMSNORM, SEPI_SILU_PAIR>(a, sms, st, g.pdl);
       default: return cudaErrorInvalidValue;
     }
   }
   // Batches up to 64 rows at split 1: the packed batched kernel
   // (k_w16_batch.cu), which has the row-pair form.
-  if (!peer && fk_gemv_w16_batches(g, w)) return fk_launch_gemv_batch_w16(g, w, gamma, sms, st);
+  if (!peer && fk_gemv_w16_batches(g, w)) return fk_launch_gemv_batch_w16(g, E::kElem, w, gamma, sms, st);
   // Past those: the chunked kernel, which has no row-pair or peer forms, 32
   // batch rows a launch.
   if (g.silu_pair || peer || !(g.split == 1 || g.split == 2 || g.split == 4 || g.split == 8))
@@ -633,11 +623,11 @@ cudaError_t fk_launch_gemv_w16(const FkGemv& g, const uint16_t* w, const uint16_
     const bool add = a.r != nullptr;
     cudaError_t e;
     switch (g.prologue) {
-      case FK_PRO_NONE: e = add ? launch_chunk<PRO_NONE, true>(a, st, g.pdl) : launch_chunk<PRO_NONE, false>(a, st, g.pdl); break;
+      case FK_PRO_NONE: e = add ? launch_chunk<E, PRO_NONE, true>(a, st, g.pdl) : launch_chunk<E, PRO_NONE, false>(a, st, g.pdl); break;
       case FK_PRO_RMSNORM:
-        e = add ? launch_chunk<PRO_RMSNORM, true>(a, st, g.pdl) : launch_chunk<PRO_RMSNORM, false>(a, st, g.pdl);
+        e = add ? launch_chunk<E, PRO_RMSNORM, true>(a, st, g.pdl) : launch_chunk<E, PRO_RMSNORM, false>(a, st, g.pdl);
         break;
-      case FK_PRO_SILU: e = add ? launch_chunk<PRO_SILU, true>(a, st, g.pdl) : launch_chunk<PRO_SILU, false>(a, st, g.pdl); break;
+      case FK_PRO_SILU: e = add ? launch_chunk<E, PRO_SILU, true>(a, st, g.pdl) : launch_chunk<E, PRO_SILU, false>(a, st, g.pdl); break;
       default: return cudaErrorInvalidValue;
     }
     if (e != cudaSuccess) return e;
@@ -645,39 +635,75 @@ cudaError_t fk_launch_gemv_w16(const FkGemv& g, const uint16_t* w, const uint16_
   return cudaSuccess;
 }
 
-cudaError_t fk_launch_gather_w16(const uint16_t* table, uint32_t width, const uint32_t* tokens, uint32_t m,
-                                 float factor, float* y, bool pdl, cudaStream_t s) {
-  if (m == 0) return cudaSuccess;
-  if (width % 4 != 0) return cudaErrorInvalidValue;
-  return fk_launch_ex(fk::w16::gather_w16_kernel, dim3((width / 4 + 255) / 256, m), dim3(256), 0, s, pdl, table,
-                      width, tokens, factor, y);
-}
-
-cudaError_t fk_launch_rmsnorm_rows_w16(const float* x, const uint16_t* gamma, float* y, uint32_t rows, uint32_t h,
-                                       float eps, float factor, cudaStream_t s) {
-  if (rows == 0) return cudaSuccess;
-  if (h % 4 != 0) return cudaErrorInvalidValue;
+template <class E>
+static cudaError_t rmsnorm_rows(const float* x, const uint16_t* gamma, float* y, uint32_t rows, uint32_t h, float eps,
+                                float factor, cudaStream_t s) {
   const uint32_t packs = h / 4;
   if (packs <= 256)
-    fk::w16::rmsnorm_rows_w16_kernel<1><<<rows, 256, 0, s>>>(x, gamma, y, h, eps, factor);
+    rmsnorm_rows_w16_kernel<E, 1><<<rows, 256, 0, s>>>(x, gamma, y, h, eps, factor);
   else if (packs <= 1024)
-    fk::w16::rmsnorm_rows_w16_kernel<4><<<rows, 256, 0, s>>>(x, gamma, y, h, eps, factor);
+    rmsnorm_rows_w16_kernel<E, 4><<<rows, 256, 0, s>>>(x, gamma, y, h, eps, factor);
   else if (packs <= 4096)
-    fk::w16::rmsnorm_rows_w16_kernel<16><<<rows, 256, 0, s>>>(x, gamma, y, h, eps, factor);
+    rmsnorm_rows_w16_kernel<E, 16><<<rows, 256, 0, s>>>(x, gamma, y, h, eps, factor);
   else
     return cudaErrorInvalidValue;
   return cudaGetLastError();
 }
 
-cudaError_t fk_launch_split_tf32_w16(const uint16_t* x, float* hi, float* lo, uint64_t n, cudaStream_t s) {
-  if (n == 0) return cudaSuccess;
-  fk::w16::split_tf32_w16_kernel<<<fk::w16::grid_for(n), 256, 0, s>>>(x, hi, lo, n);
+template <class E>
+static cudaError_t split_tf32(const uint16_t* x, float* hi, float* lo, uint64_t n, cudaStream_t s) {
+  split_tf32_w16_kernel<E><<<grid_for(n), 256, 0, s>>>(x, hi, lo, n);
   return cudaGetLastError();
 }
 
-cudaError_t fk_launch_fill_normal_w16(uint16_t* out, uint64_t n, uint64_t seed, double mu, double sigma,
+template <class E>
+static cudaError_t fill_normal(uint16_t* out, uint64_t n, uint64_t seed, double mu, double sigma, cudaStream_t s) {
+  fill_normal_w16_kernel<E><<<grid_for((n + 1) / 2), 256, 0, s>>>(out, n, seed, mu, sigma);
+  return cudaGetLastError();
+}
+
+}  // namespace w16
+}  // namespace fk
+
+cudaError_t fk_launch_gemv_w16(const FkGemv& g, FkElem e, const uint16_t* w, const uint16_t* gamma, int sms,
+                               cudaStream_t st) {
+  if (g.n == 0 || g.m == 0) return cudaSuccess;
+#define CALL(E) fk::w16::gemv<E>(g, w, gamma, sms, st)
+  return FK_BY_ELEM16(e, CALL);
+#undef CALL
+}
+
+cudaError_t fk_launch_gather_w16(FkElem e, const uint16_t* table, uint32_t width, const uint32_t* tokens, uint32_t m,
+                                 float factor, float* y, bool pdl, cudaStream_t s) {
+  if (m == 0) return cudaSuccess;
+  if (width % 4 != 0) return cudaErrorInvalidValue;
+#define CALL(E)                                                                                                     \
+  fk_launch_ex(fk::w16::gather_w16_kernel<E>, dim3((width / 4 + 255) / 256, m), dim3(256), 0, s, pdl, table, width, \
+               tokens, factor, y)
+  return FK_BY_ELEM16(e, CALL);
+#undef CALL
+}
+
+cudaError_t fk_launch_rmsnorm_rows_w16(FkElem e, const float* x, const uint16_t* gamma, float* y, uint32_t rows,
+                                       uint32_t h, float eps, float factor, cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  if (h % 4 != 0) return cudaErrorInvalidValue;
+#define CALL(E) fk::w16::rmsnorm_rows<E>(x, gamma, y, rows, h, eps, factor, s)
+  return FK_BY_ELEM16(e, CALL);
+#undef CALL
+}
+
+cudaError_t fk_launch_split_tf32_w16(FkElem e, const uint16_t* x, float* hi, float* lo, uint64_t n, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+#define CALL(E) fk::w16::split_tf32<E>(x, hi, lo, n, s)
+  return FK_BY_ELEM16(e, CALL);
+#undef CALL
+}
+
+cudaError_t fk_launch_fill_normal_w16(FkElem e, uint16_t* out, uint64_t n, uint64_t seed, double mu, double sigma,
                                       cudaStream_t s) {
   if (n == 0) return cudaSuccess;
-  fk::w16::fill_normal_w16_kernel<<<fk::w16::grid_for((n + 1) / 2), 256, 0, s>>>(out, n, seed, mu, sigma);
-  return cudaGetLastError();
+#define CALL(E) fk::w16::fill_normal<E>(out, n, seed, mu, sigma, s)
+  return FK_BY_ELEM16(e, CALL);
+#undef CALL
 }

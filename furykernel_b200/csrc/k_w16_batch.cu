@@ -1,10 +1,13 @@
-// The batched GEMV (k_gemv_batch.cu) for bf16 weights: the same kernel,
-// the same packed f32x2 arithmetic in the same order, with each weight pack
-// of four bf16 (8 bytes) and the RMSNorm gain widened to binary32 exactly
-// where they are read (widenBF16, src/FuryKernel/Numerics.hs:33-38), so its
-// outputs are the f32 kernel's over the widened weights. Derived from that
-// file line for line; only the weight and gain loads differ.
+// The batched GEMV (k_gemv_batch.cu) for 16-bit weights, bf16 or f16: the
+// same kernel, the same packed f32x2 arithmetic in the same order, with each
+// weight pack of four 16-bit elements (8 bytes) and the RMSNorm gain widened
+// to binary32 exactly where they are read (widenBF16 and widenF16,
+// src/FuryKernel/Numerics.hs:33-38 and :51-66; the element type a tag,
+// fk_elem16.cuh), so its outputs are the f32 kernel's over the widened
+// weights. Derived from that file line for line; only the weight and gain
+// loads differ.
 #include "fk_common.cuh"
+#include "fk_elem16.cuh"
 #include "fk_kernels.h"
 
 namespace fk {
@@ -38,12 +41,6 @@ __device__ __forceinline__ float silu_pair_of(float a, float b) {
   return __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, e)), b);
 }
 
-// Four bf16 weights of a pack (8 bytes), widened: element 0 is the low
-// half of the first word.
-__device__ __forceinline__ float4 widen4(uint2 r) {
-  return make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xFFFF0000u), __uint_as_float(r.y << 16),
-                     __uint_as_float(r.y & 0xFFFF0000u));
-}
 __device__ __forceinline__ uint2 ld_stream2(const uint2* p) {
   uint2 v;
   asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
@@ -110,7 +107,7 @@ __device__ __forceinline__ float4 prologue(const BatchArgs& a, float4 v, float s
 
 // Raw chunk -> compute buffer: plane 2p holds {x0, x0', x1, x1'} and plane
 // 2p + 1 {x2, x2', x3, x3'} of batch rows 2p and 2p + 1 (rows past mp zero).
-template <int M, int PRO>
+template <class E, int M, int PRO>
 __device__ __forceinline__ void interleave_chunk(const BatchArgs& a, const float4* raw, float4* xs,
                                                  const float* scales, uint32_t row0, uint32_t mp, uint32_t c,
                                                  uint32_t packs) {
@@ -121,7 +118,7 @@ __device__ __forceinline__ void interleave_chunk(const BatchArgs& a, const float
     if (j >= len) continue;
     const uint32_t i0 = 2 * p, i1 = 2 * p + 1;
     float4 g = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    if (PRO == BPRO_RMSNORM && a.gamma) g = widen4(__ldg(reinterpret_cast<const uint2*>(a.gamma) + base + j));
+    if (PRO == BPRO_RMSNORM && a.gamma) g = E::widen4(__ldg(reinterpret_cast<const uint2*>(a.gamma) + base + j));
     const float4 zero = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     const float4 u = i0 < mp ? prologue<PRO>(a, raw[i0 * kChunk + j], PRO == BPRO_RMSNORM ? scales[row0 + i0] : 0.0f, g)
                              : zero;
@@ -132,7 +129,7 @@ __device__ __forceinline__ void interleave_chunk(const BatchArgs& a, const float
   }
 }
 
-template <int M, int PRO, int EPI>
+template <class E, int M, int PRO, int EPI>
 __global__ void __launch_bounds__(batch_warps<M>() * 32, 1) gemv_batch_w16_kernel(BatchArgs a) {
   extern __shared__ float4 smem4[];  // raw [M][kChunk], then compute [2][M][kChunk]
   float4* raw = smem4;
@@ -215,13 +212,13 @@ __global__ void __launch_bounds__(batch_warps<M>() * 32, 1) gemv_batch_w16_kerne
       if (active) {
         const uint32_t g0 = min(g, packs - 1);
 #pragma unroll
-        for (int r = 0; r < kBatchRows; ++r) wv[r] = widen4(ld_stream2(wrow + roff[r] + g0));
+        for (int r = 0; r < kBatchRows; ++r) wv[r] = E::widen4(ld_stream2(wrow + roff[r] + g0));
       }
       for (uint32_t c = 0; c < chunks; ++c) {
         float4* xs = comp + (size_t)(c & 1) * M * kChunk;
         cp_async_wait_all();
         __syncthreads();  // chunk c's copies are in; compute buffer c & 1 is free
-        interleave_chunk<M, PRO>(a, raw, xs, scales, p0, mp, c, packs);
+        interleave_chunk<E, M, PRO>(a, raw, xs, scales, p0, mp, c, packs);
         __syncthreads();  // the raw buffer is free, chunk c is interleaved
         if (c + 1 < chunks) {
           copy_chunk(a, raw, p0, mp, c + 1, packs);
@@ -246,7 +243,7 @@ __global__ void __launch_bounds__(batch_warps<M>() * 32, 1) gemv_batch_w16_kerne
             }
             const uint32_t gn = min(g + 32, packs - 1);
 #pragma unroll
-            for (int r = 0; r < kBatchRows; ++r) wv[r] = widen4(ld_stream2(wrow + roff[r] + gn));
+            for (int r = 0; r < kBatchRows; ++r) wv[r] = E::widen4(ld_stream2(wrow + roff[r] + gn));
             // Each 128-bit load is two packed operands as they lie.
             const ulonglong2* xc = reinterpret_cast<const ulonglong2*>(xs) + (g - c * kChunk);
 #pragma unroll
@@ -301,9 +298,9 @@ __global__ void __launch_bounds__(batch_warps<M>() * 32, 1) gemv_batch_w16_kerne
   }
 }
 
-template <int M, int PRO, int EPI>
+template <class E, int M, int PRO, int EPI>
 static cudaError_t launch_batch(const BatchArgs& a, int sms, cudaStream_t st, bool pdl) {
-  auto kern = gemv_batch_w16_kernel<M, PRO, EPI>;
+  auto kern = gemv_batch_w16_kernel<E, M, PRO, EPI>;
   const size_t smem = 3 * (size_t)M * kChunk * sizeof(float4);
   cudaError_t e = fk_allow_smem(kern, smem);
   if (e != cudaSuccess) return e;
@@ -313,10 +310,21 @@ static cudaError_t launch_batch(const BatchArgs& a, int sms, cudaStream_t st, bo
   return fk_launch_ex(kern, dim3(blocks), dim3(batch_warps<M>() * 32), smem, st, pdl, a);
 }
 
-template <int PRO, int EPI>
+template <class E, int PRO, int EPI>
 static cudaError_t batch_m(const BatchArgs& a, int sms, cudaStream_t st, bool pdl) {
-  if (a.m <= 8) return launch_batch<8, PRO, EPI>(a, sms, st, pdl);
-  return launch_batch<16, PRO, EPI>(a, sms, st, pdl);
+  if (a.m <= 8) return launch_batch<E, 8, PRO, EPI>(a, sms, st, pdl);
+  return launch_batch<E, 16, PRO, EPI>(a, sms, st, pdl);
+}
+
+template <class E>
+static cudaError_t batch(const BatchArgs& a, int prologue, int epi, int sms, cudaStream_t st, bool pdl) {
+  switch (prologue * 4 + epi) {
+    case FK_PRO_NONE * 4 + BEPI_NONE: return batch_m<E, BPRO_NONE, BEPI_NONE>(a, sms, st, pdl);
+    case FK_PRO_NONE * 4 + BEPI_ADD: return batch_m<E, BPRO_NONE, BEPI_ADD>(a, sms, st, pdl);
+    case FK_PRO_RMSNORM * 4 + BEPI_NONE: return batch_m<E, BPRO_RMSNORM, BEPI_NONE>(a, sms, st, pdl);
+    case FK_PRO_RMSNORM * 4 + BEPI_SILU_PAIR: return batch_m<E, BPRO_RMSNORM, BEPI_SILU_PAIR>(a, sms, st, pdl);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace w16b
@@ -328,7 +336,7 @@ bool fk_gemv_w16_batches(const FkGemv& g, const uint16_t* w) {
          (g.prologue == FK_PRO_NONE || g.prologue == FK_PRO_RMSNORM) && !(g.silu_pair && (g.n % 2 != 0 || g.r));
 }
 
-cudaError_t fk_launch_gemv_batch_w16(const FkGemv& g, const uint16_t* w, const uint16_t* gamma, int sms,
+cudaError_t fk_launch_gemv_batch_w16(const FkGemv& g, FkElem e, const uint16_t* w, const uint16_t* gamma, int sms,
                                      cudaStream_t st) {
   if (g.n == 0 || g.m == 0) return cudaSuccess;
   if (!fk_gemv_w16_batches(g, w)) return cudaErrorInvalidValue;
@@ -349,11 +357,7 @@ cudaError_t fk_launch_gemv_batch_w16(const FkGemv& g, const uint16_t* w, const u
   a.negzero = -0.0f;
   using namespace fk::w16b;
   const int epi = g.silu_pair ? BEPI_SILU_PAIR : (g.r ? BEPI_ADD : BEPI_NONE);
-  switch (g.prologue * 4 + epi) {
-    case FK_PRO_NONE * 4 + BEPI_NONE: return batch_m<BPRO_NONE, BEPI_NONE>(a, sms, st, g.pdl);
-    case FK_PRO_NONE * 4 + BEPI_ADD: return batch_m<BPRO_NONE, BEPI_ADD>(a, sms, st, g.pdl);
-    case FK_PRO_RMSNORM * 4 + BEPI_NONE: return batch_m<BPRO_RMSNORM, BEPI_NONE>(a, sms, st, g.pdl);
-    case FK_PRO_RMSNORM * 4 + BEPI_SILU_PAIR: return batch_m<BPRO_RMSNORM, BEPI_SILU_PAIR>(a, sms, st, g.pdl);
-    default: return cudaErrorInvalidValue;
-  }
+#define CALL(E) batch<E>(a, g.prologue, epi, sms, st, g.pdl)
+  return FK_BY_ELEM16(e, CALL);
+#undef CALL
 }

@@ -233,7 +233,7 @@ extern "C" int fkc_kv_arena_elem(fkc_ctx* c, uint32_t layers, uint32_t slots, ui
                                  uint32_t head_dim, uint32_t elem_bytes, void** k_base, void** v_base) {
   if (!c || !k_base || !v_base) return fail(FKC_ERR_ARGUMENT, "fkc_kv_arena_elem: null argument.");
   if (elem_bytes != 2 && elem_bytes != 4)
-    return fail(FKC_ERR_ARGUMENT, "fkc_kv_arena_elem: elements of %u bytes; a cache holds 2 (bf16) or 4 (f32).",
+    return fail(FKC_ERR_ARGUMENT, "fkc_kv_arena_elem: elements of %u bytes; a cache holds 2 (bf16, f16) or 4 (f32).",
                 elem_bytes);
   const size_t per = (size_t)slots * kv_heads * length * head_dim * elem_bytes;
   const size_t total = per * layers;
@@ -276,7 +276,14 @@ extern "C" int fkc_fill_normal(fkc_ctx* c, void* dptr, uint64_t n, uint64_t seed
 extern "C" int fkc_fill_normal_bf16(fkc_ctx* c, void* dptr, uint64_t n, uint64_t seed, double mu, double sigma) {
   if (!c || (n && !dptr)) return fail(FKC_ERR_ARGUMENT, "fkc_fill_normal_bf16: null argument.");
   cudaSetDevice(c->device);
-  FKC_CUDA(fk_launch_fill_normal_w16((uint16_t*)dptr, n, seed, mu, sigma, c->stream), "fkc_fill_normal_bf16");
+  FKC_CUDA(fk_launch_fill_normal_w16(FK_BF16, (uint16_t*)dptr, n, seed, mu, sigma, c->stream), "fkc_fill_normal_bf16");
+  return FKC_OK;
+}
+
+extern "C" int fkc_fill_normal_f16(fkc_ctx* c, void* dptr, uint64_t n, uint64_t seed, double mu, double sigma) {
+  if (!c || (n && !dptr)) return fail(FKC_ERR_ARGUMENT, "fkc_fill_normal_f16: null argument.");
+  cudaSetDevice(c->device);
+  FKC_CUDA(fk_launch_fill_normal_w16(FK_F16, (uint16_t*)dptr, n, seed, mu, sigma, c->stream), "fkc_fill_normal_f16");
   return FKC_OK;
 }
 
@@ -666,34 +673,43 @@ int l_silu_pairs(fkc_ctx* c, const Params& p, void* const* bufs) {
   return launched(fk_launch_silu_pairs(CF(0), F(1), p.u(0), c->stream), "silu_pairs");
 }
 
-// ---- bf16 weights (the entries' `w`, `gamma`, `table` buffers are bf16) ----
+// ---- 16-bit weights (the entries' `w`, `gamma`, `table` buffers are bf16 or
+// f16, EL) and 16-bit KV caches (`k_cache`, `v_cache`) ----
 #define W16(i) ((const uint16_t*)bufs[i])
 #define M16(i) ((uint16_t*)bufs[i])
+// An entry's name: a 16-bit weights form (WN) or KV cache form (KN) of base.
+#define WN(base) (EL == FK_F16 ? base "_wf16" : base "_wbf16")
+#define KN(base) (EL == FK_F16 ? base "_kvf16" : base "_kvbf16")
 
+template <FkElem EL>
 int gemv_w16(fkc_ctx* c, const FkGemv& g, const uint16_t* w, const uint16_t* gamma, const char* name) {
-  return launched(fk_launch_gemv_w16(g, w, gamma, c->sms, c->stream), name);
+  return launched(fk_launch_gemv_w16(g, EL, w, gamma, c->sms, c->stream), name);
 }
+template <FkElem EL>
 int l_gemv_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
   FkGemv g = gemv_base(c, p);
   g.x = CF(1), g.y = F(2);
   g.prologue = FK_PRO_NONE;
-  return gemv_w16(c, g, W16(0), nullptr, "gemv_wbf16");
+  return gemv_w16<EL>(c, g, W16(0), nullptr, WN("gemv"));
 }
+template <FkElem EL>
 int l_gemv_add_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
   FkGemv g = gemv_base(c, p);
   g.x = CF(1), g.r = CF(2), g.y = F(3);
   g.ldr = p.u(6);
   g.prologue = FK_PRO_NONE;
-  return gemv_w16(c, g, W16(0), nullptr, "gemv_add_wbf16");
+  return gemv_w16<EL>(c, g, W16(0), nullptr, WN("gemv_add"));
 }
+template <FkElem EL>
 int l_gemv_rmsnorm_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
   FkGemv g = gemv_base(c, p);
   g.x = CF(1), g.y = F(3);
   g.eps = p.f(6);
   g.factor = p.f(7);
   g.prologue = FK_PRO_RMSNORM;
-  return gemv_w16(c, g, W16(0), W16(2), "gemv_rmsnorm_wbf16");
+  return gemv_w16<EL>(c, g, W16(0), W16(2), WN("gemv_rmsnorm"));
 }
+template <FkElem EL>
 int l_gemv_rmsnorm_silu_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
   FkGemv g = gemv_base(c, p);
   g.x = CF(1), g.y = F(3);
@@ -702,31 +718,34 @@ int l_gemv_rmsnorm_silu_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
   g.prologue = FK_PRO_RMSNORM;
   g.silu_pair = true;
   if (g.n % 2 != 0)
-    return fail(FKC_ERR_ARGUMENT, "gemv_rmsnorm_silu_wbf16: n %u is not a whole number of row pairs.", g.n);
+    return fail(FKC_ERR_ARGUMENT, "%s: n %u is not a whole number of row pairs.", WN("gemv_rmsnorm_silu"), g.n);
   if (!fk_gemv_streams(g) && !fk_gemv_w16_batches(g, W16(0)))
     return fail(FKC_ERR_ARGUMENT,
-                "gemv_rmsnorm_silu_wbf16: m %u, k %u and split %u are past what the row-pair kernels take (m at most "
-                "64, split 1 past m 4).",
-                g.m, g.k, g.split);
-  return gemv_w16(c, g, W16(0), W16(2), "gemv_rmsnorm_silu_wbf16");
+                "%s: m %u, k %u and split %u are past what the row-pair kernels take (m at most 64, split 1 past m "
+                "4).",
+                WN("gemv_rmsnorm_silu"), g.m, g.k, g.split);
+  return gemv_w16<EL>(c, g, W16(0), W16(2), WN("gemv_rmsnorm_silu"));
 }
+template <FkElem EL>
 int l_gemv_silu_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
   FkGemv g = gemv_base(c, p);
   g.x = CF(1), g.y = F(2);
   g.up_off = p.u(6);
   g.prologue = FK_PRO_SILU;
-  return gemv_w16(c, g, W16(0), nullptr, "gemv_silu_wbf16");
+  return gemv_w16<EL>(c, g, W16(0), nullptr, WN("gemv_silu"));
 }
+template <FkElem EL>
 int l_gemv_silu_add_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
   FkGemv g = gemv_base(c, p);
   g.x = CF(1), g.r = CF(2), g.y = F(3);
   g.ldr = p.u(6);
   g.up_off = p.u(7);
   g.prologue = FK_PRO_SILU;
-  return gemv_w16(c, g, W16(0), nullptr, "gemv_silu_add_wbf16");
+  return gemv_w16<EL>(c, g, W16(0), nullptr, WN("gemv_silu_add"));
 }
+template <FkElem EL>
 int l_gemv_scatter_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
-  if (!have_peers(c)) return fail(FKC_ERR_STATE, "gemv_scatter_wbf16: the context has no peer set.");
+  if (!have_peers(c)) return fail(FKC_ERR_STATE, "%s: the context has no peer set.", WN("gemv_scatter"));
   FkGemv g = {};
   g.x = CF(1);
   g.n = p.u(0), g.k = p.u(1), g.m = p.u(2), g.split = p.u(3), g.ldx = p.u(4), g.xbuf = p.u(5);
@@ -737,9 +756,10 @@ int l_gemv_scatter_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
   g.peers = c->peers;
   g.err = c->status;
   if (!fk_gemv_streams(g))
-    return fail(FKC_ERR_ARGUMENT, "gemv_scatter_wbf16: m %u is past the streaming kernel's 4.", g.m);
-  return gemv_w16(c, g, W16(0), nullptr, "gemv_scatter_wbf16");
+    return fail(FKC_ERR_ARGUMENT, "%s: m %u is past the streaming kernel's 4.", WN("gemv_scatter"), g.m);
+  return gemv_w16<EL>(c, g, W16(0), nullptr, WN("gemv_scatter"));
 }
+template <FkElem EL>
 int reduce_gemv_w16(fkc_ctx* c, const Params& p, void* const* bufs, bool silu, const char* name) {
   if (!have_peers(c)) return fail(FKC_ERR_STATE, "%s: the context has no peer set.", name);
   FkGemv g = {};
@@ -753,35 +773,40 @@ int reduce_gemv_w16(fkc_ctx* c, const Params& p, void* const* bufs, bool silu, c
   g.err = c->status;
   if (g.ldx != g.k) return fail(FKC_ERR_ARGUMENT, "%s: the residual rows must be whole (ldr %u, k %u).", name, g.ldx, g.k);
   if (!fk_gemv_streams(g)) return fail(FKC_ERR_ARGUMENT, "%s: m %u is past the streaming kernel's 4.", name, g.m);
-  return gemv_w16(c, g, W16(0), W16(2), name);
+  return gemv_w16<EL>(c, g, W16(0), W16(2), name);
 }
+template <FkElem EL>
 int l_gemv_reduce_rmsnorm_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
-  return reduce_gemv_w16(c, p, bufs, false, "gemv_reduce_rmsnorm_wbf16");
+  return reduce_gemv_w16<EL>(c, p, bufs, false, WN("gemv_reduce_rmsnorm"));
 }
+template <FkElem EL>
 int l_gemv_reduce_rmsnorm_silu_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
-  return reduce_gemv_w16(c, p, bufs, true, "gemv_reduce_rmsnorm_silu_wbf16");
+  return reduce_gemv_w16<EL>(c, p, bufs, true, WN("gemv_reduce_rmsnorm_silu"));
 }
+template <FkElem EL>
 int l_gather_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
-  return launched(fk_launch_gather_w16(W16(0), p.u(0), CU(1), p.u(1), p.f(2), F(2), c->pdl, c->stream),
-                  "gather_wbf16");
+  return launched(fk_launch_gather_w16(EL, W16(0), p.u(0), CU(1), p.u(1), p.f(2), F(2), c->pdl, c->stream),
+                  WN("gather"));
 }
+template <FkElem EL>
 int l_rmsnorm_rows_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
-  return launched(fk_launch_rmsnorm_rows_w16(CF(0), W16(1), F(2), p.u(0), p.u(1), p.f(2), p.f(3), c->stream),
-                  "rmsnorm_rows_wbf16");
+  return launched(fk_launch_rmsnorm_rows_w16(EL, CF(0), W16(1), F(2), p.u(0), p.u(1), p.f(2), p.f(3), c->stream),
+                  WN("rmsnorm_rows"));
 }
+template <FkElem EL>
 int l_split_tf32_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
-  return launched(fk_launch_split_tf32_w16(W16(0), F(1), F(2), p.u(0), c->stream), "split_tf32_wbf16");
+  return launched(fk_launch_split_tf32_w16(EL, W16(0), F(1), F(2), p.u(0), c->stream), WN("split_tf32"));
 }
 
-// ---- bf16 KV caches (the entries' `k_cache`, `v_cache` buffers are bf16) ----
+template <FkElem EL>
 int l_kv_store_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
   FkKvStore a = {};
   a.qkv = CF(0), a.cos_t = CF(1), a.sin_t = CF(2), a.pos = CU(3), a.slot = CU(4);
   a.m = p.u(0), a.kv_heads = p.u(1), a.d = p.u(2), a.length = p.u(3), a.rotated = p.u(4);
   a.ldq = p.u(5), a.k_off = p.u(6), a.v_off = p.u(7);
   a.pdl = c->pdl;
-  if (a.rotated > a.d / 2) return fail(FKC_ERR_ARGUMENT, "kv_store_ring_kvbf16: rotated %u is more than d/2.", a.rotated);
-  return launched(fk_launch_kv_store16(a, M16(5), M16(6), c->stream), "kv_store_ring_kvbf16");
+  if (a.rotated > a.d / 2) return fail(FKC_ERR_ARGUMENT, "%s: rotated %u is more than d/2.", KN("kv_store_ring"), a.rotated);
+  return launched(fk_launch_kv_store16(a, EL, M16(5), M16(6), c->stream), KN("kv_store_ring"));
 }
 FkAttend attend_base(fkc_ctx* c, const Params& p, void* const* bufs) {
   FkAttend a = {};
@@ -790,40 +815,43 @@ FkAttend attend_base(fkc_ctx* c, const Params& p, void* const* bufs) {
   a.pdl = c->pdl;
   return a;
 }
+template <FkElem EL>
 int l_attend_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
   FkAttend a = attend_base(c, p, bufs);
   a.part_m = F(7), a.part_l = F(8), a.part_acc = F(9);
   a.chunk = p.u(6), a.max_splits = p.u(7), a.ldq = p.u(8), a.q_off = p.u(9);
   a.scale = p.f(10);
   if (a.kv_heads == 0 || a.heads % a.kv_heads != 0)
-    return fail(FKC_ERR_ARGUMENT, "attend_split_kvbf16: %u heads do not share %u KV heads in groups.", a.heads,
+    return fail(FKC_ERR_ARGUMENT, "%s: %u heads do not share %u KV heads in groups.", KN("attend_split"), a.heads,
                 a.kv_heads);
-  return launched(fk_launch_attend16(a, W16(5), W16(6), c->stream), "attend_split_kvbf16");
+  return launched(fk_launch_attend16(a, EL, W16(5), W16(6), c->stream), KN("attend_split"));
 }
+template <FkElem EL>
 int l_attend_decode_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
   FkAttend a = attend_base(c, p, bufs);
   a.part_m = F(7), a.part_l = F(8), a.part_acc = F(9);
   a.chunk = p.u(6), a.max_splits = p.u(7), a.ldq = p.u(8), a.q_off = p.u(9);
   a.scale = p.f(12);
   if (a.kv_heads == 0 || a.heads % a.kv_heads != 0)
-    return fail(FKC_ERR_ARGUMENT, "attend_decode_kvbf16: %u heads do not share %u KV heads in groups.", a.heads,
+    return fail(FKC_ERR_ARGUMENT, "%s: %u heads do not share %u KV heads in groups.", KN("attend_decode"), a.heads,
                 a.kv_heads);
-  if (a.rotated > a.d / 2) return fail(FKC_ERR_ARGUMENT, "attend_decode_kvbf16: rotated %u is more than d/2.", a.rotated);
-  return launched(fk_launch_attend_decode16(a, p.u(10), p.u(11), M16(5), M16(6), c->stream), "attend_decode_kvbf16");
+  if (a.rotated > a.d / 2) return fail(FKC_ERR_ARGUMENT, "%s: rotated %u is more than d/2.", KN("attend_decode"), a.rotated);
+  return launched(fk_launch_attend_decode16(a, EL, p.u(10), p.u(11), M16(5), M16(6), c->stream), KN("attend_decode"));
 }
+template <FkElem EL>
 int l_attend_prompt_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
   FkAttend a = attend_base(c, p, bufs);
   a.ldq = p.u(6), a.q_off = p.u(7);
   a.scale = p.f(10);
   if (a.kv_heads == 0 || a.heads % a.kv_heads != 0)
-    return fail(FKC_ERR_ARGUMENT, "attend_prompt_kvbf16: %u heads do not share %u KV heads in groups.", a.heads,
+    return fail(FKC_ERR_ARGUMENT, "%s: %u heads do not share %u KV heads in groups.", KN("attend_prompt"), a.heads,
                 a.kv_heads);
-  if (a.rotated > a.d / 2) return fail(FKC_ERR_ARGUMENT, "attend_prompt_kvbf16: rotated %u is more than d/2.", a.rotated);
+  if (a.rotated > a.d / 2) return fail(FKC_ERR_ARGUMENT, "%s: rotated %u is more than d/2.", KN("attend_prompt"), a.rotated);
   if (p.u(9) >= a.length)
-    return fail(FKC_ERR_ARGUMENT, "attend_prompt_kvbf16: max_pos %u is not within the ring's length %u.", p.u(9),
+    return fail(FKC_ERR_ARGUMENT, "%s: max_pos %u is not within the ring's length %u.", KN("attend_prompt"), p.u(9),
                 a.length);
-  return launched(fk_launch_attend_prompt16(a, W16(5), W16(6), F(7), p.u(8), p.u(9), c->stream),
-                  "attend_prompt_kvbf16");
+  return launched(fk_launch_attend_prompt16(a, EL, W16(5), W16(6), F(7), p.u(8), p.u(9), c->stream),
+                  KN("attend_prompt"));
 }
 
 // ---- routed experts ------------------------------------------------------
@@ -837,17 +865,18 @@ int l_route_topk_scaled(fkc_ctx* c, const Params& p, void* const* bufs) {
                   "route_topk_scaled");
 }
 // gemv_routed: table ids x y | entries n kk m k split ldx ldy per_rank
-int gemv_routed(fkc_ctx* c, const Params& p, void* const* bufs, bool bf16, const char* name) {
+int gemv_routed(fkc_ctx* c, const Params& p, void* const* bufs, FkElem el, const char* name) {
   if (p.u(8) > 1) return fail(FKC_ERR_ARGUMENT, "%s: per_rank is %u, not 0 or 1.", name, p.u(8));
-  return launched(fk_launch_gemv_routed(bufs[0], bf16, p.u(0), p.u(1), p.u(2), CU(1), p.u(3), p.u(4), CF(2), p.u(6),
+  return launched(fk_launch_gemv_routed(bufs[0], el, p.u(0), p.u(1), p.u(2), CU(1), p.u(3), p.u(4), CF(2), p.u(6),
                                         p.u(8) != 0, p.u(5), F(3), p.u(7), c->pdl, c->stream),
                   name);
 }
 int l_gemv_routed(fkc_ctx* c, const Params& p, void* const* bufs) {
-  return gemv_routed(c, p, bufs, false, "gemv_routed");
+  return gemv_routed(c, p, bufs, FK_F32, "gemv_routed");
 }
+template <FkElem EL>
 int l_gemv_routed_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
-  return gemv_routed(c, p, bufs, true, "gemv_routed_wbf16");
+  return gemv_routed(c, p, bufs, EL, WN("gemv_routed"));
 }
 // gated_gelu: x y | segments f
 int l_gated_gelu(fkc_ctx* c, const Params& p, void* const* bufs) {
@@ -862,7 +891,7 @@ int l_combine_ranks_add(fkc_ctx* c, const Params& p, void* const* bufs) {
 // ---- paged KV caches: block tables into pools of blocks --------------------
 // kv_store_paged: qkv cos sin pos table k_cache v_cache
 //   | m kv_heads d block_size table_len blocks rotated ldq k_off v_off
-int kv_store_paged(fkc_ctx* c, const Params& p, void* const* bufs, bool bf16, const char* name) {
+int kv_store_paged(fkc_ctx* c, const Params& p, void* const* bufs, FkElem el, const char* name) {
   FkKvStore a = {};
   a.qkv = CF(0), a.cos_t = CF(1), a.sin_t = CF(2), a.pos = CU(3);
   a.m = p.u(0), a.kv_heads = p.u(1), a.d = p.u(2), a.rotated = p.u(6);
@@ -870,17 +899,18 @@ int kv_store_paged(fkc_ctx* c, const Params& p, void* const* bufs, bool bf16, co
   a.pdl = c->pdl;
   const FkPaged pg = {CU(4), p.u(3), p.u(4), p.u(5)};
   if (a.rotated > a.d / 2) return fail(FKC_ERR_ARGUMENT, "%s: rotated %u is more than d/2.", name, a.rotated);
-  return launched(fk_launch_kv_store_paged(a, pg, bufs[5], bufs[6], bf16, c->stream), name);
+  return launched(fk_launch_kv_store_paged(a, pg, bufs[5], bufs[6], el, c->stream), name);
 }
 int l_kv_store_paged(fkc_ctx* c, const Params& p, void* const* bufs) {
-  return kv_store_paged(c, p, bufs, false, "kv_store_paged");
+  return kv_store_paged(c, p, bufs, FK_F32, "kv_store_paged");
 }
+template <FkElem EL>
 int l_kv_store_paged_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
-  return kv_store_paged(c, p, bufs, true, "kv_store_paged_kvbf16");
+  return kv_store_paged(c, p, bufs, EL, KN("kv_store_paged"));
 }
 // attend_split_paged: qkv cos sin pos table k_cache v_cache part_m part_l part_acc
 //   | m heads kv_heads d block_size table_len blocks rotated chunk max_splits ldq q_off scale
-int attend_paged(fkc_ctx* c, const Params& p, void* const* bufs, bool bf16, const char* name) {
+int attend_paged(fkc_ctx* c, const Params& p, void* const* bufs, FkElem el, const char* name) {
   FkAttend a = {};
   a.qkv = CF(0), a.cos_t = CF(1), a.sin_t = CF(2), a.pos = CU(3);
   a.part_m = F(7), a.part_l = F(8), a.part_acc = F(9);
@@ -892,18 +922,19 @@ int attend_paged(fkc_ctx* c, const Params& p, void* const* bufs, bool bf16, cons
   if (a.kv_heads == 0 || a.heads % a.kv_heads != 0)
     return fail(FKC_ERR_ARGUMENT, "%s: %u heads do not share %u KV heads in groups.", name, a.heads, a.kv_heads);
   if (a.rotated > a.d / 2) return fail(FKC_ERR_ARGUMENT, "%s: rotated %u is more than d/2.", name, a.rotated);
-  return launched(fk_launch_attend_paged(a, pg, bufs[5], bufs[6], bf16, c->stream), name);
+  return launched(fk_launch_attend_paged(a, pg, bufs[5], bufs[6], el, c->stream), name);
 }
 int l_attend_paged(fkc_ctx* c, const Params& p, void* const* bufs) {
-  return attend_paged(c, p, bufs, false, "attend_split_paged");
+  return attend_paged(c, p, bufs, FK_F32, "attend_split_paged");
 }
+template <FkElem EL>
 int l_attend_paged_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
-  return attend_paged(c, p, bufs, true, "attend_split_paged_kvbf16");
+  return attend_paged(c, p, bufs, EL, KN("attend_split_paged"));
 }
 // attend_prompt_paged: qkv cos sin pos table k_cache v_cache out
 //   | m heads kv_heads d block_size table_len blocks rotated ldq q_off ldo max_pos scale
 // A prompt's rows of one sequence: row 0's block table serves them all.
-int attend_prompt_paged(fkc_ctx* c, const Params& p, void* const* bufs, bool bf16, const char* name) {
+int attend_prompt_paged(fkc_ctx* c, const Params& p, void* const* bufs, FkElem el, const char* name) {
   FkAttend a = {};
   a.qkv = CF(0), a.cos_t = CF(1), a.sin_t = CF(2), a.pos = CU(3);
   a.m = p.u(0), a.heads = p.u(1), a.kv_heads = p.u(2), a.d = p.u(3), a.rotated = p.u(7);
@@ -917,18 +948,21 @@ int attend_prompt_paged(fkc_ctx* c, const Params& p, void* const* bufs, bool bf1
   if ((uint64_t)p.u(11) >= (uint64_t)pg.table_len * pg.block_size)
     return fail(FKC_ERR_ARGUMENT, "%s: max_pos %u is past the block table's %u positions.", name, p.u(11),
                 pg.table_len * pg.block_size);
-  return launched(fk_launch_attend_prompt_paged(a, pg, bufs[5], bufs[6], bf16, F(7), p.u(10), p.u(11), c->stream),
+  return launched(fk_launch_attend_prompt_paged(a, pg, bufs[5], bufs[6], el, F(7), p.u(10), p.u(11), c->stream),
                   name);
 }
 int l_attend_prompt_paged(fkc_ctx* c, const Params& p, void* const* bufs) {
-  return attend_prompt_paged(c, p, bufs, false, "attend_prompt_paged");
+  return attend_prompt_paged(c, p, bufs, FK_F32, "attend_prompt_paged");
 }
+template <FkElem EL>
 int l_attend_prompt_paged_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
-  return attend_prompt_paged(c, p, bufs, true, "attend_prompt_paged_kvbf16");
+  return attend_prompt_paged(c, p, bufs, EL, KN("attend_prompt_paged"));
 }
 
 #undef W16
 #undef M16
+#undef WN
+#undef KN
 
 #undef F
 #undef CF
@@ -1212,36 +1246,47 @@ std::vector<KernelSpec> make_table() {
                {{"r", "read", "f32"}, {"ws", "read", "f32"}, {"segs", "read", "f32"}, {"y", "write", "f32"}},
                {dim("m", 1, 65535), dim("k", 1, 8), dim("d", 1, kMax)},
                l_combine_ranks_add});
-  // The bf16 forms: an f32 entry's parameters with some buffers bf16 (the
-  // model's weights, or its KV caches) and their own launchers.
+  // The 16-bit forms: an f32 entry's parameters with some buffers bf16 or
+  // f16 (the model's weights, or its KV caches) and their own launchers.
   struct Variant {
     const char* base;
     const char* name;
     std::vector<const char*> retyped;
     LaunchFn launch;
+    const char* type;
   };
+#define W_FORMS(base, fn, ...)                                       \
+  {base, base "_wbf16", {__VA_ARGS__}, fn<FK_BF16>, "bf16"}, {       \
+    base, base "_wf16", {__VA_ARGS__}, fn<FK_F16>, "f16"             \
+  }
+#define KV_FORMS(base, fn)                                                        \
+  {base, base "_kvbf16", {"k_cache", "v_cache"}, fn<FK_BF16>, "bf16"}, {          \
+    base, base "_kvf16", {"k_cache", "v_cache"}, fn<FK_F16>, "f16"                \
+  }
   const std::vector<Variant> variants = {
-      {"gemv", "gemv_wbf16", {"w"}, l_gemv_w16},
-      {"gemv_add", "gemv_add_wbf16", {"w"}, l_gemv_add_w16},
-      {"gemv_rmsnorm", "gemv_rmsnorm_wbf16", {"w", "gamma"}, l_gemv_rmsnorm_w16},
-      {"gemv_rmsnorm_silu", "gemv_rmsnorm_silu_wbf16", {"w", "gamma"}, l_gemv_rmsnorm_silu_w16},
-      {"gemv_silu", "gemv_silu_wbf16", {"w"}, l_gemv_silu_w16},
-      {"gemv_silu_add", "gemv_silu_add_wbf16", {"w"}, l_gemv_silu_add_w16},
-      {"gemv_scatter", "gemv_scatter_wbf16", {"w"}, l_gemv_scatter_w16},
-      {"gemv_reduce_rmsnorm", "gemv_reduce_rmsnorm_wbf16", {"w", "gamma"}, l_gemv_reduce_rmsnorm_w16},
-      {"gemv_reduce_rmsnorm_silu", "gemv_reduce_rmsnorm_silu_wbf16", {"w", "gamma"}, l_gemv_reduce_rmsnorm_silu_w16},
-      {"gather", "gather_wbf16", {"table"}, l_gather_w16},
-      {"rmsnorm_rows", "rmsnorm_rows_wbf16", {"gamma"}, l_rmsnorm_rows_w16},
-      {"split_tf32", "split_tf32_wbf16", {"x"}, l_split_tf32_w16},
-      {"kv_store_ring", "kv_store_ring_kvbf16", {"k_cache", "v_cache"}, l_kv_store_kv16},
-      {"attend_split", "attend_split_kvbf16", {"k_cache", "v_cache"}, l_attend_kv16},
-      {"attend_decode", "attend_decode_kvbf16", {"k_cache", "v_cache"}, l_attend_decode_kv16},
-      {"attend_prompt", "attend_prompt_kvbf16", {"k_cache", "v_cache"}, l_attend_prompt_kv16},
-      {"kv_store_paged", "kv_store_paged_kvbf16", {"k_cache", "v_cache"}, l_kv_store_paged_kv16},
-      {"attend_split_paged", "attend_split_paged_kvbf16", {"k_cache", "v_cache"}, l_attend_paged_kv16},
-      {"attend_prompt_paged", "attend_prompt_paged_kvbf16", {"k_cache", "v_cache"}, l_attend_prompt_paged_kv16},
-      {"gemv_routed", "gemv_routed_wbf16", {"table"}, l_gemv_routed_w16},
+      W_FORMS("gemv", l_gemv_w16, "w"),
+      W_FORMS("gemv_add", l_gemv_add_w16, "w"),
+      W_FORMS("gemv_rmsnorm", l_gemv_rmsnorm_w16, "w", "gamma"),
+      W_FORMS("gemv_rmsnorm_silu", l_gemv_rmsnorm_silu_w16, "w", "gamma"),
+      W_FORMS("gemv_silu", l_gemv_silu_w16, "w"),
+      W_FORMS("gemv_silu_add", l_gemv_silu_add_w16, "w"),
+      W_FORMS("gemv_scatter", l_gemv_scatter_w16, "w"),
+      W_FORMS("gemv_reduce_rmsnorm", l_gemv_reduce_rmsnorm_w16, "w", "gamma"),
+      W_FORMS("gemv_reduce_rmsnorm_silu", l_gemv_reduce_rmsnorm_silu_w16, "w", "gamma"),
+      W_FORMS("gather", l_gather_w16, "table"),
+      W_FORMS("rmsnorm_rows", l_rmsnorm_rows_w16, "gamma"),
+      W_FORMS("split_tf32", l_split_tf32_w16, "x"),
+      W_FORMS("gemv_routed", l_gemv_routed_w16, "table"),
+      KV_FORMS("kv_store_ring", l_kv_store_kv16),
+      KV_FORMS("attend_split", l_attend_kv16),
+      KV_FORMS("attend_decode", l_attend_decode_kv16),
+      KV_FORMS("attend_prompt", l_attend_prompt_kv16),
+      KV_FORMS("kv_store_paged", l_kv_store_paged_kv16),
+      KV_FORMS("attend_split_paged", l_attend_paged_kv16),
+      KV_FORMS("attend_prompt_paged", l_attend_prompt_paged_kv16),
   };
+#undef W_FORMS
+#undef KV_FORMS
   for (const Variant& v : variants) {
     KernelSpec k;
     bool found = false;
@@ -1255,7 +1300,7 @@ std::vector<KernelSpec> make_table() {
     k.launch = v.launch;
     for (BufSpec& b : k.bufs)
       for (const char* r : v.retyped)
-        if (strcmp(b.name, r) == 0) b.type = "bf16";
+        if (strcmp(b.name, r) == 0) b.type = v.type;
     t.push_back(k);
   }
   // The C layout (Abi.hs:113-133) and the canonical text (Abi.hs:136-159).

@@ -212,26 +212,30 @@ SPEC_KERNELS = {
 }
 
 
-# The bf16 forms (the model's weights, or its KV caches, in bf16: the
-# reference's element types, Build.hs:171-194): an f32 entry's parameters
-# with the named buffers bf16.
+# The 16-bit forms (the model's weights, or its KV caches, in bf16 or f16:
+# the reference's element types, Build.hs:171-194, Check.hs:105-111,
+# Graph.hs:169-180): an f32 entry's parameters with the named buffers of
+# that type, named by the suffix of the type.
+WEIGHT_SUFFIX = {"f32": "", "bf16": "_wbf16", "f16": "_wf16"}
+CACHE_SUFFIX = {"f32": "", "bf16": "_kvbf16", "f16": "_kvf16"}
 _VARIANTS = [
-    *[(base, base + "_wbf16", {"w", "gamma"})
+    *[(base, base + WEIGHT_SUFFIX[t], {"w", "gamma"}, t)
+      for t in ("bf16", "f16")
       for base in ("gemv", "gemv_add", "gemv_rmsnorm", "gemv_rmsnorm_silu", "gemv_silu", "gemv_silu_add",
                    "gemv_scatter", "gemv_reduce_rmsnorm", "gemv_reduce_rmsnorm_silu")],
-    ("gather", "gather_wbf16", {"table"}),
-    ("rmsnorm_rows", "rmsnorm_rows_wbf16", {"gamma"}),
-    ("split_tf32", "split_tf32_wbf16", {"x"}),
-    ("gemv_routed", "gemv_routed_wbf16", {"table"}),
-    *[(base, base + "_kvbf16", {"k_cache", "v_cache"})
+    *[(base, base + WEIGHT_SUFFIX[t], {buf}, t)
+      for t in ("bf16", "f16")
+      for base, buf in (("gather", "table"), ("rmsnorm_rows", "gamma"), ("split_tf32", "x"),
+                        ("gemv_routed", "table"))],
+    *[(base, base + CACHE_SUFFIX[t], {"k_cache", "v_cache"}, t)
+      for t in ("bf16", "f16")
       for base in ("kv_store_ring", "attend_split", "attend_decode", "attend_prompt", "kv_store_paged",
                    "attend_split_paged", "attend_prompt_paged")],
 ]
-for _base, _name, _retyped in _VARIANTS:
+for _base, _name, _retyped, _t in _VARIANTS:
     _k = SPEC_KERNELS[_base]
-    SPEC_KERNELS[_name] = KernelSig(_name, [Buffer(b.name, b.access, "bf16" if b.name in _retyped else b.type)
+    SPEC_KERNELS[_name] = KernelSig(_name, [Buffer(b.name, b.access, _t if b.name in _retyped else b.type)
                                             for b in _k.buffers], _k.params, threads=_k.threads)
-W16_SUFFIX, KV16_SUFFIX = "_wbf16", "_kvbf16"
 
 
 class CudaBackend:

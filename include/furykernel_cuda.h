@@ -90,10 +90,11 @@ int fkc_host_free(void *host);
  * is slots * kv_heads * length * head_dim elements. */
 int fkc_kv_arena(fkc_ctx *ctx, uint32_t layers, uint32_t slots, uint32_t kv_heads, uint32_t length,
                  uint32_t head_dim, void **k_base, void **v_base);
-/* The same arena with elements of elem_bytes: 4 (f32) or 2 (bf16, the
- * element type the reference gives a cache, CacheBF16, Graph.hs:165-180;
- * the *_kvbf16 table entries read and write it). The layer stride is
- * slots * kv_heads * length * head_dim elements of that size. */
+/* The same arena with elements of elem_bytes: 4 (f32) or 2 (bf16 or f16, the
+ * element types the reference gives a cache, CacheBF16 and CacheF16,
+ * Graph.hs:165-180; the *_kvbf16 and *_kvf16 table entries read and write
+ * it). The layer stride is slots * kv_heads * length * head_dim elements of
+ * that size. */
 int fkc_kv_arena_elem(fkc_ctx *ctx, uint32_t layers, uint32_t slots, uint32_t kv_heads, uint32_t length,
                       uint32_t head_dim, uint32_t elem_bytes, void **k_base, void **v_base);
 /* RoPE tables: the cosine and sine of p * theta^(-2i/d) for p < positions,
@@ -108,6 +109,9 @@ int fkc_fill_uniform(fkc_ctx *ctx, void *dptr, uint64_t n, uint64_t seed, double
 /* fkc_fill_normal's values rounded to bf16 (nearest, ties to even: narrowBF16,
  * src/FuryKernel/Numerics.hs:41-48), n bf16 elements at dptr. */
 int fkc_fill_normal_bf16(fkc_ctx *ctx, void *dptr, uint64_t n, uint64_t seed, double mu, double sigma);
+/* The same values rounded to f16 (nearest, ties to even, gradual underflow:
+ * narrowF16, src/FuryKernel/Numerics.hs:100-130), n f16 elements at dptr. */
+int fkc_fill_normal_f16(fkc_ctx *ctx, void *dptr, uint64_t n, uint64_t seed, double mu, double sigma);
 
 /* ---- the kernel table (LoweredKernel, Backend.hs:203-228) ----------------- */
 int fkc_kernel_count(void);
