@@ -14,7 +14,11 @@ _LIB = None
 _PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_build", "libfurykernel_host.so")
 
 FKH_OK, FKH_ERR_ARGUMENT, FKH_ERR_SPACE, FKH_ERR_INTERNAL = 0, 1, 2, 3
-ABI_VERSION = 5
+ABI_VERSION = 6
+
+
+# The shape's element-type codes, in order (fkh_llama_shape).
+ELEMENT_TYPES = ("f32", "bf16", "f16")
 
 
 class Shape(ctypes.Structure):
@@ -22,7 +26,7 @@ class Shape(ctypes.Structure):
                                                 "layers")] + \
                [("theta", ctypes.c_double), ("eps", ctypes.c_double)] + \
                [(n, ctypes.c_uint64) for n in ("slots", "length", "positions")] + \
-               [("weights_bf16", ctypes.c_int), ("cache_bf16", ctypes.c_int)] + \
+               [("weights_type", ctypes.c_int), ("cache_type", ctypes.c_int)] + \
                [("blocks", ctypes.c_uint64), ("block_size", ctypes.c_uint64)] + \
                [("experts", ctypes.c_uint64), ("top_k", ctypes.c_uint64)]
 
@@ -110,11 +114,11 @@ def _text(call, *args) -> str:
 def shape(s) -> Shape:
     """A LlamaShape (program.llama) as the C struct."""
     for what, t in (("weights", s.weights), ("cache", s.cache)):
-        if t not in ("f32", "bf16"):
-            raise N.Refused(N.FKC_ERR_ARGUMENT, f"the {what}' element type {t} is not f32 or bf16.")
+        if t not in ELEMENT_TYPES:
+            raise N.Refused(N.FKC_ERR_ARGUMENT, f"the {what}' element type {t} is not f32, bf16 or f16.")
     return Shape(s.d_model, s.heads, s.kv_heads, s.head_dim, s.ffn, s.vocab, s.layers, s.theta, s.eps, s.slots,
-                 s.length, s.positions, int(s.weights == "bf16"), int(s.cache == "bf16"), s.blocks, s.block_size,
-                 s.experts, s.top_k)
+                 s.length, s.positions, ELEMENT_TYPES.index(s.weights), ELEMENT_TYPES.index(s.cache), s.blocks,
+                 s.block_size, s.experts, s.top_k)
 
 
 def llama_program_text(s, which: str) -> str:

@@ -69,6 +69,7 @@ def lib() -> ctypes.CDLL:
             "fkc_fill_normal": (i32, [vp, vp, u64, u64, ctypes.c_double, ctypes.c_double]),
             "fkc_fill_uniform": (i32, [vp, vp, u64, u64, ctypes.c_double, ctypes.c_double]),
             "fkc_fill_normal_bf16": (i32, [vp, vp, u64, u64, ctypes.c_double, ctypes.c_double]),
+            "fkc_fill_normal_f16": (i32, [vp, vp, u64, u64, ctypes.c_double, ctypes.c_double]),
             "fkc_kernel_count": (i32, []),
             "fkc_kernel_describe": (i32, [i32, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(ctypes.c_char_p),
                                           ctypes.POINTER(u64), ctypes.POINTER(u32), ctypes.POINTER(u32),
@@ -307,6 +308,10 @@ class Context:
     def fill_normal_bf16(self, buf: DeviceBuffer, seed: int, mu: float = 0.0, sigma: float = 1.0) -> None:
         """fill_normal's values rounded to bf16, nbytes / 2 of them."""
         check(lib().fkc_fill_normal_bf16(self.handle, buf.ptr, buf.nbytes // 2, seed, mu, sigma))
+
+    def fill_normal_f16(self, buf: DeviceBuffer, seed: int, mu: float = 0.0, sigma: float = 1.0) -> None:
+        """fill_normal's values rounded to f16, nbytes / 2 of them."""
+        check(lib().fkc_fill_normal_f16(self.handle, buf.ptr, buf.nbytes // 2, seed, mu, sigma))
 
     def fill_uniform(self, buf: DeviceBuffer, seed: int, a: float = -1.0, b: float = 1.0) -> None:
         check(lib().fkc_fill_uniform(self.handle, buf.ptr, buf.nbytes // 4, seed, a, b))

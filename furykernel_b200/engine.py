@@ -32,6 +32,7 @@ from . import _native as N
 from .program import plan as PL
 from .program.graph import Paged, SCache, SRowInts, SWeight
 from .program.llama import LlamaShape, embed_program, head_program, layer_program
+from .target import CACHE_SUFFIX, WEIGHT_SUFFIX
 
 
 class Unlowerable(N.Refused):
@@ -82,31 +83,25 @@ def _work_text(p, step) -> str:
 
 
 # A kernel's element-type form: the f32 entry's name, or with the suffix of
-# its bf16 weights or its bf16 KV caches.
-W16, KV16 = "_wbf16", "_kvbf16"
-
-
+# its 16-bit weights or its 16-bit KV caches (target.WEIGHT_SUFFIX,
+# target.CACHE_SUFFIX).
 def kernel_form(kernel: str) -> tuple:
     """(the f32 entry's name, the suffix of the form)."""
-    for suffix in (W16, KV16):
+    for suffix in ("_wbf16", "_wf16", "_kvbf16", "_kvf16"):
         if kernel.endswith(suffix):
             return kernel[:-len(suffix)], suffix
     return kernel, ""
 
 
 def _weight_suffix(step, t: str) -> str:
-    if t == "f32":
-        return ""
-    if t == "bf16":
-        return W16
+    if t in WEIGHT_SUFFIX:
+        return WEIGHT_SUFFIX[t]
     raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: no kernel reads {t} weights.")
 
 
 def _cache_suffix(step, elem: str) -> str:
-    if elem == "f32":
-        return ""
-    if elem == "bf16":
-        return KV16
+    if elem in CACHE_SUFFIX:
+        return CACHE_SUFFIX[elem]
     raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: no kernel reads {elem} caches.")
 
 
@@ -351,7 +346,7 @@ class Llama:
     tensor-parallel group: the weights (seeded on the device, or given), the
     Ring KV arena, the plans of the embedding, a layer and the head, and the
     captured decode step. Activations are f32; the weights and the caches
-    are f32 or bf16, as the shape says (`weights`, `cache`).
+    are f32, bf16 or f16, as the shape says (`weights`, `cache`).
 
     With `world` ranks, each holds heads/world query and KV heads with their
     rows of q/k/v and columns of o, ffn/world rows of gate and up with their
@@ -378,16 +373,16 @@ class Llama:
         self.ctx, self.full, self.s, self.m = ctx, full, s, batch
         self.rank, self.world = rank, world
         # Bytes of a weight and of a cache element.
-        self.wb = {"f32": 4, "bf16": 2}.get(s.weights)
-        self.cb = {"f32": 4, "bf16": 2}.get(s.cache)
+        self.wb = {"f32": 4, "bf16": 2, "f16": 2}.get(s.weights)
+        self.cb = {"f32": 4, "bf16": 2, "f16": 2}.get(s.cache)
         if self.wb is None or self.cb is None:
             raise N.Refused(N.FKC_ERR_ARGUMENT, f"no kernels for {s.weights} weights and {s.cache} caches.")
         if s.experts and (world > 1 or batch * s.top_k > 64 or s.experts > 1024):
             raise N.Refused(N.FKC_ERR_ARGUMENT, "routed experts: one GPU, at most 64 (row, expert) pairs a step "
                                                 "and 1024 experts.")
         if self.wb == 2 and any(n % 8 for n in (s.d_model, s.q_width, s.kv_width, s.ffn)):
-            raise N.Refused(N.FKC_ERR_ARGUMENT, "bf16 weights: d_model, the q and kv widths and ffn must be multiples "
-                            "of 8, so that every weight starts on a 16-byte boundary.")
+            raise N.Refused(N.FKC_ERR_ARGUMENT, "16-bit weights: d_model, the q and kv widths and ffn must be "
+                            "multiples of 8, so that every weight starts on a 16-byte boundary.")
         # For decode batches the streaming and batched GEMVs take (up to 64
         # rows), the arena interleaves gate and up rows (gate_i at row 2i, up_i at
         # 2i + 1), so that the [gate; up] step computes mlp_act = silu(gate) *
@@ -411,10 +406,10 @@ class Llama:
         self.layer_elems = sum(self.layer_sizes())
         wb = self.wb
         self.arena = ctx.alloc(wb * (s.layers * self.layer_elems + full.vocab * d + d))
-        fill = ctx.fill_normal if wb == 4 else ctx.fill_normal_bf16
+        fill = self._fill(s.weights)
         if host_weights is None:
             # A rank's layer shards from its own seed; the embedding and the
-            # norms alike on every rank (bf16: the same values, rounded).
+            # norms alike on every rank (16-bit: the same values, rounded).
             layers = N.DeviceBuffer(ctx, self.arena.ptr, wb * s.layers * self.layer_elems)
             fill(layers, seed + 7919 * rank, 0.0, 0.02)
             rest = N.DeviceBuffer(ctx, self.embed_ptr(), wb * (full.vocab * d + d))
@@ -428,7 +423,7 @@ class Llama:
         self.kbase, self.vbase = self._kv_arena()
         if prefill_kv is not None:
             kv = s.layers * self._kv_units() * s.kv_heads * self._kv_unit_len() * s.head_dim
-            cfill = ctx.fill_normal if self.cb == 4 else ctx.fill_normal_bf16
+            cfill = self._fill(s.cache)
             cfill(N.DeviceBuffer(ctx, self.kbase, self.cb * kv), seed + 1 + 17 * rank, 0.0, prefill_kv)
             cfill(N.DeviceBuffer(ctx, self.vbase, self.cb * kv), seed + 2 + 17 * rank, 0.0, prefill_kv)
         m = batch
@@ -516,6 +511,12 @@ class Llama:
 
     def layer_order(self) -> tuple:
         return self.MOE_ORDER if self.s.experts else self.LAYER_ORDER
+
+    def _fill(self, t: str):
+        """The seeded normal fill of elements of type t (16-bit: the f32
+        fill's values, rounded)."""
+        return {"f32": self.ctx.fill_normal, "bf16": self.ctx.fill_normal_bf16,
+                "f16": self.ctx.fill_normal_f16}[t]
 
     def layer_sizes(self) -> list:
         s = self.s

@@ -173,7 +173,7 @@ struct LlamaShape {
   uint64_t d_model = 4096, heads = 32, kv_heads = 32, head_dim = 128, ffn = 11008, vocab = 32000, layers = 32;
   double theta = 10000.0, eps = 1e-5;
   uint64_t slots = 1, length = 4096, positions = 4096;
-  std::string weights = "f32", cache = "f32";  // element types: "f32" or "bf16"
+  std::string weights = "f32", cache = "f32";  // element types: "f32", "bf16" or "f16"
   // Routed experts in place of the dense FFN: `experts` of ffn each, every
   // row taking its top_k (experts 0: the dense SiLU-gated FFN).
   uint64_t experts = 0, top_k = 2;
@@ -183,8 +183,8 @@ struct LlamaShape {
   uint64_t blocks = 0, block_size = 0;
   bool paged() const { return block_size > 0; }
   uint64_t table_len() const { return paged() ? (positions + block_size - 1) / block_size : 0; }
-  uint64_t weight_bytes() const { return weights == "bf16" ? 2 : 4; }
-  uint64_t cache_bytes() const { return cache == "bf16" ? 2 : 4; }
+  uint64_t weight_bytes() const { return weights == "f32" ? 4 : 2; }
+  uint64_t cache_bytes() const { return cache == "f32" ? 4 : 2; }
   uint64_t q_width() const { return heads * head_dim; }
   uint64_t kv_width() const { return kv_heads * head_dim; }
 };
@@ -278,9 +278,12 @@ std::vector<Launch> lower_steps(const Program& p, const Step& step, const Bindin
                                 const AttnBufs& attn);
 
 // A kernel's element-type form: the f32 entry's name, or with the suffix of
-// its bf16 weights (kW16) or its bf16 KV caches (kKV16).
-constexpr const char* kW16 = "_wbf16";
-constexpr const char* kKV16 = "_kvbf16";
+// its 16-bit weights (_wbf16, _wf16) or 16-bit KV caches (_kvbf16, _kvf16).
+// weight_form / cache_form: the suffix for weights or caches of element
+// type t ("f32": none); they throw Refusal, naming `what`, for a type no
+// kernel reads.
+std::string weight_form(const std::string& t, const std::string& what);
+std::string cache_form(const std::string& t, const std::string& what);
 std::pair<std::string, std::string> kernel_form(const std::string& kernel);
 
 // The whole decode step of the Llama engine (furykernel_b200/engine.py):

@@ -60,8 +60,12 @@ fkh::LlamaShape shape_of(const fkh_llama_shape& s) {
   o.slots = s.slots;
   o.length = s.length;
   o.positions = s.positions;
-  o.weights = s.weights_bf16 ? "bf16" : "f32";
-  o.cache = s.cache_bf16 ? "bf16" : "f32";
+  static const char* const types[] = {"f32", "bf16", "f16"};
+  if (s.weights_type < 0 || s.weights_type > 2 || s.cache_type < 0 || s.cache_type > 2)
+    throw fkh::Refusal("the shape's element types are " + std::to_string(s.weights_type) + " and " +
+                       std::to_string(s.cache_type) + ", not 0 (f32), 1 (bf16) or 2 (f16).");
+  o.weights = types[s.weights_type];
+  o.cache = types[s.cache_type];
   o.blocks = s.blocks;
   o.block_size = s.block_size;
   o.experts = s.experts;

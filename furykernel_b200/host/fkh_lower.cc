@@ -48,22 +48,28 @@ typename M::mapped_type at(const M& m, const std::string& key, const std::string
   return it->second;
 }
 
-std::string weight_suffix(const Step& step, const std::string& t) {
-  if (t == "f32") return "";
-  if (t == "bf16") return kW16;
-  throw Refusal(step.name + ": no kernel reads " + t + " weights.");
-}
+std::string weight_suffix(const Step& step, const std::string& t) { return weight_form(t, step.name); }
 
-std::string cache_suffix(const Step& step, const std::string& elem) {
-  if (elem == "f32") return "";
-  if (elem == "bf16") return kKV16;
-  throw Refusal(step.name + ": no kernel reads " + elem + " caches.");
-}
+std::string cache_suffix(const Step& step, const std::string& elem) { return cache_form(elem, step.name); }
 
 }  // namespace
 
+std::string weight_form(const std::string& t, const std::string& what) {
+  if (t == "f32") return "";
+  if (t == "bf16") return "_wbf16";
+  if (t == "f16") return "_wf16";
+  throw Refusal(what + ": no kernel reads " + t + " weights.");
+}
+
+std::string cache_form(const std::string& t, const std::string& what) {
+  if (t == "f32") return "";
+  if (t == "bf16") return "_kvbf16";
+  if (t == "f16") return "_kvf16";
+  throw Refusal(what + ": no kernel reads " + t + " caches.");
+}
+
 std::pair<std::string, std::string> kernel_form(const std::string& kernel) {
-  for (const char* suffix : {kW16, kKV16}) {
+  for (const char* suffix : {"_wbf16", "_wf16", "_kvbf16", "_kvf16"}) {
     const size_t n = std::char_traits<char>::length(suffix);
     if (kernel.size() > n && kernel.compare(kernel.size() - n, n, suffix) == 0)
       return {kernel.substr(0, kernel.size() - n), suffix};
@@ -366,8 +372,7 @@ std::vector<Launch> lower_steps(const Program& p, const Step& step, const Bindin
     const View x = stored(nn.op.values[0]), y = stored(nn.outputs[0]), out = stored(lin.outputs[0]);
     if (x.ld != x.width || y.ld != y.width) throw Refusal(step.name + ": a stored norm of rows that are not whole.");
     const Source& w = p.sources[lin.op.sources[0]];
-    const std::string wt = w.kind.type == "bf16" ? kW16 : w.kind.type == "f32" ? "" : "?";
-    if (wt == "?") throw Refusal(step.name + ": no kernel reads " + w.kind.type + " weights.");
+    const std::string wt = weight_form(w.kind.type, step.name);
     return {make("rmsnorm_rows" + wt,
                  {{"rows", m}, {"h", (double)x.width}, {"eps", nn.op.eps}, {"factor", nn.op.factor}},
                  {x.ptr(), weight(p.sources[nn.op.sources[0]].name), y.ptr()}),
@@ -381,8 +386,7 @@ std::vector<Launch> lower_steps(const Program& p, const Step& step, const Bindin
   if (routed_route || routed_gate) {
     const Node& lr = node("LinearRouted");
     const Source& t = p.sources[lr.op.sources[0]];
-    const std::string tsuf = t.kind.type == "bf16" ? kW16 : t.kind.type == "f32" ? "" : "?";
-    if (tsuf == "?") throw Refusal(step.name + ": no kernel reads " + t.kind.type + " weights.");
+    const std::string tsuf = weight_form(t.kind.type, step.name);
     const uint64_t n = t.kind.dims[0], kk = t.kind.dims[1];
     const View ids = stored(lr.op.values[0]), y = stored(lr.outputs[0]);
     const uint64_t k = ids.width;

@@ -40,8 +40,8 @@ std::vector<Launch> prefill_launches(const LlamaLaunchDesc& d, const PrefillDesc
   // model's element types.
   std::map<std::string, std::vector<const Launch*>> by;
   for (const Launch& L : decode) by[kernel_form(L.kernel).first].push_back(&L);
-  const std::string wsuf = s.weights == "bf16" ? kW16 : "";
-  const std::string csuf = s.cache == "bf16" ? kKV16 : "";
+  const std::string wsuf = weight_form(s.weights, "prefill");
+  const std::string csuf = cache_form(s.cache, "prefill");
   auto need = [&](const std::string& k, uint64_t i) -> const Launch& {
     auto it = by.find(k);
     if (it == by.end() || it->second.size() <= i) throw Refusal("prefill: the decode step has no " + k + " launch.");

@@ -33,7 +33,8 @@ from __future__ import annotations
 import numpy as np
 
 from . import _native as N
-from .engine import KV16, W16, Launch, Llama, kernel_form
+from .engine import Launch, Llama, kernel_form
+from .target import CACHE_SUFFIX, WEIGHT_SUFFIX
 
 
 class Prefill:
@@ -54,11 +55,11 @@ class Prefill:
                 raise N.Refused(N.FKC_ERR_ARGUMENT, f"prefill: the GEMM's K ({what} {k}) is not a multiple of 32.")
         # The layers' TF32 halves, laid out as the weight arena, a layer a
         # launch.
-        # (bf16 weights: the widened weight is the high half, the low half 0.)
+        # (16-bit weights: the widened weight is the high half, the low half 0.)
         per = eng.layer_elems
         self.w_hi = ctx.alloc(4 * s.layers * per)
         self.w_lo = ctx.alloc(4 * s.layers * per)
-        split = "split_tf32" + (W16 if eng.wb == 2 else "")
+        split = "split_tf32" + WEIGHT_SUFFIX[eng.s.weights]
         for l in range(s.layers):
             at = 4 * l * per
             ctx.launch(split, {"n": per}, [eng.arena.ptr + eng.wb * l * per, self.w_hi.ptr + at, self.w_lo.ptr + at])
@@ -134,8 +135,8 @@ class Prefill:
         by = {}
         for L in eng.launches:
             by.setdefault(kernel_form(L.kernel)[0], []).append(L)
-        wsuf = W16 if eng.wb == 2 else ""
-        csuf = KV16 if eng.cb == 2 else ""
+        wsuf = WEIGHT_SUFFIX[eng.s.weights]
+        csuf = CACHE_SUFFIX[eng.s.cache]
         g0 = by["gather"][0]
         out = [Launch(g0.kernel, dict(g0.params, m=m), [g0.bufs[0], tok, self.x.ptr])]
         if "attend_decode" in by:  # the decode step fused them: split its launches back into the two steps

@@ -2,8 +2,8 @@
 builder: one layer (RMSNorm, q/k/v, RoPE, KV store, attention, o, residual,
 RMSNorm, SiLU-gated FFN, residual), the embedding, and the head (final
 norm, tied LM head, greedy token). Activations are f32; the weights and the
-Ring KV caches are f32 (the BASELINE configurations) or bf16 (the
-reference's own element types)."""
+KV caches are f32 (the BASELINE configurations), bf16 (the reference's own
+element types) or f16."""
 
 from __future__ import annotations
 
@@ -28,8 +28,12 @@ class LlamaShape:
     slots: int = 1  # sequences the ring holds
     length: int = 4096  # ring length
     positions: int = 4096  # bound of the positions a row may have
-    weights: str = "f32"  # every weight's element type: "f32", or "bf16" (the reference's, Build.hs:171-175)
-    cache: str = "f32"  # the KV caches' element type: "f32", or "bf16" (CacheBF16, Graph.hs:165-180)
+    # Every weight's element type: "f32", "bf16" (the reference's,
+    # Build.hs:171-175) or "f16" (Check.hs:105-111).
+    weights: str = "f32"
+    # The KV caches' element type: "f32", "bf16" (CacheBF16) or "f16"
+    # (CacheF16, Graph.hs:165-180).
+    cache: str = "f32"
     # A paged cache (Graph.hs:144-152) instead of the ring: a pool of `blocks`
     # blocks of `block_size` positions a layer, which each row lists in its
     # block table of table_len entries. 0: the ring of `slots` and `length`.

@@ -40,7 +40,7 @@ enum {
 };
 
 /* The library's ABI version (this header's FKH_ABI_VERSION). */
-#define FKH_ABI_VERSION 5
+#define FKH_ABI_VERSION 6
 FKH_API int fkh_abi_version(void);
 
 /* A Llama-shaped model (the shapes of the programs the engine plans). */
@@ -48,8 +48,10 @@ typedef struct {
   uint64_t d_model, heads, kv_heads, head_dim, ffn, vocab, layers;
   double theta, eps;
   uint64_t slots, length, positions;
-  int weights_bf16; /* every weight bf16 (the reference's element type), else f32 */
-  int cache_bf16;   /* the KV caches bf16 (CacheBF16), else f32 */
+  /* Element types: 0 f32, 1 bf16, 2 f16 (weights: Check.hs:105-111, bf16 the
+   * reference's own; caches: CacheElem, Graph.hs:169-180). */
+  int weights_type; /* every weight's */
+  int cache_type;   /* the KV caches' */
   /* A paged cache (Paged, Graph.hs:144-152): a pool of `blocks` blocks of
    * `block_size` positions a layer, each row's block table of
    * ceil(positions / block_size) entries; block_size 0: the ring. */

@@ -59,6 +59,8 @@ void fko_softmax_rows(const float *x, uint32_t rows, uint32_t h, float *y, int t
 void fko_gemm_tile(const float *a, uint32_t M, uint32_t K, const float *b, uint32_t N, float *c, int threads);
 float fko_widen_bf16(uint16_t b);
 uint16_t fko_narrow_bf16(float x);
+float fko_widen_f16(uint16_t h);
+uint16_t fko_narrow_f16(float x);
 void fko_gemv_bf16(const uint16_t *w, uint32_t n, uint32_t k, const uint16_t *x, uint32_t m, uint32_t pack,
                    uint32_t split, uint16_t *y, int threads);
 void fko_gemv(const float *w, uint32_t n, uint32_t k, const float *x, uint32_t m,

@@ -341,6 +341,62 @@ uint16_t fko_narrow_bf16(float x) {
   return (uint16_t)((w + 0x7FFFu + lsb) >> 16);
 }
 
+/* binary16 <-> binary32. Widening is exact; a NaN comes out quiet, its sign */
+/* and payload kept (widenF16, Numerics.hs:51-66). Narrowing rounds to       */
+/* nearest, ties to even, with gradual underflow; past the largest finite    */
+/* value by half an ulp or more to infinity; a NaN keeps its sign and top 9  */
+/* payload bits and comes out quiet (narrowF16, Numerics.hs:100-130).        */
+
+float fko_widen_f16(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  const uint32_t e = (h >> 10) & 0x1Fu;
+  uint32_t m = h & 0x3FFu, w;
+  if (e == 0x1F)
+    w = m ? 0x7FC00000u | (m << 13) : 0x7F800000u;
+  else if (e)
+    w = ((e + 112u) << 23) | (m << 13);
+  else if (!m)
+    w = 0;
+  else {
+    /* m * 2^-24 = (m << s) * 2^(-24 - s): with the leading 1 at bit 10 that */
+    /* is 1.f * 2^(-14 - s), biased exponent 113 - s.                         */
+    uint32_t s = 0;
+    while (!(m & 0x400u)) {
+      m <<= 1;
+      ++s;
+    }
+    w = ((113u - s) << 23) | ((m & 0x3FFu) << 13);
+  }
+  w |= sign;
+  float f;
+  memcpy(&f, &w, 4);
+  return f;
+}
+
+/* kept rounded up when what was shifted off is past half, or half and kept */
+/* odd.                                                                     */
+static uint32_t round_even(uint32_t kept, uint32_t rest, uint32_t half) {
+  return rest > half || (rest == half && (kept & 1u)) ? kept + 1u : kept;
+}
+
+uint16_t fko_narrow_f16(float x) {
+  uint32_t w;
+  memcpy(&w, &x, 4);
+  const uint16_t sign = (uint16_t)((w >> 16) & 0x8000u);
+  const int e = (int)((w >> 23) & 0xFFu);
+  const uint32_t m = w & 0x7FFFFFu;
+  if (e == 0xFF) return (uint16_t)(sign | (m ? 0x7E00u | (m >> 13) : 0x7C00u));
+  const int unbiased = e - 127;
+  if (unbiased >= 16) return (uint16_t)(sign | 0x7C00u);
+  if (unbiased >= -14) /* a carry out of the mantissa moves the exponent, up to infinity */
+    return (uint16_t)(sign | round_even(((uint32_t)(unbiased + 15) << 10) | (m >> 13), m & 0x1FFFu, 0x1000u));
+  /* Subnormal or zero: in units of 2^-24 the value is (1.m) * 2^(unbiased + 24). */
+  const int shift = -(unbiased + 1);
+  if (e == 0 || shift > 24) return sign;
+  const uint32_t full = m | 0x800000u;
+  return (uint16_t)(sign | round_even(full >> shift, full & ((1u << shift) - 1u), 1u << (shift - 1)));
+}
+
 void fko_gemv_bf16(const uint16_t *w, uint32_t n, uint32_t k, const uint16_t *x, uint32_t m, uint32_t pack,
                    uint32_t split, uint16_t *y, int threads) {
   const uint32_t packs = k / pack, chains = pack / 4;

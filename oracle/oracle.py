@@ -48,7 +48,8 @@ def build() -> str:
 def lib():
     global _lib
     if _lib is None:
-        if not os.path.exists(_LIB_PATH):
+        sources = [os.path.join(_HERE, f) for f in ("fko_cpu.c", "fko_eval.c", "fko.h", "Makefile")]
+        if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < max(map(os.path.getmtime, sources)):
             build()
         L = ctypes.CDLL(_LIB_PATH)
         sig = {
@@ -72,6 +73,8 @@ def lib():
             "fko_gemm_tile": (None, [_f32p, _u32, _u32, _f32p, _u32, _f32p, _int]),
             "fko_widen_bf16": (_f32, [ctypes.c_uint16]),
             "fko_narrow_bf16": (ctypes.c_uint16, [_f32]),
+            "fko_widen_f16": (_f32, [ctypes.c_uint16]),
+            "fko_narrow_f16": (ctypes.c_uint16, [_f32]),
             "fko_rope_tables": (None, [_f64, _u32, _u32, _u32, _f32p, _f32p]),
             "fko_rope": (None, [_f32p, _u32, _u32, _u32, _u32, _u32p, _f32p, _f32p, _f32p]),
             "fko_kv_store_ring": (None, [_f32p, _u32, _u32, _u32, _u32, _u32p, _u32p, _f32p]),
@@ -224,6 +227,98 @@ def widen_bf16(b) -> np.ndarray:
     nan = ((w & 0x7F800000) == 0x7F800000) & ((w & 0x007FFFFF) != 0)
     w[nan] |= 0x00400000
     return w.view(np.float32)
+
+
+def narrow_f16(a) -> np.ndarray:
+    """binary32 -> binary16 bits: nearest, ties to even, gradual underflow,
+    half an ulp past the largest finite value or more to infinity, a NaN
+    quiet with its sign and top payload bits (narrowF16,
+    src/FuryKernel/Numerics.hs:100-130), vectorised on the bits."""
+    a = np.ascontiguousarray(a, np.float32)
+    w = a.view(np.uint32).astype(np.int64)
+    sign = (w >> 16) & 0x8000
+    e = (w >> 23) & 0xFF
+    m = w & 0x7FFFFF
+    unbiased = e - 127
+
+    def round_even(kept, rest, half):
+        return kept + ((rest > half) | ((rest == half) & ((kept & 1) == 1)))
+
+    out = np.zeros(a.shape, np.int64)
+    normal = (unbiased >= -14) & (unbiased < 16) & (e != 0xFF)
+    out[normal] = round_even(((unbiased[normal] + 15) << 10) | (m[normal] >> 13), m[normal] & 0x1FFF, 0x1000)
+    shift = -(unbiased + 1)
+    sub = (unbiased < -14) & (e != 0) & (shift <= 24)
+    full = m[sub] | 0x800000
+    s = shift[sub]
+    out[sub] = round_even(full >> s, full & ((1 << s) - 1), 1 << (s - 1))
+    out[(unbiased >= 16) & (e != 0xFF)] = 0x7C00
+    out[(e == 0xFF) & (m == 0)] = 0x7C00
+    nan = (e == 0xFF) & (m != 0)
+    out[nan] = 0x7E00 | (m[nan] >> 13)
+    return (out | sign).astype(np.uint16)
+
+
+def widen_f16(h) -> np.ndarray:
+    """binary16 bits -> binary32, exact, a NaN quiet with its sign and
+    payload (widenF16, src/FuryKernel/Numerics.hs:51-66), vectorised."""
+    h = np.ascontiguousarray(h, np.uint16)
+    out = h.view(np.float16).astype(np.float32)
+    bits = h.astype(np.uint32)
+    nan = ((bits & 0x7C00) == 0x7C00) & ((bits & 0x3FF) != 0)
+    ov = out.view(np.uint32)
+    ov[nan] = ((bits[nan] & 0x8000) << 16) | 0x7FC00000 | ((bits[nan] & 0x3FF) << 13)
+    return out
+
+
+def _round_to_grid(x, lowest: int, digits: int, overflow: float):
+    """binary64 values rounded once, to nearest with ties to even, to a
+    format whose significands have `digits` bits after the leading one and
+    whose exponents go down to `lowest` (gradual underflow below it); a
+    rounded magnitude at or past `overflow` is infinity. NaNs, infinities
+    and zeros are kept."""
+    x = np.asarray(x, np.float64)
+    out = x.copy()
+    ok = np.isfinite(x) & (x != 0)
+    _, exp = np.frexp(x[ok])
+    e = np.maximum(exp - 1, lowest)  # the leading bit's exponent, floored at the normal range
+    ulp = np.ldexp(1.0, e - digits)
+    rounded = np.rint(x[ok] / ulp) * ulp  # exact scalings; rint ties to even
+    rounded[np.abs(rounded) >= overflow] = np.copysign(np.inf, rounded[np.abs(rounded) >= overflow])
+    out[ok] = rounded
+    return out
+
+
+def narrow_f16_f64(x) -> np.ndarray:
+    """binary64 -> binary16 bits in one rounding, not through binary32
+    (narrowF16Double, src/FuryKernel/Numerics.hs:132-155): nearest, ties to
+    even, gradual underflow, overflow to infinity, the sign of zero kept, a
+    NaN quiet with its sign and top payload bits."""
+    x = np.asarray(x, np.float64)
+    with np.errstate(over="ignore"):
+        bits = _round_to_grid(x, -14, 10, 65536.0).astype(np.float16).view(np.uint16)
+    w = x.view(np.uint64)
+    nan = np.isnan(x)
+    bits[nan] = (((w[nan] >> 48) & 0x8000) | 0x7E00 | ((w[nan] >> 42) & 0x1FF)).astype(np.uint16)
+    return bits
+
+
+def round_bf16_f64(x) -> np.ndarray:
+    """binary64 values rounded once to bfloat16's values, as binary64
+    (roundBF16, src/FuryKernel/Program/Eval.hs:669-682): nearest, ties to
+    even, the exponent floored at -126, a magnitude of 2^128 or more
+    infinity."""
+    return _round_to_grid(x, -126, 7, 2.0 ** 128)
+
+
+def round_to(t: str, x) -> np.ndarray:
+    """binary64 values rounded to a cache's element type, directly from the
+    binary64 (roundTo, src/FuryKernel/Program/Eval.hs:930-934)."""
+    if t == "bf16":
+        return round_bf16_f64(x)
+    if t == "f16":
+        return widen_f16(narrow_f16_f64(x)).astype(np.float64)
+    raise ValueError(f"no rounding to {t}")
 
 
 def rope_tables(theta: float, d: int, rotated: int, positions: int):

@@ -12,22 +12,39 @@ import numpy as np
 from oracle import oracle as O
 
 
-def download_f32(eng, ptr, n, elem_bytes):
-    """n elements at a device address as f32: bf16 ones widened (exact)."""
+def widen(t: str, bits) -> np.ndarray:
+    """16-bit elements of type t ("bf16", "f16") as f32, exactly."""
+    return O.widen_bf16(bits) if t == "bf16" else O.widen_f16(bits)
+
+
+def narrow(t: str, a) -> np.ndarray:
+    """f32 values rounded to type t ("bf16", "f16"), as its bits."""
+    return O.narrow_bf16(a) if t == "bf16" else O.narrow_f16(a)
+
+
+def rounded(t: str, a) -> np.ndarray:
+    """f32 values as an element of type t holds them."""
+    a = np.asarray(a, np.float32)
+    return a if t == "f32" else widen(t, narrow(t, a)).reshape(a.shape)
+
+
+def download_f32(eng, ptr, n, t):
+    """n elements of type t ("f32", "bf16", "f16") at a device address as
+    f32: 16-bit ones widened (exact)."""
     from furykernel_b200 import _native as N
 
-    raw = np.empty(n, np.float32 if elem_bytes == 4 else np.uint16)
+    raw = np.empty(n, np.float32 if t == "f32" else np.uint16)
     N.check(N.lib().fkc_buf_download(eng.ctx.handle, raw.ctypes.data, ptr, raw.nbytes))
-    return raw if elem_bytes == 4 else O.widen_bf16(raw)
+    return raw if t == "f32" else widen(t, raw)
 
 
 def host_model(eng):
-    """The engine's weights, per layer, as the device holds them (bf16
+    """The engine's weights, per layer, as the device holds them (16-bit
     weights widened to f32, exactly)."""
     s = eng.s
     d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
     wb = getattr(eng, "wb", 4)
-    flat = download_f32(eng, eng.arena.ptr, eng.arena.nbytes // wb, wb)
+    flat = download_f32(eng, eng.arena.ptr, eng.arena.nbytes // wb, s.weights)
     layers = []
     for l in range(s.layers):
         base = l * eng.layer_elems
@@ -52,15 +69,14 @@ def host_model(eng):
 
 
 def host_caches(eng):
-    """The KV caches as the device holds them, as f32 (bf16 widened):
+    """The KV caches as the device holds them, as f32 (16-bit widened):
     [layers, slots, kv_heads, length, d] rings, or [layers, blocks,
     kv_heads, block_size, d] pools."""
     s = eng.s
     units, unit_len = (s.blocks, s.block_size) if getattr(s, "paged", False) else (s.slots, s.length)
     n = s.layers * units * s.kv_heads * unit_len * s.head_dim
-    cb = getattr(eng, "cb", 4)
-    k = download_f32(eng, eng.kbase, n, cb)
-    v = download_f32(eng, eng.vbase, n, cb)
+    k = download_f32(eng, eng.kbase, n, s.cache)
+    v = download_f32(eng, eng.vbase, n, s.cache)
     shp = (s.layers, units, s.kv_heads, unit_len, s.head_dim)
     return k.reshape(shp), v.reshape(shp)
 
@@ -93,11 +109,13 @@ def splits_of(eng):
 
 def oracle_decode(eng, layers, embed, final_norm, kcache, vcache, tokens, pos, slot, threads=0):
     """The CPU target's bits for one decode step; the caches are updated in
-    place as the step's stores leave them (bf16 caches: each stored element
-    rounded to bf16, Eval.hs:9). Returns (ids, logits, x)."""
+    place as the step's stores leave them (16-bit caches: each stored element
+    rounded to the cache's type, Eval.hs:9). Returns (ids, logits, x)."""
     s = eng.s
-    as_stored = (lambda a: O.widen_bf16(O.narrow_bf16(a)).reshape(a.shape)) if getattr(eng, "cb", 4) == 2 \
-        else (lambda a: a)
+
+    def as_stored(a):
+        return rounded(s.cache, a)
+
     threads = threads or O.threads_default()
     d, qw, kvw, f, hd = s.d_model, s.q_width, s.kv_width, s.ffn, s.head_dim
     cos_t, sin_t = O.rope_tables(s.theta, hd, hd // 2, s.positions)
@@ -193,6 +211,25 @@ def oracle_decode_tp(s, world, layers, embed, final_norm, kcache, vcache, tokens
     return O.argmax(logits), logits, x
 
 
+def may_store(t, exact, bound, got) -> bool:
+    """Whether a kernel may have stored `got` for elements of the given
+    exact values and bounds in a cache of type t (mayStore,
+    src/FuryKernel/Program/Eval.hs:924-944): an unbounded element anything;
+    a NaN exact value a NaN; else, f32: within the widened bound; 16-bit:
+    between the roundings to t of the exact value less and plus it."""
+    exact, bound, got = (np.asarray(a, np.float64) for a in (exact, bound, got))
+    e = O.widened(bound)
+    free = np.isinf(bound)
+    nan = np.isnan(exact) & ~free
+    rest = ~free & ~nan
+    if t == "f32":
+        ok = np.abs(got[rest] - exact[rest]) <= e[rest]
+    else:
+        lo, hi = O.round_to(t, exact[rest] - e[rest]), O.round_to(t, exact[rest] + e[rest])
+        ok = (lo <= got[rest]) & (got[rest] <= hi)
+    return bool(np.all(ok) and np.all(np.isnan(got[nan])))
+
+
 def referee_decode(eng, layers, embed, final_norm, kcache_after, vcache_after, tokens, pos, slot):
     """The f64 evaluator's values and bounds for the same step, attention
     reading the caches as the kernels left them (evaluateStored,
@@ -216,7 +253,7 @@ def referee_decode(eng, layers, embed, final_norm, kcache_after, vcache_after, t
                     exact = vals[0][r, h * hd:(h + 1) * hd]
                     bound = vals[1][r, h * hd:(h + 1) * hd]
                     got = cache[at].astype(np.float64)
-                    stored_ok &= bool(np.all(np.abs(got - exact) <= O.widened(bound)))
+                    stored_ok &= may_store(s.cache, exact, bound, got)
         qr = O.r_rope(q, hd, hd // 2, s.theta, pos)
         att = O.r_attend(qr, s.heads, s.kv_heads, hd, s.length, pos, slot, kc.astype(np.float64),
                          vc.astype(np.float64), 1.0 / math.sqrt(hd))

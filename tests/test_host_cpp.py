@@ -38,6 +38,9 @@ SHAPES = [
     LlamaShape(d_model=512, heads=4, kv_heads=2, head_dim=128, ffn=1024, vocab=3000, layers=2, positions=96,
                blocks=64, block_size=16),
     LlamaShape(layers=32, positions=4096, blocks=4096, block_size=16, weights="bf16", cache="bf16"),
+    LlamaShape(weights="f16", cache="f16"),
+    LlamaShape(d_model=512, heads=4, kv_heads=2, head_dim=128, ffn=1024, vocab=3000, layers=2, positions=96,
+               blocks=64, block_size=16, weights="f16", cache="bf16"),
     LlamaShape(d_model=512, heads=4, kv_heads=4, head_dim=128, ffn=256, vocab=3000, layers=2, slots=2, length=96,
                positions=96, experts=8, top_k=2),
 ]
@@ -148,7 +151,7 @@ def fake_engine(full, batch, rank=0, world=1, peer_exchange=True, fuse_attention
                             ffn=full.ffn // world)
     e.full, e.s, e.m, e.rank, e.world = full, s, batch, rank, world
     e.ctx = SimpleNamespace(sms=sms)
-    e.wb, e.cb = (2 if full.weights == "bf16" else 4), (2 if full.cache == "bf16" else 4)
+    e.wb, e.cb = (4 if full.weights == "f32" else 2), (4 if full.cache == "f32" else 2)
     e.gate_up_interleaved = batch <= 64
     e.peer_exchange = world > 1 and batch <= 4 and peer_exchange
     e.vocab_local = full.vocab // world
@@ -226,6 +229,17 @@ CASES = (
        for b in (1, 5)]
     + [(dataclasses.replace(small(b), experts=8, top_k=2, weights="bf16", cache="bf16"), b, 0, 1, True, None)
        for b in (1, 12)]
+    # f16 weights and f16 caches (and mixed with bf16): every batch form, tensor parallelism, paged, experts
+    + [(dataclasses.replace(small(b), weights="f16", cache="f16"), b, 0, 1, True, f)
+       for b, f in ((1, None), (3, False), (5, None), (9, True), (65, None))]
+    + [(dataclasses.replace(tp_shape(b), weights="f16", cache="f16"), b, r, 2, peer, None) for b in (1, 16)
+       for r in (0, 1) for peer in (True, False)]
+    + [(dataclasses.replace(small(b), weights=w, cache=c), b, 0, 1, True, None) for b in (1, 8)
+       for w, c in (("f16", "bf16"), ("bf16", "f16"), ("f32", "f16"))]
+    + [(dataclasses.replace(small(b), blocks=64, block_size=16, weights="f16", cache="f16"), b, 0, 1, True, None)
+       for b in (1, 9)]
+    + [(dataclasses.replace(small(b), experts=8, top_k=2, weights="f16", cache="f16"), b, 0, 1, True, None)
+       for b in (1, 12)]
 )
 
 
@@ -301,6 +315,11 @@ PREFILL_CASES = (
     + [(dataclasses.replace(small(b), blocks=64, block_size=16, cache=c), b, 0, 1, True, 96, one, m)
        for b, one, m, c in ((1, False, 90, "f32"), (1, True, 96, "f32"), (4, True, 50, "bf16"), (8, False, 96, "bf16"))]
     + [(dataclasses.replace(tp_shape(1), blocks=32, block_size=8), 1, 1, 2, True, 32, False, 32)]
+    # f16 weights and caches, ring and paged
+    + [(dataclasses.replace(small(b), weights="f16", cache="f16"), b, 0, 1, True, 128, one, m)
+       for b, one, m in ((1, False, 100), (1, True, 64))]
+    + [(dataclasses.replace(small(4), blocks=64, block_size=16, weights="f16", cache="f16"), 4, 0, 1, True, 96,
+        True, 50)]
 )
 
 

@@ -13,6 +13,7 @@ import os
 import numpy as np
 import pytest
 
+from furykernel_b200.target import WEIGHT_SUFFIX
 from oracle import oracle as O
 from tests import model_check as MC
 
@@ -70,14 +71,17 @@ def test_gemv_routed_shared_and_per_rank(ctx, entries, n, kk, m, k, split):
         ctx.launch("gemv_routed", {"entries": entries, "n": n, "kk": kk, "m": m, "k": k, "split": split, "ldx": xw,
                                    "ldy": k * n, "per_rank": per_rank}, [td, idd, xd, yd])
         assert same_bits(yd.download(), O.gemv_routed(table, ids, x, split, THREADS))
-        # The bf16 table form: the f32 arithmetic over the widened entries.
-        bits = O.narrow_bf16(table).reshape(table.shape)
-        bd = ctx.to_device(bits)
-        ctx.launch("gemv_routed_wbf16", {"entries": entries, "n": n, "kk": kk, "m": m, "k": k, "split": split,
-                                         "ldx": xw, "ldy": k * n, "per_rank": per_rank}, [bd, idd, xd, yd])
-        widened = O.widen_bf16(bits).reshape(table.shape)
-        assert same_bits(yd.download(), O.gemv_routed(widened, ids, x, split, THREADS))
-        for b in (xd, yd, bd):
+        # The 16-bit table forms: the f32 arithmetic over the widened entries.
+        for t in ("bf16", "f16"):
+            bits = MC.narrow(t, table).reshape(table.shape)
+            bd = ctx.to_device(bits)
+            ctx.launch("gemv_routed" + WEIGHT_SUFFIX[t], {"entries": entries, "n": n, "kk": kk, "m": m, "k": k,
+                                                         "split": split, "ldx": xw, "ldy": k * n,
+                                                         "per_rank": per_rank}, [bd, idd, xd, yd])
+            widened = MC.widen(t, bits).reshape(table.shape)
+            assert same_bits(yd.download(), O.gemv_routed(widened, ids, x, split, THREADS))
+            bd.free()
+        for b in (xd, yd):
             b.free()
     td.free()
     idd.free()
@@ -100,7 +104,7 @@ def test_gated_gelu_and_combine(ctx):
 
 
 @pytest.mark.parametrize("batch,experts,top_k,weights", [(1, 8, 2, "f32"), (3, 8, 2, "f32"), (9, 16, 4, "f32"),
-                                                         (2, 8, 2, "bf16"), (12, 8, 2, "bf16")])
+                                                         (2, 8, 2, "bf16"), (12, 8, 2, "bf16"), (5, 8, 2, "f16")])
 def test_moe_model_decode_step(ctx, batch, experts, top_k, weights):
     """A decode step of a model whose FFN is routed experts, captured as a
     graph, against the oracle's decode: the same ids, logits and residual

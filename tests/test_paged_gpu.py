@@ -1,5 +1,5 @@
-"""Parity of the paged-cache kernels (`*_paged`, f32 and bf16 caches) on a
-B200, through the C ABI.
+"""Parity of the paged-cache kernels (`*_paged`, f32, bf16 and f16 caches)
+on a B200, through the C ABI.
 
 A paged cache holds a row's position t in block table[t / block_size] of a
 pool (src/FuryKernel/Program/Eval.hs:592-602); the kernels keep the ring
@@ -18,6 +18,7 @@ import os
 import numpy as np
 import pytest
 
+from furykernel_b200.target import CACHE_SUFFIX
 from oracle import oracle as O
 from tests import model_check as MC
 
@@ -50,13 +51,13 @@ def disjoint_tables(seed, m, table_len, blocks):
     return perm.reshape(m, table_len).astype(np.uint32)
 
 
-@pytest.mark.parametrize("bf16", [False, True])
+@pytest.mark.parametrize("t", ["f32", "bf16", "f16"])
 @pytest.mark.parametrize("m,heads,kv_heads,block_size,positions,chunk", [
     (2, 4, 2, 16, [5, 40], 16),
     (3, 8, 8, 32, [0, 129, 191], 64),
     (1, 32, 32, 16, [2047], 128),
 ])
-def test_paged_store_and_attention(ctx, bf16, m, heads, kv_heads, block_size, positions, chunk):
+def test_paged_store_and_attention(ctx, t, m, heads, kv_heads, block_size, positions, chunk):
     d = 128
     width = (heads + 2 * kv_heads) * d
     qkv = O.normal(101, m * width).reshape(m, width)
@@ -68,9 +69,9 @@ def test_paged_store_and_attention(ctx, bf16, m, heads, kv_heads, block_size, po
     shape = (blocks, kv_heads, block_size, d)
     kpool = O.normal(103, int(np.prod(shape))).reshape(shape)
     vpool = O.normal(104, int(np.prod(shape))).reshape(shape)
-    if bf16:
-        kbits, vbits = O.narrow_bf16(kpool).reshape(shape), O.narrow_bf16(vpool).reshape(shape)
-        kpool, vpool = O.widen_bf16(kbits).reshape(shape), O.widen_bf16(vbits).reshape(shape)
+    if t != "f32":
+        kbits, vbits = MC.narrow(t, kpool).reshape(shape), MC.narrow(t, vpool).reshape(shape)
+        kpool, vpool = MC.widen(t, kbits).reshape(shape), MC.widen(t, vbits).reshape(shape)
         dk, dv = ctx.to_device(kbits), ctx.to_device(vbits)
     else:
         dk, dv = ctx.to_device(kpool), ctx.to_device(vpool)
@@ -81,7 +82,7 @@ def test_paged_store_and_attention(ctx, bf16, m, heads, kv_heads, block_size, po
     pm, pl = ctx.empty(m * heads * max_splits), ctx.empty(m * heads * max_splits)
     pa = ctx.empty(m * heads * max_splits * d)
     out = ctx.empty((m, heads * d))
-    suffix = "_kvbf16" if bf16 else ""
+    suffix = CACHE_SUFFIX[t]
     pg = {"block_size": block_size, "table_len": table_len, "blocks": blocks}
     ctx.launch("kv_store_paged" + suffix,
                dict(pg, m=m, kv_heads=kv_heads, d=d, rotated=d // 2, ldq=width, k_off=heads * d,
@@ -94,7 +95,9 @@ def test_paged_store_and_attention(ctx, bf16, m, heads, kv_heads, block_size, po
                                   "ldo": heads * d}, [pm, pl, pa, dpos, out])
 
     # The oracle: each row's blocks as a ring, the stores, the ring attention.
-    as_stored = (lambda a: O.widen_bf16(O.narrow_bf16(a)).reshape(a.shape)) if bf16 else (lambda a: a)
+    def as_stored(a):
+        return MC.rounded(t, a)
+
     kr, vr = MC.pool_to_rings(kpool, tables), MC.pool_to_rings(vpool, tables)
     length, rows = table_len * block_size, np.arange(m, dtype=np.uint32)
     krot = O.rope(qkv[:, heads * d:(heads + kv_heads) * d], kv_heads, d, d // 2, pos, cos_t, sin_t)
@@ -104,9 +107,9 @@ def test_paged_store_and_attention(ctx, bf16, m, heads, kv_heads, block_size, po
     kwant, vwant = kpool.copy(), vpool.copy()
     MC.rings_to_pool(kr, tables, kwant)
     MC.rings_to_pool(vr, tables, vwant)
-    if bf16:
-        assert np.array_equal(dk.download(), O.narrow_bf16(kwant).reshape(shape))
-        assert np.array_equal(dv.download(), O.narrow_bf16(vwant).reshape(shape))
+    if t != "f32":
+        assert np.array_equal(dk.download(), MC.narrow(t, kwant).reshape(shape))
+        assert np.array_equal(dv.download(), MC.narrow(t, vwant).reshape(shape))
     else:
         assert same_bits(dk.download(), kwant) and same_bits(dv.download(), vwant)
     qrot = O.rope(qkv[:, :heads * d], heads, d, d // 2, pos, cos_t, sin_t)
@@ -117,8 +120,8 @@ def test_paged_store_and_attention(ctx, bf16, m, heads, kv_heads, block_size, po
         b.free()
 
 
-@pytest.mark.parametrize("bf16", [False, True])
-def test_paged_prompt_attention_matches_the_ring_form(ctx, bf16):
+@pytest.mark.parametrize("t", ["f32", "bf16", "f16"])
+def test_paged_prompt_attention_matches_the_ring_form(ctx, t):
     """One prompt's rows through its block table: the same bits as the ring
     prompt kernel over the blocks gathered into a slot."""
     m, heads, kv_heads, d, block_size = 70, 4, 2, 128, 16
@@ -131,9 +134,9 @@ def test_paged_prompt_attention_matches_the_ring_form(ctx, bf16):
     shape = (blocks, kv_heads, block_size, d)
     kpool = O.normal(113, int(np.prod(shape))).reshape(shape)
     vpool = O.normal(114, int(np.prod(shape))).reshape(shape)
-    if bf16:
-        kbits, vbits = O.narrow_bf16(kpool).reshape(shape), O.narrow_bf16(vpool).reshape(shape)
-        kpool, vpool = O.widen_bf16(kbits).reshape(shape), O.widen_bf16(vbits).reshape(shape)
+    if t != "f32":
+        kbits, vbits = MC.narrow(t, kpool).reshape(shape), MC.narrow(t, vpool).reshape(shape)
+        kpool, vpool = MC.widen(t, kbits).reshape(shape), MC.widen(t, vbits).reshape(shape)
         dk, dv = ctx.to_device(kbits), ctx.to_device(vbits)
     else:
         dk, dv = ctx.to_device(kpool), ctx.to_device(vpool)
@@ -146,7 +149,7 @@ def test_paged_prompt_attention_matches_the_ring_form(ctx, bf16):
     o_paged, o_ring = ctx.empty((m, heads * d)), ctx.empty((m, heads * d))
     common = {"m": m, "heads": heads, "kv_heads": kv_heads, "d": d, "rotated": d // 2, "ldq": width, "q_off": 0,
               "ldo": heads * d, "max_pos": m - 1, "scale": 1.0 / math.sqrt(d)}
-    ctx.launch("attend_prompt_paged" + ("_kvbf16" if bf16 else ""),
+    ctx.launch("attend_prompt_paged" + CACHE_SUFFIX[t],
                dict(common, block_size=block_size, table_len=table_len, blocks=blocks),
                [dq, dcos, dsin, dpos, dtab, dk, dv, o_paged])
     ctx.launch("attend_prompt", dict(common, length=length), [dq, dcos, dsin, dpos, dslot, rk, rv, o_ring])
@@ -155,7 +158,7 @@ def test_paged_prompt_attention_matches_the_ring_form(ctx, bf16):
         b.free()
 
 
-@pytest.mark.parametrize("batch,cache", [(1, "f32"), (3, "f32"), (9, "bf16"), (2, "bf16")])
+@pytest.mark.parametrize("batch,cache", [(1, "f32"), (3, "f32"), (9, "bf16"), (2, "bf16"), (4, "f16")])
 def test_paged_model_decode_step(ctx, batch, cache):
     """A decode step of a model with paged caches, captured as a graph,
     against the oracle's decode over the rows' blocks: the same ids, logits
