@@ -14,7 +14,7 @@ _LIB = None
 _PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_build", "libfurykernel_host.so")
 
 FKH_OK, FKH_ERR_ARGUMENT, FKH_ERR_SPACE, FKH_ERR_INTERNAL = 0, 1, 2, 3
-ABI_VERSION = 6
+ABI_VERSION = 7
 
 
 # The shape's element-type codes, in order (fkh_llama_shape).
@@ -49,7 +49,8 @@ class Desc(ctypes.Structure):
                [(n, ctypes.c_int) for n in ("gate_up_interleaved", "peer_exchange", "fuse_attention")] + \
                [(n, ctypes.c_uint64) for n in DESC_ADDRS] + [("part", ctypes.c_uint64 * 3)] + \
                [("splits", ctypes.POINTER(ctypes.c_uint32)), ("nsplits", ctypes.c_size_t)] + \
-               [(n, ctypes.c_uint64) for n in MOE_ADDRS]
+               [(n, ctypes.c_uint64) for n in MOE_ADDRS] + \
+               [("gated", ctypes.c_int), ("store_gelus", ctypes.c_int)]
 
 
 def lib():
@@ -143,10 +144,12 @@ def split_for(n_rows: int, k: int, sms: int) -> int:
 
 
 def _desc(full, batch, rank, world, sms, chunk, gate_up_interleaved, peer_exchange, fuse_attention, addrs,
-          splits=None) -> Desc:
+          splits=None, gated=False, store_gelus=False) -> Desc:
     """The descriptor; `splits` maps GEMV shapes (n, k) to a selection's
-    split-K (the array stays alive as the descriptor's `_keep`)."""
+    split-K (the array stays alive as the descriptor's `_keep`); `gated`
+    and `store_gelus` are the layer's plan options."""
     d = Desc()
+    d.gated, d.store_gelus = int(gated), int(store_gelus)
     if splits:
         flat = (ctypes.c_uint32 * (3 * len(splits)))(*[v for (n, k), s in sorted(splits.items()) for v in (n, k, s)])
         d.splits, d.nsplits = ctypes.cast(flat, ctypes.POINTER(ctypes.c_uint32)), len(splits)
@@ -184,10 +187,11 @@ def _collect(call, *args) -> list:
 
 
 def llama_launches(full, batch: int, rank: int, world: int, sms: int, chunk: int, gate_up_interleaved: bool,
-                   peer_exchange: bool, fuse_attention: bool, addrs: dict, splits=None) -> list:
+                   peer_exchange: bool, fuse_attention: bool, addrs: dict, splits=None, gated=False,
+                   store_gelus=False) -> list:
     """The decode step's launch list (fkh_llama_launches)."""
     d = _desc(full, batch, rank, world, sms, chunk, gate_up_interleaved, peer_exchange, fuse_attention, addrs,
-              splits)
+              splits, gated, store_gelus)
     return _collect(lib().fkh_llama_launches, ctypes.byref(d))
 
 

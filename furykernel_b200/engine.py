@@ -292,34 +292,42 @@ def lower_steps(p, step, b: Binding, tables: dict, attn: dict) -> list:
                        [x.ptr, b.weights[p.source(nn.op.sources[0]).name], y.ptr]),
                 Launch("gemv" + wt, {"n": n, "k": k, "m": b.m, "split": attn.get("split", 1), "ldx": y.ld,
                                      "ldy": out.ld}, [b.weights[w.name], y.ptr, out.ptr])]
-    if kinds in ([("Anchor", "LinearRouted"), ("Recompute", "Route")],
-                 [("Anchor", "LinearRouted"), ("Recompute", "GatedGelu")]):
-        lr = node("LinearRouted")
-        t = p.source(lr.op.sources[0])
-        tsuf = _weight_suffix(step, t.kind.type)
-        n, kk = t.kind.dims
-        ids_v, x_id = lr.op.values
-        ids, y = stored(ids_v), stored(lr.outputs[0])
-        k = ids.width
+    # Routed experts: the route, the GELU gate and the routed GEMV, each a
+    # step of its own (the gated plan's, Plan.hs:246-251, with or without
+    # stored gelus) or the route or the gate recomputed in the GEMV's step.
+    routed_shapes = ([("Recompute", "Route")], [("Recompute", "GatedGelu")], [("Anchor", "LinearRouted")],
+                     [("Anchor", "LinearRouted"), ("Recompute", "Route")],
+                     [("Anchor", "LinearRouted"), ("Recompute", "GatedGelu")])
+    if kinds in routed_shapes:
+        ops = {op for _, op in kinds}
         out = []
-        if kinds[1][1] == "Route":
+        if "Route" in ops:
             r = node("Route")
-            logits, ws = stored(r.op.values[0]), stored(r.outputs[1])
             if r.op.args[0].expert_scale is not None:
                 raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: no kernel scales a route's experts here.")
-            out.append(Launch("route_topk", {"m": b.m, "n": logits.width, "k": k, "ldx": logits.ld},
+            logits, ids, ws = stored(r.op.values[0]), stored(r.outputs[0]), stored(r.outputs[1])
+            out.append(Launch("route_topk", {"m": b.m, "n": logits.width, "k": ids.width, "ldx": logits.ld},
                               [logits.ptr, ids.ptr, ws.ptr]))
-            x = stored(x_id)
-        else:
+        if "GatedGelu" in ops:
             g = node("GatedGelu")
             gu, x = stored(g.op.values[0]), stored(g.outputs[0])
+            f = p.value(g.outputs[0]).shape.segment
             if gu.ld != gu.width or x.ld != x.width:
                 raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: a gate of rows that are not whole.")
-            out.append(Launch("gated_gelu", {"segments": b.m * k, "f": kk}, [gu.ptr, x.ptr]))
-        out.append(Launch("gemv_routed" + tsuf, {"entries": t.kind.entries, "n": n, "kk": kk, "m": b.m, "k": k,
-                                          "split": attn.get("split", 1), "ldx": x.ld, "ldy": y.ld,
-                                          "per_rank": int(x.width != kk)},
-                          [b.weights[t.name], ids.ptr, x.ptr, y.ptr]))
+            if f == 0 or x.width % f:
+                raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: a gate whose rows are not whole segments.")
+            out.append(Launch("gated_gelu", {"segments": b.m * (x.width // f), "f": f}, [gu.ptr, x.ptr]))
+        if "LinearRouted" in ops:
+            lr = node("LinearRouted")
+            t = p.source(lr.op.sources[0])
+            tsuf = _weight_suffix(step, t.kind.type)
+            n, kk = t.kind.dims
+            ids_v, x_id = lr.op.values
+            ids, x, y = stored(ids_v), stored(x_id), stored(lr.outputs[0])
+            out.append(Launch("gemv_routed" + tsuf, {"entries": t.kind.entries, "n": n, "kk": kk, "m": b.m,
+                                                     "k": ids.width, "split": attn.get("split", 1), "ldx": x.ld,
+                                                     "ldy": y.ld, "per_rank": int(x.width != kk)},
+                              [b.weights[t.name], ids.ptr, x.ptr, y.ptr]))
         return out
     if kinds == [("Recompute", "Add"), ("Recompute", "CombineRanks")]:
         c, a = node("CombineRanks"), node("Add")
@@ -360,7 +368,7 @@ class Llama:
     def __init__(self, ctx: N.Context, shape: LlamaShape, batch: int, seed: int = 2026, chunk: int = 32,
                  pdl: bool = True, prefill_kv: float | None = None, rank: int = 0, world: int = 1,
                  host_weights=None, peer_exchange: bool = True, fuse_attention: bool | None = None,
-                 selection: str | None = None):
+                 selection: str | None = None, gated: bool = False, store_gelus: bool = False):
         import dataclasses
 
         full = shape
@@ -371,6 +379,9 @@ class Llama:
         s = dataclasses.replace(full, heads=full.heads // world, kv_heads=full.kv_heads // world,
                                 ffn=full.ffn // world)
         self.ctx, self.full, self.s, self.m = ctx, full, s, batch
+        # The layer's plan options: a route in a step of its own (optGated),
+        # gelus stored by their own step (optStoreGelus).
+        self.gated, self.store_gelus = gated, store_gelus
         self.rank, self.world = rank, world
         # Bytes of a weight and of a cache element.
         self.wb = {"f32": 4, "bf16": 2, "f16": 2}.get(s.weights)
@@ -396,7 +407,8 @@ class Llama:
         self.vocab_local = full.vocab // world
         self.plans = {
             "embed": PL.plan(PL.DEFAULT, embed_program(full)),
-            "layer": PL.plan(PL.PlanOptions(sequence_rows=batch if s.slots == 1 else 1), layer_program(s)),
+            "layer": PL.plan(PL.PlanOptions(gated=gated, store_gelus=store_gelus,
+                                            sequence_rows=batch if s.slots == 1 else 1), layer_program(s)),
             "head": PL.plan(PL.DEFAULT, head_program(dataclasses.replace(full, vocab=self.vocab_local))),
         }
         # Weights: per layer [q;k;v], o, [gate;up], down, two norms; then the
@@ -568,7 +580,8 @@ class Llama:
         """fkh_llama_desc's fields: the shape, the batch, the rank, the
         choices and the addresses."""
         return (self.full, self.m, self.rank, self.world, self.ctx.sms, self.chunk, self.gate_up_interleaved,
-                self.peer_exchange, self.fuse_attention, self.launch_addresses(), getattr(self, "splits", None))
+                self.peer_exchange, self.fuse_attention, self.launch_addresses(), getattr(self, "splits", None),
+                getattr(self, "gated", False), getattr(self, "store_gelus", False))
 
     def _launches_restated(self) -> list:
         """The same launch list in Python (the restatement the host

@@ -307,6 +307,9 @@ struct LlamaLaunchDesc {
   // and weights, the experts' gate/up rows, their gate, their outputs.
   uint64_t mlp_in = 0, router_logits = 0, route_ids = 0, route_weights = 0, experts_gu = 0, experts_act = 0,
            experts_out = 0;
+  // The layer's plan options beyond the defaults (PlanOptions, Plan.hs:243-268):
+  // a route in a step of its own, gelus stored by their own step.
+  bool gated = false, store_gelus = false;
 };
 
 std::vector<Launch> llama_launches(const LlamaLaunchDesc& d);

@@ -120,6 +120,8 @@ fkh::LlamaLaunchDesc desc_of(const fkh_llama_desc& desc) {
   d.experts_gu = desc.experts_gu;
   d.experts_act = desc.experts_act;
   d.experts_out = desc.experts_out;
+  d.gated = desc.gated != 0;
+  d.store_gelus = desc.store_gelus != 0;
   if (desc.nsplits && !desc.splits) throw fkh::Refusal("nsplits without splits.");
   for (size_t i = 0; i < desc.nsplits; ++i) {
     const uint32_t s = desc.splits[3 * i + 2];

@@ -381,43 +381,51 @@ std::vector<Launch> lower_steps(const Program& p, const Step& step, const Bindin
                   {"ldx", (double)y.ld}, {"ldy", (double)out.ld}},
                  {weight(w.name), y.ptr(), out.ptr()})};
   }
+  // Routed experts: the route, the GELU gate and the routed GEMV, each a
+  // step of its own (the gated plan's, Plan.hs:246-251, with or without
+  // stored gelus) or the route or the gate recomputed in the GEMV's step.
+  const bool lone_route = kinds == KP{{"Recompute", "Route"}};
+  const bool lone_gate = kinds == KP{{"Recompute", "GatedGelu"}};
+  const bool lone_routed = kinds == KP{{"Anchor", "LinearRouted"}};
   const bool routed_route = kinds == KP{{"Anchor", "LinearRouted"}, {"Recompute", "Route"}};
   const bool routed_gate = kinds == KP{{"Anchor", "LinearRouted"}, {"Recompute", "GatedGelu"}};
-  if (routed_route || routed_gate) {
-    const Node& lr = node("LinearRouted");
-    const Source& t = p.sources[lr.op.sources[0]];
-    const std::string tsuf = weight_form(t.kind.type, step.name);
-    const uint64_t n = t.kind.dims[0], kk = t.kind.dims[1];
-    const View ids = stored(lr.op.values[0]), y = stored(lr.outputs[0]);
-    const uint64_t k = ids.width;
+  if (lone_route || lone_gate || lone_routed || routed_route || routed_gate) {
     std::vector<Launch> out;
-    View x;
-    if (routed_route) {
+    if (lone_route || routed_route) {
       const Node& r = node("Route");
       if (r.op.route.expert_scale) throw Refusal(step.name + ": no kernel scales a route's experts here.");
-      const View logits = stored(r.op.values[0]), ws = stored(r.outputs[1]);
+      const View logits = stored(r.op.values[0]), ids = stored(r.outputs[0]), ws = stored(r.outputs[1]);
       out.push_back(make("route_topk",
-                         {{"m", m}, {"n", (double)logits.width}, {"k", (double)k}, {"ldx", (double)logits.ld}},
+                         {{"m", m}, {"n", (double)logits.width}, {"k", (double)ids.width}, {"ldx", (double)logits.ld}},
                          {logits.ptr(), ids.ptr(), ws.ptr()}));
-      x = stored(lr.op.values[1]);
-    } else {
-      const Node& g = node("GatedGelu");
-      const View gu = stored(g.op.values[0]);
-      x = stored(g.outputs[0]);
-      if (gu.ld != gu.width || x.ld != x.width) throw Refusal(step.name + ": a gate of rows that are not whole.");
-      out.push_back(make("gated_gelu", {{"segments", m * (double)k}, {"f", (double)kk}}, {gu.ptr(), x.ptr()}));
     }
-    out.push_back(make("gemv_routed" + tsuf,
-                       {{"entries", (double)t.kind.entries},
-                        {"n", (double)n},
-                        {"kk", (double)kk},
-                        {"m", m},
-                        {"k", (double)k},
-                        {"split", 1.0},
-                        {"ldx", (double)x.ld},
-                        {"ldy", (double)y.ld},
-                        {"per_rank", x.width != kk ? 1.0 : 0.0}},
-                       {weight(t.name), ids.ptr(), x.ptr(), y.ptr()}));
+    if (lone_gate || routed_gate) {
+      const Node& g = node("GatedGelu");
+      const View gu = stored(g.op.values[0]), x = stored(g.outputs[0]);
+      const uint64_t f = p.values[g.outputs[0]].shape.segment;
+      if (gu.ld != gu.width || x.ld != x.width) throw Refusal(step.name + ": a gate of rows that are not whole.");
+      if (f == 0 || x.width % f != 0) throw Refusal(step.name + ": a gate whose rows are not whole segments.");
+      out.push_back(make("gated_gelu", {{"segments", m * (double)(x.width / f)}, {"f", (double)f}},
+                         {gu.ptr(), x.ptr()}));
+    }
+    if (lone_routed || routed_route || routed_gate) {
+      const Node& lr = node("LinearRouted");
+      const Source& t = p.sources[lr.op.sources[0]];
+      const std::string tsuf = weight_form(t.kind.type, step.name);
+      const uint64_t n = t.kind.dims[0], kk = t.kind.dims[1];
+      const View ids = stored(lr.op.values[0]), x = stored(lr.op.values[1]), y = stored(lr.outputs[0]);
+      out.push_back(make("gemv_routed" + tsuf,
+                         {{"entries", (double)t.kind.entries},
+                          {"n", (double)n},
+                          {"kk", (double)kk},
+                          {"m", m},
+                          {"k", (double)ids.width},
+                          {"split", 1.0},
+                          {"ldx", (double)x.ld},
+                          {"ldy", (double)y.ld},
+                          {"per_rank", x.width != kk ? 1.0 : 0.0}},
+                         {weight(t.name), ids.ptr(), x.ptr(), y.ptr()}));
+    }
     return out;
   }
   if (kinds == KP{{"Recompute", "Add"}, {"Recompute", "CombineRanks"}}) {
@@ -686,6 +694,8 @@ std::vector<Launch> llama_launches(const LlamaLaunchDesc& d) {
 
   PlanOptions layer_opts;
   layer_opts.sequence_rows = s.slots == 1 ? m : 1;
+  layer_opts.gated = d.gated;
+  layer_opts.store_gelus = d.store_gelus;
   LlamaShape head_shape = full;
   head_shape.vocab = vocab_local;
   const Plan embed_plan = plan(PlanOptions{}, embed_program(full));

@@ -40,7 +40,7 @@ enum {
 };
 
 /* The library's ABI version (this header's FKH_ABI_VERSION). */
-#define FKH_ABI_VERSION 6
+#define FKH_ABI_VERSION 7
 FKH_API int fkh_abi_version(void);
 
 /* A Llama-shaped model (the shapes of the programs the engine plans). */
@@ -106,6 +106,10 @@ typedef struct {
    * experts' gate/up rows [batch, top_k * 2 ffn], their gate
    * [batch, top_k * ffn], their outputs [batch, top_k * d]. */
   uint64_t mlp_in, router_logits, route_ids, route_weights, experts_gu, experts_act, experts_out;
+  /* The layer's plan options (PlanOptions, Plan.hs:243-268): a route in a
+   * step of its own (optGated), gelus stored by their own step
+   * (optStoreGelus). */
+  int gated, store_gelus;
 } fkh_llama_desc;
 
 /* A launch list: kernel names of the CUDA target's table, parameters by

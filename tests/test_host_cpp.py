@@ -143,7 +143,8 @@ class Buf:
         return self.ptr
 
 
-def fake_engine(full, batch, rank=0, world=1, peer_exchange=True, fuse_attention=None, sms=148, chunk=32):
+def fake_engine(full, batch, rank=0, world=1, peer_exchange=True, fuse_attention=None, sms=148, chunk=32,
+                gated=False, store_gelus=False):
     """A Llama with the attributes its launch lists read, at stand-in
     addresses (no device): the same decisions as its constructor."""
     e = object.__new__(Llama)
@@ -157,9 +158,11 @@ def fake_engine(full, batch, rank=0, world=1, peer_exchange=True, fuse_attention
     e.vocab_local = full.vocab // world
     e.plans = {
         "embed": PL.plan(PL.DEFAULT, embed_program(full)),
-        "layer": PL.plan(PL.PlanOptions(sequence_rows=batch if s.slots == 1 else 1), layer_program(s)),
+        "layer": PL.plan(PL.PlanOptions(gated=gated, store_gelus=store_gelus,
+                                        sequence_rows=batch if s.slots == 1 else 1), layer_program(s)),
         "head": PL.plan(PL.DEFAULT, head_program(dataclasses.replace(full, vocab=e.vocab_local))),
     }
+    e.gated, e.store_gelus = gated, store_gelus
     d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
     e.layer_elems = sum(e.layer_sizes())
     at = iter(range(1, 100))
@@ -256,6 +259,28 @@ def test_decode_launches_alike(case):
         for k, v in w.params.items():  # floats keep their bits (f32 parameters)
             if isinstance(v, float):
                 assert math.isclose(g.params[k], v, rel_tol=0, abs_tol=0) or g.params[k] == v
+
+
+# The layer's plan options (the reference's optGated and optStoreGelus):
+# routed experts with the route, the gate and the routed GEMVs as steps of
+# their own.
+GATED_CASES = [(dataclasses.replace(small(b), experts=8, top_k=2, weights=w), b, g, sg)
+               for b in (1, 5) for w in ("f32", "bf16") for g, sg in ((True, False), (True, True), (False, True))]
+
+
+@pytest.mark.parametrize("case", range(len(GATED_CASES)))
+def test_gated_plans_launch_alike(case):
+    full, batch, gated, store_gelus = GATED_CASES[case]
+    e = fake_engine(full, batch, gated=gated, store_gelus=store_gelus)
+    want = e._launches_restated()
+    got = e._launches()
+    assert [L.kernel for L in got] == [L.kernel for L in want]
+    for g, w in zip(got, want):
+        assert g.bufs == w.bufs and g.params == w.params, (g.kernel, g.params, w.params)
+    # The same kernels as the default plan's, in the same order: the route,
+    # the gate and the routed GEMVs are launched as they were.
+    base = fake_engine(full, batch)._launches()
+    assert [L.kernel for L in got] == [L.kernel for L in base]
 
 
 def test_unlowerable_steps_are_refused_alike():

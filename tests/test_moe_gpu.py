@@ -103,18 +103,21 @@ def test_gated_gelu_and_combine(ctx):
         b.free()
 
 
-@pytest.mark.parametrize("batch,experts,top_k,weights", [(1, 8, 2, "f32"), (3, 8, 2, "f32"), (9, 16, 4, "f32"),
-                                                         (2, 8, 2, "bf16"), (12, 8, 2, "bf16"), (5, 8, 2, "f16")])
-def test_moe_model_decode_step(ctx, batch, experts, top_k, weights):
+@pytest.mark.parametrize("batch,experts,top_k,weights,gated,store_gelus", [
+    (1, 8, 2, "f32", False, False), (3, 8, 2, "f32", False, False), (9, 16, 4, "f32", False, False),
+    (2, 8, 2, "bf16", False, False), (12, 8, 2, "bf16", False, False), (5, 8, 2, "f16", False, False),
+    (3, 8, 2, "f32", True, False), (3, 8, 2, "f32", True, True), (4, 8, 2, "bf16", False, True)])
+def test_moe_model_decode_step(ctx, batch, experts, top_k, weights, gated, store_gelus):
     """A decode step of a model whose FFN is routed experts, captured as a
     graph, against the oracle's decode: the same ids, logits and residual
-    rows, bit for bit."""
+    rows, bit for bit -- with the default plan, and with the route and the
+    gate in steps of their own (optGated, optStoreGelus)."""
     from furykernel_b200.engine import Llama
     from furykernel_b200.program.llama import LlamaShape
 
     s = LlamaShape(d_model=512, heads=4, kv_heads=4, head_dim=128, ffn=256, vocab=3000, layers=2, slots=batch,
                    length=96, positions=96, experts=experts, top_k=top_k, weights=weights)
-    eng = Llama(ctx, s, batch, seed=500 + batch, chunk=32, prefill_kv=1.0)
+    eng = Llama(ctx, s, batch, seed=500 + batch, chunk=32, prefill_kv=1.0, gated=gated, store_gelus=store_gelus)
     tokens = O.ints(29 + batch, batch, s.vocab)
     pos = ((np.arange(batch) * 37 + 5) % 96).astype(np.uint32)
     slot = np.arange(batch, dtype=np.uint32)
