@@ -14,7 +14,7 @@ _LIB = None
 _PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_build", "libfurykernel_host.so")
 
 FKH_OK, FKH_ERR_ARGUMENT, FKH_ERR_SPACE, FKH_ERR_INTERNAL = 0, 1, 2, 3
-ABI_VERSION = 7
+ABI_VERSION = 8
 
 
 # The shape's element-type codes, in order (fkh_llama_shape).
@@ -199,9 +199,13 @@ PREFILL_ADDRS = ("w_hi", "w_lo", "tokens", "pos", "slot", "x", "a", "a_hi", "a_l
                  "gu", "act")
 
 
+PREFILL_MOE_ADDRS = ("router_logits", "route_ids", "route_weights", "experts_gu", "experts_act", "experts_out")
+
+
 class PrefillDesc(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint64) for n in ("rows", "chunk", "positions")] + [("one_slot", ctypes.c_int)] + \
-               [(n, ctypes.c_uint64) for n in PREFILL_ADDRS] + [("part", ctypes.c_uint64 * 3)]
+               [(n, ctypes.c_uint64) for n in PREFILL_ADDRS] + [("part", ctypes.c_uint64 * 3)] + \
+               [(n, ctypes.c_uint64) for n in PREFILL_MOE_ADDRS]
 
 
 def prefill_launches(decode: tuple, rows: int, chunk: int, positions: int, one_slot: bool, addrs: dict,
@@ -213,6 +217,8 @@ def prefill_launches(decode: tuple, rows: int, chunk: int, positions: int, one_s
     p.rows, p.chunk, p.positions, p.one_slot = rows, chunk, positions, int(one_slot)
     for n in PREFILL_ADDRS:
         setattr(p, n, int(addrs[n]))
+    for n in PREFILL_MOE_ADDRS:
+        setattr(p, n, int(addrs.get(n, 0)))
     for i, a in enumerate(addrs["part"]):
         p.part[i] = int(a)
     return _collect(lib().fkh_llama_prefill_launches, ctypes.byref(d), ctypes.byref(p), m)

@@ -24,7 +24,7 @@ namespace fk {
 namespace moe {
 
 constexpr uint32_t kMaxRanks = 8;
-constexpr uint32_t kMaxPairs = 64;  // (row, rank) pairs a launch routes
+constexpr uint32_t kPairWindow = 1024;  // (row, rank) pairs a block lists at a time
 
 // The route: a warp a row; lane l holds logits l, l + 32, ... (n <= 1024).
 __global__ void __launch_bounds__(32) route_topk_kernel(const float* __restrict__ x, uint32_t n, uint32_t k,
@@ -110,66 +110,78 @@ __device__ __forceinline__ float4 ld_pack(const typename E::Storage* row, uint32
 }
 
 // The routed GEMV: a block a (expert, 8 output rows), a warp a row. The
-// block lists the (row, rank) pairs whose route chose its expert and, for
-// up to 4 pairs at a time, streams the expert's row once for them, each
-// pair's dot in the GEMV contract's order. Experts no row chose read no
-// weights. E: the table's element type, f32, bf16 or f16 (widened where
-// read).
+// block walks the (row, rank) pairs in windows of kPairWindow, lists those
+// whose route chose its expert and, for up to 4 pairs at a time, streams
+// the expert's row once for them, each pair's dot in the GEMV contract's
+// order (a pair's result does not depend on which pairs share its pass).
+// Experts no row chose read no weights. E: the table's element type, f32,
+// bf16 or f16 (widened where read).
 template <class E>
 __global__ void __launch_bounds__(256) gemv_routed_kernel(RoutedArgs a) {
-  __shared__ uint32_t pairs[kMaxPairs];
+  __shared__ uint32_t pairs[kPairWindow];
   __shared__ uint32_t npairs;
   const uint32_t e = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   grid_wait();
   grid_launch_dependents();
-  if (threadIdx.x == 0) {
-    uint32_t c = 0;
-    for (uint32_t p = 0; p < a.m * a.k && c < kMaxPairs; ++p)
-      if (a.ids[p] == e) pairs[c++] = p;
-    npairs = c;
-  }
-  __syncthreads();
-  const uint32_t P = npairs;
+  const uint32_t all = a.m * a.k;
   const uint32_t o = blockIdx.y * 8u + (uint32_t)warp;
-  if (P == 0 || o >= a.n) return;
   const uint32_t packs = a.kk >> 2;
   const uint32_t stride = 32u * a.split;
-  const typename E::Storage* wr = reinterpret_cast<const typename E::Storage*>(a.table) + ((size_t)e * a.n + o) * a.kk;
-  for (uint32_t p0 = 0; p0 < P; p0 += kPairsAPass) {
-    const uint32_t np = min((uint32_t)kPairsAPass, P - p0);
-    const float4* xs[kPairsAPass];
-#pragma unroll
-    for (int q = 0; q < kPairsAPass; ++q) {
-      const uint32_t pr = pairs[p0 + min((uint32_t)q, np - 1)];
-      const uint32_t r = pr / a.k, j = pr % a.k;
-      xs[q] = reinterpret_cast<const float4*>(a.x + (size_t)r * a.ldx + (a.per_rank ? (size_t)j * a.kk : 0));
-    }
-    float total[kPairsAPass];
-    for (uint32_t sq = 0; sq < a.split; ++sq) {
-      float acc[kPairsAPass];
-#pragma unroll
-      for (int q = 0; q < kPairsAPass; ++q) acc[q] = 0.0f;
-      for (uint32_t jj = sq * 32u + (uint32_t)lane; jj < packs; jj += stride) {
-        const float4 wv = ld_pack<E>(wr, jj);
-#pragma unroll
-        for (int q = 0; q < kPairsAPass; ++q)
-          if ((uint32_t)q < np) acc[q] = __fadd_rn(acc[q], pack_dot(__ldg(xs[q] + jj), wv));
+  const typename E::Storage* wr =
+      reinterpret_cast<const typename E::Storage*>(a.table) + ((size_t)e * a.n + (o < a.n ? o : 0)) * a.kk;
+  for (uint32_t w0 = 0; w0 < all; w0 += kPairWindow) {
+    const uint32_t w1 = min(all, w0 + kPairWindow);
+    __syncthreads();  // every warp is done with the last window's list
+    if (warp == 0) {  // the window's pairs that chose e, in order: a ballot per 32
+      uint32_t c = 0;
+      for (uint32_t base = w0; base < w1; base += 32u) {
+        const uint32_t p = base + (uint32_t)lane;
+        const bool hit = p < w1 && a.ids[p] == e;
+        const uint32_t mask = __ballot_sync(0xffffffffu, hit);
+        if (hit) pairs[c + __popc(mask & ((1u << lane) - 1u))] = p;
+        c += __popc(mask);
       }
+      if (lane == 0) npairs = c;
+    }
+    __syncthreads();
+    const uint32_t P = npairs;
+    if (P == 0 || o >= a.n) continue;
+    for (uint32_t p0 = 0; p0 < P; p0 += kPairsAPass) {
+      const uint32_t np = min((uint32_t)kPairsAPass, P - p0);
+      const float4* xs[kPairsAPass];
 #pragma unroll
       for (int q = 0; q < kPairsAPass; ++q) {
-        const float part = warp_sum(acc[q]);
-        total[q] = sq == 0 ? part : __fadd_rn(total[q], part);
+        const uint32_t pr = pairs[p0 + min((uint32_t)q, np - 1)];
+        const uint32_t r = pr / a.k, j = pr % a.k;
+        xs[q] = reinterpret_cast<const float4*>(a.x + (size_t)r * a.ldx + (a.per_rank ? (size_t)j * a.kk : 0));
       }
-    }
-    if (lane == 0) {
+      float total[kPairsAPass];
+      for (uint32_t sq = 0; sq < a.split; ++sq) {
+        float acc[kPairsAPass];
 #pragma unroll
-      for (int q = 0; q < kPairsAPass; ++q)
-        if ((uint32_t)q < np) {
-          const uint32_t pr = pairs[p0 + q];
-          const uint32_t r = pr / a.k, j = pr % a.k;
-          a.y[(size_t)r * a.ldy + (size_t)j * a.n + o] = total[q];
+        for (int q = 0; q < kPairsAPass; ++q) acc[q] = 0.0f;
+        for (uint32_t jj = sq * 32u + (uint32_t)lane; jj < packs; jj += stride) {
+          const float4 wv = ld_pack<E>(wr, jj);
+#pragma unroll
+          for (int q = 0; q < kPairsAPass; ++q)
+            if ((uint32_t)q < np) acc[q] = __fadd_rn(acc[q], pack_dot(__ldg(xs[q] + jj), wv));
         }
+#pragma unroll
+        for (int q = 0; q < kPairsAPass; ++q) {
+          const float part = warp_sum(acc[q]);
+          total[q] = sq == 0 ? part : __fadd_rn(total[q], part);
+        }
+      }
+      if (lane == 0) {
+#pragma unroll
+        for (int q = 0; q < kPairsAPass; ++q)
+          if ((uint32_t)q < np) {
+            const uint32_t pr = pairs[p0 + q];
+            const uint32_t r = pr / a.k, j = pr % a.k;
+            a.y[(size_t)r * a.ldy + (size_t)j * a.n + o] = total[q];
+          }
+      }
     }
   }
 }
@@ -231,7 +243,7 @@ cudaError_t fk_launch_gemv_routed(const void* table, FkElem el, uint32_t entries
                                   const uint32_t* ids, uint32_t m, uint32_t k, const float* x, uint32_t ldx,
                                   bool per_rank, uint32_t split, float* y, uint32_t ldy, bool pdl, cudaStream_t s) {
   if (m == 0 || n == 0) return cudaSuccess;
-  if (kk % 4 != 0 || kk == 0 || k == 0 || entries == 0 || (uint64_t)m * k > fk::moe::kMaxPairs || split == 0 ||
+  if (kk % 4 != 0 || kk == 0 || k == 0 || entries == 0 || (uint64_t)m * k > 0xFFFFFFFFull || split == 0 ||
       ldx < (per_rank ? k * kk : kk) || ldy < k * n)
     return cudaErrorInvalidValue;
   fk::moe::RoutedArgs a;

@@ -977,7 +977,9 @@ ParamSpec f32(const char* n) { return {n, "f32", false, 0, 0, 0}; }
 
 std::vector<KernelSpec> make_table() {
   std::vector<KernelSpec> t;
-  auto gemv_dims = std::vector<ParamSpec>{dim("n", 1, 1048576), dim("k", 4, 65536, 4), dim("m", 1, 64),
+  // m: any batch; the launchers take up to 4 rows streaming, up to 64 in the
+  // packed batched kernel, and past that 32 rows a launch of the chunked one.
+  auto gemv_dims = std::vector<ParamSpec>{dim("n", 1, 1048576), dim("k", 4, 65536, 4), dim("m", 1, 65535),
                                           dim("split", 1, 8),   u32("ldx"),           u32("ldy")};
   auto with = [](std::vector<ParamSpec> a, std::initializer_list<ParamSpec> b) {
     a.insert(a.end(), b.begin(), b.end());
@@ -1236,7 +1238,7 @@ std::vector<KernelSpec> make_table() {
   t.push_back({"gemv_routed",
                256,
                {{"table", "read", "f32"}, {"ids", "read", "u32"}, {"x", "read", "f32"}, {"y", "write", "f32"}},
-               {dim("entries", 1, 4096), dim("n", 1, 1048576), dim("kk", 4, 65536, 4), dim("m", 1, 64),
+               {dim("entries", 1, 4096), dim("n", 1, 1048576), dim("kk", 4, 65536, 4), dim("m", 1, 65535),
                 dim("k", 1, 8), dim("split", 1, 8), u32("ldx"), u32("ldy"), u32("per_rank")},
                l_gemv_routed});
   t.push_back({"gated_gelu", 256, {{"x", "read", "f32"}, {"y", "write", "f32"}},

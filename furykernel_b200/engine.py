@@ -388,9 +388,8 @@ class Llama:
         self.cb = {"f32": 4, "bf16": 2, "f16": 2}.get(s.cache)
         if self.wb is None or self.cb is None:
             raise N.Refused(N.FKC_ERR_ARGUMENT, f"no kernels for {s.weights} weights and {s.cache} caches.")
-        if s.experts and (world > 1 or batch * s.top_k > 64 or s.experts > 1024):
-            raise N.Refused(N.FKC_ERR_ARGUMENT, "routed experts: one GPU, at most 64 (row, expert) pairs a step "
-                                                "and 1024 experts.")
+        if s.experts and (world > 1 or s.experts > 1024):
+            raise N.Refused(N.FKC_ERR_ARGUMENT, "routed experts: one GPU and at most 1024 experts.")
         if self.wb == 2 and any(n % 8 for n in (s.d_model, s.q_width, s.kv_width, s.ffn)):
             raise N.Refused(N.FKC_ERR_ARGUMENT, "16-bit weights: d_model, the q and kv widths and ffn must be "
                             "multiples of 8, so that every weight starts on a 16-byte boundary.")

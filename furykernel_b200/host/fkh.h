@@ -332,6 +332,9 @@ struct PrefillDesc {
   uint64_t tokens = 0, pos = 0, slot = 0;
   uint64_t x = 0, a = 0, a_hi = 0, a_lo = 0, qkv = 0, att = 0, tmp = 0, x1 = 0, gu = 0, act = 0;
   uint64_t part[3] = {0, 0, 0};
+  // Routed experts: the rows' router logits, route ids and weights, the
+  // experts' gate/up rows, their gate and their outputs.
+  uint64_t router_logits = 0, route_ids = 0, route_weights = 0, experts_gu = 0, experts_act = 0, experts_out = 0;
 };
 
 std::vector<Launch> prefill_launches(const LlamaLaunchDesc& decode, const PrefillDesc& p, uint64_t m);

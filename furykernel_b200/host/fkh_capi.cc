@@ -214,6 +214,12 @@ int fkh_llama_prefill_launches(const fkh_llama_desc* desc, const fkh_prefill_des
     p.gu = prefill->gu;
     p.act = prefill->act;
     for (int i = 0; i < 3; ++i) p.part[i] = prefill->part[i];
+    p.router_logits = prefill->router_logits;
+    p.route_ids = prefill->route_ids;
+    p.route_weights = prefill->route_weights;
+    p.experts_gu = prefill->experts_gu;
+    p.experts_act = prefill->experts_act;
+    p.experts_out = prefill->experts_out;
     auto l = std::make_unique<fkh_launches>();
     l->list = fkh::prefill_launches(desc_of(*desc), p, m);
     *out = l.release();

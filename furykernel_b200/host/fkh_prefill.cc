@@ -2,7 +2,10 @@
 // once, the decode layer's plan run over m rows with the linears as
 // tcgen05 3xTF32 GEMM tiles (gemm_tf32x3) instead of GEMVs. The decode
 // step's own launches are the templates of the gather, the KV stores and
-// the attention (their shapes, tables and caches).
+// the attention (their shapes, tables and caches). A layer of routed
+// experts runs its experts through the decode step's own kernels over the
+// m rows (the router GEMV, the route, the expert-grouped routed GEMVs, the
+// gate, the combine), so its arithmetic is the decode step's.
 #include "fkh.h"
 
 namespace fkh {
@@ -153,6 +156,34 @@ std::vector<Launch> prefill_launches(const LlamaLaunchDesc& d, const PrefillDesc
     out.push_back(make("add", {{"n", (double)(m * dm)}}, {p.x, p.tmp, p.x1}));
     out.push_back(make("rmsnorm_rows" + wsuf, {{"rows", md}, {"h", (double)dm}, {"eps", eps}, {"factor", 1.0}},
                        {p.x1, w.at("mlp_norm"), p.a}));
+    if (s.experts) {
+      const uint64_t e = s.experts, k = s.top_k;
+      out.push_back(make("gemv" + wsuf,
+                         {{"n", (double)e}, {"k", (double)dm}, {"m", md}, {"split", 1.0}, {"ldx", (double)dm},
+                          {"ldy", (double)e}},
+                         {w.at("router"), p.a, p.router_logits}));
+      out.push_back(make("route_topk", {{"m", md}, {"n", (double)e}, {"k", (double)k}, {"ldx", (double)e}},
+                         {p.router_logits, p.route_ids, p.route_weights}));
+      auto routed = [&](uint64_t table, uint64_t n, uint64_t kk, uint64_t x, uint64_t ldx, uint64_t y, bool per_rank) {
+        return make("gemv_routed" + wsuf,
+                    {{"entries", (double)e},
+                     {"n", (double)n},
+                     {"kk", (double)kk},
+                     {"m", md},
+                     {"k", (double)k},
+                     {"split", 1.0},
+                     {"ldx", (double)ldx},
+                     {"ldy", (double)(k * n)},
+                     {"per_rank", per_rank ? 1.0 : 0.0}},
+                    {table, p.route_ids, x, y});
+      };
+      out.push_back(routed(w.at("experts_gate_up"), 2 * f, dm, p.a, dm, p.experts_gu, false));
+      out.push_back(make("gated_gelu", {{"segments", md * (double)k}, {"f", (double)f}}, {p.experts_gu, p.experts_act}));
+      out.push_back(routed(w.at("experts_down"), dm, f, p.experts_act, k * f, p.experts_out, true));
+      out.push_back(make("combine_ranks_add", {{"m", md}, {"k", (double)k}, {"d", (double)dm}},
+                         {p.x1, p.route_weights, p.experts_out, p.x}));
+      continue;
+    }
     if (d.gate_up_interleaved) {  // rows gate_0, up_0, ...: the GEMM's columns likewise
       out.push_back(gemm(p.a, dm, w.at("gate_proj"), 2 * f, p.gu, 2 * f));
       out.push_back(make("silu_pairs", {{"n", (double)(m * f)}}, {p.gu, p.act}));

@@ -45,9 +45,6 @@ class Prefill:
     def __init__(self, eng: Llama, rows: int, chunk: int | None = None, positions: int | None = None,
                  one_slot: bool = False):
         ctx, s = eng.ctx, eng.s
-        if getattr(s, "experts", 0):
-            raise N.Refused(N.FKC_ERR_ARGUMENT, "prefill: routed experts run through the decode step's kernels; "
-                                                "no GEMM form of them is built.")
         self.eng, self.ctx, self.R = eng, ctx, rows
         d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
         for what, k in (("d_model", d), ("q width", qw), ("ffn", f)):
@@ -80,6 +77,15 @@ class Prefill:
         self.x1 = ctx.zeros((R, d))
         self.gu = ctx.zeros((R, 2 * f))
         self.act = ctx.zeros((R, f))
+        # Routed experts over the rows, through the decode step's kernels:
+        # the router's logits, the route, the experts' gate/up rows, their
+        # gate, their outputs.
+        self.moe = {}
+        if s.experts:
+            e, k = s.experts, s.top_k
+            self.moe = {"router_logits": ctx.zeros((R, e)), "route_ids": ctx.zeros((R, k), np.uint32),
+                        "route_weights": ctx.zeros((R, k)), "experts_gu": ctx.zeros((R, k * 2 * f)),
+                        "experts_act": ctx.zeros((R, k * f)), "experts_out": ctx.zeros((R, k * d))}
         self.chunk = chunk or eng.chunk
         # Splits a row's attention can have: up to the largest position a
         # prefill here stores (the engine's positions unless given).
@@ -117,6 +123,7 @@ class Prefill:
         rs4 = 4 * self.rs
         addrs.update(tokens=self.rows_buf.ptr, pos=self.rows_buf.ptr + rs4, slot=self.rows_buf.ptr + 2 * rs4,
                      part=[b.ptr for b in self.part])
+        addrs.update({n: b.ptr for n, b in self.moe.items()})
         return [Launch(k, p, b) for k, p, b in _host.prefill_launches(
             self.eng.launch_args(), self.R, self.chunk, self.positions, self.one_slot, addrs, m)]
 
@@ -195,6 +202,24 @@ class Prefill:
             out.append(Launch("add", {"n": m * d}, [self.x.ptr, self.tmp.ptr, self.x1.ptr]))
             out.append(Launch("rmsnorm_rows" + wsuf, {"rows": m, "h": d, "eps": eps, "factor": 1.0},
                               [self.x1.ptr, w["mlp_norm"], self.a.ptr]))
+            if s.experts:  # the decode step's kernels over the m rows
+                e, k, b = s.experts, s.top_k, {n: v.ptr for n, v in self.moe.items()}
+                out.append(Launch("gemv" + wsuf, {"n": e, "k": d, "m": m, "split": 1, "ldx": d, "ldy": e},
+                                  [w["router"], self.a.ptr, b["router_logits"]]))
+                out.append(Launch("route_topk", {"m": m, "n": e, "k": k, "ldx": e},
+                                  [b["router_logits"], b["route_ids"], b["route_weights"]]))
+
+                def routed(table, n, kk, x, ldx, y, per_rank):
+                    return Launch("gemv_routed" + wsuf, {"entries": e, "n": n, "kk": kk, "m": m, "k": k, "split": 1,
+                                                         "ldx": ldx, "ldy": k * n, "per_rank": per_rank},
+                                  [table, b["route_ids"], x, y])
+
+                out.append(routed(w["experts_gate_up"], 2 * f, d, self.a.ptr, d, b["experts_gu"], 0))
+                out.append(Launch("gated_gelu", {"segments": m * k, "f": f}, [b["experts_gu"], b["experts_act"]]))
+                out.append(routed(w["experts_down"], d, f, b["experts_act"], k * f, b["experts_out"], 1))
+                out.append(Launch("combine_ranks_add", {"m": m, "k": k, "d": d},
+                                  [self.x1.ptr, b["route_weights"], b["experts_out"], self.x.ptr]))
+                continue
             if eng.gate_up_interleaved:  # rows gate_0, up_0, ...: columns likewise
                 out.append(self._gemm(self.a.ptr, d, w["gate_proj"], 2 * f, self.gu.ptr, 2 * f))
                 out.append(Launch("silu_pairs", {"n": m * f}, [self.gu.ptr, self.act.ptr]))
@@ -252,9 +277,11 @@ class Prefill:
         self.graph(m).launch()
 
     def gemm_flops(self, rows: int) -> int:
-        """Useful flops of the GEMMs over `rows` rows (2 a multiply-add)."""
+        """Useful flops of the GEMMs over `rows` rows (2 a multiply-add); with
+        routed experts only the attention's projections are GEMMs."""
         s = self.eng.s
-        return 2 * rows * s.layers * (self.eng.layer_elems - 2 * s.d_model)
+        per = sum(self.eng.layer_sizes()[:4]) if s.experts else self.eng.layer_elems - 2 * s.d_model
+        return 2 * rows * s.layers * per
 
     def close(self) -> None:
         """Destroys the graphs and frees the TF32 halves and scratch."""
@@ -262,8 +289,9 @@ class Prefill:
             g.destroy()
         self.graphs = {}
         for b in [self.w_hi, self.w_lo, self.rows_buf, self.x, self.a, self.a_hi, self.a_lo, self.qkv, self.att,
-                  self.tmp, self.x1, self.gu, self.act] + self.part:
+                  self.tmp, self.x1, self.gu, self.act] + self.part + list(self.moe.values()):
             b.free()
+        self.moe = {}
 
 
 def prompt_rows(prompts, slots):

@@ -95,7 +95,8 @@ def _f(name):
     return Param(name, "f32")
 
 
-_GEMV = [_dim("n", 1, 1048576), _dim("k", 4, 65536, 4), _dim("m", 1, 64), _dim("split", 1, 8), _u("ldx"), _u("ldy")]
+_GEMV = [_dim("n", 1, 1048576), _dim("k", 4, 65536, 4), _dim("m", 1, 65535), _dim("split", 1, 8), _u("ldx"),
+         _u("ldy")]
 _MAX = 4294967295
 
 SPEC_KERNELS = {
@@ -182,7 +183,7 @@ SPEC_KERNELS = {
         KernelSig("route_topk_scaled", [_f32("x"), _f32("scale"), _u32("ids", "write"), _f32("ws", "write")],
                   [_dim("m", 1, 65535), _dim("n", 1, 1024), _dim("k", 1, 8), _u("ldx")], threads=32),
         KernelSig("gemv_routed", [_f32("table"), _u32("ids"), _f32("x"), _f32("y", "write")],
-                  [_dim("entries", 1, 4096), _dim("n", 1, 1048576), _dim("kk", 4, 65536, 4), _dim("m", 1, 64),
+                  [_dim("entries", 1, 4096), _dim("n", 1, 1048576), _dim("kk", 4, 65536, 4), _dim("m", 1, 65535),
                    _dim("k", 1, 8), _dim("split", 1, 8), _u("ldx"), _u("ldy"), _u("per_rank")]),
         KernelSig("gated_gelu", [_f32("x"), _f32("y", "write")], [_dim("segments", 1, _MAX), _dim("f", 1, _MAX)]),
         KernelSig("combine_ranks_add", [_f32("r"), _f32("ws"), _f32("segs"), _f32("y", "write")],

@@ -40,7 +40,7 @@ enum {
 };
 
 /* The library's ABI version (this header's FKH_ABI_VERSION). */
-#define FKH_ABI_VERSION 7
+#define FKH_ABI_VERSION 8
 FKH_API int fkh_abi_version(void);
 
 /* A Llama-shaped model (the shapes of the programs the engine plans). */
@@ -143,6 +143,11 @@ typedef struct {
   uint64_t tokens, pos, slot; /* [rows] u32 each */
   uint64_t x, a, a_hi, a_lo, qkv, att, tmp, x1, gu, act;
   uint64_t part[3];
+  /* Routed experts over the rows (the decode step's kernels): the router's
+   * logits [rows, experts], the route's ids (u32) and weights [rows, top_k],
+   * the experts' gate/up rows [rows, top_k * 2 ffn], their gate
+   * [rows, top_k * ffn], their outputs [rows, top_k * d]. */
+  uint64_t router_logits, route_ids, route_weights, experts_gu, experts_act, experts_out;
 } fkh_prefill_desc;
 
 /* The prefill of m rows (1..rows); `desc` is the decode step's, whose own

@@ -318,6 +318,10 @@ def fake_prefill(eng, rows, chunk=None, positions=None, one_slot=False):
     p.max_splits = (p.positions + p.chunk - 1) // p.chunk
     p.one_slot = one_slot and p.positions <= min(s.length, 1408)
     p.part = [Buf((7 << 44) + (i << 36)) for i in range(3)]
+    p.moe = {}
+    if s.experts:
+        p.moe = {n: Buf((9 << 44) + (i << 36)) for i, n in enumerate(
+            ("router_logits", "route_ids", "route_weights", "experts_gu", "experts_act", "experts_out"))}
     return p
 
 
@@ -340,6 +344,11 @@ PREFILL_CASES = (
     + [(dataclasses.replace(small(b), blocks=64, block_size=16, cache=c), b, 0, 1, True, 96, one, m)
        for b, one, m, c in ((1, False, 90, "f32"), (1, True, 96, "f32"), (4, True, 50, "bf16"), (8, False, 96, "bf16"))]
     + [(dataclasses.replace(tp_shape(1), blocks=32, block_size=8), 1, 1, 2, True, 32, False, 32)]
+    # routed experts: the decode step's kernels over the prompt rows
+    + [(dataclasses.replace(small(b), experts=8, top_k=2, weights=w), b, 0, 1, True, rows, one, m)
+       for b, rows, one, m, w in ((1, 128, False, 100, "f32"), (2, 128, True, 64, "f32"), (3, 96, False, 96, "bf16"),
+                                  (1, 128, False, 70, "f16"))]
+    + [(dataclasses.replace(small(4), experts=4, top_k=1, blocks=64, block_size=16), 4, 0, 1, True, 96, True, 50)]
     # f16 weights and caches, ring and paged
     + [(dataclasses.replace(small(b), weights="f16", cache="f16"), b, 0, 1, True, 128, one, m)
        for b, one, m in ((1, False, 100), (1, True, 64))]

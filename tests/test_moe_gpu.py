@@ -129,3 +129,57 @@ def test_moe_model_decode_step(ctx, batch, experts, top_k, weights, gated, store
     assert np.array_equal(ids, want_ids)
     assert same_bits(eng.logits.download(), want_logits)
     assert same_bits(eng.x.download(), want_x)
+
+
+@pytest.mark.parametrize("weights,one_slot", [("f32", False), ("f32", True), ("bf16", False)])
+def test_moe_prefill(ctx, weights, one_slot):
+    """Prefill of a model whose FFN is routed experts: the last layer's
+    experts over the prompt rows are the decode step's kernels, so from the
+    rows prefill left (the attention residual and its norm) the oracle
+    gives their logits, route, outputs and the layer's output bit for bit;
+    the decode step from the caches prefill left is the oracle's too."""
+    from furykernel_b200.engine import Llama
+    from furykernel_b200.prefill import Prefill, prompt_chunks
+    from furykernel_b200.program.llama import LlamaShape
+
+    batch = 2
+    s = LlamaShape(d_model=512, heads=4, kv_heads=4, head_dim=128, ffn=256, vocab=3000, layers=2, slots=batch,
+                   length=96, positions=96, experts=8, top_k=2, weights=weights)
+    eng = Llama(ctx, s, batch, seed=520, chunk=16)
+    pre = Prefill(eng, rows=128, one_slot=one_slot)
+    layers, embed, final_norm = MC.host_model(eng)
+    lens = [41, 30]
+    prompts = [O.ints(230 + i, n, s.vocab) for i, n in enumerate(lens)]
+    toks = np.concatenate([p[:-1] for p in prompts])
+    poss = np.concatenate([np.arange(n - 1, dtype=np.uint32) for n in lens])
+    sl = np.concatenate([np.full(n - 1, i, np.uint32) for i, n in enumerate(lens)])
+    runs = prompt_chunks(pre, toks, poss, sl)
+    for i, n in runs:
+        pre.run(toks[i:i + n], poss[i:i + n], sl[i:i + n])
+    ctx.sync()
+    # The last run's last layer, recomputed from its attention residual.
+    m = runs[-1][1]
+    w = layers[-1]
+    d = s.d_model
+    x1 = pre.x1.download()[:m]
+    a = O.rmsnorm_rows(x1, w["mlp_norm"], np.float32(s.eps), 1.0, THREADS)
+    assert same_bits(pre.a.download()[:m], a)
+    logits = O.gemv(w["router"], a, 1, THREADS)
+    assert same_bits(pre.moe["router_logits"].download()[:m], logits)
+    ids, ws = O.route_topk(logits, s.top_k)
+    assert np.array_equal(pre.moe["route_ids"].download()[:m], ids)
+    gu = O.gemv_routed(w["egu"], ids, a, 1, THREADS)
+    eo = O.gemv_routed(w["edn"], ids, O.gated_gelu(gu, s.ffn), 1, THREADS)
+    assert same_bits(pre.moe["experts_out"].download()[:m], eo)
+    assert same_bits(pre.x.download()[:m], O.combine_ranks_add(x1, ws, eo).reshape(m, d))
+    # The decode step from each prompt's last token, from the caches prefill left.
+    kc, vc = MC.host_caches(eng)
+    last = np.array([p[-1] for p in prompts], np.uint32)
+    lpos = np.array([n - 1 for n in lens], np.uint32)
+    slots = np.arange(batch, dtype=np.uint32)
+    eng.set_rows(last, lpos, slots)
+    got_ids = eng.step()
+    want_ids, want_logits, _ = MC.oracle_decode(eng, layers, embed, final_norm, kc, vc, last, lpos, slots)
+    assert same_bits(eng.logits.download(), want_logits)
+    assert np.array_equal(got_ids, want_ids)
+    pre.close()
