@@ -388,8 +388,8 @@ class Llama:
         self.cb = {"f32": 4, "bf16": 2, "f16": 2}.get(s.cache)
         if self.wb is None or self.cb is None:
             raise N.Refused(N.FKC_ERR_ARGUMENT, f"no kernels for {s.weights} weights and {s.cache} caches.")
-        if s.experts and (world > 1 or s.experts > 1024):
-            raise N.Refused(N.FKC_ERR_ARGUMENT, "routed experts: one GPU and at most 1024 experts.")
+        if s.experts > 1024:
+            raise N.Refused(N.FKC_ERR_ARGUMENT, "routed experts: at most 1024 experts.")
         if self.wb == 2 and any(n % 8 for n in (s.d_model, s.q_width, s.kv_width, s.ffn)):
             raise N.Refused(N.FKC_ERR_ARGUMENT, "16-bit weights: d_model, the q and kv widths and ffn must be "
                             "multiples of 8, so that every weight starts on a 16-byte boundary.")
@@ -402,7 +402,8 @@ class Llama:
         # Tensor parallelism's sums travel through peer memory (the context's
         # peer set, tp.init) for the batches the streaming GEMV takes; larger
         # batches use NCCL.
-        self.peer_exchange = world > 1 and batch <= 4 and peer_exchange
+        # (Routed experts sum their ranks' shares by NCCL.)
+        self.peer_exchange = world > 1 and batch <= 4 and peer_exchange and not s.experts
         self.vocab_local = full.vocab // world
         self.plans = {
             "embed": PL.plan(PL.DEFAULT, embed_program(full)),
@@ -428,6 +429,8 @@ class Llama:
             for l in range(s.layers):
                 w = self.layer_weights(l)
                 fill(N.DeviceBuffer(ctx, w["attn_norm"], 2 * wb * d), seed + 3 * l + 1, 0.0, 0.02)
+                if s.experts:  # the router is whole on every rank
+                    fill(N.DeviceBuffer(ctx, w["router"], wb * s.experts * d), seed + 611953 + l, 0.0, 0.02)
         else:
             self.arena.upload(host_weights)
         self.cos, self.sin = ctx.rope_tables(s.theta, s.head_dim, s.head_dim // 2, s.positions)
@@ -690,6 +693,9 @@ class Llama:
         return out
 
     def _tensor_parallel(self, launches: list) -> list:
+        if self.peer_exchange and self.s.experts:
+            raise Unlowerable(N.FKC_ERR_ARGUMENT, "routed experts over several ranks: their sums travel by NCCL, not "
+                                                  "peer memory.")
         if self.peer_exchange:
             return self._tensor_parallel_peers(launches)
         return self._tensor_parallel_nccl(launches)
@@ -731,8 +737,9 @@ class Llama:
 
     def _tensor_parallel_nccl(self, launches: list) -> list:
         """With NCCL: the row-parallel projections' residual epilogues move
-        after the allreduce of their partial sums; the greedy pick gathers
-        the shards' candidates."""
+        after the allreduce of their partial sums, the experts' outputs (each
+        rank's share of every expert's FFN) are summed before they are
+        combined, and the greedy pick gathers the shards' candidates."""
         m, d = self.m, self.s.d_model
         P = self.partial.ptr
         out = []
@@ -746,6 +753,10 @@ class Llama:
                 out.append(Launch(base[:-4] + suf, params, [w, x, P]))
                 out.append(Launch("__allreduce__", {"count": m * d}, [P]))
                 out.append(Launch("add", {"n": m * d}, [r, P, y]))
+            elif L.kernel == "combine_ranks_add":
+                p = L.params
+                out.append(Launch("__allreduce__", {"count": p["m"] * p["k"] * p["d"]}, [L.bufs[2]]))
+                out.append(L)
             elif L.kernel == "argmax":
                 x, ids = L.bufs
                 out.append(Launch("argmax_pairs", dict(L.params, offset=self.rank * self.vocab_local),
@@ -844,7 +855,10 @@ def shard_weights(full: LlamaShape, layers: list, embed: np.ndarray, final_norm:
 
     `layers` holds per layer the f32 arrays q [H*hd, d], k and v
     [KV*hd, d], o [d, H*hd], gate and up [F, d], down [d, F], attn_norm and
-    mlp_norm [d]."""
+    mlp_norm [d]; with routed experts, router [E, d], egu [E, 2F, d] (each
+    expert's gate rows, then its up rows) and edn [E, d, F] in place of gate,
+    up and down. A rank holds the whole router and, of every expert, the
+    gate and up rows and the down columns of its ffn slice."""
     hd, d = full.head_dim, full.d_model
     hq, hk, fl = full.heads // world, full.kv_heads // world, full.ffn // world
     qs = slice(rank * hq * hd, (rank + 1) * hq * hd)
@@ -852,9 +866,14 @@ def shard_weights(full: LlamaShape, layers: list, embed: np.ndarray, final_norm:
     fs = slice(rank * fl, (rank + 1) * fl)
     parts = []
     for w in layers:
+        parts += [w["q"][qs], w["k"][ks], w["v"][ks], np.ascontiguousarray(w["o"][:, qs])]
+        if full.experts:
+            f = full.ffn
+            egu = np.concatenate([w["egu"][:, fs], w["egu"][:, f + rank * fl:f + (rank + 1) * fl]], axis=1)
+            parts += [w["router"], egu, np.ascontiguousarray(w["edn"][:, :, fs]), w["attn_norm"], w["mlp_norm"]]
+            continue
         gate, up = w["gate"][fs], w["up"][fs]
         gu = np.stack([gate, up], axis=1).reshape(2 * fl, d) if interleave else [gate, up]
-        parts += [w["q"][qs], w["k"][ks], w["v"][ks], np.ascontiguousarray(w["o"][:, qs])]
         parts += [gu] if interleave else gu
         parts += [np.ascontiguousarray(w["down"][:, fs]), w["attn_norm"], w["mlp_norm"]]
     parts += [embed, final_norm]

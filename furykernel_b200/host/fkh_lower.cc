@@ -543,8 +543,9 @@ std::vector<Launch> tensor_parallel_peers(const std::vector<Launch>& in, const L
 }
 
 // With NCCL: the row-parallel projections' residual epilogues move after the
-// allreduce of their partial sums; the greedy pick gathers the shards'
-// candidates.
+// allreduce of their partial sums, the experts' outputs (each rank's share
+// of every expert's FFN) are summed before they are combined, and the greedy
+// pick gathers the shards' candidates.
 std::vector<Launch> tensor_parallel_nccl(const std::vector<Launch>& in, const LlamaLaunchDesc& d,
                                          uint64_t vocab_local) {
   std::vector<Launch> out;
@@ -570,6 +571,13 @@ std::vector<Launch> tensor_parallel_nccl(const std::vector<Launch>& in, const Ll
       add.params = {{"n", (double)(m * dm)}};
       add.bufs = {L.bufs[2], d.partial, L.bufs[3]};
       out.push_back(add);
+    } else if (L.kernel == "combine_ranks_add") {
+      Launch ar;
+      ar.kernel = "__allreduce__";
+      ar.params = {{"count", L.param("m") * L.param("k") * L.param("d")}};
+      ar.bufs = {L.bufs[2]};
+      out.push_back(ar);
+      out.push_back(L);
     } else if (L.kernel == "argmax") {
       Launch a;
       a.kernel = "argmax_pairs";
@@ -762,6 +770,8 @@ std::vector<Launch> llama_launches(const LlamaLaunchDesc& d) {
       out.push_back(lower_step(head_plan.program, st, hb, d.cos_t, d.sin_t, attn));
   }
   if (d.gate_up_interleaved) silu_on_tiles(out, f, d.gu, d.act);
+  if (d.world > 1 && d.peer_exchange && s.experts)
+    throw Refusal("routed experts over several ranks: their sums travel by NCCL, not peer memory.");
   if (d.world > 1)
     out = d.peer_exchange ? tensor_parallel_peers(out, d, vocab_local) : tensor_parallel_nccl(out, d, vocab_local);
   if (d.fuse_attention) out = fuse_attention(out);

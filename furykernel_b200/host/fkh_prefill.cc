@@ -180,6 +180,8 @@ std::vector<Launch> prefill_launches(const LlamaLaunchDesc& d, const PrefillDesc
       out.push_back(routed(w.at("experts_gate_up"), 2 * f, dm, p.a, dm, p.experts_gu, false));
       out.push_back(make("gated_gelu", {{"segments", md * (double)k}, {"f", (double)f}}, {p.experts_gu, p.experts_act}));
       out.push_back(routed(w.at("experts_down"), dm, f, p.experts_act, k * f, p.experts_out, true));
+      // Each rank ran its ffn slice of every expert: their outputs are summed first.
+      if (d.world > 1) out.push_back(make("__allreduce__", {{"count", (double)(m * k * dm)}}, {p.experts_out}));
       out.push_back(make("combine_ranks_add", {{"m", md}, {"k", (double)k}, {"d", (double)dm}},
                          {p.x1, p.route_weights, p.experts_out, p.x}));
       continue;

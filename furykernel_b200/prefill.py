@@ -217,6 +217,8 @@ class Prefill:
                 out.append(routed(w["experts_gate_up"], 2 * f, d, self.a.ptr, d, b["experts_gu"], 0))
                 out.append(Launch("gated_gelu", {"segments": m * k, "f": f}, [b["experts_gu"], b["experts_act"]]))
                 out.append(routed(w["experts_down"], d, f, b["experts_act"], k * f, b["experts_out"], 1))
+                if eng.world > 1:  # each rank ran its ffn slice of every expert: their outputs summed first
+                    out.append(Launch("__allreduce__", {"count": m * k * d}, [b["experts_out"]]))
                 out.append(Launch("combine_ranks_add", {"m": m, "k": k, "d": d},
                                   [self.x1.ptr, b["route_weights"], b["experts_out"], self.x.ptr]))
                 continue

@@ -163,9 +163,12 @@ def oracle_decode_tp(s, world, layers, embed, final_norm, kcache, vcache, tokens
     peer exchange: each rank's shard GEMVs in the contract's order over its
     own slice, the row-parallel partials added in rank order, then the
     residual: x1 = x + (((P_0 + P_1) + ...)). `layers` holds the whole
-    model (q, k, v, o, gate, up, down, attn_norm, mlp_norm per layer); the
-    caches [layers, slots, kv_heads, length, hd] are updated in place.
-    Returns (ids, logits, x)."""
+    model (q, k, v, o, gate, up, down, attn_norm, mlp_norm per layer; with
+    routed experts router, egu and edn in place of gate, up and down: every
+    rank routes with the whole router, runs its ffn slice of each chosen
+    expert, and the ranks' expert outputs are added in rank order before
+    the combine); the caches [layers, slots, kv_heads, length, hd] are
+    updated in place. Returns (ids, logits, x)."""
     threads = threads or O.threads_default()
     d, hd = s.d_model, s.head_dim
     hq, hk, fl, vl = s.heads // world, s.kv_heads // world, s.ffn // world, s.vocab // world
@@ -200,6 +203,16 @@ def oracle_decode_tp(s, world, layers, embed, final_norm, kcache, vcache, tokens
         x1 = O.add(x, ranked_sum(parts))
         m2 = O.rmsnorm_rows(x1, w["mlp_norm"], eps, 1.0, threads)
         parts = []
+        if getattr(s, "experts", 0):
+            ids, ws = O.route_topk(O.gemv(w["router"], m2, 1, threads), s.top_k)
+            for r in range(world):
+                egu = np.ascontiguousarray(np.concatenate(
+                    [w["egu"][:, r * fl:(r + 1) * fl], w["egu"][:, s.ffn + r * fl:s.ffn + (r + 1) * fl]], axis=1))
+                edn = np.ascontiguousarray(w["edn"][:, :, r * fl:(r + 1) * fl])
+                gu = O.gemv_routed(egu, ids, m2, 1, threads)
+                parts.append(O.gemv_routed(edn, ids, O.gated_gelu(gu, fl), 1, threads))
+            x = O.combine_ranks_add(x1, ws, ranked_sum(parts))
+            continue
         for r in range(world):
             fs = slice(r * fl, (r + 1) * fl)
             g = O.gemv(w["gate"][fs], m2, 1, threads)

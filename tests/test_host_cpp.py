@@ -154,7 +154,7 @@ def fake_engine(full, batch, rank=0, world=1, peer_exchange=True, fuse_attention
     e.ctx = SimpleNamespace(sms=sms)
     e.wb, e.cb = (4 if full.weights == "f32" else 2), (4 if full.cache == "f32" else 2)
     e.gate_up_interleaved = batch <= 64
-    e.peer_exchange = world > 1 and batch <= 4 and peer_exchange
+    e.peer_exchange = world > 1 and batch <= 4 and peer_exchange and not s.experts
     e.vocab_local = full.vocab // world
     e.plans = {
         "embed": PL.plan(PL.DEFAULT, embed_program(full)),
@@ -232,6 +232,9 @@ CASES = (
        for b in (1, 5)]
     + [(dataclasses.replace(small(b), experts=8, top_k=2, weights="bf16", cache="bf16"), b, 0, 1, True, None)
        for b in (1, 12)]
+    # routed experts over ranks: each rank's ffn slice of every expert, the sums by NCCL
+    + [(dataclasses.replace(tp_shape(b), ffn=256, experts=8, top_k=2), b, r, w, peer, None) for w in (2, 4)
+       for r in (0, w - 1) for b in (1, 5) for peer in (True, False)]
     # f16 weights and f16 caches (and mixed with bf16): every batch form, tensor parallelism, paged, experts
     + [(dataclasses.replace(small(b), weights="f16", cache="f16"), b, 0, 1, True, f)
        for b, f in ((1, None), (3, False), (5, None), (9, True), (65, None))]
@@ -349,6 +352,7 @@ PREFILL_CASES = (
        for b, rows, one, m, w in ((1, 128, False, 100, "f32"), (2, 128, True, 64, "f32"), (3, 96, False, 96, "bf16"),
                                   (1, 128, False, 70, "f16"))]
     + [(dataclasses.replace(small(4), experts=4, top_k=1, blocks=64, block_size=16), 4, 0, 1, True, 96, True, 50)]
+    + [(dataclasses.replace(tp_shape(2), ffn=256, experts=8, top_k=2), 2, r, 2, False, 64, False, 40) for r in (0, 1)]
     # f16 weights and caches, ring and paged
     + [(dataclasses.replace(small(b), weights="f16", cache="f16"), b, 0, 1, True, 128, one, m)
        for b, one, m in ((1, False, 100), (1, True, 64))]

@@ -117,3 +117,72 @@ def test_tp2_sharding_on_gloo(interleave):
     assert all(p.exitcode == 0 for p in procs)
     results = dict(q.get(timeout=10) for _ in range(2))
     assert results == {0: True, 1: True}
+
+
+SM = dataclasses.replace(S, ffn=16, experts=4, top_k=2)
+
+
+def moe_model(seed=5):
+    rng = np.random.default_rng(seed)
+    d, hd, e, f = SM.d_model, SM.head_dim, SM.experts, SM.ffn
+    layers = [{"q": rng.standard_normal((SM.heads * hd, d)), "k": rng.standard_normal((SM.kv_heads * hd, d)),
+               "v": rng.standard_normal((SM.kv_heads * hd, d)), "o": rng.standard_normal((d, SM.heads * hd)),
+               "router": rng.standard_normal((e, d)), "egu": rng.standard_normal((e, 2 * f, d)),
+               "edn": rng.standard_normal((e, d, f)), "attn_norm": rng.standard_normal(d),
+               "mlp_norm": rng.standard_normal(d)} for _ in range(SM.layers)]
+    return layers, rng.standard_normal((SM.vocab, d)), rng.standard_normal(d)
+
+
+def gelu(v):
+    return 0.5 * v * (1 + np.tanh(np.sqrt(2 / np.pi) * (v + 0.044715 * v ** 3)))
+
+
+def moe_rank_main(rank, world, port, q):
+    """Each rank reads its arena back in the engine's MoE layout (the whole
+    router, its ffn slice of every expert) and runs its slice of the chosen
+    experts; the allreduce of the slices is the whole experts' output."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import torch
+
+    layers, embed, final_norm = moe_model()
+    arena = shard_weights(SM, layers, embed.astype(np.float32), final_norm.astype(np.float32), rank, world)
+    arena = arena.astype(np.float64)
+    d, qw, kvw, e, k = SM.d_model, SM.q_width // world, SM.kv_width // world, SM.experts, SM.top_k
+    fl, f = SM.ffn // world, SM.ffn
+    sizes = [("q", qw * d), ("k", kvw * d), ("v", kvw * d), ("o", d * qw), ("router", e * d),
+             ("egu", e * 2 * fl * d), ("edn", e * d * fl), ("attn_norm", d), ("mlp_norm", d)]
+    x = np.linspace(-1, 1, d)
+    ok, at = True, 0
+    for whole in layers:
+        w = {}
+        for name, n in sizes:
+            w[name] = arena[at:at + n]
+            at += n
+        router, egu, edn = w["router"].reshape(e, d), w["egu"].reshape(e, 2 * fl, d), w["edn"].reshape(e, d, fl)
+        ok &= np.array_equal(router, np.float32(whole["router"]).astype(np.float64))
+        logits = router @ x
+        top = np.argsort(-logits, kind="stable")[:k]
+        part = np.concatenate([edn[j] @ (gelu(egu[j, :fl] @ x) * (egu[j, fl:] @ x)) for j in top])
+        t = torch.tensor(part)
+        dist.all_reduce(t)
+        w32 = {n: np.float32(whole[n]).astype(np.float64) for n in ("egu", "edn")}
+        want = np.concatenate([w32["edn"][j] @ (gelu(w32["egu"][j, :f] @ x) * (w32["egu"][j, f:] @ x)) for j in top])
+        ok &= np.allclose(t.numpy(), want)
+    ok &= at + SM.vocab * d + d == arena.size
+    q.put((rank, bool(ok)))
+    dist.destroy_process_group()
+
+
+def test_tp2_moe_sharding_on_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=moe_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    assert all(p.exitcode == 0 for p in procs)
+    results = dict(q.get(timeout=10) for _ in range(2))
+    assert results == {0: True, 1: True}

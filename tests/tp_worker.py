@@ -15,7 +15,7 @@ from oracle import oracle as O  # noqa: E402
 
 
 def model(s):
-    d, hd, f = s.d_model, s.head_dim, s.ffn
+    d, hd, f, e = s.d_model, s.head_dim, s.ffn, s.experts
     layers = []
     for l in range(s.layers):
         seed = 1000 + 10 * l
@@ -24,21 +24,30 @@ def model(s):
             "k": O.normal(seed + 1, s.kv_heads * hd * d, 0, 0.02).reshape(s.kv_heads * hd, d),
             "v": O.normal(seed + 2, s.kv_heads * hd * d, 0, 0.02).reshape(s.kv_heads * hd, d),
             "o": O.normal(seed + 3, d * s.heads * hd, 0, 0.02).reshape(d, s.heads * hd),
-            "gate": O.normal(seed + 4, f * d, 0, 0.02).reshape(f, d),
-            "up": O.normal(seed + 5, f * d, 0, 0.02).reshape(f, d),
-            "down": O.normal(seed + 6, d * f, 0, 0.02).reshape(d, f),
             "attn_norm": O.uniform(seed + 7, d, 0.5, 1.5),
             "mlp_norm": O.uniform(seed + 8, d, 0.5, 1.5),
         })
+        if e:  # routed experts: the router, each expert's [gate; up] rows and down
+            layers[-1].update(router=O.normal(seed + 4, e * d, 0, 0.02).reshape(e, d),
+                              egu=O.normal(seed + 5, e * 2 * f * d, 0, 0.02).reshape(e, 2 * f, d),
+                              edn=O.normal(seed + 6, e * d * f, 0, 0.02).reshape(e, d, f))
+        else:
+            layers[-1].update(gate=O.normal(seed + 4, f * d, 0, 0.02).reshape(f, d),
+                              up=O.normal(seed + 5, f * d, 0, 0.02).reshape(f, d),
+                              down=O.normal(seed + 6, d * f, 0, 0.02).reshape(d, f))
     embed = O.normal(77, s.vocab * d, 0, 0.02).reshape(s.vocab, d)
     final_norm = O.uniform(78, d, 0.5, 1.5)
     return layers, embed, final_norm
 
 
-def shape(batch=2):
-    """The test model: 8 heads, so that it shards over 2, 4 or 8 ranks."""
+def shape(batch=2, moe=False):
+    """The test model: 8 heads, so that it shards over 2, 4 or 8 ranks; with
+    `moe`, its FFN routed experts (the top 2 of 8, ffn 256 each)."""
     from furykernel_b200.program.llama import LlamaShape
 
+    if moe:
+        return LlamaShape(d_model=512, heads=8, kv_heads=8, head_dim=128, ffn=256, vocab=3000, layers=2,
+                          slots=batch, length=64, positions=64, experts=8, top_k=2)
     return LlamaShape(d_model=512, heads=8, kv_heads=8, head_dim=128, ffn=1024, vocab=3000, layers=2, slots=batch,
                       length=64, positions=64)
 
@@ -50,7 +59,7 @@ def main():
 
     ctx, rank, world, local = tp.init()
     batch = 2
-    s = shape(batch)
+    s = shape(batch, moe=len(sys.argv) > 2 and sys.argv[2] == "moe")
     layers, embed, final_norm = model(s)
     arena = shard_weights(s, layers, embed, final_norm, rank, world, interleave=batch <= 4)
     eng = Llama(ctx, s, batch, chunk=16, rank=rank, world=world, host_weights=arena)
