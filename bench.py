@@ -45,10 +45,11 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--config", default="5", choices=["5", "1", "2", "3a", "3b", "3c", "4"],
                     help="5: the 32-layer decode step (default); 1, 2, 3a, 3b, 3c, 4: BASELINE's other configs")
-    ap.add_argument("--weights", default="f32", choices=["f32", "bf16"],
+    ap.add_argument("--weights", default="f32", choices=["f32", "bf16", "f16"],
                     help="config 5: the model's weights (f32, the BASELINE configuration; bf16, the reference's "
-                         "own element type)")
-    ap.add_argument("--cache", default="f32", choices=["f32", "bf16"], help="config 5: the KV caches' element type")
+                         "own element type; f16)")
+    ap.add_argument("--cache", default="f32", choices=["f32", "bf16", "f16"],
+                    help="config 5: the KV caches' element type")
     return ap.parse_args()
 
 
