@@ -14,7 +14,7 @@ _LIB = None
 _PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_build", "libfurykernel_host.so")
 
 FKH_OK, FKH_ERR_ARGUMENT, FKH_ERR_SPACE, FKH_ERR_INTERNAL = 0, 1, 2, 3
-ABI_VERSION = 8
+ABI_VERSION = 9
 
 
 # The shape's element-type codes, in order (fkh_llama_shape).
@@ -28,7 +28,8 @@ class Shape(ctypes.Structure):
                [(n, ctypes.c_uint64) for n in ("slots", "length", "positions")] + \
                [("weights_type", ctypes.c_int), ("cache_type", ctypes.c_int)] + \
                [("blocks", ctypes.c_uint64), ("block_size", ctypes.c_uint64)] + \
-               [("experts", ctypes.c_uint64), ("top_k", ctypes.c_uint64)]
+               [("experts", ctypes.c_uint64), ("top_k", ctypes.c_uint64)] + \
+               [("expert_scale", ctypes.c_int)]
 
 
 class PlanOptions(ctypes.Structure):
@@ -119,7 +120,7 @@ def shape(s) -> Shape:
             raise N.Refused(N.FKC_ERR_ARGUMENT, f"the {what}' element type {t} is not f32, bf16 or f16.")
     return Shape(s.d_model, s.heads, s.kv_heads, s.head_dim, s.ffn, s.vocab, s.layers, s.theta, s.eps, s.slots,
                  s.length, s.positions, ELEMENT_TYPES.index(s.weights), ELEMENT_TYPES.index(s.cache), s.blocks,
-                 s.block_size, s.experts, s.top_k)
+                 s.block_size, s.experts, s.top_k, int(getattr(s, "expert_scale", False)))
 
 
 def llama_program_text(s, which: str) -> str:

@@ -182,8 +182,10 @@ cudaError_t fk_launch_attend_paged(const FkAttend& a, const FkPaged& pg, const v
 cudaError_t fk_launch_attend_prompt_paged(const FkAttend& a, const FkPaged& pg, const void* kc, const void* vc,
                                           FkElem e, float* out, uint32_t ldo, uint32_t max_pos, cudaStream_t s);
 // Routed experts (k_moe.cu); the experts' table f32, bf16 or f16.
+// scale: the experts' scales of element type scale_elem, or null.
 cudaError_t fk_launch_route_topk(const float* x, uint32_t m, uint32_t n, uint32_t k, uint32_t ldx,
-                                 const float* scale, uint32_t* ids, float* ws, bool pdl, cudaStream_t s);
+                                 const void* scale, FkElem scale_elem, uint32_t* ids, float* ws, bool pdl,
+                                 cudaStream_t s);
 cudaError_t fk_launch_gemv_routed(const void* table, FkElem e, uint32_t entries, uint32_t n, uint32_t kk,
                                   const uint32_t* ids, uint32_t m, uint32_t k, const float* x, uint32_t ldx,
                                   bool per_rank, uint32_t split, float* y, uint32_t ldy, bool pdl, cudaStream_t s);

@@ -26,9 +26,20 @@ namespace moe {
 constexpr uint32_t kMaxRanks = 8;
 constexpr uint32_t kPairWindow = 1024;  // (row, rank) pairs a block lists at a time
 
+// An expert's scale: f32, or a 16-bit type widened exactly.
+template <class E>
+__device__ __forceinline__ float scale_of(const void* scale, uint32_t i) {
+  if constexpr (E::kElem == FK_F32)
+    return static_cast<const float*>(scale)[i];
+  else
+    return E::widen(static_cast<const uint16_t*>(scale)[i]);
+}
+
 // The route: a warp a row; lane l holds logits l, l + 32, ... (n <= 1024).
+// E: the expert scales' element type (scale null: no scales).
+template <class E>
 __global__ void __launch_bounds__(32) route_topk_kernel(const float* __restrict__ x, uint32_t n, uint32_t k,
-                                                        uint32_t ldx, const float* __restrict__ scale,
+                                                        uint32_t ldx, const void* __restrict__ scale,
                                                         uint32_t* __restrict__ ids, float* __restrict__ ws) {
   grid_wait();
   grid_launch_dependents();
@@ -77,7 +88,7 @@ __global__ void __launch_bounds__(32) route_topk_kernel(const float* __restrict_
     }
     for (uint32_t j = 0; j < k; ++j) {
       float w = __fdiv_rn(e[j], total);
-      if (scale) w = __fmul_rn(w, scale[picked[j]]);
+      if (scale) w = __fmul_rn(w, scale_of<E>(scale, picked[j]));
       ids[(size_t)r * k + j] = picked[j];
       ws[(size_t)r * k + j] = w;
     }
@@ -233,10 +244,22 @@ static unsigned grid_for(uint64_t n) {
 }  // namespace fk
 
 cudaError_t fk_launch_route_topk(const float* x, uint32_t m, uint32_t n, uint32_t k, uint32_t ldx,
-                                 const float* scale, uint32_t* ids, float* ws, bool pdl, cudaStream_t s) {
+                                 const void* scale, FkElem scale_elem, uint32_t* ids, float* ws, bool pdl,
+                                 cudaStream_t s) {
   if (m == 0) return cudaSuccess;
   if (n == 0 || n > 1024 || k == 0 || k > fk::moe::kMaxRanks || k > n || ldx < n) return cudaErrorInvalidValue;
-  return fk_launch_ex(fk::moe::route_topk_kernel, dim3(m), dim3(32), 0, s, pdl, x, n, k, ldx, scale, ids, ws);
+  switch (scale_elem) {
+    case FK_F32:
+      return fk_launch_ex(fk::moe::route_topk_kernel<fk::F32>, dim3(m), dim3(32), 0, s, pdl, x, n, k, ldx, scale,
+                          ids, ws);
+    case FK_BF16:
+      return fk_launch_ex(fk::moe::route_topk_kernel<fk::Bf16>, dim3(m), dim3(32), 0, s, pdl, x, n, k, ldx, scale,
+                          ids, ws);
+    case FK_F16:
+      return fk_launch_ex(fk::moe::route_topk_kernel<fk::F16>, dim3(m), dim3(32), 0, s, pdl, x, n, k, ldx, scale,
+                          ids, ws);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t fk_launch_gemv_routed(const void* table, FkElem el, uint32_t entries, uint32_t n, uint32_t kk,

@@ -857,11 +857,13 @@ int l_attend_prompt_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
 // ---- routed experts ------------------------------------------------------
 // route_topk: x ids ws | m n k ldx; route_topk_scaled: x scale ids ws | m n k ldx
 int l_route_topk(fkc_ctx* c, const Params& p, void* const* bufs) {
-  return launched(fk_launch_route_topk(CF(0), p.u(0), p.u(1), p.u(2), p.u(3), nullptr, U(1), F(2), c->pdl, c->stream),
+  return launched(fk_launch_route_topk(CF(0), p.u(0), p.u(1), p.u(2), p.u(3), nullptr, FK_F32, U(1), F(2), c->pdl,
+                                       c->stream),
                   "route_topk");
 }
 int l_route_topk_scaled(fkc_ctx* c, const Params& p, void* const* bufs) {
-  return launched(fk_launch_route_topk(CF(0), p.u(0), p.u(1), p.u(2), p.u(3), CF(1), U(2), F(3), c->pdl, c->stream),
+  return launched(fk_launch_route_topk(CF(0), p.u(0), p.u(1), p.u(2), p.u(3), bufs[1], FK_F32, U(2), F(3), c->pdl,
+                                       c->stream),
                   "route_topk_scaled");
 }
 // gemv_routed: table ids x y | entries n kk m k split ldx ldy per_rank
@@ -873,6 +875,13 @@ int gemv_routed(fkc_ctx* c, const Params& p, void* const* bufs, FkElem el, const
 }
 int l_gemv_routed(fkc_ctx* c, const Params& p, void* const* bufs) {
   return gemv_routed(c, p, bufs, FK_F32, "gemv_routed");
+}
+// route_topk_scaled with 16-bit expert scales (the model's weights' type).
+template <FkElem EL>
+int l_route_topk_scaled_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return launched(fk_launch_route_topk(CF(0), p.u(0), p.u(1), p.u(2), p.u(3), bufs[1], EL, U(2), F(3), c->pdl,
+                                       c->stream),
+                  WN("route_topk_scaled"));
 }
 template <FkElem EL>
 int l_gemv_routed_w16(fkc_ctx* c, const Params& p, void* const* bufs) {
@@ -1279,6 +1288,7 @@ std::vector<KernelSpec> make_table() {
       W_FORMS("rmsnorm_rows", l_rmsnorm_rows_w16, "gamma"),
       W_FORMS("split_tf32", l_split_tf32_w16, "x"),
       W_FORMS("gemv_routed", l_gemv_routed_w16, "table"),
+      W_FORMS("route_topk_scaled", l_route_topk_scaled_w16, "scale"),
       KV_FORMS("kv_store_ring", l_kv_store_kv16),
       KV_FORMS("attend_split", l_attend_kv16),
       KV_FORMS("attend_decode", l_attend_decode_kv16),

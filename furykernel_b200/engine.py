@@ -303,11 +303,14 @@ def lower_steps(p, step, b: Binding, tables: dict, attn: dict) -> list:
         out = []
         if "Route" in ops:
             r = node("Route")
-            if r.op.args[0].expert_scale is not None:
-                raise Unlowerable(N.FKC_ERR_ARGUMENT, f"{step.name}: no kernel scales a route's experts here.")
             logits, ids, ws = stored(r.op.values[0]), stored(r.outputs[0]), stored(r.outputs[1])
-            out.append(Launch("route_topk", {"m": b.m, "n": logits.width, "k": ids.width, "ldx": logits.ld},
-                              [logits.ptr, ids.ptr, ws.ptr]))
+            params = {"m": b.m, "n": logits.width, "k": ids.width, "ldx": logits.ld}
+            if r.op.args[0].expert_scale is not None:  # each expert's weight times its scale
+                sc = p.source(r.op.args[0].expert_scale)
+                out.append(Launch("route_topk_scaled" + _weight_suffix(step, sc.kind.type), params,
+                                  [logits.ptr, b.weights[sc.name], ids.ptr, ws.ptr]))
+            else:
+                out.append(Launch("route_topk", params, [logits.ptr, ids.ptr, ws.ptr]))
         if "GatedGelu" in ops:
             g = node("GatedGelu")
             gu, x = stored(g.op.values[0]), stored(g.outputs[0])
@@ -390,6 +393,9 @@ class Llama:
             raise N.Refused(N.FKC_ERR_ARGUMENT, f"no kernels for {s.weights} weights and {s.cache} caches.")
         if s.experts > 1024:
             raise N.Refused(N.FKC_ERR_ARGUMENT, "routed experts: at most 1024 experts.")
+        if s.experts and s.expert_scale and (s.experts * self.wb) % 16:
+            raise N.Refused(N.FKC_ERR_ARGUMENT, "expert scales: the experts' scales must fill whole 16 bytes, so that "
+                                                "the weights after them start on a 16-byte boundary.")
         if self.wb == 2 and any(n % 8 for n in (s.d_model, s.q_width, s.kv_width, s.ffn)):
             raise N.Refused(N.FKC_ERR_ARGUMENT, "16-bit weights: d_model, the q and kv widths and ffn must be "
                             "multiples of 8, so that every weight starts on a 16-byte boundary.")
@@ -429,8 +435,10 @@ class Llama:
             for l in range(s.layers):
                 w = self.layer_weights(l)
                 fill(N.DeviceBuffer(ctx, w["attn_norm"], 2 * wb * d), seed + 3 * l + 1, 0.0, 0.02)
-                if s.experts:  # the router is whole on every rank
+                if s.experts:  # the router (and the experts' scales) whole on every rank
                     fill(N.DeviceBuffer(ctx, w["router"], wb * s.experts * d), seed + 611953 + l, 0.0, 0.02)
+                    if s.expert_scale:
+                        fill(N.DeviceBuffer(ctx, w["expert_scale"], wb * s.experts), seed + 711957 + l, 1.0, 0.25)
         else:
             self.arena.upload(host_weights)
         self.cos, self.sin = ctx.rope_tables(s.theta, s.head_dim, s.head_dim // 2, s.positions)
@@ -524,6 +532,8 @@ class Llama:
                  "mlp_norm")
 
     def layer_order(self) -> tuple:
+        if self.s.experts and getattr(self.s, "expert_scale", False):  # the scales after the router
+            return self.MOE_ORDER[:5] + ("expert_scale",) + self.MOE_ORDER[5:]
         return self.MOE_ORDER if self.s.experts else self.LAYER_ORDER
 
     def _fill(self, t: str):
@@ -536,7 +546,9 @@ class Llama:
         s = self.s
         d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
         if s.experts:
-            return [qw * d, kvw * d, kvw * d, d * qw, s.experts * d, s.experts * 2 * f * d, s.experts * d * f, d, d]
+            scale = [s.experts] if getattr(s, "expert_scale", False) else []
+            return [qw * d, kvw * d, kvw * d, d * qw, s.experts * d] + scale + \
+                [s.experts * 2 * f * d, s.experts * d * f, d, d]
         return [qw * d, kvw * d, kvw * d, d * qw, f * d, f * d, d * f, d, d]
 
     def layer_weights(self, l: int) -> dict:
@@ -870,7 +882,8 @@ def shard_weights(full: LlamaShape, layers: list, embed: np.ndarray, final_norm:
         if full.experts:
             f = full.ffn
             egu = np.concatenate([w["egu"][:, fs], w["egu"][:, f + rank * fl:f + (rank + 1) * fl]], axis=1)
-            parts += [w["router"], egu, np.ascontiguousarray(w["edn"][:, :, fs]), w["attn_norm"], w["mlp_norm"]]
+            parts += [w["router"]] + ([w["expert_scale"]] if full.expert_scale else [])
+            parts += [egu, np.ascontiguousarray(w["edn"][:, :, fs]), w["attn_norm"], w["mlp_norm"]]
             continue
         gate, up = w["gate"][fs], w["up"][fs]
         gu = np.stack([gate, up], axis=1).reshape(2 * fl, d) if interleave else [gate, up]

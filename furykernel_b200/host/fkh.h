@@ -177,6 +177,10 @@ struct LlamaShape {
   // Routed experts in place of the dense FFN: `experts` of ffn each, every
   // row taking its top_k (experts 0: the dense SiLU-gated FFN).
   uint64_t experts = 0, top_k = 2;
+  // Each chosen expert's weight times its own scale (the route's expert
+  // scale, RouteSpec, Graph.hs:249-257): a weight [experts] of the
+  // weights' type after the router.
+  bool expert_scale = false;
   // A paged cache (Graph.hs:144-152) instead of the ring: a pool of `blocks`
   // blocks of `block_size` positions a layer, each row's block table of
   // table_len() entries. block_size 0: the ring of `slots` and `length`.

@@ -66,6 +66,7 @@ fkh::LlamaShape shape_of(const fkh_llama_shape& s) {
                        std::to_string(s.cache_type) + ", not 0 (f32), 1 (bf16) or 2 (f16).");
   o.weights = types[s.weights_type];
   o.cache = types[s.cache_type];
+  o.expert_scale = s.expert_scale != 0;
   o.blocks = s.blocks;
   o.block_size = s.block_size;
   o.experts = s.experts;

@@ -393,11 +393,16 @@ std::vector<Launch> lower_steps(const Program& p, const Step& step, const Bindin
     std::vector<Launch> out;
     if (lone_route || routed_route) {
       const Node& r = node("Route");
-      if (r.op.route.expert_scale) throw Refusal(step.name + ": no kernel scales a route's experts here.");
       const View logits = stored(r.op.values[0]), ids = stored(r.outputs[0]), ws = stored(r.outputs[1]);
-      out.push_back(make("route_topk",
-                         {{"m", m}, {"n", (double)logits.width}, {"k", (double)ids.width}, {"ldx", (double)logits.ld}},
-                         {logits.ptr(), ids.ptr(), ws.ptr()}));
+      const std::vector<std::pair<std::string, double>> params = {
+          {"m", m}, {"n", (double)logits.width}, {"k", (double)ids.width}, {"ldx", (double)logits.ld}};
+      if (r.op.route.expert_scale) {  // each expert's weight times its scale
+        const Source& sc = p.sources[*r.op.route.expert_scale];
+        out.push_back(make("route_topk_scaled" + weight_form(sc.kind.type, step.name), params,
+                           {logits.ptr(), weight(sc.name), ids.ptr(), ws.ptr()}));
+      } else {
+        out.push_back(make("route_topk", params, {logits.ptr(), ids.ptr(), ws.ptr()}));
+      }
     }
     if (lone_gate || routed_gate) {
       const Node& g = node("GatedGelu");
@@ -652,41 +657,37 @@ namespace {
 // A layer's weights in the arena, in order: q k v o, the dense FFN's gate
 // up down (or the router and the experts' gate/up and down tables), the
 // two norms.
-void layer_layout(const LlamaShape& s, uint64_t (&sizes)[9], const char* (&names)[9]) {
+// A layer's weights in the arena, in order: (name, elements).
+std::vector<std::pair<const char*, uint64_t>> layer_layout(const LlamaShape& s) {
   const uint64_t dm = s.d_model, qw = s.q_width(), kvw = s.kv_width(), f = s.ffn, e = s.experts;
-  const uint64_t dense[9] = {qw * dm, kvw * dm, kvw * dm, dm * qw, f * dm, f * dm, dm * f, dm, dm};
-  const uint64_t moe[9] = {qw * dm, kvw * dm, kvw * dm, dm * qw, e * dm, e * 2 * f * dm, e * dm * f, dm, dm};
-  const char* dn[9] = {"q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj", "attn_norm",
-                       "mlp_norm"};
-  const char* mn[9] = {"q_proj", "k_proj", "v_proj", "o_proj", "router", "experts_gate_up", "experts_down",
-                       "attn_norm", "mlp_norm"};
-  for (int i = 0; i < 9; ++i) {
-    sizes[i] = e ? moe[i] : dense[i];
-    names[i] = e ? mn[i] : dn[i];
+  std::vector<std::pair<const char*, uint64_t>> out = {
+      {"q_proj", qw * dm}, {"k_proj", kvw * dm}, {"v_proj", kvw * dm}, {"o_proj", dm * qw}};
+  if (e) {
+    out.push_back({"router", e * dm});
+    if (s.expert_scale) out.push_back({"expert_scale", e});
+    out.insert(out.end(), {{"experts_gate_up", e * 2 * f * dm}, {"experts_down", e * dm * f}});
+  } else {
+    out.insert(out.end(), {{"gate_proj", f * dm}, {"up_proj", f * dm}, {"down_proj", dm * f}});
   }
+  out.insert(out.end(), {{"attn_norm", dm}, {"mlp_norm", dm}});
+  return out;
 }
 
 }  // namespace
 
 uint64_t layer_elems(const LlamaShape& s) {
-  uint64_t sizes[9];
-  const char* names[9];
-  layer_layout(s, sizes, names);
   uint64_t t = 0;
-  for (uint64_t v : sizes) t += v;
+  for (const auto& [name, n] : layer_layout(s)) t += n;
   return t;
 }
 
 std::map<std::string, uint64_t> layer_weights(const LlamaShape& s, uint64_t arena, uint64_t l) {
-  uint64_t sizes[9];
-  const char* names[9];
-  layer_layout(s, sizes, names);
   std::map<std::string, uint64_t> w;
   const uint64_t wb = s.weight_bytes();
   uint64_t at = arena + wb * l * layer_elems(s);
-  for (int i = 0; i < 9; ++i) {
-    w[names[i]] = at;
-    at += wb * sizes[i];
+  for (const auto& [name, n] : layer_layout(s)) {
+    w[name] = at;
+    at += wb * n;
   }
   return w;
 }

@@ -162,8 +162,13 @@ std::vector<Launch> prefill_launches(const LlamaLaunchDesc& d, const PrefillDesc
                          {{"n", (double)e}, {"k", (double)dm}, {"m", md}, {"split", 1.0}, {"ldx", (double)dm},
                           {"ldy", (double)e}},
                          {w.at("router"), p.a, p.router_logits}));
-      out.push_back(make("route_topk", {{"m", md}, {"n", (double)e}, {"k", (double)k}, {"ldx", (double)e}},
-                         {p.router_logits, p.route_ids, p.route_weights}));
+      const std::vector<std::pair<std::string, double>> rp = {
+          {"m", md}, {"n", (double)e}, {"k", (double)k}, {"ldx", (double)e}};
+      if (s.expert_scale)
+        out.push_back(make("route_topk_scaled" + wsuf, rp,
+                           {p.router_logits, w.at("expert_scale"), p.route_ids, p.route_weights}));
+      else
+        out.push_back(make("route_topk", rp, {p.router_logits, p.route_ids, p.route_weights}));
       auto routed = [&](uint64_t table, uint64_t n, uint64_t kk, uint64_t x, uint64_t ldx, uint64_t y, bool per_rank) {
         return make("gemv_routed" + wsuf,
                     {{"entries", (double)e},

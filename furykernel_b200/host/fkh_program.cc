@@ -272,8 +272,10 @@ Program layer_program(const LlamaShape& s, const std::string& name) {
   const int mlp_norm = b.weight("mlp_norm", {s.d_model}, s.weights);
   // The dense FFN's weights, or the router and the experts' tables.
   int wg = -1, wu = -1, wd = -1, router = -1, egu = -1, edn = -1;
+  std::optional<int> expert_scale;
   if (s.experts) {
     router = b.weight("router", {s.experts, s.d_model}, s.weights);
+    if (s.expert_scale) expert_scale = b.weight("expert_scale", {s.experts}, s.weights);
     egu = b.table("experts_gate_up", s.experts, {2 * s.ffn, s.d_model}, s.weights);
     edn = b.table("experts_down", s.experts, {s.d_model, s.ffn}, s.weights);
   } else {
@@ -306,7 +308,7 @@ Program layer_program(const LlamaShape& s, const std::string& name) {
   int ffn_out;
   if (s.experts) {  // each row's top_k experts, GELU-gated, weighted by the route
     const int logits = b.linear("router_logits", router, 0, m);
-    const auto [ids, ws] = b.route("route", s.top_k, std::nullopt, logits);
+    const auto [ids, ws] = b.route("route", s.top_k, expert_scale, logits);
     const int gu = b.linear_routed("experts_gu", egu, ids, m);
     const int act = b.gated_gelu("experts_act", gu);
     const int eo = b.linear_routed("experts_out", edn, ids, act);

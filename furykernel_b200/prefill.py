@@ -206,8 +206,12 @@ class Prefill:
                 e, k, b = s.experts, s.top_k, {n: v.ptr for n, v in self.moe.items()}
                 out.append(Launch("gemv" + wsuf, {"n": e, "k": d, "m": m, "split": 1, "ldx": d, "ldy": e},
                                   [w["router"], self.a.ptr, b["router_logits"]]))
-                out.append(Launch("route_topk", {"m": m, "n": e, "k": k, "ldx": e},
-                                  [b["router_logits"], b["route_ids"], b["route_weights"]]))
+                rp = {"m": m, "n": e, "k": k, "ldx": e}
+                if s.expert_scale:
+                    out.append(Launch("route_topk_scaled" + wsuf, rp, [b["router_logits"], w["expert_scale"],
+                                                                       b["route_ids"], b["route_weights"]]))
+                else:
+                    out.append(Launch("route_topk", rp, [b["router_logits"], b["route_ids"], b["route_weights"]]))
 
                 def routed(table, n, kk, x, ldx, y, per_rank):
                     return Launch("gemv_routed" + wsuf, {"entries": e, "n": n, "kk": kk, "m": m, "k": k, "split": 1,

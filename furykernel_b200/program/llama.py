@@ -43,6 +43,9 @@ class LlamaShape:
     # row taking its top_k (experts 0: the dense SiLU-gated FFN).
     experts: int = 0
     top_k: int = 2
+    # Each chosen expert's weight times its own scale (the route's expert
+    # scale, RouteSpec, Graph.hs:249-257): a weight [experts] after the router.
+    expert_scale: bool = False
 
     @property
     def q_width(self):
@@ -79,6 +82,7 @@ def layer_program(s: LlamaShape, name: str = "layer"):
     # The dense FFN's weights, or the router and the experts' tables.
     if s.experts:
         router = b.weight("router", [s.experts, s.d_model], s.weights)
+        scale = b.weight("expert_scale", [s.experts], s.weights) if s.expert_scale else None
         egu = b.table("experts_gate_up", s.experts, [2 * s.ffn, s.d_model], s.weights)
         edn = b.table("experts_down", s.experts, [s.d_model, s.ffn], s.weights)
     else:
@@ -105,7 +109,7 @@ def layer_program(s: LlamaShape, name: str = "layer"):
     m = b.rmsnorm("mlp_in", s.eps, mlp_norm, 1.0, x1)
     if s.experts:  # each row's top_k experts, GELU-gated, weighted by the route
         logits = b.linear("router_logits", router, 0, m)
-        ids, ws = b.route("route", s.top_k, None, logits)
+        ids, ws = b.route("route", s.top_k, scale, logits)
         gu = b.linear_routed("experts_gu", egu, ids, m)
         act = b.gated_gelu("experts_act", gu)
         eo = b.linear_routed("experts_out", edn, ids, act)

@@ -227,7 +227,7 @@ _VARIANTS = [
     *[(base, base + WEIGHT_SUFFIX[t], {buf}, t)
       for t in ("bf16", "f16")
       for base, buf in (("gather", "table"), ("rmsnorm_rows", "gamma"), ("split_tf32", "x"),
-                        ("gemv_routed", "table"))],
+                        ("gemv_routed", "table"), ("route_topk_scaled", "scale"))],
     *[(base, base + CACHE_SUFFIX[t], {"k_cache", "v_cache"}, t)
       for t in ("bf16", "f16")
       for base in ("kv_store_ring", "attend_split", "attend_decode", "attend_prompt", "kv_store_paged",

@@ -40,7 +40,7 @@ enum {
 };
 
 /* The library's ABI version (this header's FKH_ABI_VERSION). */
-#define FKH_ABI_VERSION 8
+#define FKH_ABI_VERSION 9
 FKH_API int fkh_abi_version(void);
 
 /* A Llama-shaped model (the shapes of the programs the engine plans). */
@@ -59,6 +59,9 @@ typedef struct {
   /* Routed experts in place of the dense FFN: `experts` of ffn each, every
    * row its top_k (experts 0: the dense FFN). */
   uint64_t experts, top_k;
+  /* Each chosen expert's weight times its scale, a weight [experts] after
+   * the router (the route's expert scale, RouteSpec, Graph.hs:249-257). */
+  int expert_scale;
 } fkh_llama_shape;
 
 /* The planner's options (PlanOptions, src/FuryKernel/Program/Plan.hs:243-268). */

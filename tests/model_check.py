@@ -51,7 +51,9 @@ def host_model(eng):
         at = base
         w = {}
         e = getattr(s, "experts", 0)
-        ffn = [("router", e, d), ("egu", e * 2 * f, d), ("edn", e * d, f)] if e else [("gu", 2 * f, d), ("down", d, f)]
+        scale = [("expert_scale", 1, e)] if e and getattr(s, "expert_scale", False) else []
+        ffn = [("router", e, d)] + scale + [("egu", e * 2 * f, d), ("edn", e * d, f)] if e else \
+            [("gu", 2 * f, d), ("down", d, f)]
         for name, rows, cols in [("qkv", qw + 2 * kvw, d), ("o", d, qw)] + ffn + [("attn_norm", 1, d),
                                                                                    ("mlp_norm", 1, d)]:
             w[name] = flat[at:at + rows * cols].reshape(rows, cols) if rows > 1 else flat[at:at + cols].copy()
@@ -145,7 +147,7 @@ def oracle_decode(eng, layers, embed, final_norm, kcache, vcache, tokens, pos, s
         if getattr(s, "experts", 0):  # the router, the top k, the experts' GELU-gated FFNs, their weighted sum
             m_in = O.rmsnorm_rows(x1, w["mlp_norm"], eps, 1.0, threads)
             logits = O.gemv(w["router"], m_in, next(splits), threads)
-            ids, ws = O.route_topk(logits, s.top_k)
+            ids, ws = O.route_topk(logits, s.top_k, w.get("expert_scale"))
             gu = O.gemv_routed(w["egu"], ids, m_in, next(splits), threads)
             eo = O.gemv_routed(w["edn"], ids, O.gated_gelu(gu, f), next(splits), threads)
             x = O.combine_ranks_add(x1, ws, eo)
@@ -204,7 +206,7 @@ def oracle_decode_tp(s, world, layers, embed, final_norm, kcache, vcache, tokens
         m2 = O.rmsnorm_rows(x1, w["mlp_norm"], eps, 1.0, threads)
         parts = []
         if getattr(s, "experts", 0):
-            ids, ws = O.route_topk(O.gemv(w["router"], m2, 1, threads), s.top_k)
+            ids, ws = O.route_topk(O.gemv(w["router"], m2, 1, threads), s.top_k, w.get("expert_scale"))
             for r in range(world):
                 egu = np.ascontiguousarray(np.concatenate(
                     [w["egu"][:, r * fl:(r + 1) * fl], w["egu"][:, s.ffn + r * fl:s.ffn + (r + 1) * fl]], axis=1))

@@ -232,6 +232,11 @@ CASES = (
        for b in (1, 5)]
     + [(dataclasses.replace(small(b), experts=8, top_k=2, weights="bf16", cache="bf16"), b, 0, 1, True, None)
        for b in (1, 12)]
+    # a route with expert scales (a weight of the model's type after the router)
+    + [(dataclasses.replace(small(b), experts=8, top_k=2, expert_scale=True, weights=w), b, 0, 1, True, None)
+       for b in (1, 9) for w in ("f32", "bf16", "f16")]
+    + [(dataclasses.replace(tp_shape(2), ffn=256, experts=8, top_k=2, expert_scale=True), 2, r, 2, False, None)
+       for r in (0, 1)]
     # routed experts over ranks: each rank's ffn slice of every expert, the sums by NCCL
     + [(dataclasses.replace(tp_shape(b), ffn=256, experts=8, top_k=2), b, r, w, peer, None) for w in (2, 4)
        for r in (0, w - 1) for b in (1, 5) for peer in (True, False)]
@@ -353,6 +358,8 @@ PREFILL_CASES = (
                                   (1, 128, False, 70, "f16"))]
     + [(dataclasses.replace(small(4), experts=4, top_k=1, blocks=64, block_size=16), 4, 0, 1, True, 96, True, 50)]
     + [(dataclasses.replace(tp_shape(2), ffn=256, experts=8, top_k=2), 2, r, 2, False, 64, False, 40) for r in (0, 1)]
+    + [(dataclasses.replace(small(2), experts=8, top_k=2, expert_scale=True, weights="bf16"), 2, 0, 1, True, 64,
+        False, 40)]
     # f16 weights and caches, ring and paged
     + [(dataclasses.replace(small(b), weights="f16", cache="f16"), b, 0, 1, True, 128, one, m)
        for b, one, m in ((1, False, 100), (1, True, 64))]

@@ -54,6 +54,13 @@ def test_route_topk(ctx, m, n, k):
     ctx.launch("route_topk_scaled", {"m": m, "n": n, "k": k, "ldx": n}, [xd, sd, ids, ws])
     want_ids, want_ws = O.route_topk(x, k, scale)
     assert np.array_equal(ids.download(), want_ids) and same_bits(ws.download(), want_ws)
+    for t in ("bf16", "f16"):  # scales of the weights' 16-bit type, widened where read
+        bits = MC.narrow(t, scale)
+        bd = ctx.to_device(bits)
+        ctx.launch("route_topk_scaled" + WEIGHT_SUFFIX[t], {"m": m, "n": n, "k": k, "ldx": n}, [xd, bd, ids, ws])
+        want_ids, want_ws = O.route_topk(x, k, MC.widen(t, bits))
+        assert np.array_equal(ids.download(), want_ids) and same_bits(ws.download(), want_ws)
+        bd.free()
     for b in (xd, ids, ws, sd):
         b.free()
 
@@ -106,7 +113,8 @@ def test_gated_gelu_and_combine(ctx):
 @pytest.mark.parametrize("batch,experts,top_k,weights,gated,store_gelus", [
     (1, 8, 2, "f32", False, False), (3, 8, 2, "f32", False, False), (9, 16, 4, "f32", False, False),
     (2, 8, 2, "bf16", False, False), (12, 8, 2, "bf16", False, False), (5, 8, 2, "f16", False, False),
-    (3, 8, 2, "f32", True, False), (3, 8, 2, "f32", True, True), (4, 8, 2, "bf16", False, True)])
+    (3, 8, 2, "f32", True, False), (3, 8, 2, "f32", True, True), (4, 8, 2, "bf16", False, True),
+    (3, 8, 2, "f32", "scale", False), (2, 8, 2, "bf16", "scale", False)])
 def test_moe_model_decode_step(ctx, batch, experts, top_k, weights, gated, store_gelus):
     """A decode step of a model whose FFN is routed experts, captured as a
     graph, against the oracle's decode: the same ids, logits and residual
@@ -115,8 +123,10 @@ def test_moe_model_decode_step(ctx, batch, experts, top_k, weights, gated, store
     from furykernel_b200.engine import Llama
     from furykernel_b200.program.llama import LlamaShape
 
+    scaled = gated == "scale"  # the route's expert scales, the default plan
+    gated = gated is True
     s = LlamaShape(d_model=512, heads=4, kv_heads=4, head_dim=128, ffn=256, vocab=3000, layers=2, slots=batch,
-                   length=96, positions=96, experts=experts, top_k=top_k, weights=weights)
+                   length=96, positions=96, experts=experts, top_k=top_k, weights=weights, expert_scale=scaled)
     eng = Llama(ctx, s, batch, seed=500 + batch, chunk=32, prefill_kv=1.0, gated=gated, store_gelus=store_gelus)
     tokens = O.ints(29 + batch, batch, s.vocab)
     pos = ((np.arange(batch) * 37 + 5) % 96).astype(np.uint32)
