@@ -867,10 +867,11 @@ def shard_weights(full: LlamaShape, layers: list, embed: np.ndarray, final_norm:
 
     `layers` holds per layer the f32 arrays q [H*hd, d], k and v
     [KV*hd, d], o [d, H*hd], gate and up [F, d], down [d, F], attn_norm and
-    mlp_norm [d]; with routed experts, router [E, d], egu [E, 2F, d] (each
-    expert's gate rows, then its up rows) and edn [E, d, F] in place of gate,
-    up and down. A rank holds the whole router and, of every expert, the
-    gate and up rows and the down columns of its ffn slice."""
+    mlp_norm [d]; with routed experts, router [E, d], expert_scale [E] (with
+    the shape's expert_scale), egu [E, 2F, d] (each expert's gate rows, then
+    its up rows) and edn [E, d, F] in place of gate, up and down. A rank
+    holds the whole router and scales and, of every expert, the gate and up
+    rows and the down columns of its ffn slice."""
     hd, d = full.head_dim, full.d_model
     hq, hk, fl = full.heads // world, full.kv_heads // world, full.ffn // world
     qs = slice(rank * hq * hd, (rank + 1) * hq * hd)
