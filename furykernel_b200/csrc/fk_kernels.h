@@ -181,6 +181,9 @@ cudaError_t fk_launch_attend_paged(const FkAttend& a, const FkPaged& pg, const v
                                    cudaStream_t s);
 cudaError_t fk_launch_attend_prompt_paged(const FkAttend& a, const FkPaged& pg, const void* kc, const void* vc,
                                           FkElem e, float* out, uint32_t ldo, uint32_t max_pos, cudaStream_t s);
+// The KV store folded into the split attention (every table entry distinct).
+cudaError_t fk_launch_attend_decode_paged(const FkAttend& a, const FkPaged& pg, void* kc, void* vc, FkElem e,
+                                          uint32_t k_off, uint32_t v_off, cudaStream_t s);
 // Routed experts (k_moe.cu); the experts' table f32, bf16 or f16.
 // scale: the experts' scales of element type scale_elem, or null.
 cudaError_t fk_launch_route_topk(const float* x, uint32_t m, uint32_t n, uint32_t k, uint32_t ldx,

@@ -126,15 +126,37 @@ struct AttendArgs {
   Pool P;
   const St<E>* kc;
   const St<E>* vc;
+  uint32_t k_off, v_off;  // FUSED: the new key's and value's columns in a qkv row
+  St<E>* kc_w;            // FUSED: the caches, written
+  St<E>* vc_w;
 };
+
+// A value as a cache of type E holds it.
+template <class E>
+__device__ __forceinline__ float as_held(float v) {
+  if constexpr (E::kElem == FK_F32)
+    return v;
+  else
+    return E::widen(E::narrow(v));
+}
 
 // The attention anchor: persistent blocks of 4 warps over the step's items
 // (row, head, split), item i at block i mod G; warp w takes positions w,
 // w + 4, ... of its split, 8 at a time (the ring kernel's order).
-template <class E>
+//
+// FUSED (attend_decode_paged): the KV store folded in, as the ring's
+// attend_decode does it. The split that holds the row's position p uses
+// the new key (rotated) and value as the cache holds them, in place of what
+// it loads at p, and one block a (row, KV head) stores them. The same bits
+// as the store then the attention, when no row reads an element another
+// row stores in the same step: every block-table entry distinct (the
+// engine checks its tables for that).
+template <class E, bool FUSED>
 __global__ void __launch_bounds__(128, 4) attend_paged_kernel(AttendArgs<E> f) {
   const FkAttend& a = f.a;
   __shared__ float qrot[kHeadDim];
+  __shared__ float krot[FUSED ? kHeadDim : 1];
+  __shared__ float vnew[FUSED ? kHeadDim : 1];
   __shared__ float scores[kMaxChunk];
   __shared__ float4 accw[kAttWarps][kHeadDim / 4];
   __shared__ float lw[kAttWarps];
@@ -172,6 +194,7 @@ __global__ void __launch_bounds__(128, 4) attend_paged_kernel(AttendArgs<E> f) {
     const uint32_t t0 = j * a.chunk;
     const uint32_t t1 = min(p + 1, t0 + a.chunk);
     const uint32_t kvh = h / group;
+    const bool fresh = FUSED && j == splits - 1;  // the split that holds p
 
     float4 kv[B], vv[B];
 #pragma unroll
@@ -190,7 +213,27 @@ __global__ void __launch_bounds__(128, 4) attend_paged_kernel(AttendArgs<E> f) {
       qrot[threadIdx.x] = q0;
       qrot[threadIdx.x + kHeadDim / 2] = q1;
     }
+    if (fresh) {
+      const float* krow = a.qkv + (size_t)r * a.ldq + f.k_off + (size_t)kvh * kHeadDim;
+      const float* vrow = a.qkv + (size_t)r * a.ldq + f.v_off + (size_t)kvh * kHeadDim;
+      if (threadIdx.x >= kHeadDim / 2) {
+        const uint32_t i = threadIdx.x - kHeadDim / 2;
+        float k0, k1;
+        rope2(krow, i, kHeadDim / 2, a.rotated, a.cos_t + (size_t)p * a.rotated, a.sin_t + (size_t)p * a.rotated,
+              k0, k1);
+        krot[i] = as_held<E>(k0);
+        krot[i + kHeadDim / 2] = as_held<E>(k1);
+      }
+      vnew[threadIdx.x] = as_held<E>(vrow[threadIdx.x]);
+    }
     __syncthreads();
+    if (fresh && h % group == 0) {  // the KV store, once a (row, KV head)
+      const uint64_t at = at_of(f.P, r, p, kvh, a.kv_heads, kHeadDim);
+      if (at != ~0ull) {
+        st_elem<E>(f.kc_w + at + threadIdx.x, krot[threadIdx.x]);
+        st_elem<E>(f.vc_w + at + threadIdx.x, vnew[threadIdx.x]);
+      }
+    }
     const float4 qv = reinterpret_cast<const float4*>(qrot)[lane];
 
     for (uint32_t t = t0 + warp; t < t1; t += kStep) {
@@ -205,7 +248,9 @@ __global__ void __launch_bounds__(128, 4) attend_paged_kernel(AttendArgs<E> f) {
 #pragma unroll
       for (int u = 0; u < B; ++u) {
         const uint32_t tt = t + u * kAttWarps;
-        const float sc = __fmul_rn(warp_sum(__fadd_rn(0.0f, pack_dot(qv, kv[u]))), a.scale);
+        float4 kk = kv[u];
+        if (fresh && tt == p) kk = reinterpret_cast<const float4*>(krot)[lane];
+        const float sc = __fmul_rn(warp_sum(__fadd_rn(0.0f, pack_dot(qv, kk))), a.scale);
         if (lane == 0 && tt < t1) scores[tt - t0] = sc;
       }
     }
@@ -232,7 +277,7 @@ __global__ void __launch_bounds__(128, 4) attend_paged_kernel(AttendArgs<E> f) {
         const uint32_t tt = t + u * kAttWarps;
         const float e = __shfl_sync(0xffffffffu, e_lane, warp + u * kAttWarps);
         if (tt < t1) {
-          const float4 v4 = vv[u];
+          const float4 v4 = fresh && tt == p ? reinterpret_cast<const float4*>(vnew)[lane] : vv[u];
           l = __fadd_rn(l, e);
           acc.x = __fadd_rn(acc.x, __fmul_rn(e, v4.x));
           acc.y = __fadd_rn(acc.y, __fmul_rn(e, v4.y));
@@ -386,19 +431,27 @@ cudaError_t launch_store(const FkKvStore& a, const FkPaged& pg, void* kc, void* 
   return fk_launch_ex(kv_store_paged_kernel<E>, dim3(a.kv_heads, a.m), dim3(a.d / 2), 0, s, a.pdl, st);
 }
 
-template <class E>
-cudaError_t launch_attend(const FkAttend& a, const FkPaged& pg, const void* kc, const void* vc, cudaStream_t s) {
+template <class E, bool FUSED>
+cudaError_t launch_attend(const FkAttend& a, const FkPaged& pg, const void* kc, const void* vc, uint32_t k_off,
+                          uint32_t v_off, cudaStream_t s) {
   if (a.m == 0) return cudaSuccess;
   if (a.d != kHeadDim || a.chunk == 0 || a.chunk > kMaxChunk || a.kv_heads == 0 || a.heads % a.kv_heads != 0 ||
       a.m > kMaxAttendRows || (uint64_t)a.m * a.heads * a.max_splits >= (1ull << 32) || pg.block_size == 0 ||
       pg.table_len == 0 || !pg.table || !kc || !vc)
     return cudaErrorInvalidValue;
-  AttendArgs<E> f;
+  AttendArgs<E> f = {};
   f.a = a;
   f.P = Pool{pg.table, pg.block_size, pg.table_len, pg.blocks};
   f.kc = static_cast<const St<E>*>(kc);
   f.vc = static_cast<const St<E>*>(vc);
-  auto kern = attend_paged_kernel<E>;
+  if (FUSED) {
+    if (a.rotated > kHeadDim / 2) return cudaErrorInvalidValue;
+    f.k_off = k_off;
+    f.v_off = v_off;
+    f.kc_w = const_cast<St<E>*>(f.kc);
+    f.vc_w = const_cast<St<E>*>(f.vc);
+  }
+  auto kern = attend_paged_kernel<E, FUSED>;
   int dev = 0, sms = 148, per_sm = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -426,7 +479,7 @@ cudaError_t launch_prompt(const FkAttend& a, const FkPaged& pg, const void* kc, 
   auto kern = attend_prompt_paged_kernel<E>;
   cudaError_t e = fk_allow_smem(kern, smem);
   if (e != cudaSuccess) return e;
-  AttendArgs<E> f;
+  AttendArgs<E> f = {};
   f.a = a;
   f.P = Pool{pg.table, pg.block_size, pg.table_len, pg.blocks};
   f.kc = static_cast<const St<E>*>(kc);
@@ -454,7 +507,14 @@ cudaError_t fk_launch_kv_store_paged(const FkKvStore& a, const FkPaged& pg, void
 
 cudaError_t fk_launch_attend_paged(const FkAttend& a, const FkPaged& pg, const void* kc, const void* vc, FkElem e,
                                    cudaStream_t s) {
-#define CALL(E) fk::paged::launch_attend<E>(a, pg, kc, vc, s)
+#define CALL(E) fk::paged::launch_attend<E, false>(a, pg, kc, vc, 0, 0, s)
+  return FK_BY_ELEM(e, CALL);
+#undef CALL
+}
+
+cudaError_t fk_launch_attend_decode_paged(const FkAttend& a, const FkPaged& pg, void* kc, void* vc, FkElem e,
+                                          uint32_t k_off, uint32_t v_off, cudaStream_t s) {
+#define CALL(E) fk::paged::launch_attend<E, true>(a, pg, kc, vc, k_off, v_off, s)
   return FK_BY_ELEM(e, CALL);
 #undef CALL
 }

@@ -940,6 +940,31 @@ template <FkElem EL>
 int l_attend_paged_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
   return attend_paged(c, p, bufs, EL, KN("attend_split_paged"));
 }
+// attend_decode_paged: qkv cos sin pos table k_cache v_cache part_m part_l part_acc
+//   | m heads kv_heads d block_size table_len blocks rotated chunk max_splits ldq q_off k_off v_off scale
+// The KV store folded into the split attention; every block-table entry
+// distinct (no row reads what another row stores).
+int attend_decode_paged(fkc_ctx* c, const Params& p, void* const* bufs, FkElem el, const char* name) {
+  FkAttend a = {};
+  a.qkv = CF(0), a.cos_t = CF(1), a.sin_t = CF(2), a.pos = CU(3);
+  a.part_m = F(7), a.part_l = F(8), a.part_acc = F(9);
+  a.m = p.u(0), a.heads = p.u(1), a.kv_heads = p.u(2), a.d = p.u(3), a.rotated = p.u(7);
+  a.chunk = p.u(8), a.max_splits = p.u(9), a.ldq = p.u(10), a.q_off = p.u(11);
+  a.scale = p.f(14);
+  a.pdl = c->pdl;
+  const FkPaged pg = {CU(4), p.u(4), p.u(5), p.u(6)};
+  if (a.kv_heads == 0 || a.heads % a.kv_heads != 0)
+    return fail(FKC_ERR_ARGUMENT, "%s: %u heads do not share %u KV heads in groups.", name, a.heads, a.kv_heads);
+  if (a.rotated > a.d / 2) return fail(FKC_ERR_ARGUMENT, "%s: rotated %u is more than d/2.", name, a.rotated);
+  return launched(fk_launch_attend_decode_paged(a, pg, bufs[5], bufs[6], el, p.u(12), p.u(13), c->stream), name);
+}
+int l_attend_decode_paged(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return attend_decode_paged(c, p, bufs, FK_F32, "attend_decode_paged");
+}
+template <FkElem EL>
+int l_attend_decode_paged_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
+  return attend_decode_paged(c, p, bufs, EL, KN("attend_decode_paged"));
+}
 // attend_prompt_paged: qkv cos sin pos table k_cache v_cache out
 //   | m heads kv_heads d block_size table_len blocks rotated ldq q_off ldo max_pos scale
 // A prompt's rows of one sequence: row 0's block table serves them all.
@@ -1219,6 +1244,23 @@ std::vector<KernelSpec> make_table() {
                 dim("block_size", 1, 65536), dim("table_len", 1, kMax), dim("blocks", 1, kMax), u32("rotated"),
                 dim("chunk", 1, 256), dim("max_splits", 1, 65535), u32("ldq"), u32("q_off"), f32("scale")},
                l_attend_paged});
+  t.push_back({"attend_decode_paged",
+               128,
+               {{"qkv", "read", "f32"},
+                {"cos", "read", "f32"},
+                {"sin", "read", "f32"},
+                {"pos", "read", "u32"},
+                {"table", "read", "u32"},
+                {"k_cache", "read_write", "f32"},
+                {"v_cache", "read_write", "f32"},
+                {"part_m", "write", "f32"},
+                {"part_l", "write", "f32"},
+                {"part_acc", "write", "f32"}},
+               {dim("m", 1, 64), dim("heads", 1, 1024), dim("kv_heads", 1, 1024), dim("d", 128, 128),
+                dim("block_size", 1, 65536), dim("table_len", 1, kMax), dim("blocks", 1, kMax), u32("rotated"),
+                dim("chunk", 1, 256), dim("max_splits", 1, 65535), u32("ldq"), u32("q_off"), u32("k_off"),
+                u32("v_off"), f32("scale")},
+               l_attend_decode_paged});
   t.push_back({"attend_prompt_paged",
                128,
                {{"qkv", "read", "f32"},
@@ -1295,6 +1337,7 @@ std::vector<KernelSpec> make_table() {
       KV_FORMS("attend_prompt", l_attend_prompt_kv16),
       KV_FORMS("kv_store_paged", l_kv_store_paged_kv16),
       KV_FORMS("attend_split_paged", l_attend_paged_kv16),
+      KV_FORMS("attend_decode_paged", l_attend_decode_paged_kv16),
       KV_FORMS("attend_prompt_paged", l_attend_prompt_paged_kv16),
   };
 #undef W_FORMS

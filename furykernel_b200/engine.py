@@ -494,7 +494,9 @@ class Llama:
         # (No fused form reads a paged cache.)
         if fuse_attention is None:
             fuse_attention = m <= 4
-        self.fuse_attention = fuse_attention and m <= 64 and not s.paged
+        # (A paged cache's fused form needs every block-table entry
+        # distinct: set_rows checks the tables it uploads.)
+        self.fuse_attention = fuse_attention and m <= 64
         # A committed selection (furykernel_b200.select): each GEMV shape's
         # split-K, the same at every batch.
         self.splits = {}
@@ -662,19 +664,23 @@ class Llama:
 
     def _fuse_attention(self, launches: list) -> list:
         """Each layer's KV store and split attention launches, when they bind
-        the same row of q/k/v, positions, slots and caches, become one
-        attend_decode launch (the same bits); the combine follows."""
+        the same row of q/k/v, positions, slots (or block tables) and caches,
+        become one attend_decode (attend_decode_paged) launch (the same
+        bits); the combine follows."""
+        fused = {("kv_store_ring", "attend_split"): ("attend_decode", ("ldq", "rotated", "d", "kv_heads", "length")),
+                 ("kv_store_paged", "attend_split_paged"): (
+                     "attend_decode_paged", ("ldq", "rotated", "d", "kv_heads", "block_size", "table_len", "blocks"))}
         out, i = [], 0
         while i < len(launches):
             pair = [kernel_form(L.kernel) for L in launches[i:i + 2]]
-            if (i + 1 < len(launches) and [b for b, _ in pair] == ["kv_store_ring", "attend_split"]
-                    and pair[0][1] == pair[1][1]):
+            form = fused.get(tuple(b for b, _ in pair)) if i + 1 < len(launches) else None
+            if form and pair[0][1] == pair[1][1]:
                 kv, at = launches[i:i + 2]
                 same = (kv.bufs[0] == at.bufs[0] and list(kv.bufs[3:7]) == list(at.bufs[3:7])
-                        and all(kv.params[k] == at.params[k] for k in ("ldq", "rotated", "d", "kv_heads", "length")))
+                        and all(kv.params[k] == at.params[k] for k in form[1]))
                 if same:
                     p = dict(at.params, k_off=kv.params["k_off"], v_off=kv.params["v_off"])
-                    out.append(Launch("attend_decode" + pair[0][1], p, list(at.bufs)))
+                    out.append(Launch(form[0] + pair[0][1], p, list(at.bufs)))
                     i += 2
                     continue
             out.append(launches[i])
@@ -828,9 +834,10 @@ class Llama:
                                                     f"({self.m}, {self.s.table_len}).")
         slots = np.asarray(slots if slots is not None else np.arange(self.m), np.uint32)
         self.check_rows(tokens, positions, slots)
-        if self.fuse_attention and len(np.unique(slots)) != len(slots):
-            raise N.Refused(N.FKC_ERR_ARGUMENT, "a decode step's rows must sit in distinct slots (the fused "
-                                                "attention stores a row's key while the others read).")
+        if self.fuse_attention and np.unique(slots).size != slots.size:
+            what = "every block-table entry distinct" if self.s.paged else "its rows in distinct slots"
+            raise N.Refused(N.FKC_ERR_ARGUMENT, f"a decode step needs {what} (the fused attention stores a row's "
+                                                "key while the others read).")
         self.tokens.upload(np.asarray(tokens, np.uint32))
         self.pos.upload(np.asarray(positions, np.uint32))
         self.slot.upload(slots)

@@ -609,21 +609,28 @@ std::vector<Launch> tensor_parallel_nccl(const std::vector<Launch>& in, const Ll
 
 // Each layer's KV store and split attention, when they bind the same row of
 // q/k/v, positions, slots and caches, become one attend_decode launch.
+// A paged cache's pair likewise becomes attend_decode_paged (the engine
+// holds every block-table entry distinct).
 std::vector<Launch> fuse_attention(const std::vector<Launch>& in) {
   std::vector<Launch> out;
   for (size_t i = 0; i < in.size(); ++i) {
     const auto kvf = kernel_form(in[i].kernel);
     const auto atf = i + 1 < in.size() ? kernel_form(in[i + 1].kernel) : std::pair<std::string, std::string>{};
-    if (i + 1 < in.size() && kvf.first == "kv_store_ring" && atf.first == "attend_split" && kvf.second == atf.second) {
+    const bool ring = kvf.first == "kv_store_ring" && atf.first == "attend_split";
+    const bool paged = kvf.first == "kv_store_paged" && atf.first == "attend_split_paged";
+    if (i + 1 < in.size() && (ring || paged) && kvf.second == atf.second) {
       const Launch& kv = in[i];
       const Launch& at = in[i + 1];
       bool same = kv.bufs[0] == at.bufs[0] &&
                   std::equal(kv.bufs.begin() + 3, kv.bufs.begin() + 7, at.bufs.begin() + 3);
-      for (const char* k : {"ldq", "rotated", "d", "kv_heads", "length"})
+      const std::vector<const char*> keys =
+          ring ? std::vector<const char*>{"ldq", "rotated", "d", "kv_heads", "length"}
+               : std::vector<const char*>{"ldq", "rotated", "d", "kv_heads", "block_size", "table_len", "blocks"};
+      for (const char* k : keys)
         if (kv.param(k) != at.param(k)) same = false;
       if (same) {
         Launch f;
-        f.kernel = "attend_decode" + kvf.second;
+        f.kernel = (ring ? "attend_decode" : "attend_decode_paged") + kvf.second;
         f.params = at.params;
         f.set("k_off", kv.param("k_off"));
         f.set("v_off", kv.param("v_off"));

@@ -72,8 +72,21 @@ std::vector<Launch> prefill_launches(const LlamaLaunchDesc& d, const PrefillDesc
         ap.emplace_back(k, L->param(k));
       unfused.push_back(make("attend_split" + csuf, ap, {L->bufs.begin(), L->bufs.begin() + 10}));
     }
-    for (const Launch& L : unfused) by[kernel_form(L.kernel).first].push_back(&L);
   }
+  if (by.count("attend_decode_paged")) {  // likewise for a paged cache
+    for (const Launch* L : by["attend_decode_paged"]) {
+      std::vector<std::pair<std::string, double>> kp, ap;
+      for (const char* k : {"m", "kv_heads", "d", "block_size", "table_len", "blocks", "rotated", "ldq", "k_off",
+                            "v_off"})
+        kp.emplace_back(k, L->param(k));
+      for (const char* k : {"m", "heads", "kv_heads", "d", "block_size", "table_len", "blocks", "rotated", "chunk",
+                            "max_splits", "ldq", "q_off", "scale"})
+        ap.emplace_back(k, L->param(k));
+      unfused.push_back(make("kv_store_paged" + csuf, kp, {L->bufs.begin(), L->bufs.begin() + 7}));
+      unfused.push_back(make("attend_split_paged" + csuf, ap, {L->bufs.begin(), L->bufs.begin() + 10}));
+    }
+  }
+  for (const Launch& L : unfused) by[kernel_form(L.kernel).first].push_back(&L);
   double eps = 0;
   bool have_eps = false;
   for (const Launch& L : decode)

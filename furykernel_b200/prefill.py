@@ -156,6 +156,14 @@ class Prefill:
                 by.setdefault("attend_split", []).append(Launch("attend_split" + csuf, {
                     k: p[k] for k in ("m", "heads", "kv_heads", "d", "length", "rotated", "chunk", "max_splits",
                                       "ldq", "q_off", "scale")}, L.bufs[:10]))
+        for L in by.get("attend_decode_paged", []):  # likewise for a paged cache
+            p = L.params
+            by.setdefault("kv_store_paged", []).append(Launch("kv_store_paged" + csuf, {
+                k: p[k] for k in ("m", "kv_heads", "d", "block_size", "table_len", "blocks", "rotated", "ldq",
+                                  "k_off", "v_off")}, L.bufs[:7]))
+            by.setdefault("attend_split_paged", []).append(Launch("attend_split_paged" + csuf, {
+                k: p[k] for k in ("m", "heads", "kv_heads", "d", "block_size", "table_len", "blocks", "rotated",
+                                  "chunk", "max_splits", "ldq", "q_off", "scale")}, L.bufs[:10]))
         eps = None
         for L in eng.launches:
             if L.kernel.startswith("gemv") and "eps" in L.params:

@@ -202,6 +202,15 @@ SPEC_KERNELS = {
                    _dim("block_size", 1, 65536), _dim("table_len", 1, _MAX), _dim("blocks", 1, _MAX), _u("rotated"),
                    _dim("chunk", 1, 256), _dim("max_splits", 1, 65535), _u("ldq"), _u("q_off"), _f("scale")],
                   threads=128),
+        KernelSig("attend_decode_paged",
+                  [_f32("qkv"), _f32("cos"), _f32("sin"), _u32("pos"), _u32("table"), _f32("k_cache", "read_write"),
+                   _f32("v_cache", "read_write"), _f32("part_m", "write"), _f32("part_l", "write"),
+                   _f32("part_acc", "write")],
+                  [_dim("m", 1, 64), _dim("heads", 1, 1024), _dim("kv_heads", 1, 1024), _dim("d", 128, 128),
+                   _dim("block_size", 1, 65536), _dim("table_len", 1, _MAX), _dim("blocks", 1, _MAX), _u("rotated"),
+                   _dim("chunk", 1, 256), _dim("max_splits", 1, 65535), _u("ldq"), _u("q_off"), _u("k_off"),
+                   _u("v_off"), _f("scale")],
+                  threads=128),
         KernelSig("attend_prompt_paged",
                   [_f32("qkv"), _f32("cos"), _f32("sin"), _u32("pos"), _u32("table"), _f32("k_cache"),
                    _f32("v_cache"), _f32("out", "write")],
@@ -231,7 +240,7 @@ _VARIANTS = [
     *[(base, base + CACHE_SUFFIX[t], {"k_cache", "v_cache"}, t)
       for t in ("bf16", "f16")
       for base in ("kv_store_ring", "attend_split", "attend_decode", "attend_prompt", "kv_store_paged",
-                   "attend_split_paged", "attend_prompt_paged")],
+                   "attend_split_paged", "attend_decode_paged", "attend_prompt_paged")],
 ]
 for _base, _name, _retyped, _t in _VARIANTS:
     _k = SPEC_KERNELS[_base]

@@ -10,6 +10,7 @@ import dataclasses
 import math
 from types import SimpleNamespace
 
+import numpy as np
 import pytest
 
 from furykernel_b200 import _host as H
@@ -179,7 +180,7 @@ def fake_engine(full, batch, rank=0, world=1, peer_exchange=True, fuse_attention
     e.part = [Buf((5 << 44) + (i << 32)) for i in range(3)]
     if fuse_attention is None:
         fuse_attention = batch <= 4
-    e.fuse_attention = fuse_attention and batch <= 64 and not s.paged
+    e.fuse_attention = fuse_attention and batch <= 64
     return e
 
 
@@ -391,3 +392,15 @@ def test_prefill_rows_are_bounded():
     for m in (0, 17):
         with pytest.raises(N.Refused, match="outside 1..16"):
             p.launches(m)
+
+
+def test_fused_paged_decode_needs_distinct_table_entries():
+    """The fused paged attention stores a row's key while the other rows
+    read: the engine takes only tables whose entries are all distinct."""
+    full = dataclasses.replace(small(2), blocks=64, block_size=16)
+    e = fake_engine(full, 2)
+    assert e.fuse_attention
+    tables = np.arange(2 * full.table_len, dtype=np.uint32).reshape(2, full.table_len)
+    tables[1, 3] = tables[0, 0]  # a block in both rows' tables
+    with pytest.raises(N.Refused, match="every block-table entry distinct"):
+        e.set_rows(np.array([1, 2], np.uint32), np.array([5, 7], np.uint32), tables)

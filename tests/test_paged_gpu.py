@@ -116,6 +116,22 @@ def test_paged_store_and_attention(ctx, t, m, heads, kv_heads, block_size, posit
     want, _ = O.attend(qrot, heads, kv_heads, d, length, pos, rows, kr, vr, np.float32(1.0 / math.sqrt(d)), chunk,
                        4, max_splits, THREADS)
     assert same_bits(out.download(), want)
+    # The fused form (the store folded into the attention; the tables'
+    # entries distinct): the same output and the same pools.
+    dk.upload(kbits if t != "f32" else kpool)
+    dv.upload(vbits if t != "f32" else vpool)
+    ctx.launch("attend_decode_paged" + suffix,
+               dict(pg, m=m, heads=heads, kv_heads=kv_heads, d=d, rotated=d // 2, chunk=chunk, max_splits=max_splits,
+                    ldq=width, q_off=0, k_off=heads * d, v_off=(heads + kv_heads) * d, scale=1.0 / math.sqrt(d)),
+               [dq, dcos, dsin, dpos, dtab, dk, dv, pm, pl, pa])
+    ctx.launch("attend_combine", {"m": m, "heads": heads, "d": d, "chunk": chunk, "max_splits": max_splits,
+                                  "ldo": heads * d}, [pm, pl, pa, dpos, out])
+    assert same_bits(out.download(), want)
+    if t != "f32":
+        assert np.array_equal(dk.download(), MC.narrow(t, kwant).reshape(shape))
+        assert np.array_equal(dv.download(), MC.narrow(t, vwant).reshape(shape))
+    else:
+        assert same_bits(dk.download(), kwant) and same_bits(dv.download(), vwant)
     for b in (dq, dpos, dtab, dk, dv, dcos, dsin, pm, pl, pa, out):
         b.free()
 
