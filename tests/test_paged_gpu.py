@@ -198,3 +198,38 @@ def test_paged_model_decode_step(ctx, batch, cache):
     assert same_bits(eng.x.download(), want_x)
     gk, gv = MC.host_caches(eng)
     assert same_bits(gk, kc) and same_bits(gv, vc)
+
+
+@pytest.mark.parametrize("cache,one_slot", [("f32", False), ("f32", True), ("bf16", True), ("f16", False)])
+def test_paged_prefill_then_decode(ctx, cache, one_slot):
+    """Prompts prefilled into a paged pool through the rows' block tables,
+    then a decode step (fused: the tables' entries distinct) from the pools
+    prefill left: the oracle's ids and logits, bit for bit."""
+    from furykernel_b200.engine import Llama
+    from furykernel_b200.prefill import Prefill, prompt_chunks
+    from furykernel_b200.program.llama import LlamaShape
+
+    batch = 2
+    s = LlamaShape(d_model=512, heads=4, kv_heads=4, head_dim=128, ffn=1024, vocab=3000, layers=2, positions=96,
+                   blocks=2 * 6 + 4, block_size=16, cache=cache)
+    eng = Llama(ctx, s, batch, seed=620, chunk=16)
+    pre = Prefill(eng, rows=128, one_slot=one_slot)
+    layers, embed, final_norm = MC.host_model(eng)
+    tables = disjoint_tables(621, batch, s.table_len, s.blocks)
+    lens = [37, 52]
+    prompts = [O.ints(640 + i, n, s.vocab) for i, n in enumerate(lens)]
+    toks = np.concatenate([p[:-1] for p in prompts])
+    poss = np.concatenate([np.arange(n - 1, dtype=np.uint32) for n in lens])
+    rows = np.concatenate([np.full(n - 1, i) for i, n in enumerate(lens)])
+    for i, n in prompt_chunks(pre, toks, poss, rows):
+        pre.run(toks[i:i + n], poss[i:i + n], tables[rows[i:i + n]])
+    ctx.sync()
+    kc, vc = MC.host_caches(eng)
+    last = np.array([p[-1] for p in prompts], np.uint32)
+    lpos = np.array([n - 1 for n in lens], np.uint32)
+    eng.set_rows(last, lpos, tables)
+    ids = eng.step()
+    want_ids, want_logits, _ = MC.oracle_decode(eng, layers, embed, final_norm, kc, vc, last, lpos, tables)
+    assert same_bits(eng.logits.download(), want_logits)
+    assert np.array_equal(ids, want_ids)
+    pre.close()
