@@ -647,8 +647,8 @@ class Llama:
         # The engine's greedy feedback: the ids become the next step's
         # tokens and the positions advance, so replays decode on their own.
         out.append(Launch("advance", {"m": m}, [self.out_ids.ptr, self.tokens.ptr, self.pos.ptr]))
-        for L in out:  # split-K per GEMV shape
-            if L.kernel.startswith("gemv"):
+        for L in out:  # split-K per GEMV shape (the routed GEMV keeps the lowering's split 1)
+            if L.kernel.startswith("gemv") and not L.kernel.startswith("gemv_routed"):
                 # A selection's pick for the shape, the same at every batch;
                 # else one, which the streaming (m <= 4) and batched
                 # (m <= 64) kernels keep (their parallelism is rows whatever

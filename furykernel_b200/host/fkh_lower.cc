@@ -793,9 +793,10 @@ std::vector<Launch> llama_launches(const LlamaLaunchDesc& d) {
   // Split-K a GEMV: a selection's pick for its shape, the same at every
   // batch (so that a row's bits do not depend on its batch); else one,
   // which the streaming and batched kernels keep (past 64 rows, the
-  // chunked kernel's choice for the shape).
+  // chunked kernel's choice for the shape). The routed GEMV keeps the
+  // lowering's split 1 (its `k` is the route's rank count).
   for (Launch& L : out) {
-    if (L.kernel.rfind("gemv", 0) != 0) continue;
+    if (L.kernel.rfind("gemv", 0) != 0 || L.kernel.rfind("gemv_routed", 0) == 0) continue;
     const uint64_t n = (uint64_t)L.param("n"), k = (uint64_t)L.param("k");
     auto it = d.splits.find({n, k});
     const uint64_t split = it != d.splits.end() ? it->second : m <= 64 ? 1 : split_for(n, k, d.sms);

@@ -20,10 +20,11 @@ SPLITS = (1, 2, 4, 8)
 
 def gemv_classes(eng) -> list:
     """The engine's GEMV classes (n, k, m), m its batch, in launch order,
-    each once (from the host library's launch list)."""
+    each once (from the host library's launch list); the routed GEMV is no
+    member (its split is the lowering's)."""
     out = []
     for L in getattr(eng, "launches", None) or eng._launches():
-        if L.kernel.startswith("gemv"):
+        if L.kernel.startswith("gemv") and not L.kernel.startswith("gemv_routed"):
             c = (L.params["n"], L.params["k"], eng.m)
             if c not in out:
                 out.append(c)

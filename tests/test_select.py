@@ -349,3 +349,18 @@ def test_tuning_picks_the_split_fastest_over_every_batch():
     assert select.choose(classes, times) == [1, 1, 8]
     with pytest.raises(N.Refused, match="no split is kept at every batch"):
         select.choose([(1, 4, 1), (1, 4, 2)], {(1, 4, 1): {1: 1.0}, (1, 4, 2): {2: 1.0}})
+
+
+def test_routed_gemvs_are_no_gemv_class():
+    """A model of routed experts: its classes are the dense GEMVs' (the
+    projections, the router, the head), never the routed GEMV's, whose `k`
+    is the route's rank count."""
+    import dataclasses
+
+    from furykernel_b200 import select as S
+    from tests.test_host_cpp import fake_engine, small
+
+    e = fake_engine(dataclasses.replace(small(3), experts=8, top_k=2), 3)
+    classes = S.gemv_classes(e)
+    assert classes and all(k >= 256 for _, k, _ in classes)
+    assert (8, 512, 3) in classes  # the router
