@@ -50,6 +50,9 @@ def parse():
                          "own element type; f16)")
     ap.add_argument("--cache", default="f32", choices=["f32", "bf16", "f16"],
                     help="config 5: the KV caches' element type")
+    ap.add_argument("--block-size", type=int, default=0,
+                    help="config 5: a paged KV cache of blocks of this many positions, each row's blocks its own "
+                         "(0, the default: Ring caches)")
     return ap.parse_args()
 
 
@@ -202,11 +205,12 @@ NCU_TRAFFIC = {
 }
 
 
-def prompt_prefill(ctx, eng, b: int, local: int):
+def prompt_prefill(ctx, eng, b: int, local: int, tables=None):
     """Config 5's prompt: b prompts of PROMPT ids U[0, vocab) (numpy PCG64,
     seed 512, the same on every rank), every row but the last prefilled
     through the layers with the 3xTF32 GEMMs, then one decode step from the
-    last ids. Returns (the first generated ids, the prefill's line)."""
+    last ids. With a paged cache, `tables` holds each prompt's block table.
+    Returns (the first generated ids, the prefill's line)."""
     import numpy as np
     import torch
 
@@ -221,22 +225,23 @@ def prompt_prefill(ctx, eng, b: int, local: int):
     # Capture, then one untimed pass (a graph's first replay uploads it, and
     # NCCL's first captured collectives set up): prefill writes the same
     # keys and values again in the timed pass.
+    seq = sl if tables is None else tables[sl]  # each row's slot, or its block table
     for i, m in chunks:
-        pre.run(toks[i:i + m], poss[i:i + m], sl[i:i + m])
+        pre.run(toks[i:i + m], poss[i:i + m], seq[i:i + m])
     ctx.sync()
     torch.cuda.set_device(local)
     stream = torch.cuda.ExternalStream(ctx.stream())
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i, m in chunks:
-        pre.run(toks[i:i + m], poss[i:i + m], sl[i:i + m])
+        pre.run(toks[i:i + m], poss[i:i + m], seq[i:i + m])
     e1.record(stream)
     e1.synchronize()
     ms = e0.elapsed_time(e1)
     rows = len(toks)
     flops = pre.gemm_flops(rows)
     pre.close()
-    eng.set_rows(prompts[:, -1], np.full(b, PROMPT - 1, np.uint32), slots)
+    eng.set_rows(prompts[:, -1], np.full(b, PROMPT - 1, np.uint32), slots if tables is None else tables)
     ids = eng.step()
     info = {"prompts": b, "prompt_len": PROMPT, "rows": rows, "launch_rows": R, "ms": ms,
             "tokens_per_s": rows / (ms / 1e3), "gemm_flops_per_gpu": flops,
@@ -304,18 +309,25 @@ def run_ours(args):
     metric, dtype = model_types(args)
     b = args.batch
     length = 4096 if b <= 4 else 1024
+    bs = args.block_size
+    paged = {}
+    if bs:  # a pool of blocks, each row's table its own blocks (distinct entries)
+        table_len = (length + bs - 1) // bs
+        paged = {"blocks": b * table_len, "block_size": bs}
     shape = LlamaShape(layers=args.layers, slots=b, length=length, positions=length, weights=args.weights,
-                       cache=args.cache)
+                       cache=args.cache, **paged)
     ctx = N.Context(local)
     eng = Llama(ctx, shape, b, seed=2026, chunk=32)
-    tokens, prefill = prompt_prefill(ctx, eng, b, local)
+    tables = np.arange(b * table_len, dtype=np.uint32).reshape(b, table_len) if bs else None
+    tokens, prefill = prompt_prefill(ctx, eng, b, local, tables)
     slots = np.arange(b, dtype=np.uint32)
-    eng.set_rows(tokens, np.full(b, PROMPT, np.uint32), slots)
+    seqs = slots if tables is None else tables
+    eng.set_rows(tokens, np.full(b, PROMPT, np.uint32), seqs)
     graph = eng.capture()
     for _ in range(args.warmup):
         graph.launch()
     ctx.sync()
-    eng.set_rows(tokens, np.full(b, PROMPT, np.uint32), slots)
+    eng.set_rows(tokens, np.full(b, PROMPT, np.uint32), seqs)
     with Clocks(local) as clk:
         ms = graph.time(0, args.steps)
     clocks = clk.summary()
@@ -351,12 +363,12 @@ def run_ours(args):
     # End to end through the C ABI: host token ids and positions in (pinned),
     # the graph replayed, the greedy ids back, every step.
     rs = eng.row_stride
-    host_in = N.pinned((3 * rs,), np.uint32)
+    host_in = N.pinned((eng.rows_words,), np.uint32)
     host_out = N.pinned((b,), np.uint32)
     host_in[:] = 0
     host_in[:b] = tokens
     host_in[rs:rs + b] = PROMPT
-    host_in[2 * rs:2 * rs + b] = slots
+    host_in[2 * rs:2 * rs + seqs.size] = seqs.reshape(-1)
     rows_ptr = eng.rows.ptr
     for _ in range(3):
         N.check(N.lib().fkc_step(ctx.handle, graph.handle, host_in.ctypes.data, rows_ptr, host_in.nbytes,
@@ -380,6 +392,7 @@ def run_ours(args):
         "config": {"workload": f"config 5 decode, batch {b}, context {PROMPT}..{PROMPT + args.steps}",
                    "model": "llama-shaped 32 layers, d 4096, 32 heads x 128, ffn 11008, vocab 32000, tied head",
                    "global_batch": b, "seq_len": PROMPT, "parallelism": "tp1", "kv_length": length,
+                   "kv_layout": f"paged, blocks of {bs} positions" if bs else "ring",
                    "l2": "no flush: each step streams %.1f GB of weights, > 126 MB L2" % (eng.weight_bytes() / 1e9)},
         "hbm": {"step_algorithmic_bytes": step_bytes, "achieved_gbs": step_gbs,
                 "frac_of_8tbs": step_gbs / 8000.0, "frac_of_peak": step_gbs / hbm_peak, "peak": hbm_peak,
