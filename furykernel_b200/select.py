@@ -101,3 +101,55 @@ def tune(ctx, classes, reps: int = 20, warmup: int = 3, path: str | None = None)
         with open(path, "w") as f:
             f.write(text)
     return text
+
+
+def classes_for(shape, batch: int, sms: int, chunk: int = 32) -> list:
+    """The GEMV classes (n, k, batch) of a one-GPU decode step of `shape`
+    at `batch`, from the host library's launch list at stand-in addresses
+    (no device memory): the engine's own choices of forms."""
+    addrs = {n: (i + 1) << 32 for i, n in enumerate(H.DESC_ADDRS + H.MOE_ADDRS)}
+    addrs["part"] = [(64 + i) << 32 for i in range(3)]
+    out = []
+    for kernel, params, _ in H.llama_launches(shape, batch, 0, 1, sms, chunk, batch <= 64, False, batch <= 4,
+                                              addrs):
+        if kernel.startswith("gemv") and not kernel.startswith("gemv_routed"):
+            c = (params["n"], params["k"], batch)
+            if c not in out:
+                out.append(c)
+    return out
+
+
+def main(argv=None) -> None:
+    """python -m furykernel_b200.select tune [--batches 1,4,16,64] [--layers L] [--out FILE]: times the
+    GEMV variants of config 5's decode step on GPU 0 and writes the selection."""
+    import argparse
+
+    from .program.llama import LlamaShape
+
+    ap = argparse.ArgumentParser(prog="python -m furykernel_b200.select")
+    ap.add_argument("command", choices=["tune", "classes"])
+    ap.add_argument("--batches", default="1,4,16,64")
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--sms", type=int, default=148, help="classes: the multiprocessors to prune for")
+    ap.add_argument("--out", default=None)
+    args = ap.parse_args(argv)
+    batches = [int(b) for b in args.batches.split(",")]
+
+    def shape(b):  # config 5's model at batch b: a slot a row
+        length = 4096 if b <= 4 else 1024
+        return LlamaShape(layers=args.layers, slots=b, length=length, positions=length)
+
+    if args.command == "classes":
+        for b in batches:
+            print(b, classes_for(shape(b), b, args.sms))
+        return
+    ctx = N.Context(0)
+    try:
+        classes = [c for b in batches for c in classes_for(shape(b), b, ctx.sms)]
+        print(tune(ctx, classes, path=args.out))
+    finally:
+        ctx.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -364,3 +364,15 @@ def test_routed_gemvs_are_no_gemv_class():
     classes = S.gemv_classes(e)
     assert classes and all(k >= 256 for _, k, _ in classes)
     assert (8, 512, 3) in classes  # the router
+
+
+def test_classes_for_a_shape_are_the_engines():
+    """classes_for (no device) names the same GEMV classes as the engine's
+    launch list at every batch form: streaming, batched, chunked."""
+    from furykernel_b200 import select as S
+    from tests.test_host_cpp import fake_engine, small
+
+    for b in (1, 5, 80):
+        e = fake_engine(small(b), b)
+        assert S.classes_for(small(b), b, 148) == S.gemv_classes(e)
+    S.main(["classes", "--batches", "1,16", "--layers", "1"])
