@@ -304,6 +304,8 @@ def run_ours(args):
     if world > 1:
         from furykernel_b200 import tp
 
+        if args.block_size:
+            raise SystemExit("bench: --block-size is for one GPU; the tensor-parallel bench runs Ring caches.")
         return tp.bench_main(args, model_types(args)[0], PROMPT, prompt_prefill)
 
     metric, dtype = model_types(args)
