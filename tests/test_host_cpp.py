@@ -404,3 +404,31 @@ def test_fused_paged_decode_needs_distinct_table_entries():
     tables[1, 3] = tables[0, 0]  # a block in both rows' tables
     with pytest.raises(N.Refused, match="every block-table entry distinct"):
         e.set_rows(np.array([1, 2], np.uint32), np.array([5, 7], np.uint32), tables)
+
+
+# Mixtures of the options: element types, paged caches, routed experts with
+# scales, gated plans, ranks.
+MIXED_CASES = [
+    (dataclasses.replace(small(3), experts=8, top_k=2, expert_scale=True, weights="f16", cache="bf16", blocks=64,
+                         block_size=16), 3, 0, 1, True, True, False),
+    (dataclasses.replace(small(2), experts=8, top_k=2, weights="bf16", cache="f16", blocks=64, block_size=16),
+     2, 0, 1, True, True, True),
+    (dataclasses.replace(tp_shape(5), ffn=256, experts=8, top_k=2, expert_scale=True, weights="bf16", blocks=48,
+                         block_size=8), 5, 1, 2, False, False, True),
+    (dataclasses.replace(small(70), experts=4, top_k=1, weights="f16", cache="f16"), 70, 0, 1, True, False, False),
+]
+
+
+@pytest.mark.parametrize("case", range(len(MIXED_CASES)))
+def test_mixed_options_launch_alike(case):
+    full, batch, rank, world, peer, gated, store_gelus = MIXED_CASES[case]
+    e = fake_engine(full, batch, rank, world, peer, gated=gated, store_gelus=store_gelus)
+    want, got = e._launches_restated(), e._launches()
+    assert [L.kernel for L in got] == [L.kernel for L in want]
+    for g, w in zip(got, want):
+        assert g.bufs == w.bufs and g.params == w.params, (g.kernel, g.params, w.params)
+    e.launches = got
+    if world == 1:  # and the prefill over the same engine
+        p = fake_prefill(e, 64)
+        pw, pg = p._launches_restated(40), p.launches(40)
+        assert [(L.kernel, L.params, L.bufs) for L in pg] == [(L.kernel, L.params, L.bufs) for L in pw]
