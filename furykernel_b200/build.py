@@ -50,7 +50,7 @@ def stale() -> bool:
 def _compile(src: str, obj: str, inc: str, ptxas_v: bool, verbose: bool) -> None:
     """One translation unit, written under a temporary name and then renamed,
     so that an interrupted compile leaves no object that looks current."""
-    tmp = obj + ".tmp.o"
+    tmp = f"{obj[:-2]}.{os.getpid()}.tmp.o"
     cmd = ["nvcc", *ARCH, "-O3", "-lineinfo", "--fmad=false", "-std=c++17", "-Xcompiler", "-fPIC",
            "-I", inc, "-c", src, "-o", tmp]
     if ptxas_v:

@@ -48,9 +48,16 @@ def build() -> str:
 def lib():
     global _lib
     if _lib is None:
+        import fcntl
+
         sources = [os.path.join(_HERE, f) for f in ("fko_cpu.c", "fko_eval.c", "fko.h", "Makefile")]
-        if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < max(map(os.path.getmtime, sources)):
-            build()
+        os.makedirs(os.path.dirname(_LIB_PATH), exist_ok=True)
+        # One process builds at a time (ranks of a multi-process test start
+        # together); the others find the library current when they get the lock.
+        with open(_LIB_PATH + ".lock", "w") as lock:
+            fcntl.flock(lock, fcntl.LOCK_EX)
+            if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < max(map(os.path.getmtime, sources)):
+                build()
         L = ctypes.CDLL(_LIB_PATH)
         sig = {
             "fko_random": (_u64, [_u64, _u64]),
