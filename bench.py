@@ -125,14 +125,17 @@ class Clocks:
 # The CPU path: the reference's CPU target restated (oracle/), timed
 
 
-def cpu_model(batch: int):
-    """Host copies of one full-size layer's weights, the tied embedding, the
-    norms and a layer's KV cache, seeded as the device's are."""
-    import numpy as np
-
+def cpu_model(batch: int, positions: int):
+    """Host copies of config 5's model for the CPU path: one full-size
+    layer's weights (q/k/v, o, gate/up, down, the two norm gains), the tied
+    embedding and the final norm, and a Ring KV cache of `positions` for each
+    of the 32 layers (keys and values N(0, 1), batch rows in their own
+    slots). The 32 layer passes of a step all read the one layer's 809 MB of
+    weights: far past any host cache, so a pass costs what a distinct
+    layer's would. The caches are distinct a layer, as a model's are."""
     from oracle import oracle as O
 
-    d, h, hd, f, V, L = 4096, 32, 128, 11008, 32000, 1024
+    d, h, hd, f, V = 4096, 32, 128, 11008, 32000
     w = {
         "qkv": O.normal(11, 3 * d * d, 0.0, 0.02).reshape(3 * d, d),
         "o": O.normal(12, d * d, 0.0, 0.02).reshape(d, d),
@@ -140,60 +143,89 @@ def cpu_model(batch: int):
         "down": O.normal(14, d * f, 0.0, 0.02).reshape(d, f),
         "embed": O.normal(15, V * d, 0.0, 0.02).reshape(V, d),
         "g1": O.normal(16, d, 0.0, 0.02), "g2": O.normal(17, d, 0.0, 0.02), "gf": O.normal(18, d, 0.0, 0.02),
-        "kc": O.normal(20, batch * h * L * hd).reshape(batch, h, L, hd),
-        "vc": O.normal(21, batch * h * L * hd).reshape(batch, h, L, hd),
+        "kc": [O.normal(1000 + 2 * i, batch * h * positions * hd).reshape(batch, h, positions, hd)
+               for i in range(32)],
+        "vc": [O.normal(1001 + 2 * i, batch * h * positions * hd).reshape(batch, h, positions, hd)
+               for i in range(32)],
+        "positions": positions,
     }
-    w["cos"], w["sin"] = O.rope_tables(10000.0, hd, hd // 2, L)
+    w["cos"], w["sin"] = O.rope_tables(10000.0, hd, hd // 2, positions)
     w["tok"] = O.ints(22, batch, V)
     return w
 
 
-def cpu_sample(threads: int, batch: int, w: dict, min_seconds: float = 10.0):
-    """Seconds for one decode step of the full model on the CPU, from a
-    bounded sample: one full-size layer (q/k/v, RoPE, KV store, attention at
-    context 512, o, SiLU FFN) and the head per repetition, the layer's time
-    scaled by 32. Returns (seconds per step, description)."""
+def cpu_step(threads: int, w: dict, tokens, pos):
+    """One greedy decode step of the 32-layer model on the host, in the CPU
+    target's arithmetic (oracle/): the embedding gather; each of the 32
+    layers' RMSNorm + q/k/v GEMV, RoPE, the KV store at `pos`, the split
+    attention over positions 0..pos, the o GEMV + residual, RMSNorm +
+    gate/up GEMV, SiLU-gate, the down GEMV + residual; then the final norm,
+    the tied LM head and the argmax. Returns the ids."""
     import math
 
     import numpy as np
 
     from oracle import oracle as O
 
-    d, h, hd, f, L = 4096, 32, 128, 11008, 1024
-    pos = np.full(batch, PROMPT, np.uint32)
-    slot = np.arange(batch, dtype=np.uint32)
+    d, h, hd, f = 4096, 32, 128, 11008
+    L = w["positions"]
+    b = len(tokens)
+    slot = np.arange(b, dtype=np.uint32)
     eps, scale = np.float32(1e-5), np.float32(1.0 / math.sqrt(hd))
-
-    def layer(x):
+    x = O.gather(w["embed"], tokens)
+    for layer in range(32):
+        kc, vc = w["kc"][layer], w["vc"][layer]
         qkv = O.gemv(w["qkv"], O.rmsnorm_rows(x, w["g1"], eps, 1.0, threads), 1, threads)
         kr = O.rope(qkv[:, d:2 * d], h, hd, hd // 2, pos, w["cos"], w["sin"])
-        O.kv_store_ring(kr, h, hd, L, pos, slot, w["kc"])
-        O.kv_store_ring(np.ascontiguousarray(qkv[:, 2 * d:]), h, hd, L, pos, slot, w["vc"])
+        O.kv_store_ring(kr, h, hd, L, pos, slot, kc)
+        O.kv_store_ring(np.ascontiguousarray(qkv[:, 2 * d:]), h, hd, L, pos, slot, vc)
         qr = O.rope(qkv[:, :d], h, hd, hd // 2, pos, w["cos"], w["sin"])
-        att, _ = O.attend(qr, h, h, hd, L, pos, slot, w["kc"], w["vc"], scale, 128, 4, L // 128, threads)
-        x1 = O.add(x, O.gemv(w["o"], att, 2, threads))
-        gu = O.gemv(w["gu"], O.rmsnorm_rows(x1, w["g2"], eps, 1.0, threads), 1, threads)
-        return O.add(x1, O.gemv(w["down"], O.silu_mul(gu[:, :f], gu[:, f:]), 2, threads))
+        att, _ = O.attend(qr, h, h, hd, L, pos, slot, kc, vc, scale, 128, 4, (L + 127) // 128, threads)
+        x = O.add(x, O.gemv(w["o"], att, 2, threads))
+        gu = O.gemv(w["gu"], O.rmsnorm_rows(x, w["g2"], eps, 1.0, threads), 1, threads)
+        x = O.add(x, O.gemv(w["down"], O.silu_mul(gu[:, :f], gu[:, f:]), 2, threads))
+    return O.argmax(O.gemv(w["embed"], O.rmsnorm_rows(x, w["gf"], eps, 1.0, threads), 1, threads))
 
-    def head(x):
-        return O.argmax(O.gemv(w["embed"], O.rmsnorm_rows(x, w["gf"], eps, 1.0, threads), 1, threads))
 
-    t_layer, t_head, reps = 0.0, 0.0, 0
-    start = time.perf_counter()
-    while reps < 1 or (time.perf_counter() - start < min_seconds and reps < 20):
-        x = O.gather(w["embed"], w["tok"])
-        t0 = time.perf_counter()
-        x = layer(x)
-        t1 = time.perf_counter()
-        head(x)
-        t2 = time.perf_counter()
-        t_layer += t1 - t0
-        t_head += t2 - t1
-        reps += 1
-    per_step = 32 * t_layer / reps + t_head / reps
-    desc = (f"{reps} repetition(s) of one full-size layer (d 4096, ffn 11008, 32 heads, context {PROMPT}) and the "
-            f"head (vocab 32000) at batch {batch}, CPU-target arithmetic in C; step = 32 x layer + head")
-    return per_step, desc
+def cpu_decode(threads: int, w: dict, steps: int, warmup: int):
+    """Greedy decode on the host from position PROMPT: `warmup` steps, then
+    the positions reset to PROMPT (as the GPU arm's are) and `steps` timed
+    steps, each step's ids fed to the next. Returns the seconds a step."""
+    import numpy as np
+
+    b = len(w["tok"])
+    tokens = w["tok"].astype(np.uint32)
+    for i in range(warmup):
+        tokens = cpu_step(threads, w, tokens, np.full(b, PROMPT + i, np.uint32))
+    tokens = w["tok"].astype(np.uint32)
+    t0 = time.perf_counter()
+    for i in range(steps):
+        tokens = cpu_step(threads, w, tokens, np.full(b, PROMPT + i, np.uint32))
+    return (time.perf_counter() - t0) / steps
+
+
+def cpu_step_text(b: int, steps: int, threads: int) -> str:
+    return (f"{steps} whole greedy decode step(s) of the 32-layer model at batch {b} from context {PROMPT}, in "
+            "the CPU target's arithmetic (oracle/, C): every layer's GEMVs, RoPE, KV store and attention and the "
+            "LM head; the 32 layer passes read one full-size layer's weights (809 MB, far past any host cache), "
+            f"each layer its own KV cache; {threads} thread(s)"
+            + ("" if threads > 1 else ", as the CPU target runs"))
+
+
+def config5(b: int, steps: int, world: int, length: int, bs: int = 0, weights: str = "f32") -> dict:
+    """Config 5's workload description, the same for both arms."""
+    gb = 26.4 if weights == "f32" else 13.2
+    return {"workload": f"config 5 decode, batch {b}, context {PROMPT}..{PROMPT + steps}",
+            "model": "llama-shaped 32 layers, d 4096, 32 heads x 128, ffn 11008, vocab 32000, tied head",
+            "global_batch": b, "seq_len": PROMPT, "parallelism": f"tp{world}", "kv_length": length,
+            "kv_layout": f"paged, blocks of {bs} positions" if bs else "ring",
+            "l2": f"no flush: each step streams {gb} GB of weights, > 126 MB L2"}
+
+
+def kv_length(b: int) -> int:
+    """Config 5's KV positions: the 512-position prompt and 128 decode steps
+    (640) for large batches; 4096 up to batch 4, config 5's longest."""
+    return 4096 if b <= 4 else PROMPT + 128
 
 
 # DRAM bytes (read + write) of one launch, from ncu captures of the same
@@ -251,35 +283,45 @@ def prompt_prefill(ctx, eng, b: int, local: int, tables=None):
     return ids, info
 
 
+def cpu_positions(args) -> int:
+    """The host caches' ring length: the prompt, the decode steps and one,
+    rounded up to the attention's chunk of 128."""
+    need = PROMPT + max(args.steps, args.warmup) + 1
+    return (need + 127) // 128 * 128
+
+
 def run_reference(args):
+    """The reference's CPU path on the host: the CPU target's arithmetic
+    (oracle/, the C restatement of FuryKernel.Cpu: no GHC or rustc on this
+    image), whole 32-layer greedy decode steps, one thread as the CPU target
+    runs (src/FuryKernel/Cpu.hs:259-266). Rank 0 alone runs; the other ranks
+    exit. After the timed steps, one step on all host threads (OpenMP over
+    rows and heads, a variant of ours) is reported beside it."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
     from oracle import oracle as O
 
     O.build()
-    w = cpu_model(args.batch)
-    times = []
-    desc = ""
-    for _ in range(max(args.warmup, 0)):
-        cpu_sample(threads, args.batch, w, min_seconds=0.0)
-    for _ in range(args.steps):
-        t, desc = cpu_sample(threads, args.batch, w, min_seconds=0.0)
-        times.append(t)
-    per_step = sum(times) / len(times)
-    value = args.batch / per_step
+    b = args.batch
+    w = cpu_model(b, cpu_positions(args))
+    per_step = cpu_decode(1, w, args.steps, args.warmup)
+    value = b / per_step
+    threads = os.cpu_count() or 1
+    omp = cpu_decode(threads, w, 1, 0)
+    metric, dtype = model_types(args)
     line = {
-        "impl": "reference", "metric": model_types(args)[0], "value": value, "unit": "tokens/s",
+        "impl": "reference", "metric": metric, "value": value, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": model_types(args)[1],
-        "data": "synthetic (seeded)",
-        "config": {"workload": f"config 5 decode, batch {args.batch}, context {PROMPT}", "global_batch": args.batch,
-                   "seq_len": PROMPT, "parallelism": "cpu"},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": desc + "; per step one sample, OpenMP over rows and heads"
-                                   + ("" if model_types(args)[1] == "f32" else
-                                      "; bf16 weights and caches are the same arithmetic over widened values")},
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": dtype,
+        "data": "synthetic: seeded N(0,0.02) weights, N(0,1) KV caches of the 512-position prompt, seeded ids",
+        "config": config5(b, args.steps, args.gpus, kv_length(b), args.block_size, args.weights),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": 1, "kind": "port",
+                         "sample": cpu_step_text(b, args.steps, 1)
+                                   + ("" if dtype == "f32" else
+                                      "; 16-bit weights and caches are the same arithmetic over widened values")},
+        "cpu_openmp": {"value": b / omp, "unit": "tokens/s", "cores": threads, "kind": "port (ours: OpenMP)",
+                       "sample": cpu_step_text(b, 1, threads)},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -306,11 +348,14 @@ def run_ours(args):
 
         if args.block_size:
             raise SystemExit("bench: --block-size is for one GPU; the tensor-parallel bench runs Ring caches.")
-        return tp.bench_main(args, model_types(args)[0], PROMPT, prompt_prefill)
+        length = kv_length(args.batch)
+        return tp.bench_main(args, model_types(args)[0], PROMPT, prompt_prefill,
+                             lambda world, n: config5(args.batch, args.steps, world, n, 0, args.weights), length,
+                             Clocks)
 
     metric, dtype = model_types(args)
     b = args.batch
-    length = 4096 if b <= 4 else 1024
+    length = kv_length(b)
     bs = args.block_size
     paged = {}
     if bs:  # a pool of blocks, each row's table its own blocks (distinct entries)
@@ -391,11 +436,7 @@ def run_ours(args):
         "vs_baseline": None, "dtype": dtype,
         "data": "synthetic: seeded N(0,0.02) weights made on the device; prompts of 512 ids U[0,32000) (numpy "
                 "PCG64 seed 512) prefilled through the model",
-        "config": {"workload": f"config 5 decode, batch {b}, context {PROMPT}..{PROMPT + args.steps}",
-                   "model": "llama-shaped 32 layers, d 4096, 32 heads x 128, ffn 11008, vocab 32000, tied head",
-                   "global_batch": b, "seq_len": PROMPT, "parallelism": "tp1", "kv_length": length,
-                   "kv_layout": f"paged, blocks of {bs} positions" if bs else "ring",
-                   "l2": "no flush: each step streams %.1f GB of weights, > 126 MB L2" % (eng.weight_bytes() / 1e9)},
+        "config": config5(b, args.steps, 1, length, bs, args.weights),
         "hbm": {"step_algorithmic_bytes": step_bytes, "achieved_gbs": step_gbs,
                 "frac_of_8tbs": step_gbs / 8000.0, "frac_of_peak": step_gbs / hbm_peak, "peak": hbm_peak,
                 "peak_kind": peak_kind},
@@ -412,10 +453,10 @@ def run_ours(args):
         "prefill": prefill,
     }
     if not args.no_cpu_baseline and rank == 0:
-        threads = 1
-        t, desc = cpu_sample(threads, b, cpu_model(b))
-        line["cpu_baseline"] = {"value": b / t, "unit": "tokens/s", "cores": threads, "kind": "port",
-                                "sample": desc + "; single-threaded, as the CPU target runs"}
+        steps = 2
+        t = cpu_decode(1, cpu_model(b, (PROMPT + steps + 127) // 128 * 128), steps, 0)
+        line["cpu_baseline"] = {"value": b / t, "unit": "tokens/s", "cores": 1, "kind": "port",
+                                "sample": cpu_step_text(b, steps, 1)}
     print(json.dumps(line), flush=True)
     graph.destroy()
     ctx.close()

@@ -31,6 +31,7 @@ constexpr size_t FK_XREGION = 256 + (size_t)FK_XBUFS * FK_MAX_PEERS * FK_XSLOT *
 struct FkPeers {
   char* base[FK_MAX_PEERS];  // each rank's region as this process maps it
   unsigned world, rank;
+  long long wait_cycles;  // a wait's bound in SM clock cycles (the context's setting)
 };
 
 struct FkGemv {

@@ -13,7 +13,11 @@
 
 namespace fk {
 
-constexpr long long kPeerWaitCycles = 4000000000LL;  // ~2 s
+// A wait's bound when the context gives none: about 2 s at the B200's clock.
+constexpr long long kPeerWaitCycles = 4000000000LL;
+__device__ __forceinline__ long long wait_bound(const FkPeers& P) {
+  return P.wait_cycles > 0 ? P.wait_cycles : kPeerWaitCycles;
+}
 
 __device__ __forceinline__ uint32_t* xflags(char* base) { return reinterpret_cast<uint32_t*>(base); }
 __device__ __forceinline__ uint32_t* xepoch(char* base) { return reinterpret_cast<uint32_t*>(base + 128); }
@@ -94,7 +98,7 @@ __device__ __forceinline__ bool peers_wait_rows(const FkPeers& P, uint32_t buf, 
     for (uint32_t q = 0; q < P.world && ok; ++q) {
       const long long t0 = clock64();
       while ((int32_t)(ld_acquire_sys(xflags(me) + buf * FK_MAX_PEERS + q) - target) < 0) {
-        if (clock64() - t0 > kPeerWaitCycles) {
+        if (clock64() - t0 > wait_bound(P)) {
           if (err) atomicCAS(err, 0, 10 + (int)buf);
           ok = 0;
           break;
@@ -117,7 +121,7 @@ __device__ __forceinline__ bool peers_wait(const FkPeers& P, uint32_t buf, int* 
     for (uint32_t q = 0; q < P.world && ok; ++q) {
       const long long t0 = clock64();
       while (ld_acquire_sys(xflags(me) + buf * FK_MAX_PEERS + q) < e) {
-        if (clock64() - t0 > kPeerWaitCycles) {
+        if (clock64() - t0 > wait_bound(P)) {
           if (err) atomicCAS(err, 0, 10 + (int)buf);
           ok = 0;
           break;

@@ -141,6 +141,14 @@ extern "C" int fkc_set_pdl(fkc_ctx* c, int enabled) {
   return FKC_OK;
 }
 
+extern "C" int fkc_set_wait_limit(fkc_ctx* c, unsigned microseconds) {
+  if (!c) return fail(FKC_ERR_ARGUMENT, "fkc_set_wait_limit: null context.");
+  int khz = 0;
+  FKC_CUDA(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, c->device), "fkc_set_wait_limit");
+  c->peers.wait_cycles = (long long)microseconds * (long long)khz / 1000;
+  return FKC_OK;
+}
+
 extern "C" int fkc_sync(fkc_ctx* c) {
   if (!c) return fail(FKC_ERR_ARGUMENT, "fkc_sync: null context.");
   cudaSetDevice(c->device);

@@ -1,10 +1,14 @@
 """Tensor parallelism across the GPUs of one box: one process per GPU.
 
 torch.distributed (NCCL) is the plumbing: the group's rendezvous, barriers,
-the exchange of the shim's NCCL unique id, and the max over ranks of a
-timing. The data path -- the allreduce after each row-parallel projection
-and the gather of the greedy candidates -- runs on the shim's own NCCL
-communicator, on the context's stream, inside the captured decode graph.
+the exchange of the shim's NCCL unique id and of the peer regions' IPC
+handles, and the max over ranks of a timing. The data path -- the sum after
+each row-parallel projection and the gather of the greedy candidates -- runs
+inside the captured decode graph on the context's stream: over NVLink peer
+memory for decode batches of up to 4 rows (the row-parallel GEMV writes its
+partial rows into every rank's region and the next GEMV's prologue sums
+them, fk_peers.cuh), and on the shim's own NCCL communicator for larger
+batches, the prompt prefill and routed-expert models.
 """
 
 from __future__ import annotations
@@ -87,9 +91,14 @@ def max_over_ranks(v: float) -> float:
     return float(t.item())
 
 
-def bench_main(args, metric: str, prompt: int, prefill_fn) -> None:
+def bench_main(args, metric: str, prompt: int, prefill_fn, config_fn, length: int, clocks_cls=None) -> None:
     """The decode bench at N ranks: each rank replays its shard's captured
-    step; the step time is the max over ranks of the device-timed replays."""
+    step; the step time is the max over ranks of the device-timed replays.
+    `config_fn(world, length)` describes the workload; `clocks_cls(device)`,
+    when given, samples the SM clocks of rank 0's GPU over the timed
+    replays."""
+    import contextlib
+
     import torch.distributed as dist
 
     from .engine import Llama
@@ -97,7 +106,6 @@ def bench_main(args, metric: str, prompt: int, prefill_fn) -> None:
 
     ctx, rank, world, local = init()
     b = args.batch
-    length = 4096 if b <= 4 else 1024
     wt, ct = getattr(args, "weights", "f32"), getattr(args, "cache", "f32")
     shape = LlamaShape(layers=args.layers, slots=b, length=length, positions=length, weights=wt, cache=ct)
     eng = Llama(ctx, shape, b, seed=2026, chunk=32, rank=rank, world=world)
@@ -114,7 +122,9 @@ def bench_main(args, metric: str, prompt: int, prefill_fn) -> None:
     eng.set_rows(tokens, np.full(b, prompt, np.uint32), slots)
     dist.barrier()
     ctx.sync()
-    ms = graph.time(0, args.steps)
+    clk = clocks_cls(local) if (clocks_cls is not None and rank == 0) else contextlib.nullcontext()
+    with clk:
+        ms = graph.time(0, args.steps)
     dist.barrier()
     ms = max_over_ranks(ms)
     ms_step = ms / args.steps
@@ -146,15 +156,14 @@ def bench_main(args, metric: str, prompt: int, prefill_fn) -> None:
             "dtype": "f32" if (wt, ct) == ("f32", "f32") else f"{wt} weights, {ct} KV caches, f32 activations",
             "data": "synthetic: seeded N(0,0.02) weights made on the device; prompts of 512 ids U[0,32000) (numpy "
                     "PCG64 seed 512) prefilled through the model",
-            "config": {"workload": f"config 5 decode, batch {b}, context {prompt}..{prompt + args.steps}",
-                       "model": "llama-shaped 32 layers, d 4096, 32 heads x 128, ffn 11008, vocab 32000, tied head",
-                       "global_batch": b, "seq_len": prompt, "parallelism": f"tp{world}", "kv_length": length,
-                       "l2": "no flush: each step streams the shard's weights, > 126 MB L2"},
+            "config": config_fn(world, length),
             "hbm": {"per_gpu_step_bytes": per_rank, "per_gpu_achieved_gbs": per_rank / (ms_step / 1e3) / 1e9},
             "e2e": {"value": b * args.steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(host_in.nbytes),
                     "d2h_bytes_per_step": int(host_out.nbytes)},
             "gpu_launches": eng.launch_count() * args.steps,
             "prefill": prefill,
         }
+        if clocks_cls is not None:
+            line["clocks"] = clk.summary()
         print(json.dumps(line), flush=True)
     finish(ctx, [graph])

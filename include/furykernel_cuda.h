@@ -69,8 +69,16 @@ int fkc_sync(fkc_ctx *ctx);
 /* Synchronizes, then reads and clears the context's device status word:
  * 0, or the code a kernel with bounded waits recorded when one ran out
  * (the tensor-core GEMM: 1 a stage never filled, 2 a stage never freed,
- * 3 the accumulator never completed). */
+ * 3 the accumulator never completed; the tensor-parallel exchange: 10 + the
+ * exchange buffer whose peers' rows or signal never came). */
 int fkc_status(fkc_ctx *ctx, int *code);
+/* The bound of each wait on another rank (the tensor-parallel exchange's),
+ * in microseconds at the device's highest SM clock; 0 restores the default
+ * of about 2 s. A wait that runs out records its status (fkc_status) and
+ * the kernel goes on with what it has, so that the context stays usable.
+ * Applies to launches made after the call (a captured graph keeps the
+ * bound it was captured with). */
+int fkc_set_wait_limit(fkc_ctx *ctx, unsigned microseconds);
 
 /* ---- memory ------------------------------------------------------------- */
 /* Buffers the engine binds to kernels (the reference's caller-owned slices,

@@ -6,14 +6,9 @@ A 16-bit weight widens exactly to f32 and a 16-bit cache holds each stored
 value rounded to its type (src/FuryKernel/Program/Eval.hs:9), so every form
 is held bit for bit to the f32 kernel over the widened weights or caches --
 itself bit-exact with the oracle -- and to the oracle directly; the decode
-step of a 16-bit model to the oracle's decode over the widened model.
-
-These forms have not run on a B200 yet: the module runs only with
-FURYKERNEL_NEW_KERNELS=1 in the environment, so that a run of the GPU suite
-exercises only kernels that have passed on a GPU before."""
+step of a 16-bit model to the oracle's decode over the widened model."""
 
 import math
-import os
 
 import numpy as np
 import pytest
@@ -22,10 +17,7 @@ from furykernel_b200.target import CACHE_SUFFIX, WEIGHT_SUFFIX
 from oracle import oracle as O
 from tests import model_check as MC
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("FURYKERNEL_NEW_KERNELS") != "1",
-                                 reason="the 16-bit forms have not run on a B200 yet (FURYKERNEL_NEW_KERNELS=1 runs "
-                                        "them)")]
+pytestmark = pytest.mark.gpu
 TYPES = ("bf16", "f16")
 
 THREADS = O.threads_default()

@@ -406,14 +406,17 @@ def test_dimension_refusal_text(ctx):
 
     # Buffers large enough for the refused shapes, so that nothing could
     # reach past them even if a check were missing.
-    x = ctx.empty(65 * 8)
-    y = ctx.empty(65 * 8)
+    x = ctx.empty(65536 * 8)
+    y = ctx.empty(65536 * 8)
     with pytest.raises(N.Refused) as e:
         ctx.launch("softmax_rows", {"rows": 1, "h": 6}, [x, y])
     assert str(e.value) == "softmax_rows: the dimension h is 6, outside its range 4..16384 multiple of 4."
     with pytest.raises(N.Refused) as e:
-        ctx.launch("gemv", {"n": 4, "k": 4, "m": 65, "split": 1, "ldx": 4, "ldy": 4}, [x, x, y])
-    assert str(e.value) == "gemv: the dimension m is 65, outside its range 1..64."
+        ctx.launch("gemv", {"n": 4, "k": 4, "m": 65536, "split": 1, "ldx": 4, "ldy": 4}, [x, x, y])
+    assert str(e.value) == "gemv: the dimension m is 65536, outside its range 1..65535."
+    with pytest.raises(N.Refused) as e:
+        ctx.launch("gemv", {"n": 4, "k": 4, "m": 1, "split": 9, "ldx": 4, "ldy": 4}, [x, x, y])
+    assert str(e.value) == "gemv: the dimension split is 9, outside its range 1..8."
     x.free()
     y.free()
 

@@ -2,13 +2,8 @@
 route, the expert-grouped routed GEMV, the GELU-tanh gate and the
 rank-weighted combine, each bit for bit with the oracle's restatement
 (oracle/fko_cpu.c), and a decode step of a model whose FFN is routed
-experts, bit for bit with the oracle's decode.
+experts, bit for bit with the oracle's decode."""
 
-These kernels have not run on a B200 yet: the module runs only with
-FURYKERNEL_NEW_KERNELS=1 in the environment, so that a run of the GPU suite
-exercises only kernels that have passed on a GPU before."""
-
-import os
 
 import numpy as np
 import pytest
@@ -17,10 +12,7 @@ from furykernel_b200.target import WEIGHT_SUFFIX
 from oracle import oracle as O
 from tests import model_check as MC
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("FURYKERNEL_NEW_KERNELS") != "1",
-                                 reason="the routed-expert kernels have not run on a B200 yet "
-                                        "(FURYKERNEL_NEW_KERNELS=1 runs them)")]
+pytestmark = pytest.mark.gpu
 
 THREADS = O.threads_default()
 

@@ -6,14 +6,9 @@ pool (src/FuryKernel/Program/Eval.hs:592-602); the kernels keep the ring
 kernels' arithmetic position for position, so each is held bit for bit to
 the oracle's ring arithmetic over the row's blocks gathered in table order
 (tests/model_check.py: pool_to_rings), and the decode step of a model with
-paged caches to the oracle's decode.
-
-These kernels have not run on a B200 yet: the module runs only with
-FURYKERNEL_NEW_KERNELS=1 in the environment, so that a run of the GPU suite
-exercises only kernels that have passed on a GPU before."""
+paged caches to the oracle's decode."""
 
 import math
-import os
 
 import numpy as np
 import pytest
@@ -22,10 +17,7 @@ from furykernel_b200.target import CACHE_SUFFIX
 from oracle import oracle as O
 from tests import model_check as MC
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("FURYKERNEL_NEW_KERNELS") != "1",
-                                 reason="the paged kernels have not run on a B200 yet (FURYKERNEL_NEW_KERNELS=1 "
-                                        "runs them)")]
+pytestmark = pytest.mark.gpu
 
 THREADS = O.threads_default()
 

@@ -93,8 +93,6 @@ def test_tp_decode_step_within_bounds(tmp_path, world):
     assert np.array_equal(ids[0][decided], ref_ids[decided])
 
 
-@pytest.mark.skipif(os.environ.get("FURYKERNEL_NEW_KERNELS") != "1",
-                    reason="routed experts have not run on a B200 yet (FURYKERNEL_NEW_KERNELS=1 runs them)")
 def test_tp_moe_decode_step(tmp_path):
     """Routed experts over 2 ranks: the router whole on each, each rank's ffn
     slice of every expert, the experts' outputs and the attention's partials
