@@ -54,6 +54,7 @@ def lib() -> ctypes.CDLL:
             "fkc_stream": (i32, [vp, pvp]),
             "fkc_sm_count": (i32, [vp, ctypes.POINTER(i32)]),
             "fkc_set_pdl": (i32, [vp, i32]),
+            "fkc_set_wait_limit": (i32, [vp, u32]),
             "fkc_sync": (i32, [vp]),
             "fkc_status": (i32, [vp, ctypes.POINTER(i32)]),
             "fkc_buf_alloc": (i32, [vp, sz, pvp]),
@@ -271,6 +272,11 @@ class Context:
 
     def set_pdl(self, on: bool) -> None:
         check(lib().fkc_set_pdl(self.handle, 1 if on else 0))
+
+    def set_wait_limit(self, microseconds: int) -> None:
+        """The bound of each wait on another rank, in microseconds (0: the
+        default, about 2 s)."""
+        check(lib().fkc_set_wait_limit(self.handle, microseconds))
 
     def sync(self) -> None:
         check(lib().fkc_sync(self.handle))

@@ -155,7 +155,10 @@ int fkc_launch(fkc_ctx *ctx, int kernel, const void *params, size_t params_len, 
  * Runs on the current device, on `stream` (a cudaStream_t, NULL for the
  * default stream). The first call on a device looks up the array's device
  * address (cudaGetSymbolAddress) with that device current: make that first
- * call before any stream capture. Every call on a device shares the one
+ * call before any stream capture. The address found is kept for the life of
+ * the process: after a cudaDeviceReset of a device (which ends the memory
+ * of its primary context) this entry point must not be called on that
+ * device again in the same process. Every call on a device shares the one
  * array, which keeps the last call's contents; calls that overlap on the GPU
  * (on different streams without ordering between them) race and must not
  * be made. Nothing here calls cudaMalloc, cudaFree or any allocating

@@ -437,3 +437,49 @@ def test_graph_capture_replays_launches(ctx):
     g.destroy()
     for buf in (da, db, dy):
         buf.free()
+
+
+def test_peer_wait_runs_out_and_reports():
+    """A tensor-parallel exchange whose other rank never writes: the wait
+    gives up at the context's bound (here 100 us), the kernel returns, the
+    status word says which exchange buffer (10 + buffer), and the context
+    stays usable. Both "ranks'" regions are on this GPU; the second rank
+    simply never runs, so its row count never comes."""
+    import ctypes
+    import time
+
+    from furykernel_b200 import _native as N
+
+    L = N.lib()
+    c = N.Context(0)
+    try:
+        words = L.fkc_peer_region_bytes() // 4
+        r0, r1 = c.zeros(words), c.zeros(words)
+        N.check(L.fkc_peer_set(c.handle, 2, 0, (ctypes.c_void_p * 2)(r0.ptr, r1.ptr)))
+        c.set_wait_limit(100)
+        d, k, n = 256, 128, 64
+        w1 = c.to_device(O.normal(91, d * k, 0.0, 0.02).reshape(d, k))
+        x = c.to_device(O.normal(92, k).reshape(1, k))
+        # Rank 0's row-parallel GEMV: its partial rows into both regions,
+        # counted in; rank 1's count in rank 0's region stays 0.
+        c.launch("gemv_scatter", {"n": d, "k": k, "m": 1, "split": 1, "ldx": k, "xbuf": 1}, [w1, x])
+        assert c.status() == 0
+        w2 = c.to_device(O.normal(93, n * d, 0.0, 0.02).reshape(n, d))
+        r = c.to_device(O.normal(94, d).reshape(1, d))
+        g = c.to_device(O.uniform(95, d, 0.5, 1.5))
+        xout, y = c.empty((1, d)), c.empty((1, n))
+        t0 = time.perf_counter()
+        c.launch("gemv_reduce_rmsnorm", {"n": n, "k": d, "m": 1, "split": 1, "ldr": d, "ldy": n, "eps": 1e-5,
+                                         "factor": 1.0, "xbuf": 1}, [w2, r, g, xout, y])
+        assert c.status() == 11
+        assert time.perf_counter() - t0 < 1.0  # the default bound alone is about 2 s
+        # Rank 0's own rows did arrive in its region (its count is d).
+        flags = r0.download()[:8 * 3].view(np.uint32).reshape(3, 8)
+        assert flags[1, 0] == d and flags[1, 1] == 0
+        # The context still launches and reports a clean status.
+        a, b, s = c.to_device(O.normal(96, 1024)), c.to_device(O.normal(97, 1024)), c.empty(1024)
+        c.launch("add", {"n": 1024}, [a, b, s])
+        assert same_bits(s.download(), O.add(O.normal(96, 1024), O.normal(97, 1024)))
+        assert c.status() == 0
+    finally:
+        c.close()

@@ -1,8 +1,9 @@
 """The reduction entry point that allocates nothing (fkc_reduce_sum_f32_noalloc),
 for callers that cannot call cudaMalloc: called through the C ABI, its
 output must be the bits of the table's reduce_groups + reduce_final on the
-same input, on two calls in a row (the second after the first has left its
-scratch behind), and a size past its static scratch must be refused.
+same input, and of the oracle's restatement of the CPU target's order, on
+two calls in a row (the second after the first has left its scratch
+behind), and a size past its static scratch must be refused.
 
 Kept in a file that pytest collects last, so that a run that stops at its
 first failure has run every other test first."""
@@ -61,6 +62,9 @@ def test_noalloc_sum_matches_the_table_kernels_twice(ctx):
         got = yd.download()[0]
         want = table_sum(ctx, xd, n)
         assert np.float32(got).view(np.uint32) == np.float32(want).view(np.uint32), (n, got, want)
+        # And the CPU target's order, restated by the oracle, bit for bit.
+        ref = O.reduce_sum(x, O.threads_default())
+        assert np.float32(got).view(np.uint32) == np.float32(ref).view(np.uint32), (n, got, ref)
         xd.free()
         yd.free()
 
