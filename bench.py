@@ -237,6 +237,55 @@ NCU_TRAFFIC = {
 }
 
 
+def kernel_roofline(ctx, eng, L, local: int, peak: float, peak_kind: str, b: int, share: float) -> dict:
+    """One GEMV launch of the step timed alone (20 launches after 3, CUDA
+    events on the context's stream), against the measured HBM peak: its
+    algorithmic bytes (the weights once, x and y) over its mean duration."""
+    import torch
+
+    for _ in range(3):
+        L.run(ctx)
+    ctx.sync()
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 20
+    e0.record(stream)
+    for _ in range(reps):
+        L.run(ctx)
+    e1.record(stream)
+    e1.synchronize()
+    k_ms = e0.elapsed_time(e1) / reps
+    p = L.params
+    outs = p["n"] // 2 if "_silu" in L.kernel and "rmsnorm" in L.kernel else p["n"]  # a row pair, one output
+    k_bytes = eng.wb * (p["n"] * p["k"] + p["k"]) + 4 * (p["m"] * p["k"] + p["m"] * outs)
+    k_gbs = k_bytes / (k_ms / 1e3) / 1e9
+    traffic = NCU_TRAFFIC.get((L.kernel, p["n"], p["k"], p["m"]), (None, None))
+    return {"kernel": "%s %d x %d, batch %d" % (L.kernel, p["n"], p["k"], b), "bound": "hbm",
+            "achieved": k_gbs, "peak": peak, "unit": "GB/s", "frac": k_gbs / peak, "traffic": traffic[0],
+            "traffic_source": traffic[1], "algorithmic_bytes": k_bytes, "launch_ms": k_ms, "peak_kind": peak_kind,
+            "weight_share_of_step": share}
+
+
+GEN_STEPS = 128
+
+
+def generation_run(eng, graph, tokens, seqs, prefill: dict) -> dict:
+    """Config 5's whole request after its prompt: GEN_STEPS greedy decode
+    steps from position PROMPT (the captured step replayed, each feeding
+    its ids to the next, device-timed), and with the prompt's prefill time
+    the request's generated tokens a second."""
+    import numpy as np
+
+    b = len(tokens)
+    eng.set_rows(tokens, np.full(b, PROMPT, np.uint32), seqs)
+    ms = graph.time(0, GEN_STEPS)
+    return {"prompt": PROMPT, "decode_steps": GEN_STEPS, "contexts": f"{PROMPT}..{PROMPT + GEN_STEPS}",
+            "decode_ms": ms, "decode_tokens_per_s": b * GEN_STEPS / (ms / 1e3),
+            "prefill_ms": prefill["ms"],
+            "request_tokens_per_s": b * GEN_STEPS / ((ms + prefill["ms"]) / 1e3),
+            "note": "generated tokens over the prompt's prefill plus the decode steps, device time"}
+
+
 def prompt_prefill(ctx, eng, b: int, local: int, tables=None):
     """Config 5's prompt: b prompts of PROMPT ids U[0, vocab) (numpy PCG64,
     seed 512, the same on every rank), every row but the last prefilled
@@ -351,7 +400,7 @@ def run_ours(args):
         length = kv_length(args.batch)
         return tp.bench_main(args, model_types(args)[0], PROMPT, prompt_prefill,
                              lambda world, n: config5(args.batch, args.steps, world, n, 0, args.weights), length,
-                             Clocks)
+                             Clocks, generation_run)
 
     metric, dtype = model_types(args)
     b = args.batch
@@ -385,27 +434,26 @@ def run_ours(args):
     step_bytes = eng.algorithmic_bytes(contexts)
     step_gbs = step_bytes / (ms_step / 1e3) / 1e9
 
-    # The dominant kernel: the GEMV over [gate; up] (the largest weight
-    # stream), timed alone by CUDA events on the context's stream.
-    L = max((L for L in eng.launches if L.kernel.startswith("gemv")), key=lambda L: L.params["n"] * L.params["k"])
-    for _ in range(3):
-        L.run(ctx)
-    ctx.sync()
+    # The dominant kernel: the GEMV shape that streams the most weight bytes
+    # a step (the [gate; up] GEMV, 32 launches), timed alone by CUDA events
+    # on the context's stream; the LM head (the largest single launch)
+    # beside it.
     import torch
 
     torch.cuda.set_device(local)
-    stream = torch.cuda.ExternalStream(ctx.stream())
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 20
-    e0.record(stream)
-    for _ in range(reps):
-        L.run(ctx)
-    e1.record(stream)
-    e1.synchronize()
-    k_ms = e0.elapsed_time(e1) / reps
-    p = L.params
-    k_bytes = eng.wb * (p["n"] * p["k"] + p["k"]) + 4 * (p["m"] * p["k"] + p["m"] * p["n"])
-    k_gbs = k_bytes / (k_ms / 1e3) / 1e9
+    gemvs = [L for L in eng.launches if L.kernel.startswith("gemv")]
+    per_shape = {}
+    for L in gemvs:
+        key = (L.kernel, L.params["n"], L.params["k"])
+        per_shape[key] = per_shape.get(key, 0) + L.params["n"] * L.params["k"]
+    dominant = max(per_shape, key=per_shape.get)
+    L_dom = next(L for L in gemvs if (L.kernel, L.params["n"], L.params["k"]) == dominant)
+    L_head = max(gemvs, key=lambda L: L.params["n"] * L.params["k"])
+    roof = {}
+    for name, L in (("dominant", L_dom), ("lm_head", L_head)):
+        roof[name] = kernel_roofline(ctx, eng, L, local, hbm_peak, peak_kind, b,
+                                     share=per_shape[(L.kernel, L.params["n"], L.params["k"])] /
+                                     sum(per_shape.values()))
 
     # End to end through the C ABI: host token ids and positions in (pinned),
     # the graph replayed, the greedy ids back, every step.
@@ -429,6 +477,7 @@ def run_ours(args):
         host_in[rs:rs + b] += 1
     e2e_s = time.perf_counter() - t0
     e2e = b * args.steps / e2e_s
+    generation = generation_run(eng, graph, tokens, seqs, prefill)
 
     line = {
         "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
@@ -440,17 +489,14 @@ def run_ours(args):
         "hbm": {"step_algorithmic_bytes": step_bytes, "achieved_gbs": step_gbs,
                 "frac_of_8tbs": step_gbs / 8000.0, "frac_of_peak": step_gbs / hbm_peak, "peak": hbm_peak,
                 "peak_kind": peak_kind},
-        "roofline": {"kernel": "%s %d x %d (the largest weight stream of a step, one launch, batch %d)"
-                               % (L.kernel, p["n"], p["k"], b), "bound": "hbm",
-                     "achieved": k_gbs, "peak": hbm_peak, "unit": "GB/s", "frac": k_gbs / hbm_peak,
-                     "traffic": NCU_TRAFFIC.get((L.kernel, p["n"], p["k"], p["m"]), (None,))[0],
-                     "traffic_source": NCU_TRAFFIC.get((L.kernel, p["n"], p["k"], p["m"]), (None, None))[1],
-                     "algorithmic_bytes": k_bytes, "launch_ms": k_ms, "peak_kind": peak_kind},
+        "roofline": roof["dominant"],
+        "roofline_lm_head": roof["lm_head"],
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": int(host_in.nbytes),
                 "d2h_bytes_per_step": int(host_out.nbytes)},
         "gpu_launches": eng.launch_count() * args.steps,
         "clocks": clocks,
         "prefill": prefill,
+        "generation": generation,
     }
     if not args.no_cpu_baseline and rank == 0:
         steps = 2

@@ -55,6 +55,10 @@ def lib() -> ctypes.CDLL:
             "fkc_sm_count": (i32, [vp, ctypes.POINTER(i32)]),
             "fkc_set_pdl": (i32, [vp, i32]),
             "fkc_set_wait_limit": (i32, [vp, u32]),
+            "fkc_set_prefetch": (i32, [vp, u64]),
+            "fkc_set_l2_prefetch": (i32, [vp, vp, u64]),
+            "fkc_set_wait_stats": (i32, [vp, i32]),
+            "fkc_read_wait_stats": (i32, [vp, ctypes.POINTER(u64), ctypes.POINTER(u64)]),
             "fkc_sync": (i32, [vp]),
             "fkc_status": (i32, [vp, ctypes.POINTER(i32)]),
             "fkc_buf_alloc": (i32, [vp, sz, pvp]),
@@ -273,10 +277,31 @@ class Context:
     def set_pdl(self, on: bool) -> None:
         check(lib().fkc_set_pdl(self.handle, 1 if on else 0))
 
+    def set_prefetch(self, nbytes: int) -> None:
+        """The L2 bulk-prefetch budget of later streaming GEMV launches (0:
+        the first lines of each warp's first row only)."""
+        check(lib().fkc_set_prefetch(self.handle, nbytes))
+
+    def set_l2_prefetch(self, ptr: int, nbytes: int) -> None:
+        """A range later attention launches bring toward L2 while they run
+        (0, 0: none)."""
+        check(lib().fkc_set_l2_prefetch(self.handle, ptr or None, nbytes))
+
     def set_wait_limit(self, microseconds: int) -> None:
         """The bound of each wait on another rank, in microseconds (0: the
         default, about 2 s)."""
         check(lib().fkc_set_wait_limit(self.handle, microseconds))
+
+    def set_wait_stats(self, on: bool) -> None:
+        """Whether blocks that wait on their peers add their waits to the
+        context's totals (launches and captures after the call)."""
+        check(lib().fkc_set_wait_stats(self.handle, 1 if on else 0))
+
+    def read_wait_stats(self) -> tuple:
+        """(nanoseconds waited, waits) since the last read; then cleared."""
+        ns, n = ctypes.c_uint64(), ctypes.c_uint64()
+        check(lib().fkc_read_wait_stats(self.handle, ctypes.byref(ns), ctypes.byref(n)))
+        return ns.value, n.value
 
     def sync(self) -> None:
         check(lib().fkc_sync(self.handle))

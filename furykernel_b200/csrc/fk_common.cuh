@@ -81,6 +81,32 @@ __device__ __forceinline__ float4 ld_stream(const float4* p) {
   return v;
 }
 
+// A bulk prefetch of [p, p + bytes) into L2 by the copy engine, in pieces of
+// at most 32 KiB: p 16-byte aligned, bytes a multiple of 16. Nothing waits
+// for it; a later load of those lines finds them in L2.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  const char* c = static_cast<const char*>(p);
+  for (uint32_t off = 0; off < bytes; off += 32768u) {
+    const uint32_t n = bytes - off < 32768u ? bytes - off : 32768u;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(c + off), "r"(n) : "memory");
+  }
+}
+
+// This block's slice of [p, p + bytes) brought toward L2 by one thread (p
+// 16-byte aligned, bytes a multiple of 16; the slices of all blocks of the
+// grid cover the range once). Null p: nothing.
+__device__ __forceinline__ void prefetch_l2_slice(const void* p, unsigned long long bytes) {
+  if (!p || threadIdx.x != 0) return;
+  const unsigned long long per = ((bytes + gridDim.x - 1) / gridDim.x + 15) & ~15ull;
+  const unsigned long long off = (unsigned long long)blockIdx.x * per;
+  if (off >= bytes) return;
+  const unsigned long long n = bytes - off < per ? bytes - off : per;
+  for (unsigned long long done = 0; done < n; done += 0x40000000ull) {
+    const unsigned long long piece = n - done < 0x40000000ull ? n - done : 0x40000000ull;
+    prefetch_l2_bulk(static_cast<const char*>(p) + off + done, (uint32_t)piece);
+  }
+}
+
 // Programmatic dependent launch: wait for the grids this one depends on,
 // and let the next one be scheduled.
 __device__ __forceinline__ void grid_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

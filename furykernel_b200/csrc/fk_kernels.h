@@ -32,6 +32,7 @@ struct FkPeers {
   char* base[FK_MAX_PEERS];  // each rank's region as this process maps it
   unsigned world, rank;
   long long wait_cycles;  // a wait's bound in SM clock cycles (the context's setting)
+  unsigned long long* stats;  // null, or [ns waited, waits]: each block's wait added by its thread 0
 };
 
 struct FkGemv {
@@ -53,6 +54,10 @@ struct FkGemv {
   unsigned xbuf;
   float* xout;     // FK_PRO_REDUCE_RMSNORM: where block 0 stores the reduced rows
   int* err;        // the context's status word
+  // Weight bytes (all blocks together) the streaming kernel brings toward
+  // L2 by bulk prefetch before it waits for its predecessor
+  // (fkc_set_prefetch). 0: only the first lines of each warp's first row.
+  size_t prefetch;
 };
 
 struct FkAttend {
@@ -70,6 +75,12 @@ struct FkAttend {
   uint32_t ldq, q_off;
   float scale;
   bool pdl;
+  // A range the launch's blocks bring toward L2 (bulk prefetch, a slice a
+  // block) before they wait for their predecessor: the next GEMV's weights,
+  // which then stream while the attention runs (fkc_set_l2_prefetch). Null:
+  // none.
+  const void* pf;
+  unsigned long long pf_bytes;
 };
 
 // The decode step's KV store and attention in one launch (rows in distinct

@@ -19,6 +19,21 @@ __device__ __forceinline__ long long wait_bound(const FkPeers& P) {
   return P.wait_cycles > 0 ? P.wait_cycles : kPeerWaitCycles;
 }
 
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// With statistics on, the time a block's wait took, added to the context's
+// totals (nanoseconds, and one wait).
+__device__ __forceinline__ void wait_stats_add(const FkPeers& P, unsigned long long t0) {
+  if (P.stats) {
+    atomicAdd(P.stats, global_ns() - t0);
+    atomicAdd(P.stats + 1, 1ull);
+  }
+}
+
 __device__ __forceinline__ uint32_t* xflags(char* base) { return reinterpret_cast<uint32_t*>(base); }
 __device__ __forceinline__ uint32_t* xepoch(char* base) { return reinterpret_cast<uint32_t*>(base + 128); }
 __device__ __forceinline__ uint32_t* xcounter(char* base) { return reinterpret_cast<uint32_t*>(base + 160); }
@@ -94,6 +109,7 @@ __device__ __forceinline__ bool peers_wait_rows(const FkPeers& P, uint32_t buf, 
   if (threadIdx.x == 0) {
     char* me = P.base[P.rank];
     const uint32_t target = *reinterpret_cast<volatile uint32_t*>(xepoch(me) + buf) * rows;
+    const unsigned long long w0 = P.stats ? global_ns() : 0ull;
     ok = 1;
     for (uint32_t q = 0; q < P.world && ok; ++q) {
       const long long t0 = clock64();
@@ -105,6 +121,7 @@ __device__ __forceinline__ bool peers_wait_rows(const FkPeers& P, uint32_t buf, 
         }
       }
     }
+    wait_stats_add(P, w0);
   }
   __syncthreads();
   return ok != 0;
@@ -117,6 +134,7 @@ __device__ __forceinline__ bool peers_wait(const FkPeers& P, uint32_t buf, int* 
   if (threadIdx.x == 0) {
     char* me = P.base[P.rank];
     const uint32_t e = *reinterpret_cast<volatile uint32_t*>(xepoch(me) + buf);
+    const unsigned long long w0 = P.stats ? global_ns() : 0ull;
     ok = 1;
     for (uint32_t q = 0; q < P.world && ok; ++q) {
       const long long t0 = clock64();
@@ -128,6 +146,7 @@ __device__ __forceinline__ bool peers_wait(const FkPeers& P, uint32_t buf, int* 
         }
       }
     }
+    wait_stats_add(P, w0);
   }
   __syncthreads();
   return ok != 0;

@@ -79,8 +79,19 @@ __global__ void __launch_bounds__(128, 4) attend_kernel(FkAttendDecode f) {
   __shared__ float lw[kAttWarps];
   extern __shared__ uint32_t first[];  // [m + 1]: items before row r
 
-  grid_wait();
-  grid_launch_dependents();
+  prefetch_l2_slice(a.pf, a.pf_bytes);
+  // FUSED: the cached keys and values an item reads were stored by earlier
+  // steps (this step's own key and value are substituted where the item
+  // reads them, below), and the positions and slots were set before the
+  // step's first launch: the block's first keys and values are requested
+  // before it waits for the q/k/v GEMV, so that their latency hides under
+  // that launch's end. The unfused kernel follows the KV store step and
+  // waits first.
+  bool waited = !FUSED;
+  if (!FUSED) {
+    grid_wait();
+    grid_launch_dependents();
+  }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     uint32_t acc = 0;
@@ -128,6 +139,11 @@ __global__ void __launch_bounds__(128, 4) attend_kernel(FkAttendDecode f) {
       const size_t at = (base + tt % a.length) * (kHeadDim / 4) + lane;
       kv[u] = tt < t1 ? __ldcs(kc4 + at) : make_float4(0, 0, 0, 0);
       vv[u] = tt < t1 ? __ldcs(vc4 + at) : make_float4(0, 0, 0, 0);
+    }
+    if (!waited) {  // q, the new key and value: the q/k/v GEMV's outputs
+      grid_wait();
+      grid_launch_dependents();
+      waited = true;
     }
 
     __syncthreads();  // the previous item's shared arrays are free
@@ -220,8 +236,8 @@ __global__ void __launch_bounds__(128, 4) attend_kernel(FkAttendDecode f) {
       a.part_l[at] = lt;
       a.part_m[at] = mx;
     }
-
   }
+  if (!waited) grid_launch_dependents();  // a block without items
 }
 
 // Attention over a prompt's rows (prefill), tiled by queries: one block a

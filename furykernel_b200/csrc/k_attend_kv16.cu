@@ -98,8 +98,14 @@ __global__ void __launch_bounds__(128, 4) attend16_kernel(Attend16 f) {
   __shared__ float lw[kAttWarps];
   extern __shared__ uint32_t first[];  // [m + 1]: items before row r
 
-  grid_wait();
-  grid_launch_dependents();
+  prefetch_l2_slice(a.pf, a.pf_bytes);
+  // FUSED: the block's first keys and values are requested before it waits
+  // for the q/k/v GEMV (k_attend.cu's attend_kernel says why that is sound).
+  bool waited = !FUSED;
+  if (!FUSED) {
+    grid_wait();
+    grid_launch_dependents();
+  }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     uint32_t acc = 0;
@@ -144,6 +150,11 @@ __global__ void __launch_bounds__(128, 4) attend16_kernel(Attend16 f) {
       const size_t at = (base + tt % a.length) * (kHeadDim / 4) + lane;
       kv[u] = tt < t1 ? __ldcs(kc2 + at) : zero2;
       vv[u] = tt < t1 ? __ldcs(vc2 + at) : zero2;
+    }
+    if (!waited) {
+      grid_wait();
+      grid_launch_dependents();
+      waited = true;
     }
 
     __syncthreads();  // the previous item's shared arrays are free
@@ -243,6 +254,7 @@ __global__ void __launch_bounds__(128, 4) attend16_kernel(Attend16 f) {
       a.part_m[at] = mx;
     }
   }
+  if (!waited) grid_launch_dependents();  // a block without items
 }
 
 // Attention over a prompt's rows in one slot (prefill), k_attend.cu's

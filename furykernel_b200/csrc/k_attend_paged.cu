@@ -162,8 +162,14 @@ __global__ void __launch_bounds__(128, 4) attend_paged_kernel(AttendArgs<E> f) {
   __shared__ float lw[kAttWarps];
   extern __shared__ uint32_t first[];  // [m + 1]: items before row r
 
-  grid_wait();
-  grid_launch_dependents();
+  prefetch_l2_slice(a.pf, a.pf_bytes);
+  // FUSED: the block's first keys and values are requested before it waits
+  // for the q/k/v GEMV (k_attend.cu's attend_kernel says why that is sound).
+  bool waited = !FUSED;
+  if (!FUSED) {
+    grid_wait();
+    grid_launch_dependents();
+  }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     uint32_t acc = 0;
@@ -203,6 +209,11 @@ __global__ void __launch_bounds__(128, 4) attend_paged_kernel(AttendArgs<E> f) {
       const uint64_t at = tt < t1 ? at_of(f.P, r, tt, kvh, a.kv_heads, kHeadDim) : ~0ull;
       kv[u] = at != ~0ull ? ld_pack<E>(f.kc + at + 4 * lane) : zero4;
       vv[u] = at != ~0ull ? ld_pack<E>(f.vc + at + 4 * lane) : zero4;
+    }
+    if (!waited) {
+      grid_wait();
+      grid_launch_dependents();
+      waited = true;
     }
 
     __syncthreads();  // the previous item's shared arrays are free
@@ -304,6 +315,7 @@ __global__ void __launch_bounds__(128, 4) attend_paged_kernel(AttendArgs<E> f) {
       a.part_m[at] = mx;
     }
   }
+  if (!waited) grid_launch_dependents();  // a block without items
 }
 
 // Attention over a prompt's rows of one sequence (prefill), the ring

@@ -60,6 +60,7 @@ struct StreamArgs {
   uint32_t xbuf;
   float* xout;
   int* err;
+  size_t prefetch;  // bulk L2 prefetch budget of the launch (FkGemv::prefetch)
 };
 
 enum { SPRO_NONE = 0, SPRO_RMSNORM = 1, SPRO_SILU = 2, SPRO_REDUCE_RMSNORM = 3 };
@@ -125,16 +126,32 @@ __global__ void __launch_bounds__(512, 2) gemv_stream_w16_kernel(StreamArgs a) {
   const uint32_t units = a.n / per_unit;
   const uint32_t G = gridDim.x;
 
-  // The weights depend on no earlier launch: start this warp's first rows
-  // toward L2 while the previous kernel finishes.
+  // The weights depend on no earlier launch: while the previous kernels
+  // finish, start this block's rows toward L2. With a prefetch budget
+  // (fkc_set_prefetch), the copy engine brings the block's units in the
+  // order its warps read them (warp w: slots w, w + 16, ...) up to the
+  // block's share of the budget; otherwise each warp's first 8 KB.
   {
-    const uint32_t u0 = EPI == SEPI_SCATTER ? (uint32_t)((uint64_t)units * blockIdx.x / G) + (uint32_t)warp
-                                            : blockIdx.x + (uint32_t)warp * G;
-    if (u0 < units) {
-      const char* row = reinterpret_cast<const char*>(a.w + (size_t)u0 * per_unit * a.k);
-      const size_t bytes = (size_t)per_unit * a.k * 2;
-      for (size_t off = (size_t)lane * 128; off < bytes && off < 8192; off += 32 * 128)
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(row + off));
+    const size_t unit_bytes = (size_t)per_unit * a.k * 2;
+    if (a.prefetch > 0) {
+      const uint32_t p_lo = EPI == SEPI_SCATTER ? (uint32_t)((uint64_t)units * blockIdx.x / G) : 0u;
+      const uint32_t p_hi = EPI == SEPI_SCATTER ? (uint32_t)((uint64_t)units * (blockIdx.x + 1) / G) : 0u;
+      const size_t budget = a.prefetch / G;
+      if (lane == 0 && (reinterpret_cast<uintptr_t>(a.w) & 15) == 0 && unit_bytes % 16 == 0 && unit_bytes <= 0xFFFFFFF0u) {
+        for (uint32_t slot = (uint32_t)warp; (size_t)slot * unit_bytes < budget; slot += kStreamWarps) {
+          const uint32_t u = EPI == SEPI_SCATTER ? p_lo + slot : blockIdx.x + slot * G;
+          if (EPI == SEPI_SCATTER ? u >= p_hi : u >= units) break;
+          prefetch_l2_bulk(a.w + (size_t)u * per_unit * a.k, (uint32_t)unit_bytes);
+        }
+      }
+    } else {
+      const uint32_t u0 = EPI == SEPI_SCATTER ? (uint32_t)((uint64_t)units * blockIdx.x / G) + (uint32_t)warp
+                                              : blockIdx.x + (uint32_t)warp * G;
+      if (u0 < units) {
+        const char* row = reinterpret_cast<const char*>(a.w + (size_t)u0 * per_unit * a.k);
+        for (size_t off = (size_t)lane * 128; off < unit_bytes && off < 8192; off += 32 * 128)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(row + off));
+      }
     }
   }
   grid_wait();
@@ -575,6 +592,7 @@ static cudaError_t gemv(const FkGemv& g, const uint16_t* w, const uint16_t* gamm
     a.xbuf = g.xbuf;
     a.xout = g.xout;
     a.err = g.err;
+    a.prefetch = g.prefetch;
     const int epi = g.scatter ? SEPI_SCATTER : g.silu_pair ? SEPI_SILU_PAIR : (g.r ? SEPI_ADD : SEPI_NONE);
     switch (g.prologue * 4 + epi) {
       case FK_PRO_NONE * 4 + SEPI_NONE: return stream_m<E, SPRO_NONE, SEPI_NONE>(a, sms, st, g.pdl);

@@ -71,6 +71,10 @@ struct fkc_ctx {
   // by rank (fkc_peer_set).
   FkPeers peers = {};
   std::unordered_set<void*> opened;  // peers' regions mapped here
+  unsigned long long* wait_stats = nullptr;  // fkc_set_wait_stats: [ns waited, waits]
+  size_t prefetch = 0;  // fkc_set_prefetch: the streaming GEMVs' L2 prefetch budget
+  const void* l2pf = nullptr;  // fkc_set_l2_prefetch: a range the attention launches prefetch
+  unsigned long long l2pf_bytes = 0;
 };
 
 struct fkc_graph {
@@ -118,6 +122,7 @@ extern "C" int fkc_close(fkc_ctx* c) {
   if (c->red_chains) cudaFree(c->red_chains);
   if (c->red_done) cudaFree(c->red_done);
   if (c->status) cudaFree(c->status);
+  if (c->wait_stats) cudaFree(c->wait_stats);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
   return FKC_OK;
@@ -146,6 +151,47 @@ extern "C" int fkc_set_wait_limit(fkc_ctx* c, unsigned microseconds) {
   int khz = 0;
   FKC_CUDA(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, c->device), "fkc_set_wait_limit");
   c->peers.wait_cycles = (long long)microseconds * (long long)khz / 1000;
+  return FKC_OK;
+}
+
+extern "C" int fkc_set_prefetch(fkc_ctx* c, unsigned long long bytes) {
+  if (!c) return fail(FKC_ERR_ARGUMENT, "fkc_set_prefetch: null context.");
+  c->prefetch = (size_t)bytes;
+  return FKC_OK;
+}
+
+extern "C" int fkc_set_l2_prefetch(fkc_ctx* c, const void* p, unsigned long long bytes) {
+  if (!c) return fail(FKC_ERR_ARGUMENT, "fkc_set_l2_prefetch: null context.");
+  if (p && (((uintptr_t)p & 15) || bytes % 16))
+    return fail(FKC_ERR_ARGUMENT, "fkc_set_l2_prefetch: the range must start on a 16-byte boundary and hold whole "
+                                  "16 bytes.");
+  c->l2pf = bytes ? p : nullptr;
+  c->l2pf_bytes = p ? bytes : 0;
+  return FKC_OK;
+}
+
+extern "C" int fkc_set_wait_stats(fkc_ctx* c, int enabled) {
+  if (!c) return fail(FKC_ERR_ARGUMENT, "fkc_set_wait_stats: null context.");
+  if (c->capturing) return fail(FKC_ERR_STATE, "fkc_set_wait_stats: not during a capture.");
+  cudaSetDevice(c->device);
+  if (enabled && !c->wait_stats) {
+    FKC_CUDA(cudaMalloc(&c->wait_stats, 2 * sizeof(unsigned long long)), "fkc_set_wait_stats");
+    FKC_CUDA(cudaMemset(c->wait_stats, 0, 2 * sizeof(unsigned long long)), "fkc_set_wait_stats");
+  }
+  c->peers.stats = enabled ? c->wait_stats : nullptr;
+  return FKC_OK;
+}
+
+extern "C" int fkc_read_wait_stats(fkc_ctx* c, unsigned long long* ns_waited, unsigned long long* waits) {
+  if (!c || !ns_waited || !waits) return fail(FKC_ERR_ARGUMENT, "fkc_read_wait_stats: null argument.");
+  *ns_waited = 0, *waits = 0;
+  if (!c->wait_stats) return FKC_OK;
+  cudaSetDevice(c->device);
+  unsigned long long h[2];
+  FKC_CUDA(cudaStreamSynchronize(c->stream), "fkc_read_wait_stats");
+  FKC_CUDA(cudaMemcpy(h, c->wait_stats, sizeof h, cudaMemcpyDeviceToHost), "fkc_read_wait_stats");
+  FKC_CUDA(cudaMemset(c->wait_stats, 0, sizeof h), "fkc_read_wait_stats");
+  *ns_waited = h[0], *waits = h[1];
   return FKC_OK;
 }
 
@@ -392,7 +438,9 @@ int l_softmax_rows(fkc_ctx* c, const Params& p, void* const* bufs) {
 
 // Decode batches of up to 4 rows stream through the persistent kernel; larger
 // batches take the chunked one. Both keep the GEMV order contract.
-cudaError_t run_gemv(fkc_ctx* c, const FkGemv& g) {
+cudaError_t run_gemv(fkc_ctx* c, const FkGemv& g0) {
+  FkGemv g = g0;
+  g.prefetch = c->prefetch;
   if (fk_gemv_streams(g)) return fk_launch_gemv_stream(g, c->sms, c->stream);
   if (fk_gemv_batches(g)) return fk_launch_gemv_batch(g, c->sms, c->stream);
   return fk_launch_gemv(g, c->stream);
@@ -492,6 +540,7 @@ int l_attend(fkc_ctx* c, const Params& p, void* const* bufs) {
   a.chunk = p.u(6), a.max_splits = p.u(7), a.ldq = p.u(8), a.q_off = p.u(9);
   a.scale = p.f(10);
   a.pdl = c->pdl;
+  a.pf = c->l2pf, a.pf_bytes = c->l2pf_bytes;
   if (a.kv_heads == 0 || a.heads % a.kv_heads != 0)
     return fail(FKC_ERR_ARGUMENT, "attend_split: %u heads do not share %u KV heads in groups.", a.heads, a.kv_heads);
   return launched(fk_launch_attend(a, c->stream), "attend_split");
@@ -512,6 +561,7 @@ int l_attend_decode(fkc_ctx* c, const Params& p, void* const* bufs) {
   f.k_off = p.u(10), f.v_off = p.u(11);
   a.scale = p.f(12);
   a.pdl = c->pdl;
+  a.pf = c->l2pf, a.pf_bytes = c->l2pf_bytes;
   if (a.kv_heads == 0 || a.heads % a.kv_heads != 0)
     return fail(FKC_ERR_ARGUMENT, "attend_decode: %u heads do not share %u KV heads in groups.", a.heads, a.kv_heads);
   if (a.rotated > a.d / 2) return fail(FKC_ERR_ARGUMENT, "attend_decode: rotated %u is more than d/2.", a.rotated);
@@ -616,6 +666,7 @@ int l_gemv_scatter(fkc_ctx* c, const Params& p, void* const* bufs) {
   g.peers = c->peers;
   g.err = c->status;
   if (!fk_gemv_streams(g)) return fail(FKC_ERR_ARGUMENT, "gemv_scatter: m %u is past the streaming kernel's 4.", g.m);
+  g.prefetch = c->prefetch;
   return launched(fk_launch_gemv_stream(g, c->sms, c->stream), "gemv_scatter");
 }
 
@@ -635,6 +686,7 @@ int reduce_gemv(fkc_ctx* c, const Params& p, void* const* bufs, bool silu, const
   g.err = c->status;
   if (g.ldx != g.k) return fail(FKC_ERR_ARGUMENT, "%s: the residual rows must be whole (ldr %u, k %u).", name, g.ldx, g.k);
   if (!fk_gemv_streams(g)) return fail(FKC_ERR_ARGUMENT, "%s: m %u is past the streaming kernel's 4.", name, g.m);
+  g.prefetch = c->prefetch;
   return launched(fk_launch_gemv_stream(g, c->sms, c->stream), name);
 }
 int l_gemv_reduce_rmsnorm(fkc_ctx* c, const Params& p, void* const* bufs) {
@@ -690,7 +742,9 @@ int l_silu_pairs(fkc_ctx* c, const Params& p, void* const* bufs) {
 #define KN(base) (EL == FK_F16 ? base "_kvf16" : base "_kvbf16")
 
 template <FkElem EL>
-int gemv_w16(fkc_ctx* c, const FkGemv& g, const uint16_t* w, const uint16_t* gamma, const char* name) {
+int gemv_w16(fkc_ctx* c, const FkGemv& g0, const uint16_t* w, const uint16_t* gamma, const char* name) {
+  FkGemv g = g0;
+  g.prefetch = c->prefetch;
   return launched(fk_launch_gemv_w16(g, EL, w, gamma, c->sms, c->stream), name);
 }
 template <FkElem EL>
@@ -821,6 +875,7 @@ FkAttend attend_base(fkc_ctx* c, const Params& p, void* const* bufs) {
   a.qkv = CF(0), a.cos_t = CF(1), a.sin_t = CF(2), a.pos = CU(3), a.slot = CU(4);
   a.m = p.u(0), a.heads = p.u(1), a.kv_heads = p.u(2), a.d = p.u(3), a.length = p.u(4), a.rotated = p.u(5);
   a.pdl = c->pdl;
+  a.pf = c->l2pf, a.pf_bytes = c->l2pf_bytes;
   return a;
 }
 template <FkElem EL>
@@ -935,6 +990,7 @@ int attend_paged(fkc_ctx* c, const Params& p, void* const* bufs, FkElem el, cons
   a.chunk = p.u(8), a.max_splits = p.u(9), a.ldq = p.u(10), a.q_off = p.u(11);
   a.scale = p.f(12);
   a.pdl = c->pdl;
+  a.pf = c->l2pf, a.pf_bytes = c->l2pf_bytes;
   const FkPaged pg = {CU(4), p.u(4), p.u(5), p.u(6)};
   if (a.kv_heads == 0 || a.heads % a.kv_heads != 0)
     return fail(FKC_ERR_ARGUMENT, "%s: %u heads do not share %u KV heads in groups.", name, a.heads, a.kv_heads);
@@ -960,6 +1016,7 @@ int attend_decode_paged(fkc_ctx* c, const Params& p, void* const* bufs, FkElem e
   a.chunk = p.u(8), a.max_splits = p.u(9), a.ldq = p.u(10), a.q_off = p.u(11);
   a.scale = p.f(14);
   a.pdl = c->pdl;
+  a.pf = c->l2pf, a.pf_bytes = c->l2pf_bytes;
   const FkPaged pg = {CU(4), p.u(4), p.u(5), p.u(6)};
   if (a.kv_heads == 0 || a.heads % a.kv_heads != 0)
     return fail(FKC_ERR_ARGUMENT, "%s: %u heads do not share %u KV heads in groups.", name, a.heads, a.kv_heads);

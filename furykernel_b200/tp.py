@@ -91,7 +91,42 @@ def max_over_ranks(v: float) -> float:
     return float(t.item())
 
 
-def bench_main(args, metric: str, prompt: int, prefill_fn, config_fn, length: int, clocks_cls=None) -> None:
+def peer_wait_profile(ctx, eng, steps: int) -> dict:
+    """How long the peer exchanges of a step wait, after the timed run: the
+    step captured again with wait statistics on (each waiting block adds its
+    wait, fkc_set_wait_stats) and replayed `steps` times on every rank.
+    Reports, over ranks, the mean time a block waited at one exchange and
+    the exchanges of a step; their product is the time a rank's blocks
+    spend waiting for their peers in a step."""
+    import torch.distributed as dist
+
+    exchanges = sum(1 for L in eng.launches if L.kernel.startswith(("gemv_reduce_rmsnorm", "argmax_gather_pick")))
+    ctx.set_wait_stats(True)
+    eng.graph = None
+    g = eng.capture()
+    ctx.set_wait_stats(False)
+    dist.barrier()
+    ctx.sync()
+    ms = g.time(1, steps)
+    ns, n = ctx.read_wait_stats()
+    g.destroy()
+    eng.graph = None
+    per_wait_us = ns / max(n, 1) / 1e3
+    import torch
+
+    t = torch.tensor([per_wait_us, ms / steps], dtype=torch.float64, device="cuda")
+    got = [torch.zeros_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(got, t)
+    per_rank = [float(x[0]) for x in got]
+    return {"us_per_block_wait_by_rank": per_rank, "exchanges_per_step": exchanges,
+            "us_waited_per_step_max_rank": max(per_rank) * exchanges,
+            "ms_per_step_with_stats_max_rank": max(float(x[1]) for x in got),
+            "note": "mean over the waiting blocks of one exchange's wait (device clock), from a separate capture "
+                    "with wait statistics on; not inside the timed region"}
+
+
+def bench_main(args, metric: str, prompt: int, prefill_fn, config_fn, length: int, clocks_cls=None,
+               generation_fn=None) -> None:
     """The decode bench at N ranks: each rank replays its shard's captured
     step; the step time is the max over ranks of the device-timed replays.
     `config_fn(world, length)` describes the workload; `clocks_cls(device)`,
@@ -148,6 +183,12 @@ def bench_main(args, metric: str, prompt: int, prefill_fn, config_fn, length: in
         host_in[rs:rs + b] += 1
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     per_rank = eng.algorithmic_bytes([prompt + args.steps / 2] * b)
+    waits = peer_wait_profile(ctx, eng, args.steps) if eng.peer_exchange else None
+    generation = None
+    if generation_fn is not None:
+        dist.barrier()
+        generation = generation_fn(eng, graph, tokens, slots, prefill)
+        generation["decode_ms"] = max_over_ranks(generation["decode_ms"])
     if rank == 0:
         line = {
             "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -165,5 +206,12 @@ def bench_main(args, metric: str, prompt: int, prefill_fn, config_fn, length: in
         }
         if clocks_cls is not None:
             line["clocks"] = clk.summary()
+        if waits is not None:
+            line["peer_waits"] = waits
+        if generation is not None:
+            g = generation
+            g["decode_tokens_per_s"] = b * g["decode_steps"] / (g["decode_ms"] / 1e3)
+            g["request_tokens_per_s"] = b * g["decode_steps"] / ((g["decode_ms"] + g["prefill_ms"]) / 1e3)
+            line["generation"] = g
         print(json.dumps(line), flush=True)
     finish(ctx, [graph])

@@ -65,6 +65,22 @@ int fkc_sm_count(fkc_ctx *ctx, int *sms);
 /* Launch later kernels as programmatic dependents of the previous launch
  * (overlaps a launch's start with its predecessor's end). Default off. */
 int fkc_set_pdl(fkc_ctx *ctx, int enabled);
+/* The weight bytes each later weight-streaming GEMV launch (decode batches
+ * of up to 4 rows) brings toward L2 by bulk prefetch, all its blocks
+ * together, in the order its warps read them, before it waits for its
+ * predecessor; 0 (the default): only the first lines of each warp's first
+ * row. The blocks that become resident while the previous launch drains
+ * start their weight stream early (measured on the 32-layer decode step:
+ * 64 MiB takes about 2% off a batch-1 step, adds about 2% at batch 4). A
+ * launch setting like fkc_set_pdl: captured into graphs as it stands. */
+int fkc_set_prefetch(fkc_ctx *ctx, unsigned long long bytes);
+/* A device range (16-byte aligned, whole 16 bytes) that later decode
+ * attention launches (attend_split, attend_decode and their 16-bit and
+ * paged forms) bring toward L2 by bulk prefetch, a slice a block, before
+ * they wait for their predecessor: the next GEMV's weights, which then
+ * stream from HBM while the latency-bound attention runs. p NULL or bytes 0:
+ * none (the default). A launch setting like fkc_set_pdl. */
+int fkc_set_l2_prefetch(fkc_ctx *ctx, const void *p, unsigned long long bytes);
 int fkc_sync(fkc_ctx *ctx);
 /* Synchronizes, then reads and clears the context's device status word:
  * 0, or the code a kernel with bounded waits recorded when one ran out
@@ -79,6 +95,14 @@ int fkc_status(fkc_ctx *ctx, int *code);
  * Applies to launches made after the call (a captured graph keeps the
  * bound it was captured with). */
 int fkc_set_wait_limit(fkc_ctx *ctx, unsigned microseconds);
+/* Statistics of those waits, for finding what limits tensor-parallel steps:
+ * while on, every block that waits on its peers adds the time it waited
+ * (device clock, nanoseconds) and one wait to the context's totals, which
+ * fkc_read_wait_stats synchronizes, returns and clears. Off by default (the
+ * totals cost two atomics a block a wait); applies to launches made, or
+ * graphs captured, after the call; not during a capture. */
+int fkc_set_wait_stats(fkc_ctx *ctx, int enabled);
+int fkc_read_wait_stats(fkc_ctx *ctx, unsigned long long *ns_waited, unsigned long long *waits);
 
 /* ---- memory ------------------------------------------------------------- */
 /* Buffers the engine binds to kernels (the reference's caller-owned slices,

@@ -468,11 +468,19 @@ def test_peer_wait_runs_out_and_reports():
         r = c.to_device(O.normal(94, d).reshape(1, d))
         g = c.to_device(O.uniform(95, d, 0.5, 1.5))
         xout, y = c.empty((1, d)), c.empty((1, n))
+        c.set_wait_stats(True)
         t0 = time.perf_counter()
         c.launch("gemv_reduce_rmsnorm", {"n": n, "k": d, "m": 1, "split": 1, "ldr": d, "ldy": n, "eps": 1e-5,
                                          "factor": 1.0, "xbuf": 1}, [w2, r, g, xout, y])
         assert c.status() == 11
         assert time.perf_counter() - t0 < 1.0  # the default bound alone is about 2 s
+        # Every block waited about the bound (SM cycles at the highest
+        # clock: at least 100 us of device time, well under a second).
+        ns, waits = c.read_wait_stats()
+        c.set_wait_stats(False)
+        assert 1 <= waits <= 2 * c.sms
+        assert 90_000 <= ns / waits < 1e9, (ns, waits)
+        assert c.read_wait_stats() == (0, 0)
         # Rank 0's own rows did arrive in its region (its count is d).
         flags = r0.download()[:8 * 3].view(np.uint32).reshape(3, 8)
         assert flags[1, 0] == d and flags[1, 1] == 0
