@@ -22,6 +22,7 @@
 
 #include "fk_common.cuh"
 #include "fk_kernels.h"
+#include "fk_tcgen05.cuh"
 
 namespace fk {
 
@@ -36,96 +37,7 @@ constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at the B200's clock
 // Error codes the kernel records (first one wins).
 enum { GEMM_OK = 0, GEMM_TIMEOUT_FULL = 1, GEMM_TIMEOUT_EMPTY = 2, GEMM_TIMEOUT_ACCUM = 3 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.b32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Waits for the barrier's phase, at most kWaitCycles; false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  const long long t0 = clock64();
-  while (!mbar_try(bar, parity))
-    if (clock64() - t0 > kWaitCycles) return false;
-  return true;
-}
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          dst),
-      "l"(map), "r"(x), "r"(y), "r"(bar)
-      : "memory");
-}
-
-// The shared-memory matrix descriptor of a K-major operand tile in the
-// 128-byte-swizzled canonical layout: rows of 128 bytes, 8-row atoms 1024
-// bytes apart (stride byte offset), descriptor version 1, swizzle mode 2.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
-  d |= (uint64_t)(16u >> 4) << 16;
-  d |= (uint64_t)(1024u >> 4) << 32;
-  d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
-  return d;
-}
-
-// The instruction descriptor of kind::tf32: f32 accumulators, TF32 A and B,
-// both K-major, N = kGN, M = kGM.
-__host__ __device__ constexpr uint32_t tf32_idesc() {
-  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(kGN >> 3) << 17) | ((uint32_t)(kGM >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_tf32(uint32_t tmem, uint64_t da, uint64_t db, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem),
-      "l"(da), "l"(db), "r"(tf32_idesc()), "r"(accumulate));
-}
-
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void record(int* err, int code) {
-  if (err) atomicCAS(err, 0, code);
-}
+using namespace tc;
 
 __global__ void __launch_bounds__(192, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
@@ -171,7 +83,7 @@ __global__ void __launch_bounds__(192, 1)
     // The producer: K slabs of the four operand tiles into the ring.
     for (uint32_t kb = 0; kb < kblocks; ++kb) {
       const uint32_t s = kb % kStages, use = kb / kStages;
-      if (use > 0 && !mbar_wait(smem_u32(&bars[kStages + s]), (use - 1) & 1)) {
+      if (use > 0 && !mbar_wait(smem_u32(&bars[kStages + s]), (use - 1) & 1, kWaitCycles)) {
         record(err, GEMM_TIMEOUT_EMPTY);
         aborted = 1;
         break;
@@ -190,7 +102,7 @@ __global__ void __launch_bounds__(192, 1)
     bool ok = true;
     for (uint32_t kb = 0; kb < kblocks && ok; ++kb) {
       const uint32_t s = kb % kStages, use = kb / kStages;
-      if (!mbar_wait(smem_u32(&bars[s]), use & 1)) {
+      if (!mbar_wait(smem_u32(&bars[s]), use & 1, kWaitCycles)) {
         record(err, GEMM_TIMEOUT_FULL);
         ok = false;
         break;
@@ -204,9 +116,9 @@ __global__ void __launch_bounds__(192, 1)
       for (uint32_t kk = 0; kk < kGK / 8; ++kk) {
         const uint32_t off = kk * 32;  // 8 floats of K within the 128-byte row
         const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
-        mma_tf32(tmem, sw128_desc(a_hi + off), sw128_desc(w_hi + off), acc);
-        mma_tf32(tmem, sw128_desc(a_hi + off), sw128_desc(w_lo + off), 1u);
-        mma_tf32(tmem, sw128_desc(a_lo + off), sw128_desc(w_hi + off), 1u);
+        mma_tf32(tmem, sw128_desc(a_hi + off), sw128_desc(w_hi + off), tf32_idesc(kGN), acc);
+        mma_tf32(tmem, sw128_desc(a_hi + off), sw128_desc(w_lo + off), tf32_idesc(kGN), 1u);
+        mma_tf32(tmem, sw128_desc(a_lo + off), sw128_desc(w_hi + off), tf32_idesc(kGN), 1u);
       }
       mma_commit(smem_u32(&bars[kStages + s]));  // the stage is free once these finish
     }
@@ -216,7 +128,7 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp < 4) {
     // The epilogue: warp w reads TMEM lanes (rows) 32w .. 32w + 31.
-    if (!mbar_wait(smem_u32(&bars[2 * kStages]), 0)) {
+    if (!mbar_wait(smem_u32(&bars[2 * kStages]), 0, kWaitCycles)) {
       record(err, GEMM_TIMEOUT_ACCUM);
     } else if (!aborted) {
       fence_after();

@@ -628,6 +628,20 @@ int l_gemm_tf32x3(fkc_ctx* c, const Params& p, void* const* bufs) {
   return launched(e, "gemm_tf32x3");
 }
 
+// gemm_tf32x3w: a a_hi a_lo w c | M N K ldc. A is split into the caller's
+// a_hi / a_lo first; W (f32, as the weight arena holds it) is split inside
+// the kernel. The tile width is the shape's (fk_gemm_tf32x3w_tile).
+int l_gemm_tf32x3w(fkc_ctx* c, const Params& p, void* const* bufs) {
+  const uint32_t M = p.u(0), N = p.u(1), K = p.u(2), ldc = p.u(3);
+  if (ldc < N) return fail(FKC_ERR_ARGUMENT, "gemm_tf32x3w: ldc %u is less than N %u.", ldc, N);
+  const uint32_t tn = fk_gemm_tf32x3w_tile(M, N, c->sms);
+  cudaError_t e = fk_launch_split_tf32(CF(0), F(1), F(2), (uint64_t)M * K, c->stream);
+  if (e == cudaSuccess)
+    e = fk_launch_gemm_tf32x3w(CF(1), CF(2), CF(3), F(4), M, N, K, ldc, tn, c->peers.wait_cycles, c->status,
+                               c->stream);
+  return launched(e, "gemm_tf32x3w");
+}
+
 // argmax_pairs: x pairs | m n ldx offset
 int l_argmax_pairs(fkc_ctx* c, const Params& p, void* const* bufs) {
   return launched(fk_launch_argmax_pairs(CF(0), p.u(0), p.u(1), p.u(2), p.u(3), U(1), nullptr, c->pdl, c->stream),
@@ -1224,6 +1238,15 @@ std::vector<KernelSpec> make_table() {
                 {"c", "write", "f32"}},
                {dim("M", 1, 1048576), dim("N", 1, 1048576), dim("K", 32, 1048576, 32), u32("ldc")},
                l_gemm_tf32x3});
+  t.push_back({"gemm_tf32x3w",
+               320,
+               {{"a", "read", "f32"},
+                {"a_hi", "read_write", "f32"},
+                {"a_lo", "read_write", "f32"},
+                {"w", "read", "f32"},
+                {"c", "write", "f32"}},
+               {dim("M", 1, 1048576), dim("N", 1, 1048576), dim("K", 32, 1048576, 32), u32("ldc")},
+               l_gemm_tf32x3w});
   t.push_back({"argmax_pairs",
                1024,
                {{"x", "read", "f32"}, {"pairs", "write", "u32"}},

@@ -97,13 +97,19 @@ std::vector<Launch> prefill_launches(const LlamaLaunchDesc& d, const PrefillDesc
     }
   if (!have_eps) throw Refusal("prefill: the decode step normalizes nothing.");
 
-  // The TF32 halves are f32 arenas laid out as the weight arena.
+  // f32 weights: the GEMM reads them from the weight arena and splits them
+  // into their TF32 halves itself (gemm_tf32x3w). 16-bit weights: their
+  // widened halves are f32 arenas laid out as the weight arena (the low
+  // half 0), read by gemm_tf32x3.
   const uint64_t wb = s.weight_bytes();
+  const bool f32w = wb == 4;
   auto hi = [&](uint64_t w) { return p.w_hi + (w - d.arena) * 4 / wb; };
   auto lo = [&](uint64_t w) { return p.w_lo + (w - d.arena) * 4 / wb; };
   auto gemm = [&](uint64_t a, uint64_t K, uint64_t w, uint64_t N, uint64_t c, uint64_t ldc) {
-    return make("gemm_tf32x3", {{"M", (double)m}, {"N", (double)N}, {"K", (double)K}, {"ldc", (double)ldc}},
-                {a, p.a_hi, p.a_lo, hi(w), lo(w), c});
+    const std::vector<std::pair<std::string, double>> prm = {
+        {"M", (double)m}, {"N", (double)N}, {"K", (double)K}, {"ldc", (double)ldc}};
+    if (f32w) return make("gemm_tf32x3w", prm, {a, p.a_hi, p.a_lo, w, c});
+    return make("gemm_tf32x3", prm, {a, p.a_hi, p.a_lo, hi(w), lo(w), c});
   };
   const double md = (double)m;
 

@@ -1,5 +1,5 @@
 """Prompt prefill for the Llama engine: every prompt row through the layers
-at once, the projections as tcgen05 3xTF32 GEMMs (`gemm_tf32x3`), which
+at once, the projections as tcgen05 3xTF32 GEMMs (`gemm_tf32x3w`), which
 store each row's keys and values in the Ring caches; then the engine's
 decode step continues from the last prompt row.
 
@@ -21,8 +21,10 @@ run over R rows with the linears as tiles instead of GEMVs:
 The GEMMs are 3xTF32 (a_hi b_hi + a_hi b_lo + a_lo b_hi, f32 accumulation
 in TMEM), so prefill agrees with the binary32 contract within the f64
 evaluator's bounds, not bit for bit; the decode steps after it are the
-contract's bits given the caches prefill left. The weights' TF32 halves
-are split once, into two arenas laid out as the weight arena.
+contract's bits given the caches prefill left. f32 weights are read from
+the weight arena and split into their TF32 halves inside the GEMM
+(`gemm_tf32x3w`); 16-bit weights are widened once into two arenas laid out
+as the weight arena (`gemm_tf32x3`).
 
 With tensor parallelism each rank runs its shard's GEMMs; the row-parallel
 partials (o, down) are summed by an NCCL allreduce before the residual add.
@@ -50,16 +52,20 @@ class Prefill:
         for what, k in (("d_model", d), ("q width", qw), ("ffn", f)):
             if k % 32:
                 raise N.Refused(N.FKC_ERR_ARGUMENT, f"prefill: the GEMM's K ({what} {k}) is not a multiple of 32.")
-        # The layers' TF32 halves, laid out as the weight arena, a layer a
-        # launch.
-        # (16-bit weights: the widened weight is the high half, the low half 0.)
+        # f32 weights: the GEMMs read the weight arena and split each slab
+        # into its TF32 halves on the chip (gemm_tf32x3w). 16-bit weights:
+        # the widened weights (the high halves; the low halves 0) in two
+        # arenas laid out as the weight arena, a layer a launch.
         per = eng.layer_elems
-        self.w_hi = ctx.alloc(4 * s.layers * per)
-        self.w_lo = ctx.alloc(4 * s.layers * per)
-        split = "split_tf32" + WEIGHT_SUFFIX[eng.s.weights]
-        for l in range(s.layers):
-            at = 4 * l * per
-            ctx.launch(split, {"n": per}, [eng.arena.ptr + eng.wb * l * per, self.w_hi.ptr + at, self.w_lo.ptr + at])
+        self.w_hi = self.w_lo = None
+        if eng.wb != 4:
+            self.w_hi = ctx.alloc(4 * s.layers * per)
+            self.w_lo = ctx.alloc(4 * s.layers * per)
+            split = "split_tf32" + WEIGHT_SUFFIX[eng.s.weights]
+            for l in range(s.layers):
+                at = 4 * l * per
+                ctx.launch(split, {"n": per},
+                           [eng.arena.ptr + eng.wb * l * per, self.w_hi.ptr + at, self.w_lo.ptr + at])
         R = rows
         kmax = max(d, qw, f)
         # Tokens, positions, then each row's slot or (paged) block table.
@@ -107,8 +113,10 @@ class Prefill:
         return self.w_lo.ptr + (ptr - self.eng.arena.ptr) * 4 // self.eng.wb
 
     def _gemm(self, a, K: int, w: int, N: int, c, ldc: int) -> Launch:
-        return Launch("gemm_tf32x3", {"M": self.m, "N": N, "K": K, "ldc": ldc},
-                      [a, self.a_hi.ptr, self.a_lo.ptr, self._hi(w), self._lo(w), c])
+        params = {"M": self.m, "N": N, "K": K, "ldc": ldc}
+        if self.w_hi is None:
+            return Launch("gemm_tf32x3w", params, [a, self.a_hi.ptr, self.a_lo.ptr, w, c])
+        return Launch("gemm_tf32x3", params, [a, self.a_hi.ptr, self.a_lo.ptr, self._hi(w), self._lo(w), c])
 
     def launches(self, m: int) -> list:
         """The launch list over the first m rows of the row buffers, from
@@ -118,8 +126,9 @@ class Prefill:
         if not 1 <= m <= self.R:
             raise N.Refused(N.FKC_ERR_ARGUMENT, f"prefill: {m} rows, outside 1..{self.R}.")
         self.m = m
-        addrs = {n: getattr(self, n).ptr for n in ("w_hi", "w_lo", "x", "a", "a_hi", "a_lo", "qkv", "att", "tmp",
-                                                   "x1", "gu", "act")}
+        addrs = {n: getattr(self, n).ptr for n in ("x", "a", "a_hi", "a_lo", "qkv", "att", "tmp", "x1", "gu", "act")}
+        addrs.update(w_hi=self.w_hi.ptr if self.w_hi is not None else 0,
+                     w_lo=self.w_lo.ptr if self.w_lo is not None else 0)
         rs4 = 4 * self.rs
         addrs.update(tokens=self.rows_buf.ptr, pos=self.rows_buf.ptr + rs4, slot=self.rows_buf.ptr + 2 * rs4,
                      part=[b.ptr for b in self.part])
@@ -302,8 +311,9 @@ class Prefill:
         for g in self.graphs.values():
             g.destroy()
         self.graphs = {}
-        for b in [self.w_hi, self.w_lo, self.rows_buf, self.x, self.a, self.a_hi, self.a_lo, self.qkv, self.att,
-                  self.tmp, self.x1, self.gu, self.act] + self.part + list(self.moe.values()):
+        bufs = [self.rows_buf, self.x, self.a, self.a_hi, self.a_lo, self.qkv, self.att, self.tmp, self.x1, self.gu,
+                self.act] + self.part + list(self.moe.values())
+        for b in bufs + [b for b in (self.w_hi, self.w_lo) if b is not None]:
             b.free()
         self.moe = {}
 

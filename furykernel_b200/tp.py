@@ -155,10 +155,13 @@ def bench_main(args, metric: str, prompt: int, prefill_fn, config_fn, length: in
         graph.launch()
     ctx.sync()
     eng.set_rows(tokens, np.full(b, prompt, np.uint32), slots)
-    dist.barrier()
-    ctx.sync()
+    # Rank 0's clock sampler starts (and settles) before the barrier, so
+    # that every rank's timed replays start together: a rank that starts
+    # late holds the others in their peer exchanges.
     clk = clocks_cls(local) if (clocks_cls is not None and rank == 0) else contextlib.nullcontext()
     with clk:
+        dist.barrier()
+        ctx.sync()
         ms = graph.time(0, args.steps)
     dist.barrier()
     ms = max_over_ranks(ms)

@@ -1,8 +1,11 @@
-"""The prefill GEMM on tcgen05 tensor cores (3xTF32) through the C ABI,
+"""The prefill GEMMs on tcgen05 tensor cores (3xTF32) through the C ABI,
 against the f64 evaluator: every element within its binary32 bound
 (dotA, src/FuryKernel/Program/Eval.hs:747-754) and the normwise relative
 error max|C - C64| / max|C64| <= 1e-4 (the path's GEMM tolerance). The
-tensor cores sum in their own order, so no bit comparison."""
+tensor cores sum in their own order, so no bit comparison with the CPU
+target; gemm_tf32x3w (W split inside the kernel, per-shape tile widths)
+is held to those bounds and to gemm_tf32x3's bits (the same products in
+the same order)."""
 
 import numpy as np
 import pytest
@@ -52,3 +55,37 @@ def test_gemm_tf32x3_within_bounds(ctx, M, N, K):
     rows = np.arange(0, M, max(1, M // 4))[:4]  # the referee's bounds on a sample of rows
     ref = O.r_linear(w, O.r_input(a[rows]))
     assert O.within(c[rows], ref).all()
+
+
+def gemm_w(ctx, a, w):
+    M, K = a.shape
+    n = w.shape[0]
+    da, dw = ctx.to_device(a), ctx.to_device(w)
+    ahi, alo = ctx.empty((M, K)), ctx.empty((M, K))
+    dc = ctx.zeros((M, n))
+    ctx.launch("gemm_tf32x3w", {"M": M, "N": n, "K": K, "ldc": n}, [da, ahi, alo, dw, dc])
+    status = ctx.status()
+    c = dc.download()
+    for b in (da, dw, ahi, alo, dc):
+        b.free()
+    return c, status
+
+
+# Shapes whose tile widths (the launcher's pick on 148 SMs) are 16, 80, 112,
+# 144, 160 and 240: one 32-column piece to seven, with and without a
+# 16-column tail; ragged M and N; 2 to 6 ring stages.
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (129, 130, 96), (512, 2752, 256), (511, 4096, 128),
+                                   (640, 8192, 64), (512, 11008, 4096), (1024, 4096, 256)])
+def test_gemm_tf32x3w_within_bounds_and_as_split_kernel(ctx, M, N, K):
+    a = O.normal(5 + M, M * K).reshape(M, K)
+    w = O.normal(6 + N, N * K, 0.0, 0.02).reshape(N, K)
+    c, status = gemm_w(ctx, a, w)
+    assert status == 0
+    exact = a.astype(np.float64) @ w.astype(np.float64).T
+    assert np.max(np.abs(c - exact)) / np.max(np.abs(exact)) <= 1e-4
+    rows = np.arange(0, M, max(1, M // 4))[:4]
+    ref = O.r_linear(w, O.r_input(a[rows]))
+    assert O.within(c[rows], ref).all()
+    c0, status0, _, _ = gemm(ctx, a, w)
+    assert status0 == 0
+    assert np.array_equal(c.view(np.uint32), c0.view(np.uint32))

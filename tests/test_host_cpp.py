@@ -321,6 +321,8 @@ def fake_prefill(eng, rows, chunk=None, positions=None, one_slot=False):
     at = iter(range(1, 100))
     for name in ("w_hi", "w_lo", "rows_buf", "x", "a", "a_hi", "a_lo", "qkv", "att", "tmp", "x1", "gu", "act"):
         setattr(p, name, Buf((6 << 44) + (next(at) << 36)))
+    if eng.wb == 4:  # f32 weights: the GEMMs read the weight arena (no TF32 arenas)
+        p.w_hi = p.w_lo = None
     p.rs = (rows + 3) // 4 * 4
     p.chunk = chunk or eng.chunk
     p.positions = positions or s.positions
