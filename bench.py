@@ -576,7 +576,7 @@ def run_gemm(args):
             "data": "synthetic: A N(0,1), W N(0,0.02), seeded on the device",
             "config": {"workload": "config 3c prefill GEMM [512 x 4096] x [4096 x 11008]", "M": M, "K": K, "N": NN,
                        "parallelism": f"column split over {world}", "status": status, "kernel": kernel,
-                       "tile": f"128 x {tile_width(M, n, ctx.sms)}",
+                       "tile": f"{tile_rows(M, n, ctx.sms)} rows of A x 128 rows of W",
                        "l2": "inputs 8 + 180 MB per call (> L2 for the weights)"},
             "roofline": {"bound": "tensor", "achieved": 3 * tflops, "peak": tf32_peak, "unit": "TFLOP/s",
                          "frac": 3 * tflops / tf32_peak, "traffic": None, "peak_kind": kind,
@@ -591,12 +591,12 @@ def run_gemm(args):
         dist.destroy_process_group()
 
 
-def tile_width(M: int, N: int, sms: int) -> int:
-    """gemm_tf32x3w's tile width for M x N (the launcher's rule, restated):
-    among 16..256 by 16, the fewest rounds x (width + 24), the wider on a
-    tie."""
-    mt = (M + 127) // 128
-    return min(range(256, 15, -16), key=lambda tn: (-(-mt * -(-N // tn) // sms)) * (tn + 24))
+def tile_rows(M: int, N: int, sms: int) -> int:
+    """gemm_tf32x3w's A rows a tile (128 W rows each) for M x N (the
+    launcher's rule, restated): among 16..256 by 16, the fewest rounds x
+    (rows + 24), the wider on a tie."""
+    wt = (N + 127) // 128
+    return min(range(256, 15, -16), key=lambda tm: (-(-wt * -(-M // tm) // sms)) * (tm + 24))
 
 
 def gemm_cpu_baseline(M: int, K: int, N: int, rows: int = 4) -> dict:

@@ -3,9 +3,11 @@ against the f64 evaluator: every element within its binary32 bound
 (dotA, src/FuryKernel/Program/Eval.hs:747-754) and the normwise relative
 error max|C - C64| / max|C64| <= 1e-4 (the path's GEMM tolerance). The
 tensor cores sum in their own order, so no bit comparison with the CPU
-target; gemm_tf32x3w (W split inside the kernel, per-shape tile widths)
-is held to those bounds and to gemm_tf32x3's bits (the same products in
-the same order)."""
+target. gemm_tf32x3w (W split on the chip and held in tensor memory as the
+MMA's A operand, the tile transposed, per-shape tile widths) forms the same
+three products as gemm_tf32x3 from the same halves; it is held to the same
+bounds and to within 2^-20 of gemm_tf32x3's result (max |C - C0| /
+max |C0|), the tensor cores' accumulation order being theirs in both."""
 
 import numpy as np
 import pytest
@@ -71,11 +73,12 @@ def gemm_w(ctx, a, w):
     return c, status
 
 
-# Shapes whose tile widths (the launcher's pick on 148 SMs) are 16, 80, 112,
-# 144, 160 and 240: one 32-column piece to seven, with and without a
-# 16-column tail; ragged M and N; 2 to 6 ring stages.
+# Shapes whose tiles (128 W rows x tm A rows, the launcher's pick on 148
+# SMs) have tm 16, 96, 128, 160, 176 and 256: a 16-column accumulator to
+# eight 32-column pieces, with and without a 16-column tail; ragged M and
+# N; 3 and 4 ring stages.
 @pytest.mark.parametrize("M,N,K", [(128, 128, 64), (129, 130, 96), (512, 2752, 256), (511, 4096, 128),
-                                   (640, 8192, 64), (512, 11008, 4096), (1024, 4096, 256)])
+                                   (640, 8192, 64), (512, 11008, 4096), (1024, 4096, 256), (1536, 11008, 128)])
 def test_gemm_tf32x3w_within_bounds_and_as_split_kernel(ctx, M, N, K):
     a = O.normal(5 + M, M * K).reshape(M, K)
     w = O.normal(6 + N, N * K, 0.0, 0.02).reshape(N, K)
@@ -88,4 +91,4 @@ def test_gemm_tf32x3w_within_bounds_and_as_split_kernel(ctx, M, N, K):
     assert O.within(c[rows], ref).all()
     c0, status0, _, _ = gemm(ctx, a, w)
     assert status0 == 0
-    assert np.array_equal(c.view(np.uint32), c0.view(np.uint32))
+    assert np.max(np.abs(c.astype(np.float64) - c0)) <= np.max(np.abs(c0)) * 2.0 ** -20
