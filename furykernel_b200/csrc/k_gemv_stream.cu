@@ -23,8 +23,9 @@
 // Tensor parallelism (fk_peers.cuh): the row-parallel projections scatter
 // their partial rows into every rank's exchange region (SEPI_SCATTER: a
 // block owns a contiguous run of rows, stages them in shared memory, writes
-// the run into this rank's slot of every region and counts its rows in with
-// a release add a rank); the
+// the run into this rank's slot of every region and counts itself in; the
+// launch's last block publishes all rows to every rank with one
+// system-scope fence); the
 // next GEMV's prologue (SPRO_REDUCE_RMSNORM) waits for every rank's rows,
 // forms the residual row x_new = r + (((P_0 + P_1) + P_2) + ...), ranks in
 // order, so that every rank holds the same bits, stores it (block 0), and
@@ -246,7 +247,7 @@ __global__ void __launch_bounds__(512, 2) gemv_stream_kernel(StreamArgs a) {
         dst[(size_t)i * a.n + s_lo + j] = outs[i][j];
       }
     }
-    peers_count_rows(a.peers, a.xbuf, cnt);
+    peers_count_rows(a.peers, a.xbuf, units);
   }
 }
 

@@ -259,7 +259,7 @@ __global__ void __launch_bounds__(512, 2) gemv_stream_w16_kernel(StreamArgs a) {
         dst[(size_t)i * a.n + s_lo + j] = outs[i][j];
       }
     }
-    peers_count_rows(a.peers, a.xbuf, cnt);
+    peers_count_rows(a.peers, a.xbuf, units);
   }
 }
 
