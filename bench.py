@@ -387,7 +387,7 @@ def run_ours(args):
 
     from furykernel_b200 import _native as N
     from furykernel_b200.engine import Llama
-    from furykernel_b200.program.llama import LlamaShape
+    from furykernel_b200.shape import LlamaShape
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -652,7 +652,7 @@ def run_kernel_config(args):
 
     from furykernel_b200 import _native as N
     from furykernel_b200.engine import Launch, Llama
-    from furykernel_b200.program.llama import LlamaShape
+    from furykernel_b200.shape import LlamaShape
     from oracle import oracle as O
 
     torch.cuda.set_device(0)

@@ -1,7 +1,7 @@
 """ctypes binding of libfurykernel_host.so (include/furykernel_host.h): the
 programs, the planner and the lowering in C++. The Llama engine takes its
-launch list from here; the Python restatement in `program/` and `engine.py`
-is the same algorithm, kept as the checker the tests compare against."""
+launch list from here; the Python restatement under `tests/restated/` is the
+same algorithm, kept as the checker the tests compare against."""
 
 from __future__ import annotations
 
@@ -114,7 +114,7 @@ def _text(call, *args) -> str:
 
 
 def shape(s) -> Shape:
-    """A LlamaShape (program.llama) as the C struct."""
+    """A LlamaShape (furykernel_b200.shape) as the C struct."""
     for what, t in (("weights", s.weights), ("cache", s.cache)):
         if t not in ELEMENT_TYPES:
             raise N.Refused(N.FKC_ERR_ARGUMENT, f"the {what}' element type {t} is not f32, bf16 or f16.")

@@ -168,7 +168,7 @@ class Builder {
 
 // The Llama-shaped programs of this path (one decoder layer, the embedding,
 // the head): f32 activations; f32 or bf16 weights and KV caches
-// (furykernel_b200/program/llama.py states them too).
+// (tests/restated/llama.py states them too).
 struct LlamaShape {
   uint64_t d_model = 4096, heads = 32, kv_heads = 32, head_dim = 128, ffn = 11008, vocab = 32000, layers = 32;
   double theta = 10000.0, eps = 1e-5;

@@ -124,7 +124,7 @@ def main(argv=None) -> None:
     GEMV variants of config 5's decode step on GPU 0 and writes the selection."""
     import argparse
 
-    from .program.llama import LlamaShape
+    from .shape import LlamaShape
 
     ap = argparse.ArgumentParser(prog="python -m furykernel_b200.select")
     ap.add_argument("command", choices=["tune", "classes"])

@@ -137,7 +137,7 @@ def bench_main(args, metric: str, prompt: int, prefill_fn, config_fn, length: in
     import torch.distributed as dist
 
     from .engine import Llama
-    from .program.llama import LlamaShape
+    from .shape import LlamaShape
 
     ctx, rank, world, local = init()
     b = args.batch

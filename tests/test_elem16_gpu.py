@@ -188,7 +188,7 @@ def test_attend_prompt_kv16_matches_the_f32_form_over_widened_caches(ctx, t):
 
 
 def small_shape(batch, weights="bf16", cache="bf16"):
-    from furykernel_b200.program.llama import LlamaShape
+    from furykernel_b200.shape import LlamaShape
 
     return LlamaShape(d_model=512, heads=4, kv_heads=4, head_dim=128, ffn=1024, vocab=3000, layers=2, slots=batch,
                       length=96, positions=96, weights=weights, cache=cache)

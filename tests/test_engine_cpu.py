@@ -8,6 +8,7 @@ import numpy as np
 
 from furykernel_b200.engine import Launch, Llama
 from furykernel_b200.prefill import prompt_chunks, prompt_rows
+from tests.restated import lowering as RL
 
 
 def kv_launch(qkv=100, pos=200, slot=300, kc=400, vc=500, ldq=1536, rotated=64, length=96):
@@ -25,7 +26,7 @@ def attend_launch(qkv=100, pos=200, slot=300, kc=400, vc=500, ldq=1536, rotated=
 
 def test_fuse_attention_merges_a_store_and_its_attention():
     combine = Launch("attend_combine", {"m": 2}, [21, 22, 23, 200, 600])
-    out = Llama._fuse_attention(SimpleNamespace(), [Launch("gemv", {}, []), kv_launch(), attend_launch(), combine])
+    out = RL.fuse_attention(SimpleNamespace(), [Launch("gemv", {}, []), kv_launch(), attend_launch(), combine])
     assert [L.kernel for L in out] == ["gemv", "attend_decode", "attend_combine"]
     fused = out[1]
     assert fused.bufs == attend_launch().bufs
@@ -36,7 +37,7 @@ def test_fuse_attention_merges_a_store_and_its_attention():
 def test_fuse_attention_leaves_mismatched_launches():
     for kw in ({"qkv": 101}, {"slot": 301}, {"kc": 401}, {"ldq": 1540}, {"rotated": 32}, {"length": 64}):
         launches = [kv_launch(**kw), attend_launch()]
-        out = Llama._fuse_attention(SimpleNamespace(), launches)
+        out = RL.fuse_attention(SimpleNamespace(), launches)
         assert [L.kernel for L in out] == ["kv_store_ring", "attend_split"], kw
 
 

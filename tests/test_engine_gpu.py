@@ -22,7 +22,7 @@ def ctx():
 
 
 def small_shape(batch, layers=2, d=512, heads=4, ffn=1024, vocab=3000, length=96):
-    from furykernel_b200.program.llama import LlamaShape
+    from furykernel_b200.shape import LlamaShape
 
     return LlamaShape(d_model=d, heads=heads, kv_heads=heads, head_dim=128, ffn=ffn, vocab=vocab, layers=layers,
                       slots=batch, length=length, positions=length)

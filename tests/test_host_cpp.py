@@ -16,10 +16,13 @@ import pytest
 from furykernel_b200 import _host as H
 from furykernel_b200 import _native as N
 from furykernel_b200.engine import Llama
-from furykernel_b200.program import plan as PL
-from furykernel_b200.program.build import program
-from furykernel_b200.program.graph import render_program, whole_row
-from furykernel_b200.program.llama import LlamaShape, embed_program, head_program, layer_program
+from furykernel_b200.shape import LlamaShape
+from tests.restated import lowering as RL
+from tests.restated import plan as PL
+from tests.restated import prefill as RP
+from tests.restated.build import program
+from tests.restated.graph import render_program, whole_row
+from tests.restated.llama import embed_program, head_program, layer_program
 
 from tests.test_program import LAYER_PLAN, OPTION_SETS, two_tiles
 from tests.test_program import head_program as golden_head
@@ -126,7 +129,7 @@ def test_text_entry_reports_the_size_it_needs():
 
 
 def test_split_for_alike():
-    from furykernel_b200.engine import split_for
+    from tests.restated.lowering import split_for
 
     for n in (1, 512, 4096, 12288, 22016, 32000):
         for k in (64, 1024, 4096, 11008):
@@ -157,12 +160,6 @@ def fake_engine(full, batch, rank=0, world=1, peer_exchange=True, fuse_attention
     e.gate_up_interleaved = batch <= 64
     e.peer_exchange = world > 1 and batch <= 4 and peer_exchange and not s.experts
     e.vocab_local = full.vocab // world
-    e.plans = {
-        "embed": PL.plan(PL.DEFAULT, embed_program(full)),
-        "layer": PL.plan(PL.PlanOptions(gated=gated, store_gelus=store_gelus,
-                                        sequence_rows=batch if s.slots == 1 else 1), layer_program(s)),
-        "head": PL.plan(PL.DEFAULT, head_program(dataclasses.replace(full, vocab=e.vocab_local))),
-    }
     e.gated, e.store_gelus = gated, store_gelus
     d, qw, kvw, f = s.d_model, s.q_width, s.kv_width, s.ffn
     e.layer_elems = sum(e.layer_sizes())
@@ -259,7 +256,7 @@ CASES = (
 def test_decode_launches_alike(case):
     full, batch, rank, world, peer, fuse = CASES[case]
     e = fake_engine(full, batch, rank, world, peer, fuse)
-    want = e._launches_restated()
+    want = RL.decode_launches(e)
     got = e._launches()
     assert [L.kernel for L in got] == [L.kernel for L in want]
     for g, w in zip(got, want):
@@ -281,7 +278,7 @@ GATED_CASES = [(dataclasses.replace(small(b), experts=8, top_k=2, weights=w), b,
 def test_gated_plans_launch_alike(case):
     full, batch, gated, store_gelus = GATED_CASES[case]
     e = fake_engine(full, batch, gated=gated, store_gelus=store_gelus)
-    want = e._launches_restated()
+    want = RL.decode_launches(e)
     got = e._launches()
     assert [L.kernel for L in got] == [L.kernel for L in want]
     for g, w in zip(got, want):
@@ -298,7 +295,7 @@ def test_unlowerable_steps_are_refused_alike():
                       positions=16)
     e = fake_engine(full, 8)
     with pytest.raises(N.Refused):
-        e._launches_restated()
+        RL.decode_launches(e)
     with pytest.raises(N.Refused, match="no kernel runs"):
         e._launches()
 
@@ -375,11 +372,11 @@ PREFILL_CASES = (
 def test_prefill_launches_alike(case):
     full, batch, rank, world, peer, rows, one_slot, m = PREFILL_CASES[case]
     e = fake_engine(full, batch, rank, world, peer)
-    e.launches = e._launches_restated()
+    e.launches = RL.decode_launches(e)
     # as the bench sizes it: positions up to the prompt's rows
     p = fake_prefill(e, rows, positions=rows if rows == 512 else None, one_slot=one_slot)
     assert p.one_slot == one_slot
-    want = p._launches_restated(m)
+    want = RP.prefill_launches(p, m)
     got = p.launches(m)
     assert [L.kernel for L in got] == [L.kernel for L in want]
     for g, w in zip(got, want):
@@ -389,7 +386,7 @@ def test_prefill_launches_alike(case):
 
 def test_prefill_rows_are_bounded():
     e = fake_engine(small(1), 1)
-    e.launches = e._launches_restated()
+    e.launches = RL.decode_launches(e)
     p = fake_prefill(e, 16)
     for m in (0, 17):
         with pytest.raises(N.Refused, match="outside 1..16"):
@@ -425,12 +422,12 @@ MIXED_CASES = [
 def test_mixed_options_launch_alike(case):
     full, batch, rank, world, peer, gated, store_gelus = MIXED_CASES[case]
     e = fake_engine(full, batch, rank, world, peer, gated=gated, store_gelus=store_gelus)
-    want, got = e._launches_restated(), e._launches()
+    want, got = RL.decode_launches(e), e._launches()
     assert [L.kernel for L in got] == [L.kernel for L in want]
     for g, w in zip(got, want):
         assert g.bufs == w.bufs and g.params == w.params, (g.kernel, g.params, w.params)
     e.launches = got
     if world == 1:  # and the prefill over the same engine
         p = fake_prefill(e, 64)
-        pw, pg = p._launches_restated(40), p.launches(40)
+        pw, pg = RP.prefill_launches(p, 40), p.launches(40)
         assert [(L.kernel, L.params, L.bufs) for L in pg] == [(L.kernel, L.params, L.bufs) for L in pw]

@@ -3,10 +3,11 @@ are stand-ins; nothing runs)."""
 
 import pytest
 
-from furykernel_b200 import engine as E
+from tests.restated import lowering as E
 from furykernel_b200 import target as T
-from furykernel_b200.program import plan as PL
-from furykernel_b200.program.llama import LlamaShape, embed_program, head_program, layer_program
+from tests.restated import plan as PL
+from furykernel_b200.shape import LlamaShape
+from tests.restated.llama import embed_program, head_program, layer_program
 
 
 def fake_binding(s, m):

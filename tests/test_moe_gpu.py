@@ -113,7 +113,7 @@ def test_moe_model_decode_step(ctx, batch, experts, top_k, weights, gated, store
     rows, bit for bit -- with the default plan, and with the route and the
     gate in steps of their own (optGated, optStoreGelus)."""
     from furykernel_b200.engine import Llama
-    from furykernel_b200.program.llama import LlamaShape
+    from furykernel_b200.shape import LlamaShape
 
     scaled = gated == "scale"  # the route's expert scales, the default plan
     gated = gated is True
@@ -142,7 +142,7 @@ def test_moe_prefill(ctx, weights, one_slot):
     the decode step from the caches prefill left is the oracle's too."""
     from furykernel_b200.engine import Llama
     from furykernel_b200.prefill import Prefill, prompt_chunks
-    from furykernel_b200.program.llama import LlamaShape
+    from furykernel_b200.shape import LlamaShape
 
     batch = 2
     s = LlamaShape(d_model=512, heads=4, kv_heads=4, head_dim=128, ffn=256, vocab=3000, layers=2, slots=batch,

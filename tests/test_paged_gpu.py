@@ -172,7 +172,7 @@ def test_paged_model_decode_step(ctx, batch, cache):
     against the oracle's decode over the rows' blocks: the same ids, logits
     and residual rows, bit for bit, and the same pools."""
     from furykernel_b200.engine import Llama
-    from furykernel_b200.program.llama import LlamaShape
+    from furykernel_b200.shape import LlamaShape
 
     s = LlamaShape(d_model=512, heads=4, kv_heads=4, head_dim=128, ffn=1024, vocab=3000, layers=2, positions=96,
                    blocks=6 * batch + 5, block_size=16, cache=cache)
@@ -199,7 +199,7 @@ def test_paged_prefill_then_decode(ctx, cache, one_slot):
     prefill left: the oracle's ids and logits, bit for bit."""
     from furykernel_b200.engine import Llama
     from furykernel_b200.prefill import Prefill, prompt_chunks
-    from furykernel_b200.program.llama import LlamaShape
+    from furykernel_b200.shape import LlamaShape
 
     batch = 2
     s = LlamaShape(d_model=512, heads=4, kv_heads=4, head_dim=128, ffn=1024, vocab=3000, layers=2, positions=96,

@@ -115,7 +115,7 @@ def test_attention_over_prompt_rows(ctx):
 def test_prefill_then_decode(ctx, batch, one_slot):
     from furykernel_b200.engine import Llama
     from furykernel_b200.prefill import Prefill
-    from furykernel_b200.program.llama import LlamaShape
+    from furykernel_b200.shape import LlamaShape
 
     s = LlamaShape(d_model=512, heads=4, kv_heads=4, head_dim=128, ffn=1024, vocab=3000, layers=2, slots=batch,
                    length=96, positions=96)

@@ -5,9 +5,9 @@ import math
 
 import pytest
 
-from furykernel_b200.program import plan as PL
-from furykernel_b200.program.build import program
-from furykernel_b200.program.graph import AttendTo, AttnSpec, Ring, RopeSpec, StoreAt, whole_row
+from tests.restated import plan as PL
+from tests.restated.build import program
+from tests.restated.graph import AttendTo, AttnSpec, Ring, RopeSpec, StoreAt, whole_row
 
 
 def layer(k_eq_v: bool):
@@ -254,7 +254,7 @@ def test_forty_doublings_planned_once():
 
 def test_render_program_golden():
     # ProgramTest.hs:116-125.
-    from furykernel_b200.program.graph import render_program
+    from tests.restated.graph import render_program
 
     b = program("small")
     x = b.input("x", whole_row(4))
@@ -309,7 +309,7 @@ def embed_program():
 
 def names_both(prog, opts):
     from furykernel_b200 import _host as H
-    from furykernel_b200.program.graph import render_program
+    from tests.restated.graph import render_program
 
     py = [s.name for s in PL.plan(opts, prog).steps]
     text = H.plan_text(render_program(prog), opts.horizontal, opts.gated, opts.store_gelus, opts.sequence_rows)
@@ -337,7 +337,7 @@ def test_stored_gelus_and_gated_routes():
 
 def test_gated_a_route_the_program_outputs_is_stored_beside_the_experts_route():
     from furykernel_b200 import _host as H
-    from furykernel_b200.program.graph import render_program
+    from tests.restated.graph import render_program
 
     want = [
         "plan predicting",
@@ -373,7 +373,7 @@ def test_gated_a_route_the_program_outputs_is_stored_beside_the_experts_route():
 
 def test_the_embedding_one_light_step():
     from furykernel_b200 import _host as H
-    from furykernel_b200.program.graph import render_program
+    from tests.restated.graph import render_program
 
     want = ["plan embed", "  step s0_x", "    recompute x", "    stores x f32"]
     assert PL.render_plan(PL.plan(PL.DEFAULT, embed_program())).splitlines() == want

@@ -11,6 +11,7 @@ import pytest
 
 from furykernel_b200 import _host as H
 from furykernel_b200 import _native as N
+from tests.restated import lowering as RL
 
 # ---------------------------------------------------------------------------
 # JSON (JsonTest.hs)
@@ -298,7 +299,7 @@ def test_everything_else_validation_refuses():
 
 def test_the_engine_takes_each_shape_s_split_from_a_selection():
     from furykernel_b200 import select
-    from furykernel_b200.program.llama import LlamaShape
+    from furykernel_b200.shape import LlamaShape
     from tests.test_host_cpp import fake_engine
 
     s = LlamaShape(layers=2, slots=1, length=4096, positions=4096)
@@ -310,7 +311,7 @@ def test_the_engine_takes_each_shape_s_split_from_a_selection():
     text = H.gemv_selection_render(classes, picks, 148)
     e.splits = select.splits_for(e, text)
     assert e.splits == {(n, k): p for (n, k, _), p in zip(classes, picks)}
-    got, want = e._launches(), e._launches_restated()
+    got, want = e._launches(), RL.decode_launches(e)
     assert [(L.kernel, L.params, L.bufs) for L in got] == [(L.kernel, L.params, L.bufs) for L in want]
     assert {(L.params["n"], L.params["k"]): L.params["split"] for L in got if L.kernel.startswith("gemv")} == \
         e.splits
@@ -318,7 +319,7 @@ def test_the_engine_takes_each_shape_s_split_from_a_selection():
 
 def test_a_selection_for_other_classes_is_refused():
     from furykernel_b200 import select
-    from furykernel_b200.program.llama import LlamaShape
+    from furykernel_b200.shape import LlamaShape
     from tests.test_host_cpp import fake_engine
 
     e = fake_engine(LlamaShape(layers=1, slots=4, length=64, positions=64), 4)
@@ -328,7 +329,7 @@ def test_a_selection_for_other_classes_is_refused():
 
 
 def test_row_pair_kernels_take_split_one_past_batch_four():
-    from furykernel_b200.program.llama import LlamaShape
+    from furykernel_b200.shape import LlamaShape
     from tests.test_host_cpp import fake_engine
 
     e = fake_engine(LlamaShape(layers=1, slots=8, length=64, positions=64), 8)
@@ -336,7 +337,7 @@ def test_row_pair_kernels_take_split_one_past_batch_four():
     with pytest.raises(N.Refused, match="row-pair kernels take split 1 past batch 4, not 2"):
         e._launches()
     with pytest.raises(N.Refused, match="row-pair kernels take split 1 past batch 4, not 2"):
-        e._launches_restated()
+        RL.decode_launches(e)
 
 
 def test_tuning_picks_the_split_fastest_over_every_batch():

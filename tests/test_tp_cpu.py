@@ -14,7 +14,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from furykernel_b200.engine import shard_weights
-from furykernel_b200.program.llama import LlamaShape
+from furykernel_b200.shape import LlamaShape
 
 S = LlamaShape(d_model=64, heads=4, kv_heads=2, head_dim=8, ffn=48, vocab=40, layers=2, slots=1, length=16,
                positions=16)

@@ -43,7 +43,7 @@ def model(s):
 def shape(batch=2, moe=False):
     """The test model: 8 heads, so that it shards over 2, 4 or 8 ranks; with
     `moe`, its FFN routed experts (the top 2 of 8, ffn 256 each)."""
-    from furykernel_b200.program.llama import LlamaShape
+    from furykernel_b200.shape import LlamaShape
 
     if moe:
         return LlamaShape(d_model=512, heads=8, kv_heads=8, head_dim=128, ffn=256, vocab=3000, layers=2,
