@@ -170,6 +170,9 @@ def parse_abi(text: str):
             continue
         if w[0] == "buffer":
             bufs.append(BufferBinding(w[1], w[2], w[3], int(w[5])))
+        elif w[0] == "table":  # bound after the buffers; a read-only table's line names no access
+            access = "read" if len(w) == 5 else w[2]
+            bufs.append(BufferBinding(w[1], access, w[-3], int(w[-1])))
         elif w[0] == "param":
             params.append(ParamField(w[1], w[2], int(w[4])))
     return bufs, params
@@ -355,7 +358,8 @@ class Context:
                 DeviceBuffer(self, s.value, n, np.float32, (positions, rotated)))
 
     def launch(self, kernel: str, params: dict, bufs: list) -> None:
-        """Launches a table entry: params by name, buffers in declaration order."""
+        """Launches a table entry: params by name, buffers in declaration
+        order, then its tables (device addresses of arrays of addresses)."""
         e = table().get(kernel)
         if e is None:
             raise Refused(FKC_ERR_ARGUMENT, f"The target has no kernel {kernel}.")

@@ -1,11 +1,12 @@
 // Attention over paged KV caches (Paged blocks blockSize kvHeads headDim,
-// src/FuryKernel/Program/Graph.hs:144-152): each layer's keys and values
-// live in a pool of blocks of `block_size` positions, and each row lists its
-// sequence's blocks in a block table of `table_len` u32 entries. Position p,
-// KV head h of a row is at element (h * block_size + p mod block_size) * d
-// of block table[p / block_size] (cacheIndex, src/FuryKernel/Program/
-// Eval.hs:592-602); the pool holds its blocks back to back, so block b
-// starts at element b * kv_heads * block_size * d.
+// src/FuryKernel/Program/Graph.hs:144-152): a cache is `blocks` blocks of
+// `block_size` positions, each an array of its own wherever the engine
+// allocated it, reached through a table of the blocks' addresses (the
+// launch's k_cache and v_cache tables: u64 entries, IR.hs:400-429); each
+// row lists its sequence's blocks by index in a block table of `table_len`
+// u32 entries. Position p, KV head h of a row is at element
+// (h * block_size + p mod block_size) * d of block table[p / block_size]
+// (cacheIndex, src/FuryKernel/Program/Eval.hs:592-602).
 //
 // Arithmetic: the ring kernels' (k_attend.cu), position for position -- the
 // KV store rotates each key and stores it and the value at the row's
@@ -17,9 +18,11 @@
 // bf16 or f16 (stores rounded to the cache's type, nearest even, reads
 // widened: Eval.hs:9; the type a tag, fk_elem16.cuh).
 //
-// A table entry at or past the pool's `blocks` is not read or written: its
-// keys and values read as 0 and its stores are dropped (the engine checks
-// the tables it uploads; this keeps a bad entry from reaching past the pool).
+// A block-table entry at or past `blocks` is not read or written: its keys
+// and values read as 0 and its stores are dropped (the engine checks the
+// tables it uploads; this keeps a bad entry from reaching past the address
+// tables). The addresses themselves are the caller's: each must point at a
+// block of kv_heads * block_size * d elements of the cache's type.
 #include "fk_common.cuh"
 #include "fk_elem16.cuh"
 #include "fk_kernels.h"
@@ -77,27 +80,35 @@ __device__ __forceinline__ void rope2(const float* __restrict__ src, uint32_t i,
 }
 
 struct Pool {
-  const uint32_t* table;  // [m, table_len]
+  const uint32_t* table;  // [m, table_len] each row's blocks, by index
+  const uint64_t* kblk;   // [blocks] each block's address: keys
+  const uint64_t* vblk;   // and values
   uint32_t block_size, table_len, blocks;
 };
 
-// The element index of (row r, position t, KV head h, element 0), or
-// UINT64_MAX where the row's table has no block there.
+// Where (row r, position t, KV head h, element 0) is: the block's index in
+// the high word, the element within the block in the low word; UINT64_MAX
+// where the row's table has no block there.
 __device__ __forceinline__ uint64_t at_of(const Pool& P, uint32_t r, uint32_t t, uint32_t h, uint32_t kv_heads,
                                           uint32_t d) {
   const uint32_t slot = t / P.block_size;
   if (slot >= P.table_len) return ~0ull;
   const uint32_t block = __ldg(P.table + (size_t)r * P.table_len + slot);
   if (block >= P.blocks) return ~0ull;
-  return (((uint64_t)block * kv_heads + h) * P.block_size + t % P.block_size) * d;
+  return ((uint64_t)block << 32) | ((h * P.block_size + t % P.block_size) * d);
+}
+
+// The element `at` (from at_of) of a cache through its blocks' addresses.
+template <class E>
+__device__ __forceinline__ St<E>* elem_at(const uint64_t* blk, uint64_t at) {
+  return reinterpret_cast<St<E>*>(__ldg(reinterpret_cast<const unsigned long long*>(blk) + (at >> 32))) +
+         (uint32_t)at;
 }
 
 template <class E>
 struct StoreArgs {
   FkKvStore a;  // a.slot, a.kc, a.vc, a.length unused
   Pool P;
-  St<E>* kc;
-  St<E>* vc;
 };
 
 // The KV store step: grid (kv_heads, m), d / 2 threads.
@@ -114,21 +125,19 @@ __global__ void kv_store_paged_kernel(StoreArgs<E> s) {
   const float* vrow = a.qkv + (size_t)r * a.ldq + a.v_off + (size_t)h * a.d;
   float lo, hi;
   rope2(krow, i, half, a.rotated, a.cos_t + (size_t)p * a.rotated, a.sin_t + (size_t)p * a.rotated, lo, hi);
-  st_elem<E>(s.kc + at + i, lo);
-  st_elem<E>(s.kc + at + i + half, hi);
-  st_elem<E>(s.vc + at + i, vrow[i]);
-  st_elem<E>(s.vc + at + i + half, vrow[i + half]);
+  St<E>* kp = elem_at<E>(s.P.kblk, at);
+  St<E>* vp = elem_at<E>(s.P.vblk, at);
+  st_elem<E>(kp + i, lo);
+  st_elem<E>(kp + i + half, hi);
+  st_elem<E>(vp + i, vrow[i]);
+  st_elem<E>(vp + i + half, vrow[i + half]);
 }
 
 template <class E>
 struct AttendArgs {
   FkAttend a;  // a.slot, a.kc, a.vc, a.length unused
   Pool P;
-  const St<E>* kc;
-  const St<E>* vc;
   uint32_t k_off, v_off;  // FUSED: the new key's and value's columns in a qkv row
-  St<E>* kc_w;            // FUSED: the caches, written
-  St<E>* vc_w;
 };
 
 // A value as a cache of type E holds it.
@@ -207,8 +216,8 @@ __global__ void __launch_bounds__(128, 4) attend_paged_kernel(AttendArgs<E> f) {
     for (int u = 0; u < B; ++u) {
       const uint32_t tt = t0 + warp + u * kAttWarps;
       const uint64_t at = tt < t1 ? at_of(f.P, r, tt, kvh, a.kv_heads, kHeadDim) : ~0ull;
-      kv[u] = at != ~0ull ? ld_pack<E>(f.kc + at + 4 * lane) : zero4;
-      vv[u] = at != ~0ull ? ld_pack<E>(f.vc + at + 4 * lane) : zero4;
+      kv[u] = at != ~0ull ? ld_pack<E>(elem_at<E>(f.P.kblk, at) + 4 * lane) : zero4;
+      vv[u] = at != ~0ull ? ld_pack<E>(elem_at<E>(f.P.vblk, at) + 4 * lane) : zero4;
     }
     if (!waited) {
       grid_wait();
@@ -241,8 +250,8 @@ __global__ void __launch_bounds__(128, 4) attend_paged_kernel(AttendArgs<E> f) {
     if (fresh && h % group == 0) {  // the KV store, once a (row, KV head)
       const uint64_t at = at_of(f.P, r, p, kvh, a.kv_heads, kHeadDim);
       if (at != ~0ull) {
-        st_elem<E>(f.kc_w + at + threadIdx.x, krot[threadIdx.x]);
-        st_elem<E>(f.vc_w + at + threadIdx.x, vnew[threadIdx.x]);
+        st_elem<E>(elem_at<E>(f.P.kblk, at) + threadIdx.x, krot[threadIdx.x]);
+        st_elem<E>(elem_at<E>(f.P.vblk, at) + threadIdx.x, vnew[threadIdx.x]);
       }
     }
     const float4 qv = reinterpret_cast<const float4*>(qrot)[lane];
@@ -253,7 +262,7 @@ __global__ void __launch_bounds__(128, 4) attend_paged_kernel(AttendArgs<E> f) {
         for (int u = 0; u < B; ++u) {
           const uint32_t tt = t + u * kAttWarps;
           const uint64_t at = tt < t1 ? at_of(f.P, r, tt, kvh, a.kv_heads, kHeadDim) : ~0ull;
-          kv[u] = at != ~0ull ? ld_pack<E>(f.kc + at + 4 * lane) : zero4;
+          kv[u] = at != ~0ull ? ld_pack<E>(elem_at<E>(f.P.kblk, at) + 4 * lane) : zero4;
         }
       }
 #pragma unroll
@@ -278,7 +287,7 @@ __global__ void __launch_bounds__(128, 4) attend_paged_kernel(AttendArgs<E> f) {
         for (int u = 0; u < B; ++u) {
           const uint32_t tt = t + u * kAttWarps;
           const uint64_t at = tt < t1 ? at_of(f.P, r, tt, kvh, a.kv_heads, kHeadDim) : ~0ull;
-          vv[u] = at != ~0ull ? ld_pack<E>(f.vc + at + 4 * lane) : zero4;
+          vv[u] = at != ~0ull ? ld_pack<E>(elem_at<E>(f.P.vblk, at) + 4 * lane) : zero4;
         }
       }
       const uint32_t g0 = t - (uint32_t)warp - t0;
@@ -363,7 +372,7 @@ __global__ void __launch_bounds__(128) attend_prompt_paged_kernel(AttendArgs<E> 
     for (uint32_t e = threadIdx.x; e < kPromptTile * kHeadDim; e += blockDim.x) {
       const uint32_t k = e / kHeadDim, dd = e % kHeadDim;
       const uint64_t at = t0 + k < keys ? at_of(f.P, 0, t0 + k, kvh, a.kv_heads, kHeadDim) : ~0ull;
-      kt[dd * kPromptTile + k] = at != ~0ull ? ld_elem<E>(f.kc + at + dd) : 0.0f;
+      kt[dd * kPromptTile + k] = at != ~0ull ? ld_elem<E>(elem_at<E>(f.P.kblk, at) + dd) : 0.0f;
     }
     __syncthreads();
 #pragma unroll
@@ -398,7 +407,7 @@ __global__ void __launch_bounds__(128) attend_prompt_paged_kernel(AttendArgs<E> 
     for (uint32_t e = threadIdx.x; e < kPromptTile * kHeadDim; e += blockDim.x) {
       const uint32_t k = e / kHeadDim, dd = e % kHeadDim;
       const uint64_t at = t0 + k < keys ? at_of(f.P, 0, t0 + k, kvh, a.kv_heads, kHeadDim) : ~0ull;
-      vt[e] = at != ~0ull ? ld_elem<E>(f.vc + at + dd) : 0.0f;
+      vt[e] = at != ~0ull ? ld_elem<E>(elem_at<E>(f.P.vblk, at) + dd) : 0.0f;
     }
     __syncthreads();
 #pragma unroll
@@ -435,11 +444,11 @@ cudaError_t launch_store(const FkKvStore& a, const FkPaged& pg, void* kc, void* 
   if (a.m == 0) return cudaSuccess;
   if (a.d % 2 != 0 || a.d > 2048 || pg.block_size == 0 || pg.table_len == 0 || !pg.table || !kc || !vc)
     return cudaErrorInvalidValue;
+  if ((uint64_t)a.kv_heads * pg.block_size * a.d >= (1ull << 32)) return cudaErrorInvalidValue;
   StoreArgs<E> st;
   st.a = a;
-  st.P = Pool{pg.table, pg.block_size, pg.table_len, pg.blocks};
-  st.kc = static_cast<St<E>*>(kc);
-  st.vc = static_cast<St<E>*>(vc);
+  st.P = Pool{pg.table, static_cast<const uint64_t*>(kc), static_cast<const uint64_t*>(vc), pg.block_size,
+              pg.table_len, pg.blocks};
   return fk_launch_ex(kv_store_paged_kernel<E>, dim3(a.kv_heads, a.m), dim3(a.d / 2), 0, s, a.pdl, st);
 }
 
@@ -451,17 +460,15 @@ cudaError_t launch_attend(const FkAttend& a, const FkPaged& pg, const void* kc, 
       a.m > kMaxAttendRows || (uint64_t)a.m * a.heads * a.max_splits >= (1ull << 32) || pg.block_size == 0 ||
       pg.table_len == 0 || !pg.table || !kc || !vc)
     return cudaErrorInvalidValue;
+  if ((uint64_t)a.kv_heads * pg.block_size * kHeadDim >= (1ull << 32)) return cudaErrorInvalidValue;
   AttendArgs<E> f = {};
   f.a = a;
-  f.P = Pool{pg.table, pg.block_size, pg.table_len, pg.blocks};
-  f.kc = static_cast<const St<E>*>(kc);
-  f.vc = static_cast<const St<E>*>(vc);
+  f.P = Pool{pg.table, static_cast<const uint64_t*>(kc), static_cast<const uint64_t*>(vc), pg.block_size,
+             pg.table_len, pg.blocks};
   if (FUSED) {
     if (a.rotated > kHeadDim / 2) return cudaErrorInvalidValue;
     f.k_off = k_off;
     f.v_off = v_off;
-    f.kc_w = const_cast<St<E>*>(f.kc);
-    f.vc_w = const_cast<St<E>*>(f.vc);
   }
   auto kern = attend_paged_kernel<E, FUSED>;
   int dev = 0, sms = 148, per_sm = 0;
@@ -491,11 +498,11 @@ cudaError_t launch_prompt(const FkAttend& a, const FkPaged& pg, const void* kc, 
   auto kern = attend_prompt_paged_kernel<E>;
   cudaError_t e = fk_allow_smem(kern, smem);
   if (e != cudaSuccess) return e;
+  if ((uint64_t)a.kv_heads * pg.block_size * kHeadDim >= (1ull << 32)) return cudaErrorInvalidValue;
   AttendArgs<E> f = {};
   f.a = a;
-  f.P = Pool{pg.table, pg.block_size, pg.table_len, pg.blocks};
-  f.kc = static_cast<const St<E>*>(kc);
-  f.vc = static_cast<const St<E>*>(vc);
+  f.P = Pool{pg.table, static_cast<const uint64_t*>(kc), static_cast<const uint64_t*>(vc), pg.block_size,
+             pg.table_len, pg.blocks};
   const dim3 grid((a.m + kPromptTile - 1) / kPromptTile, a.heads);
   return fk_launch_ex(kern, grid, dim3(128), smem, s, a.pdl, f, out, ldo, max_pos);
 }

@@ -394,6 +394,9 @@ struct KernelSpec {
   uint32_t params_size = 0;
   std::string abi;
   uint64_t hash = 0;
+  // Tables of device addresses, bound after the buffers (IR.hs:400-429):
+  // each entry the start of an array of the table's type.
+  std::vector<BufSpec> tables = {};
 };
 
 uint64_t fnv1a(const void* p, size_t n) {
@@ -974,8 +977,10 @@ int l_combine_ranks_add(fkc_ctx* c, const Params& p, void* const* bufs) {
                   "combine_ranks_add");
 }
 
-// ---- paged KV caches: block tables into pools of blocks --------------------
-// kv_store_paged: qkv cos sin pos table k_cache v_cache
+// ---- paged KV caches: each row's block table (indices), the blocks reached
+// through the caches' tables of block addresses (bound after the buffers,
+// as the reference's ABI orders tables: Abi.hs:136-159) -------------------
+// kv_store_paged: qkv cos sin pos table | tables k_cache v_cache
 //   | m kv_heads d block_size table_len blocks rotated ldq k_off v_off
 int kv_store_paged(fkc_ctx* c, const Params& p, void* const* bufs, FkElem el, const char* name) {
   FkKvStore a = {};
@@ -994,12 +999,12 @@ template <FkElem EL>
 int l_kv_store_paged_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
   return kv_store_paged(c, p, bufs, EL, KN("kv_store_paged"));
 }
-// attend_split_paged: qkv cos sin pos table k_cache v_cache part_m part_l part_acc
+// attend_split_paged: qkv cos sin pos table part_m part_l part_acc | tables k_cache v_cache
 //   | m heads kv_heads d block_size table_len blocks rotated chunk max_splits ldq q_off scale
 int attend_paged(fkc_ctx* c, const Params& p, void* const* bufs, FkElem el, const char* name) {
   FkAttend a = {};
   a.qkv = CF(0), a.cos_t = CF(1), a.sin_t = CF(2), a.pos = CU(3);
-  a.part_m = F(7), a.part_l = F(8), a.part_acc = F(9);
+  a.part_m = F(5), a.part_l = F(6), a.part_acc = F(7);
   a.m = p.u(0), a.heads = p.u(1), a.kv_heads = p.u(2), a.d = p.u(3), a.rotated = p.u(7);
   a.chunk = p.u(8), a.max_splits = p.u(9), a.ldq = p.u(10), a.q_off = p.u(11);
   a.scale = p.f(12);
@@ -1009,7 +1014,7 @@ int attend_paged(fkc_ctx* c, const Params& p, void* const* bufs, FkElem el, cons
   if (a.kv_heads == 0 || a.heads % a.kv_heads != 0)
     return fail(FKC_ERR_ARGUMENT, "%s: %u heads do not share %u KV heads in groups.", name, a.heads, a.kv_heads);
   if (a.rotated > a.d / 2) return fail(FKC_ERR_ARGUMENT, "%s: rotated %u is more than d/2.", name, a.rotated);
-  return launched(fk_launch_attend_paged(a, pg, bufs[5], bufs[6], el, c->stream), name);
+  return launched(fk_launch_attend_paged(a, pg, bufs[8], bufs[9], el, c->stream), name);
 }
 int l_attend_paged(fkc_ctx* c, const Params& p, void* const* bufs) {
   return attend_paged(c, p, bufs, FK_F32, "attend_split_paged");
@@ -1018,14 +1023,14 @@ template <FkElem EL>
 int l_attend_paged_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
   return attend_paged(c, p, bufs, EL, KN("attend_split_paged"));
 }
-// attend_decode_paged: qkv cos sin pos table k_cache v_cache part_m part_l part_acc
+// attend_decode_paged: qkv cos sin pos table part_m part_l part_acc | tables k_cache v_cache
 //   | m heads kv_heads d block_size table_len blocks rotated chunk max_splits ldq q_off k_off v_off scale
 // The KV store folded into the split attention; every block-table entry
 // distinct (no row reads what another row stores).
 int attend_decode_paged(fkc_ctx* c, const Params& p, void* const* bufs, FkElem el, const char* name) {
   FkAttend a = {};
   a.qkv = CF(0), a.cos_t = CF(1), a.sin_t = CF(2), a.pos = CU(3);
-  a.part_m = F(7), a.part_l = F(8), a.part_acc = F(9);
+  a.part_m = F(5), a.part_l = F(6), a.part_acc = F(7);
   a.m = p.u(0), a.heads = p.u(1), a.kv_heads = p.u(2), a.d = p.u(3), a.rotated = p.u(7);
   a.chunk = p.u(8), a.max_splits = p.u(9), a.ldq = p.u(10), a.q_off = p.u(11);
   a.scale = p.f(14);
@@ -1035,7 +1040,7 @@ int attend_decode_paged(fkc_ctx* c, const Params& p, void* const* bufs, FkElem e
   if (a.kv_heads == 0 || a.heads % a.kv_heads != 0)
     return fail(FKC_ERR_ARGUMENT, "%s: %u heads do not share %u KV heads in groups.", name, a.heads, a.kv_heads);
   if (a.rotated > a.d / 2) return fail(FKC_ERR_ARGUMENT, "%s: rotated %u is more than d/2.", name, a.rotated);
-  return launched(fk_launch_attend_decode_paged(a, pg, bufs[5], bufs[6], el, p.u(12), p.u(13), c->stream), name);
+  return launched(fk_launch_attend_decode_paged(a, pg, bufs[8], bufs[9], el, p.u(12), p.u(13), c->stream), name);
 }
 int l_attend_decode_paged(fkc_ctx* c, const Params& p, void* const* bufs) {
   return attend_decode_paged(c, p, bufs, FK_F32, "attend_decode_paged");
@@ -1044,7 +1049,7 @@ template <FkElem EL>
 int l_attend_decode_paged_kv16(fkc_ctx* c, const Params& p, void* const* bufs) {
   return attend_decode_paged(c, p, bufs, EL, KN("attend_decode_paged"));
 }
-// attend_prompt_paged: qkv cos sin pos table k_cache v_cache out
+// attend_prompt_paged: qkv cos sin pos table out | tables k_cache v_cache
 //   | m heads kv_heads d block_size table_len blocks rotated ldq q_off ldo max_pos scale
 // A prompt's rows of one sequence: row 0's block table serves them all.
 int attend_prompt_paged(fkc_ctx* c, const Params& p, void* const* bufs, FkElem el, const char* name) {
@@ -1061,7 +1066,7 @@ int attend_prompt_paged(fkc_ctx* c, const Params& p, void* const* bufs, FkElem e
   if ((uint64_t)p.u(11) >= (uint64_t)pg.table_len * pg.block_size)
     return fail(FKC_ERR_ARGUMENT, "%s: max_pos %u is past the block table's %u positions.", name, p.u(11),
                 pg.table_len * pg.block_size);
-  return launched(fk_launch_attend_prompt_paged(a, pg, bufs[5], bufs[6], el, F(7), p.u(10), p.u(11), c->stream),
+  return launched(fk_launch_attend_prompt_paged(a, pg, bufs[6], bufs[7], el, F(5), p.u(10), p.u(11), c->stream),
                   name);
 }
 int l_attend_prompt_paged(fkc_ctx* c, const Params& p, void* const* bufs) {
@@ -1309,13 +1314,12 @@ std::vector<KernelSpec> make_table() {
                 {"cos", "read", "f32"},
                 {"sin", "read", "f32"},
                 {"pos", "read", "u32"},
-                {"table", "read", "u32"},
-                {"k_cache", "read_write", "f32"},
-                {"v_cache", "read_write", "f32"}},
+                {"table", "read", "u32"}},
                {dim("m", 1, 65535), dim("kv_heads", 1, 1024), dim("d", 2, 2048, 2), dim("block_size", 1, 65536),
                 dim("table_len", 1, kMax), dim("blocks", 1, kMax), u32("rotated"), u32("ldq"), u32("k_off"),
                 u32("v_off")},
                l_kv_store_paged});
+  t.back().tables = {{"k_cache", "read_write", "f32"}, {"v_cache", "read_write", "f32"}};
   t.push_back({"attend_split_paged",
                128,
                {{"qkv", "read", "f32"},
@@ -1323,8 +1327,6 @@ std::vector<KernelSpec> make_table() {
                 {"sin", "read", "f32"},
                 {"pos", "read", "u32"},
                 {"table", "read", "u32"},
-                {"k_cache", "read", "f32"},
-                {"v_cache", "read", "f32"},
                 {"part_m", "write", "f32"},
                 {"part_l", "write", "f32"},
                 {"part_acc", "write", "f32"}},
@@ -1332,6 +1334,7 @@ std::vector<KernelSpec> make_table() {
                 dim("block_size", 1, 65536), dim("table_len", 1, kMax), dim("blocks", 1, kMax), u32("rotated"),
                 dim("chunk", 1, 256), dim("max_splits", 1, 65535), u32("ldq"), u32("q_off"), f32("scale")},
                l_attend_paged});
+  t.back().tables = {{"k_cache", "read", "f32"}, {"v_cache", "read", "f32"}};
   t.push_back({"attend_decode_paged",
                128,
                {{"qkv", "read", "f32"},
@@ -1339,8 +1342,6 @@ std::vector<KernelSpec> make_table() {
                 {"sin", "read", "f32"},
                 {"pos", "read", "u32"},
                 {"table", "read", "u32"},
-                {"k_cache", "read_write", "f32"},
-                {"v_cache", "read_write", "f32"},
                 {"part_m", "write", "f32"},
                 {"part_l", "write", "f32"},
                 {"part_acc", "write", "f32"}},
@@ -1349,6 +1350,7 @@ std::vector<KernelSpec> make_table() {
                 dim("chunk", 1, 256), dim("max_splits", 1, 65535), u32("ldq"), u32("q_off"), u32("k_off"),
                 u32("v_off"), f32("scale")},
                l_attend_decode_paged});
+  t.back().tables = {{"k_cache", "read_write", "f32"}, {"v_cache", "read_write", "f32"}};
   t.push_back({"attend_prompt_paged",
                128,
                {{"qkv", "read", "f32"},
@@ -1356,13 +1358,12 @@ std::vector<KernelSpec> make_table() {
                 {"sin", "read", "f32"},
                 {"pos", "read", "u32"},
                 {"table", "read", "u32"},
-                {"k_cache", "read", "f32"},
-                {"v_cache", "read", "f32"},
                 {"out", "write", "f32"}},
                {dim("m", 1, 65535), dim("heads", 1, 1024), dim("kv_heads", 1, 1024), dim("d", 128, 128),
                 dim("block_size", 1, 65536), dim("table_len", 1, kMax), dim("blocks", 1, kMax), u32("rotated"),
                 u32("ldq"), u32("q_off"), u32("ldo"), dim("max_pos", 0, 1407), f32("scale")},
                l_attend_prompt_paged});
+  t.back().tables = {{"k_cache", "read", "f32"}, {"v_cache", "read", "f32"}};
   // Routed experts (Graph.hs:306-340).
   t.push_back({"route_topk",
                32,
@@ -1441,9 +1442,10 @@ std::vector<KernelSpec> make_table() {
     if (!found) continue;
     k.name = v.name;
     k.launch = v.launch;
-    for (BufSpec& b : k.bufs)
-      for (const char* r : v.retyped)
-        if (strcmp(b.name, r) == 0) b.type = v.type;
+    for (std::vector<BufSpec>* list : {&k.bufs, &k.tables})
+      for (BufSpec& b : *list)
+        for (const char* r : v.retyped)
+          if (strcmp(b.name, r) == 0) b.type = v.type;
     t.push_back(k);
   }
   // The C layout (Abi.hs:113-133) and the canonical text (Abi.hs:136-159).
@@ -1459,6 +1461,10 @@ std::vector<KernelSpec> make_table() {
     k.params_size = k.params.empty() ? 0 : (off + align - 1) / align * align;
     std::string a = "abi 1\n";
     for (auto& b : k.bufs) a += std::string("buffer ") + b.name + " " + b.access + " " + b.type + " align 16\n";
+    // A read-only table's line names no access (Abi.hs:143-152).
+    for (auto& b : k.tables)
+      a += std::string("table ") + b.name + (strcmp(b.access, "read") == 0 ? "" : std::string(" ") + b.access) + " " +
+           b.type + " align 16\n";
     for (size_t i = 0; i < k.params.size(); ++i)
       a += std::string("param ") + k.params[i].name + " " + k.params[i].type + " at " + std::to_string(k.offsets[i]) +
            "\n";
@@ -1496,7 +1502,7 @@ extern "C" int fkc_kernel_describe(int id, const char** name, const char** abi, 
   if (hash) *hash = k.hash;
   if (threads) *threads = k.threads;
   if (params_size) *params_size = k.params_size;
-  if (buffers) *buffers = (uint32_t)k.bufs.size();
+  if (buffers) *buffers = (uint32_t)(k.bufs.size() + k.tables.size());
   return FKC_OK;
 }
 
@@ -1525,12 +1531,19 @@ extern "C" int fkc_launch(fkc_ctx* c, int kernel, const void* params, size_t par
   if (params_len != k.params_size)
     return fail(FKC_ERR_ARGUMENT, "%s: the parameter struct is %zu bytes, not %u.", k.name, params_len,
                 k.params_size);
-  if (nbufs != (int)k.bufs.size())
-    return fail(FKC_ERR_ARGUMENT, "%s: %d buffers bound, not %zu.", k.name, nbufs, k.bufs.size());
-  for (int i = 0; i < nbufs; ++i)
+  const int nb = (int)k.bufs.size(), nt = (int)k.tables.size();
+  if (nbufs != nb + nt) {
+    if (nt) return fail(FKC_ERR_ARGUMENT, "%s: %d bindings, not %d buffers and %d tables.", k.name, nbufs, nb, nt);
+    return fail(FKC_ERR_ARGUMENT, "%s: %d buffers bound, not %d.", k.name, nbufs, nb);
+  }
+  for (int i = 0; i < nb; ++i)
     if (!bufs[i] || ((uintptr_t)bufs[i] & 15u))
       return fail(FKC_ERR_ARGUMENT, "%s: buffer %s is %s.", k.name, k.bufs[i].name,
                   bufs[i] ? "not aligned to 16 bytes" : "null");
+  for (int i = 0; i < nt; ++i)  // a table is an array of 8-byte addresses
+    if (!bufs[nb + i] || ((uintptr_t)bufs[nb + i] & 7u))
+      return fail(FKC_ERR_ARGUMENT, "%s: table %s is %s.", k.name, k.tables[i].name,
+                  bufs[nb + i] ? "not aligned to 8 bytes" : "null");
   Params p{(const unsigned char*)params, &k.offsets};
   // The dimensions' ranges first, as the CPU target's asserts (Emit/Rust.hs:94-104).
   for (size_t i = 0; i < k.params.size(); ++i) {

@@ -130,6 +130,14 @@ class Llama:
             self.arena.upload(host_weights)
         self.cos, self.sin = ctx.rope_tables(s.theta, s.head_dim, s.head_dim // 2, s.positions)
         self.kbase, self.vbase = self._kv_arena()
+        # A paged cache's kernels reach each block through a table of the
+        # blocks' addresses (the Paged layout, src/FuryKernel/Program/
+        # Graph.hs:144-152; tables, IR.hs:400-429): [layers][blocks] u64 for
+        # the keys and for the values, here pointing into the pool's blocks
+        # (set_block_addresses points them anywhere else).
+        self.ktab = self.vtab = None
+        if s.paged:
+            self.ktab, self.vtab = self._block_table(self.kbase), self._block_table(self.vbase)
         if prefill_kv is not None:
             kv = s.layers * self._kv_units() * s.kv_heads * self._kv_unit_len() * s.head_dim
             cfill = self._fill(s.cache)
@@ -263,8 +271,47 @@ class Llama:
     def final_norm_ptr(self) -> int:
         return self.embed_ptr() + self.wb * self.full.vocab * self.full.d_model
 
-    def kv_layer(self, l: int):
+    def block_bytes(self) -> int:
+        """Bytes of one block of a paged cache: kv_heads x block_size x head_dim elements."""
         s = self.s
+        return self.cb * s.kv_heads * s.block_size * s.head_dim
+
+    def _block_table(self, pool: int):
+        """A [layers][blocks] u64 table of the pool's blocks' addresses."""
+        s = self.s
+        addr = pool + np.arange(s.layers * s.blocks, dtype=np.uint64) * np.uint64(self.block_bytes())
+        return self.ctx.to_device(addr.reshape(s.layers, s.blocks))
+
+    def set_block_addresses(self, layer: int, keys, values) -> None:
+        """Points a paged cache's blocks of one layer at arrays of the
+        caller's (each block_bytes() long, 16-byte aligned, wherever it was
+        allocated): `keys[b]` and `values[b]` the device addresses of block
+        b's keys and values. The launch list binds the tables, so a captured
+        step reads the new addresses on its next replay."""
+        s = self.s
+        if not s.paged:
+            raise N.Refused(N.FKC_ERR_ARGUMENT, "set_block_addresses: the engine's caches are Ring caches.")
+        if not 0 <= layer < s.layers:
+            raise N.Refused(N.FKC_ERR_ARGUMENT, f"set_block_addresses: layer {layer} of {s.layers}.")
+        rows = []
+        for what, a in (("key", keys), ("value", values)):
+            a = np.asarray(a, np.uint64)
+            if a.shape != (s.blocks,):
+                raise N.Refused(N.FKC_ERR_ARGUMENT, f"set_block_addresses: {a.size} {what} blocks, not {s.blocks}.")
+            if np.any(a == 0) or np.any(a % 16):
+                raise N.Refused(N.FKC_ERR_ARGUMENT, f"set_block_addresses: a {what} block's address is null or "
+                                                    "not 16-byte aligned.")
+            rows.append(a)
+        for tab, row in ((self.ktab, rows[0]), (self.vtab, rows[1])):
+            N.check(N.lib().fkc_buf_upload(self.ctx.handle, tab.ptr + 8 * layer * s.blocks, row.ctypes.data,
+                                           row.nbytes))
+
+    def kv_layer(self, l: int):
+        """A layer's caches as its launches bind them: a ring's slab of the
+        arena, or a paged cache's row of each block-address table."""
+        s = self.s
+        if s.paged:
+            return self.ktab.ptr + 8 * l * s.blocks, self.vtab.ptr + 8 * l * s.blocks
         per = self.cb * self._kv_units() * s.kv_heads * self._kv_unit_len() * s.head_dim
         return self.kbase + l * per, self.vbase + l * per
 
@@ -272,7 +319,8 @@ class Llama:
     def launch_addresses(self) -> dict:
         """The device addresses the decode step's launches bind (the C++
         host library's fkh_llama_desc)."""
-        return {"arena": self.arena.ptr, "kbase": self.kbase, "vbase": self.vbase, "cos_t": self.cos.ptr,
+        kb, vb = (self.ktab.ptr, self.vtab.ptr) if self.s.paged else (self.kbase, self.vbase)
+        return {"arena": self.arena.ptr, "kbase": kb, "vbase": vb, "cos_t": self.cos.ptr,
                 "sin_t": self.sin.ptr, "tokens": self.tokens.ptr, "pos": self.pos.ptr, "slot": self.slot.ptr,
                 "x": self.x.ptr, "x1": self.x1.ptr, "qkv": self.qkv.ptr, "att": self.att.ptr, "gu": self.gu.ptr,
                 "act": self.act.ptr, "logits": self.logits.ptr, "out_ids": self.out_ids.ptr,

@@ -229,16 +229,14 @@ Launch lower_step(const Program& p, const Step& step, const Binding& b, uint64_t
                   {"q_off", (double)q.col},
                   {"scale", spec.scale}};
     }
-    L.bufs = {q.base,
-              cos_t,
-              sin_t,
-              at(b.ints, src_name(att->op.sources[2]), step.name),
-              at(b.ints, src_name(att->op.sources[3]), step.name),
-              at(b.caches, kc.name, step.name),
-              at(b.caches, src_name(att->op.sources[1]), step.name),
-              attn.partials[0],
-              attn.partials[1],
-              attn.partials[2]};
+    const uint64_t kaddr = at(b.caches, kc.name, step.name), vaddr = at(b.caches, src_name(att->op.sources[1]), step.name);
+    L.bufs = {q.base, cos_t, sin_t, at(b.ints, src_name(att->op.sources[2]), step.name),
+              at(b.ints, src_name(att->op.sources[3]), step.name)};
+    // A ring's caches are buffers before the partials; a paged cache's
+    // tables of block addresses come after every buffer.
+    if (kc.kind.ring) L.bufs.insert(L.bufs.end(), {kaddr, vaddr});
+    L.bufs.insert(L.bufs.end(), {attn.partials[0], attn.partials[1], attn.partials[2]});
+    if (!kc.kind.ring) L.bufs.insert(L.bufs.end(), {kaddr, vaddr});
     return L;
   }
 
@@ -621,8 +619,11 @@ std::vector<Launch> fuse_attention(const std::vector<Launch>& in) {
     if (i + 1 < in.size() && (ring || paged) && kvf.second == atf.second) {
       const Launch& kv = in[i];
       const Launch& at = in[i + 1];
-      bool same = kv.bufs[0] == at.bufs[0] &&
-                  std::equal(kv.bufs.begin() + 3, kv.bufs.begin() + 7, at.bufs.begin() + 3);
+      // The same q/k/v rows, positions, slots (block tables) and caches: a
+      // ring's caches are the attention's buffers 5 and 6, a paged cache's
+      // address tables its bindings 8 and 9 (after the partials).
+      bool same = kv.bufs[0] == at.bufs[0] && std::equal(kv.bufs.begin() + 3, kv.bufs.begin() + 5, at.bufs.begin() + 3) &&
+                  std::equal(kv.bufs.begin() + 5, kv.bufs.begin() + 7, at.bufs.begin() + (ring ? 5 : 8));
       const std::vector<const char*> keys =
           ring ? std::vector<const char*>{"ldq", "rotated", "d", "kv_heads", "length"}
                : std::vector<const char*>{"ldq", "rotated", "d", "kv_heads", "block_size", "table_len", "blocks"};
@@ -738,7 +739,9 @@ std::vector<Launch> llama_launches(const LlamaLaunchDesc& d) {
   }
   // A layer's caches: its ring's slots, or its pool's blocks.
   const uint64_t units = s.paged() ? s.blocks : s.slots, unit_len = s.paged() ? s.block_size : s.length;
-  const uint64_t per_cache = s.cache_bytes() * units * s.kv_heads * unit_len * s.head_dim;
+  // A ring's layer is a slab of the arena; a paged cache's layer is its row
+  // of the [layers, blocks] table of block addresses.
+  const uint64_t per_cache = s.paged() ? 8 * s.blocks : s.cache_bytes() * units * s.kv_heads * unit_len * s.head_dim;
   for (uint64_t l = 0; l < s.layers; ++l) {
     Binding b;
     b.weights = layer_weights(s, d.arena, l);

@@ -82,7 +82,9 @@ std::vector<Launch> prefill_launches(const LlamaLaunchDesc& d, const PrefillDesc
       for (const char* k : {"m", "heads", "kv_heads", "d", "block_size", "table_len", "blocks", "rotated", "chunk",
                             "max_splits", "ldq", "q_off", "scale"})
         ap.emplace_back(k, L->param(k));
-      unfused.push_back(make("kv_store_paged" + csuf, kp, {L->bufs.begin(), L->bufs.begin() + 7}));
+      // The store: the attention's first five buffers and its two tables.
+      unfused.push_back(make("kv_store_paged" + csuf, kp,
+                             {L->bufs[0], L->bufs[1], L->bufs[2], L->bufs[3], L->bufs[4], L->bufs[8], L->bufs[9]}));
       unfused.push_back(make("attend_split_paged" + csuf, ap, {L->bufs.begin(), L->bufs.begin() + 10}));
     }
   }
@@ -142,7 +144,7 @@ std::vector<Launch> prefill_launches(const LlamaLaunchDesc& d, const PrefillDesc
                           {"ldo", (double)qw},
                           {"max_pos", (double)(p.positions - 1)},
                           {"scale", at.param("scale")}},
-                         {p.qkv, at.bufs[1], at.bufs[2], p.pos, p.slot, at.bufs[5], at.bufs[6], p.att}));
+                         {p.qkv, at.bufs[1], at.bufs[2], p.pos, p.slot, p.att, at.bufs[8], at.bufs[9]}));
     } else if (p.one_slot) {
       out.push_back(make("attend_prompt" + csuf,
                          {{"m", md},
@@ -161,8 +163,10 @@ std::vector<Launch> prefill_launches(const LlamaLaunchDesc& d, const PrefillDesc
       out.push_back(with(at,
                          {{"m", md}, {"ldq", (double)nq}, {"chunk", (double)p.chunk},
                           {"max_splits", (double)max_splits}},
-                         {p.qkv, at.bufs[1], at.bufs[2], p.pos, p.slot, at.bufs[5], at.bufs[6], p.part[0], p.part[1],
-                          p.part[2]}));
+                         paged ? std::vector<uint64_t>{p.qkv, at.bufs[1], at.bufs[2], p.pos, p.slot, p.part[0],
+                                                       p.part[1], p.part[2], at.bufs[8], at.bufs[9]}
+                               : std::vector<uint64_t>{p.qkv, at.bufs[1], at.bufs[2], p.pos, p.slot, at.bufs[5],
+                                                       at.bufs[6], p.part[0], p.part[1], p.part[2]}));
       out.push_back(with(cb,
                          {{"m", md}, {"chunk", (double)p.chunk}, {"max_splits", (double)max_splits},
                           {"ldo", (double)qw}},

@@ -18,7 +18,7 @@ from __future__ import annotations
 from dataclasses import dataclass, field
 
 from . import abi as A
-from .abi import Buffer, DimRange, KernelSig, Param
+from .abi import Buffer, DimRange, KernelSig, Param, Table
 
 
 @dataclass(frozen=True)
@@ -192,36 +192,36 @@ SPEC_KERNELS = {
         KernelSig("gated_gelu", [_f32("x"), _f32("y", "write")], [_dim("segments", 1, _MAX), _dim("f", 1, _MAX)]),
         KernelSig("combine_ranks_add", [_f32("r"), _f32("ws"), _f32("segs"), _f32("y", "write")],
                   [_dim("m", 1, 65535), _dim("k", 1, 8), _dim("d", 1, _MAX)]),
-        # Paged caches (Graph.hs:144-152): a row's block table instead of its slot.
+        # Paged caches (Graph.hs:144-152): a row's block table (indices)
+        # instead of its slot; each cache's blocks through a table of their
+        # addresses (IR.hs:400-429), bound after the buffers.
         KernelSig("kv_store_paged",
-                  [_f32("qkv"), _f32("cos"), _f32("sin"), _u32("pos"), _u32("table"), _f32("k_cache", "read_write"),
-                   _f32("v_cache", "read_write")],
+                  [_f32("qkv"), _f32("cos"), _f32("sin"), _u32("pos"), _u32("table")],
                   [_dim("m", 1, 65535), _dim("kv_heads", 1, 1024), _dim("d", 2, 2048, 2), _dim("block_size", 1, 65536),
                    _dim("table_len", 1, _MAX), _dim("blocks", 1, _MAX), _u("rotated"), _u("ldq"), _u("k_off"),
-                   _u("v_off")], threads=64),
+                   _u("v_off")], tables=[Table("k_cache", "read_write", "f32"), Table("v_cache", "read_write", "f32")],
+                  threads=64),
         KernelSig("attend_split_paged",
-                  [_f32("qkv"), _f32("cos"), _f32("sin"), _u32("pos"), _u32("table"), _f32("k_cache"),
-                   _f32("v_cache"), _f32("part_m", "write"), _f32("part_l", "write"), _f32("part_acc", "write")],
+                  [_f32("qkv"), _f32("cos"), _f32("sin"), _u32("pos"), _u32("table"), _f32("part_m", "write"),
+                   _f32("part_l", "write"), _f32("part_acc", "write")],
                   [_dim("m", 1, 16384), _dim("heads", 1, 1024), _dim("kv_heads", 1, 1024), _dim("d", 128, 128),
                    _dim("block_size", 1, 65536), _dim("table_len", 1, _MAX), _dim("blocks", 1, _MAX), _u("rotated"),
                    _dim("chunk", 1, 256), _dim("max_splits", 1, 65535), _u("ldq"), _u("q_off"), _f("scale")],
-                  threads=128),
+                  tables=[Table("k_cache", "read", "f32"), Table("v_cache", "read", "f32")], threads=128),
         KernelSig("attend_decode_paged",
-                  [_f32("qkv"), _f32("cos"), _f32("sin"), _u32("pos"), _u32("table"), _f32("k_cache", "read_write"),
-                   _f32("v_cache", "read_write"), _f32("part_m", "write"), _f32("part_l", "write"),
-                   _f32("part_acc", "write")],
+                  [_f32("qkv"), _f32("cos"), _f32("sin"), _u32("pos"), _u32("table"), _f32("part_m", "write"),
+                   _f32("part_l", "write"), _f32("part_acc", "write")],
                   [_dim("m", 1, 64), _dim("heads", 1, 1024), _dim("kv_heads", 1, 1024), _dim("d", 128, 128),
                    _dim("block_size", 1, 65536), _dim("table_len", 1, _MAX), _dim("blocks", 1, _MAX), _u("rotated"),
                    _dim("chunk", 1, 256), _dim("max_splits", 1, 65535), _u("ldq"), _u("q_off"), _u("k_off"),
                    _u("v_off"), _f("scale")],
-                  threads=128),
+                  tables=[Table("k_cache", "read_write", "f32"), Table("v_cache", "read_write", "f32")], threads=128),
         KernelSig("attend_prompt_paged",
-                  [_f32("qkv"), _f32("cos"), _f32("sin"), _u32("pos"), _u32("table"), _f32("k_cache"),
-                   _f32("v_cache"), _f32("out", "write")],
+                  [_f32("qkv"), _f32("cos"), _f32("sin"), _u32("pos"), _u32("table"), _f32("out", "write")],
                   [_dim("m", 1, 65535), _dim("heads", 1, 1024), _dim("kv_heads", 1, 1024), _dim("d", 128, 128),
                    _dim("block_size", 1, 65536), _dim("table_len", 1, _MAX), _dim("blocks", 1, _MAX),
                    _u("rotated"), _u("ldq"), _u("q_off"), _u("ldo"), _dim("max_pos", 0, 1407), _f("scale")],
-                  threads=128),
+                  tables=[Table("k_cache", "read", "f32"), Table("v_cache", "read", "f32")], threads=128),
     ]
 }
 
@@ -249,7 +249,9 @@ _VARIANTS = [
 for _base, _name, _retyped, _t in _VARIANTS:
     _k = SPEC_KERNELS[_base]
     SPEC_KERNELS[_name] = KernelSig(_name, [Buffer(b.name, b.access, _t if b.name in _retyped else b.type)
-                                            for b in _k.buffers], _k.params, threads=_k.threads)
+                                            for b in _k.buffers], _k.params,
+                                    [Table(b.name, b.access, _t if b.name in _retyped else b.type)
+                                     for b in _k.tables], threads=_k.threads)
 
 
 class CudaBackend:

@@ -93,7 +93,10 @@ typedef struct {
   int gate_up_interleaved, peer_exchange, fuse_attention;
   /* the weight arena: per layer q k v o gate up down attn_norm mlp_norm,
    * then the whole embedding table and the final norm; the Ring KV arena's
-   * key and value bases (fkc_kv_arena) */
+   * key and value bases (fkc_kv_arena), or, for a paged cache, the keys' and
+   * the values' tables of block addresses, [layers][blocks] u64 each (every
+   * block an array of kv_heads * block_size * head_dim elements, wherever
+   * it lies) */
   uint64_t arena, kbase, vbase;
   uint64_t cos_t, sin_t;           /* fkc_rope_tables */
   uint64_t tokens, pos, slot;      /* [batch] u32 each */

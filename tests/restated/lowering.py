@@ -168,7 +168,7 @@ def lower_step(p, step, b: Binding, tables: dict, attn: dict) -> Launch:
                            "blocks": layout.blocks, "rotated": qn.op.args[0].rotated, "chunk": attn["chunk"],
                            "max_splits": attn["max_splits"], "ldq": q.ld, "q_off": q.col, "scale": spec.scale},
                           [q.base, tables["cos"], tables["sin"], b.ints[pos], b.ints[slot],
-                           b.caches[kc], b.caches[vc], part[0], part[1], part[2]])
+                           part[0], part[1], part[2], b.caches[kc], b.caches[vc]])  # the tables after the buffers
         return Launch("attend_split" + ct,
                       {"m": b.m, "heads": spec.heads, "kv_heads": spec.kv_heads, "d": spec.head_dim,
                        "length": layout.length, "rotated": qn.op.args[0].rotated, "chunk": attn["chunk"],
@@ -413,7 +413,9 @@ def fuse_attention(eng, launches: list) -> list:
         form = fused.get(tuple(b for b, _ in pair)) if i + 1 < len(launches) else None
         if form and pair[0][1] == pair[1][1]:
             kv, at = launches[i:i + 2]
-            same = (kv.bufs[0] == at.bufs[0] and list(kv.bufs[3:7]) == list(at.bufs[3:7])
+            tabs = 5 if pair[1][0] == "attend_split" else 8  # a ring's cache buffers, or a paged cache's tables
+            same = (kv.bufs[0] == at.bufs[0] and list(kv.bufs[3:5]) == list(at.bufs[3:5])
+                    and list(kv.bufs[5:7]) == list(at.bufs[tabs:tabs + 2])
                     and all(kv.params[k] == at.params[k] for k in form[1]))
             if same:
                 p = dict(at.params, k_off=kv.params["k_off"], v_off=kv.params["v_off"])

@@ -58,7 +58,7 @@ def prefill_launches(pre, m: int) -> list:
         p = L.params
         by.setdefault("kv_store_paged", []).append(Launch("kv_store_paged" + csuf, {
             k: p[k] for k in ("m", "kv_heads", "d", "block_size", "table_len", "blocks", "rotated", "ldq",
-                              "k_off", "v_off")}, L.bufs[:7]))
+                              "k_off", "v_off")}, L.bufs[:5] + L.bufs[8:10]))
         by.setdefault("attend_split_paged", []).append(Launch("attend_split_paged" + csuf, {
             k: p[k] for k in ("m", "heads", "kv_heads", "d", "block_size", "table_len", "blocks", "rotated",
                               "chunk", "max_splits", "ldq", "q_off", "scale")}, L.bufs[:10]))
@@ -86,7 +86,7 @@ def prefill_launches(pre, m: int) -> list:
                 "block_size": ap["block_size"], "table_len": ap["table_len"], "blocks": ap["blocks"],
                 "rotated": ap["rotated"], "ldq": nq, "q_off": ap["q_off"], "ldo": qw,
                 "max_pos": pre.positions - 1, "scale": ap["scale"]},
-                [pre.qkv.ptr, at.bufs[1], at.bufs[2], pos, slot, at.bufs[5], at.bufs[6], pre.att.ptr]))
+                [pre.qkv.ptr, at.bufs[1], at.bufs[2], pos, slot, pre.att.ptr, at.bufs[8], at.bufs[9]]))
         elif pre.one_slot:
             ap = at.params
             out.append(Launch("attend_prompt" + csuf, {
@@ -97,6 +97,8 @@ def prefill_launches(pre, m: int) -> list:
         else:
             out.append(Launch(at.kernel, dict(at.params, m=m, ldq=nq, chunk=pre.chunk,
                                                    max_splits=pre.max_splits),
+                              [pre.qkv.ptr, at.bufs[1], at.bufs[2], pos, slot, pre.part[0].ptr, pre.part[1].ptr,
+                               pre.part[2].ptr, at.bufs[8], at.bufs[9]] if paged else
                               [pre.qkv.ptr, at.bufs[1], at.bufs[2], pos, slot, at.bufs[5], at.bufs[6],
                                pre.part[0].ptr, pre.part[1].ptr, pre.part[2].ptr]))
             out.append(Launch("attend_combine", dict(cb.params, m=m, chunk=pre.chunk,

@@ -166,6 +166,9 @@ def fake_engine(full, batch, rank=0, world=1, peer_exchange=True, fuse_attention
     at = iter(range(1, 100))
     e.arena = Buf(1 << 44)
     e.kbase, e.vbase = 2 << 44, 3 << 44
+    e.ktab = e.vtab = None
+    if s.paged:  # the block-address tables
+        e.ktab, e.vtab = Buf(5 << 44), Buf((5 << 44) + (1 << 40))
     for name in ("cos", "sin", "tokens", "pos", "slot", "out_ids", "x", "x1", "partial", "qkv", "att", "gu",
                  "act", "logits", "pairs", "pairs_all"):
         setattr(e, name, Buf((4 << 44) + (next(at) << 32)))
