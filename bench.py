@@ -43,8 +43,9 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", default="5", choices=["5", "1", "2", "3a", "3b", "3c", "4"],
-                    help="5: the 32-layer decode step (default); 1, 2, 3a, 3b, 3c, 4: BASELINE's other configs")
+    ap.add_argument("--config", default="5", choices=["5", "1", "2", "3a", "3b", "3c", "4", "5g", "5h"],
+                    help="5: the 32-layer decode step (default); 1, 2, 3a, 3b, 3c, 4: BASELINE's other configs; "
+                         "5g, 5h: config 5's [gate;up] GEMV and its LM head alone, batch 1 (for kernel profiles)")
     ap.add_argument("--weights", default="f32", choices=["f32", "bf16", "f16"],
                     help="config 5: the model's weights (f32, the BASELINE configuration; bf16, the reference's "
                          "own element type; f16)")
@@ -690,6 +691,27 @@ def run_kernel_config(args):
         O.softmax_rows(O.rmsnorm_rows(hx, hg, 1e-5, 1.0, 1), 1)
         cpu_ms = (time.perf_counter() - t0) * 1e3
         cpu_sample_text = "the whole pass, fko_rmsnorm_rows + fko_softmax_rows, 1 thread"
+    elif cfg in ("5g", "5h"):
+        # One layer's [gate; up] GEMV (rows interleaved, the RMSNorm prologue,
+        # the SiLU-pair epilogue) or the LM head (the RMSNorm prologue), as
+        # the config-5 step launches them at batch 1: 4 copies of the weights
+        # in rotation, so that each launch streams its weights from HBM.
+        n, kern = (22016, "gemv_rmsnorm_silu") if cfg == "5g" else (32000, "gemv_rmsnorm")
+        k = 4096
+        x, g, y = ctx.empty((1, k)), ctx.empty(k), ctx.empty((1, n))
+        ctx.fill_normal(x, 2, 0.0, 1.0)
+        ctx.fill_uniform(g, 3, 0.5, 1.5)
+        ws = [ctx.empty((n, k)) for _ in range(4)]
+        for i, w in enumerate(ws):
+            ctx.fill_normal(w, 10 + i, 0.0, 0.02)
+        p = {"n": n, "k": k, "m": 1, "split": 1, "ldx": k, "ldy": n // 2 if cfg == "5g" else n, "eps": 1e-5,
+             "factor": 1.0}
+        rot = [[Launch(kern, p, [w.ptr, x.ptr, g.ptr, y.ptr])] for w in ws]
+        ms = time_graph(ctx, None, args.steps, args.warmup, rotate=rot)
+        outs = n // 2 if cfg == "5g" else n
+        nbytes = 4 * (n * k + k + k + outs)
+        workload = f"config 5's {'[gate; up] GEMV' if cfg == '5g' else 'LM head'} {n} x {k}, batch 1 ({kern})"
+        unit_label = "GEMVs/s"
     elif cfg in ("3a", "3b"):
         m = 1 if cfg == "3a" else 16
         n, k = 11008, 4096
@@ -745,7 +767,7 @@ def main():
     args = parse()
     if args.config == "3c":
         return run_gemm(args)
-    if args.config in ("1", "2", "3a", "3b", "4"):
+    if args.config in ("1", "2", "3a", "3b", "4", "5g", "5h"):
         return run_kernel_config(args)
     if args.impl == "reference":
         run_reference(args)

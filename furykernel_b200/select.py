@@ -136,7 +136,7 @@ def main(argv=None) -> None:
     batches = [int(b) for b in args.batches.split(",")]
 
     def shape(b):  # config 5's model at batch b: a slot a row
-        length = 4096 if b <= 4 else 1024
+        length = 4096 if b <= 4 else 640  # config 5: a 512-position prompt and 128 steps
         return LlamaShape(layers=args.layers, slots=b, length=length, positions=length)
 
     if args.command == "classes":
