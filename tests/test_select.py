@@ -377,3 +377,22 @@ def test_classes_for_a_shape_are_the_engines():
         e = fake_engine(small(b), b)
         assert S.classes_for(small(b), b, 148) == S.gemv_classes(e)
     S.main(["classes", "--batches", "1,16", "--layers", "1"])
+
+
+def test_the_committed_b200_selection_validates_for_config_5():
+    """The selection tuned on a B200 (python -m furykernel_b200.select tune,
+    148 SMs) for config 5's GEMV classes at batches 1, 4, 16 and 64 reads
+    back against the current kernels' identities and picks, for every
+    class, the split the engine takes by default (1)."""
+    import os
+
+    from furykernel_b200 import select as S
+    from furykernel_b200.shape import LlamaShape
+
+    path = os.path.join(os.path.dirname(S.__file__), "selections", "config5_b200.json")
+    text = open(path).read()
+    classes = []
+    for b in (1, 4, 16, 64):
+        length = 4096 if b <= 4 else 640
+        classes += S.classes_for(LlamaShape(slots=b, length=length, positions=length), b, 148)
+    assert H.gemv_selection_validate(text, classes, 148) == [1] * len(classes)
