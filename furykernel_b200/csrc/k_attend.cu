@@ -14,6 +14,7 @@
 // adds the splits in order before dividing.
 #include "fk_common.cuh"
 #include "fk_kernels.h"
+#include "fk_prompt.cuh"
 
 namespace fk {
 
@@ -240,120 +241,29 @@ __global__ void __launch_bounds__(128, 4) attend_kernel(FkAttendDecode f) {
   if (!waited) grid_launch_dependents();  // a block without items
 }
 
-// Attention over a prompt's rows (prefill), tiled by queries: one block a
-// (tile of 32 rows, head), all rows in one slot, each row over the
-// positions <= its own (stored before, by kv_store_ring). Keys come 32 at a
-// time into shared memory (transposed, so a lane takes a key) and are
-// shared by the tile's 32 rows, instead of every row reading its own keys.
-// Two passes: the scores (each a sequential dot over the head's dims,
-// times the scale) into shared memory with the rows' maxima, then the
-// weights exp(s - max) (binary64, rounded once) and their sums e and e v.
-// The orders differ from the decode kernel's, so prefill is held to the f64
-// evaluator's bounds (like its GEMMs), not to the split kernel's bits.
-constexpr int kPromptTile = 32;  // query rows a block, keys a round
+// Attention over a prompt's rows (prefill), all rows in one slot, each row
+// over the positions <= its own (stored before, by kv_store_ring): the
+// register-tiled body of fk_prompt.cuh over the Ring f32 caches.
+struct RingPromptSrc {
+  const float* kc;
+  const float* vc;
+  size_t base;  // position 0 of the rows' (slot, KV head), in elements / d
+  __device__ __forceinline__ void bind(const FkAttend& a, uint32_t kvh) {
+    kc = a.kc;
+    vc = a.vc;
+    base = ((size_t)a.slot[0] * a.kv_heads + kvh) * a.length;
+  }
+  __device__ __forceinline__ float4 k4(uint32_t t, uint32_t dd) const {
+    return __ldg(reinterpret_cast<const float4*>(kc + (base + t) * kHeadDim + dd));
+  }
+  __device__ __forceinline__ float4 v4(uint32_t t, uint32_t dd) const {
+    return __ldg(reinterpret_cast<const float4*>(vc + (base + t) * kHeadDim + dd));
+  }
+};
 
-__global__ void __launch_bounds__(128) attend_prompt_kernel(FkAttend a, float* __restrict__ out, uint32_t ldo,
-                                                            uint32_t max_pos) {
-  extern __shared__ float psm[];
-  float* qs = psm;                                // [32][128] the tile's rotated queries
-  float* kt = qs + kPromptTile * kHeadDim;        // [128][32] keys, transposed
-  float* vt = kt + kHeadDim * kPromptTile;        // [32][128] values
-  float* sc = vt + kPromptTile * kHeadDim;        // [32][max_pos + 1] scores
-  const uint32_t ncols = max_pos + 1;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint32_t r0 = blockIdx.x * kPromptTile, h = blockIdx.y;
-  const uint32_t rows = min((uint32_t)kPromptTile, a.m - r0);
-  const uint32_t kvh = h / (a.heads / a.kv_heads);
-  const size_t base = ((size_t)a.slot[0] * a.kv_heads + kvh) * a.length;
-  grid_wait();
-  grid_launch_dependents();
-
-  // The tile's queries, rotated.
-  for (uint32_t i = warp; i < kPromptTile; i += 4) {
-    if (i < rows) {
-      const uint32_t r = r0 + i, p = a.pos[r];
-      for (uint32_t c = lane; c < kHeadDim / 2; c += 32)
-        rope_pair(a.qkv + (size_t)r * a.ldq + a.q_off + (size_t)h * kHeadDim, qs + i * kHeadDim, c, kHeadDim / 2,
-                  a.rotated, a.cos_t + (size_t)p * a.rotated, a.sin_t + (size_t)p * a.rotated);
-    }
-  }
-  uint32_t tile_max = 0;
-  for (uint32_t i = 0; i < rows; ++i) tile_max = max(tile_max, a.pos[r0 + i]);
-  const uint32_t keys = min(tile_max + 1, ncols);  // positions past max_pos are the caller's error: not read
-  __syncthreads();
-
-  // Pass 1: scores. Warp w takes rows w, w + 4, ...; lane k the round's key k.
-  float mx[kPromptTile / 4];
-#pragma unroll
-  for (int u = 0; u < kPromptTile / 4; ++u) mx[u] = -INFINITY;
-  for (uint32_t t0 = 0; t0 < keys; t0 += kPromptTile) {
-    for (uint32_t e = threadIdx.x; e < kPromptTile * kHeadDim; e += blockDim.x) {
-      const uint32_t k = e / kHeadDim, dd = e % kHeadDim;
-      kt[dd * kPromptTile + k] = t0 + k < keys ? a.kc[(base + t0 + k) * kHeadDim + dd] : 0.0f;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int u = 0; u < kPromptTile / 4; ++u) {
-      const uint32_t i = warp + 4 * u;
-      if (i < rows) {
-        const float* q = qs + i * kHeadDim;
-        float dot = 0.0f;
-        for (uint32_t dd = 0; dd < kHeadDim; ++dd) dot = __fadd_rn(dot, __fmul_rn(q[dd], kt[dd * kPromptTile + lane]));
-        const uint32_t t = t0 + lane;
-        const float s = __fmul_rn(dot, a.scale);
-        if (t <= a.pos[r0 + i] && t < ncols) {
-          sc[i * ncols + t] = s;
-          mx[u] = max_number(mx[u], s);
-        }
-      }
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int u = 0; u < kPromptTile / 4; ++u) mx[u] = warp_max(mx[u]);
-
-  // Pass 2: weights, their sum and the weighted values (lane: dims lane + 32 j).
-  float l[kPromptTile / 4];
-  float acc[kPromptTile / 4][4];
-#pragma unroll
-  for (int u = 0; u < kPromptTile / 4; ++u) {
-    l[u] = 0.0f;
-#pragma unroll
-    for (int jd = 0; jd < 4; ++jd) acc[u][jd] = 0.0f;
-  }
-  for (uint32_t t0 = 0; t0 < keys; t0 += kPromptTile) {
-    for (uint32_t e = threadIdx.x; e < kPromptTile * kHeadDim; e += blockDim.x) {
-      const uint32_t k = e / kHeadDim, dd = e % kHeadDim;
-      vt[e] = t0 + k < keys ? a.vc[(base + t0 + k) * kHeadDim + dd] : 0.0f;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int u = 0; u < kPromptTile / 4; ++u) {
-      const uint32_t i = warp + 4 * u;
-      if (i < rows) {
-        const uint32_t t = t0 + lane;
-        const float e = t <= a.pos[r0 + i] && t < ncols ? exp_rounded(__fsub_rn(sc[i * ncols + t], mx[u])) : 0.0f;
-        l[u] = __fadd_rn(l[u], e);
-        for (uint32_t k = 0; k < kPromptTile; ++k) {
-          const float ek = __shfl_sync(0xffffffffu, e, k);
-#pragma unroll
-          for (int jd = 0; jd < 4; ++jd)
-            acc[u][jd] = __fadd_rn(acc[u][jd], __fmul_rn(ek, vt[k * kHeadDim + lane + 32 * jd]));
-        }
-      }
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int u = 0; u < kPromptTile / 4; ++u) {
-    const uint32_t i = warp + 4 * u;
-    const float lt = warp_sum(l[u]);
-    if (i < rows) {
-#pragma unroll
-      for (int jd = 0; jd < 4; ++jd)
-        out[(size_t)(r0 + i) * ldo + (size_t)h * kHeadDim + lane + 32 * jd] = __fdiv_rn(acc[u][jd], lt);
-    }
-  }
+__global__ void __launch_bounds__(prompt::kThreads) attend_prompt_kernel(FkAttend a, float* __restrict__ out,
+                                                                         uint32_t ldo, uint32_t max_pos) {
+  prompt::attend_prompt_body(a, RingPromptSrc{}, out, ldo, max_pos);
 }
 
 // The combine step: grid (heads, m), d threads. The largest maximum M (the
@@ -461,12 +371,14 @@ cudaError_t fk_launch_attend_decode(const FkAttendDecode& f, cudaStream_t s) { r
 cudaError_t fk_launch_attend_prompt(const FkAttend& a, float* out, uint32_t ldo, uint32_t max_pos, cudaStream_t s) {
   if (a.m == 0) return cudaSuccess;
   if (a.d != fk::kHeadDim || a.kv_heads == 0 || a.heads % a.kv_heads != 0 || max_pos >= a.length) return cudaErrorInvalidValue;
-  const size_t smem = (3 * (size_t)fk::kPromptTile * fk::kHeadDim + (size_t)fk::kPromptTile * (max_pos + 1)) * 4;
-  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  if (ldo % 4 != 0 || ((uintptr_t)out | (uintptr_t)a.kc | (uintptr_t)a.vc) % 16 != 0)
+    return cudaErrorInvalidValue;  // 16-byte loads and stores
+  const size_t smem = fk::prompt::kSmemBytes;
   cudaError_t e = fk_allow_smem(fk::attend_prompt_kernel, smem);
   if (e != cudaSuccess) return e;
-  const dim3 grid((a.m + fk::kPromptTile - 1) / fk::kPromptTile, a.heads);
-  return fk_launch_ex(fk::attend_prompt_kernel, grid, dim3(128), smem, s, a.pdl, a, out, ldo, max_pos);
+  const dim3 grid((a.m + fk::prompt::kRows - 1) / fk::prompt::kRows, a.heads);
+  return fk_launch_ex(fk::attend_prompt_kernel, grid, dim3(fk::prompt::kThreads), smem, s, a.pdl, a, out, ldo,
+                      max_pos);
 }
 
 cudaError_t fk_launch_combine(const FkCombine& a, cudaStream_t s) {

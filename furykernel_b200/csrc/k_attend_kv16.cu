@@ -18,6 +18,7 @@
 #include "fk_common.cuh"
 #include "fk_elem16.cuh"
 #include "fk_kernels.h"
+#include "fk_prompt.cuh"
 
 namespace fk {
 namespace kv16 {
@@ -257,116 +258,29 @@ __global__ void __launch_bounds__(128, 4) attend16_kernel(Attend16 f) {
   if (!waited) grid_launch_dependents();  // a block without items
 }
 
-// Attention over a prompt's rows in one slot (prefill), k_attend.cu's
-// attend_prompt_kernel over 16-bit caches: a block a (32 query rows, head);
-// keys and values 32 at a time into shared memory, widened.
-constexpr int kPromptTile = 32;
+// Attention over a prompt's rows in one slot (prefill): the register-tiled
+// body of fk_prompt.cuh over 16-bit Ring caches, four elements a load,
+// widened.
+template <class E>
+struct Ring16PromptSrc {
+  const uint16_t* kc;
+  const uint16_t* vc;
+  size_t base;  // position 0 of the rows' (slot, KV head), in elements / d
+  __device__ __forceinline__ void bind(const FkAttend& a, uint32_t kvh) {
+    base = ((size_t)a.slot[0] * a.kv_heads + kvh) * a.length;
+  }
+  __device__ __forceinline__ float4 k4(uint32_t t, uint32_t dd) const {
+    return E::widen4(__ldg(reinterpret_cast<const uint2*>(kc + (base + t) * kHeadDim + dd)));
+  }
+  __device__ __forceinline__ float4 v4(uint32_t t, uint32_t dd) const {
+    return E::widen4(__ldg(reinterpret_cast<const uint2*>(vc + (base + t) * kHeadDim + dd)));
+  }
+};
 
 template <class E>
-__global__ void __launch_bounds__(128) attend_prompt16_kernel(Attend16 f, float* __restrict__ out, uint32_t ldo,
-                                                              uint32_t max_pos) {
-  const FkAttend& a = f.a;
-  extern __shared__ float psm[];
-  float* qs = psm;                          // [32][128] the tile's rotated queries
-  float* kt = qs + kPromptTile * kHeadDim;  // [128][32] keys, transposed
-  float* vt = kt + kHeadDim * kPromptTile;  // [32][128] values
-  float* sc = vt + kPromptTile * kHeadDim;  // [32][max_pos + 1] scores
-  const uint32_t ncols = max_pos + 1;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint32_t r0 = blockIdx.x * kPromptTile, h = blockIdx.y;
-  const uint32_t rows = min((uint32_t)kPromptTile, a.m - r0);
-  const uint32_t kvh = h / (a.heads / a.kv_heads);
-  const size_t base = ((size_t)a.slot[0] * a.kv_heads + kvh) * a.length;
-  grid_wait();
-  grid_launch_dependents();
-
-  for (uint32_t i = warp; i < kPromptTile; i += 4) {
-    if (i < rows) {
-      const uint32_t r = r0 + i, p = a.pos[r];
-      for (uint32_t c = lane; c < kHeadDim / 2; c += 32) {
-        float q0, q1;
-        rope2(a.qkv + (size_t)r * a.ldq + a.q_off + (size_t)h * kHeadDim, c, kHeadDim / 2, a.rotated,
-              a.cos_t + (size_t)p * a.rotated, a.sin_t + (size_t)p * a.rotated, q0, q1);
-        qs[i * kHeadDim + c] = q0;
-        qs[i * kHeadDim + c + kHeadDim / 2] = q1;
-      }
-    }
-  }
-  uint32_t tile_max = 0;
-  for (uint32_t i = 0; i < rows; ++i) tile_max = max(tile_max, a.pos[r0 + i]);
-  const uint32_t keys = min(tile_max + 1, ncols);
-  __syncthreads();
-
-  float mx[kPromptTile / 4];
-#pragma unroll
-  for (int u = 0; u < kPromptTile / 4; ++u) mx[u] = -INFINITY;
-  for (uint32_t t0 = 0; t0 < keys; t0 += kPromptTile) {
-    for (uint32_t e = threadIdx.x; e < kPromptTile * kHeadDim; e += blockDim.x) {
-      const uint32_t k = e / kHeadDim, dd = e % kHeadDim;
-      kt[dd * kPromptTile + k] = t0 + k < keys ? E::widen(f.kc[(base + t0 + k) * kHeadDim + dd]) : 0.0f;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int u = 0; u < kPromptTile / 4; ++u) {
-      const uint32_t i = warp + 4 * u;
-      if (i < rows) {
-        const float* q = qs + i * kHeadDim;
-        float dot = 0.0f;
-        for (uint32_t dd = 0; dd < kHeadDim; ++dd) dot = __fadd_rn(dot, __fmul_rn(q[dd], kt[dd * kPromptTile + lane]));
-        const uint32_t t = t0 + lane;
-        const float s = __fmul_rn(dot, a.scale);
-        if (t <= a.pos[r0 + i] && t < ncols) {
-          sc[i * ncols + t] = s;
-          mx[u] = max_number(mx[u], s);
-        }
-      }
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int u = 0; u < kPromptTile / 4; ++u) mx[u] = warp_max(mx[u]);
-
-  float l[kPromptTile / 4];
-  float acc[kPromptTile / 4][4];
-#pragma unroll
-  for (int u = 0; u < kPromptTile / 4; ++u) {
-    l[u] = 0.0f;
-#pragma unroll
-    for (int jd = 0; jd < 4; ++jd) acc[u][jd] = 0.0f;
-  }
-  for (uint32_t t0 = 0; t0 < keys; t0 += kPromptTile) {
-    for (uint32_t e = threadIdx.x; e < kPromptTile * kHeadDim; e += blockDim.x) {
-      const uint32_t k = e / kHeadDim, dd = e % kHeadDim;
-      vt[e] = t0 + k < keys ? E::widen(f.vc[(base + t0 + k) * kHeadDim + dd]) : 0.0f;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int u = 0; u < kPromptTile / 4; ++u) {
-      const uint32_t i = warp + 4 * u;
-      if (i < rows) {
-        const uint32_t t = t0 + lane;
-        const float e = t <= a.pos[r0 + i] && t < ncols ? exp_rounded(__fsub_rn(sc[i * ncols + t], mx[u])) : 0.0f;
-        l[u] = __fadd_rn(l[u], e);
-        for (uint32_t k = 0; k < kPromptTile; ++k) {
-          const float ek = __shfl_sync(0xffffffffu, e, k);
-#pragma unroll
-          for (int jd = 0; jd < 4; ++jd)
-            acc[u][jd] = __fadd_rn(acc[u][jd], __fmul_rn(ek, vt[k * kHeadDim + lane + 32 * jd]));
-        }
-      }
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int u = 0; u < kPromptTile / 4; ++u) {
-    const uint32_t i = warp + 4 * u;
-    const float lt = warp_sum(l[u]);
-    if (i < rows) {
-#pragma unroll
-      for (int jd = 0; jd < 4; ++jd)
-        out[(size_t)(r0 + i) * ldo + (size_t)h * kHeadDim + lane + 32 * jd] = __fdiv_rn(acc[u][jd], lt);
-    }
-  }
+__global__ void __launch_bounds__(prompt::kThreads) attend_prompt16_kernel(Attend16 f, float* __restrict__ out,
+                                                                           uint32_t ldo, uint32_t max_pos) {
+  prompt::attend_prompt_body(f.a, Ring16PromptSrc<E>{f.kc, f.vc, 0}, out, ldo, max_pos);
 }
 
 template <class E, bool FUSED>
@@ -394,11 +308,13 @@ cudaError_t launch_attend16(const Attend16& f, cudaStream_t s) {
 }
 
 template <class E>
-cudaError_t launch_prompt16(const Attend16& f, float* out, uint32_t ldo, uint32_t max_pos, size_t smem, cudaStream_t s) {
+cudaError_t launch_prompt16(const Attend16& f, float* out, uint32_t ldo, uint32_t max_pos, cudaStream_t s) {
+  const size_t smem = prompt::kSmemBytes;
   cudaError_t e = fk_allow_smem(attend_prompt16_kernel<E>, smem);
   if (e != cudaSuccess) return e;
-  const dim3 grid((f.a.m + kPromptTile - 1) / kPromptTile, f.a.heads);
-  return fk_launch_ex(attend_prompt16_kernel<E>, grid, dim3(128), smem, s, f.a.pdl, f, out, ldo, max_pos);
+  const dim3 grid((f.a.m + prompt::kRows - 1) / prompt::kRows, f.a.heads);
+  return fk_launch_ex(attend_prompt16_kernel<E>, grid, dim3(prompt::kThreads), smem, s, f.a.pdl, f, out, ldo,
+                      max_pos);
 }
 
 }  // namespace kv16
@@ -447,14 +363,13 @@ cudaError_t fk_launch_attend_prompt16(const FkAttend& a, FkElem e, const uint16_
   if (a.d != fk::kv16::kHeadDim || a.kv_heads == 0 || a.heads % a.kv_heads != 0 || max_pos >= a.length || !kc ||
       !vc)
     return cudaErrorInvalidValue;
-  const size_t smem =
-      (3 * (size_t)fk::kv16::kPromptTile * fk::kv16::kHeadDim + (size_t)fk::kv16::kPromptTile * (max_pos + 1)) * 4;
-  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  if (ldo % 4 != 0 || ((uintptr_t)out % 16 | (uintptr_t)kc % 8 | (uintptr_t)vc % 8) != 0)
+    return cudaErrorInvalidValue;  // 16-byte stores, 8-byte loads
   fk::kv16::Attend16 f = {};
   f.a = a;
   f.kc = kc;
   f.vc = vc;
-#define CALL(E) fk::kv16::launch_prompt16<E>(f, out, ldo, max_pos, smem, s)
+#define CALL(E) fk::kv16::launch_prompt16<E>(f, out, ldo, max_pos, s)
   return FK_BY_ELEM16(e, CALL);
 #undef CALL
 }

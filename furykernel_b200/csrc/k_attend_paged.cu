@@ -26,6 +26,7 @@
 #include "fk_common.cuh"
 #include "fk_elem16.cuh"
 #include "fk_kernels.h"
+#include "fk_prompt.cuh"
 
 namespace fk {
 namespace paged {
@@ -34,7 +35,6 @@ constexpr int kAttWarps = 4;
 constexpr int kHeadDim = 128;
 constexpr int kMaxChunk = 256;
 constexpr uint32_t kMaxAttendRows = 16384;
-constexpr int kPromptTile = 32;
 
 // The element forms of a cache of type E: a pack of four elements widened
 // to f32, an element widened, an element stored (16-bit types: rounded to
@@ -327,116 +327,35 @@ __global__ void __launch_bounds__(128, 4) attend_paged_kernel(AttendArgs<E> f) {
   if (!waited) grid_launch_dependents();  // a block without items
 }
 
-// Attention over a prompt's rows of one sequence (prefill), the ring
-// prompt kernel's two passes (k_attend.cu): a block a (32 query rows,
-// head); keys and values 32 positions at a time into shared memory, through
-// row 0's block table (the prompt's rows share their sequence's table).
+// Attention over a prompt's rows of one sequence (prefill): the
+// register-tiled body of fk_prompt.cuh, positions through row 0's block
+// table (the prompt's rows share their sequence's table). A position whose
+// block is not in the table reads as zeros.
 template <class E>
-__global__ void __launch_bounds__(128) attend_prompt_paged_kernel(AttendArgs<E> f, float* __restrict__ out,
-                                                                  uint32_t ldo, uint32_t max_pos) {
-  const FkAttend& a = f.a;
-  extern __shared__ float psm[];
-  float* qs = psm;                          // [32][128] the tile's rotated queries
-  float* kt = qs + kPromptTile * kHeadDim;  // [128][32] keys, transposed
-  float* vt = kt + kHeadDim * kPromptTile;  // [32][128] values
-  float* sc = vt + kPromptTile * kHeadDim;  // [32][max_pos + 1] scores
-  const uint32_t ncols = max_pos + 1;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint32_t r0 = blockIdx.x * kPromptTile, h = blockIdx.y;
-  const uint32_t rows = min((uint32_t)kPromptTile, a.m - r0);
-  const uint32_t kvh = h / (a.heads / a.kv_heads);
-  grid_wait();
-  grid_launch_dependents();
+struct PagedPromptSrc {
+  Pool P;
+  uint32_t kvh, kv_heads;
+  __device__ __forceinline__ void bind(const FkAttend& a, uint32_t h) {
+    kvh = h;
+    kv_heads = a.kv_heads;
+  }
+  __device__ __forceinline__ float4 load(const uint64_t* blk, uint32_t t, uint32_t dd) const {
+    const uint64_t at = at_of(P, 0, t, kvh, kv_heads, kHeadDim);
+    if (at == ~0ull) return make_float4(0.f, 0.f, 0.f, 0.f);
+    const St<E>* p = elem_at<E>(blk, at) + dd;
+    if constexpr (E::kElem == FK_F32)
+      return __ldg(reinterpret_cast<const float4*>(p));
+    else
+      return E::widen4(__ldg(reinterpret_cast<const uint2*>(p)));
+  }
+  __device__ __forceinline__ float4 k4(uint32_t t, uint32_t dd) const { return load(P.kblk, t, dd); }
+  __device__ __forceinline__ float4 v4(uint32_t t, uint32_t dd) const { return load(P.vblk, t, dd); }
+};
 
-  for (uint32_t i = warp; i < kPromptTile; i += 4) {
-    if (i < rows) {
-      const uint32_t r = r0 + i, p = a.pos[r];
-      for (uint32_t c = lane; c < kHeadDim / 2; c += 32) {
-        float q0, q1;
-        rope2(a.qkv + (size_t)r * a.ldq + a.q_off + (size_t)h * kHeadDim, c, kHeadDim / 2, a.rotated,
-              a.cos_t + (size_t)p * a.rotated, a.sin_t + (size_t)p * a.rotated, q0, q1);
-        qs[i * kHeadDim + c] = q0;
-        qs[i * kHeadDim + c + kHeadDim / 2] = q1;
-      }
-    }
-  }
-  uint32_t tile_max = 0;
-  for (uint32_t i = 0; i < rows; ++i) tile_max = max(tile_max, a.pos[r0 + i]);
-  const uint32_t keys = min(tile_max + 1, ncols);
-  __syncthreads();
-
-  float mx[kPromptTile / 4];
-#pragma unroll
-  for (int u = 0; u < kPromptTile / 4; ++u) mx[u] = -INFINITY;
-  for (uint32_t t0 = 0; t0 < keys; t0 += kPromptTile) {
-    for (uint32_t e = threadIdx.x; e < kPromptTile * kHeadDim; e += blockDim.x) {
-      const uint32_t k = e / kHeadDim, dd = e % kHeadDim;
-      const uint64_t at = t0 + k < keys ? at_of(f.P, 0, t0 + k, kvh, a.kv_heads, kHeadDim) : ~0ull;
-      kt[dd * kPromptTile + k] = at != ~0ull ? ld_elem<E>(elem_at<E>(f.P.kblk, at) + dd) : 0.0f;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int u = 0; u < kPromptTile / 4; ++u) {
-      const uint32_t i = warp + 4 * u;
-      if (i < rows) {
-        const float* q = qs + i * kHeadDim;
-        float dot = 0.0f;
-        for (uint32_t dd = 0; dd < kHeadDim; ++dd) dot = __fadd_rn(dot, __fmul_rn(q[dd], kt[dd * kPromptTile + lane]));
-        const uint32_t t = t0 + lane;
-        const float s = __fmul_rn(dot, a.scale);
-        if (t <= a.pos[r0 + i] && t < ncols) {
-          sc[i * ncols + t] = s;
-          mx[u] = max_number(mx[u], s);
-        }
-      }
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int u = 0; u < kPromptTile / 4; ++u) mx[u] = warp_max(mx[u]);
-
-  float l[kPromptTile / 4];
-  float acc[kPromptTile / 4][4];
-#pragma unroll
-  for (int u = 0; u < kPromptTile / 4; ++u) {
-    l[u] = 0.0f;
-#pragma unroll
-    for (int jd = 0; jd < 4; ++jd) acc[u][jd] = 0.0f;
-  }
-  for (uint32_t t0 = 0; t0 < keys; t0 += kPromptTile) {
-    for (uint32_t e = threadIdx.x; e < kPromptTile * kHeadDim; e += blockDim.x) {
-      const uint32_t k = e / kHeadDim, dd = e % kHeadDim;
-      const uint64_t at = t0 + k < keys ? at_of(f.P, 0, t0 + k, kvh, a.kv_heads, kHeadDim) : ~0ull;
-      vt[e] = at != ~0ull ? ld_elem<E>(elem_at<E>(f.P.vblk, at) + dd) : 0.0f;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int u = 0; u < kPromptTile / 4; ++u) {
-      const uint32_t i = warp + 4 * u;
-      if (i < rows) {
-        const uint32_t t = t0 + lane;
-        const float e = t <= a.pos[r0 + i] && t < ncols ? exp_rounded(__fsub_rn(sc[i * ncols + t], mx[u])) : 0.0f;
-        l[u] = __fadd_rn(l[u], e);
-        for (uint32_t k = 0; k < kPromptTile; ++k) {
-          const float ek = __shfl_sync(0xffffffffu, e, k);
-#pragma unroll
-          for (int jd = 0; jd < 4; ++jd)
-            acc[u][jd] = __fadd_rn(acc[u][jd], __fmul_rn(ek, vt[k * kHeadDim + lane + 32 * jd]));
-        }
-      }
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int u = 0; u < kPromptTile / 4; ++u) {
-    const uint32_t i = warp + 4 * u;
-    const float lt = warp_sum(l[u]);
-    if (i < rows) {
-#pragma unroll
-      for (int jd = 0; jd < 4; ++jd)
-        out[(size_t)(r0 + i) * ldo + (size_t)h * kHeadDim + lane + 32 * jd] = __fdiv_rn(acc[u][jd], lt);
-    }
-  }
+template <class E>
+__global__ void __launch_bounds__(prompt::kThreads) attend_prompt_paged_kernel(AttendArgs<E> f, float* __restrict__ out,
+                                                                               uint32_t ldo, uint32_t max_pos) {
+  prompt::attend_prompt_body(f.a, PagedPromptSrc<E>{f.P, 0, 0}, out, ldo, max_pos);
 }
 
 template <class E>
@@ -493,8 +412,8 @@ cudaError_t launch_prompt(const FkAttend& a, const FkPaged& pg, const void* kc, 
   if (a.d != kHeadDim || a.kv_heads == 0 || a.heads % a.kv_heads != 0 || pg.block_size == 0 ||
       pg.table_len == 0 || !pg.table || !kc || !vc || (uint64_t)max_pos >= (uint64_t)pg.table_len * pg.block_size)
     return cudaErrorInvalidValue;
-  const size_t smem = (3 * (size_t)kPromptTile * kHeadDim + (size_t)kPromptTile * (max_pos + 1)) * 4;
-  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  if (ldo % 4 != 0 || (uintptr_t)out % 16 != 0) return cudaErrorInvalidValue;  // 16-byte stores
+  const size_t smem = prompt::kSmemBytes;
   auto kern = attend_prompt_paged_kernel<E>;
   cudaError_t e = fk_allow_smem(kern, smem);
   if (e != cudaSuccess) return e;
@@ -503,8 +422,8 @@ cudaError_t launch_prompt(const FkAttend& a, const FkPaged& pg, const void* kc, 
   f.a = a;
   f.P = Pool{pg.table, static_cast<const uint64_t*>(kc), static_cast<const uint64_t*>(vc), pg.block_size,
              pg.table_len, pg.blocks};
-  const dim3 grid((a.m + kPromptTile - 1) / kPromptTile, a.heads);
-  return fk_launch_ex(kern, grid, dim3(128), smem, s, a.pdl, f, out, ldo, max_pos);
+  const dim3 grid((a.m + prompt::kRows - 1) / prompt::kRows, a.heads);
+  return fk_launch_ex(kern, grid, dim3(prompt::kThreads), smem, s, a.pdl, f, out, ldo, max_pos);
 }
 
 }  // namespace paged

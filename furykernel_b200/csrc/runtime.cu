@@ -1188,7 +1188,7 @@ std::vector<KernelSpec> make_table() {
                 u32("q_off"), u32("k_off"), u32("v_off"), f32("scale")},
                l_attend_decode});
   t.push_back({"attend_prompt",
-               128,
+               256,
                {{"qkv", "read", "f32"},
                 {"cos", "read", "f32"},
                 {"sin", "read", "f32"},
@@ -1198,7 +1198,7 @@ std::vector<KernelSpec> make_table() {
                 {"v_cache", "read", "f32"},
                 {"out", "write", "f32"}},
                {dim("m", 1, 65535), dim("heads", 1, 1024), dim("kv_heads", 1, 1024), dim("d", 128, 128),
-                dim("length", 1, kMax), u32("rotated"), u32("ldq"), u32("q_off"), u32("ldo"), dim("max_pos", 0, 1407),
+                dim("length", 1, kMax), u32("rotated"), u32("ldq"), u32("q_off"), u32("ldo"), dim("max_pos", 0, kMax - 1),
                 f32("scale")},
                l_attend_prompt});
   t.push_back({"attend_combine",
@@ -1352,7 +1352,7 @@ std::vector<KernelSpec> make_table() {
                l_attend_decode_paged});
   t.back().tables = {{"k_cache", "read_write", "f32"}, {"v_cache", "read_write", "f32"}};
   t.push_back({"attend_prompt_paged",
-               128,
+               256,
                {{"qkv", "read", "f32"},
                 {"cos", "read", "f32"},
                 {"sin", "read", "f32"},
@@ -1361,7 +1361,7 @@ std::vector<KernelSpec> make_table() {
                 {"out", "write", "f32"}},
                {dim("m", 1, 65535), dim("heads", 1, 1024), dim("kv_heads", 1, 1024), dim("d", 128, 128),
                 dim("block_size", 1, 65536), dim("table_len", 1, kMax), dim("blocks", 1, kMax), u32("rotated"),
-                u32("ldq"), u32("q_off"), u32("ldo"), dim("max_pos", 0, 1407), f32("scale")},
+                u32("ldq"), u32("q_off"), u32("ldo"), dim("max_pos", 0, kMax - 1), f32("scale")},
                l_attend_prompt_paged});
   t.back().tables = {{"k_cache", "read", "f32"}, {"v_cache", "read", "f32"}};
   // Routed experts (Graph.hs:306-340).

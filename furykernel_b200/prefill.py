@@ -98,10 +98,10 @@ class Prefill:
         self.positions = positions or s.positions
         self.max_splits = (self.positions + self.chunk - 1) // self.chunk
         # One prompt (one slot) a run: the attention tiled by queries
-        # (attend_prompt), keys shared by 32 rows, instead of the decode
-        # attention over every row.
+        # (attend_prompt), each round of keys shared by 64 rows, instead of
+        # the decode attention over every row.
         span = s.table_len * s.block_size if s.paged else s.length
-        self.one_slot = one_slot and self.positions <= min(span, 1408)
+        self.one_slot = one_slot and self.positions <= span
         ms = R * s.heads * self.max_splits
         self.part = [ctx.zeros(ms), ctx.zeros(ms), ctx.zeros(ms * s.head_dim)]
         self.graphs: dict = {}

@@ -139,7 +139,7 @@ SPEC_KERNELS = {
                    _f32("v_cache"), _f32("out", "write")],
                   [_dim("m", 1, 65535), _dim("heads", 1, 1024), _dim("kv_heads", 1, 1024), _dim("d", 128, 128),
                    _dim("length", 1, _MAX), _u("rotated"), _u("ldq"), _u("q_off"), _u("ldo"),
-                   _dim("max_pos", 0, 1407), _f("scale")], threads=128),
+                   _dim("max_pos", 0, _MAX - 1), _f("scale")], threads=256),
         KernelSig("attend_combine",
                   [_f32("part_m"), _f32("part_l"), _f32("part_acc"), _u32("pos"), _f32("out", "write")],
                   [_dim("m", 1, 65535), _dim("heads", 1, 1024), _dim("d", 1, 1024), _dim("chunk", 1, 256),
@@ -220,8 +220,8 @@ SPEC_KERNELS = {
                   [_f32("qkv"), _f32("cos"), _f32("sin"), _u32("pos"), _u32("table"), _f32("out", "write")],
                   [_dim("m", 1, 65535), _dim("heads", 1, 1024), _dim("kv_heads", 1, 1024), _dim("d", 128, 128),
                    _dim("block_size", 1, 65536), _dim("table_len", 1, _MAX), _dim("blocks", 1, _MAX),
-                   _u("rotated"), _u("ldq"), _u("q_off"), _u("ldo"), _dim("max_pos", 0, 1407), _f("scale")],
-                  tables=[Table("k_cache", "read", "f32"), Table("v_cache", "read", "f32")], threads=128),
+                   _u("rotated"), _u("ldq"), _u("q_off"), _u("ldo"), _dim("max_pos", 0, _MAX - 1), _f("scale")],
+                  tables=[Table("k_cache", "read", "f32"), Table("v_cache", "read", "f32")], threads=256),
     ]
 }
 

@@ -327,7 +327,7 @@ def fake_prefill(eng, rows, chunk=None, positions=None, one_slot=False):
     p.chunk = chunk or eng.chunk
     p.positions = positions or s.positions
     p.max_splits = (p.positions + p.chunk - 1) // p.chunk
-    p.one_slot = one_slot and p.positions <= min(s.length, 1408)
+    p.one_slot = one_slot and p.positions <= s.length
     p.part = [Buf((7 << 44) + (i << 36)) for i in range(3)]
     p.moe = {}
     if s.experts:

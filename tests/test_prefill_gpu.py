@@ -44,15 +44,18 @@ def test_silu_pairs_bits(ctx):
     dy.free()
 
 
-def test_prompt_attention_within_bounds(ctx):
-    """attend_prompt (query-tiled, for prefill): 70 rows of one prompt at
-    positions 0..69 over the stored keys and values, within the f64
-    evaluator's bounds and 1e-4 normwise (its orders differ from the split
-    kernel's)."""
-    m, heads, kv_heads, length, d = 70, 4, 2, 96, 128
+@pytest.mark.parametrize("m,heads,kv_heads,length,start", [(70, 4, 2, 96, 0), (300, 4, 4, 512, 0), (1, 2, 1, 64, 0),
+                                                           (257, 2, 1, 1024, 700), (129, 3, 1, 2048, 1900)])
+def test_prompt_attention_within_bounds(ctx, m, heads, kv_heads, length, start):
+    """attend_prompt (query-tiled, for prefill): m rows of one prompt at
+    positions start..start+m-1 over the stored keys and values (a prompt
+    after `start` earlier positions; one ragged tile of 64 rows; rounds of
+    64 positions, the last one partial), within the f64 evaluator's bounds
+    and 1e-4 normwise (its orders differ from the split kernel's)."""
+    d = 128
     width = (heads + 2 * kv_heads) * d
-    qkv = O.normal(91, m * width).reshape(m, width)
-    pos = np.arange(m, dtype=np.uint32)
+    qkv = O.normal(91 + m, m * width).reshape(m, width)
+    pos = np.arange(start, start + m, dtype=np.uint32)
     slot = np.full(m, 1, np.uint32)
     kc = O.normal(92, 2 * kv_heads * length * d).reshape(2, kv_heads, length, d)
     vc = O.normal(93, 2 * kv_heads * length * d).reshape(2, kv_heads, length, d)
@@ -60,7 +63,8 @@ def test_prompt_attention_within_bounds(ctx):
     dcos, dsin = ctx.rope_tables(10000.0, d, d // 2, length)
     out = ctx.empty((m, heads * d))
     ctx.launch("attend_prompt", {"m": m, "heads": heads, "kv_heads": kv_heads, "d": d, "length": length,
-                                 "rotated": d // 2, "ldq": width, "q_off": 0, "ldo": heads * d, "max_pos": m - 1,
+                                 "rotated": d // 2, "ldq": width, "q_off": 0, "ldo": heads * d,
+                                 "max_pos": start + m - 1,
                                  "scale": 1.0 / math.sqrt(d)}, [dq, dcos, dsin, dpos, dslot, dkc, dvc, out])
     got = out.download()
     qref = O.r_rope(O.r_input(qkv[:, :heads * d]), d, d // 2, 10000.0, pos)
