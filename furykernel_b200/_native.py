@@ -58,6 +58,7 @@ def lib() -> ctypes.CDLL:
             "fkc_set_prefetch": (i32, [vp, u64]),
             "fkc_set_l2_prefetch": (i32, [vp, vp, u64]),
             "fkc_set_wait_stats": (i32, [vp, i32]),
+            "fkc_set_gemm_tile": (i32, [vp, ctypes.c_uint, ctypes.c_uint]),
             "fkc_read_wait_stats": (i32, [vp, ctypes.POINTER(u64), ctypes.POINTER(u64)]),
             "fkc_sync": (i32, [vp]),
             "fkc_status": (i32, [vp, ctypes.POINTER(i32)]),
@@ -294,6 +295,12 @@ class Context:
         """The bound of each wait on another rank, in microseconds (0: the
         default, about 2 s)."""
         check(lib().fkc_set_wait_limit(self.handle, microseconds))
+
+    def set_gemm_tile(self, tm: int, split: int = 1) -> None:
+        """gemm_tf32x3w's tile for later launches: tm A rows against 128 W
+        rows, K whole (split 1) or in two added halves (split 2); tm 0, the
+        shape's own pick."""
+        check(lib().fkc_set_gemm_tile(self.handle, tm, split))
 
     def set_wait_stats(self, on: bool) -> None:
         """Whether blocks that wait on their peers add their waits to the

@@ -162,12 +162,17 @@ cudaError_t fk_launch_split_tf32(const float* x, float* hi, float* lo, uint64_t 
 cudaError_t fk_launch_gemm_tf32x3(const float* a_hi, const float* a_lo, const float* w_hi, const float* w_lo,
                                   float* c, uint32_t M, uint32_t N, uint32_t K, uint32_t ldc, int* err,
                                   cudaStream_t s);
-// The 3xTF32 GEMM over f32 weights as they lie (W split inside the kernel),
-// 128 x tn tiles; fk_gemm_tf32x3w_tile picks tn for a shape.
-uint32_t fk_gemm_tf32x3w_tile(uint32_t M, uint32_t N, int sms);
+// The 3xTF32 GEMM over f32 weights as they lie (W split inside the kernel):
+// tiles of 128 W rows x tm A rows, K whole or split in two halves that add
+// into C; fk_gemm_tf32x3w_tile picks one for a shape.
+struct FkGemmTile {
+  uint32_t tm;
+  uint32_t split;  // 1 or 2
+};
+FkGemmTile fk_gemm_tf32x3w_tile(uint32_t M, uint32_t N, uint32_t K, int sms);
 cudaError_t fk_launch_gemm_tf32x3w(const float* a_hi, const float* a_lo, const float* w, float* c, uint32_t M,
-                                   uint32_t N, uint32_t K, uint32_t ldc, uint32_t tn, long long wait_cycles, int* err,
-                                   cudaStream_t s);
+                                   uint32_t N, uint32_t K, uint32_t ldc, FkGemmTile tile, long long wait_cycles,
+                                   int* err, cudaStream_t s);
 cudaError_t fk_launch_fill_normal(float* out, uint64_t n, uint64_t seed, double mu, double sigma, cudaStream_t s);
 cudaError_t fk_launch_fill_uniform(float* out, uint64_t n, uint64_t seed, double a, double b, cudaStream_t s);
 // 16-bit weights, bf16 or f16 (k_w16.cu): the f32 kernels' arithmetic over

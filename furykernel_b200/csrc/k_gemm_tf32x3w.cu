@@ -11,23 +11,28 @@
 //
 // The MMA computes the tile transposed, D = W A^T: a CTA owns 128 rows of W
 // (the MMA's M, one TMEM lane each) and tm rows of A (the MMA's N, tm a
-// multiple of 16 up to 256, chosen per shape by the launcher so that the
-// tiles fill the SMs in as few rounds as possible). W is the MMA's A
-// operand and lives in tensor memory: its split never touches shared
-// memory's MMA operand path, whose bandwidth the MMA's B operand needs. K
-// moves in slabs of 32 floats through `stages` buffers:
-//   warp 4      TMA: the slab's A_hi and A_lo rows and its 128 W rows
-//               (128-byte swizzle) into shared memory;
-//   warps 0..3  the W split: thread t reads row t of the W slab (its eight
-//               16-byte chunks, where the swizzle put them: conflict-free),
-//               splits the 32 floats in registers and stores the high and
-//               low parts into its TMEM lane (tcgen05.st); after the last
-//               slab, the epilogue: warp w reads lanes 32w..32w+31 of the
-//               accumulator (tcgen05.ld) and stores C, the lanes'
+// multiple of 16 up to 256). W is the MMA's A operand and lives in tensor
+// memory: its split never touches shared memory's MMA operand path, whose
+// bandwidth the MMA's B operand needs. K moves in slabs of 16 floats
+// (64-byte rows, 64-byte swizzle) through `stages` buffers:
+//   warp 4      TMA: the slab's A_hi and A_lo rows and its 128 W rows;
+//   warps 0..3  the W split: thread t reads row t of the W slab (its four
+//               16-byte chunks, where the swizzle put them), splits the 16
+//               floats in registers and stores the high and low parts into
+//               16 + 16 columns of its TMEM lane (tcgen05.st); after the
+//               last slab, the epilogue: warp w reads lanes 32w..32w+31 of
+//               the accumulator (tcgen05.ld) and stores C, the lanes'
 //               consecutive columns of a row of C together;
 //   warp 5      one thread issues tcgen05.mma kind::tf32 (128 x tm x 8, A
 //               from TMEM, B K-major from shared memory): hi*hi, lo*hi,
 //               hi*lo, into a TMEM accumulator of tm columns.
+// A kind::tf32 MMA costs about 140 SM cycles up to N = 176 and 168 at
+// N = 256 (measured on a B200, K 8): the wide tile nearly doubles the
+// flops an instruction, and 16-float slabs keep 5 stages of a 256-row
+// tile in shared memory. Shapes with fewer tiles than SMs split K in two
+// (grid z): each half adds its partial tile into C, which the launcher
+// zeroes first; two additions onto zero give the same bits in either
+// order, so the result does not depend on which half lands first.
 // Every wait is bounded: past its bound the kernel records a status code
 // (fkc_status), waits (bounded) for its own TMA loads in flight, frees its
 // TMEM and returns. No TMA multicast: every load reads this GPU's memory.
@@ -44,27 +49,41 @@ namespace gw {
 
 using namespace tc;
 
-constexpr uint32_t kBW = 128, kBK = 32;  // W rows a tile (TMEM lanes), K a slab
+constexpr uint32_t kBW = 128, kBK = 16;  // W rows a tile (TMEM lanes), K a slab
+constexpr uint32_t kRowBytes = kBK * 4;   // a slab's row: 64 bytes
 constexpr uint32_t kMaxTm = 256;
-constexpr uint32_t kTmemCols = 512;       // accumulator [0, 256), W stages from 256, 64 columns each
+constexpr uint32_t kTmemCols = 512;       // accumulator [0, 256), W stages from 256, 32 columns each
 constexpr uint32_t kWCol0 = 256;
 constexpr uint32_t kThreads = 192;        // 6 warps
-constexpr uint32_t kMaxStages = 4;
+constexpr uint32_t kMaxStages = 8;
 constexpr uint32_t kSmemBudget = 216 * 1024;
 constexpr uint32_t kSmemFloor = 120 * 1024;  // one CTA an SM: its TMEM allocation is all of TMEM
 
 // Status codes (first one wins), after gemm_tf32x3's 1..3.
 enum { GW_TIMEOUT_EMPTY = 4, GW_TIMEOUT_FULL = 5, GW_TIMEOUT_SPLIT = 6, GW_TIMEOUT_ACCUM = 7 };
 
-// A stage: A_hi then A_lo, tm rows of 128 bytes each, then the W slab's
-// 128 rows.
-constexpr uint32_t kWSlab = kBW * kBK * 4;  // 16 KiB
-__host__ __device__ constexpr uint32_t stage_bytes(uint32_t tm) { return 2 * tm * kBK * 4 + kWSlab; }
+// A stage: A_hi then A_lo, tm rows of 64 bytes each, then the W slab's 128
+// rows.
+constexpr uint32_t kWSlab = kBW * kRowBytes;  // 8 KiB
+__host__ __device__ constexpr uint32_t stage_bytes(uint32_t tm) { return 2 * tm * kRowBytes + kWSlab; }
 
 __device__ __forceinline__ uint32_t tf32_rna(float v) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
   return r;
+}
+
+// The shared-memory matrix descriptor of a K-major operand tile in the
+// 64-byte-swizzled canonical layout: rows of 64 bytes, 8-row atoms 512 bytes
+// apart (stride byte offset), descriptor version 1, swizzle mode 4.
+__device__ __forceinline__ uint64_t sw64_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)(16u >> 4) << 16;
+  d |= (uint64_t)(512u >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)4 << 61;
+  return d;
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -75,9 +94,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const uint32_t sb = stage_bytes(tm);
-  // Barriers after the ring: full[S] (the A slab's TMA bytes), split[S]
-  // (the four split warps stored the W slab), empty[S] (the slab's MMAs
-  // done: its shared and tensor memory free), accum (every MMA done).
+  // Barriers after the ring: full[S] (the slab's TMA bytes), split[S] (the
+  // four split warps stored the W slab), empty[S] (the slab's MMAs done:
+  // its shared and tensor memory free), accum (every MMA done).
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + stages * sb);
   uint64_t* full = bars;
   uint64_t* split = bars + kMaxStages;
@@ -88,9 +107,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // A tiles vary fastest: the CTAs that share a W tile run together, so it
-  // crosses HBM once and is reused from L2.
+  // crosses HBM once and is reused from L2. blockIdx.z: the K half.
   const uint32_t m0 = blockIdx.x * tm, n0 = blockIdx.y * kBW;
-  const uint32_t kblocks = K / kBK;
+  const uint32_t kblocks = K / kBK, per = (kblocks + gridDim.z - 1) / gridDim.z;
+  const uint32_t kbeg = blockIdx.z * per, kend = min(kblocks, kbeg + per);
+  const uint32_t nk = kend > kbeg ? kend - kbeg : 0;
 
   if (threadIdx.x == 0) {
     aborted = 0;
@@ -116,11 +137,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp < 4) {
     // The W split, a row a thread (TMEM lane 32 warp + lane). Chunk j of
-    // row r sits at chunk j ^ (r % 8) of the row (128-byte swizzle).
+    // row r sits at chunk j ^ ((r / 2) % 4) of the row (64-byte swizzle).
     const uint32_t row = 32 * warp + lane;
     const uint32_t lane_addr = tmem + ((32 * warp) << 16);
-    for (uint32_t kb = 0; kb < kblocks; ++kb) {
-      const uint32_t s = kb % stages, use = kb / stages;
+    for (uint32_t i = 0; i < nk; ++i) {
+      const uint32_t s = i % stages, use = i / stages;
       // One lane waits and tells the others, so that the warp stays together
       // for its warp-wide TMEM stores.
       int ready = 0;
@@ -130,21 +151,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         aborted = 1;
         break;
       }
-      const float4* wr = reinterpret_cast<const float4*>(smem + s * sb + 2 * tm * kBK * 4 + row * 128);
-      uint32_t hi[32], lo[32];
+      const float4* wr = reinterpret_cast<const float4*>(smem + s * sb + 2 * tm * kRowBytes + row * kRowBytes);
+      uint32_t hl[32];  // the high parts, then the low parts
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 v = wr[i ^ (row & 7)];
+      for (int j = 0; j < 4; ++j) {
+        const float4 v = wr[j ^ ((row >> 1) & 3)];
         const float x[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          hi[4 * i + j] = tf32_rna(x[j]);
-          lo[4 * i + j] = tf32_rna(__fsub_rn(x[j], __uint_as_float(hi[4 * i + j])));
+        for (int q = 0; q < 4; ++q) {
+          hl[4 * j + q] = tf32_rna(x[q]);
+          hl[16 + 4 * j + q] = tf32_rna(__fsub_rn(x[q], __uint_as_float(hl[4 * j + q])));
         }
       }
-      const uint32_t col = kWCol0 + 64 * s;
-      tmem_st32(lane_addr + col, hi);
-      tmem_st32(lane_addr + col + 32, lo);
+      tmem_st32(lane_addr + kWCol0 + 32 * s, hl);
       tmem_wait_st();
       fence_before();
       __syncwarp();
@@ -154,8 +173,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // The producer. `issued` counts the slabs whose loads went out, so that
     // after an abort it can wait for the ones still in flight.
     uint32_t issued = 0;
-    for (uint32_t kb = 0; kb < kblocks; ++kb) {
-      const uint32_t s = kb % stages, use = kb / stages;
+    for (uint32_t i = 0; i < nk; ++i) {
+      const uint32_t s = i % stages, use = i / stages;
       if (use > 0 && !mbar_wait(smem_u32(&empty[s]), (use - 1) & 1, wait_cycles)) {
         record(err, GW_TIMEOUT_EMPTY);
         aborted = 1;
@@ -165,27 +184,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint8_t* st = smem + s * sb;
       const uint32_t bar = smem_u32(&full[s]);
       mbar_expect_tx(bar, sb);
-      const int x = (int)(kb * kBK);
+      const int x = (int)((kbeg + i) * kBK);
       tma_load_2d(smem_u32(st), &ta_hi, x, (int)m0, bar);
-      tma_load_2d(smem_u32(st + tm * kBK * 4), &ta_lo, x, (int)m0, bar);
-      tma_load_2d(smem_u32(st + 2 * tm * kBK * 4), &tw, x, (int)n0, bar);
+      tma_load_2d(smem_u32(st + tm * kRowBytes), &ta_lo, x, (int)m0, bar);
+      tma_load_2d(smem_u32(st + 2 * tm * kRowBytes), &tw, x, (int)n0, bar);
       ++issued;
     }
     // Loads in flight finish before the CTA leaves (bounded).
     const uint32_t first = issued > stages ? issued - stages : 0;
-    for (uint32_t kb = first; kb < issued; ++kb)
-      if (!mbar_wait(smem_u32(&full[kb % stages]), (kb / stages) & 1, wait_cycles)) record(err, GW_TIMEOUT_FULL);
+    for (uint32_t i = first; i < issued; ++i)
+      if (!mbar_wait(smem_u32(&full[i % stages]), (i / stages) & 1, wait_cycles)) record(err, GW_TIMEOUT_FULL);
   } else if (warp == 5 && lane == 0) {
-    // The MMA issuer: three TF32 products a K step of 8, 4 steps a slab.
+    // The MMA issuer: three TF32 products a K step of 8, 2 steps a slab.
     const uint32_t idesc = tf32_idesc(tm, kBW);
     bool ok = true;
-    for (uint32_t kb = 0; kb < kblocks && ok; ++kb) {
-      const uint32_t s = kb % stages, use = kb / stages;
-      if (!mbar_wait(smem_u32(&full[s]), use & 1, wait_cycles)) {
-        record(err, GW_TIMEOUT_FULL);
-        ok = false;
-        break;
-      }
+    for (uint32_t i = 0; i < nk && ok; ++i) {
+      const uint32_t s = i % stages, use = i / stages;
       if (!mbar_wait(smem_u32(&split[s]), use & 1, wait_cycles)) {
         record(err, GW_TIMEOUT_SPLIT);
         ok = false;
@@ -193,15 +207,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_after();
       const uint32_t b_hi = smem_u32(smem + s * sb);
-      const uint32_t b_lo = b_hi + tm * kBK * 4;
-      const uint32_t w_hi = tmem + kWCol0 + 64 * s, w_lo = w_hi + 32;
+      const uint32_t b_lo = b_hi + tm * kRowBytes;
+      const uint32_t w_hi = tmem + kWCol0 + 32 * s, w_lo = w_hi + 16;
 #pragma unroll
       for (uint32_t kk = 0; kk < kBK / 8; ++kk) {
-        const uint32_t off = kk * 32;  // 8 floats of K within the 128-byte row
-        const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
-        mma_tf32_ts(tmem, w_hi + 8 * kk, sw128_desc(b_hi + off), idesc, acc);
-        mma_tf32_ts(tmem, w_lo + 8 * kk, sw128_desc(b_hi + off), idesc, 1u);
-        mma_tf32_ts(tmem, w_hi + 8 * kk, sw128_desc(b_lo + off), idesc, 1u);
+        const uint32_t off = kk * 32;  // 8 floats of K within the 64-byte row
+        const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+        mma_tf32_ts(tmem, w_hi + 8 * kk, sw64_desc(b_hi + off), idesc, acc);
+        mma_tf32_ts(tmem, w_lo + 8 * kk, sw64_desc(b_hi + off), idesc, 1u);
+        mma_tf32_ts(tmem, w_hi + 8 * kk, sw64_desc(b_lo + off), idesc, 1u);
       }
       mma_commit(smem_u32(&empty[s]));  // the slab's buffers are free once these finish
     }
@@ -209,10 +223,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!ok) aborted = 1;
   }
 
-  if (warp < 4) {
+  if (warp < 4 && nk > 0) {
     // The epilogue: lane 32w + l of the accumulator is W row n0 + 32w + l,
     // column j is A row m0 + j; C[m0 + j][n] from each, a row of C's 32
-    // consecutive columns a store instruction across the warp.
+    // consecutive columns a store (or, K split, an addition) across the warp.
     int done = 0;
     if (lane == 0) done = mbar_wait(smem_u32(accum), 0, wait_cycles) ? 1 : 0;
     done = __shfl_sync(0xffffffffu, done, 0);
@@ -221,23 +235,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (!__shfl_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&aborted), 0)) {
       fence_after();
       const uint32_t n = n0 + 32 * warp + lane;
-      const bool live = n < N;
+      const bool live = n < N, add = gridDim.z > 1;
 #pragma unroll 1
-      for (uint32_t cc = 0; cc < tm; cc += 32) {
-        const uint32_t taddr = tmem + ((32 * warp) << 16) + cc;
-        if (cc + 32 <= tm) {
-          uint32_t r[32];
-          tmem_ld32(taddr, r);
+      for (uint32_t cc = 0; cc < tm; cc += 16) {
+        uint32_t r[16];
+        tmem_ld16(tmem + ((32 * warp) << 16) + cc, r);
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (live && m0 + cc + j < M) c[(size_t)(m0 + cc + j) * ldc + n] = __uint_as_float(r[j]);
-        } else {
-          uint32_t r[16];
-          tmem_ld16(taddr, r);
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (live && m0 + cc + j < M) c[(size_t)(m0 + cc + j) * ldc + n] = __uint_as_float(r[j]);
-        }
+        for (int j = 0; j < 16; ++j)
+          if (live && m0 + cc + j < M) {
+            float* at = c + (size_t)(m0 + cc + j) * ldc + n;
+            if (add)
+              atomicAdd(at, __uint_as_float(r[j]));
+            else
+              *at = __uint_as_float(r[j]);
+          }
       }
     }
   }
@@ -265,8 +276,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn_w() {
   return fn;
 }
 
-// A row-major [rows, K] f32 matrix as TMA tiles of 32 x box_rows (x = K),
-// 128-byte swizzle; rows past the matrix read as zeros.
+// A row-major [rows, K] f32 matrix as TMA tiles of 16 x box_rows (x = K),
+// 64-byte swizzle; rows past the matrix read as zeros.
 bool make_map_w(CUtensorMap* map, const float* base, uint32_t rows, uint32_t K, uint32_t box_rows) {
   auto fn = encode_fn_w();
   if (!fn) return false;
@@ -275,38 +286,45 @@ bool make_map_w(CUtensorMap* map, const float* base, uint32_t rows, uint32_t K, 
   cuuint32_t box[2] = {fk::gw::kBK, box_rows};
   cuuint32_t estr[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
 
-// The A rows a tile for M x N on `sms` SMs: among 16, 32, ..., 256, the
-// one whose tiles (128 W rows each) take the fewest rounds, rounds x
-// (tm + 24) (a tile's fixed cost counted as 24 rows), the wider on a tie.
-uint32_t fk_gemm_tf32x3w_tile(uint32_t M, uint32_t N, int sms) {
-  const uint64_t wt = (N + fk::gw::kBW - 1) / fk::gw::kBW;
-  uint32_t best = 256;
-  uint64_t best_cost = ~0ull;
-  for (uint32_t tm = 256; tm >= 16; tm -= 16) {
-    const uint64_t tiles = wt * ((M + tm - 1) / tm);
-    const uint64_t rounds = (tiles + (uint64_t)sms - 1) / (uint64_t)sms;
-    const uint64_t cost = rounds * (tm + 24);
-    if (cost < best_cost) {
-      best_cost = cost;
-      best = tm;
+// The tile for M x N x K on `sms` SMs: tm among 16, 32, ..., 256 and K
+// split in 1 or 2, the least modelled time: rounds of CTAs x (slabs a CTA x
+// a slab's cost + the epilogue), with a 16-float slab's cost 350 + 0.62 tm
+// SM cycles (from the measured MMA costs above) and an epilogue of
+// 8 tm cycles, twice that when it adds.
+FkGemmTile fk_gemm_tf32x3w_tile(uint32_t M, uint32_t N, uint32_t K, int sms) {
+  FkGemmTile best = {256, 1};
+  double best_cost = 1e300;
+  const uint64_t wt = (N + fk::gw::kBW - 1) / fk::gw::kBW, kblocks = K / fk::gw::kBK;
+  for (uint32_t split = 1; split <= 2; ++split) {
+    if (split == 2 && kblocks < 8) break;
+    for (uint32_t tm = 256; tm >= 16; tm -= 16) {
+      const uint64_t ctas = wt * ((M + tm - 1) / tm) * split;
+      const uint64_t rounds = (ctas + (uint64_t)sms - 1) / (uint64_t)sms;
+      const double slab = 693.0 + 1.23 * tm;
+      const double cost = (double)rounds * ((double)((kblocks + split - 1) / split) * slab + 8.0 * tm * split);
+      if (cost < best_cost) {
+        best_cost = cost;
+        best = {tm, split};
+      }
     }
   }
   return best;
 }
 
 cudaError_t fk_launch_gemm_tf32x3w(const float* a_hi, const float* a_lo, const float* w, float* c, uint32_t M,
-                                   uint32_t N, uint32_t K, uint32_t ldc, uint32_t tm, long long wait_cycles, int* err,
-                                   cudaStream_t s) {
+                                   uint32_t N, uint32_t K, uint32_t ldc, FkGemmTile tile, long long wait_cycles,
+                                   int* err, cudaStream_t s) {
   using namespace fk::gw;
   if (M == 0 || N == 0) return cudaSuccess;
+  const uint32_t tm = tile.tm;
   if (K == 0 || K % kBK != 0 || tm == 0 || tm % 16 != 0 || tm > kMaxTm || ldc < N ||
-      ((uintptr_t)a_hi | (uintptr_t)a_lo | (uintptr_t)w) & 15)
+      (tile.split != 1 && tile.split != 2) || ((uintptr_t)a_hi | (uintptr_t)a_lo | (uintptr_t)w) & 15)
     return cudaErrorInvalidValue;
   uint32_t stages = kSmemBudget / stage_bytes(tm);
   if (stages > kMaxStages) stages = kMaxStages;
@@ -320,7 +338,12 @@ cudaError_t fk_launch_gemm_tf32x3w(const float* a_hi, const float* a_lo, const f
   if (e != cudaSuccess) return e;
   const uint32_t wtiles = (N + kBW - 1) / kBW;
   if (wtiles > 65535) return cudaErrorInvalidValue;
-  dim3 grid((M + tm - 1) / tm, wtiles);
+  if (tile.split > 1) {
+    // The halves add into C: zero it first (in the launch's stream order).
+    e = cudaMemset2DAsync(c, (size_t)ldc * 4, 0, (size_t)N * 4, M, s);
+    if (e != cudaSuccess) return e;
+  }
+  dim3 grid((M + tm - 1) / tm, wtiles, tile.split);
   gemm_tf32x3w_kernel<<<grid, kThreads, smem, s>>>(ma_hi, ma_lo, mw, c, M, N, K, ldc, tm, stages,
                                                     wait_cycles > 0 ? wait_cycles : 4000000000LL, err);
   return cudaGetLastError();

@@ -75,6 +75,7 @@ struct fkc_ctx {
   size_t prefetch = 0;  // fkc_set_prefetch: the streaming GEMVs' L2 prefetch budget
   const void* l2pf = nullptr;  // fkc_set_l2_prefetch: a range the attention launches prefetch
   unsigned long long l2pf_bytes = 0;
+  FkGemmTile gemm_tile = {0, 1};  // fkc_set_gemm_tile: tm 0 = the shape's own pick
 };
 
 struct fkc_graph {
@@ -167,6 +168,15 @@ extern "C" int fkc_set_l2_prefetch(fkc_ctx* c, const void* p, unsigned long long
                                   "16 bytes.");
   c->l2pf = bytes ? p : nullptr;
   c->l2pf_bytes = p ? bytes : 0;
+  return FKC_OK;
+}
+
+extern "C" int fkc_set_gemm_tile(fkc_ctx* c, unsigned tm, unsigned split) {
+  if (!c) return fail(FKC_ERR_ARGUMENT, "fkc_set_gemm_tile: null context.");
+  if (tm != 0 && (tm > 256 || tm % 16 != 0))
+    return fail(FKC_ERR_ARGUMENT, "fkc_set_gemm_tile: tm %u is not a multiple of 16 in 16..256.", tm);
+  if (split != 1 && split != 2) return fail(FKC_ERR_ARGUMENT, "fkc_set_gemm_tile: split %u is not 1 or 2.", split);
+  c->gemm_tile = {tm, split};
   return FKC_OK;
 }
 
@@ -633,14 +643,15 @@ int l_gemm_tf32x3(fkc_ctx* c, const Params& p, void* const* bufs) {
 
 // gemm_tf32x3w: a a_hi a_lo w c | M N K ldc. A is split into the caller's
 // a_hi / a_lo first; W (f32, as the weight arena holds it) is split inside
-// the kernel. The tile width is the shape's (fk_gemm_tf32x3w_tile).
+// the kernel. The tile is the shape's (fk_gemm_tf32x3w_tile), or the one
+// fkc_set_gemm_tile set.
 int l_gemm_tf32x3w(fkc_ctx* c, const Params& p, void* const* bufs) {
   const uint32_t M = p.u(0), N = p.u(1), K = p.u(2), ldc = p.u(3);
   if (ldc < N) return fail(FKC_ERR_ARGUMENT, "gemm_tf32x3w: ldc %u is less than N %u.", ldc, N);
-  const uint32_t tn = fk_gemm_tf32x3w_tile(M, N, c->sms);
+  const FkGemmTile tile = c->gemm_tile.tm ? c->gemm_tile : fk_gemm_tf32x3w_tile(M, N, K, c->sms);
   cudaError_t e = fk_launch_split_tf32(CF(0), F(1), F(2), (uint64_t)M * K, c->stream);
   if (e == cudaSuccess)
-    e = fk_launch_gemm_tf32x3w(CF(1), CF(2), CF(3), F(4), M, N, K, ldc, tn, c->peers.wait_cycles, c->status,
+    e = fk_launch_gemm_tf32x3w(CF(1), CF(2), CF(3), F(4), M, N, K, ldc, tile, c->peers.wait_cycles, c->status,
                                c->stream);
   return launched(e, "gemm_tf32x3w");
 }
@@ -1244,13 +1255,13 @@ std::vector<KernelSpec> make_table() {
                {dim("M", 1, 1048576), dim("N", 1, 1048576), dim("K", 32, 1048576, 32), u32("ldc")},
                l_gemm_tf32x3});
   t.push_back({"gemm_tf32x3w",
-               320,
+               192,
                {{"a", "read", "f32"},
                 {"a_hi", "read_write", "f32"},
                 {"a_lo", "read_write", "f32"},
                 {"w", "read", "f32"},
                 {"c", "write", "f32"}},
-               {dim("M", 1, 1048576), dim("N", 1, 1048576), dim("K", 32, 1048576, 32), u32("ldc")},
+               {dim("M", 1, 1048576), dim("N", 1, 1048576), dim("K", 16, 1048576, 16), u32("ldc")},
                l_gemm_tf32x3w});
   t.push_back({"argmax_pairs",
                1024,

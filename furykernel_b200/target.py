@@ -159,8 +159,8 @@ SPEC_KERNELS = {
                   threads=192),
         KernelSig("gemm_tf32x3w",
                   [_f32("a"), _f32("a_hi", "read_write"), _f32("a_lo", "read_write"), _f32("w"), _f32("c", "write")],
-                  [_dim("M", 1, 1048576), _dim("N", 1, 1048576), _dim("K", 32, 1048576, 32), _u("ldc")],
-                  threads=320),
+                  [_dim("M", 1, 1048576), _dim("N", 1, 1048576), _dim("K", 16, 1048576, 16), _u("ldc")],
+                  threads=192),
         KernelSig("argmax_pairs", [_f32("x"), _u32("pairs", "write")],
                   [_dim("m", 1, 65535), _dim("n", 1, _MAX), _u("ldx"), _u("offset")], threads=1024),
         KernelSig("argmax_pick", [_u32("pairs"), _u32("ids", "write")], [_dim("shards", 1, 64), _dim("m", 1, 65535)]),
