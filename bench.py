@@ -584,7 +584,7 @@ def run_gemm(args):
             "data": "synthetic: A N(0,1), W N(0,0.02), seeded on the device",
             "config": {"workload": "config 3c prefill GEMM [512 x 4096] x [4096 x 11008]", "M": M, "K": K, "N": NN,
                        "parallelism": f"column split over {world}", "status": status, "kernel": kernel,
-                       "tile": "%d rows of A x 128 rows of W, K in %d" % gemm_tile(M, n, K, ctx.sms),
+                       "tile": "%d rows of A x 128 rows of W on %d CTAs" % gemm_tile(M, n, K, ctx.sms),
                        "l2": "inputs 8 + 180 MB per call (> L2 for the weights)"},
             "roofline": {"bound": "tensor", "achieved": 3 * tflops, "peak": tf32_peak, "unit": "TFLOP/s",
                          "frac": 3 * tflops / tf32_peak, "traffic": None, "peak_kind": kind,
@@ -601,18 +601,22 @@ def run_gemm(args):
 
 def gemm_tile(M: int, N: int, K: int, sms: int) -> tuple:
     """gemm_tf32x3w's tile for M x N x K (the launcher's rule, restated):
-    (tm A rows against 128 W rows, K split in 1 or 2), the least modelled
-    time: rounds x (slabs of 16 a CTA x (693 + 1.23 tm) + 8 tm x split)."""
-    wt, kb = (N + 127) // 128, K // 16
+    (tm A rows against 128 W rows, G CTAs), G = tiles, 2 tiles or (more
+    tiles than SMs) sms, the least modelled time: a CTA's slabs of 16 x
+    6 (138 + 0.117 tm) + its pieces x (500 + 8 tm)."""
+    wt, S = (N + 127) // 128, K // 16
     best, best_cost = (256, 1), float("inf")
-    for split in (1, 2):
-        if split == 2 and kb < 8:
-            break
-        for tm in range(256, 15, -16):
-            rounds = -(-wt * -(-M // tm) * split // sms)
-            cost = rounds * (-(-kb // split) * (693.0 + 1.23 * tm) + 8.0 * tm * split)
+    for tm in range(256, 15, -16):
+        tiles = wt * -(-M // tm)
+        slab, epi = 6 * (138.0 + 0.117 * tm), 500.0 + 8.0 * tm
+        for g, G in enumerate((tiles, 2 * tiles, sms)):
+            if G > sms or (g == 1 and S < 2) or (g == 2 and tiles <= sms):
+                continue
+            per = -(-tiles * S // G)
+            pieces = 1.0 if g < 2 else -(-per // S) + 1.0
+            cost = per * slab + pieces * epi
             if cost < best_cost:
-                best, best_cost = (tm, split), cost
+                best, best_cost = (tm, G), cost
     return best
 
 

@@ -296,11 +296,12 @@ class Context:
         default, about 2 s)."""
         check(lib().fkc_set_wait_limit(self.handle, microseconds))
 
-    def set_gemm_tile(self, tm: int, split: int = 1) -> None:
+    def set_gemm_tile(self, tm: int, parts: int = 1) -> None:
         """gemm_tf32x3w's tile for later launches: tm A rows against 128 W
-        rows, K whole (split 1) or in two added halves (split 2); tm 0, the
+        rows; parts 1, a tile a CTA; 2, two K halves a tile; 0, an equal
+        share of the slabs to each of min(tiles, SMs) CTAs. tm 0, the
         shape's own pick."""
-        check(lib().fkc_set_gemm_tile(self.handle, tm, split))
+        check(lib().fkc_set_gemm_tile(self.handle, tm, parts))
 
     def set_wait_stats(self, on: bool) -> None:
         """Whether blocks that wait on their peers add their waits to the

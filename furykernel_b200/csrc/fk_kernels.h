@@ -163,11 +163,13 @@ cudaError_t fk_launch_gemm_tf32x3(const float* a_hi, const float* a_lo, const fl
                                   float* c, uint32_t M, uint32_t N, uint32_t K, uint32_t ldc, int* err,
                                   cudaStream_t s);
 // The 3xTF32 GEMM over f32 weights as they lie (W split inside the kernel):
-// tiles of 128 W rows x tm A rows, K whole or split in two halves that add
-// into C; fk_gemm_tf32x3w_tile picks one for a shape.
+// tiles of 128 W rows x tm A rows on `grid` CTAs, each an equal share of
+// the tiles' K slabs (grid = tiles: a tile each; 2 tiles: two halves each;
+// fewer than the tiles: at most two CTAs a tile, their parts added into
+// C); fk_gemm_tf32x3w_tile picks one for a shape.
 struct FkGemmTile {
   uint32_t tm;
-  uint32_t split;  // 1 or 2
+  uint32_t grid;
 };
 FkGemmTile fk_gemm_tf32x3w_tile(uint32_t M, uint32_t N, uint32_t K, int sms);
 cudaError_t fk_launch_gemm_tf32x3w(const float* a_hi, const float* a_lo, const float* w, float* c, uint32_t M,

@@ -8,6 +8,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
 #include <mutex>
 #include <string>
 #include <unordered_set>
@@ -75,7 +76,7 @@ struct fkc_ctx {
   size_t prefetch = 0;  // fkc_set_prefetch: the streaming GEMVs' L2 prefetch budget
   const void* l2pf = nullptr;  // fkc_set_l2_prefetch: a range the attention launches prefetch
   unsigned long long l2pf_bytes = 0;
-  FkGemmTile gemm_tile = {0, 1};  // fkc_set_gemm_tile: tm 0 = the shape's own pick
+  unsigned gemm_tm = 0, gemm_parts = 1;  // fkc_set_gemm_tile: tm 0 = the shape's own pick
 };
 
 struct fkc_graph {
@@ -171,12 +172,13 @@ extern "C" int fkc_set_l2_prefetch(fkc_ctx* c, const void* p, unsigned long long
   return FKC_OK;
 }
 
-extern "C" int fkc_set_gemm_tile(fkc_ctx* c, unsigned tm, unsigned split) {
+extern "C" int fkc_set_gemm_tile(fkc_ctx* c, unsigned tm, unsigned parts) {
   if (!c) return fail(FKC_ERR_ARGUMENT, "fkc_set_gemm_tile: null context.");
   if (tm != 0 && (tm > 256 || tm % 16 != 0))
     return fail(FKC_ERR_ARGUMENT, "fkc_set_gemm_tile: tm %u is not a multiple of 16 in 16..256.", tm);
-  if (split != 1 && split != 2) return fail(FKC_ERR_ARGUMENT, "fkc_set_gemm_tile: split %u is not 1 or 2.", split);
-  c->gemm_tile = {tm, split};
+  if (parts > 2) return fail(FKC_ERR_ARGUMENT, "fkc_set_gemm_tile: parts %u is not 0, 1 or 2.", parts);
+  c->gemm_tm = tm;
+  c->gemm_parts = parts;
   return FKC_OK;
 }
 
@@ -648,7 +650,14 @@ int l_gemm_tf32x3(fkc_ctx* c, const Params& p, void* const* bufs) {
 int l_gemm_tf32x3w(fkc_ctx* c, const Params& p, void* const* bufs) {
   const uint32_t M = p.u(0), N = p.u(1), K = p.u(2), ldc = p.u(3);
   if (ldc < N) return fail(FKC_ERR_ARGUMENT, "gemm_tf32x3w: ldc %u is less than N %u.", ldc, N);
-  const FkGemmTile tile = c->gemm_tile.tm ? c->gemm_tile : fk_gemm_tf32x3w_tile(M, N, K, c->sms);
+  FkGemmTile tile = fk_gemm_tf32x3w_tile(M, N, K, c->sms);
+  if (c->gemm_tm) {
+    const uint64_t tiles = (uint64_t)((N + 127) / 128) * ((M + c->gemm_tm - 1) / c->gemm_tm);
+    const uint64_t g = c->gemm_parts == 1 ? tiles : c->gemm_parts == 2 ? 2 * tiles
+                                                                       : std::min<uint64_t>(tiles, c->sms);
+    if (g > 0x7fffffffull) return fail(FKC_ERR_ARGUMENT, "gemm_tf32x3w: %llu CTAs for the set tile.", (unsigned long long)g);
+    tile = {c->gemm_tm, (uint32_t)g};
+  }
   cudaError_t e = fk_launch_split_tf32(CF(0), F(1), F(2), (uint64_t)M * K, c->stream);
   if (e == cudaSuccess)
     e = fk_launch_gemm_tf32x3w(CF(1), CF(2), CF(3), F(4), M, N, K, ldc, tile, c->peers.wait_cycles, c->status,

@@ -82,10 +82,13 @@ int fkc_set_prefetch(fkc_ctx *ctx, unsigned long long bytes);
  * none (the default). A launch setting like fkc_set_pdl. */
 int fkc_set_l2_prefetch(fkc_ctx *ctx, const void *p, unsigned long long bytes);
 /* The tile of later gemm_tf32x3w launches: tm A rows (a multiple of 16 up
- * to 256) against 128 W rows, K whole (split 1) or in two halves that add
- * into C (split 2). tm 0 (the default): each launch picks its shape's tile.
- * A launch setting like fkc_set_pdl, for tuning and tests. */
-int fkc_set_gemm_tile(fkc_ctx *ctx, unsigned tm, unsigned split);
+ * to 256) against 128 W rows, and how the tiles' K slabs go to CTAs: parts
+ * 1, a tile a CTA; 2, each tile in two halves; 0, an equal share of all
+ * the slabs to each of min(tiles, SMs) CTAs (a tile in at most two). Parts
+ * of a tile add into C (zeroed first). tm 0 (the default): each launch
+ * picks its shape's tile. A launch setting like fkc_set_pdl, for tuning
+ * and tests. */
+int fkc_set_gemm_tile(fkc_ctx *ctx, unsigned tm, unsigned parts);
 int fkc_sync(fkc_ctx *ctx);
 /* Synchronizes, then reads and clears the context's device status word:
  * 0, or the code a kernel with bounded waits recorded when one ran out

@@ -98,18 +98,22 @@ def test_gemm_tf32x3w_within_bounds_and_as_split_kernel(ctx, M, N, K):
     assert np.max(np.abs(c.astype(np.float64) - c0)) <= np.max(np.abs(c0)) * 2.0 ** -14
 
 
-# Tiles set by hand (fkc_set_gemm_tile): the widest tile with K whole and
-# split in two halves that add into C, the narrowest, and an odd width; a
-# ragged shape (M, N not multiples of the tile, K a multiple of 16 but not
-# of 32) and config 5's down projection. The halves' sum is exact in either
-# order (two additions onto zero), so every tile is held to the same bounds.
-@pytest.mark.parametrize("M,N,K,tm,split", [(300, 1000, 4112, 256, 2), (300, 1000, 4112, 256, 1),
+# Tiles set by hand (fkc_set_gemm_tile): the widest tile with K whole, in
+# two halves that add into C, and in equal shares over the SMs (a tile in
+# two CTAs, pieces of any length); the narrowest and an odd width; a ragged
+# shape (M, N not multiples of the tile, K a multiple of 16 but not of 32,
+# an odd number of slabs), config 5's down projection and config 3c. Two
+# parts of a tile add onto zero, the same bits in either order, so every
+# tile gives the same bits run after run and is held to the same bounds.
+@pytest.mark.parametrize("M,N,K,tm,parts", [(300, 1000, 4112, 256, 2), (300, 1000, 4112, 256, 1),
                                             (300, 1000, 4112, 16, 2), (300, 1000, 4112, 48, 1),
-                                            (511, 4096, 11008, 256, 2), (64, 384, 48, 32, 2)])
-def test_gemm_tf32x3w_set_tiles(ctx, M, N, K, tm, split):
+                                            (511, 4096, 11008, 256, 2), (64, 384, 48, 32, 2),
+                                            (300, 4000, 4112, 16, 0), (512, 11008, 4096, 256, 0),
+                                            (300, 1000, 4112, 32, 0)])
+def test_gemm_tf32x3w_set_tiles(ctx, M, N, K, tm, parts):
     a = O.normal(7 + M, M * K).reshape(M, K)
     w = O.normal(8 + N, N * K, 0.0, 0.02).reshape(N, K)
-    ctx.set_gemm_tile(tm, split)
+    ctx.set_gemm_tile(tm, parts)
     try:
         c, status = gemm_w(ctx, a, w)
         c2, status2 = gemm_w(ctx, a, w)
