@@ -233,8 +233,10 @@ def kv_length(b: int) -> int:
 # kernel and shape (dram__bytes_read.sum + dram__bytes_write.sum, one
 # capture each; the summaries under profiles/ give the commands).
 NCU_TRAFFIC = {
-    ("gemv_rmsnorm", 32000, 4096, 1): (524.35e6 + 3.43e6, "profiles/gemv_stream_lm_head_b1.md"),
+    ("gemv_rmsnorm_silu", 22016, 4096, 1): (360.78e6 + 3.81e6, "profiles/gemv_stream_gateup_b1.md"),
+    ("gemv_rmsnorm", 32000, 4096, 1): (524.35e6 + 3.51e6, "profiles/gemv_stream_lm_head_b1.md"),
     ("gemv", 11008, 4096, 16): (180.90e6 + 3.87e6, "profiles/gemv_batch_b16.md"),
+    ("gemm_tf32x3w", 512, 11008, 4096): (285.73e6 + 22.33e6, "profiles/gemm_tf32x3w_3c.md"),
 }
 
 
@@ -587,7 +589,9 @@ def run_gemm(args):
                        "tile": "%d rows of A x 128 rows of W on %d CTAs" % gemm_tile(M, n, K, ctx.sms),
                        "l2": "inputs 8 + 180 MB per call (> L2 for the weights)"},
             "roofline": {"bound": "tensor", "achieved": 3 * tflops, "peak": tf32_peak, "unit": "TFLOP/s",
-                         "frac": 3 * tflops / tf32_peak, "traffic": None, "peak_kind": kind,
+                         "frac": 3 * tflops / tf32_peak,
+                         "traffic": NCU_TRAFFIC[("gemm_tf32x3w", M, NN, K)][0] if world == 1 else None,
+                         "traffic_source": NCU_TRAFFIC[("gemm_tf32x3w", M, NN, K)][1], "peak_kind": kind,
                          "note": "achieved counts the 3 TF32 products the tensor pipe runs"},
             "gpu_launches": 2 * args.steps, "clocks": clk.summary(),  # split_tf32 of A, then the GEMM (+ a memset node)
         }
