@@ -722,18 +722,32 @@ def run_kernel_config(args):
         # in rotation, so that each launch streams its weights from HBM.
         n, kern = (22016, "gemv_rmsnorm_silu") if cfg == "5g" else (32000, "gemv_rmsnorm")
         k = 4096
-        x, g, y = ctx.empty((1, k)), ctx.empty(k), ctx.empty((1, n))
+        # --weights bf16 / f16: the 16-bit form of the launch (weights and
+        # gain in that type, x and y f32), as the config-5 step with those
+        # weights launches it.
+        wt = args.weights
+        eb = 4 if wt == "f32" else 2
+        kern += {"f32": "", "bf16": "_wbf16", "f16": "_wf16"}[wt]
+        x, y = ctx.empty((1, k)), ctx.empty((1, n))
         ctx.fill_normal(x, 2, 0.0, 1.0)
-        ctx.fill_uniform(g, 3, 0.5, 1.5)
-        ws = [ctx.empty((n, k)) for _ in range(4)]
+        if wt == "f32":
+            g = ctx.empty(k)
+            ctx.fill_uniform(g, 3, 0.5, 1.5)
+        else:
+            g = ctx.empty(k, np.uint16)
+            (ctx.fill_normal_bf16 if wt == "bf16" else ctx.fill_normal_f16)(g, 3, 1.0, 0.25)
+        ws = [ctx.empty((n, k), np.float32 if wt == "f32" else np.uint16) for _ in range(4)]
         for i, w in enumerate(ws):
-            ctx.fill_normal(w, 10 + i, 0.0, 0.02)
+            if wt == "f32":
+                ctx.fill_normal(w, 10 + i, 0.0, 0.02)
+            else:
+                (ctx.fill_normal_bf16 if wt == "bf16" else ctx.fill_normal_f16)(w, 10 + i, 0.0, 0.02)
         p = {"n": n, "k": k, "m": 1, "split": 1, "ldx": k, "ldy": n // 2 if cfg == "5g" else n, "eps": 1e-5,
              "factor": 1.0}
         rot = [[Launch(kern, p, [w.ptr, x.ptr, g.ptr, y.ptr])] for w in ws]
         ms = time_graph(ctx, None, args.steps, args.warmup, rotate=rot)
         outs = n // 2 if cfg == "5g" else n
-        nbytes = 4 * (n * k + k + k + outs)
+        nbytes = eb * (n * k + k) + 4 * (k + outs)
         workload = f"config 5's {'[gate; up] GEMV' if cfg == '5g' else 'LM head'} {n} x {k}, batch 1 ({kern})"
         unit_label = "GEMVs/s"
     elif cfg in ("3a", "3b"):
@@ -775,7 +789,9 @@ def run_kernel_config(args):
     value = (args.batch if cfg == "4" else 1) / (ms / 1e3)
     line = {"metric": workload, "value": value, "unit": unit_label, "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic, seeded on the device",
+            "vs_baseline": None,
+            "dtype": f"{args.weights} weights, f32 arithmetic" if cfg in ("5g", "5h") and args.weights != "f32" else "f32",
+            "data": "synthetic, seeded on the device",
             "config": {"workload": workload},
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                          "traffic": NCU_TRAFFIC[("gemv", 11008, 4096, 16)][0] if cfg == "3b" else None,

@@ -25,11 +25,57 @@ __global__ void gather_kernel(const float* __restrict__ table, uint32_t width, c
   reinterpret_cast<float4*>(y + (size_t)r * width)[j] = v;
 }
 
+// One thread's part of a row's first maximum: elements t, t + T, ... (or,
+// with vec, packs of 4 at t, t + T, ..., four packs in flight, then the
+// tail past the last whole pack), in increasing index order; an element is
+// taken when greater than the best so far, or when it is the first
+// candidate equal to it (-inf), never a NaN.
+__device__ __forceinline__ void scan_first_max(const float* __restrict__ xr, uint32_t n, bool vec, float& bv,
+                                               uint32_t& bi) {
+  bv = -INFINITY;
+  bi = 0xffffffffu;
+  auto take = [&](float v, uint32_t j) {
+    if (v > bv || (bi == 0xffffffffu && v == bv)) {
+      bv = v;
+      bi = j;
+    }
+  };
+  const uint32_t T = blockDim.x;
+  uint32_t j0 = 0;
+  if (vec) {
+    const float4* x4 = reinterpret_cast<const float4*>(xr);
+    const uint32_t packs = n / 4;
+    uint32_t p = threadIdx.x;
+    for (; p + 3 * T < packs; p += 4 * T) {
+      float4 q[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) q[u] = __ldg(x4 + p + u * T);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t j = 4 * (p + u * T);
+        take(q[u].x, j);
+        take(q[u].y, j + 1);
+        take(q[u].z, j + 2);
+        take(q[u].w, j + 3);
+      }
+    }
+    for (; p < packs; p += T) {
+      const float4 q = __ldg(x4 + p);
+      take(q.x, 4 * p);
+      take(q.y, 4 * p + 1);
+      take(q.z, 4 * p + 2);
+      take(q.w, 4 * p + 3);
+    }
+    j0 = 4 * packs;
+  }
+  for (uint32_t j = j0 + threadIdx.x; j < n; j += T) take(xr[j], j);
+}
+
 // ArgMax (Eval.hs:545-548, 684-685): the fold keeps the first index whose
 // value is greater than all before it, so NaNs past the first element are
 // never taken and a NaN first element is the answer. Each thread scans its
-// elements in index order; pairs combine by "greater, or equal at a lower
-// index". Grid m, 1024 threads.
+// elements in index order (scan_first_max); pairs combine by "greater, or
+// equal at a lower index". Grid m, 1024 threads.
 __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ x, uint32_t n, uint32_t ldx,
                                                       uint32_t* __restrict__ ids) {
   __shared__ float sv[32];
@@ -38,15 +84,9 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
   grid_launch_dependents();
   const uint32_t r = blockIdx.x;
   const float* xr = x + (size_t)r * ldx;
-  float bv = -INFINITY;
-  uint32_t bi = 0xffffffffu;
-  for (uint32_t j = threadIdx.x; j < n; j += blockDim.x) {
-    const float v = xr[j];
-    if (v > bv || (bi == 0xffffffffu && v == bv)) {
-      bv = v;
-      bi = j;
-    }
-  }
+  float bv;
+  uint32_t bi;
+  scan_first_max(xr, n, ((uintptr_t)x % 16 == 0) && ldx % 4 == 0, bv, bi);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -90,15 +130,9 @@ __global__ void __launch_bounds__(1024) argmax_pairs_kernel(const float* __restr
   grid_launch_dependents();
   const uint32_t r = blockIdx.x;
   const float* xr = x + (size_t)r * ldx;
-  float bv = -INFINITY;
-  uint32_t bi = 0xffffffffu;
-  for (uint32_t j = threadIdx.x; j < n; j += blockDim.x) {
-    const float v = xr[j];
-    if (v > bv || (bi == 0xffffffffu && v == bv)) {
-      bv = v;
-      bi = j;
-    }
-  }
+  float bv;
+  uint32_t bi;
+  scan_first_max(xr, n, ((uintptr_t)x % 16 == 0) && ldx % 4 == 0, bv, bi);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {

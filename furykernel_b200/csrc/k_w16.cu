@@ -112,6 +112,60 @@ __device__ __forceinline__ void row_totals(const uint2* __restrict__ wr, const f
   }
 }
 
+// Two rows' totals at once (a gate/up pair, or two units of a warp), each
+// in row_totals' order: their loads interleaved, 8 packs of each row in
+// flight a lane, so that a warp has as many bytes in flight as with one
+// row but pays the pause between rows (the last loads' latency, the lanes'
+// sums) once for the two.
+template <class E, int M>
+__device__ __forceinline__ void row_totals2(const uint2* __restrict__ wa, const uint2* __restrict__ wb,
+                                            const float4* __restrict__ xs4, uint32_t packs, uint32_t m, uint32_t s,
+                                            int lane, float (&ta)[M], float (&tb)[M]) {
+  constexpr int F = kInFlight / 2;
+  const uint32_t stride = 32u * s;
+  for (uint32_t q = 0; q < s; ++q) {
+    float acca[M], accb[M];
+#pragma unroll
+    for (int i = 0; i < M; ++i) acca[i] = accb[i] = 0.0f;
+    uint32_t j = q * 32u + (uint32_t)lane;
+    for (; j + (F - 1) * stride < packs; j += F * stride) {
+      uint2 ra[F], rb[F];
+#pragma unroll
+      for (int u = 0; u < F; ++u) {
+        ra[u] = ld_stream2(wa + j + u * stride);
+        rb[u] = ld_stream2(wb + j + u * stride);
+      }
+#pragma unroll
+      for (int u = 0; u < F; ++u) {
+        const float4 va = E::widen4(ra[u]), vb = E::widen4(rb[u]);
+#pragma unroll
+        for (int i = 0; i < M; ++i)
+          if (i < (int)m) {
+            const float4 xv = xs4[(size_t)i * packs + j + u * stride];
+            acca[i] = __fadd_rn(acca[i], pack_dot(xv, va));
+            accb[i] = __fadd_rn(accb[i], pack_dot(xv, vb));
+          }
+      }
+    }
+    for (; j < packs; j += stride) {
+      const float4 va = E::widen4(ld_stream2(wa + j)), vb = E::widen4(ld_stream2(wb + j));
+#pragma unroll
+      for (int i = 0; i < M; ++i)
+        if (i < (int)m) {
+          const float4 xv = xs4[(size_t)i * packs + j];
+          acca[i] = __fadd_rn(acca[i], pack_dot(xv, va));
+          accb[i] = __fadd_rn(accb[i], pack_dot(xv, vb));
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < M; ++i) {
+      const float pa = warp_sum(acca[i]), pb = warp_sum(accb[i]);
+      ta[i] = q == 0 ? pa : __fadd_rn(ta[i], pa);
+      tb[i] = q == 0 ? pb : __fadd_rn(tb[i], pb);
+    }
+  }
+}
+
 // Persistent blocks of 16 warps; unit u (a row, or a gate/up row pair) goes
 // to block u mod G and, within it, warp (u / G) mod 16; a scattering block
 // owns the contiguous rows [s_lo, s_hi) instead.
@@ -222,28 +276,58 @@ __global__ void __launch_bounds__(512, 2) gemv_stream_w16_kernel(StreamArgs a) {
   const uint32_t s_hi = (uint32_t)((uint64_t)units * (blockIdx.x + 1) / G);
   // Weight rows are k bf16 = k / 4 packs of 8 bytes.
   const uint2* w2 = reinterpret_cast<const uint2*>(a.w);
-  for (uint32_t slot = (uint32_t)warp;; slot += kStreamWarps) {
-    const uint32_t u = EPI == SEPI_SCATTER ? s_lo + slot : blockIdx.x + slot * G;
-    if (EPI == SEPI_SCATTER ? u >= s_hi : u >= units) break;
-    float t0[M], t1[M];
-    row_totals<E, M>(w2 + (size_t)u * per_unit * packs, xs4, packs, a.m, a.split, lane, t0);
-    if (EPI == SEPI_SILU_PAIR) row_totals<E, M>(w2 + ((size_t)u * 2 + 1) * packs, xs4, packs, a.m, a.split, lane, t1);
-    if (lane == 0) {
+  // A unit's totals out: staged (scatter), or through the epilogue to y.
+  auto emit = [&](uint32_t u, const float(&t0)[M], const float(&t1)[M]) {
+    if (lane != 0) return;
 #pragma unroll
-      for (int i = 0; i < M; ++i) {
-        if (i >= (int)a.m) break;
-        if (EPI == SEPI_SCATTER) {
-          outs[i][u - s_lo] = t0[i];
-          continue;
-        }
-        float v;
-        if (EPI == SEPI_SILU_PAIR)
-          v = silu_of(t0[i], t1[i]);
-        else if (EPI == SEPI_ADD)
-          v = __fadd_rn(a.r[(size_t)i * a.ldr + u], t0[i]);
-        else
-          v = t0[i];
-        a.y[(size_t)i * a.ldy + u] = v;
+    for (int i = 0; i < M; ++i) {
+      if (i >= (int)a.m) break;
+      if (EPI == SEPI_SCATTER) {
+        outs[i][u - s_lo] = t0[i];
+        continue;
+      }
+      float v;
+      if (EPI == SEPI_SILU_PAIR)
+        v = silu_of(t0[i], t1[i]);
+      else if (EPI == SEPI_ADD)
+        v = __fadd_rn(a.r[(size_t)i * a.ldr + u], t0[i]);
+      else
+        v = t0[i];
+      a.y[(size_t)i * a.ldy + u] = v;
+    }
+  };
+  // At batch 1 a warp takes its slots two at a time (a gate/up unit's two
+  // rows, or two one-row units), their rows' loads interleaved
+  // (row_totals2); larger batches keep one row at a time, whose
+  // accumulators would not fit twice in the 64 registers a thread has.
+  constexpr bool PAIRED = M == 1;
+  auto unit_of = [&](uint32_t slot) { return EPI == SEPI_SCATTER ? s_lo + slot : blockIdx.x + slot * G; };
+  auto live = [&](uint32_t u) { return EPI == SEPI_SCATTER ? u < s_hi : u < units; };
+  for (uint32_t slot = (uint32_t)warp;; slot += (EPI == SEPI_SILU_PAIR || !PAIRED ? 1u : 2u) * kStreamWarps) {
+    const uint32_t u = unit_of(slot);
+    if (!live(u)) break;
+    float t0[M], t1[M];
+    if (EPI == SEPI_SILU_PAIR) {
+      if (PAIRED) {
+        row_totals2<E, M>(w2 + (size_t)u * 2 * packs, w2 + ((size_t)u * 2 + 1) * packs, xs4, packs, a.m, a.split,
+                          lane, t0, t1);
+      } else {
+        row_totals<E, M>(w2 + (size_t)u * 2 * packs, xs4, packs, a.m, a.split, lane, t0);
+        row_totals<E, M>(w2 + ((size_t)u * 2 + 1) * packs, xs4, packs, a.m, a.split, lane, t1);
+      }
+      emit(u, t0, t1);
+    } else if (!PAIRED) {
+      row_totals<E, M>(w2 + (size_t)u * packs, xs4, packs, a.m, a.split, lane, t0);
+      emit(u, t0, t0);
+    } else {
+      const uint32_t u2 = unit_of(slot + kStreamWarps);
+      if (live(u2)) {
+        row_totals2<E, M>(w2 + (size_t)u * packs, w2 + (size_t)u2 * packs, xs4, packs, a.m, a.split, lane, t0, t1);
+        emit(u, t0, t1);
+        emit(u2, t1, t1);
+      } else {
+        row_totals<E, M>(w2 + (size_t)u * packs, xs4, packs, a.m, a.split, lane, t0);
+        emit(u, t0, t0);
       }
     }
   }

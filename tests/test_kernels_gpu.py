@@ -351,9 +351,12 @@ def test_elementwise_and_gather(ctx):
         buf.free()
 
 
-def test_argmax_first_index_ties_and_nans(ctx):
+# n, ldx: whole packs of 4 (the vectorised scan), a ragged tail after the
+# packs, and rows that do not start on 16 bytes (the scalar scan).
+@pytest.mark.parametrize("n,ldx", [(32000, 32000), (32002, 32004), (31999, 32003)])
+def test_argmax_first_index_ties_and_nans(ctx, n, ldx):
     rows = []
-    r = O.normal(61, 32000)
+    r = O.normal(61, n)
     rows.append(r.copy())
     t = r.copy()
     t[100] = t[31000] = 50.0  # a tie: the lower index
@@ -365,18 +368,23 @@ def test_argmax_first_index_ties_and_nans(ctx):
     t[5] = np.nan
     t[7] = 60.0  # NaNs later are never taken
     rows.append(t)
-    t = np.full(32000, -np.inf, np.float32)  # all equal: index 0
+    t = np.full(n, -np.inf, np.float32)  # all equal: index 0
     rows.append(t)
-    t = np.zeros(32000, np.float32)
+    t = np.zeros(n, np.float32)
     t[3] = -0.0
     t[9] = 0.0  # +0 and -0 tie: the lower index
     rows.append(t)
+    t = r.copy()
+    t[n - 1] = 70.0  # the maximum in the last element (a ragged tail's, where there is one)
+    rows.append(t)
     x = np.stack(rows)
-    dx, di = ctx.to_device(x), ctx.empty(len(rows), np.uint32)
-    ctx.launch("argmax", {"m": len(rows), "n": 32000, "ldx": 32000}, [dx, di])
+    xp = np.zeros((len(rows), ldx), np.float32)
+    xp[:, :n] = x
+    dx, di = ctx.to_device(xp), ctx.empty(len(rows), np.uint32)
+    ctx.launch("argmax", {"m": len(rows), "n": n, "ldx": ldx}, [dx, di])
     got = di.download()
     assert np.array_equal(got, O.argmax(x))
-    assert list(got[1:]) == [100, 0, 7, 0, 0]
+    assert list(got[1:]) == [100, 0, 7, 0, 0, n - 1]
     dx.free()
     di.free()
 
