@@ -3,8 +3,7 @@
 // position's key and value are (a source with k4 / v4, four elements of a
 // position widened to f32) and runs attend_prompt_body.
 //
-// A block takes (64 query rows, head), heavy tiles (the prompt's late rows,
-// which see the most positions) first; 256 threads, thread (ty, tx) =
+// A block takes (64 query rows, head); 256 threads, thread (ty, tx) =
 // (tid / 16, tid % 16) owning rows 4ty..4ty+3. Positions go 64 at a time
 // through shared memory: the round's keys (rows padded to 132 floats, so
 // that the 16-byte reads of consecutive keys fall in distinct banks) and
@@ -18,6 +17,16 @@
 // values' rows are stored permuted (position tx + 16j of the round at row
 // 4tx + j) so that a thread's weights, four consecutive floats, meet them
 // in order.
+//
+// The blocks' order balances the causal work across the SMs: a tile of the
+// prompt's late rows sees up to 8 times the positions of an early one, and
+// two blocks share an SM. Block L (in launch order) of the first wave (one
+// block an SM) takes the L-th heaviest (tile, head); block S + j of the
+// second takes the j-th lightest, which lands on the SM whose first block
+// took the j-th heaviest, so each SM's two tiles add up to about the same
+// number of positions (measured on config 5: the busiest SM's FMA pipe at
+// 89% while the average SM's was at 43%, with the tiles launched heavy
+// first in tile order).
 //
 // The orders, the fused products and expf differ from the decode kernels'
 // and from the CPU target's, so prefill attention is held to the f64
@@ -81,7 +90,12 @@ __device__ __forceinline__ void attend_prompt_body(const FkAttend& a, Src src, f
   float* ps = ks;
   const uint32_t tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const uint32_t lane = tid & 31, warp = tid >> 5;
-  const uint32_t tile = gridDim.x - 1 - blockIdx.x, h = blockIdx.y;
+  // The grid is (S, waves): S the first wave's blocks (prompt_grid).
+  const uint32_t T = (a.m + kRows - 1) / kRows, H = a.heads, N = T * H, S = gridDim.x;
+  const uint32_t L = blockIdx.x + S * blockIdx.y;
+  if (L >= N) return;  // the last wave's padding
+  const uint32_t o = L < S ? L : N - 1 - (L - S);  // the item's rank, heaviest first
+  const uint32_t tile = T - 1 - o / H, h = o % H;
   const uint32_t r0 = tile * kRows;
   const uint32_t rows = min(kRows, a.m - r0);
   const uint32_t ncols = max_pos + 1;
@@ -220,6 +234,23 @@ __device__ __forceinline__ void attend_prompt_body(const FkAttend& a, Src src, f
           make_float4(acc[ri][4] / l, acc[ri][5] / l, acc[ri][6] / l, acc[ri][7] / l);
     }
   }
+}
+
+// The launch grid for m rows and `heads` heads: (S, waves), S the first
+// wave (the SM count, or fewer blocks), the blocks past m's items idle.
+inline dim3 prompt_grid(uint32_t m, uint32_t heads) {
+  static int sms[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!sms[dev]) {
+    int n = 148;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1) n = 148;
+    sms[dev] = n;
+  }
+  const uint32_t items = (m + kRows - 1) / kRows * heads;
+  const uint32_t S = items < (uint32_t)sms[dev] ? items : (uint32_t)sms[dev];
+  return dim3(S, (items + S - 1) / S);
 }
 
 }  // namespace prompt

@@ -376,7 +376,7 @@ cudaError_t fk_launch_attend_prompt(const FkAttend& a, float* out, uint32_t ldo,
   const size_t smem = fk::prompt::kSmemBytes;
   cudaError_t e = fk_allow_smem(fk::attend_prompt_kernel, smem);
   if (e != cudaSuccess) return e;
-  const dim3 grid((a.m + fk::prompt::kRows - 1) / fk::prompt::kRows, a.heads);
+  const dim3 grid = fk::prompt::prompt_grid(a.m, a.heads);
   return fk_launch_ex(fk::attend_prompt_kernel, grid, dim3(fk::prompt::kThreads), smem, s, a.pdl, a, out, ldo,
                       max_pos);
 }

@@ -312,7 +312,7 @@ cudaError_t launch_prompt16(const Attend16& f, float* out, uint32_t ldo, uint32_
   const size_t smem = prompt::kSmemBytes;
   cudaError_t e = fk_allow_smem(attend_prompt16_kernel<E>, smem);
   if (e != cudaSuccess) return e;
-  const dim3 grid((f.a.m + prompt::kRows - 1) / prompt::kRows, f.a.heads);
+  const dim3 grid = prompt::prompt_grid(f.a.m, f.a.heads);
   return fk_launch_ex(attend_prompt16_kernel<E>, grid, dim3(prompt::kThreads), smem, s, f.a.pdl, f, out, ldo,
                       max_pos);
 }

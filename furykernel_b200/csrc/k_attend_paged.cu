@@ -422,7 +422,7 @@ cudaError_t launch_prompt(const FkAttend& a, const FkPaged& pg, const void* kc, 
   f.a = a;
   f.P = Pool{pg.table, static_cast<const uint64_t*>(kc), static_cast<const uint64_t*>(vc), pg.block_size,
              pg.table_len, pg.blocks};
-  const dim3 grid((a.m + prompt::kRows - 1) / prompt::kRows, a.heads);
+  const dim3 grid = prompt::prompt_grid(a.m, a.heads);
   return fk_launch_ex(kern, grid, dim3(prompt::kThreads), smem, s, a.pdl, f, out, ldo, max_pos);
 }
 
