@@ -126,3 +126,25 @@ def test_gemm_tf32x3w_set_tiles(ctx, M, N, K, tm, parts):
     rows = np.arange(0, M, max(1, M // 4))[:4]
     ref = O.r_linear(w, O.r_input(a[rows]))
     assert O.within(c[rows], ref).all()
+
+
+def test_split_tf32_vector_and_scalar_forms_agree(ctx):
+    """split_tf32 over n a multiple of 4 (16-byte loads and stores) and over
+    n + 1 (an element at a time): the same bits for the shared elements,
+    each half a TF32 value and hi + lo within 2^-21 of x."""
+    n = 1000
+    x = O.normal(17, n + 1)
+    dx = ctx.to_device(x)
+    outs = []
+    for m in (n, n + 1):
+        hi, lo = ctx.empty(m), ctx.empty(m)
+        ctx.launch("split_tf32", {"n": m}, [dx, hi, lo])
+        outs.append((hi.download(), lo.download()))
+        hi.free()
+        lo.free()
+    (h4, l4), (h1, l1) = outs
+    assert np.array_equal(h4.view(np.uint32), h1[:n].view(np.uint32))
+    assert np.array_equal(l4.view(np.uint32), l1[:n].view(np.uint32))
+    assert np.all(h1.view(np.uint32) & 0x1FFF == 0) and np.all(l1.view(np.uint32) & 0x1FFF == 0)
+    assert np.all(np.abs(h1.astype(np.float64) + l1 - x) <= np.abs(x) * 2.0 ** -21)
+    dx.free()
