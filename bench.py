@@ -4,16 +4,19 @@ on B200, through the planned launch sequence captured as one CUDA graph.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
 
 One step is one greedy decode step of the whole model at batch B (default
-1): the embedding gather, 32 planned layers (7 launches each), the head's
-norm + tied LM head + argmax, and the feedback of the ids. Weights are
-seeded N(0, 0.02) on the device; the KV cache holds a 512-position
-prompt's keys and values (seeded N(0, 1)) and decode continues from
-position 512. Every step streams the 26.4 GB of weights, far more than L2.
+1): the embedding gather, 32 planned layers (6 launches each at batch 1:
+q/k/v, the fused KV store + attention, its combine, o, [gate; up], down),
+the head's norm + tied LM head + argmax, and the feedback of the ids.
+Weights are seeded N(0, 0.02) on the device; the KV cache holds a
+512-position prompt's keys and values (seeded N(0, 1)) and decode continues
+from position 512. Every step streams the 26.4 GB of weights, far more than
+L2.
 
 --impl reference times the reference's CPU path instead: the C
-restatement of the FuryKernel.Cpu target's arithmetic (oracle/), on all host
-threads, over a bounded sample (one full-size layer and the head per step,
-scaled to 32 layers).
+restatement of the FuryKernel.Cpu target's arithmetic (oracle/), whole
+32-layer greedy decode steps on one thread as the CPU target runs (the 32
+layer passes read one full-size layer's weights, far past any host cache),
+then one step on all host threads reported beside it.
 """
 
 from __future__ import annotations
