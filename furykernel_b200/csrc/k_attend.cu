@@ -269,34 +269,50 @@ __global__ void __launch_bounds__(prompt::kThreads) attend_prompt_kernel(FkAtten
 // The combine step: grid (heads, m), d threads. The largest maximum M (the
 // maximum is exact in any order) and each split's weight exp(m_j - M) are
 // computed once a block, into shared memory; every thread then adds the
-// splits in order for its dimension.
+// splits in order for its dimension. A thread's first kCombineHeld
+// accumulators are requested together with the maxima, so that a decode
+// step's few splits cost one round trip to L2, not one for every 8.
+constexpr int kCombineHeld = 32;
 __global__ void combine_kernel(FkCombine a) {
   extern __shared__ float wsplit[];  // [max_splits] weights, then [max_splits] sums
   float* lsplit = wsplit + a.max_splits;
-  __shared__ float top_s;
   grid_wait();
   grid_launch_dependents();
   const uint32_t h = blockIdx.x, r = blockIdx.y, i = threadIdx.x;
   const uint32_t splits = (a.pos[r] + 1 + a.chunk - 1) / a.chunk;
   const size_t at = ((size_t)r * a.heads + h) * a.max_splits;
-  if (threadIdx.x < 32) {
-    float top = -INFINITY;
-    for (uint32_t j = threadIdx.x; j < splits; j += 32) top = max_number(top, a.part_m[at + j]);
+  float held[kCombineHeld];
+#pragma unroll
+  for (int u = 0; u < kCombineHeld; ++u) held[u] = (uint32_t)u < splits ? a.part_acc[(at + u) * a.d + i] : 0.0f;
+  if (threadIdx.x < 32) {  // one warp: M, then the weights and sums (lane j's first split kept in registers)
+    const uint32_t j0 = threadIdx.x;
+    const float m0 = j0 < splits ? a.part_m[at + j0] : -INFINITY;
+    const float l0 = j0 < splits ? a.part_l[at + j0] : 0.0f;
+    float top = j0 < splits ? max_number(-INFINITY, m0) : -INFINITY;
+    for (uint32_t j = j0 + 32; j < splits; j += 32) top = max_number(top, a.part_m[at + j]);
     top = warp_max(top);
-    if (threadIdx.x == 0) top_s = top;
-  }
-  __syncthreads();
-  const float top = top_s;
-  for (uint32_t j = threadIdx.x; j < splits; j += blockDim.x) {
-    wsplit[j] = exp_rounded(__fsub_rn(a.part_m[at + j], top));
-    lsplit[j] = a.part_l[at + j];
+    if (j0 < splits) {
+      wsplit[j0] = exp_rounded(__fsub_rn(m0, top));
+      lsplit[j0] = l0;
+    }
+    for (uint32_t j = j0 + 32; j < splits; j += 32) {
+      wsplit[j] = exp_rounded(__fsub_rn(a.part_m[at + j], top));
+      lsplit[j] = a.part_l[at + j];
+    }
   }
   __syncthreads();
   const float w0 = wsplit[0];
   float l = __fmul_rn(lsplit[0], w0);
-  float o = __fmul_rn(a.part_acc[at * a.d + i], w0);
-  // The splits in order; their accumulators 8 loads at a time in flight.
-  uint32_t j = 1;
+  float o = __fmul_rn(held[0], w0);
+  // The splits in order: the held ones, then the rest 8 loads at a time in flight.
+#pragma unroll
+  for (int u = 1; u < kCombineHeld; ++u) {
+    if ((uint32_t)u < splits) {
+      l = __fadd_rn(l, __fmul_rn(lsplit[u], wsplit[u]));
+      o = __fadd_rn(o, __fmul_rn(held[u], wsplit[u]));
+    }
+  }
+  uint32_t j = kCombineHeld;
   for (; j + 8 <= splits; j += 8) {
     float v[8];
 #pragma unroll

@@ -258,6 +258,10 @@ def test_gemv_bf16_special_values(ctx):
     (3, 8, 8, 300, [0, 129, 299], 64),
     (1, 32, 32, 2304, [2048], 128),
     (4, 4, 4, 40, [45, 3, 39, 80], 32),  # positions past the ring's length wrap
+    # The combine holds 32 splits in registers, then loads 8 at a time, then one:
+    # 32 and 34 splits at the boundary, 66 through all three.
+    (2, 4, 4, 1100, [1023, 1056], 32),
+    (1, 4, 2, 2304, [2100], 32),
 ])
 def test_attention_path(ctx, m, heads, kv_heads, length, positions, chunk):
     d = 128
