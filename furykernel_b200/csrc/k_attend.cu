@@ -12,6 +12,8 @@
 // adding e and e * v from 0, and the warps' sums are added in warp order.
 // The combine rescales each split by exp(m - M), M the largest maximum, and
 // adds the splits in order before dividing.
+#include <algorithm>
+
 #include "fk_common.cuh"
 #include "fk_kernels.h"
 #include "fk_prompt.cuh"
@@ -39,11 +41,15 @@ __device__ __forceinline__ void rope_pair(const float* __restrict__ src, float* 
   }
 }
 
-// The KV store step: grid (kv_heads, m), d / 2 threads.
+// The KV store step: grid (ceil(kv_heads / hb), m), hb * d / 2 threads, hb
+// heads a block (4 at d = 128: a prompt's rows in blocks of 256 threads, not
+// thousands of 64-thread blocks).
 __global__ void kv_store_kernel(FkKvStore a) {
   grid_wait();
   grid_launch_dependents();
-  const uint32_t h = blockIdx.x, r = blockIdx.y, i = threadIdx.x, half = a.d / 2;
+  const uint32_t half = a.d / 2;
+  const uint32_t h = blockIdx.x * (blockDim.x / half) + threadIdx.x / half, r = blockIdx.y, i = threadIdx.x % half;
+  if (h >= a.kv_heads) return;
   const uint32_t p = a.pos[r];
   const size_t at = (((size_t)a.slot[r] * a.kv_heads + h) * a.length + p % a.length) * a.d;
   const float* krow = a.qkv + (size_t)r * a.ldq + a.k_off + (size_t)h * a.d;
@@ -344,8 +350,10 @@ __global__ void rope_kernel(const float* __restrict__ x, uint32_t heads, uint32_
 
 cudaError_t fk_launch_kv_store(const FkKvStore& a, cudaStream_t s) {
   if (a.m == 0) return cudaSuccess;
-  if (a.d % 2 != 0 || a.d > 2048) return cudaErrorInvalidValue;
-  return fk_launch_ex(fk::kv_store_kernel, dim3(a.kv_heads, a.m), dim3(a.d / 2), 0, s, a.pdl, a);
+  if (a.d % 2 != 0 || a.d > 2048 || a.kv_heads == 0) return cudaErrorInvalidValue;
+  const uint32_t half = a.d / 2;
+  const uint32_t hb = std::max(1u, std::min(a.kv_heads, 256u / half));  // heads a block
+  return fk_launch_ex(fk::kv_store_kernel, dim3((a.kv_heads + hb - 1) / hb, a.m), dim3(hb * half), 0, s, a.pdl, a);
 }
 
 namespace {

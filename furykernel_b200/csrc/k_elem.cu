@@ -219,6 +219,16 @@ __global__ void add_kernel(const float* __restrict__ a, const float* __restrict_
     y[i] = __fadd_rn(a[i], b[i]);
 }
 
+// The same sums, four a thread with 16-byte loads and stores (n4 = n / 4;
+// every array 16-byte aligned).
+__global__ void add4_kernel(const float4* __restrict__ a, const float4* __restrict__ b, float4* __restrict__ y,
+                            uint64_t n4) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n4; i += (uint64_t)gridDim.x * blockDim.x) {
+    const float4 u = a[i], v = b[i];
+    y[i] = make_float4(__fadd_rn(u.x, v.x), __fadd_rn(u.y, v.y), __fadd_rn(u.z, v.z), __fadd_rn(u.w, v.w));
+  }
+}
+
 // SiLU-gate, silu(a) * b with silu(a) = a / (1 + exp(-a)).
 __global__ void silu_mul_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ y,
                                 uint64_t n) {
@@ -329,7 +339,12 @@ static unsigned grid_for(uint64_t n) {
 
 cudaError_t fk_launch_add(const float* a, const float* b, float* y, uint64_t n, cudaStream_t s) {
   if (n == 0) return cudaSuccess;
-  fk::add_kernel<<<grid_for(n), 256, 0, s>>>(a, b, y, n);
+  if (n % 4 == 0 && (((uintptr_t)a | (uintptr_t)b | (uintptr_t)y) & 15) == 0)
+    fk::add4_kernel<<<grid_for(n / 4), 256, 0, s>>>(reinterpret_cast<const float4*>(a),
+                                                    reinterpret_cast<const float4*>(b), reinterpret_cast<float4*>(y),
+                                                    n / 4);
+  else
+    fk::add_kernel<<<grid_for(n), 256, 0, s>>>(a, b, y, n);
   return cudaGetLastError();
 }
 

@@ -262,6 +262,8 @@ def test_gemv_bf16_special_values(ctx):
     # 32 and 34 splits at the boundary, 66 through all three.
     (2, 4, 4, 1100, [1023, 1056], 32),
     (1, 4, 2, 2304, [2100], 32),
+    # The KV store takes 4 heads a block: 6 leave the second block half idle.
+    (2, 12, 6, 64, [10, 50], 16),
 ])
 def test_attention_path(ctx, m, heads, kv_heads, length, positions, chunk):
     d = 128
@@ -342,6 +344,9 @@ def test_elementwise_and_gather(ctx):
     da, db, dy = ctx.to_device(a), ctx.to_device(b), ctx.empty(n)
     ctx.launch("add", {"n": n}, [da, db, dy])
     assert same_bits(dy.download(), O.add(a, b))
+    # A count that is not a multiple of 4 takes the scalar form: the same sums.
+    ctx.launch("add", {"n": n - 3}, [da, db, dy])
+    assert same_bits(dy.download()[:n - 3], O.add(a[:n - 3], b[:n - 3]))
     ctx.launch("silu_mul", {"n": n}, [da, db, dy])
     assert same_bits(dy.download(), O.silu_mul(a, b))
     ref = O.r_silu_mul(O.r_input(a), O.r_input(b))
