@@ -56,13 +56,16 @@ struct Store16 {
   uint16_t* vc;
 };
 
-// The KV store step: grid (kv_heads, m), d / 2 threads.
+// The KV store step: grid (ceil(kv_heads / hb), m), hb * d / 2 threads, hb
+// heads a block (4 at d = 128).
 template <class E>
 __global__ void kv_store16_kernel(Store16 s) {
   const FkKvStore& a = s.a;
   grid_wait();
   grid_launch_dependents();
-  const uint32_t h = blockIdx.x, r = blockIdx.y, i = threadIdx.x, half = a.d / 2;
+  const uint32_t half = a.d / 2;
+  const uint32_t h = blockIdx.x * (blockDim.x / half) + threadIdx.x / half, r = blockIdx.y, i = threadIdx.x % half;
+  if (h >= a.kv_heads) return;
   const uint32_t p = a.pos[r];
   const size_t at = (((size_t)a.slot[r] * a.kv_heads + h) * a.length + p % a.length) * a.d;
   const float* krow = a.qkv + (size_t)r * a.ldq + a.k_off + (size_t)h * a.d;
@@ -322,12 +325,15 @@ cudaError_t launch_prompt16(const Attend16& f, float* out, uint32_t ldo, uint32_
 
 cudaError_t fk_launch_kv_store16(const FkKvStore& a, FkElem e, uint16_t* kc, uint16_t* vc, cudaStream_t s) {
   if (a.m == 0) return cudaSuccess;
-  if (a.d % 2 != 0 || a.d > 2048 || !kc || !vc) return cudaErrorInvalidValue;
+  if (a.d % 2 != 0 || a.d > 2048 || a.kv_heads == 0 || !kc || !vc) return cudaErrorInvalidValue;
   fk::kv16::Store16 st;
   st.a = a;
   st.kc = kc;
   st.vc = vc;
-#define CALL(E) fk_launch_ex(fk::kv16::kv_store16_kernel<E>, dim3(a.kv_heads, a.m), dim3(a.d / 2), 0, s, a.pdl, st)
+  const uint32_t half = a.d / 2;
+  const uint32_t hb = half >= 256 ? 1u : (a.kv_heads < 256u / half ? a.kv_heads : 256u / half);  // heads a block
+#define CALL(E) \
+  fk_launch_ex(fk::kv16::kv_store16_kernel<E>, dim3((a.kv_heads + hb - 1) / hb, a.m), dim3(hb * half), 0, s, a.pdl, st)
   return FK_BY_ELEM16(e, CALL);
 #undef CALL
 }

@@ -111,13 +111,16 @@ struct StoreArgs {
   Pool P;
 };
 
-// The KV store step: grid (kv_heads, m), d / 2 threads.
+// The KV store step: grid (ceil(kv_heads / hb), m), hb * d / 2 threads, hb
+// heads a block (4 at d = 128).
 template <class E>
 __global__ void kv_store_paged_kernel(StoreArgs<E> s) {
   const FkKvStore& a = s.a;
   grid_wait();
   grid_launch_dependents();
-  const uint32_t h = blockIdx.x, r = blockIdx.y, i = threadIdx.x, half = a.d / 2;
+  const uint32_t half = a.d / 2;
+  const uint32_t h = blockIdx.x * (blockDim.x / half) + threadIdx.x / half, r = blockIdx.y, i = threadIdx.x % half;
+  if (h >= a.kv_heads) return;
   const uint32_t p = a.pos[r];
   const uint64_t at = at_of(s.P, r, p, h, a.kv_heads, a.d);
   if (at == ~0ull) return;
@@ -361,14 +364,18 @@ __global__ void __launch_bounds__(prompt::kThreads) attend_prompt_paged_kernel(A
 template <class E>
 cudaError_t launch_store(const FkKvStore& a, const FkPaged& pg, void* kc, void* vc, cudaStream_t s) {
   if (a.m == 0) return cudaSuccess;
-  if (a.d % 2 != 0 || a.d > 2048 || pg.block_size == 0 || pg.table_len == 0 || !pg.table || !kc || !vc)
+  if (a.d % 2 != 0 || a.d > 2048 || a.kv_heads == 0 || pg.block_size == 0 || pg.table_len == 0 || !pg.table || !kc ||
+      !vc)
     return cudaErrorInvalidValue;
   if ((uint64_t)a.kv_heads * pg.block_size * a.d >= (1ull << 32)) return cudaErrorInvalidValue;
   StoreArgs<E> st;
   st.a = a;
   st.P = Pool{pg.table, static_cast<const uint64_t*>(kc), static_cast<const uint64_t*>(vc), pg.block_size,
               pg.table_len, pg.blocks};
-  return fk_launch_ex(kv_store_paged_kernel<E>, dim3(a.kv_heads, a.m), dim3(a.d / 2), 0, s, a.pdl, st);
+  const uint32_t half = a.d / 2;
+  const uint32_t hb = half >= 256 ? 1u : (a.kv_heads < 256u / half ? a.kv_heads : 256u / half);  // heads a block
+  return fk_launch_ex(kv_store_paged_kernel<E>, dim3((a.kv_heads + hb - 1) / hb, a.m), dim3(hb * half), 0, s, a.pdl,
+                      st);
 }
 
 template <class E, bool FUSED>
