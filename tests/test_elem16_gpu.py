@@ -109,6 +109,7 @@ def test_gather_rmsnorm_rows_and_split_w16(ctx, t):
     (3, 8, 8, 300, [0, 129, 299], 64),
     (1, 32, 32, 2304, [2048], 128),
     (4, 4, 4, 40, [45, 3, 39, 80], 32),  # positions past the ring's length wrap
+    (2, 12, 6, 64, [10, 50], 16),  # the store's 4 heads a block: the second block half idle
 ])
 def test_attention_kv16(ctx, t, m, heads, kv_heads, length, positions, chunk):
     cs = CACHE_SUFFIX[t]

@@ -55,6 +55,7 @@ def disjoint_tables(seed, m, table_len, blocks):
     (2, 4, 2, 16, [5, 40], 16),
     (3, 8, 8, 32, [0, 129, 191], 64),
     (1, 32, 32, 16, [2047], 128),
+    (2, 12, 6, 16, [10, 50], 16),  # the store's 4 heads a block: the second block half idle
 ])
 def test_paged_store_and_attention(ctx, t, m, heads, kv_heads, block_size, positions, chunk):
     d = 128
